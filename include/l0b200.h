@@ -1,0 +1,456 @@
+/*
+ * l0b200.h -- C ABI of the B200 (sm_100a) backend for the l0llm decoder hot path.
+ *
+ * The library replaces the kernel surface that l0llm's C# decoder calls through the external
+ * LevelZero.NET 2.0.0 package: LevelZeroRuntime / ComputeDevice / SharedBuffer<T> /
+ * LlmKernelSuite and its ops. Each entry point names the reference call site it stands in for
+ * (paths are relative to the l0llm repository; `L/` = src/HFLabs.ML.LLM.LevelZero/).
+ *
+ * Conventions
+ *  - Every function returns an l0b_status; 0 (L0B_OK) is success. On failure l0b_last_error()
+ *    returns a thread-local, human-readable message. Argument errors map to the exception types
+ *    the reference throws (ArgumentException, ArgumentOutOfRangeException, NotSupportedException,
+ *    InvalidOperationException), see l0b_status.
+ *  - Handles are opaque. The caller owns them and frees them with the matching *_free call; the
+ *    library never frees a buffer it did not allocate.
+ *  - Buffers live in device memory (HBM). The reference's host-addressable USM pointer
+ *    (SharedBuffer.Pointer) is replaced by l0b_buffer_read / l0b_buffer_write of element ranges.
+ *  - Ops enqueue work on the device's stream. Between l0b_device_begin_recording and
+ *    l0b_device_end_recording they are recorded into a command list instead; end_recording submits
+ *    the list as one CUDA graph launch and waits (the reference's one submit + one wait per token).
+ *    Buffer writes made while recording take effect before the list runs, as host writes to USM do.
+ *  - One host thread per device. No entry point is re-entrant for the same device.
+ *  - No CPU fallback: without a usable sm_100 device every op returns L0B_ERR_NO_DEVICE.
+ */
+#ifndef L0B200_H
+#define L0B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(_WIN32)
+#define L0B_API __declspec(dllexport)
+#else
+#define L0B_API __attribute__((visibility("default")))
+#endif
+
+typedef enum l0b_status {
+    L0B_OK = 0,
+    L0B_ERR_ARGUMENT = 1,          /* ArgumentException / ArgumentNullException */
+    L0B_ERR_OUT_OF_RANGE = 2,      /* ArgumentOutOfRangeException */
+    L0B_ERR_UNSUPPORTED = 3,       /* NotSupportedException */
+    L0B_ERR_INVALID_OPERATION = 4, /* InvalidOperationException */
+    L0B_ERR_INVALID_DATA = 5,      /* InvalidDataException */
+    L0B_ERR_CUDA = 6,              /* a CUDA runtime call failed */
+    L0B_ERR_OUT_OF_MEMORY = 7,
+    L0B_ERR_NO_DEVICE = 8,         /* no sm_100 device: LevelZeroRuntime.IsAvailable() == false */
+    L0B_ERR_TIMEOUT = 9,           /* a bounded device-side wait gave up */
+    L0B_ERR_NCCL = 10
+} l0b_status;
+
+typedef enum l0b_dtype {
+    L0B_F32 = 0,
+    L0B_F16 = 1,
+    L0B_BF16 = 2,
+    L0B_I8 = 3,
+    L0B_I32 = 4,
+    L0B_U8 = 5
+} l0b_dtype;
+
+typedef struct l0b_device l0b_device;
+typedef struct l0b_buffer l0b_buffer;
+typedef struct l0b_suite l0b_suite;
+typedef struct l0b_model l0b_model;
+typedef struct l0b_comm l0b_comm;
+
+/* ------------------------------------------------------------------------------------------ */
+/* Errors and versions                                                                         */
+/* ------------------------------------------------------------------------------------------ */
+
+/* Message of the last failed call on this thread ("" if none). Valid until the next call. */
+L0B_API const char* l0b_last_error(void);
+/* Library ABI version, (major << 16) | minor. */
+L0B_API int32_t l0b_version(void);
+/* Number of device kernels this process has launched through the library (immediate launches and
+ * kernel nodes of submitted command lists). Used by benchmarks to count launches. */
+L0B_API int64_t l0b_kernel_launch_count(void);
+
+/* ------------------------------------------------------------------------------------------ */
+/* Runtime and device  (LevelZeroRuntime, ComputeDevice: src/l0llm/Program.cs:124,138-141,      */
+/*                      L/LevelZeroLlmEngine.cs:355-361, L/LlmModel.cs:353-442)                 */
+/* ------------------------------------------------------------------------------------------ */
+
+/* LevelZeroRuntime.IsAvailable(): *available = 1 when an sm_100 device is present. */
+L0B_API l0b_status l0b_runtime_is_available(int32_t* available);
+/* LevelZeroRuntime.EnumerateDevices(): number of usable devices. */
+L0B_API l0b_status l0b_device_count(int32_t* count);
+/* DeviceInfo{Name}: writes a NUL-terminated name (truncated to name_len) and SM count. */
+L0B_API l0b_status l0b_device_info(int32_t index, char* name, int32_t name_len, int32_t* sm_count,
+                                   int64_t* total_bytes);
+/* LevelZeroRuntime.GetDevice / GetDefaultDevice (index 0). */
+L0B_API l0b_status l0b_device_create(int32_t index, l0b_device** out);
+/* ComputeDevice.Dispose. Frees the stream, cached command lists and internal scratch. */
+L0B_API l0b_status l0b_device_free(l0b_device* dev);
+/* ComputeDevice.BeginRecording / EndRecording / AbortRecording / IsRecording. */
+L0B_API l0b_status l0b_device_begin_recording(l0b_device* dev);
+L0B_API l0b_status l0b_device_end_recording(l0b_device* dev);
+L0B_API l0b_status l0b_device_abort_recording(l0b_device* dev);
+L0B_API l0b_status l0b_device_is_recording(l0b_device* dev, int32_t* recording);
+/* Waits until all work enqueued on the device's stream is done. */
+L0B_API l0b_status l0b_device_synchronize(l0b_device* dev);
+/* The device's cudaStream_t, for callers that interleave their own work (e.g. torch). */
+L0B_API l0b_status l0b_device_stream(l0b_device* dev, void** stream);
+/* Number of command lists built (captured + instantiated) and reused since creation. */
+L0B_API l0b_status l0b_device_graph_stats(l0b_device* dev, int64_t* built, int64_t* reused,
+                                          int64_t* updated);
+/* Enables (1) or disables (0) programmatic dependent launch between consecutive kernels. */
+L0B_API l0b_status l0b_device_set_pdl(l0b_device* dev, int32_t enabled);
+
+/* ------------------------------------------------------------------------------------------ */
+/* Buffers  (SharedBuffer<T>: Write/ToArray/Pointer/Count/Dispose, L/LlmSequenceState.cs:60-80) */
+/* ------------------------------------------------------------------------------------------ */
+
+/* ComputeDevice.AllocShared<T>(count): zero-filled device buffer of count elements. */
+L0B_API l0b_status l0b_buffer_alloc(l0b_device* dev, l0b_dtype dtype, int64_t count, l0b_buffer** out);
+/* ComputeDevice.AllocShared<T>(T[] data). */
+L0B_API l0b_status l0b_buffer_alloc_from(l0b_device* dev, l0b_dtype dtype, int64_t count,
+                                         const void* host, l0b_buffer** out);
+L0B_API l0b_status l0b_buffer_free(l0b_buffer* buf);
+/* SharedBuffer.Write(T[]) at an element offset (Marshal.Copy into Pointer + offset). */
+L0B_API l0b_status l0b_buffer_write(l0b_buffer* buf, int64_t offset, const void* host, int64_t count);
+/* SharedBuffer.ToArray() / Marshal.Copy out of Pointer + offset. Waits for prior work. */
+L0B_API l0b_status l0b_buffer_read(l0b_buffer* buf, int64_t offset, void* host, int64_t count);
+/* Device-to-device copy of count elements (same dtype). */
+L0B_API l0b_status l0b_buffer_copy(l0b_buffer* dst, int64_t dst_offset, l0b_buffer* src,
+                                   int64_t src_offset, int64_t count);
+/* Sets every element to zero (stream-ordered). */
+L0B_API l0b_status l0b_buffer_zero(l0b_buffer* buf);
+L0B_API l0b_status l0b_buffer_count(l0b_buffer* buf, int64_t* count);
+L0B_API l0b_status l0b_buffer_dtype(l0b_buffer* buf, l0b_dtype* dtype);
+/* Raw device address (for interop with other CUDA code in the same process). */
+L0B_API l0b_status l0b_buffer_device_ptr(l0b_buffer* buf, void** ptr);
+
+/* ------------------------------------------------------------------------------------------ */
+/* Kernel suite  (LlmKernelSuite.Create/Dispose/EnsureQ8Scratch/Q8Scratch; statics of          */
+/*                LlmGemvKernel / LlmGemvQ8Kernel: L/LlmModel.cs:131-144, L/LlmMatrix.cs:242-253) */
+/* ------------------------------------------------------------------------------------------ */
+
+L0B_API l0b_status l0b_suite_create(l0b_device* dev, l0b_suite** out);
+L0B_API l0b_status l0b_suite_free(l0b_suite* suite);
+/* LlmKernelSuite.GemvQ8 != null: this backend always has the int8 kernels (returns 1). */
+L0B_API int32_t l0b_suite_has_q8(l0b_suite* suite);
+/* LlmKernelSuite.EnsureQ8Scratch(device, rows, width): sizes the shared activation scratch. */
+L0B_API l0b_status l0b_suite_ensure_q8_scratch(l0b_suite* suite, int32_t rows, int32_t width);
+/* LlmQ8Activations.RowCapacity of the current scratch (0 when none). */
+L0B_API int32_t l0b_suite_q8_scratch_rows(l0b_suite* suite);
+/* LlmGemvKernel.Supports(N): N % 4 == 0. */
+L0B_API int32_t l0b_gemv_supports(int32_t n);
+/* LlmGemvKernel.MaxRows: rows one ExecuteRows call (and one prefill chunk) takes. */
+L0B_API int32_t l0b_gemv_max_rows(void);
+/* LlmGemvQ8Kernel.Supports(N, K): N % 4 == 0 && K % 32 == 0. */
+L0B_API int32_t l0b_gemv_q8_supports(int32_t n, int32_t k);
+/* LlmGemvQ8Kernel.GroupSize (32). */
+L0B_API int32_t l0b_gemv_q8_group_size(void);
+
+/* ------------------------------------------------------------------------------------------ */
+/* Int8 weight format  (LlmQ8Quantizer.QuantizeOutIn, L/LlmMatrix.cs:89-93)                    */
+/*                                                                                            */
+/* Weights stay in the HuggingFace [out, in] order: words[o*K/4 + i/4] holds the int8 of input  */
+/* i in byte (i % 4), i.e. a row-major int8 [N, K] array. One half scale per `group` inputs     */
+/* per output: scales[o*(K/group) + i/group]; group == K gives per-output-channel scales.       */
+/* Symmetric quantization: s = half(max|w| / 127) over the group, q = clamp(rint(w / s),        */
+/* -127, 127) with rint rounding half to even; an all-zero group gets s = 0 and q = 0.          */
+/* ------------------------------------------------------------------------------------------ */
+
+/* Host quantizer: hf [N, K] fp32 -> words (N*K/4 int32) + scales (N*K/group fp16 bits). */
+L0B_API l0b_status l0b_q8_quantize_out_in(const float* hf, int32_t n, int32_t k, int32_t group,
+                                          int32_t* words, uint16_t* scales);
+/* Device quantizer with the same result: w [N, K] (f32/f16/bf16 buffer) -> q (i8 buffer) + s (f16). */
+L0B_API l0b_status l0b_q8_quantize_device(l0b_suite* suite, l0b_device* dev, int32_t n, int32_t k,
+                                          int32_t group, l0b_buffer* w, l0b_buffer* q, l0b_buffer* s);
+
+/* ------------------------------------------------------------------------------------------ */
+/* Ops of LlmKernelSuite, argument orders as the reference calls them                          */
+/* Activations are f32 buffers as in the reference unless a dtype is stated.                   */
+/* ------------------------------------------------------------------------------------------ */
+
+/* Embedding.Execute(dev, ids, table, out, h, count) -- L/LlmModel.cs:360,424.
+ * out[e] = table[ids[e / h] * h + e % h] for e < count. table: f32/f16/bf16 [vocab, h]. */
+L0B_API l0b_status l0b_embedding_execute(l0b_suite* s, l0b_device* d, l0b_buffer* ids, l0b_buffer* table,
+                                         l0b_buffer* out, int32_t h, int32_t count);
+
+/* RMSNorm.Execute(dev, x, res, w, out, eps, width, rows, addResidual) --
+ * L/LlmDecoderLayer.cs:167,183-184,311-312; L/LlmModel.cs:394.
+ * With add_residual: x += res (in place) first. Then out = x * rsqrt(mean(x^2) + eps) * w per row.
+ * out may alias x (per-head QK-norm). res may be NULL when add_residual == 0. */
+L0B_API l0b_status l0b_rmsnorm_execute(l0b_suite* s, l0b_device* d, l0b_buffer* x, l0b_buffer* res,
+                                       l0b_buffer* w, l0b_buffer* out, float eps, int32_t width,
+                                       int32_t rows, int32_t add_residual);
+
+/* Gemv.Execute(dev, N, K, x, W, y) -- L/LlmMatrix.cs:134,138. W f32/f16 stored [in=K, out=N]
+ * (the reference layout, L/LlmMatrix.cs:5). y[n] = sum_k x[k] * W[k, n]. Requires N % 4 == 0. */
+L0B_API l0b_status l0b_gemv_execute(l0b_suite* s, l0b_device* d, int32_t n, int32_t k, l0b_buffer* x,
+                                    l0b_buffer* w, l0b_buffer* y);
+/* Gemv.ExecuteRows(dev, M, N, K, x, W, y) -- L/LlmMatrix.cs:161,165. X [M, K], Y [M, N]. */
+L0B_API l0b_status l0b_gemv_execute_rows(l0b_suite* s, l0b_device* d, int32_t m, int32_t n, int32_t k,
+                                         l0b_buffer* x, l0b_buffer* w, l0b_buffer* y);
+/* Gemm.Execute(dev, M, N, K, A, B, C) -- L/LlmMatrix.cs:142,169. f32 C[M,N] = A[M,K] * B[K,N]. */
+L0B_API l0b_status l0b_gemm_execute(l0b_suite* s, l0b_device* d, int32_t m, int32_t n, int32_t k,
+                                    l0b_buffer* a, l0b_buffer* b, l0b_buffer* c);
+
+/* GemvQ8.Quantize(dev, rows, K, x, scratch) -- L/LlmMatrix.cs:129,156,201. Stages `rows` rows of
+ * the f32 activations x [rows, K] in the suite's activation scratch (sized by ensure_q8_scratch).
+ * This backend multiplies int8 weights with 16/32-bit activations (W8A16 and wider), so staging
+ * keeps the activations exact (f32) instead of quantizing them. */
+L0B_API l0b_status l0b_gemv_q8_quantize(l0b_suite* s, l0b_device* d, int32_t rows, int32_t k, l0b_buffer* x);
+/* GemvQ8.Execute / ExecuteRows(dev, [M,] N, K, scratch, words, scales, y) -- L/LlmMatrix.cs:130,157,
+ * 235,239. words: i8 (or i32-packed) [N, K]; scales f16 [N, K/32]. Y [M, N] f32. */
+L0B_API l0b_status l0b_gemv_q8_execute(l0b_suite* s, l0b_device* d, int32_t n, int32_t k,
+                                       l0b_buffer* words, l0b_buffer* scales, l0b_buffer* y);
+L0B_API l0b_status l0b_gemv_q8_execute_rows(l0b_suite* s, l0b_device* d, int32_t m, int32_t n, int32_t k,
+                                            l0b_buffer* words, l0b_buffer* scales, l0b_buffer* y);
+
+/* BiasAdd.Execute(dev, x, b, width, rows) -- L/LlmDecoderLayer.cs:303-305,356-358. x[r,:] += b. */
+L0B_API l0b_status l0b_bias_add_execute(l0b_suite* s, l0b_device* d, l0b_buffer* x, l0b_buffer* b,
+                                        int32_t width, int32_t rows);
+
+/* RoPE.Execute(dev, q, k, positions, hd, nH, nKv, theta, tokens) -- L/LlmDecoderLayer.cs:415-417.
+ * HF rotate-half pairing (i, i + hd/2); inverse frequencies theta^(-2i/hd) computed in double and
+ * rounded to f32 (L/RopeFrequencies.cs:75-80); angle = f32(position) * inv_freq in f32. */
+L0B_API l0b_status l0b_rope_execute(l0b_suite* s, l0b_device* d, l0b_buffer* q, l0b_buffer* k,
+                                    l0b_buffer* positions, int32_t head_dim, int32_t n_heads,
+                                    int32_t n_kv_heads, float theta, int32_t tokens);
+/* RoPE.ExecuteWithFrequencies(dev, q, k, positions, invFreq, hd, nH, nKv, attnScale, tokens,
+ * rotaryDim) -- L/LlmDecoderLayer.cs:421-423. Rotates the first rotary_dim elements of each head
+ * with the table inv_freq [rotary_dim/2]; cos and sin are multiplied by attn_scale. */
+L0B_API l0b_status l0b_rope_execute_with_frequencies(l0b_suite* s, l0b_device* d, l0b_buffer* q,
+                                                     l0b_buffer* k, l0b_buffer* positions,
+                                                     l0b_buffer* inv_freq, int32_t head_dim,
+                                                     int32_t n_heads, int32_t n_kv_heads,
+                                                     float attn_scale, int32_t tokens, int32_t rotary_dim);
+
+/* KvCacheStore.Execute / ExecuteRows(dev, k, v, Kc, Vc, pos0, kvDim[, tokens]) --
+ * L/LlmDecoderLayer.cs:322,368. Kc[pos0 + t, :] = k[t, :]; cache dtype f32/f16/bf16. */
+L0B_API l0b_status l0b_kv_cache_store_execute(l0b_suite* s, l0b_device* d, l0b_buffer* k, l0b_buffer* v,
+                                              l0b_buffer* kc, l0b_buffer* vc, int32_t pos0, int32_t kv_dim);
+L0B_API l0b_status l0b_kv_cache_store_execute_rows(l0b_suite* s, l0b_device* d, l0b_buffer* k,
+                                                   l0b_buffer* v, l0b_buffer* kc, l0b_buffer* vc,
+                                                   int32_t pos0, int32_t kv_dim, int32_t tokens);
+
+/* Attention.Execute(dev, q, Kc, Vc, out, hd, nH, nKv, seqLen, maxSeq) -- L/LlmDecoderLayer.cs:325-327.
+ * One query token over cache slots [0, seq_len): out = softmax(q K^T / sqrt(hd)) V per head, query
+ * head h reading kv head h / (nH / nKv). Split-KV with online softmax: no 15000-token cap. */
+L0B_API l0b_status l0b_attention_execute(l0b_suite* s, l0b_device* d, l0b_buffer* q, l0b_buffer* kc,
+                                         l0b_buffer* vc, l0b_buffer* out, int32_t head_dim,
+                                         int32_t n_heads, int32_t n_kv_heads, int32_t seq_len,
+                                         int32_t max_seq);
+/* Attention.ExecutePrefill(dev, q, Kc, Vc, out, hd, nH, nKv, pos0, tokens, maxSeq) --
+ * L/LlmDecoderLayer.cs:369-371. Query t (position pos0 + t) attends to slots [0, pos0 + t]. */
+L0B_API l0b_status l0b_attention_execute_prefill(l0b_suite* s, l0b_device* d, l0b_buffer* q,
+                                                 l0b_buffer* kc, l0b_buffer* vc, l0b_buffer* out,
+                                                 int32_t head_dim, int32_t n_heads, int32_t n_kv_heads,
+                                                 int32_t pos0, int32_t tokens, int32_t max_seq);
+
+/* SigmoidGate.Execute(dev, x, gate, n) -- L/LlmDecoderLayer.cs:330,374. x *= sigmoid(gate). */
+L0B_API l0b_status l0b_sigmoid_gate_execute(l0b_suite* s, l0b_device* d, l0b_buffer* x, l0b_buffer* gate,
+                                            int32_t n);
+/* SwiGLU.Execute(dev, gate, up, n) -- L/LlmDecoderLayer.cs:189,265. gate = silu(gate) * up. */
+L0B_API l0b_status l0b_swiglu_execute(l0b_suite* s, l0b_device* d, l0b_buffer* gate, l0b_buffer* up,
+                                      int32_t n);
+/* Add.Execute(dev, hidden, down, n) -- L/LlmDecoderLayer.cs:194,267. hidden += down. */
+L0B_API l0b_status l0b_add_execute(l0b_suite* s, l0b_device* d, l0b_buffer* hidden, l0b_buffer* down,
+                                   int32_t n);
+/* Copy.Execute(dev, src, dst, offset, n) -- L/LlmModel.cs:368. dst[0, n) = src[offset, offset + n). */
+L0B_API l0b_status l0b_copy_execute(l0b_suite* s, l0b_device* d, l0b_buffer* src, l0b_buffer* dst,
+                                    int32_t offset, int32_t n);
+/* Sampling.Execute(dev, logits, sampled, temperature, randomVal, vocab) -- L/LlmModel.cs:398.
+ * temperature == 0: argmax (lowest index on ties). Otherwise the smallest index whose cumulative
+ * softmax(logits / temperature) mass reaches random_val * total. */
+L0B_API l0b_status l0b_sampling_execute(l0b_suite* s, l0b_device* d, l0b_buffer* logits,
+                                        l0b_buffer* sampled, float temperature, float random_val,
+                                        int32_t vocab);
+
+/* CausalConv.Execute(dev, qkv, convState, convW, out, convDim, k, tokens) -- L/LlmDecoderLayer.cs:392.
+ * Depthwise causal conv1d over [history (k-1 taps, oldest first) ++ tokens], then SiLU; the history
+ * is shifted to hold the last k-1 inputs. convW [convDim, k]. */
+L0B_API l0b_status l0b_causal_conv_execute(l0b_suite* s, l0b_device* d, l0b_buffer* qkv,
+                                           l0b_buffer* conv_state, l0b_buffer* conv_w, l0b_buffer* out,
+                                           int32_t conv_dim, int32_t kernel, int32_t tokens);
+/* GatedDelta.Execute(dev, conv, z, b, a, A_log, dt_bias, normW, S, out, Hv, dk, dv, tokens, eps) --
+ * L/LlmDecoderLayer.cs:393-395. Per token in order: q,k L2-normalised (eps 1e-6), beta = sigmoid(b),
+ * g = -exp(A_log) * softplus(a + dt_bias), S = e^g S, S += k (beta (v - S^T k))^T, o = S^T q / sqrt(dk),
+ * out = rmsnorm(o) * normW * silu(z) per head. The reference requires Hk == Hv. */
+L0B_API l0b_status l0b_gated_delta_execute(l0b_suite* s, l0b_device* d, l0b_buffer* conv, l0b_buffer* z,
+                                           l0b_buffer* b, l0b_buffer* a, l0b_buffer* a_log,
+                                           l0b_buffer* dt_bias, l0b_buffer* norm_w, l0b_buffer* state,
+                                           l0b_buffer* out, int32_t n_v_heads, int32_t key_dim,
+                                           int32_t value_dim, int32_t tokens, float eps);
+/* Same with Hk < Hv (Qwen3.5 grouping: value head h reads key head h / (Hv / Hk)); conv rows are
+ * [q (Hk*dk) | k (Hk*dk) | v (Hv*dv)]. No reference counterpart (the reference rejects Hk != Hv,
+ * L/HfModelConfig.cs:367-370); needed by the Hk=16, Hv=32 DeltaNet configuration. */
+L0B_API l0b_status l0b_gated_delta_execute_grouped(l0b_suite* s, l0b_device* d, l0b_buffer* conv,
+                                                   l0b_buffer* z, l0b_buffer* b, l0b_buffer* a,
+                                                   l0b_buffer* a_log, l0b_buffer* dt_bias,
+                                                   l0b_buffer* norm_w, l0b_buffer* state, l0b_buffer* out,
+                                                   int32_t n_k_heads, int32_t n_v_heads, int32_t key_dim,
+                                                   int32_t value_dim, int32_t tokens, float eps);
+
+/* ------------------------------------------------------------------------------------------ */
+/* Linear layers in the [out, in] layout, and the fused decode ops                              */
+/*                                                                                            */
+/* These take weights in the HuggingFace [out=N, in=K] order for every precision, which is the  */
+/* order the int8 path already uses (L/LlmMatrix.cs:89-93): each output row is one contiguous   */
+/* stream that a warp reads with 128-bit loads and reduces with shuffles.                       */
+/* w dtype: L0B_F32, L0B_F16, L0B_BF16 or L0B_I8 (then `scales` f16 [N, K/group]).             */
+/* ------------------------------------------------------------------------------------------ */
+
+/* Y[M, N] = X[M, K] * W^T (+ bias). X f32/f16/bf16, Y f32/f16/bf16; bias f32 [N] or NULL.
+ * group: int8 scale group (32, or K for per-channel); ignored for 16/32-bit weights.
+ * M of any size: small M streams the weights once per 8 rows on the CUDA cores, large M runs the
+ * tcgen05 tensor-core GEMM (16-bit weights). */
+L0B_API l0b_status l0b_linear(l0b_suite* s, l0b_device* d, int32_t m, int32_t n, int32_t k, l0b_buffer* x,
+                              l0b_buffer* w, l0b_buffer* scales, int32_t group, l0b_buffer* bias,
+                              l0b_buffer* y);
+
+typedef enum l0b_epilogue {
+    L0B_EPI_STORE = 0,  /* out[m, n] = y[m, n] (+ bias) */
+    L0B_EPI_ACCUM = 1,  /* out[m, n] += y[m, n] (+ bias): the residual add of o_proj / down_proj */
+    L0B_EPI_SWIGLU = 2  /* W = [gate; up] (N = 2 * I rows): out[m, i] = silu(y[m, i]) * y[m, i + I] */
+} l0b_epilogue;
+
+/* Fused linear layer of the decode path: optional RMSNorm of each x row with norm_w (eps) as the
+ * prologue (the input / post-attention norm, L/LlmDecoderLayer.cs:167,183-184), then the projection,
+ * then the epilogue. Replaces RMSNorm + ProjectShared(gate, up) + SwiGLU (L/LlmDecoderLayer.cs:183-189)
+ * or Project + Add (:190-194) with one kernel. out is f32. */
+L0B_API l0b_status l0b_linear_fused(l0b_suite* s, l0b_device* d, int32_t m, int32_t n, int32_t k, l0b_buffer* x,
+                                    l0b_buffer* w, l0b_buffer* scales, int32_t group, l0b_buffer* norm_w, float eps,
+                                    int32_t epilogue, l0b_buffer* bias, l0b_buffer* out);
+
+/* Raw-pointer int8 GEMV for callers that manage device memory themselves (config 0 shape:
+ * y[M,N] = x[M,K] * (q * s)^T with fp16 x and y). x_dtype/y_dtype from l0b_dtype. Enqueued on
+ * `stream` (a cudaStream_t, NULL = legacy default stream); returns immediately. */
+L0B_API l0b_status l0b_gemv_w8a16_raw(void* stream, int32_t m, int32_t n, int32_t k, const void* x,
+                                      int32_t x_dtype, const int8_t* q, const uint16_t* scales,
+                                      int32_t group, void* y, int32_t y_dtype);
+
+/* ------------------------------------------------------------------------------------------ */
+/* Decoder model  (C++ mirror of LlmModel / LlmDecoderLayer / LlmMatrix / LlmKvCache,            */
+/*                 L/LlmModel.cs:15-481, L/LlmDecoderLayer.cs:19-534)                          */
+/* ------------------------------------------------------------------------------------------ */
+
+typedef enum l0b_precision {
+    L0B_PRECISION_AUTO = 0,    /* LlmWeightPrecision.Auto -> Int8 (this backend has the int8 kernels) */
+    L0B_PRECISION_FLOAT32 = 1, /* LlmWeightPrecision.Float32 */
+    L0B_PRECISION_FLOAT16 = 2, /* LlmWeightPrecision.Float16 */
+    L0B_PRECISION_INT8 = 3,    /* LlmWeightPrecision.Int8 (scale group: l0b_model_config.q8_group) */
+    L0B_PRECISION_BFLOAT16 = 4 /* bf16 storage (no reference counterpart; Llama-3-70B configuration) */
+} l0b_precision;
+
+typedef enum l0b_rope_type {
+    L0B_ROPE_DEFAULT = 0,
+    L0B_ROPE_LINEAR = 1,
+    L0B_ROPE_YARN = 2,
+    L0B_ROPE_LLAMA3 = 3
+} l0b_rope_type;
+
+/* The fields of HfModelConfig the decoder reads (L/HfModelConfig.cs:132-205). */
+typedef struct l0b_model_config {
+    int32_t hidden_size;
+    int32_t intermediate_size;
+    int32_t num_layers;
+    int32_t num_attention_heads;
+    int32_t num_key_value_heads;
+    int32_t head_dim;
+    int32_t vocab_size;
+    int32_t max_position_embeddings;
+    float rms_norm_eps;
+    double rope_theta;
+    int32_t tie_word_embeddings;
+    int32_t attention_bias;      /* qwen2: q/k/v bias */
+    int32_t qk_norm;             /* qwen3: per-head RMSNorm on q and k */
+    int32_t rope_type;           /* l0b_rope_type */
+    double rope_factor;
+    int32_t rope_original_max_position;
+    double rope_low_freq_factor;
+    double rope_high_freq_factor;
+    double rope_beta_fast;
+    double rope_beta_slow;
+    double rope_attention_factor; /* <= 0: derive (YaRN mscale) */
+    double rope_mscale;           /* YaRN mscale, <= 0 when absent */
+    double rope_mscale_all_dim;   /* YaRN mscale_all_dim, <= 0 when absent */
+    int32_t rope_truncate;        /* YaRN: round the correction range to whole dims (default 1) */
+    double partial_rotary_factor; /* 1.0 = full rotary */
+    int32_t kv_dtype;            /* l0b_dtype of the KV cache: F32 (reference), F16 or BF16 */
+    int32_t q8_group;            /* int8 scale group: 32 (reference) or 0 = per output channel */
+    int32_t tp_size;             /* tensor-parallel ranks (1 = none) */
+    int32_t tp_rank;
+} l0b_model_config;
+
+/* Fills a config with the defaults HfModelConfig.Parse applies. */
+L0B_API l0b_status l0b_model_config_init(l0b_model_config* cfg);
+
+/* RopeFrequencies.Compute(config) -- L/RopeFrequencies.cs:60-107: the inverse frequencies of the
+ * rotary table (rotary_dim / 2 values, written when inv_freq is non-null) and the factor that
+ * multiplies cos and sin, for default / linear / yarn / llama3 scaling. */
+L0B_API l0b_status l0b_rope_frequencies(const l0b_model_config* cfg, float* inv_freq, int32_t capacity,
+                                        int32_t* count, float* attention_factor);
+
+/* Allocates the model (weights, KV caches, per-layer buffers) for max_seq_len positions.
+ * Weights are zero until loaded with l0b_model_set_tensor or l0b_model_init_synthetic.
+ * comm: NULL, or the tensor-parallel communicator when cfg->tp_size > 1. */
+L0B_API l0b_status l0b_model_create(l0b_device* dev, l0b_suite* suite, const l0b_model_config* cfg,
+                                    int32_t max_seq_len, l0b_precision precision, l0b_comm* comm,
+                                    l0b_model** out);
+L0B_API l0b_status l0b_model_free(l0b_model* model);
+/* Loads one HuggingFace-named tensor from host memory (fp32 values in the HF [out, in] order), with
+ * the reference's load-time rules: norm offset, int8 quantization or 16-bit storage, q/gate split
+ * (L/LlmLayerWeights.cs:110-212, L/LlmMatrix.cs:80-106). Names: model.embed_tokens.weight,
+ * model.norm.weight, lm_head.weight, model.layers.{i}.{input_layernorm,post_attention_layernorm}.weight,
+ * model.layers.{i}.self_attn.{q,k,v,o}_proj.weight, ...{q,k,v}_proj.bias, ...{q,k}_norm.weight,
+ * model.layers.{i}.mlp.{gate,up,down}_proj.weight. With tensor parallelism pass the full tensor; the
+ * model keeps its rank's shard. */
+L0B_API l0b_status l0b_model_set_tensor(l0b_model* model, const char* name, const float* data,
+                                        int64_t count);
+/* Seeded synthetic weights generated on the device (no host copy): projections N(0, std) (an
+ * Irwin-Hall(4) approximation of the normal), or for Int8 precision uniform int8 in [-127, 127]
+ * with fp16 scales uniform on [scale_lo, scale_hi]; biases N(0, std); norms 1. */
+L0B_API l0b_status l0b_model_init_synthetic(l0b_model* model, uint64_t seed, float std, float scale_lo,
+                                            float scale_hi);
+/* LlmModel.Prefill(promptIds): resets the sequence, ingests the prompt in chunks of
+ * l0b_gemv_max_rows() tokens and writes the logits of the next token (vocab f32, may be NULL). */
+L0B_API l0b_status l0b_model_prefill(l0b_model* model, const int32_t* ids, int32_t count, float* logits);
+/* LlmModel.Decode(tokenId): one token at Position; writes its logits (may be NULL). */
+L0B_API l0b_status l0b_model_decode(l0b_model* model, int32_t token, float* logits);
+/* LlmModel.ComputeLogits(tokenId, position). */
+L0B_API l0b_status l0b_model_compute_logits(l0b_model* model, int32_t token, int32_t position, float* logits);
+/* LlmModel.GenerateGreedy(promptIds, maxNewTokens, stopTokenIds): tokens (without the prompt) to
+ * out[0, *out_count). The argmax is taken on the device; only token ids cross to the host. */
+L0B_API l0b_status l0b_model_generate_greedy(l0b_model* model, const int32_t* ids, int32_t count,
+                                             int32_t max_new, const int32_t* stop_ids, int32_t n_stop,
+                                             int32_t* out, int32_t* out_count);
+/* LlmModel.Position / ResetSequence / MaxSeqLen / ProjectionBytes. */
+L0B_API l0b_status l0b_model_position(l0b_model* model, int32_t* position);
+L0B_API l0b_status l0b_model_reset_sequence(l0b_model* model);
+L0B_API l0b_status l0b_model_projection_bytes(l0b_model* model, int64_t* bytes);
+/* Runs `steps` greedy decode steps entirely on the device (each step's input is the previous step's
+ * argmax, no host round trip), starting from the last sampled token. Tokens to out (may be NULL).
+ * This is the device-resident throughput path that benchmarks time. */
+L0B_API l0b_status l0b_model_decode_greedy_device(l0b_model* model, int32_t steps, int32_t* out);
+/* Debug mode: run ops without command-list recording (the reference's Probe path). */
+L0B_API l0b_status l0b_model_set_recording(l0b_model* model, int32_t enabled);
+/* Selects the fused decode kernels (1, default) or the one-op-per-reference-call sequence (0). */
+L0B_API l0b_status l0b_model_set_fused(l0b_model* model, int32_t enabled);
+/* Reads layer `layer`'s KV cache rows [row0, row0 + rows) as f32 (CaptureState's KV part,
+ * L/LlmModel.cs:257-281). keys/values hold rows * kvDim floats. */
+L0B_API l0b_status l0b_model_read_kv(l0b_model* model, int32_t layer, int32_t row0, int32_t rows,
+                                     float* keys, float* values);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* L0B200_H */

@@ -1,0 +1,250 @@
+// Decode / prefill attention over the KV cache (sm_100a, CUDA cores).
+//
+// One CTA owns one KV head (and the up-to-8 query heads that share it, GQA), one split of the
+// positions and one query row. K/V tiles of 32 positions are staged in shared memory as fp32 (K rows
+// padded to HD+1 floats so the per-position dot products are bank-conflict free); each warp scores
+// 32 positions for its heads and keeps an online softmax (running max, running sum, rescaled
+// accumulator), so no score buffer grows with the sequence and there is no length cap (the
+// reference's fused kernel stops at 15000 tokens, L/LlmDecoderLayer.cs:21-22).
+//
+// Splits write (m, l, acc) partials; the last CTA of a (query, KV head) to finish -- found with an
+// atomic counter that it resets afterwards -- merges them. With rope/store_new set the kernel also
+// applies RoPE to the query and to the new key, and the CTA owning the query position writes the
+// new key/value row into the cache, replacing the separate RoPE and KvCacheStore launches.
+#include "common.cuh"
+#include "ops.cuh"
+
+namespace l0b {
+
+namespace {
+
+constexpr int kT = 32;     // positions per tile
+constexpr int kMaxG = 8;   // query heads per CTA
+
+__device__ __forceinline__ float rope_elem(const float* head, int d, int rot, int pos, const float* inv_freq,
+                                           float attn_scale) {
+    const float v = head[d];
+    if (d >= rot) return v;
+    const int half = rot >> 1;
+    const int i = d < half ? d : d - half;
+    const float ang = __fmul_rn(static_cast<float>(pos), inv_freq[i]);
+    float s, c;
+    sincosf(ang, &s, &c);
+    c = __fmul_rn(c, attn_scale);
+    s = __fmul_rn(s, attn_scale);
+    if (d < half) return __fsub_rn(__fmul_rn(v, c), __fmul_rn(head[d + half], s));
+    return __fadd_rn(__fmul_rn(v, c), __fmul_rn(head[d - half], s));
+}
+
+template <int HD>
+__global__ void __launch_bounds__(128) attn_kernel(const AttnParams p) {
+    constexpr int HPT = 128 / HD;          // head lanes per dim in the PV phase
+    constexpr int JPT = kMaxG / HPT;       // heads per thread in the PV phase
+    __shared__ float qs[kMaxG][HD];
+    __shared__ float ks[kT][HD + 1];
+    __shared__ float vs[kT][HD];
+    __shared__ float ps[kMaxG][kT];
+    __shared__ float m_s[kMaxG], l_s[kMaxG], corr_s[kMaxG];
+    __shared__ float knew[HD], vnew[HD];
+    __shared__ int last_s;
+
+    const int G = p.nh / p.nkv;
+    const int gparts = (G + kMaxG - 1) / kMaxG;
+    const int kvh = blockIdx.x / gparts, gp = blockIdx.x - (blockIdx.x / gparts) * gparts;
+    const int h0 = kvh * G + gp * kMaxG;
+    const int ng = min(kMaxG, G - gp * kMaxG);
+    const int split = blockIdx.y, b = blockIdx.z;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+
+    pdl_wait();
+    const int qpos = p.positions ? p.positions[b] : p.pos_base + b * p.pos_step;
+    const int seq = qpos + 1;
+    const int nact = (seq + p.chunk - 1) / p.chunk;
+    if (split >= nact) return;
+    pdl_launch_dependents();
+
+    const float* qb = p.q + b * p.q_bstride + static_cast<long long>(h0) * HD;
+    for (int idx = tid; idx < kMaxG * HD; idx += 128) {
+        const int j = idx / HD, d = idx - (idx / HD) * HD;
+        float v = 0.f;
+        if (j < ng) v = p.rope ? rope_elem(qb + j * HD, d, p.rot, qpos, p.inv_freq, p.attn_scale) : qb[j * HD + d];
+        qs[j][d] = v;
+    }
+    if (tid < kMaxG) {
+        m_s[tid] = kNegInf;
+        l_s[tid] = 0.f;
+    }
+    const bool owns_new = p.store_new && split == nact - 1;
+    if (owns_new) {
+        const float* kb = p.k_new + b * p.new_bstride + static_cast<long long>(kvh) * HD;
+        const float* vb = p.v_new + b * p.new_bstride + static_cast<long long>(kvh) * HD;
+        for (int d = tid; d < HD; d += 128) {
+            const float kv = p.rope ? rope_elem(kb, d, p.rot, qpos, p.inv_freq, p.attn_scale) : kb[d];
+            knew[d] = kv;
+            vnew[d] = vb[d];
+            if (gp == 0) {
+                const long long off = b * p.cache_bstride + static_cast<long long>(qpos) * p.kv_dim +
+                                      static_cast<long long>(kvh) * HD + d;
+                store_from_float(p.kc, p.cache_dtype, off, kv);
+                store_from_float(p.vc, p.cache_dtype, off, vb[d]);
+            }
+        }
+    }
+    __syncthreads();
+
+    float acc[JPT];
+#pragma unroll
+    for (int i = 0; i < JPT; ++i) acc[i] = 0.f;
+    const int dim = tid % HD, jb = tid / HD;
+
+    const int p_begin = split * p.chunk;
+    const int p_end = min(seq, p_begin + p.chunk);
+    const long long cache_base = b * p.cache_bstride + static_cast<long long>(kvh) * HD;
+    for (int t0 = p_begin; t0 < p_end; t0 += kT) {
+        for (int idx = tid; idx < kT * HD; idx += 128) {
+            const int t = idx / HD, d = idx - (idx / HD) * HD;
+            const int pos = t0 + t;
+            float kv = 0.f, vv = 0.f;
+            if (pos < p_end) {
+                if (owns_new && pos == qpos) {
+                    kv = knew[d];
+                    vv = vnew[d];
+                } else {
+                    const long long off = cache_base + static_cast<long long>(pos) * p.kv_dim + d;
+                    kv = load_as_float(p.kc, p.cache_dtype, off);
+                    vv = load_as_float(p.vc, p.cache_dtype, off);
+                }
+            }
+            ks[t][d] = kv;
+            vs[t][d] = vv;
+        }
+        __syncthreads();
+        for (int j = warp; j < ng; j += 4) {
+            float s = kNegInf;
+            if (t0 + lane < p_end) {
+                float a = 0.f;
+#pragma unroll 16
+                for (int d = 0; d < HD; ++d) a = fmaf(qs[j][d], ks[lane][d], a);
+                s = a * p.scale;
+            }
+            const float mx = warp_max(s);
+            const float m_old = m_s[j];
+            const float m_new = fmaxf(m_old, mx);
+            const float pj = s == kNegInf ? 0.f : expf(s - m_new);
+            const float sum = warp_sum(pj);
+            ps[j][lane] = pj;
+            __syncwarp();
+            if (lane == 0) {
+                const float corr = expf(m_old - m_new);
+                corr_s[j] = corr;
+                l_s[j] = l_s[j] * corr + sum;
+                m_s[j] = m_new;
+            }
+        }
+        __syncthreads();
+#pragma unroll
+        for (int i = 0; i < JPT; ++i) {
+            const int j = jb + i * HPT;
+            if (j < ng) {
+                float a = acc[i] * corr_s[j];
+#pragma unroll 8
+                for (int t = 0; t < kT; ++t) a = fmaf(ps[j][t], vs[t][dim], a);
+                acc[i] = a;
+            }
+        }
+        __syncthreads();
+    }
+
+    if (nact == 1) {
+#pragma unroll
+        for (int i = 0; i < JPT; ++i) {
+            const int j = jb + i * HPT;
+            if (j < ng) p.out[b * p.out_bstride + static_cast<long long>(h0 + j) * HD + dim] = acc[i] / l_s[j];
+        }
+        return;
+    }
+
+    const long long row = static_cast<long long>(b) * p.nh;
+#pragma unroll
+    for (int i = 0; i < JPT; ++i) {
+        const int j = jb + i * HPT;
+        if (j < ng) p.part[((row + h0 + j) * p.max_splits + split) * HD + dim] = acc[i];
+    }
+    if (tid < ng) {
+        float* ml = p.part_ml + ((row + h0 + tid) * p.max_splits + split) * 2;
+        ml[0] = m_s[tid];
+        ml[1] = l_s[tid];
+    }
+    __threadfence();
+    __syncthreads();
+    unsigned* counter = p.counters + (static_cast<long long>(b) * p.nkv + kvh) * gparts + gp;
+    if (tid == 0) last_s = atomicAdd(counter, 1u) == static_cast<unsigned>(nact - 1);
+    __syncthreads();
+    if (!last_s) return;
+    __threadfence();
+#pragma unroll
+    for (int i = 0; i < JPT; ++i) {
+        const int j = jb + i * HPT;
+        if (j >= ng) continue;
+        const float* ml = p.part_ml + (row + h0 + j) * p.max_splits * 2;
+        const float* pa = p.part + (row + h0 + j) * p.max_splits * HD;
+        float mmax = kNegInf;
+        for (int s = 0; s < nact; ++s) mmax = fmaxf(mmax, __ldcg(ml + 2 * s));
+        float lsum = 0.f, o = 0.f;
+        for (int s = 0; s < nact; ++s) {
+            const float w = expf(__ldcg(ml + 2 * s) - mmax);
+            lsum = fmaf(w, __ldcg(ml + 2 * s + 1), lsum);
+            o = fmaf(w, __ldcg(pa + static_cast<long long>(s) * HD + dim), o);
+        }
+        p.out[b * p.out_bstride + static_cast<long long>(h0 + j) * HD + dim] = o / lsum;
+    }
+    if (tid == 0) *counter = 0u;
+}
+
+template <typename F>
+l0b_status launch_attn(l0b_device* d, cudaStream_t stream, F kernel, dim3 grid, const AttnParams& p) {
+    if (d) return d->launch(kernel, grid, dim3(128), 0, p);
+    kernel<<<grid, 128, 0, stream>>>(p);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return fail(L0B_ERR_CUDA, "attention launch failed: %s", cudaGetErrorString(e));
+    add_launches(1);
+    return L0B_OK;
+}
+
+l0b_status attention_any(l0b_device* d, cudaStream_t stream, const AttnParams& p, int batch) {
+    L0B_REQUIRE(p.nkv > 0 && p.nh % p.nkv == 0, L0B_ERR_ARGUMENT, "heads %d not a multiple of kv heads %d", p.nh,
+                p.nkv);
+    L0B_REQUIRE(p.chunk > 0 && p.max_splits > 0, L0B_ERR_ARGUMENT, "bad split configuration");
+    const int G = p.nh / p.nkv;
+    const int gparts = (G + kMaxG - 1) / kMaxG;
+    dim3 grid(p.nkv * gparts, p.max_splits, batch);
+    switch (p.hd) {
+        case 64: return launch_attn(d, stream, attn_kernel<64>, grid, p);
+        case 128: return launch_attn(d, stream, attn_kernel<128>, grid, p);
+        default: return fail(L0B_ERR_UNSUPPORTED, "attention head_dim %d is not supported (64, 128)", p.hd);
+    }
+}
+
+}  // namespace
+
+l0b_status attention_launch(l0b_device* d, const AttnParams& p, int batch) {
+    return attention_any(d, d->stream, p, batch);
+}
+
+l0b_status attention_launch_stream(cudaStream_t stream, const AttnParams& p, int batch) {
+    return attention_any(nullptr, stream, p, batch);
+}
+
+size_t attention_part_floats(int batch, int nh, int max_splits, int hd) {
+    return static_cast<size_t>(batch) * nh * max_splits * (hd + 2);
+}
+
+void attention_pick_split(int max_seq, int work_items, int sm_count, int* chunk, int* max_splits) {
+    (void)work_items;
+    (void)sm_count;
+    int c = max_seq <= 2048 ? 64 : 128;
+    *chunk = c;
+    *max_splits = (max_seq + c - 1) / c;
+}
+
+}  // namespace l0b

@@ -1,0 +1,475 @@
+// Weight-streaming linear layers for decode and small batches (sm_100a).
+//
+// Layout: W is [N, K] row-major (HuggingFace [out, in]); every output row is one contiguous stream.
+// A warp owns RPW consecutive rows; each lane reads 16 bytes per row per step with a no-L1-allocate
+// 128-bit load, so a warp step moves 512 contiguous bytes per row. int8 weights are dequantised in
+// registers (exact byte -> fp32 trick, see dequant_i8x4) and multiplied in fp32 with packed f32x2
+// FMAs; the per-lane partial sums are reduced with warp shuffles. Activations are staged once per
+// CTA in shared memory as fp32, permuted lane-major so the 128-bit shared loads are conflict-free,
+// and optionally RMS-normalised on the way in (fused input/post-attention norm).
+//
+// The kernel is launched with programmatic dependent launch: before griddepcontrol.wait it
+// prefetches its first weight block into L2 (weights never depend on the previous kernel), so the
+// weight stream starts while the producer of x is still draining.
+#include "common.cuh"
+#include "gemv.cuh"
+
+namespace l0b {
+
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kWarps = kThreads / 32;
+
+// Position of element r (0 <= r < 32*VEC) of a 32*VEC-element chunk in the lane-major smem layout:
+// the j-th float4 of lane l lives at j*128 + l*4.
+template <int VEC>
+__device__ __forceinline__ int xs_perm(int r) {
+    const int l = r / VEC, j = (r % VEC) >> 2, e = r & 3;
+    return j * 128 + l * 4 + e;
+}
+
+__device__ __forceinline__ void epilogue_store(const GemvParams& p, int n, int m, float v) {
+    int s = 0;
+    while (s < p.nseg - 1 && n >= p.seg[s].row_end) ++s;
+    const int begin = s ? p.seg[s - 1].row_end : 0;
+    const int local = n - begin;
+    const GemvSeg& g = p.seg[s];
+    if (g.bias) v += g.bias[local];
+    const long long idx = static_cast<long long>(m) * g.ld + local;
+    if (p.epi == EPI_ACCUM) {
+        float* o = static_cast<float*>(g.out);
+        o[idx] += v;
+    } else if (p.epi == EPI_ARGMAX) {
+        if (g.out) store_from_float(g.out, p.out_dtype, idx, v);
+        atomicMax(p.argmax + m, argmax_key(v, n));
+    } else {
+        store_from_float(g.out, p.out_dtype, idx, v);
+    }
+}
+
+template <typename WT, int MR, int RPW>
+__global__ void __launch_bounds__(kThreads) gemv_nk_kernel(const GemvParams p) {
+    extern __shared__ float4 smem_f4[];
+    float* xs = reinterpret_cast<float*>(smem_f4);
+    __shared__ float rstd_s[MR];
+    constexpr int VEC = 16 / sizeof(WT);
+    constexpr int CH = 32 * VEC;  // elements per warp step
+    constexpr int ROWS = kWarps * RPW;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int N = p.N, K = p.K, M = p.M, kt = p.kt;
+    // SwiGLU: W is [gate; up] stacked, a warp owns pair i = (row i, row i + N/2); else RPW rows.
+    const bool swiglu = p.epi == EPI_SWIGLU;
+    const int half_n = N >> 1;
+    const int units = swiglu ? half_n : N;
+    const int per_cta = swiglu ? kWarps * (RPW / 2) : ROWS;
+    const int nblocks = (units + per_cta - 1) / per_cta;
+
+    if (p.prefetch && threadIdx.x == 0 && blockIdx.x < nblocks) {
+        const long long u0 = static_cast<long long>(blockIdx.x) * per_cta;
+        const long long u1 = min(u0 + per_cta, static_cast<long long>(units));
+        const long long row_bytes = K * static_cast<long long>(sizeof(WT));
+        for (int part = 0; part < (swiglu ? 2 : 1); ++part) {
+            const char* base = static_cast<const char*>(p.w) + (u0 + part * half_n) * row_bytes;
+            const long long bytes = (u1 - u0) * row_bytes;
+            for (long long off = 0; off < bytes; off += 32768) {
+                const long long len = min(32768LL, bytes - off);
+                prefetch_l2_bulk(base + off, static_cast<uint32_t>(len));
+            }
+        }
+    }
+    pdl_wait();
+    pdl_launch_dependents();
+
+    // RMS of each activation row (fused norm), read straight from global memory.
+    if (p.norm_w) {
+        for (int m = warp; m < MR; m += kWarps) {
+            float ss = 0.f;
+            if (m < M) {
+                for (int k = lane; k < K; k += 32) {
+                    const float v = load_as_float(p.x, p.x_dtype, m * p.x_ld + k);
+                    ss += v * v;
+                }
+            }
+            ss = warp_sum(ss);
+            if (lane == 0) rstd_s[m] = 1.0f / sqrtf(ss / static_cast<float>(K) + p.eps);
+        }
+        __syncthreads();
+    }
+
+    auto stage = [&](int k0) {
+        const int span = MR * kt;
+        for (int idx = threadIdx.x; idx < span; idx += kThreads) {
+            const int m = idx / kt, r = idx - m * kt;
+            const int k = k0 + r;
+            float v = 0.f;
+            if (m < M && k < K) {
+                v = load_as_float(p.x, p.x_dtype, m * p.x_ld + k);
+                if (p.norm_w) v = (v * rstd_s[m]) * p.norm_w[k];
+            }
+            const int c = r / CH;
+            xs[m * kt + c * CH + xs_perm<VEC>(r - c * CH)] = v;
+        }
+    };
+
+    const bool single_tile = K <= kt;
+    if (single_tile) {
+        stage(0);
+        __syncthreads();
+    }
+    const bool per_channel = sizeof(WT) == 1 && p.group >= K;
+    const int groups_per_row = sizeof(WT) == 1 ? K / p.group : 0;
+    const __half* scales = static_cast<const __half*>(p.scales);
+
+    for (int blk = blockIdx.x; blk < nblocks; blk += gridDim.x) {
+        const int unit0 = swiglu ? blk * per_cta + warp * (RPW / 2) : blk * ROWS + warp * RPW;
+        float2 acc[RPW][MR];
+#pragma unroll
+        for (int r = 0; r < RPW; ++r)
+#pragma unroll
+            for (int m = 0; m < MR; ++m) acc[r][m] = make_float2(0.f, 0.f);
+
+        const WT* wrow[RPW];
+        int rowi[RPW];
+        bool valid[RPW];
+#pragma unroll
+        for (int r = 0; r < RPW; ++r) {
+            rowi[r] = swiglu ? unit0 + (r & 1) * half_n + (r >> 1) : unit0 + r;
+            valid[r] = swiglu ? unit0 + (r >> 1) < half_n : rowi[r] < N;
+            wrow[r] = static_cast<const WT*>(p.w) + static_cast<long long>(valid[r] ? rowi[r] : 0) * K;
+        }
+
+        for (int k0 = 0; k0 < K; k0 += kt) {
+            if (!single_tile) {
+                __syncthreads();
+                stage(k0);
+                __syncthreads();
+            }
+            const int klen = min(kt, K - k0);
+            int kk = lane * VEC;
+            uint4 cur[RPW];
+#pragma unroll
+            for (int r = 0; r < RPW; ++r)
+                cur[r] = (kk < klen && valid[r]) ? ld_stream_v4(wrow[r] + k0 + kk) : make_uint4(0, 0, 0, 0);
+            for (; kk < klen; kk += CH) {
+                uint4 nxt[RPW];
+                const bool more = kk + CH < klen;
+#pragma unroll
+                for (int r = 0; r < RPW; ++r)
+                    nxt[r] = (more && valid[r]) ? ld_stream_v4(wrow[r] + k0 + kk + CH) : make_uint4(0, 0, 0, 0);
+                const int cbase = (kk / CH) * CH;  // chunk start within the tile
+#pragma unroll
+                for (int m = 0; m < MR; ++m) {
+                    const float* xb = xs + m * kt + cbase + lane * 4;
+                    if constexpr (sizeof(WT) == 1) {
+                        const float4 x0 = *reinterpret_cast<const float4*>(xb);
+                        const float4 x1 = *reinterpret_cast<const float4*>(xb + 128);
+                        const float4 x2 = *reinterpret_cast<const float4*>(xb + 256);
+                        const float4 x3 = *reinterpret_cast<const float4*>(xb + 384);
+#pragma unroll
+                        for (int r = 0; r < RPW; ++r) {
+                            float2 a = per_channel ? acc[r][m] : make_float2(0.f, 0.f);
+                            float2 lo, hi;
+                            dequant_i8x4(cur[r].x, lo, hi);
+                            a = ffma2(lo, make_float2(x0.x, x0.y), a);
+                            a = ffma2(hi, make_float2(x0.z, x0.w), a);
+                            dequant_i8x4(cur[r].y, lo, hi);
+                            a = ffma2(lo, make_float2(x1.x, x1.y), a);
+                            a = ffma2(hi, make_float2(x1.z, x1.w), a);
+                            dequant_i8x4(cur[r].z, lo, hi);
+                            a = ffma2(lo, make_float2(x2.x, x2.y), a);
+                            a = ffma2(hi, make_float2(x2.z, x2.w), a);
+                            dequant_i8x4(cur[r].w, lo, hi);
+                            a = ffma2(lo, make_float2(x3.x, x3.y), a);
+                            a = ffma2(hi, make_float2(x3.z, x3.w), a);
+                            if (per_channel) {
+                                acc[r][m] = a;
+                            } else if (valid[r]) {
+                                const float s = __half2float(
+                                    scales[static_cast<long long>(rowi[r]) * groups_per_row + (k0 + kk) / p.group]);
+                                acc[r][m] = ffma2(a, make_float2(s, s), acc[r][m]);
+                            }
+                        }
+                    } else if constexpr (sizeof(WT) == 2) {
+                        const float4 x0 = *reinterpret_cast<const float4*>(xb);
+                        const float4 x1 = *reinterpret_cast<const float4*>(xb + 128);
+#pragma unroll
+                        for (int r = 0; r < RPW; ++r) {
+                            float2 w0, w1, w2, w3;
+                            if constexpr (DT<WT>::id == L0B_F16) {
+                                w0 = half2_bits_to_float2(cur[r].x);
+                                w1 = half2_bits_to_float2(cur[r].y);
+                                w2 = half2_bits_to_float2(cur[r].z);
+                                w3 = half2_bits_to_float2(cur[r].w);
+                            } else {
+                                w0 = bf162_bits_to_float2(cur[r].x);
+                                w1 = bf162_bits_to_float2(cur[r].y);
+                                w2 = bf162_bits_to_float2(cur[r].z);
+                                w3 = bf162_bits_to_float2(cur[r].w);
+                            }
+                            float2 a = acc[r][m];
+                            a = ffma2(w0, make_float2(x0.x, x0.y), a);
+                            a = ffma2(w1, make_float2(x0.z, x0.w), a);
+                            a = ffma2(w2, make_float2(x1.x, x1.y), a);
+                            a = ffma2(w3, make_float2(x1.z, x1.w), a);
+                            acc[r][m] = a;
+                        }
+                    } else {
+                        const float4 x0 = *reinterpret_cast<const float4*>(xb);
+#pragma unroll
+                        for (int r = 0; r < RPW; ++r) {
+                            float2 a = acc[r][m];
+                            a = ffma2(make_float2(__uint_as_float(cur[r].x), __uint_as_float(cur[r].y)),
+                                      make_float2(x0.x, x0.y), a);
+                            a = ffma2(make_float2(__uint_as_float(cur[r].z), __uint_as_float(cur[r].w)),
+                                      make_float2(x0.z, x0.w), a);
+                            acc[r][m] = a;
+                        }
+                    }
+                }
+#pragma unroll
+                for (int r = 0; r < RPW; ++r) cur[r] = nxt[r];
+            }
+        }
+
+        // Reduce across the warp and run the epilogue; results are spread over lanes for the stores.
+        float res[RPW][MR];
+#pragma unroll
+        for (int r = 0; r < RPW; ++r)
+#pragma unroll
+            for (int m = 0; m < MR; ++m) {
+                float v = warp_sum(acc[r][m].x + acc[r][m].y);
+                if (per_channel && valid[r]) v *= __half2float(scales[rowi[r]]);
+                res[r][m] = v;
+            }
+        if (swiglu) {
+#pragma unroll
+            for (int r = 0; r < RPW; r += 2)
+#pragma unroll
+                for (int m = 0; m < MR; ++m)
+                    if (lane == ((r * MR + m) & 31) && m < M && valid[r])
+                        epilogue_store(p, unit0 + (r >> 1), m, silu(res[r][m]) * res[r + 1][m]);
+        } else {
+#pragma unroll
+            for (int r = 0; r < RPW; ++r)
+#pragma unroll
+                for (int m = 0; m < MR; ++m)
+                    if (lane == ((r * MR + m) & 31) && m < M && valid[r]) epilogue_store(p, rowi[r], m, res[r][m]);
+        }
+    }
+}
+
+// Generic fallback for shapes the vector kernel does not take (K not a multiple of the vector
+// width or unaligned rows): one warp per (row, activation row), scalar loads.
+template <typename WT>
+__global__ void __launch_bounds__(kThreads) gemv_nk_scalar_kernel(const GemvParams p) {
+    pdl_wait();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const long long gw = static_cast<long long>(blockIdx.x) * kWarps + warp;
+    const int pairs = p.epi == EPI_SWIGLU;
+    const long long outs = pairs ? p.N / 2 : p.N;
+    if (gw >= outs * p.M) return;
+    const int m = static_cast<int>(gw / outs);
+    const int n = static_cast<int>(gw - static_cast<long long>(m) * outs);
+    float rstd = 1.f;
+    if (p.norm_w) {
+        float ss = 0.f;
+        for (int k = lane; k < p.K; k += 32) {
+            const float v = load_as_float(p.x, p.x_dtype, m * p.x_ld + k);
+            ss += v * v;
+        }
+        ss = warp_sum(ss);
+        rstd = 1.0f / sqrtf(ss / static_cast<float>(p.K) + p.eps);
+    }
+    const __half* scales = static_cast<const __half*>(p.scales);
+    float res[2];
+    for (int t = 0; t <= pairs; ++t) {
+        const int row = pairs ? n + t * (p.N / 2) : n;
+        const WT* w = static_cast<const WT*>(p.w) + static_cast<long long>(row) * p.K;
+        float acc = 0.f;
+        for (int k = lane; k < p.K; k += 32) {
+            float xv = load_as_float(p.x, p.x_dtype, m * p.x_ld + k);
+            if (p.norm_w) xv = (xv * rstd) * p.norm_w[k];
+            float wv;
+            if constexpr (sizeof(WT) == 1) {
+                const int gpr = p.K / p.group;
+                wv = static_cast<float>(w[k]) * __half2float(scales[static_cast<long long>(row) * gpr + k / p.group]);
+            } else if constexpr (DT<WT>::id == L0B_F16) {
+                wv = __half2float(w[k]);
+            } else if constexpr (DT<WT>::id == L0B_BF16) {
+                wv = __bfloat162float(w[k]);
+            } else {
+                wv = w[k];
+            }
+            acc = fmaf(wv, xv, acc);
+        }
+        res[t] = warp_sum(acc);
+    }
+    if (lane == 0) epilogue_store(p, n, m, pairs ? silu(res[0]) * res[1] : res[0]);
+}
+
+template <typename F, typename... A>
+l0b_status launch_on(l0b_device* dev, cudaStream_t stream, F kernel, dim3 g, dim3 b, size_t smem, A... args) {
+    if (dev) return dev->launch(kernel, g, b, smem, args...);
+    kernel<<<g, b, smem, stream>>>(args...);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return fail(L0B_ERR_CUDA, "kernel launch failed: %s", cudaGetErrorString(e));
+    add_launches(1);
+    return L0B_OK;
+}
+
+template <typename WT, int MR>
+l0b_status launch_vec(l0b_device* dev, cudaStream_t stream, int sm_count, const GemvParams& p) {
+    constexpr int RPW = 2;
+    constexpr int ROWS = kWarps * RPW;
+    auto kernel = gemv_nk_kernel<WT, MR, RPW>;
+    const size_t smem = static_cast<size_t>(MR) * p.kt * sizeof(float);
+    static bool configured = false;
+    if (!configured) {
+        cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+        if (e != cudaSuccess) return fail(L0B_ERR_CUDA, "cudaFuncSetAttribute failed: %s", cudaGetErrorString(e));
+        configured = true;
+    }
+    const int units = p.epi == EPI_SWIGLU ? p.N / 2 : p.N;
+    const int per_cta = p.epi == EPI_SWIGLU ? kWarps * (RPW / 2) : ROWS;
+    const int nblocks = (units + per_cta - 1) / per_cta;
+    const int grid = nblocks < sm_count * 16 ? nblocks : sm_count * 16;
+    return launch_on(dev, stream, kernel, dim3(grid), dim3(kThreads), smem, p);
+}
+
+template <typename WT>
+l0b_status launch_typed(l0b_device* dev, cudaStream_t stream, int sm_count, GemvParams p) {
+    constexpr int VEC = 16 / sizeof(WT);
+    constexpr int CH = 32 * VEC;
+    const bool vec_ok = (p.K % VEC == 0) && (reinterpret_cast<uintptr_t>(p.w) % 16 == 0) &&
+                        (sizeof(WT) != 1 || (p.group % 16 == 0 && p.K % p.group == 0));
+    const int M = p.M;
+    for (int m0 = 0; m0 < M; m0 += 8) {
+        GemvParams q = p;
+        const int mr = M - m0 < 8 ? M - m0 : 8;
+        q.M = mr;
+        q.x = static_cast<const char*>(p.x) + static_cast<size_t>(m0) * p.x_ld * dtype_size((l0b_dtype)p.x_dtype);
+        for (int s = 0; s < q.nseg; ++s) {
+            if (!q.seg[s].out) continue;
+            const size_t es = (p.epi == EPI_ACCUM) ? 4 : dtype_size((l0b_dtype)p.out_dtype);
+            q.seg[s].out = static_cast<char*>(q.seg[s].out) + static_cast<size_t>(m0) * q.seg[s].ld * es;
+        }
+        if (q.argmax) q.argmax += m0;
+        if (!vec_ok) {
+            const long long outs = (p.epi == EPI_SWIGLU ? p.N / 2 : p.N) * static_cast<long long>(mr);
+            const int grid = static_cast<int>((outs + kWarps - 1) / kWarps);
+            L0B_TRY(launch_on(dev, stream, gemv_nk_scalar_kernel<WT>, dim3(grid), dim3(kThreads), 0, q));
+            continue;
+        }
+        // Shared-memory tile of x: the whole row when it fits (~100 KB), else multiples of a chunk.
+        const int mpad = mr <= 1 ? 1 : mr <= 2 ? 2 : mr <= 4 ? 4 : 8;
+        const int kpad = (p.K + CH - 1) / CH * CH;
+        const int budget = 100 * 1024 / (4 * mpad);
+        q.kt = kpad <= budget ? kpad : (budget / CH) * CH;
+        switch (mpad) {
+            case 1: L0B_TRY((launch_vec<WT, 1>(dev, stream, sm_count, q))); break;
+            case 2: L0B_TRY((launch_vec<WT, 2>(dev, stream, sm_count, q))); break;
+            case 4: L0B_TRY((launch_vec<WT, 4>(dev, stream, sm_count, q))); break;
+            default: L0B_TRY((launch_vec<WT, 8>(dev, stream, sm_count, q))); break;
+        }
+    }
+    return L0B_OK;
+}
+
+l0b_status gemv_dispatch(l0b_device* dev, cudaStream_t stream, int sm_count, int w_dtype, GemvParams p) {
+    L0B_REQUIRE(p.N > 0 && p.K > 0 && p.M > 0, L0B_ERR_OUT_OF_RANGE, "GEMV shape M=%d N=%d K=%d", p.M, p.N, p.K);
+    L0B_REQUIRE(p.epi != EPI_SWIGLU || p.N % 2 == 0, L0B_ERR_ARGUMENT, "SwiGLU-fused GEMV needs an even row count");
+    L0B_REQUIRE(p.nseg >= 1 && p.nseg <= 4, L0B_ERR_ARGUMENT, "1..4 output segments");
+    switch (w_dtype) {
+        case L0B_I8:
+            L0B_REQUIRE(p.scales && p.group > 0 && p.K % p.group == 0, L0B_ERR_ARGUMENT,
+                        "int8 weights need scales and a group dividing K (group %d, K %d)", p.group, p.K);
+            return launch_typed<int8_t>(dev, stream, sm_count, p);
+        case L0B_F16: return launch_typed<__half>(dev, stream, sm_count, p);
+        case L0B_BF16: return launch_typed<__nv_bfloat16>(dev, stream, sm_count, p);
+        case L0B_F32: return launch_typed<float>(dev, stream, sm_count, p);
+        default: return fail(L0B_ERR_UNSUPPORTED, "weight dtype %d is not supported", w_dtype);
+    }
+}
+
+// ---------------------------------------------------------------------------------------------
+// Reference layout W [K, N]: y[m, n] = sum_k x[m, k] * W[k, n]. A CTA owns 64 columns (16 threads
+// x 4 columns, one 8/16-byte load per row) and splits K over 16 thread rows; partial sums are
+// reduced through shared memory. Used by the reference-surface Gemv ops only.
+// ---------------------------------------------------------------------------------------------
+template <typename WT>
+__global__ void __launch_bounds__(256) gemv_kn_kernel(int M, int N, int K, const float* __restrict__ x,
+                                                      const WT* __restrict__ w, float* __restrict__ y) {
+    __shared__ float red[16][65];
+    pdl_wait();
+    const int tc = threadIdx.x & 15, tr = threadIdx.x >> 4;
+    const int n0 = blockIdx.x * 64 + tc * 4;
+    const int m = blockIdx.y;
+    float a[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int k = tr; k < K; k += 16) {
+        const float xv = x[static_cast<long long>(m) * K + k];
+        const WT* row = w + static_cast<long long>(k) * N;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            if (n0 + c < N) {
+                float wv;
+                if constexpr (sizeof(WT) == 2) wv = __half2float(row[n0 + c]);
+                else wv = row[n0 + c];
+                a[c] = fmaf(xv, wv, a[c]);
+            }
+        }
+    }
+#pragma unroll
+    for (int c = 0; c < 4; ++c) red[tr][tc * 4 + c] = a[c];
+    __syncthreads();
+    if (threadIdx.x < 64) {
+        float s = 0.f;
+#pragma unroll
+        for (int r = 0; r < 16; ++r) s += red[r][threadIdx.x];
+        const int n = blockIdx.x * 64 + threadIdx.x;
+        if (n < N) y[static_cast<long long>(m) * N + n] = s;
+    }
+}
+
+__global__ void __launch_bounds__(256) gemm_f32_kernel(int M, int N, int K, const float* __restrict__ A,
+                                                       const float* __restrict__ B, float* __restrict__ C) {
+    __shared__ float As[16][17], Bs[16][17];
+    pdl_wait();
+    const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+    const int row = blockIdx.y * 16 + ty, col = blockIdx.x * 16 + tx;
+    float acc = 0.f;
+    for (int k0 = 0; k0 < K; k0 += 16) {
+        As[ty][tx] = (row < M && k0 + tx < K) ? A[static_cast<long long>(row) * K + k0 + tx] : 0.f;
+        Bs[ty][tx] = (k0 + ty < K && col < N) ? B[static_cast<long long>(k0 + ty) * N + col] : 0.f;
+        __syncthreads();
+#pragma unroll
+        for (int kk = 0; kk < 16; ++kk) acc = fmaf(As[ty][kk], Bs[kk][tx], acc);
+        __syncthreads();
+    }
+    if (row < M && col < N) C[static_cast<long long>(row) * N + col] = acc;
+}
+
+}  // namespace
+
+l0b_status gemv_nk_launch(l0b_device* dev, int w_dtype, GemvParams p) {
+    return gemv_dispatch(dev, dev->stream, dev->sm_count, w_dtype, p);
+}
+
+l0b_status gemv_nk_launch_stream(cudaStream_t stream, int sm_count, int w_dtype, GemvParams p) {
+    return gemv_dispatch(nullptr, stream, sm_count, w_dtype, p);
+}
+
+l0b_status gemv_kn_launch(l0b_device* dev, int w_dtype, int m, int n, int k, const float* x, const void* w,
+                          float* y) {
+    dim3 grid((n + 63) / 64, m);
+    if (w_dtype == L0B_F16)
+        return dev->launch(gemv_kn_kernel<__half>, grid, dim3(256), 0, m, n, k, x, static_cast<const __half*>(w), y);
+    return dev->launch(gemv_kn_kernel<float>, grid, dim3(256), 0, m, n, k, x, static_cast<const float*>(w), y);
+}
+
+l0b_status gemm_f32_launch(l0b_device* dev, int m, int n, int k, const float* a, const float* b, float* c) {
+    dim3 grid((n + 15) / 16, (m + 15) / 16);
+    return dev->launch(gemm_f32_kernel, grid, dim3(256), 0, m, n, k, a, b, c);
+}
+
+}  // namespace l0b

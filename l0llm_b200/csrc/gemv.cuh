@@ -1,0 +1,55 @@
+// Weight-streaming GEMV/GEMM-by-rows for the [out, in] weight layout, with fused prologue and
+// epilogues. Host-side launch helpers are declared here and used by ops.cu and model.cu.
+#pragma once
+
+#include "runtime.h"
+
+namespace l0b {
+
+enum GemvEpi : int {
+    EPI_STORE = 0,   // out[m, n - seg_begin] = y (+ bias)
+    EPI_ACCUM = 1,   // out[m, n] += y               (residual add, f32 out)
+    EPI_SWIGLU = 2,  // W = [gate; up] stacked: out[m, i] = silu(y[i]) * y[i + N/2]
+    EPI_ARGMAX = 3   // store logits (optional) and fold argmax into a 64-bit key per row
+};
+
+struct GemvSeg {
+    void* out;          // output base
+    const float* bias;  // f32 [segment width] or null
+    int row_end;        // exclusive end of this segment in W's rows (SWIGLU: in output columns)
+    int ld;             // output row stride in elements
+};
+
+struct GemvParams {
+    const void* w;         // [N, K] row-major weights
+    const void* scales;    // int8: f16 [N, K / group]
+    int group;             // int8 scale group; >= K means one scale per output row
+    int N, K, M;           // W rows, inner dim, activation rows
+    const void* x;         // activations [M, K] (x_dtype), row stride x_ld
+    int x_dtype;
+    long long x_ld;
+    const float* norm_w;   // fused RMSNorm of x rows before use (null = off)
+    float eps;
+    int epi;
+    int out_dtype;
+    int nseg;
+    GemvSeg seg[4];
+    unsigned long long* argmax;  // [M] keys for EPI_ARGMAX
+    int kt;                      // K elements per shared-memory tile (a multiple of 512)
+    int prefetch;                // prefetch the first row block of weights into L2 before pdl_wait
+};
+
+// Launches y = x * W^T with the fused options in `p` (fills kt and the grid). `w_dtype` is
+// L0B_I8 / L0B_F16 / L0B_BF16 / L0B_F32. Rows of x are processed in groups of up to 8 per pass.
+l0b_status gemv_nk_launch(l0b_device* dev, int w_dtype, GemvParams p);
+
+// Raw-stream variant (no device handle): immediate launch on `stream`.
+l0b_status gemv_nk_launch_stream(cudaStream_t stream, int sm_count, int w_dtype, GemvParams p);
+
+// Reference layout [K, N] (y = x * W): Gemv.Execute/ExecuteRows for f32/f16 weights.
+l0b_status gemv_kn_launch(l0b_device* dev, int w_dtype, int m, int n, int k, const float* x, const void* w,
+                          float* y);
+// f32 C[M,N] = A[M,K] * B[K,N] (Gemm.Execute fallback for N % 4 != 0).
+l0b_status gemm_f32_launch(l0b_device* dev, int m, int n, int k, const float* a, const float* b, float* c);
+
+}  // namespace l0b

@@ -1,0 +1,1180 @@
+// C++ mirror of the reference decoder host: LlmModel (L/LlmModel.cs), LlmDecoderLayer
+// (L/LlmDecoderLayer.cs), LlmMatrix (L/LlmMatrix.cs), LlmKvCache (L/LlmKvCache.cs) and the weight
+// loading rules of LlmLayerWeights (L/LlmLayerWeights.cs:110-212).
+//
+// Two ways to run a layer:
+//  - fused (default): 5 kernels per layer at decode --
+//      QKV GEMV (+input RMSNorm prologue, +bias epilogue) -> attention (+RoPE on q and the new k,
+//      KV-cache store, split-KV softmax, merge) -> o_proj GEMV (+residual add) ->
+//      gate/up GEMV (+post-attention RMSNorm prologue, SiLU(gate)*up epilogue) -> down GEMV (+residual).
+//    Every per-token value (token id, position) lives in device memory, so a decode step records the
+//    same command list every time and replays one cached CUDA graph.
+//  - reference sequence (set_fused(0)): the op-by-op sequence of LlmDecoderLayer.Forward/ForwardBatch
+//    (RMSNorm, projections, BiasAdd, QK-norm, RoPE, KvCacheStore, Attention, o_proj, RMSNorm+residual,
+//    gate/up, SwiGLU, down, Add), used to check the fused kernels and for per-stage inspection.
+#include <cmath>
+#include <cstring>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "common.cuh"
+#include "gemv.cuh"
+#include "model.h"
+#include "ops.cuh"
+#include "suite.h"
+
+using namespace l0b;
+
+struct l0b_model {
+    l0b_device* dev = nullptr;
+    l0b_suite* suite = nullptr;
+    l0b_model_config cfg = {};
+    int max_seq = 0;
+    int precision = L0B_PRECISION_AUTO;
+    int wdtype = L0B_F16;
+    int group = 0;
+    int batch_cap = 1;  // sequences in the KV caches
+    int cap = 1;        // activation rows (max(prefill chunk, batch))
+    // Dimensions (per tensor-parallel rank).
+    int h = 0, inter = 0, nh = 0, nkv = 0, hd = 0, qdim = 0, kvdim = 0, qkv_w = 0, vocab = 0, rot = 0;
+    float attn_scale = 1.f;  // rope cos/sin factor (YaRN)
+    float softmax_scale = 1.f;
+    int cache_dtype = L0B_F32;
+    // Weights.
+    float* inv_freq = nullptr;
+    float* embed = nullptr;  // f32 [vocab, h] (the reference keeps the embedding table in f32)
+    float* final_norm = nullptr;
+    ModelMatrix lm_head;
+    std::vector<ModelLayer> layers;
+    // Activations [cap, width] f32.
+    float *hidden = nullptr, *normed = nullptr, *qkv = nullptr, *qb = nullptr, *kb = nullptr, *vb = nullptr;
+    float *attn = nullptr, *attn_proj = nullptr, *gate = nullptr, *up = nullptr, *act = nullptr, *down = nullptr;
+    float* logits = nullptr;  // [batch_cap, vocab]
+    float* head_in = nullptr; // [h] last prompt row (reference sequence: Copy.Execute)
+    // Device-side step state: io = [tok(batch_cap) | pos(batch_cap)] written in one copy.
+    int* io = nullptr;
+    int* tok = nullptr;
+    int* pos = nullptr;
+    int* prompt_tok = nullptr;  // [cap]
+    int* prompt_pos = nullptr;  // [cap]
+    int* sampled = nullptr;     // [batch_cap]
+    int* out_tokens = nullptr;  // [max_seq * batch_cap]
+    int* step_idx = nullptr;
+    unsigned long long* keys = nullptr;  // [batch_cap]
+    // Split-KV attention scratch.
+    float* part = nullptr;
+    float* part_ml = nullptr;
+    unsigned* counters = nullptr;
+    int chunk = 64, max_splits = 1;
+    // Host state.
+    int* host_io = nullptr;       // pinned [2 * batch_cap]
+    float* host_logits = nullptr; // pinned [batch_cap * vocab]
+    bool fused = true;
+    bool recording = true;
+    int position = 0;
+    std::vector<void*> allocations;
+
+    ~l0b_model() {
+        if (dev) {
+            cudaSetDevice(dev->index);
+            cudaStreamSynchronize(dev->stream);
+        }
+        for (void* p : allocations) cudaFree(p);
+        if (host_io) cudaFreeHost(host_io);
+        if (host_logits) cudaFreeHost(host_logits);
+    }
+
+    template <typename T>
+    l0b_status alloc(T** out, size_t count) {
+        void* p = nullptr;
+        const size_t bytes = count * sizeof(T) < 256 ? 256 : ((count * sizeof(T) + 255) & ~size_t(255));
+        L0B_CHECK_CUDA(cudaMalloc(&p, bytes));
+        L0B_CHECK_CUDA(cudaMemsetAsync(p, 0, bytes, dev->stream));
+        allocations.push_back(p);
+        *out = static_cast<T*>(p);
+        return L0B_OK;
+    }
+    l0b_status alloc_matrix(ModelMatrix& m, int n, int k) {
+        m.n = n;
+        m.k = k;
+        m.dtype = wdtype;
+        m.group = wdtype == L0B_I8 ? (group > 0 ? group : k) : 0;
+        if (wdtype == L0B_I8) {
+            L0B_REQUIRE(k % m.group == 0, L0B_ERR_UNSUPPORTED, "int8 scale group %d does not divide K %d", m.group, k);
+            int8_t* w;
+            L0B_TRY(alloc(&w, static_cast<size_t>(n) * k));
+            m.w = w;
+            L0B_TRY(alloc(&m.scales, static_cast<size_t>(n) * (k / m.group)));
+        } else {
+            char* w;
+            L0B_TRY(alloc(&w, static_cast<size_t>(n) * k * dtype_size(static_cast<l0b_dtype>(wdtype))));
+            m.w = w;
+        }
+        return L0B_OK;
+    }
+};
+
+namespace {
+
+// ---------------------------------------------------------------------------------------------
+// Seeded synthetic weights, generated on the device. Integer hashing and exactly rounded float
+// operations only, so a CPU restatement reproduces every value bit for bit.
+// ---------------------------------------------------------------------------------------------
+
+__host__ __device__ inline uint64_t splitmix64(uint64_t x) {
+    x += 0x9E3779B97F4A7C15ULL;
+    x = (x ^ (x >> 30)) * 0xBF58476D1CE4E5B9ULL;
+    x = (x ^ (x >> 27)) * 0x94D049BB133111EBULL;
+    return x ^ (x >> 31);
+}
+
+enum SynthMode { SYN_NORMAL = 0, SYN_CONST = 1, SYN_I8 = 2, SYN_UNIFORM = 3 };
+
+// Element i of the destination maps to index (row0 + i / row_len) * full_len + col0 + i % row_len of the
+// full HuggingFace tensor, so a tensor-parallel shard holds exactly the values of the full tensor.
+__global__ void synth_kernel(void* dst, int dtype, long long count, uint64_t stream, int mode, float a, float b,
+                             long long row_len, long long full_len, long long row0, long long col0) {
+    pdl_wait();
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < count;
+         i += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const long long r = i / row_len;
+        const long long idx = (row0 + r) * full_len + col0 + (i - r * row_len);
+        const uint64_t bits = splitmix64(stream + static_cast<uint64_t>(idx) * 0xD1B54A32D192ED03ULL);
+        if (mode == SYN_I8) {
+            static_cast<int8_t*>(dst)[i] = static_cast<int8_t>(static_cast<int>(bits % 255ULL) - 127);
+            continue;
+        }
+        float v;
+        if (mode == SYN_NORMAL) {
+            const uint32_t s = static_cast<uint32_t>(bits & 0xFFFF) + static_cast<uint32_t>((bits >> 16) & 0xFFFF) +
+                               static_cast<uint32_t>((bits >> 32) & 0xFFFF) + static_cast<uint32_t>(bits >> 48);
+            const float u = __fmul_rn(static_cast<float>(s), 1.0f / 65536.0f);
+            v = __fmul_rn(__fmul_rn(__fsub_rn(u, 2.0f), 1.7320508f), a);
+        } else if (mode == SYN_UNIFORM) {
+            const float u = __fmul_rn(static_cast<float>(bits >> 40), 1.0f / 16777216.0f);
+            v = __fadd_rn(a, __fmul_rn(u, __fsub_rn(b, a)));
+        } else {
+            v = a;
+        }
+        store_from_float(dst, dtype, i, v);
+    }
+}
+
+// Converts (or offsets) an f32 staging tensor into the destination dtype.
+__global__ void convert_kernel(const float* src, void* dst, int dtype, long long count, long long row_len,
+                               long long full_len, long long col0, float offset) {
+    pdl_wait();
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < count;
+         i += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const long long r = i / row_len;
+        const float v = src[r * full_len + col0 + (i - r * row_len)] + offset;
+        store_from_float(dst, dtype, i, v);
+    }
+}
+
+// First kernel of a fused step: token rows of the embedding table into the residual stream, and the
+// argmax keys cleared for the head.
+__global__ void step_begin_kernel(const int* tok, const float* embed, float* hidden, int h, int rows, int vocab,
+                                  unsigned long long* keys, int key_rows) {
+    pdl_wait();
+    if (blockIdx.x == 0 && threadIdx.x < key_rows) keys[threadIdx.x] = 0ull;
+    const long long total = static_cast<long long>(rows) * h;
+    for (long long e = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; e < total;
+         e += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const long long t = e / h;
+        const int id = tok[t];
+        hidden[e] = (id >= 0 && id < vocab) ? embed[static_cast<long long>(id) * h + (e - t * h)] : 0.f;
+    }
+}
+
+// Last kernel of a step: greedy token from the argmax key, fed back as the next input token; the
+// position advances by `advance`; the token is appended to the device token log.
+__global__ void step_finish_kernel(const unsigned long long* keys, int* sampled, int* tok, int* pos, int* out_tokens,
+                                   int* step_idx, int rows, int advance) {
+    pdl_wait();
+    const int b = threadIdx.x;
+    const int step = *step_idx;
+    if (b < rows) {
+        const int t = argmax_key_index(keys[b]);
+        sampled[b] = t;
+        tok[b] = t;
+        pos[b] += advance;
+        if (out_tokens) out_tokens[static_cast<long long>(step) * rows + b] = t;
+    }
+    __syncthreads();
+    if (b == 0) *step_idx = step + 1;
+}
+
+inline int grid_for(long long n, int sm) {
+    long long g = (n + 255) / 256;
+    if (g > sm * 8LL) g = sm * 8LL;
+    return g < 1 ? 1 : static_cast<int>(g);
+}
+
+uint64_t tensor_stream(uint64_t seed, uint64_t id) { return splitmix64(seed ^ (id * 0x9E3779B97F4A7C15ULL)); }
+
+// Tensor ids of the synthetic generator (also used by the CPU oracle).
+enum TensorKind {
+    T_IN_NORM = 0, T_POST_NORM, T_Q, T_K, T_V, T_O, T_GATE, T_UP, T_DOWN, T_QB, T_KB, T_VB, T_QN, T_KN,
+    T_SCALE = 16  // + projection kind: int8 scales of that projection
+};
+uint64_t layer_tensor_id(int layer, int kind) { return 1000ULL + static_cast<uint64_t>(layer) * 64 + kind; }
+constexpr uint64_t kIdEmbed = 1, kIdFinalNorm = 2, kIdLmHead = 3, kIdLmHeadScale = 4;
+
+}  // namespace
+
+// Launch helpers bound to a model -------------------------------------------------------------
+
+namespace {
+
+struct Synth {
+    l0b_model* m;
+    uint64_t seed;
+    float std;
+    float lo, hi;
+    l0b_status fill(void* dst, int dtype, long long count, uint64_t id, int mode, float a, float b,
+                    long long row_len = 0, long long full_len = 0, long long row0 = 0, long long col0 = 0) {
+        if (count == 0) return L0B_OK;
+        if (row_len <= 0) row_len = count;
+        if (full_len <= 0) full_len = row_len;
+        synth_kernel<<<grid_for(count, m->dev->sm_count), 256, 0, m->dev->stream>>>(
+            dst, dtype, count, tensor_stream(seed, id), mode, a, b, row_len, full_len, row0, col0);
+        L0B_CHECK_CUDA(cudaGetLastError());
+        return L0B_OK;
+    }
+    // A projection shard: rows [row0, row0 + rows) x cols [col0, col0 + cols) of an HF [full_n, full_k]
+    // tensor, written at row `dst_row` of the stacked matrix.
+    l0b_status matrix(ModelMatrix& mat, int dst_row, uint64_t id, uint64_t scale_id, int rows, int cols, int full_k,
+                      int row0, int col0) {
+        const long long count = static_cast<long long>(rows) * cols;
+        if (mat.dtype == L0B_I8) {
+            int8_t* q = static_cast<int8_t*>(mat.w) + static_cast<long long>(dst_row) * mat.k;
+            L0B_TRY(fill(q, L0B_I8, count, id, SYN_I8, 0.f, 0.f, cols, full_k, row0, col0));
+            // Scales: one per (row, group) of the full tensor; a column shard takes its groups.
+            const int gpr_full = full_k / mat.group;
+            const int gpr = cols / mat.group;
+            __half* s = mat.scales + static_cast<long long>(dst_row) * gpr;
+            return fill(s, L0B_F16, static_cast<long long>(rows) * gpr, scale_id, SYN_UNIFORM, lo, hi, gpr, gpr_full,
+                        row0, col0 / mat.group);
+        }
+        char* w = static_cast<char*>(mat.w) +
+                  static_cast<long long>(dst_row) * mat.k * dtype_size(static_cast<l0b_dtype>(mat.dtype));
+        return fill(w, mat.dtype, count, id, SYN_NORMAL, std, 0.f, cols, full_k, row0, col0);
+    }
+};
+
+}  // namespace
+
+// ---------------------------------------------------------------------------------------------
+// Step recording
+// ---------------------------------------------------------------------------------------------
+
+namespace {
+
+GemvParams linear_params(const ModelMatrix& w, int m_rows, const void* x, long long x_ld) {
+    GemvParams p = {};
+    p.w = w.w;
+    p.scales = w.scales;
+    p.group = w.group;
+    p.N = w.n;
+    p.K = w.k;
+    p.M = m_rows;
+    p.x = x;
+    p.x_dtype = L0B_F32;
+    p.x_ld = x_ld;
+    p.epi = EPI_STORE;
+    p.out_dtype = L0B_F32;
+    p.nseg = 1;
+    p.prefetch = 1;
+    return p;
+}
+
+l0b_status gemv(l0b_model* m, const ModelMatrix& w, const GemvParams& p) { return gemv_nk_launch(m->dev, w.dtype, p); }
+
+// Fused decoder layer for `rows` tokens. decode: each row is its own sequence (cache row b, position
+// pos[b]); prefill: the rows are consecutive positions of sequence 0 starting at pos0.
+l0b_status record_layer_fused(l0b_model* m, int li, int rows, bool decode, int pos0) {
+    ModelLayer& L = m->layers[li];
+    const l0b_model_config& c = m->cfg;
+    // 1. QKV projection with the input RMSNorm prologue and the bias epilogue.
+    GemvParams p = linear_params(L.qkv, rows, m->hidden, m->h);
+    p.norm_w = L.in_norm;
+    p.eps = c.rms_norm_eps;
+    p.seg[0] = {m->qkv, L.qkv_bias, m->qkv_w, m->qkv_w};
+    L0B_TRY(gemv(m, L.qkv, p));
+    // 2. Attention.
+    AttnParams a = {};
+    a.q = m->qkv;
+    a.q_bstride = m->qkv_w;
+    a.inv_freq = m->inv_freq;
+    a.rot = m->rot;
+    a.attn_scale = m->attn_scale;
+    a.kc = L.kc;
+    a.vc = L.vc;
+    a.cache_dtype = m->cache_dtype;
+    a.kv_dim = m->kvdim;
+    a.out = m->attn;
+    a.out_bstride = m->qdim;
+    a.nh = m->nh;
+    a.nkv = m->nkv;
+    a.hd = m->hd;
+    a.scale = m->softmax_scale;
+    if (decode) {
+        a.rope = 1;
+        a.store_new = 1;
+        a.k_new = m->qkv + m->qdim;
+        a.v_new = m->qkv + m->qdim + m->kvdim;
+        a.new_bstride = m->qkv_w;
+        a.cache_bstride = static_cast<long long>(m->max_seq) * m->kvdim;
+        a.positions = m->pos;
+        a.part = m->part;
+        a.part_ml = m->part_ml;
+        a.counters = m->counters;
+        a.chunk = m->chunk;
+        a.max_splits = m->max_splits;
+        L0B_TRY(attention_launch(m->dev, a, rows));
+    } else {
+        // Prefill: rotate and store the whole chunk first (queries attend to each other's keys).
+        L0B_TRY(k_rope(m->dev, m->qkv, m->qkv + m->qdim, m->prompt_pos, m->inv_freq, m->hd, m->nh, m->nkv,
+                       m->attn_scale, m->rot, rows, m->qkv_w, m->qkv_w));
+        L0B_TRY(k_kv_store(m->dev, m->qkv + m->qdim, m->qkv + m->qdim + m->kvdim, L.kc, L.vc, m->cache_dtype, pos0,
+                           m->kvdim, rows, m->qkv_w));
+        a.rope = 0;
+        a.store_new = 0;
+        a.cache_bstride = 0;
+        a.positions = m->prompt_pos;
+        a.chunk = (pos0 + rows + 31) / 32 * 32;
+        a.max_splits = 1;
+        L0B_TRY(attention_launch(m->dev, a, rows));
+    }
+    // 3. o_proj, added into the residual stream.
+    p = linear_params(L.o, rows, m->attn, m->qdim);
+    p.epi = EPI_ACCUM;
+    p.seg[0] = {m->hidden, nullptr, m->h, m->h};
+    L0B_TRY(gemv(m, L.o, p));
+    // 4. gate/up with the post-attention RMSNorm prologue and the SwiGLU epilogue.
+    p = linear_params(L.gate_up, rows, m->hidden, m->h);
+    p.norm_w = L.post_norm;
+    p.eps = c.rms_norm_eps;
+    p.epi = EPI_SWIGLU;
+    p.seg[0] = {m->act, nullptr, m->inter, m->inter};
+    L0B_TRY(gemv(m, L.gate_up, p));
+    // 5. down, added into the residual stream.
+    p = linear_params(L.down, rows, m->act, m->inter);
+    p.epi = EPI_ACCUM;
+    p.seg[0] = {m->hidden, nullptr, m->h, m->h};
+    return gemv(m, L.down, p);
+}
+
+// The reference op sequence of LlmDecoderLayer.Forward / ForwardBatch (L/LlmDecoderLayer.cs:129-378).
+l0b_status record_layer_reference(l0b_model* m, int li, int rows, bool decode, int pos0) {
+    ModelLayer& L = m->layers[li];
+    const l0b_model_config& c = m->cfg;
+    l0b_device* d = m->dev;
+    L0B_TRY(k_rmsnorm(d, m->hidden, nullptr, L.in_norm, m->normed, c.rms_norm_eps, m->h, rows, 0));
+    GemvParams p = linear_params(L.qkv, rows, m->normed, m->h);
+    p.nseg = 3;
+    p.seg[0] = {m->qb, nullptr, m->qdim, m->qdim};
+    p.seg[1] = {m->kb, nullptr, m->qdim + m->kvdim, m->kvdim};
+    p.seg[2] = {m->vb, nullptr, m->qkv_w, m->kvdim};
+    L0B_TRY(gemv(m, L.qkv, p));
+    if (L.qkv_bias) {
+        L0B_TRY(k_bias_add(d, m->qb, L.qkv_bias, m->qdim, rows));
+        L0B_TRY(k_bias_add(d, m->kb, L.qkv_bias + m->qdim, m->kvdim, rows));
+        L0B_TRY(k_bias_add(d, m->vb, L.qkv_bias + m->qdim + m->kvdim, m->kvdim, rows));
+    }
+    if (c.qk_norm) {
+        L0B_TRY(k_rmsnorm(d, m->qb, nullptr, L.q_norm, m->qb, c.rms_norm_eps, m->hd, rows * m->nh, 0));
+        L0B_TRY(k_rmsnorm(d, m->kb, nullptr, L.k_norm, m->kb, c.rms_norm_eps, m->hd, rows * m->nkv, 0));
+    }
+    const int* positions = decode ? m->pos : m->prompt_pos;
+    L0B_TRY(k_rope(d, m->qb, m->kb, positions, m->inv_freq, m->hd, m->nh, m->nkv, m->attn_scale, m->rot, rows));
+    L0B_TRY(k_kv_store(d, m->kb, m->vb, L.kc, L.vc, m->cache_dtype, pos0, m->kvdim, rows));
+    AttnParams a = {};
+    a.q = m->qb;
+    a.q_bstride = m->qdim;
+    a.kc = L.kc;
+    a.vc = L.vc;
+    a.cache_dtype = m->cache_dtype;
+    a.kv_dim = m->kvdim;
+    a.out = m->attn;
+    a.out_bstride = m->qdim;
+    a.nh = m->nh;
+    a.nkv = m->nkv;
+    a.hd = m->hd;
+    a.scale = m->softmax_scale;
+    a.pos_base = pos0;
+    a.pos_step = 1;
+    if (decode) {
+        a.chunk = m->chunk;
+        a.max_splits = m->max_splits;
+        a.part = m->part;
+        a.part_ml = m->part_ml;
+        a.counters = m->counters;
+    } else {
+        a.chunk = (pos0 + rows + 31) / 32 * 32;
+        a.max_splits = 1;
+    }
+    L0B_TRY(attention_launch(d, a, rows));
+    p = linear_params(L.o, rows, m->attn, m->qdim);
+    p.seg[0] = {m->attn_proj, nullptr, m->h, m->h};
+    L0B_TRY(gemv(m, L.o, p));
+    L0B_TRY(k_rmsnorm(d, m->hidden, m->attn_proj, L.post_norm, m->normed, c.rms_norm_eps, m->h, rows, 1));
+    p = linear_params(L.gate_up, rows, m->normed, m->h);
+    p.nseg = 2;
+    p.seg[0] = {m->gate, nullptr, m->inter, m->inter};
+    p.seg[1] = {m->up, nullptr, 2 * m->inter, m->inter};
+    L0B_TRY(gemv(m, L.gate_up, p));
+    L0B_TRY(k_swiglu(d, m->gate, m->up, static_cast<long long>(rows) * m->inter));
+    p = linear_params(L.down, rows, m->gate, m->inter);
+    p.seg[0] = {m->down, nullptr, m->h, m->h};
+    L0B_TRY(gemv(m, L.down, p));
+    return k_add(d, m->hidden, m->down, static_cast<long long>(rows) * m->h);
+}
+
+// Final norm, LM head and greedy argmax for `rows` rows starting at hidden row `row0`.
+l0b_status record_head(l0b_model* m, int row0, int rows, int advance) {
+    const l0b_model_config& c = m->cfg;
+    l0b_device* d = m->dev;
+    if (m->fused) {
+        GemvParams p = linear_params(m->lm_head, rows, m->hidden + static_cast<long long>(row0) * m->h, m->h);
+        p.norm_w = m->final_norm;
+        p.eps = c.rms_norm_eps;
+        p.epi = EPI_ARGMAX;
+        p.argmax = m->keys;
+        p.seg[0] = {m->logits, nullptr, m->vocab, m->vocab};
+        L0B_TRY(gemv(m, m->lm_head, p));
+    } else {
+        // L/LlmModel.cs:365-399: Copy the last row, RMSNorm, lm_head, Sampling (argmax).
+        const float* src = m->hidden;
+        if (row0 > 0) {
+            L0B_TRY(k_copy(d, m->hidden, m->head_in, static_cast<long long>(row0) * m->h,
+                           static_cast<long long>(rows) * m->h));
+            src = m->head_in;
+        }
+        L0B_TRY(k_rmsnorm(d, const_cast<float*>(src), nullptr, m->final_norm, m->normed, c.rms_norm_eps, m->h, rows, 0));
+        GemvParams p = linear_params(m->lm_head, rows, m->normed, m->h);
+        p.epi = EPI_ARGMAX;
+        p.argmax = m->keys;
+        p.seg[0] = {m->logits, nullptr, m->vocab, m->vocab};
+        L0B_TRY(gemv(m, m->lm_head, p));
+    }
+    return d->launch(step_finish_kernel, dim3(1), dim3(rows < 32 ? 32 : ((rows + 31) / 32) * 32), 0, m->keys,
+                     m->sampled, m->tok, m->pos, m->out_tokens, m->step_idx, rows, advance);
+}
+
+// One decode step for `rows` sequences whose token ids and positions are already in tok/pos.
+l0b_status record_decode_step(l0b_model* m, int rows) {
+    l0b_device* d = m->dev;
+    L0B_TRY(d->launch(step_begin_kernel, dim3(grid_for(static_cast<long long>(rows) * m->h, d->sm_count)), dim3(256),
+                      0, m->tok, m->embed, m->hidden, m->h, rows, m->vocab, m->keys, rows));
+    for (int li = 0; li < static_cast<int>(m->layers.size()); ++li) {
+        if (m->fused) L0B_TRY(record_layer_fused(m, li, rows, true, 0));
+        else {
+            // The reference sequence reads the position as an argument (KvCacheStore pos0, Attention seqLen).
+            L0B_TRY(record_layer_reference(m, li, rows, true, m->position));
+        }
+    }
+    return record_head(m, 0, rows, 1);
+}
+
+// One prefill chunk of `count` tokens at positions [pos0, pos0 + count); prompt_tok / prompt_pos hold them.
+l0b_status record_prefill_chunk(l0b_model* m, int count, int pos0, bool head) {
+    l0b_device* d = m->dev;
+    L0B_TRY(d->launch(step_begin_kernel, dim3(grid_for(static_cast<long long>(count) * m->h, d->sm_count)),
+                      dim3(256), 0, m->prompt_tok, m->embed, m->hidden, m->h, count, m->vocab, m->keys, 1));
+    for (int li = 0; li < static_cast<int>(m->layers.size()); ++li) {
+        if (m->fused) L0B_TRY(record_layer_fused(m, li, count, false, pos0));
+        else L0B_TRY(record_layer_reference(m, li, count, false, pos0));
+    }
+    if (head) L0B_TRY(record_head(m, count - 1, 1, 0));
+    return L0B_OK;
+}
+
+// Runs `body` as one command list (or immediately when recording is off) and waits.
+template <typename Body>
+l0b_status run_recorded(l0b_model* m, Body body, bool wait = true) {
+    l0b_device* d = m->dev;
+    L0B_CHECK_CUDA(cudaSetDevice(d->index));
+    if (m->recording) {
+        L0B_REQUIRE(!d->recording, L0B_ERR_INVALID_OPERATION, "the device is already recording");
+        d->recording = true;
+        d->log_used = 0;
+        l0b_status s = body();
+        if (s != L0B_OK) {
+            d->abort_recording();
+            return s;
+        }
+        L0B_TRY(d->end_recording());
+    } else {
+        L0B_TRY(body());
+    }
+    if (wait) L0B_CHECK_CUDA(cudaStreamSynchronize(d->stream));
+    return L0B_OK;
+}
+
+l0b_status write_io(l0b_model* m, int rows, const int* tokens, const int* positions) {
+    for (int b = 0; b < rows; ++b) {
+        m->host_io[b] = tokens[b];
+        m->host_io[m->batch_cap + b] = positions[b];
+    }
+    L0B_CHECK_CUDA(cudaMemcpyAsync(m->io, m->host_io, sizeof(int) * 2 * m->batch_cap, cudaMemcpyHostToDevice,
+                                   m->dev->stream));
+    return L0B_OK;
+}
+
+l0b_status read_logits(l0b_model* m, float* out, int rows) {
+    if (!out) return L0B_OK;
+    const size_t bytes = static_cast<size_t>(rows) * m->vocab * sizeof(float);
+    L0B_CHECK_CUDA(cudaMemcpyAsync(m->host_logits, m->logits, bytes, cudaMemcpyDeviceToHost, m->dev->stream));
+    L0B_CHECK_CUDA(cudaStreamSynchronize(m->dev->stream));
+    std::memcpy(out, m->host_logits, bytes);
+    return L0B_OK;
+}
+
+// LlmModel.Step (L/LlmModel.cs:402-444): one token at `position`.
+l0b_status step(l0b_model* m, int token, int position) {
+    L0B_REQUIRE(token >= 0 && token < m->vocab, L0B_ERR_OUT_OF_RANGE, "Vocabulary has %d tokens (got %d).", m->vocab,
+                token);
+    L0B_REQUIRE(position >= 0 && position < m->max_seq, L0B_ERR_OUT_OF_RANGE, "Cache holds %d positions.", m->max_seq);
+    L0B_TRY(write_io(m, 1, &token, &position));
+    const int saved = m->position;
+    m->position = position;  // the reference sequence passes it as an argument
+    l0b_status s = run_recorded(m, [&] { return record_decode_step(m, 1); });
+    m->position = saved;
+    return s;
+}
+
+// LlmModel.IngestPrompt (L/LlmModel.cs:320-333): chunks of kMaxRows tokens; a 1-token chunk is a Step.
+l0b_status ingest_prompt(l0b_model* m, const int32_t* ids, int count) {
+    const int chunk = kMaxRows < m->cap ? kMaxRows : m->cap;
+    for (int start = 0; start < count; start += chunk) {
+        const int n = count - start < chunk ? count - start : chunk;
+        const bool last = start + n == count;
+        for (int i = 0; i < n; ++i)
+            L0B_REQUIRE(ids[start + i] >= 0 && ids[start + i] < m->vocab, L0B_ERR_OUT_OF_RANGE,
+                        "Vocabulary has %d tokens (got %d).", m->vocab, ids[start + i]);
+        if (n == 1) {
+            L0B_TRY(step(m, ids[start], start));
+            continue;
+        }
+        std::vector<int> pos(n);
+        for (int i = 0; i < n; ++i) pos[i] = start + i;
+        L0B_CHECK_CUDA(cudaMemcpyAsync(m->prompt_tok, ids + start, sizeof(int) * n, cudaMemcpyHostToDevice,
+                                       m->dev->stream));
+        L0B_CHECK_CUDA(cudaMemcpyAsync(m->prompt_pos, pos.data(), sizeof(int) * n, cudaMemcpyHostToDevice,
+                                       m->dev->stream));
+        // The next decode step continues from the end of the prompt.
+        if (last) {
+            const int next_pos = start + n;
+            L0B_TRY(write_io(m, 1, ids + start + n - 1, &next_pos));
+        }
+        L0B_TRY(run_recorded(m, [&] { return record_prefill_chunk(m, n, start, last); }));
+    }
+    return L0B_OK;
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------------------------------------
+// Weight loading
+// ---------------------------------------------------------------------------------------------
+
+namespace {
+
+// Where an HF tensor goes. Column-split tensors (q/k/v/gate/up, lm_head) keep rows [r0, r0 + rows);
+// row-split tensors (o, down) keep columns [c0, c0 + cols) of every row.
+struct Target {
+    ModelMatrix* mat = nullptr;
+    int dst_row = 0;
+    float* vec = nullptr;   // f32 vector destination
+    int length = 0;         // vector length (local)
+    int full_rows = 0, full_cols = 0;
+    int row0 = 0, rows = 0, col0 = 0, cols = 0;
+    float offset = 0.f;
+    uint64_t id = 0, scale_id = 0;
+    bool embed = false;
+};
+
+bool parse_layer(const std::string& name, const std::string& prefix, int* layer, std::string* rest) {
+    if (name.compare(0, prefix.size(), prefix) != 0) return false;
+    size_t p = prefix.size();
+    size_t dot = name.find('.', p);
+    if (dot == std::string::npos) return false;
+    *layer = std::atoi(name.substr(p, dot - p).c_str());
+    *rest = name.substr(dot + 1);
+    return true;
+}
+
+l0b_status resolve(l0b_model* m, const std::string& name, Target* t) {
+    const l0b_model_config& c = m->cfg;
+    const int tp = c.tp_size > 1 ? c.tp_size : 1, rank = c.tp_size > 1 ? c.tp_rank : 0;
+    const int H = c.hidden_size, I = c.intermediate_size;
+    const int QD = c.num_attention_heads * c.head_dim, KD = c.num_key_value_heads * c.head_dim;
+    if (name == "model.embed_tokens.weight") {
+        t->embed = true;
+        t->full_rows = c.vocab_size;
+        t->full_cols = H;
+        t->id = kIdEmbed;
+        return L0B_OK;
+    }
+    if (name == "model.norm.weight") {
+        t->vec = m->final_norm;
+        t->length = H;
+        t->full_rows = 1;
+        t->full_cols = H;
+        t->id = kIdFinalNorm;
+        return L0B_OK;
+    }
+    if (name == "lm_head.weight") {
+        t->mat = &m->lm_head;
+        t->full_rows = c.vocab_size;
+        t->full_cols = H;
+        t->row0 = rank * m->vocab;
+        t->rows = m->vocab;
+        t->cols = H;
+        t->id = kIdLmHead;
+        t->scale_id = kIdLmHeadScale;
+        return L0B_OK;
+    }
+    int li;
+    std::string rest;
+    if (!parse_layer(name, "model.layers.", &li, &rest) || li < 0 || li >= c.num_layers)
+        return fail(L0B_ERR_INVALID_DATA, "unknown tensor '%s'", name.c_str());
+    ModelLayer& L = m->layers[li];
+    auto col_split = [&](ModelMatrix* mat, int dst_row, int full_rows, int kind) {
+        const int local = full_rows / tp;
+        t->mat = mat;
+        t->dst_row = dst_row;
+        t->full_rows = full_rows;
+        t->full_cols = H;
+        t->row0 = rank * local;
+        t->rows = local;
+        t->cols = H;
+        t->id = layer_tensor_id(li, kind);
+        t->scale_id = layer_tensor_id(li, T_SCALE + kind);
+    };
+    auto row_split = [&](ModelMatrix* mat, int full_cols, int kind) {
+        const int local = full_cols / tp;
+        t->mat = mat;
+        t->full_rows = H;
+        t->full_cols = full_cols;
+        t->rows = H;
+        t->col0 = rank * local;
+        t->cols = local;
+        t->id = layer_tensor_id(li, kind);
+        t->scale_id = layer_tensor_id(li, T_SCALE + kind);
+    };
+    auto vec = [&](float* dst, int full, int local, int off, int kind) {
+        t->vec = dst;
+        t->length = local;
+        t->full_rows = 1;
+        t->full_cols = full;
+        t->col0 = off;
+        t->id = layer_tensor_id(li, kind);
+    };
+    if (rest == "input_layernorm.weight") vec(L.in_norm, H, H, 0, T_IN_NORM);
+    else if (rest == "post_attention_layernorm.weight") vec(L.post_norm, H, H, 0, T_POST_NORM);
+    else if (rest == "self_attn.q_proj.weight") col_split(&L.qkv, 0, QD, T_Q);
+    else if (rest == "self_attn.k_proj.weight") col_split(&L.qkv, m->qdim, KD, T_K);
+    else if (rest == "self_attn.v_proj.weight") col_split(&L.qkv, m->qdim + m->kvdim, KD, T_V);
+    else if (rest == "self_attn.o_proj.weight") row_split(&L.o, QD, T_O);
+    else if (rest == "mlp.gate_proj.weight") col_split(&L.gate_up, 0, I, T_GATE);
+    else if (rest == "mlp.up_proj.weight") col_split(&L.gate_up, m->inter, I, T_UP);
+    else if (rest == "mlp.down_proj.weight") row_split(&L.down, I, T_DOWN);
+    else if (rest == "self_attn.q_proj.bias" && L.qkv_bias) vec(L.qkv_bias, QD, m->qdim, rank * m->qdim, T_QB);
+    else if (rest == "self_attn.k_proj.bias" && L.qkv_bias) vec(L.qkv_bias + m->qdim, KD, m->kvdim, rank * m->kvdim, T_KB);
+    else if (rest == "self_attn.v_proj.bias" && L.qkv_bias)
+        vec(L.qkv_bias + m->qdim + m->kvdim, KD, m->kvdim, rank * m->kvdim, T_VB);
+    else if (rest == "self_attn.q_norm.weight" && L.q_norm) vec(L.q_norm, c.head_dim, c.head_dim, 0, T_QN);
+    else if (rest == "self_attn.k_norm.weight" && L.k_norm) vec(L.k_norm, c.head_dim, c.head_dim, 0, T_KN);
+    else return fail(L0B_ERR_INVALID_DATA, "unknown or unused tensor '%s'", name.c_str());
+    return L0B_OK;
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------------------------------------
+// C ABI
+// ---------------------------------------------------------------------------------------------
+
+#define GUARD_BEGIN try {
+#define GUARD_END                                                                                  \
+    }                                                                                              \
+    catch (const std::bad_alloc&) {                                                                \
+        return fail(L0B_ERR_OUT_OF_MEMORY, "host allocation failed");                              \
+    }                                                                                              \
+    catch (const std::exception& e) {                                                              \
+        return fail(L0B_ERR_INVALID_OPERATION, "%s", e.what());                                    \
+    }
+
+extern "C" {
+
+L0B_API l0b_status l0b_model_config_init(l0b_model_config* c) {
+    L0B_REQUIRE(c, L0B_ERR_ARGUMENT, "config is null");
+    std::memset(c, 0, sizeof(*c));
+    c->max_position_embeddings = 2048;
+    c->rms_norm_eps = 1e-6f;
+    c->rope_theta = 10000.0;
+    c->rope_type = L0B_ROPE_DEFAULT;
+    c->rope_factor = 1.0;
+    c->rope_low_freq_factor = 1.0;
+    c->rope_high_freq_factor = 4.0;
+    c->rope_beta_fast = 32.0;
+    c->rope_beta_slow = 1.0;
+    c->rope_truncate = 1;
+    c->partial_rotary_factor = 1.0;
+    c->kv_dtype = L0B_F32;
+    c->q8_group = 32;
+    c->tp_size = 1;
+    c->tp_rank = 0;
+    return L0B_OK;
+}
+
+L0B_API l0b_status l0b_model_create(l0b_device* dev, l0b_suite* suite, const l0b_model_config* cfg, int32_t max_seq_len,
+                                    l0b_precision precision, l0b_comm* comm, l0b_model** out) {
+    GUARD_BEGIN
+    L0B_REQUIRE(dev && suite && cfg && out, L0B_ERR_ARGUMENT, "null argument");
+    *out = nullptr;
+    const l0b_model_config& c = *cfg;
+    // HfModelConfig.EnsureSupported (L/HfModelConfig.cs:211-257) for the fields this path reads.
+    L0B_REQUIRE(c.num_attention_heads > 0 && c.num_key_value_heads > 0 && c.head_dim > 0 && c.num_layers > 0,
+                L0B_ERR_INVALID_DATA, "Head counts, head_dim and layer count must be positive.");
+    L0B_REQUIRE(c.num_attention_heads % c.num_key_value_heads == 0, L0B_ERR_INVALID_DATA,
+                "num_attention_heads (%d) is not a multiple of num_key_value_heads (%d).", c.num_attention_heads,
+                c.num_key_value_heads);
+    L0B_REQUIRE(c.head_dim % 2 == 0, L0B_ERR_INVALID_DATA, "head_dim (%d) must be even for rotary embeddings.",
+                c.head_dim);
+    L0B_REQUIRE(c.hidden_size > 0 && c.intermediate_size > 0 && c.vocab_size > 0, L0B_ERR_INVALID_DATA,
+                "hidden, intermediate and vocab sizes must be positive");
+    L0B_REQUIRE(max_seq_len > 0, L0B_ERR_OUT_OF_RANGE, "maxSeqLen must be positive");
+    L0B_REQUIRE(c.kv_dtype == L0B_F32 || c.kv_dtype == L0B_F16 || c.kv_dtype == L0B_BF16, L0B_ERR_ARGUMENT,
+                "kv_dtype must be f32, f16 or bf16");
+    const int tp = c.tp_size > 1 ? c.tp_size : 1;
+    L0B_REQUIRE(tp == 1 || comm, L0B_ERR_ARGUMENT, "tensor parallelism needs a communicator");
+    L0B_REQUIRE(c.num_key_value_heads % tp == 0 && c.intermediate_size % tp == 0 && c.vocab_size % tp == 0,
+                L0B_ERR_UNSUPPORTED, "kv heads, intermediate size and vocab must divide by tp_size %d", tp);
+    L0B_REQUIRE(c.head_dim == 64 || c.head_dim == 128, L0B_ERR_UNSUPPORTED, "head_dim %d (64 or 128 are supported)",
+                c.head_dim);
+    L0B_REQUIRE((c.num_attention_heads / c.num_key_value_heads) <= 64, L0B_ERR_UNSUPPORTED, "GQA group too large");
+
+    std::unique_ptr<l0b_model> m(new l0b_model());
+    m->dev = dev;
+    m->suite = suite;
+    m->cfg = c;
+    m->max_seq = max_seq_len;
+    m->precision = precision;
+    switch (precision) {
+        case L0B_PRECISION_AUTO:
+        case L0B_PRECISION_INT8: m->wdtype = L0B_I8; break;
+        case L0B_PRECISION_FLOAT32: m->wdtype = L0B_F32; break;
+        case L0B_PRECISION_FLOAT16: m->wdtype = L0B_F16; break;
+        case L0B_PRECISION_BFLOAT16: m->wdtype = L0B_BF16; break;
+        default: return fail(L0B_ERR_ARGUMENT, "unknown precision %d", (int)precision);
+    }
+    m->group = c.q8_group;
+    m->h = c.hidden_size;
+    m->inter = c.intermediate_size / tp;
+    m->nh = c.num_attention_heads / tp;
+    m->nkv = c.num_key_value_heads / tp;
+    m->hd = c.head_dim;
+    m->qdim = m->nh * m->hd;
+    m->kvdim = m->nkv * m->hd;
+    m->qkv_w = m->qdim + 2 * m->kvdim;
+    m->vocab = c.vocab_size / tp;
+    m->cache_dtype = c.kv_dtype;
+    m->softmax_scale = static_cast<float>(1.0 / std::sqrt(static_cast<double>(c.head_dim)));
+    m->fused = !c.qk_norm;
+    m->batch_cap = 1;
+    m->cap = kMaxRows;
+    L0B_CHECK_CUDA(cudaSetDevice(dev->index));
+
+    std::vector<float> table;
+    L0B_TRY(rope_frequencies(c, &table, &m->attn_scale));
+    m->rot = static_cast<int>(table.size()) * 2;
+    L0B_TRY(m->alloc(&m->inv_freq, table.size()));
+    L0B_CHECK_CUDA(cudaMemcpy(m->inv_freq, table.data(), table.size() * sizeof(float), cudaMemcpyHostToDevice));
+
+    // Weights.
+    L0B_TRY(m->alloc(&m->embed, static_cast<size_t>(c.vocab_size) * m->h));
+    L0B_TRY(m->alloc(&m->final_norm, m->h));
+    L0B_TRY(m->alloc_matrix(m->lm_head, m->vocab, m->h));
+    m->layers.resize(c.num_layers);
+    const size_t cache_elems = static_cast<size_t>(m->batch_cap) * max_seq_len * m->kvdim;
+    for (auto& L : m->layers) {
+        L0B_TRY(m->alloc(&L.in_norm, m->h));
+        L0B_TRY(m->alloc(&L.post_norm, m->h));
+        L0B_TRY(m->alloc_matrix(L.qkv, m->qkv_w, m->h));
+        L0B_TRY(m->alloc_matrix(L.o, m->h, m->qdim));
+        L0B_TRY(m->alloc_matrix(L.gate_up, 2 * m->inter, m->h));
+        L0B_TRY(m->alloc_matrix(L.down, m->h, m->inter));
+        if (c.attention_bias) L0B_TRY(m->alloc(&L.qkv_bias, m->qkv_w));
+        if (c.qk_norm) {
+            L0B_TRY(m->alloc(&L.q_norm, m->hd));
+            L0B_TRY(m->alloc(&L.k_norm, m->hd));
+        }
+        char* kc;
+        char* vc;
+        L0B_TRY(m->alloc(&kc, cache_elems * dtype_size(static_cast<l0b_dtype>(m->cache_dtype))));
+        L0B_TRY(m->alloc(&vc, cache_elems * dtype_size(static_cast<l0b_dtype>(m->cache_dtype))));
+        L.kc = kc;
+        L.vc = vc;
+    }
+    // Norms default to 1 (identity), as a freshly initialised HF model has them.
+    {
+        const float one = 1.f;
+        std::vector<float> ones(std::max(m->h, m->hd), one);
+        L0B_CHECK_CUDA(cudaMemcpy(m->final_norm, ones.data(), m->h * sizeof(float), cudaMemcpyHostToDevice));
+        for (auto& L : m->layers) {
+            L0B_CHECK_CUDA(cudaMemcpy(L.in_norm, ones.data(), m->h * sizeof(float), cudaMemcpyHostToDevice));
+            L0B_CHECK_CUDA(cudaMemcpy(L.post_norm, ones.data(), m->h * sizeof(float), cudaMemcpyHostToDevice));
+            if (L.q_norm) {
+                L0B_CHECK_CUDA(cudaMemcpy(L.q_norm, ones.data(), m->hd * sizeof(float), cudaMemcpyHostToDevice));
+                L0B_CHECK_CUDA(cudaMemcpy(L.k_norm, ones.data(), m->hd * sizeof(float), cudaMemcpyHostToDevice));
+            }
+        }
+    }
+    // Activations.
+    const size_t cap = static_cast<size_t>(m->cap);
+    L0B_TRY(m->alloc(&m->hidden, cap * m->h));
+    L0B_TRY(m->alloc(&m->normed, cap * m->h));
+    L0B_TRY(m->alloc(&m->qkv, cap * m->qkv_w));
+    L0B_TRY(m->alloc(&m->qb, cap * m->qdim));
+    L0B_TRY(m->alloc(&m->kb, cap * m->kvdim));
+    L0B_TRY(m->alloc(&m->vb, cap * m->kvdim));
+    L0B_TRY(m->alloc(&m->attn, cap * m->qdim));
+    L0B_TRY(m->alloc(&m->attn_proj, cap * m->h));
+    L0B_TRY(m->alloc(&m->gate, cap * m->inter));
+    L0B_TRY(m->alloc(&m->up, cap * m->inter));
+    L0B_TRY(m->alloc(&m->act, cap * m->inter));
+    L0B_TRY(m->alloc(&m->down, cap * m->h));
+    L0B_TRY(m->alloc(&m->head_in, static_cast<size_t>(m->batch_cap) * m->h));
+    L0B_TRY(m->alloc(&m->logits, static_cast<size_t>(m->batch_cap) * m->vocab));
+    L0B_TRY(m->alloc(&m->io, 2 * static_cast<size_t>(m->batch_cap)));
+    m->tok = m->io;
+    m->pos = m->io + m->batch_cap;
+    L0B_TRY(m->alloc(&m->prompt_tok, cap));
+    L0B_TRY(m->alloc(&m->prompt_pos, cap));
+    L0B_TRY(m->alloc(&m->sampled, m->batch_cap));
+    L0B_TRY(m->alloc(&m->out_tokens, static_cast<size_t>(max_seq_len + 1) * m->batch_cap));
+    L0B_TRY(m->alloc(&m->step_idx, 1));
+    L0B_TRY(m->alloc(&m->keys, m->batch_cap));
+    attention_pick_split(max_seq_len, m->batch_cap * m->nkv, dev->sm_count, &m->chunk, &m->max_splits);
+    const size_t part_rows = static_cast<size_t>(m->batch_cap) * m->nh * m->max_splits;
+    L0B_TRY(m->alloc(&m->part, part_rows * m->hd));
+    L0B_TRY(m->alloc(&m->part_ml, part_rows * 2));
+    L0B_TRY(m->alloc(&m->counters, static_cast<size_t>(m->batch_cap) * m->nh));
+    L0B_CHECK_CUDA(cudaMallocHost(&m->host_io, sizeof(int) * 2 * m->batch_cap));
+    L0B_CHECK_CUDA(cudaMallocHost(&m->host_logits, sizeof(float) * m->batch_cap * m->vocab));
+    L0B_CHECK_CUDA(cudaStreamSynchronize(dev->stream));
+    *out = m.release();
+    return L0B_OK;
+    GUARD_END
+}
+
+L0B_API l0b_status l0b_model_free(l0b_model* model) {
+    delete model;
+    return L0B_OK;
+}
+
+L0B_API l0b_status l0b_model_set_tensor(l0b_model* m, const char* name, const float* data, int64_t count) {
+    GUARD_BEGIN
+    L0B_REQUIRE(m && name && data, L0B_ERR_ARGUMENT, "null argument");
+    Target t;
+    L0B_TRY(resolve(m, name, &t));
+    const long long full = static_cast<long long>(t.full_rows) * t.full_cols;
+    L0B_REQUIRE(count == full, L0B_ERR_INVALID_DATA, "Tensor '%s' has %lld values, expected %lld.", name,
+                (long long)count, full);
+    if (t.mat && t.mat->dtype == L0B_F16) {
+        // LlmMatrix.FitsInHalf (L/LlmMatrix.cs:110-120): Float16 storage refuses values a half cannot hold.
+        for (long long i = 0; i < full; ++i)
+            L0B_REQUIRE(std::isfinite(data[i]) && std::fabs(data[i]) <= 65000.f, L0B_ERR_INVALID_DATA,
+                        "Tensor '%s' has values outside the half-precision range.", name);
+    }
+    if (t.embed && m->cfg.tie_word_embeddings) {
+        // Tied head: lm_head.weight is the embedding table (L/LlmModel.cs:62).
+        L0B_TRY(l0b_model_set_tensor(m, "lm_head.weight", data, count));
+    }
+    L0B_CHECK_CUDA(cudaSetDevice(m->dev->index));
+    float* staging = nullptr;
+    L0B_CHECK_CUDA(cudaMalloc(&staging, static_cast<size_t>(full) * sizeof(float)));
+    struct Free {
+        float* p;
+        ~Free() { cudaFree(p); }
+    } guard{staging};
+    L0B_CHECK_CUDA(cudaMemcpy(staging, data, static_cast<size_t>(full) * sizeof(float), cudaMemcpyHostToDevice));
+    cudaStream_t st = m->dev->stream;
+    const int sm = m->dev->sm_count;
+    if (t.embed) {
+        L0B_CHECK_CUDA(cudaMemcpyAsync(m->embed, staging, static_cast<size_t>(full) * sizeof(float),
+                                       cudaMemcpyDeviceToDevice, st));
+    } else if (t.vec) {
+        convert_kernel<<<grid_for(t.length, sm), 256, 0, st>>>(staging, t.vec, L0B_F32, t.length, t.length, t.full_cols,
+                                                                t.col0, t.offset);
+    } else {
+        ModelMatrix& mat = *t.mat;
+        const long long count_local = static_cast<long long>(t.rows) * t.cols;
+        const float* src = staging + static_cast<long long>(t.row0) * t.full_cols;
+        if (mat.dtype == L0B_I8) {
+            // Quantise the full rows (scales over the whole input width), then keep this rank's columns.
+            float* rows_f = nullptr;
+            L0B_CHECK_CUDA(cudaMalloc(&rows_f, static_cast<size_t>(t.rows) * t.full_cols * sizeof(float)));
+            Free g2{rows_f};
+            L0B_CHECK_CUDA(cudaMemcpyAsync(rows_f, src, static_cast<size_t>(t.rows) * t.full_cols * sizeof(float),
+                                           cudaMemcpyDeviceToDevice, st));
+            int8_t* q_full = nullptr;
+            __half* s_full = nullptr;
+            L0B_CHECK_CUDA(cudaMalloc(&q_full, static_cast<size_t>(t.rows) * t.full_cols));
+            const int gfull = mat.group == mat.k ? t.full_cols : mat.group;
+            L0B_CHECK_CUDA(cudaMalloc(&s_full, static_cast<size_t>(t.rows) * (t.full_cols / gfull) * sizeof(__half)));
+            struct FreeV {
+                void* p;
+                ~FreeV() { cudaFree(p); }
+            } g3{q_full}, g4{s_full};
+            // Quantisation runs immediately (not recorded): load time.
+            const bool was = m->dev->recording;
+            m->dev->recording = false;
+            l0b_status s = k_quantize(m->dev, rows_f, L0B_F32, t.rows, t.full_cols, gfull, q_full, s_full);
+            m->dev->recording = was;
+            L0B_TRY(s);
+            int8_t* qdst = static_cast<int8_t*>(mat.w) + static_cast<long long>(t.dst_row) * mat.k;
+            L0B_CHECK_CUDA(cudaMemcpy2DAsync(qdst, mat.k, q_full + t.col0, t.full_cols, t.cols, t.rows,
+                                             cudaMemcpyDeviceToDevice, st));
+            if (gfull == t.full_cols) {
+                L0B_REQUIRE(t.cols == t.full_cols || mat.group == mat.k, L0B_ERR_UNSUPPORTED, "scale layout");
+                L0B_CHECK_CUDA(cudaMemcpyAsync(mat.scales + t.dst_row, s_full, static_cast<size_t>(t.rows) * sizeof(__half),
+                                               cudaMemcpyDeviceToDevice, st));
+            } else {
+                const int gpr_full = t.full_cols / gfull, gpr = t.cols / gfull;
+                L0B_CHECK_CUDA(cudaMemcpy2DAsync(mat.scales + static_cast<long long>(t.dst_row) * gpr,
+                                                 gpr * sizeof(__half), s_full + t.col0 / gfull,
+                                                 gpr_full * sizeof(__half), gpr * sizeof(__half), t.rows,
+                                                 cudaMemcpyDeviceToDevice, st));
+            }
+            L0B_CHECK_CUDA(cudaStreamSynchronize(st));
+        } else {
+            char* dst = static_cast<char*>(mat.w) +
+                        static_cast<long long>(t.dst_row) * mat.k * dtype_size(static_cast<l0b_dtype>(mat.dtype));
+            convert_kernel<<<grid_for(count_local, sm), 256, 0, st>>>(src, dst, mat.dtype, count_local, t.cols,
+                                                                       t.full_cols, t.col0, 0.f);
+        }
+    }
+    L0B_CHECK_CUDA(cudaGetLastError());
+    L0B_CHECK_CUDA(cudaStreamSynchronize(st));
+    return L0B_OK;
+    GUARD_END
+}
+
+L0B_API l0b_status l0b_model_init_synthetic(l0b_model* m, uint64_t seed, float std, float scale_lo, float scale_hi) {
+    GUARD_BEGIN
+    L0B_REQUIRE(m, L0B_ERR_ARGUMENT, "model is null");
+    L0B_CHECK_CUDA(cudaSetDevice(m->dev->index));
+    Synth s{m, seed, std, scale_lo, scale_hi};
+    const l0b_model_config& c = m->cfg;
+    const int tp = c.tp_size > 1 ? c.tp_size : 1, rank = c.tp_size > 1 ? c.tp_rank : 0;
+    const int H = c.hidden_size, I = c.intermediate_size;
+    const int QD = c.num_attention_heads * c.head_dim, KD = c.num_key_value_heads * c.head_dim;
+    L0B_TRY(s.fill(m->embed, L0B_F32, static_cast<long long>(c.vocab_size) * H, kIdEmbed, SYN_NORMAL, std, 0.f));
+    if (c.tie_word_embeddings) {
+        // The LM head is the embedding table (L/LlmModel.cs:62); values are stored in the model precision.
+        if (m->lm_head.dtype == L0B_I8) {
+            const bool was = m->dev->recording;
+            m->dev->recording = false;
+            l0b_status st = k_quantize(m->dev, m->embed + static_cast<long long>(rank) * m->vocab * H, L0B_F32, m->vocab,
+                                       H, m->lm_head.group, static_cast<int8_t*>(m->lm_head.w), m->lm_head.scales);
+            m->dev->recording = was;
+            L0B_TRY(st);
+        } else {
+            const long long n = static_cast<long long>(m->vocab) * H;
+            convert_kernel<<<grid_for(n, m->dev->sm_count), 256, 0, m->dev->stream>>>(
+                m->embed + static_cast<long long>(rank) * m->vocab * H, m->lm_head.w, m->lm_head.dtype, n, H, H, 0, 0.f);
+        }
+    } else {
+        L0B_TRY(s.matrix(m->lm_head, 0, kIdLmHead, kIdLmHeadScale, m->vocab, H, H, rank * m->vocab, 0));
+    }
+    for (int li = 0; li < c.num_layers; ++li) {
+        ModelLayer& L = m->layers[li];
+        auto id = [&](int kind) { return layer_tensor_id(li, kind); };
+        auto sid = [&](int kind) { return layer_tensor_id(li, T_SCALE + kind); };
+        L0B_TRY(s.matrix(L.qkv, 0, id(T_Q), sid(T_Q), m->qdim, H, H, rank * m->qdim, 0));
+        L0B_TRY(s.matrix(L.qkv, m->qdim, id(T_K), sid(T_K), m->kvdim, H, H, rank * m->kvdim, 0));
+        L0B_TRY(s.matrix(L.qkv, m->qdim + m->kvdim, id(T_V), sid(T_V), m->kvdim, H, H, rank * m->kvdim, 0));
+        L0B_TRY(s.matrix(L.o, 0, id(T_O), sid(T_O), H, m->qdim, QD, 0, rank * m->qdim));
+        L0B_TRY(s.matrix(L.gate_up, 0, id(T_GATE), sid(T_GATE), m->inter, H, H, rank * m->inter, 0));
+        L0B_TRY(s.matrix(L.gate_up, m->inter, id(T_UP), sid(T_UP), m->inter, H, H, rank * m->inter, 0));
+        L0B_TRY(s.matrix(L.down, 0, id(T_DOWN), sid(T_DOWN), H, m->inter, I, 0, rank * m->inter));
+        if (L.qkv_bias) {
+            L0B_TRY(s.fill(L.qkv_bias, L0B_F32, m->qdim, id(T_QB), SYN_NORMAL, std, 0.f, m->qdim, QD, 0, rank * m->qdim));
+            L0B_TRY(s.fill(L.qkv_bias + m->qdim, L0B_F32, m->kvdim, id(T_KB), SYN_NORMAL, std, 0.f, m->kvdim, KD, 0,
+                           rank * m->kvdim));
+            L0B_TRY(s.fill(L.qkv_bias + m->qdim + m->kvdim, L0B_F32, m->kvdim, id(T_VB), SYN_NORMAL, std, 0.f, m->kvdim,
+                           KD, 0, rank * m->kvdim));
+        }
+        (void)tp;
+    }
+    L0B_CHECK_CUDA(cudaGetLastError());
+    L0B_CHECK_CUDA(cudaStreamSynchronize(m->dev->stream));
+    return L0B_OK;
+    GUARD_END
+}
+
+L0B_API l0b_status l0b_model_prefill(l0b_model* m, const int32_t* ids, int32_t count, float* logits) {
+    GUARD_BEGIN
+    L0B_REQUIRE(m && ids, L0B_ERR_ARGUMENT, "null argument");
+    L0B_REQUIRE(count > 0, L0B_ERR_ARGUMENT, "The prompt must contain at least one token.");
+    L0B_REQUIRE(count <= m->max_seq, L0B_ERR_ARGUMENT, "Prompt of %d tokens exceeds the %d-token cache.", count,
+                m->max_seq);
+    m->position = 0;
+    L0B_TRY(ingest_prompt(m, ids, count));
+    m->position = count;
+    return read_logits(m, logits, 1);
+    GUARD_END
+}
+
+L0B_API l0b_status l0b_model_decode(l0b_model* m, int32_t token, float* logits) {
+    GUARD_BEGIN
+    L0B_REQUIRE(m, L0B_ERR_ARGUMENT, "model is null");
+    L0B_REQUIRE(m->position < m->max_seq, L0B_ERR_INVALID_OPERATION, "The %d-token KV cache is full.", m->max_seq);
+    L0B_TRY(step(m, token, m->position));
+    m->position += 1;
+    return read_logits(m, logits, 1);
+    GUARD_END
+}
+
+L0B_API l0b_status l0b_model_compute_logits(l0b_model* m, int32_t token, int32_t position, float* logits) {
+    GUARD_BEGIN
+    L0B_REQUIRE(m, L0B_ERR_ARGUMENT, "model is null");
+    L0B_TRY(step(m, token, position));
+    return read_logits(m, logits, 1);
+    GUARD_END
+}
+
+L0B_API l0b_status l0b_model_generate_greedy(l0b_model* m, const int32_t* ids, int32_t count, int32_t max_new,
+                                             const int32_t* stop_ids, int32_t n_stop, int32_t* out,
+                                             int32_t* out_count) {
+    GUARD_BEGIN
+    L0B_REQUIRE(m && ids && out_count, L0B_ERR_ARGUMENT, "null argument");
+    L0B_REQUIRE(max_new >= 0, L0B_ERR_OUT_OF_RANGE, "maxNewTokens must be non-negative");
+    L0B_REQUIRE(count > 0, L0B_ERR_ARGUMENT, "The prompt must contain at least one token.");
+    L0B_REQUIRE(count + max_new <= m->max_seq, L0B_ERR_ARGUMENT,
+                "Prompt of %d tokens plus %d new tokens exceeds the %d-token cache.", count, max_new, m->max_seq);
+    *out_count = 0;
+    if (max_new == 0) return L0B_OK;
+    L0B_REQUIRE(out, L0B_ERR_ARGUMENT, "out is null");
+    L0B_TRY(ingest_prompt(m, ids, count));
+    int next = 0;
+    L0B_CHECK_CUDA(cudaMemcpy(&next, m->sampled, sizeof(int), cudaMemcpyDeviceToHost));
+    int position = count;
+    int n = 0;
+    while (true) {
+        out[n++] = next;
+        bool stop = false;
+        for (int i = 0; i < n_stop; ++i) stop = stop || stop_ids[i] == next;
+        if (n >= max_new || stop) break;
+        L0B_TRY(step(m, next, position));
+        L0B_CHECK_CUDA(cudaMemcpy(&next, m->sampled, sizeof(int), cudaMemcpyDeviceToHost));
+        ++position;
+    }
+    *out_count = n;
+    return L0B_OK;
+    GUARD_END
+}
+
+L0B_API l0b_status l0b_model_decode_greedy_device(l0b_model* m, int32_t steps, int32_t* out) {
+    GUARD_BEGIN
+    L0B_REQUIRE(m, L0B_ERR_ARGUMENT, "model is null");
+    L0B_REQUIRE(steps >= 0, L0B_ERR_OUT_OF_RANGE, "steps must be non-negative");
+    L0B_REQUIRE(m->fused, L0B_ERR_UNSUPPORTED, "device-resident decode needs the fused path");
+    L0B_REQUIRE(m->position + steps <= m->max_seq, L0B_ERR_INVALID_OPERATION, "The %d-token KV cache is full.",
+                m->max_seq);
+    if (steps == 0) return L0B_OK;
+    l0b_device* d = m->dev;
+    L0B_CHECK_CUDA(cudaSetDevice(d->index));
+    // tok already holds the last sampled token; pos = current position; the step index restarts.
+    m->host_io[0] = m->position;
+    L0B_CHECK_CUDA(cudaMemcpyAsync(m->pos, &m->host_io[0], sizeof(int), cudaMemcpyHostToDevice, d->stream));
+    L0B_CHECK_CUDA(cudaMemsetAsync(m->step_idx, 0, sizeof(int), d->stream));
+    L0B_CHECK_CUDA(cudaMemcpyAsync(m->tok, m->sampled, sizeof(int), cudaMemcpyDeviceToDevice, d->stream));
+    for (int i = 0; i < steps; ++i) {
+        d->recording = true;
+        d->log_used = 0;
+        l0b_status s = record_decode_step(m, 1);
+        if (s != L0B_OK) {
+            d->abort_recording();
+            return s;
+        }
+        L0B_TRY(d->end_recording());
+    }
+    m->position += steps;
+    if (out) {
+        L0B_CHECK_CUDA(cudaMemcpyAsync(out, m->out_tokens, sizeof(int) * steps, cudaMemcpyDeviceToHost, d->stream));
+    }
+    L0B_CHECK_CUDA(cudaStreamSynchronize(d->stream));
+    return L0B_OK;
+    GUARD_END
+}
+
+L0B_API l0b_status l0b_model_position(l0b_model* m, int32_t* position) {
+    L0B_REQUIRE(m && position, L0B_ERR_ARGUMENT, "null argument");
+    *position = m->position;
+    return L0B_OK;
+}
+
+L0B_API l0b_status l0b_model_reset_sequence(l0b_model* m) {
+    L0B_REQUIRE(m, L0B_ERR_ARGUMENT, "model is null");
+    m->position = 0;
+    return L0B_OK;
+}
+
+L0B_API l0b_status l0b_model_projection_bytes(l0b_model* m, int64_t* bytes) {
+    L0B_REQUIRE(m && bytes, L0B_ERR_ARGUMENT, "null argument");
+    int64_t b = static_cast<int64_t>(m->lm_head.bytes());
+    for (auto& L : m->layers) b += L.qkv.bytes() + L.o.bytes() + L.gate_up.bytes() + L.down.bytes();
+    *bytes = b;
+    return L0B_OK;
+}
+
+L0B_API l0b_status l0b_model_set_recording(l0b_model* m, int32_t enabled) {
+    L0B_REQUIRE(m, L0B_ERR_ARGUMENT, "model is null");
+    m->recording = enabled != 0;
+    return L0B_OK;
+}
+
+L0B_API l0b_status l0b_model_set_fused(l0b_model* m, int32_t enabled) {
+    L0B_REQUIRE(m, L0B_ERR_ARGUMENT, "model is null");
+    L0B_REQUIRE(!enabled || !m->cfg.qk_norm, L0B_ERR_UNSUPPORTED, "the fused layer has no QK-norm");
+    m->fused = enabled != 0;
+    return L0B_OK;
+}
+
+L0B_API l0b_status l0b_model_read_kv(l0b_model* m, int32_t layer, int32_t row0, int32_t rows, float* keys,
+                                     float* values) {
+    GUARD_BEGIN
+    L0B_REQUIRE(m && keys && values, L0B_ERR_ARGUMENT, "null argument");
+    L0B_REQUIRE(layer >= 0 && layer < static_cast<int>(m->layers.size()), L0B_ERR_OUT_OF_RANGE, "layer %d", layer);
+    L0B_REQUIRE(row0 >= 0 && rows >= 0 && row0 + rows <= m->max_seq, L0B_ERR_OUT_OF_RANGE, "rows outside the cache");
+    if (rows == 0) return L0B_OK;
+    const size_t n = static_cast<size_t>(rows) * m->kvdim;
+    const size_t es = dtype_size(static_cast<l0b_dtype>(m->cache_dtype));
+    std::vector<uint8_t> tmp(n * es);
+    ModelLayer& L = m->layers[layer];
+    L0B_CHECK_CUDA(cudaStreamSynchronize(m->dev->stream));
+    for (int which = 0; which < 2; ++which) {
+        const char* src = static_cast<const char*>(which ? L.vc : L.kc) + static_cast<size_t>(row0) * m->kvdim * es;
+        L0B_CHECK_CUDA(cudaMemcpy(tmp.data(), src, n * es, cudaMemcpyDeviceToHost));
+        float* dst = which ? values : keys;
+        for (size_t i = 0; i < n; ++i) {
+            if (m->cache_dtype == L0B_F32) dst[i] = reinterpret_cast<const float*>(tmp.data())[i];
+            else if (m->cache_dtype == L0B_F16) dst[i] = __half2float(reinterpret_cast<const __half*>(tmp.data())[i]);
+            else {
+                uint32_t bits = static_cast<uint32_t>(reinterpret_cast<const uint16_t*>(tmp.data())[i]) << 16;
+                std::memcpy(&dst[i], &bits, 4);
+            }
+        }
+    }
+    return L0B_OK;
+    GUARD_END
+}
+
+}  // extern "C"

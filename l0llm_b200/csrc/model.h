@@ -1,0 +1,42 @@
+// C++ mirror of the reference decoder host (LlmModel / LlmDecoderLayer / LlmMatrix / LlmKvCache).
+#pragma once
+
+#include <cuda_fp16.h>
+
+#include <string>
+#include <vector>
+
+#include "runtime.h"
+
+namespace l0b {
+
+// LlmMatrix: one projection in the [out = n, in = k] order, f32 / f16 / bf16 or int8 + f16 scales.
+// Fused projections are stored stacked: q/k/v as [q; k; v] rows, gate/up as [gate; up] rows.
+struct ModelMatrix {
+    int n = 0, k = 0;
+    int dtype = L0B_F16;
+    void* w = nullptr;
+    __half* scales = nullptr;
+    int group = 0;  // int8 scale group (k = per output channel)
+    size_t bytes() const {
+        size_t b = static_cast<size_t>(n) * k * dtype_size(static_cast<l0b_dtype>(dtype));
+        if (dtype == L0B_I8) b += static_cast<size_t>(n) * (k / group) * 2;
+        return b;
+    }
+};
+
+struct ModelLayer {
+    float* in_norm = nullptr;
+    float* post_norm = nullptr;
+    ModelMatrix qkv, o, gate_up, down;
+    float* qkv_bias = nullptr;  // [q_dim + 2 kv_dim] or null
+    float* q_norm = nullptr;
+    float* k_norm = nullptr;
+    void* kc = nullptr;  // [batch_cap, max_seq, kv_dim] (cache dtype)
+    void* vc = nullptr;
+};
+
+// Rotary table per L/RopeFrequencies.cs:67-183 (default, linear, yarn, llama3).
+l0b_status rope_frequencies(const l0b_model_config& c, std::vector<float>* inv_freq, float* attention_factor);
+
+}  // namespace l0b

@@ -1,0 +1,74 @@
+// Host-side launchers of the op kernels (elementwise.cu, attention.cu, deltanet.cu).
+#pragma once
+
+#include <cuda_fp16.h>
+
+#include "runtime.h"
+
+namespace l0b {
+
+l0b_status k_rmsnorm(l0b_device* d, float* x, const float* res, const float* w, float* out, float eps, int width,
+                     int rows, int add_res);
+l0b_status k_bias_add(l0b_device* d, float* x, const float* b, int width, int rows);
+// q_stride / k_stride / in_stride: elements between tokens (<= 0: packed rows).
+l0b_status k_rope(l0b_device* d, float* q, float* k, const int* positions, const float* inv_freq, int hd, int nh,
+                  int nkv, float attn_scale, int rot, int tokens, long long q_stride = 0, long long k_stride = 0);
+l0b_status k_kv_store(l0b_device* d, const float* k, const float* v, void* kc, void* vc, int cache_dtype, int pos0,
+                      int kv_dim, int tokens, long long in_stride = 0);
+l0b_status k_swiglu(l0b_device* d, float* gate, const float* up, long long n);
+l0b_status k_add(l0b_device* d, float* a, const float* b, long long n);
+l0b_status k_sigmoid_gate(l0b_device* d, float* x, const float* g, long long n);
+l0b_status k_embedding(l0b_device* d, const int* ids, const void* table, int table_dtype, float* out, int h,
+                       long long count, int vocab, int* error);
+l0b_status k_copy(l0b_device* d, const float* src, float* dst, long long offset, long long n);
+l0b_status k_sampling(l0b_device* d, const float* logits, int* sampled, float temperature, float random_val,
+                      int vocab);
+l0b_status k_quantize(l0b_device* d, const void* w, int w_dtype, int n, int k, int group, int8_t* q, __half* s);
+
+// ------------------------------------------------------------------------------------------------
+// Attention (attention.cu)
+// ------------------------------------------------------------------------------------------------
+
+struct AttnParams {
+    const float* q;            // query rows: q + b * q_bstride, heads contiguous [nH * hd]
+    long long q_bstride;
+    // Fused decode: RoPE on q and on the new key (k_new) in-kernel, k/v of the query position
+    // stored to the cache by the CTA that owns it. rope == 0: q is used as is, cache already filled.
+    int rope;
+    int store_new;
+    const float* k_new;        // [nKv * hd] per b (pre-RoPE), stride new_bstride
+    const float* v_new;
+    long long new_bstride;
+    const float* inv_freq;     // [rot / 2]
+    int rot;                   // rotary dim
+    float attn_scale;
+    void* kc;                  // caches [maxSeq, kv_dim] per b, dtype cache_dtype, b stride cache_bstride
+    void* vc;
+    int cache_dtype;
+    long long cache_bstride;
+    int kv_dim;
+    // Query position of row b: positions[b] when non-null, else pos_base + b * pos_step.
+    const int* positions;
+    int pos_base;
+    int pos_step;
+    float* out;                // out + b * out_bstride, [nH * hd]
+    long long out_bstride;
+    float* part;               // split partials [B, nH, max_splits, hd]
+    float* part_ml;            // [B, nH, max_splits, 2]
+    unsigned* counters;        // [B, nKv] zeroed, reset by the last CTA
+    int nh, nkv, hd;
+    int chunk;                 // positions per split (multiple of 32)
+    int max_splits;
+    float scale;               // head_dim^-0.5
+};
+
+// Launches the split-KV attention kernel over grid (nKv, max_splits, batch).
+l0b_status attention_launch(l0b_device* d, const AttnParams& p, int batch);
+// Raw-stream variant used by callers without a device handle.
+l0b_status attention_launch_stream(cudaStream_t stream, const AttnParams& p, int batch);
+// Scratch floats / counters the kernel needs for (batch, nh, max_splits, hd).
+size_t attention_part_floats(int batch, int nh, int max_splits, int hd);
+// Picks the split length for a cache of max_seq positions and `work_items` (batch * nKv) rows.
+void attention_pick_split(int max_seq, int work_items, int sm_count, int* chunk, int* max_splits);
+
+}  // namespace l0b

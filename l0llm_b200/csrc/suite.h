@@ -1,0 +1,28 @@
+// LlmKernelSuite state: the int8 activation scratch and cached RoPE tables.
+#pragma once
+
+#include <map>
+#include <utility>
+
+#include "runtime.h"
+
+namespace l0b {
+// LlmGemvKernel.MaxRows: rows per ExecuteRows call and per prefill chunk of the model.
+constexpr int kMaxRows = 64;
+}  // namespace l0b
+
+struct l0b_suite {
+    l0b_device* dev = nullptr;
+    float* q8_x = nullptr;  // GemvQ8 activation scratch [q8_rows, q8_width] f32
+    int q8_rows = 0;
+    int q8_width = 0;
+    int q8_k = 0;
+    int* error_flag = nullptr;  // set by kernels that meet an out-of-range index (embedding ids)
+    std::map<std::pair<int, double>, float*> rope_tables;
+    ~l0b_suite();
+};
+
+namespace l0b {
+// Device table of RoPE inverse frequencies for (rotary dim, theta), built once per suite.
+l0b_status suite_rope_table(l0b_suite* s, int rot, double theta, const float** out);
+}  // namespace l0b

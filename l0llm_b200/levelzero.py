@@ -1,0 +1,663 @@
+"""Python mirror of the reference's kernel surface, bound to libl0b200.so through ctypes.
+
+Names follow the C# types the l0llm decoder calls (LevelZero.NET 2.0.0): LevelZeroRuntime,
+ComputeDevice, SharedBuffer, LlmKernelSuite with its ops (suite.Gemv.Execute(...), ...), and the
+model host LlmModel. Errors raise the exception types the reference throws. There is no CPU fallback:
+every op runs on the sm_100 device through the native library, and importing this module without the
+built library raises.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from pathlib import Path
+
+import numpy as np
+
+PKG = Path(__file__).resolve().parent
+LIB_PATH = PKG / "libl0b200.so"
+
+F32, F16, BF16, I8, I32, U8 = 0, 1, 2, 3, 4, 5
+NP_DTYPE = {F32: np.float32, F16: np.float16, BF16: np.uint16, I8: np.int8, I32: np.int32, U8: np.uint8}
+PRECISION = {"auto": 0, "float32": 1, "float16": 2, "int8": 3, "bfloat16": 4}
+ROPE_TYPES = {"default": 0, "linear": 1, "yarn": 2, "llama3": 3}
+
+
+class L0bError(RuntimeError):
+    status = -1
+
+
+class ArgumentException(L0bError, ValueError):
+    status = 1
+
+
+class ArgumentOutOfRangeException(ArgumentException):
+    status = 2
+
+
+class NotSupportedException(L0bError):
+    status = 3
+
+
+class InvalidOperationException(L0bError):
+    status = 4
+
+
+class InvalidDataException(L0bError):
+    status = 5
+
+
+class CudaError(L0bError):
+    status = 6
+
+
+class OutOfMemoryError(L0bError, MemoryError):
+    status = 7
+
+
+class NoDeviceError(L0bError):
+    status = 8
+
+
+class DeviceTimeoutError(L0bError):
+    status = 9
+
+
+class NcclError(L0bError):
+    status = 10
+
+
+_ERRORS = {c.status: c for c in (ArgumentException, ArgumentOutOfRangeException, NotSupportedException,
+                                  InvalidOperationException, InvalidDataException, CudaError, OutOfMemoryError,
+                                  NoDeviceError, DeviceTimeoutError, NcclError)}
+
+
+class ModelConfig(C.Structure):
+    """l0b_model_config: the HfModelConfig fields the decoder reads."""
+
+    _fields_ = [
+        ("hidden_size", C.c_int32), ("intermediate_size", C.c_int32), ("num_layers", C.c_int32),
+        ("num_attention_heads", C.c_int32), ("num_key_value_heads", C.c_int32), ("head_dim", C.c_int32),
+        ("vocab_size", C.c_int32), ("max_position_embeddings", C.c_int32), ("rms_norm_eps", C.c_float),
+        ("rope_theta", C.c_double), ("tie_word_embeddings", C.c_int32), ("attention_bias", C.c_int32),
+        ("qk_norm", C.c_int32), ("rope_type", C.c_int32), ("rope_factor", C.c_double),
+        ("rope_original_max_position", C.c_int32), ("rope_low_freq_factor", C.c_double),
+        ("rope_high_freq_factor", C.c_double), ("rope_beta_fast", C.c_double), ("rope_beta_slow", C.c_double),
+        ("rope_attention_factor", C.c_double), ("rope_mscale", C.c_double), ("rope_mscale_all_dim", C.c_double),
+        ("rope_truncate", C.c_int32), ("partial_rotary_factor", C.c_double), ("kv_dtype", C.c_int32),
+        ("q8_group", C.c_int32), ("tp_size", C.c_int32), ("tp_rank", C.c_int32),
+    ]
+
+
+_lib: C.CDLL | None = None
+
+
+def load_library() -> C.CDLL:
+    """Loads libl0b200.so (built by l0llm_b200.build); raises when it is missing."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not LIB_PATH.exists():
+        raise ImportError(f"{LIB_PATH} is missing: build it with `python -m l0llm_b200.build` "
+                          "(there is no CPU fallback)")
+    L = C.CDLL(str(LIB_PATH))
+    vp, i32, i64, f32 = C.c_void_p, C.c_int32, C.c_int64, C.c_float
+    pp = C.POINTER(C.c_void_p)
+    sigs = {
+        "l0b_last_error": (C.c_char_p, []),
+        "l0b_version": (i32, []),
+        "l0b_kernel_launch_count": (i64, []),
+        "l0b_runtime_is_available": (i32, [C.POINTER(i32)]),
+        "l0b_device_count": (i32, [C.POINTER(i32)]),
+        "l0b_device_info": (i32, [i32, C.c_char_p, i32, C.POINTER(i32), C.POINTER(i64)]),
+        "l0b_device_create": (i32, [i32, pp]),
+        "l0b_device_free": (i32, [vp]),
+        "l0b_device_begin_recording": (i32, [vp]),
+        "l0b_device_end_recording": (i32, [vp]),
+        "l0b_device_abort_recording": (i32, [vp]),
+        "l0b_device_is_recording": (i32, [vp, C.POINTER(i32)]),
+        "l0b_device_synchronize": (i32, [vp]),
+        "l0b_device_stream": (i32, [vp, pp]),
+        "l0b_device_graph_stats": (i32, [vp, C.POINTER(i64), C.POINTER(i64), C.POINTER(i64)]),
+        "l0b_device_set_pdl": (i32, [vp, i32]),
+        "l0b_buffer_alloc": (i32, [vp, i32, i64, pp]),
+        "l0b_buffer_alloc_from": (i32, [vp, i32, i64, vp, pp]),
+        "l0b_buffer_free": (i32, [vp]),
+        "l0b_buffer_write": (i32, [vp, i64, vp, i64]),
+        "l0b_buffer_read": (i32, [vp, i64, vp, i64]),
+        "l0b_buffer_copy": (i32, [vp, i64, vp, i64, i64]),
+        "l0b_buffer_zero": (i32, [vp]),
+        "l0b_buffer_count": (i32, [vp, C.POINTER(i64)]),
+        "l0b_buffer_dtype": (i32, [vp, C.POINTER(i32)]),
+        "l0b_buffer_device_ptr": (i32, [vp, pp]),
+        "l0b_suite_create": (i32, [vp, pp]),
+        "l0b_suite_free": (i32, [vp]),
+        "l0b_suite_has_q8": (i32, [vp]),
+        "l0b_suite_ensure_q8_scratch": (i32, [vp, i32, i32]),
+        "l0b_suite_q8_scratch_rows": (i32, [vp]),
+        "l0b_gemv_supports": (i32, [i32]),
+        "l0b_gemv_max_rows": (i32, []),
+        "l0b_gemv_q8_supports": (i32, [i32, i32]),
+        "l0b_gemv_q8_group_size": (i32, []),
+        "l0b_q8_quantize_out_in": (i32, [vp, i32, i32, i32, vp, vp]),
+        "l0b_q8_quantize_device": (i32, [vp, vp, i32, i32, i32, vp, vp, vp]),
+        "l0b_embedding_execute": (i32, [vp, vp, vp, vp, vp, i32, i32]),
+        "l0b_rmsnorm_execute": (i32, [vp, vp, vp, vp, vp, vp, f32, i32, i32, i32]),
+        "l0b_gemv_execute": (i32, [vp, vp, i32, i32, vp, vp, vp]),
+        "l0b_gemv_execute_rows": (i32, [vp, vp, i32, i32, i32, vp, vp, vp]),
+        "l0b_gemm_execute": (i32, [vp, vp, i32, i32, i32, vp, vp, vp]),
+        "l0b_gemv_q8_quantize": (i32, [vp, vp, i32, i32, vp]),
+        "l0b_gemv_q8_execute": (i32, [vp, vp, i32, i32, vp, vp, vp]),
+        "l0b_gemv_q8_execute_rows": (i32, [vp, vp, i32, i32, i32, vp, vp, vp]),
+        "l0b_bias_add_execute": (i32, [vp, vp, vp, vp, i32, i32]),
+        "l0b_rope_execute": (i32, [vp, vp, vp, vp, vp, i32, i32, i32, f32, i32]),
+        "l0b_rope_execute_with_frequencies": (i32, [vp, vp, vp, vp, vp, vp, i32, i32, i32, f32, i32, i32]),
+        "l0b_kv_cache_store_execute": (i32, [vp, vp, vp, vp, vp, vp, i32, i32]),
+        "l0b_kv_cache_store_execute_rows": (i32, [vp, vp, vp, vp, vp, vp, i32, i32, i32]),
+        "l0b_attention_execute": (i32, [vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, i32]),
+        "l0b_attention_execute_prefill": (i32, [vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, i32, i32]),
+        "l0b_sigmoid_gate_execute": (i32, [vp, vp, vp, vp, i32]),
+        "l0b_swiglu_execute": (i32, [vp, vp, vp, vp, i32]),
+        "l0b_add_execute": (i32, [vp, vp, vp, vp, i32]),
+        "l0b_copy_execute": (i32, [vp, vp, vp, vp, i32, i32]),
+        "l0b_sampling_execute": (i32, [vp, vp, vp, vp, f32, f32, i32]),
+        "l0b_causal_conv_execute": (i32, [vp, vp, vp, vp, vp, vp, i32, i32, i32]),
+        "l0b_gated_delta_execute": (i32, [vp, vp] + [vp] * 9 + [i32, i32, i32, i32, f32]),
+        "l0b_gated_delta_execute_grouped": (i32, [vp, vp] + [vp] * 9 + [i32, i32, i32, i32, i32, f32]),
+        "l0b_linear": (i32, [vp, vp, i32, i32, i32, vp, vp, vp, i32, vp, vp]),
+        "l0b_gemv_w8a16_raw": (i32, [vp, i32, i32, i32, vp, i32, vp, vp, i32, vp, i32]),
+        "l0b_linear_fused": (i32, [vp, vp, i32, i32, i32, vp, vp, vp, i32, vp, f32, i32, vp, vp]),
+        "l0b_model_config_init": (i32, [C.POINTER(ModelConfig)]),
+        "l0b_rope_frequencies": (i32, [C.POINTER(ModelConfig), vp, i32, C.POINTER(i32), C.POINTER(f32)]),
+        "l0b_model_create": (i32, [vp, vp, C.POINTER(ModelConfig), i32, i32, vp, pp]),
+        "l0b_model_free": (i32, [vp]),
+        "l0b_model_set_tensor": (i32, [vp, C.c_char_p, vp, i64]),
+        "l0b_model_init_synthetic": (i32, [vp, C.c_uint64, f32, f32, f32]),
+        "l0b_model_prefill": (i32, [vp, vp, i32, vp]),
+        "l0b_model_decode": (i32, [vp, i32, vp]),
+        "l0b_model_compute_logits": (i32, [vp, i32, i32, vp]),
+        "l0b_model_generate_greedy": (i32, [vp, vp, i32, i32, vp, i32, vp, C.POINTER(i32)]),
+        "l0b_model_position": (i32, [vp, C.POINTER(i32)]),
+        "l0b_model_reset_sequence": (i32, [vp]),
+        "l0b_model_projection_bytes": (i32, [vp, C.POINTER(i64)]),
+        "l0b_model_decode_greedy_device": (i32, [vp, i32, vp]),
+        "l0b_model_set_recording": (i32, [vp, i32]),
+        "l0b_model_set_fused": (i32, [vp, i32]),
+        "l0b_model_read_kv": (i32, [vp, i32, i32, i32, vp, vp]),
+    }
+    for name, (res, args) in sigs.items():
+        fn = getattr(L, name)
+        fn.restype = res
+        fn.argtypes = args
+    _lib = L
+    return L
+
+
+def check(status: int) -> None:
+    if status != 0:
+        msg = load_library().l0b_last_error().decode(errors="replace")
+        raise _ERRORS.get(status, L0bError)(msg or f"status {status}")
+
+
+def _p(arr: np.ndarray | None):
+    return None if arr is None else arr.ctypes.data_as(C.c_void_p)
+
+
+def _h(obj):
+    return None if obj is None else obj.handle
+
+
+# -------------------------------------------------------------------------------------------------
+# Runtime, device, buffers
+# -------------------------------------------------------------------------------------------------
+
+class LevelZeroRuntime:
+    @staticmethod
+    def IsAvailable() -> bool:
+        v = C.c_int32(0)
+        check(load_library().l0b_runtime_is_available(C.byref(v)))
+        return bool(v.value)
+
+    @staticmethod
+    def GetDefaultDevice() -> "ComputeDevice":
+        return ComputeDevice(0)
+
+    @staticmethod
+    def GetDevice(index: int) -> "ComputeDevice":
+        return ComputeDevice(index)
+
+    @staticmethod
+    def EnumerateDevices() -> list[tuple[int, str]]:
+        n = C.c_int32(0)
+        check(load_library().l0b_device_count(C.byref(n)))
+        out = []
+        for i in range(n.value):
+            name = C.create_string_buffer(256)
+            check(load_library().l0b_device_info(i, name, 256, None, None))
+            out.append((i, name.value.decode()))
+        return out
+
+
+class ComputeDevice:
+    def __init__(self, index: int = 0):
+        h = C.c_void_p()
+        check(load_library().l0b_device_create(index, C.byref(h)))
+        self.handle = h
+        self.index = index
+
+    def AllocShared(self, dtype_or_data, count: int | None = None) -> "SharedBuffer":
+        """AllocShared<T>(count) with a dtype code, or AllocShared(T[] data) with a numpy array."""
+        if isinstance(dtype_or_data, np.ndarray):
+            return SharedBuffer.from_array(self, dtype_or_data)
+        return SharedBuffer(self, dtype_or_data, count)
+
+    def BeginRecording(self):
+        check(load_library().l0b_device_begin_recording(self.handle))
+
+    def EndRecording(self):
+        check(load_library().l0b_device_end_recording(self.handle))
+
+    def AbortRecording(self):
+        check(load_library().l0b_device_abort_recording(self.handle))
+
+    @property
+    def IsRecording(self) -> bool:
+        v = C.c_int32()
+        check(load_library().l0b_device_is_recording(self.handle, C.byref(v)))
+        return bool(v.value)
+
+    def Synchronize(self):
+        check(load_library().l0b_device_synchronize(self.handle))
+
+    def graph_stats(self) -> tuple[int, int, int]:
+        b, r, u = C.c_int64(), C.c_int64(), C.c_int64()
+        check(load_library().l0b_device_graph_stats(self.handle, C.byref(b), C.byref(r), C.byref(u)))
+        return b.value, r.value, u.value
+
+    def set_pdl(self, enabled: bool):
+        check(load_library().l0b_device_set_pdl(self.handle, 1 if enabled else 0))
+
+    def Dispose(self):
+        if self.handle:
+            load_library().l0b_device_free(self.handle)
+            self.handle = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.Dispose()
+
+
+class SharedBuffer:
+    def __init__(self, device: ComputeDevice, dtype: int, count: int, _handle=None):
+        self.device = device
+        self.dtype = dtype
+        self.Count = int(count)
+        if _handle is None:
+            h = C.c_void_p()
+            check(load_library().l0b_buffer_alloc(device.handle, dtype, self.Count, C.byref(h)))
+            _handle = h
+        self.handle = _handle
+
+    @classmethod
+    def from_array(cls, device: ComputeDevice, data: np.ndarray, dtype: int | None = None) -> "SharedBuffer":
+        if dtype is None:
+            dtype = {np.dtype(np.float32): F32, np.dtype(np.float16): F16, np.dtype(np.int8): I8,
+                     np.dtype(np.int32): I32, np.dtype(np.uint8): U8, np.dtype(np.uint16): BF16}[data.dtype]
+        arr = np.ascontiguousarray(data, NP_DTYPE[dtype]).ravel()
+        b = cls(device, dtype, arr.size)
+        b.Write(arr)
+        return b
+
+    def Write(self, data: np.ndarray, offset: int = 0):
+        arr = np.ascontiguousarray(data, NP_DTYPE[self.dtype]).ravel()
+        check(load_library().l0b_buffer_write(self.handle, offset, _p(arr), arr.size))
+
+    def ToArray(self, offset: int = 0, count: int | None = None) -> np.ndarray:
+        n = self.Count - offset if count is None else count
+        out = np.zeros(n, NP_DTYPE[self.dtype])
+        check(load_library().l0b_buffer_read(self.handle, offset, _p(out), n))
+        return out
+
+    def Zero(self):
+        check(load_library().l0b_buffer_zero(self.handle))
+
+    @property
+    def Pointer(self) -> int:
+        p = C.c_void_p()
+        check(load_library().l0b_buffer_device_ptr(self.handle, C.byref(p)))
+        return p.value or 0
+
+    def Dispose(self):
+        if self.handle:
+            load_library().l0b_buffer_free(self.handle)
+            self.handle = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.Dispose()
+
+
+# -------------------------------------------------------------------------------------------------
+# Kernel suite
+# -------------------------------------------------------------------------------------------------
+
+class _Op:
+    def __init__(self, suite: "LlmKernelSuite"):
+        self.suite = suite
+        self.L = load_library()
+
+    def _s(self):
+        return self.suite.handle
+
+
+class _Embedding(_Op):
+    def Execute(self, dev, ids, table, out, h, count):
+        check(self.L.l0b_embedding_execute(self._s(), dev.handle, ids.handle, table.handle, out.handle, h, count))
+
+
+class _RMSNorm(_Op):
+    def Execute(self, dev, x, res, w, out, eps, width, rows, addResidual):
+        check(self.L.l0b_rmsnorm_execute(self._s(), dev.handle, x.handle, _h(res), w.handle, out.handle, eps, width,
+                                         rows, 1 if addResidual else 0))
+
+
+class _Gemv(_Op):
+    @staticmethod
+    def Supports(n: int) -> bool:
+        return bool(load_library().l0b_gemv_supports(n))
+
+    @staticmethod
+    def MaxRows() -> int:
+        return load_library().l0b_gemv_max_rows()
+
+    def Execute(self, dev, N, K, x, W, y):
+        check(self.L.l0b_gemv_execute(self._s(), dev.handle, N, K, x.handle, W.handle, y.handle))
+
+    def ExecuteRows(self, dev, M, N, K, x, W, y):
+        check(self.L.l0b_gemv_execute_rows(self._s(), dev.handle, M, N, K, x.handle, W.handle, y.handle))
+
+
+class _Gemm(_Op):
+    def Execute(self, dev, M, N, K, A, B, Cb):
+        check(self.L.l0b_gemm_execute(self._s(), dev.handle, M, N, K, A.handle, B.handle, Cb.handle))
+
+
+class _GemvQ8(_Op):
+    GroupSize = 32
+
+    @staticmethod
+    def Supports(n: int, k: int) -> bool:
+        return bool(load_library().l0b_gemv_q8_supports(n, k))
+
+    def Quantize(self, dev, rows, K, x, scratch=None):
+        check(self.L.l0b_gemv_q8_quantize(self._s(), dev.handle, rows, K, x.handle))
+
+    def Execute(self, dev, N, K, scratch, words, scales, y):
+        check(self.L.l0b_gemv_q8_execute(self._s(), dev.handle, N, K, words.handle, scales.handle, y.handle))
+
+    def ExecuteRows(self, dev, M, N, K, scratch, words, scales, y):
+        check(self.L.l0b_gemv_q8_execute_rows(self._s(), dev.handle, M, N, K, words.handle, scales.handle, y.handle))
+
+
+class _BiasAdd(_Op):
+    def Execute(self, dev, x, b, width, rows):
+        check(self.L.l0b_bias_add_execute(self._s(), dev.handle, x.handle, b.handle, width, rows))
+
+
+class _RoPE(_Op):
+    def Execute(self, dev, q, k, positions, hd, nH, nKv, theta, tokens):
+        check(self.L.l0b_rope_execute(self._s(), dev.handle, q.handle, k.handle, positions.handle, hd, nH, nKv, theta,
+                                      tokens))
+
+    def ExecuteWithFrequencies(self, dev, q, k, positions, invFreq, hd, nH, nKv, attnScale, tokens, rotaryDim):
+        check(self.L.l0b_rope_execute_with_frequencies(self._s(), dev.handle, q.handle, k.handle, positions.handle,
+                                                       invFreq.handle, hd, nH, nKv, attnScale, tokens, rotaryDim))
+
+
+class _KvCacheStore(_Op):
+    def Execute(self, dev, k, v, Kc, Vc, pos0, kvDim):
+        check(self.L.l0b_kv_cache_store_execute(self._s(), dev.handle, k.handle, v.handle, Kc.handle, Vc.handle, pos0,
+                                                kvDim))
+
+    def ExecuteRows(self, dev, k, v, Kc, Vc, pos0, kvDim, tokens):
+        check(self.L.l0b_kv_cache_store_execute_rows(self._s(), dev.handle, k.handle, v.handle, Kc.handle, Vc.handle,
+                                                     pos0, kvDim, tokens))
+
+
+class _Attention(_Op):
+    def Execute(self, dev, q, Kc, Vc, out, hd, nH, nKv, seqLen, maxSeq):
+        check(self.L.l0b_attention_execute(self._s(), dev.handle, q.handle, Kc.handle, Vc.handle, out.handle, hd, nH,
+                                           nKv, seqLen, maxSeq))
+
+    def ExecutePrefill(self, dev, q, Kc, Vc, out, hd, nH, nKv, pos0, tokens, maxSeq):
+        check(self.L.l0b_attention_execute_prefill(self._s(), dev.handle, q.handle, Kc.handle, Vc.handle, out.handle,
+                                                   hd, nH, nKv, pos0, tokens, maxSeq))
+
+
+class _Unary(_Op):
+    def __init__(self, suite, fn):
+        super().__init__(suite)
+        self.fn = getattr(self.L, fn)
+
+    def Execute(self, dev, a, b, n):
+        check(self.fn(self._s(), dev.handle, a.handle, b.handle, n))
+
+
+class _Copy(_Op):
+    def Execute(self, dev, src, dst, offset, n):
+        check(self.L.l0b_copy_execute(self._s(), dev.handle, src.handle, dst.handle, offset, n))
+
+
+class _Sampling(_Op):
+    def Execute(self, dev, logits, sampled, temperature, randomVal, vocab):
+        check(self.L.l0b_sampling_execute(self._s(), dev.handle, logits.handle, sampled.handle, temperature,
+                                          randomVal, vocab))
+
+
+class _CausalConv(_Op):
+    def Execute(self, dev, qkv, convState, convW, out, convDim, k, tokens):
+        check(self.L.l0b_causal_conv_execute(self._s(), dev.handle, qkv.handle, convState.handle, convW.handle,
+                                             out.handle, convDim, k, tokens))
+
+
+class _GatedDelta(_Op):
+    def Execute(self, dev, conv, z, b, a, A_log, dt_bias, normW, S, out, Hv, dk, dv, tokens, eps):
+        check(self.L.l0b_gated_delta_execute(self._s(), dev.handle, conv.handle, z.handle, b.handle, a.handle,
+                                             A_log.handle, dt_bias.handle, normW.handle, S.handle, out.handle, Hv, dk,
+                                             dv, tokens, eps))
+
+    def ExecuteGrouped(self, dev, conv, z, b, a, A_log, dt_bias, normW, S, out, Hk, Hv, dk, dv, tokens, eps):
+        check(self.L.l0b_gated_delta_execute_grouped(self._s(), dev.handle, conv.handle, z.handle, b.handle, a.handle,
+                                                     A_log.handle, dt_bias.handle, normW.handle, S.handle, out.handle,
+                                                     Hk, Hv, dk, dv, tokens, eps))
+
+
+class LlmKernelSuite:
+    """LlmKernelSuite.Create(device): the op objects the reference decoder calls."""
+
+    def __init__(self, device: ComputeDevice):
+        h = C.c_void_p()
+        check(load_library().l0b_suite_create(device.handle, C.byref(h)))
+        self.handle = h
+        self.device = device
+        self.Embedding = _Embedding(self)
+        self.RMSNorm = _RMSNorm(self)
+        self.Gemv = _Gemv(self)
+        self.Gemm = _Gemm(self)
+        self.GemvQ8 = _GemvQ8(self)
+        self.BiasAdd = _BiasAdd(self)
+        self.RoPE = _RoPE(self)
+        self.KvCacheStore = _KvCacheStore(self)
+        self.Attention = _Attention(self)
+        self.SigmoidGate = _Unary(self, "l0b_sigmoid_gate_execute")
+        self.SwiGLU = _Unary(self, "l0b_swiglu_execute")
+        self.Add = _Unary(self, "l0b_add_execute")
+        self.Copy = _Copy(self)
+        self.Sampling = _Sampling(self)
+        self.CausalConv = _CausalConv(self)
+        self.GatedDelta = _GatedDelta(self)
+
+    @classmethod
+    def Create(cls, device: ComputeDevice) -> "LlmKernelSuite":
+        return cls(device)
+
+    def EnsureQ8Scratch(self, device, rows: int, width: int):
+        check(load_library().l0b_suite_ensure_q8_scratch(self.handle, rows, width))
+
+    @property
+    def Q8ScratchRows(self) -> int:
+        return load_library().l0b_suite_q8_scratch_rows(self.handle)
+
+    def linear(self, dev, M, N, K, x, W, scales, group, bias, y):
+        """Y = X W^T for W in the [out, in] order (f32/f16/bf16/int8 + scales)."""
+        check(load_library().l0b_linear(self.handle, dev.handle, M, N, K, x.handle, W.handle, _h(scales), group,
+                                        _h(bias), y.handle))
+
+    EPI_STORE, EPI_ACCUM, EPI_SWIGLU = 0, 1, 2
+
+    def linear_fused(self, dev, M, N, K, x, W, scales, group, norm_w, eps, epilogue, bias, out):
+        """RMSNorm prologue (norm_w) + projection + store / residual-add / SwiGLU epilogue, one kernel."""
+        check(load_library().l0b_linear_fused(self.handle, dev.handle, M, N, K, x.handle, W.handle, _h(scales),
+                                              group, _h(norm_w), eps, epilogue, _h(bias), out.handle))
+
+    def Dispose(self):
+        if self.handle:
+            load_library().l0b_suite_free(self.handle)
+            self.handle = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.Dispose()
+
+
+def q8_quantize_out_in(hf: np.ndarray, group: int = 32) -> tuple[np.ndarray, np.ndarray]:
+    """LlmQ8Quantizer.QuantizeOutIn: HF [N, K] fp32 -> (int8 [N, K], fp16 scales [N, K/group])."""
+    hf = np.ascontiguousarray(hf, np.float32)
+    N, K = hf.shape
+    g = group if group > 0 else K
+    q = np.zeros((N, K), np.int8)
+    s = np.zeros((N, K // g), np.uint16)
+    check(load_library().l0b_q8_quantize_out_in(_p(hf), N, K, g, _p(q), _p(s)))
+    return q, s.view(np.float16)
+
+
+def rope_frequencies(cfg: ModelConfig) -> tuple[np.ndarray, float]:
+    n = C.c_int32()
+    att = C.c_float()
+    check(load_library().l0b_rope_frequencies(C.byref(cfg), None, 0, C.byref(n), C.byref(att)))
+    out = np.zeros(n.value, np.float32)
+    check(load_library().l0b_rope_frequencies(C.byref(cfg), _p(out), n.value, C.byref(n), C.byref(att)))
+    return out, float(att.value)
+
+
+def kernel_launch_count() -> int:
+    return int(load_library().l0b_kernel_launch_count())
+
+
+# -------------------------------------------------------------------------------------------------
+# Model host (LlmModel)
+# -------------------------------------------------------------------------------------------------
+
+def model_config(**kw) -> ModelConfig:
+    cfg = ModelConfig()
+    check(load_library().l0b_model_config_init(C.byref(cfg)))
+    for k, v in kw.items():
+        if k == "rope_type" and isinstance(v, str):
+            v = ROPE_TYPES[v]
+        setattr(cfg, k, v)
+    return cfg
+
+
+class LlmModel:
+    """LlmModel: prefill / decode / greedy generation on the device."""
+
+    def __init__(self, device: ComputeDevice, suite: LlmKernelSuite, cfg: ModelConfig, max_seq_len: int,
+                 precision: str = "auto", comm=None):
+        h = C.c_void_p()
+        check(load_library().l0b_model_create(device.handle, suite.handle, C.byref(cfg), max_seq_len,
+                                              PRECISION[precision], comm, C.byref(h)))
+        self.handle = h
+        self.cfg = cfg
+        self.vocab = cfg.vocab_size // max(1, cfg.tp_size)
+        self.MaxSeqLen = max_seq_len
+
+    def init_synthetic(self, seed: int, std: float = 0.02, scale_lo: float = 1e-3, scale_hi: float = 2e-2):
+        check(load_library().l0b_model_init_synthetic(self.handle, seed, std, scale_lo, scale_hi))
+
+    def set_tensor(self, name: str, data: np.ndarray):
+        d = np.ascontiguousarray(data, np.float32).ravel()
+        check(load_library().l0b_model_set_tensor(self.handle, name.encode(), _p(d), d.size))
+
+    def Prefill(self, ids) -> np.ndarray:
+        ids = np.ascontiguousarray(ids, np.int32)
+        logits = np.zeros(self.vocab, np.float32)
+        check(load_library().l0b_model_prefill(self.handle, _p(ids), ids.size, _p(logits)))
+        return logits
+
+    def Decode(self, token: int, logits: np.ndarray | None = None) -> np.ndarray:
+        out = np.zeros(self.vocab, np.float32) if logits is None else logits
+        check(load_library().l0b_model_decode(self.handle, int(token), _p(out)))
+        return out
+
+    def ComputeLogits(self, token: int, position: int) -> np.ndarray:
+        logits = np.zeros(self.vocab, np.float32)
+        check(load_library().l0b_model_compute_logits(self.handle, int(token), int(position), _p(logits)))
+        return logits
+
+    def GenerateGreedy(self, ids, max_new: int, stop_ids=()) -> list[int]:
+        ids = np.ascontiguousarray(ids, np.int32)
+        stops = np.ascontiguousarray(list(stop_ids) or [0], np.int32)
+        out = np.zeros(max(1, max_new), np.int32)
+        n = C.c_int32()
+        check(load_library().l0b_model_generate_greedy(self.handle, _p(ids), ids.size, max_new, _p(stops),
+                                                       len(stop_ids), _p(out), C.byref(n)))
+        return out[: n.value].tolist()
+
+    def decode_greedy_device(self, steps: int) -> np.ndarray:
+        out = np.zeros(max(1, steps), np.int32)
+        check(load_library().l0b_model_decode_greedy_device(self.handle, steps, _p(out)))
+        return out[:steps]
+
+    @property
+    def Position(self) -> int:
+        v = C.c_int32()
+        check(load_library().l0b_model_position(self.handle, C.byref(v)))
+        return v.value
+
+    def ResetSequence(self):
+        check(load_library().l0b_model_reset_sequence(self.handle))
+
+    @property
+    def ProjectionBytes(self) -> int:
+        v = C.c_int64()
+        check(load_library().l0b_model_projection_bytes(self.handle, C.byref(v)))
+        return v.value
+
+    def set_recording(self, on: bool):
+        check(load_library().l0b_model_set_recording(self.handle, 1 if on else 0))
+
+    def set_fused(self, on: bool):
+        check(load_library().l0b_model_set_fused(self.handle, 1 if on else 0))
+
+    def read_kv(self, layer: int, row0: int, rows: int) -> tuple[np.ndarray, np.ndarray]:
+        kvd = (self.cfg.num_key_value_heads // max(1, self.cfg.tp_size)) * self.cfg.head_dim
+        k = np.zeros(rows * kvd, np.float32)
+        v = np.zeros(rows * kvd, np.float32)
+        check(load_library().l0b_model_read_kv(self.handle, layer, row0, rows, _p(k), _p(v)))
+        return k.reshape(rows, kvd), v.reshape(rows, kvd)
+
+    def Dispose(self):
+        if self.handle:
+            load_library().l0b_model_free(self.handle)
+            self.handle = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.Dispose()

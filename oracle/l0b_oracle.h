@@ -1,0 +1,123 @@
+/*
+ * l0b_oracle.h -- CPU restatement of the l0llm decoder hot path. TEST INFRASTRUCTURE ONLY.
+ *
+ * This is the checker the CUDA backend is compared against (tests/, __graft_entry__.smoke() and
+ * bench.py's cpu_baseline / --impl reference arm). Nothing in the product library links or calls it.
+ *
+ * The reference (hf-laboratories/l0llm) is C#; its GPU arithmetic lives in the external NuGet package
+ * LevelZero.NET 2.0.0 (pinned in src/HFLabs.ML.LLM.LevelZero/HFLabs.ML.LLM.LevelZero.csproj:16), which is
+ * absent here, and no .NET SDK exists, so nothing of the reference can be compiled or run. Each function
+ * restates the semantics of the reference call site it names (`L/` = src/HFLabs.ML.LLM.LevelZero/,
+ * `T/` = tests/HFLabs.ML.LLM.LevelZero.Tests/) and is pinned against the reference's own known-answer
+ * tests and golden vectors: T/LlmMatrixTests.cs:99-130 (GEMV KAT), T/golden/rope.golden.json +
+ * T/RopeFrequenciesTests.cs:25-47 (RoPE tables), T/RopeLlama3Tests.cs:8-38 (llama3 table),
+ * T/LlmMatrixInt8Tests.cs:45-119 (int8 sizes and error bound). The int8 word/scale packing and the
+ * quantizer rounding of LevelZero.NET are not visible in any source: that layout is an assumption
+ * (documented in l0b200.h) and its parity is unpinned. Dot products accumulate in double, as the
+ * reference's CPU checks do (T/LlmMatrixTests.cs:71-79).
+ */
+#ifndef L0B_ORACLE_H
+#define L0B_ORACLE_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum { ORC_F32 = 0, ORC_F16 = 1, ORC_BF16 = 2, ORC_I8 = 3 };
+enum { ORC_ROPE_DEFAULT = 0, ORC_ROPE_LINEAR = 1, ORC_ROPE_YARN = 2, ORC_ROPE_LLAMA3 = 3 };
+enum { ORC_SYN_NORMAL = 0, ORC_SYN_CONST = 1, ORC_SYN_I8 = 2, ORC_SYN_UNIFORM = 3 };
+
+/* fp16 / bf16 conversions (round to nearest even). */
+uint16_t orc_f32_to_f16(float v);
+float orc_f16_to_f32(uint16_t h);
+uint16_t orc_f32_to_bf16(float v);
+float orc_bf16_to_f32(uint16_t h);
+void orc_convert(const float* src, void* dst, int dtype, int64_t n);
+
+/* y[m, n] = sum_k x[m, k] * W[n, k] with W [N, K] (HF [out, in]); int8 W dequantised with f16 scales
+ * [N, K/group]. L/LlmMatrix.cs:122-171 (GemvQ8 for int8, Gemv for 16/32-bit). */
+void orc_gemv_out_in(int M, int N, int K, const float* x, int wdtype, const void* w, const uint16_t* scales,
+                     int group, float* y);
+/* Reference layout W [K, N] (f32 or f16): y[m, n] = sum_k x[m, k] * W[k, n]. T/LlmMatrixTests.cs:71-79. */
+void orc_gemv_in_out(int M, int N, int K, const float* x, int w_is_half, const void* w, float* y);
+/* Symmetric int8 quantisation of [N, K] with one scale per `group` inputs (L/LlmMatrix.cs:89-93). */
+void orc_q8_quantize(const float* w, int N, int K, int group, int8_t* q, uint16_t* scales);
+
+/* RMSNorm.Execute (L/LlmDecoderLayer.cs:167,183-184): [x += res]; out = x * rsqrt(mean(x^2) + eps) * w. */
+void orc_rmsnorm(float* x, const float* res, const float* w, float* out, float eps, int width, int rows, int add_res);
+void orc_bias_add(float* x, const float* b, int width, int rows);
+void orc_swiglu(float* gate, const float* up, int64_t n);
+void orc_add(float* a, const float* b, int64_t n);
+void orc_sigmoid_gate(float* x, const float* g, int64_t n);
+/* Embedding.Execute (L/LlmModel.cs:360,424), table f32/f16/bf16. */
+void orc_embedding(const int* ids, const void* table, int table_dtype, float* out, int h, int64_t count);
+
+/* RopeFrequencies.Compute (L/RopeFrequencies.cs:67-183). Returns the number of frequencies. */
+int orc_rope_frequencies(int dim, double theta, int max_pos, int type, double factor, int original_max,
+                         double low_freq, double high_freq, double beta_fast, double beta_slow, double attention_factor,
+                         double mscale, double mscale_all_dim, int truncate, float* out, float* attention_out);
+/* RoPE.Execute / ExecuteWithFrequencies (L/LlmDecoderLayer.cs:411-425): HF rotate-half pairs. */
+void orc_rope(float* q, float* k, const int* positions, const float* inv_freq, int hd, int nh, int nkv,
+              float attn_scale, int rot, int tokens);
+/* KvCacheStore (L/LlmDecoderLayer.cs:322,368): rows stored at the cache dtype. */
+void orc_kv_store(const float* k, const float* v, void* kc, void* vc, int cache_dtype, int pos0, int kv_dim, int tokens);
+/* Attention.Execute / ExecutePrefill (L/LlmDecoderLayer.cs:325-327,369-371): query t sits at position
+ * pos0 + t and attends to cache slots [0, pos0 + t]; softmax(q k / sqrt(hd)) v in double. */
+void orc_attention(const float* q, const void* kc, const void* vc, int cache_dtype, float* out, int hd, int nh,
+                   int nkv, int pos0, int tokens);
+/* Sampling.Execute (L/LlmModel.cs:398): argmax (first maximum) or inverse-CDF sample. */
+int orc_argmax(const float* x, int n);
+int orc_sample(const float* logits, int vocab, float temperature, float random_val);
+
+/* Seeded synthetic tensors: restates the generator of the CUDA model (splitmix64 hashing, exactly
+ * rounded float steps), so both sides hold identical weights. */
+uint64_t orc_tensor_stream(uint64_t seed, uint64_t id);
+void orc_synth_fill(void* dst, int dtype, int64_t count, uint64_t stream, int mode, float a, float b, int64_t row_len,
+                    int64_t full_len, int64_t row0, int64_t col0);
+
+/* CausalConv.Execute (L/LlmDecoderLayer.cs:392). state [conv_dim, k-1] oldest first; w [conv_dim, k]. */
+void orc_causal_conv(const float* x, float* state, const float* w, float* out, int conv_dim, int kernel, int tokens);
+/* GatedDelta.Execute (L/LlmDecoderLayer.cs:393-395), Hk key heads shared by Hv/Hk value heads each.
+ * conv rows [q (Hk*dk) | k (Hk*dk) | v (Hv*dv)], state [Hv, dk, dv]. */
+void orc_gated_delta(const float* conv, const float* z, const float* b, const float* a, const float* a_log,
+                     const float* dt_bias, const float* norm_w, float* state, float* out, int hk, int hv, int dk,
+                     int dv, int tokens, float eps);
+
+/* ----------------------------------------------------------------------------------------------- */
+/* Whole decoder (LlmModel.Step / LlmDecoderLayer.Forward, L/LlmModel.cs:402-444,                   */
+/* L/LlmDecoderLayer.cs:129-196, 290-334), one token at a time.                                      */
+/* ----------------------------------------------------------------------------------------------- */
+typedef struct orc_config {
+    int hidden, inter, layers, heads, kv_heads, head_dim, vocab, max_pos;
+    float eps;
+    double theta;
+    int tie, bias, qk_norm;
+    int rope_type;
+    double rope_factor;
+    int rope_original_max;
+    double rope_low, rope_high, rope_beta_fast, rope_beta_slow, rope_attention;
+    int wdtype, group, kv_dtype;
+} orc_config;
+
+typedef struct orc_model orc_model;
+orc_model* orc_model_create(const orc_config* cfg, int max_seq);
+void orc_model_free(orc_model* m);
+int orc_model_init_synthetic(orc_model* m, uint64_t seed, float std, float scale_lo, float scale_hi);
+int orc_model_set_tensor(orc_model* m, const char* name, const float* data, int64_t count);
+/* Feeds token `token` at `position` and writes the vocab logits of the next token. */
+int orc_model_step(orc_model* m, int token, int position, float* logits);
+/* Runs only `layers_to_run` layers (<= cfg.layers) for timing samples; 0 = all. */
+void orc_model_set_layer_limit(orc_model* m, int layers_to_run);
+/* Reads the K/V cache rows of a layer as f32. */
+int orc_model_read_kv(orc_model* m, int layer, int row0, int rows, float* keys, float* values);
+/* Threads used by the oracle's parallel loops (OpenMP). */
+int orc_num_threads(void);
+void orc_set_num_threads(int n);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif
