@@ -444,6 +444,17 @@ L0B_API l0b_status l0b_model_decode_greedy_device(l0b_model* model, int32_t step
 L0B_API l0b_status l0b_model_set_recording(l0b_model* model, int32_t enabled);
 /* Selects the fused decode kernels (1, default) or the one-op-per-reference-call sequence (0). */
 L0B_API l0b_status l0b_model_set_fused(l0b_model* model, int32_t enabled);
+/* LlmDecoderLayer.Probe (L/LlmDecoderLayer.cs:113-119): when set, steps run the reference op sequence
+ * without command-list recording and call `fn` after each stage of each layer with a host copy of the
+ * stage's buffer (row 0 of the step). Stages: input_norm, q, k, v (after bias, before RoPE), attn_out
+ * (after o_proj), post_norm, mlp_out, output. The host copy is reused: copy what you need inside the
+ * callback. fn = NULL removes the probe. */
+typedef void (*l0b_probe_fn)(void* user, int32_t layer, const char* stage, const float* values, int64_t count);
+L0B_API l0b_status l0b_model_set_probe(l0b_model* model, l0b_probe_fn fn, void* user);
+/* Copies raw weight storage of layer `layer` (-1 = LM head) for inspection: kind 0 = stacked q/k/v,
+ * 1 = o_proj, 2 = stacked gate/up, 3 = down_proj (weights in the model precision's dtype, [out, in]);
+ * kind 4..7 = the int8 scales of the same matrices. bytes must equal the storage size. */
+L0B_API l0b_status l0b_model_read_weight(l0b_model* model, int32_t layer, int32_t kind, void* out, int64_t bytes);
 /* Reads layer `layer`'s KV cache rows [row0, row0 + rows) as f32 (CaptureState's KV part,
  * L/LlmModel.cs:257-281). keys/values hold rows * kvDim floats. */
 L0B_API l0b_status l0b_model_read_kv(l0b_model* model, int32_t layer, int32_t row0, int32_t rows,

@@ -73,6 +73,9 @@ struct l0b_model {
     bool fused = true;
     bool recording = true;
     int position = 0;
+    l0b_probe_fn probe = nullptr;
+    void* probe_user = nullptr;
+    std::vector<float> probe_host;
     std::vector<void*> allocations;
 
     ~l0b_model() {
@@ -292,6 +295,17 @@ GemvParams linear_params(const ModelMatrix& w, int m_rows, const void* x, long l
 
 l0b_status gemv(l0b_model* m, const ModelMatrix& w, const GemvParams& p) { return gemv_nk_launch(m->dev, w.dtype, p); }
 
+// Probe (LlmDecoderLayer.Emit, L/LlmDecoderLayer.cs:427): hand a host copy of row 0 of a stage buffer to
+// the callback. Only reached when the step runs unrecorded.
+l0b_status emit(l0b_model* m, int li, const char* stage, const float* dptr, long long count) {
+    if (!m->probe) return L0B_OK;
+    m->probe_host.resize(static_cast<size_t>(count));
+    L0B_CHECK_CUDA(cudaStreamSynchronize(m->dev->stream));
+    L0B_CHECK_CUDA(cudaMemcpy(m->probe_host.data(), dptr, count * sizeof(float), cudaMemcpyDeviceToHost));
+    m->probe(m->probe_user, li, stage, m->probe_host.data(), count);
+    return L0B_OK;
+}
+
 // Fused decoder layer for `rows` tokens. decode: each row is its own sequence (cache row b, position
 // pos[b]); prefill: the rows are consecutive positions of sequence 0 starting at pos0.
 l0b_status record_layer_fused(l0b_model* m, int li, int rows, bool decode, int pos0) {
@@ -373,6 +387,7 @@ l0b_status record_layer_reference(l0b_model* m, int li, int rows, bool decode, i
     const l0b_model_config& c = m->cfg;
     l0b_device* d = m->dev;
     L0B_TRY(k_rmsnorm(d, m->hidden, nullptr, L.in_norm, m->normed, c.rms_norm_eps, m->h, rows, 0));
+    L0B_TRY(emit(m, li, "input_norm", m->normed, m->h));
     GemvParams p = linear_params(L.qkv, rows, m->normed, m->h);
     p.nseg = 3;
     p.seg[0] = {m->qb, nullptr, m->qdim, m->qdim};
@@ -388,6 +403,9 @@ l0b_status record_layer_reference(l0b_model* m, int li, int rows, bool decode, i
         L0B_TRY(k_rmsnorm(d, m->qb, nullptr, L.q_norm, m->qb, c.rms_norm_eps, m->hd, rows * m->nh, 0));
         L0B_TRY(k_rmsnorm(d, m->kb, nullptr, L.k_norm, m->kb, c.rms_norm_eps, m->hd, rows * m->nkv, 0));
     }
+    L0B_TRY(emit(m, li, "q", m->qb, m->qdim));
+    L0B_TRY(emit(m, li, "k", m->kb, m->kvdim));
+    L0B_TRY(emit(m, li, "v", m->vb, m->kvdim));
     const int* positions = decode ? m->pos : m->prompt_pos;
     L0B_TRY(k_rope(d, m->qb, m->kb, positions, m->inv_freq, m->hd, m->nh, m->nkv, m->attn_scale, m->rot, rows));
     L0B_TRY(k_kv_store(d, m->kb, m->vb, L.kc, L.vc, m->cache_dtype, pos0, m->kvdim, rows));
@@ -420,7 +438,9 @@ l0b_status record_layer_reference(l0b_model* m, int li, int rows, bool decode, i
     p = linear_params(L.o, rows, m->attn, m->qdim);
     p.seg[0] = {m->attn_proj, nullptr, m->h, m->h};
     L0B_TRY(gemv(m, L.o, p));
+    L0B_TRY(emit(m, li, "attn_out", m->attn_proj, m->h));
     L0B_TRY(k_rmsnorm(d, m->hidden, m->attn_proj, L.post_norm, m->normed, c.rms_norm_eps, m->h, rows, 1));
+    L0B_TRY(emit(m, li, "post_norm", m->normed, m->h));
     p = linear_params(L.gate_up, rows, m->normed, m->h);
     p.nseg = 2;
     p.seg[0] = {m->gate, nullptr, m->inter, m->inter};
@@ -430,14 +450,16 @@ l0b_status record_layer_reference(l0b_model* m, int li, int rows, bool decode, i
     p = linear_params(L.down, rows, m->gate, m->inter);
     p.seg[0] = {m->down, nullptr, m->h, m->h};
     L0B_TRY(gemv(m, L.down, p));
-    return k_add(d, m->hidden, m->down, static_cast<long long>(rows) * m->h);
+    L0B_TRY(emit(m, li, "mlp_out", m->down, m->h));
+    L0B_TRY(k_add(d, m->hidden, m->down, static_cast<long long>(rows) * m->h));
+    return emit(m, li, "output", m->hidden, m->h);
 }
 
 // Final norm, LM head and greedy argmax for `rows` rows starting at hidden row `row0`.
 l0b_status record_head(l0b_model* m, int row0, int rows, int advance) {
     const l0b_model_config& c = m->cfg;
     l0b_device* d = m->dev;
-    if (m->fused) {
+    if (m->fused && !m->probe) {
         GemvParams p = linear_params(m->lm_head, rows, m->hidden + static_cast<long long>(row0) * m->h, m->h);
         p.norm_w = m->final_norm;
         p.eps = c.rms_norm_eps;
@@ -470,7 +492,7 @@ l0b_status record_decode_step(l0b_model* m, int rows) {
     L0B_TRY(d->launch(step_begin_kernel, dim3(grid_for(static_cast<long long>(rows) * m->h, d->sm_count)), dim3(256),
                       0, m->tok, m->embed, m->hidden, m->h, rows, m->vocab, m->keys, rows));
     for (int li = 0; li < static_cast<int>(m->layers.size()); ++li) {
-        if (m->fused) L0B_TRY(record_layer_fused(m, li, rows, true, 0));
+        if (m->fused && !m->probe) L0B_TRY(record_layer_fused(m, li, rows, true, 0));
         else {
             // The reference sequence reads the position as an argument (KvCacheStore pos0, Attention seqLen).
             L0B_TRY(record_layer_reference(m, li, rows, true, m->position));
@@ -485,7 +507,7 @@ l0b_status record_prefill_chunk(l0b_model* m, int count, int pos0, bool head) {
     L0B_TRY(d->launch(step_begin_kernel, dim3(grid_for(static_cast<long long>(count) * m->h, d->sm_count)),
                       dim3(256), 0, m->prompt_tok, m->embed, m->hidden, m->h, count, m->vocab, m->keys, 1));
     for (int li = 0; li < static_cast<int>(m->layers.size()); ++li) {
-        if (m->fused) L0B_TRY(record_layer_fused(m, li, count, false, pos0));
+        if (m->fused && !m->probe) L0B_TRY(record_layer_fused(m, li, count, false, pos0));
         else L0B_TRY(record_layer_reference(m, li, count, false, pos0));
     }
     if (head) L0B_TRY(record_head(m, count - 1, 1, 0));
@@ -497,7 +519,7 @@ template <typename Body>
 l0b_status run_recorded(l0b_model* m, Body body, bool wait = true) {
     l0b_device* d = m->dev;
     L0B_CHECK_CUDA(cudaSetDevice(d->index));
-    if (m->recording) {
+    if (m->recording && !m->probe) {
         L0B_REQUIRE(!d->recording, L0B_ERR_INVALID_OPERATION, "the device is already recording");
         d->recording = true;
         d->log_used = 0;
@@ -1146,6 +1168,48 @@ L0B_API l0b_status l0b_model_set_fused(l0b_model* m, int32_t enabled) {
     L0B_REQUIRE(!enabled || !m->cfg.qk_norm, L0B_ERR_UNSUPPORTED, "the fused layer has no QK-norm");
     m->fused = enabled != 0;
     return L0B_OK;
+}
+
+L0B_API l0b_status l0b_model_set_probe(l0b_model* m, l0b_probe_fn fn, void* user) {
+    L0B_REQUIRE(m, L0B_ERR_ARGUMENT, "model is null");
+    m->probe = fn;
+    m->probe_user = user;
+    return L0B_OK;
+}
+
+L0B_API l0b_status l0b_model_read_weight(l0b_model* m, int32_t layer, int32_t kind, void* out, int64_t bytes) {
+    GUARD_BEGIN
+    L0B_REQUIRE(m && out, L0B_ERR_ARGUMENT, "null argument");
+    L0B_REQUIRE(layer >= -1 && layer < static_cast<int>(m->layers.size()), L0B_ERR_OUT_OF_RANGE, "layer %d", layer);
+    L0B_REQUIRE(kind >= 0 && kind < 8, L0B_ERR_OUT_OF_RANGE, "kind %d", kind);
+    const ModelMatrix* mats[4];
+    if (layer < 0) {
+        L0B_REQUIRE(kind % 4 == 0, L0B_ERR_ARGUMENT, "the LM head is kind 0 (weights) or 4 (scales)");
+        mats[0] = &m->lm_head;
+    } else {
+        const ModelLayer& L = m->layers[layer];
+        mats[0] = &L.qkv;
+        mats[1] = &L.o;
+        mats[2] = &L.gate_up;
+        mats[3] = &L.down;
+    }
+    const ModelMatrix& mat = *mats[kind % 4];
+    const void* src;
+    size_t size;
+    if (kind < 4) {
+        src = mat.w;
+        size = static_cast<size_t>(mat.n) * mat.k * dtype_size(static_cast<l0b_dtype>(mat.dtype));
+    } else {
+        L0B_REQUIRE(mat.dtype == L0B_I8, L0B_ERR_ARGUMENT, "the matrix has no int8 scales");
+        src = mat.scales;
+        size = static_cast<size_t>(mat.n) * (mat.k / mat.group) * sizeof(__half);
+    }
+    L0B_REQUIRE(static_cast<size_t>(bytes) == size, L0B_ERR_ARGUMENT, "storage is %zu bytes, %lld requested", size,
+                (long long)bytes);
+    L0B_CHECK_CUDA(cudaStreamSynchronize(m->dev->stream));
+    L0B_CHECK_CUDA(cudaMemcpy(out, src, size, cudaMemcpyDeviceToHost));
+    return L0B_OK;
+    GUARD_END
 }
 
 L0B_API l0b_status l0b_model_read_kv(l0b_model* m, int32_t layer, int32_t row0, int32_t rows, float* keys,

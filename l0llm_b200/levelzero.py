@@ -89,6 +89,7 @@ class ModelConfig(C.Structure):
 
 
 _lib: C.CDLL | None = None
+PROBE_FN = C.CFUNCTYPE(None, C.c_void_p, C.c_int32, C.c_char_p, C.POINTER(C.c_float), C.c_int64)
 
 
 def load_library() -> C.CDLL:
@@ -183,6 +184,8 @@ def load_library() -> C.CDLL:
         "l0b_model_set_recording": (i32, [vp, i32]),
         "l0b_model_set_fused": (i32, [vp, i32]),
         "l0b_model_read_kv": (i32, [vp, i32, i32, i32, vp, vp]),
+        "l0b_model_set_probe": (i32, [vp, PROBE_FN, vp]),
+        "l0b_model_read_weight": (i32, [vp, i32, i32, vp, i64]),
     }
     for name, (res, args) in sigs.items():
         fn = getattr(L, name)
@@ -643,6 +646,27 @@ class LlmModel:
 
     def set_fused(self, on: bool):
         check(load_library().l0b_model_set_fused(self.handle, 1 if on else 0))
+
+    @property
+    def Probe(self):
+        return getattr(self, "_probe_py", None)
+
+    @Probe.setter
+    def Probe(self, fn):
+        """LlmDecoderLayer.Probe: fn(layer, stage, values) after each stage; None removes it."""
+        self._probe_py = fn
+        if fn is None:
+            self._probe_c = None
+            check(load_library().l0b_model_set_probe(self.handle, PROBE_FN(), None))
+            return
+        self._probe_c = PROBE_FN(lambda _u, layer, stage, vals, n: fn(layer, stage.decode(),
+                                                                          np.ctypeslib.as_array(vals, (n,)).copy()))
+        check(load_library().l0b_model_set_probe(self.handle, self._probe_c, None))
+
+    def read_weight(self, layer: int, kind: int, dtype, count: int) -> np.ndarray:
+        out = np.zeros(count, dtype)
+        check(load_library().l0b_model_read_weight(self.handle, layer, kind, _p(out), out.nbytes))
+        return out
 
     def read_kv(self, layer: int, row0: int, rows: int) -> tuple[np.ndarray, np.ndarray]:
         kvd = (self.cfg.num_key_value_heads // max(1, self.cfg.tp_size)) * self.cfg.head_dim

@@ -526,7 +526,18 @@ struct orc_model {
     orc_layer* L;
     /* scratch */
     float *hidden, *normed, *q, *k, *v, *attn, *proj, *gate, *up, *down;
+    orc_probe_fn probe;
+    void* probe_user;
 };
+
+void orc_model_set_probe(orc_model* m, orc_probe_fn fn, void* user) {
+    m->probe = fn;
+    m->probe_user = user;
+}
+
+static void emit(orc_model* m, int l, const char* stage, const float* v, int64_t n) {
+    if (m->probe) m->probe(m->probe_user, l, stage, v, n);
+}
 
 static int mat_alloc(orc_mat* m, int n, int k, int dtype, int group) {
     m->n = n;
@@ -740,6 +751,7 @@ int orc_model_step(orc_model* m, int token, int position, float* logits) {
     for (int l = 0; l < nl; ++l) {
         orc_layer* L = &m->L[l];
         orc_rmsnorm(m->hidden, NULL, L->in_norm, m->normed, c->eps, H, 1, 0);
+        emit(m, l, "input_norm", m->normed, H);
         mat_apply(&L->q, m->normed, m->q);
         mat_apply(&L->k, m->normed, m->k);
         mat_apply(&L->v, m->normed, m->v);
@@ -752,16 +764,23 @@ int orc_model_step(orc_model* m, int token, int position, float* logits) {
             orc_rmsnorm(m->q, NULL, L->qn, m->q, c->eps, hd, c->heads, 0);
             orc_rmsnorm(m->k, NULL, L->kn, m->k, c->eps, hd, c->kv_heads, 0);
         }
+        emit(m, l, "q", m->q, m->qd);
+        emit(m, l, "k", m->k, m->kvd);
+        emit(m, l, "v", m->v, m->kvd);
         orc_rope(m->q, m->k, &position, m->inv_freq, hd, c->heads, c->kv_heads, m->attn_scale, m->rot, 1);
         orc_kv_store(m->k, m->v, L->kc, L->vc, c->kv_dtype, position, m->kvd, 1);
         orc_attention(m->q, L->kc, L->vc, c->kv_dtype, m->attn, hd, c->heads, c->kv_heads, position, 1);
         mat_apply(&L->o, m->attn, m->proj);
+        emit(m, l, "attn_out", m->proj, H);
         orc_rmsnorm(m->hidden, m->proj, L->post_norm, m->normed, c->eps, H, 1, 1);
+        emit(m, l, "post_norm", m->normed, H);
         mat_apply(&L->gate, m->normed, m->gate);
         mat_apply(&L->up, m->normed, m->up);
         orc_swiglu(m->gate, m->up, I);
         mat_apply(&L->down, m->gate, m->down);
+        emit(m, l, "mlp_out", m->down, H);
         orc_add(m->hidden, m->down, H);
+        emit(m, l, "output", m->hidden, H);
     }
     orc_rmsnorm(m->hidden, NULL, m->final_norm, m->normed, c->eps, H, 1, 0);
     if (logits) mat_apply(&m->lm_head, m->normed, logits);

@@ -110,6 +110,9 @@ int orc_model_set_tensor(orc_model* m, const char* name, const float* data, int6
 int orc_model_step(orc_model* m, int token, int position, float* logits);
 /* Runs only `layers_to_run` layers (<= cfg.layers) for timing samples; 0 = all. */
 void orc_model_set_layer_limit(orc_model* m, int layers_to_run);
+/* Stage callback with the reference's probe stage names (L/LlmDecoderLayer.cs:113-119). */
+typedef void (*orc_probe_fn)(void* user, int layer, const char* stage, const float* values, int64_t count);
+void orc_model_set_probe(orc_model* m, orc_probe_fn fn, void* user);
 /* Reads the K/V cache rows of a layer as f32. */
 int orc_model_read_kv(orc_model* m, int layer, int row0, int rows, float* keys, float* values);
 /* Threads used by the oracle's parallel loops (OpenMP). */

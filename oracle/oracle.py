@@ -43,6 +43,7 @@ class OrcConfig(C.Structure):
 
 
 _lib = None
+PROBE_FN = C.CFUNCTYPE(None, C.c_void_p, C.c_int, C.c_char_p, C.POINTER(C.c_float), C.c_int64)
 
 
 def lib() -> C.CDLL:
@@ -97,6 +98,7 @@ def lib() -> C.CDLL:
     L.orc_model_set_layer_limit.argtypes = [vp, C.c_int]
     L.orc_model_read_kv.restype = C.c_int
     L.orc_model_read_kv.argtypes = [vp, C.c_int, C.c_int, C.c_int, _f32p, _f32p]
+    L.orc_model_set_probe.argtypes = [vp, PROBE_FN, vp]
     L.orc_num_threads.restype = C.c_int
     L.orc_set_num_threads.argtypes = [C.c_int]
     _lib = L
@@ -226,6 +228,16 @@ class OracleModel:
         if rc != 0:
             raise ValueError("oracle step failed")
         return logits
+
+    def set_probe(self, fn):
+        """fn(layer, stage, values) after each stage of each layer; None removes it."""
+        if fn is None:
+            self._probe = None
+            lib().orc_model_set_probe(self._h, PROBE_FN(), None)
+            return
+        self._probe = PROBE_FN(lambda _u, layer, stage, vals, n: fn(layer, stage.decode(),
+                                                                        np.ctypeslib.as_array(vals, (n,)).copy()))
+        lib().orc_model_set_probe(self._h, self._probe, None)
 
     def set_layer_limit(self, n: int):
         lib().orc_model_set_layer_limit(self._h, n)

@@ -274,3 +274,57 @@ def test_config2_qwen7b_int8_shape_two_layers(lz, orc, device, suite):
         if g != w:
             assert margins[i] < 1e-2 * max(1.0, float(np.abs(want).max())), f"step {i}"
             break
+
+
+# ----------------------------------------------------------------------------------------------
+# Per-stage parity (the Probe stages of LlmDecoderLayer, T/Qwen25LayerGoldenTests.cs method) and the
+# uploaded weight storage
+# ----------------------------------------------------------------------------------------------
+
+@pytest.mark.parametrize("name,precision,wdtype,kv", [("llama3", "float32", 0, "f32"), ("qwen2", "float16", 1, "f16"),
+                                                      ("qwen3", "float32", 0, "f32"), ("qwen2", "int8", 3, "f16")])
+def test_probe_stages_match_oracle(lz, orc, device, suite, name, precision, wdtype, kv):
+    _, prompt, _, _ = hf_golden(name)
+    kvo = {"f32": 0, "f16": 1, "bf16": 2}[kv]
+    om = oracle_model(orc, name, wdtype, 0, kvo)
+    got, want = [], []
+    with make_model(lz, device, suite, name, precision, kv) as model:
+        model.Probe = lambda layer, stage, v: got.append((layer, stage, v))
+        om.set_probe(lambda layer, stage, v: want.append((layer, stage, v)))
+        for t, tok in enumerate(prompt[:3]):
+            model.ComputeLogits(int(tok), t)
+            om.step(int(tok), t)
+    om.close()
+    assert [g[:2] for g in got] == [w[:2] for w in want]
+    for (layer, stage, a), (_, _, b) in zip(got, want):
+        err = max_diff(a, b)
+        assert err <= 1e-3 + 1e-3 * float(np.abs(b).max()), f"layer {layer} stage {stage}: max diff {err}"
+
+
+@pytest.mark.parametrize("precision", ["float32", "float16", "bfloat16", "int8"])
+def test_uploaded_weights_match_hf_tensors(lz, device, suite, precision):
+    import torch
+
+    name = "llama3"
+    cfg = hf_tiny.TINY[name]
+    w = hf_tiny.weights(cfg, hf_golden(name)[0])
+    with make_model(lz, device, suite, name, precision, "f32") as model:
+        p = "model.layers.1."
+        stacks = {0: ["self_attn.q_proj", "self_attn.k_proj", "self_attn.v_proj"], 1: ["self_attn.o_proj"],
+                  2: ["mlp.gate_proj", "mlp.up_proj"], 3: ["mlp.down_proj"]}
+        for kind, names in stacks.items():
+            full = np.concatenate([w[p + n + ".weight"] for n in names])
+            if precision == "int8":
+                q = model.read_weight(1, kind, np.int8, full.size).reshape(full.shape)
+                s = model.read_weight(1, kind + 4, np.float16, full.shape[0] * (full.shape[1] // 32))
+                qw, sw = lz.q8_quantize_out_in(full, 32)
+                np.testing.assert_array_equal(q, qw)
+                np.testing.assert_array_equal(s, sw.ravel())
+            elif precision == "float32":
+                np.testing.assert_array_equal(model.read_weight(1, kind, np.float32, full.size), full.ravel())
+            elif precision == "float16":
+                np.testing.assert_array_equal(model.read_weight(1, kind, np.float16, full.size),
+                                              full.ravel().astype(np.float16))
+            else:
+                want = torch.from_numpy(full.ravel()).to(torch.bfloat16).view(torch.int16).numpy().view(np.uint16)
+                np.testing.assert_array_equal(model.read_weight(1, kind, np.uint16, full.size), want)
