@@ -301,7 +301,7 @@ l0b_status emit(l0b_model* m, int li, const char* stage, const float* dptr, long
     if (!m->probe) return L0B_OK;
     m->probe_host.resize(static_cast<size_t>(count));
     L0B_CHECK_CUDA(cudaStreamSynchronize(m->dev->stream));
-    L0B_CHECK_CUDA(cudaMemcpy(m->probe_host.data(), dptr, count * sizeof(float), cudaMemcpyDeviceToHost));
+    L0B_CHECK_CUDA(copy_sync(m->dev->stream, m->probe_host.data(), dptr, count * sizeof(float), cudaMemcpyDeviceToHost));
     m->probe(m->probe_user, li, stage, m->probe_host.data(), count);
     return L0B_OK;
 }
@@ -816,7 +816,7 @@ L0B_API l0b_status l0b_model_create(l0b_device* dev, l0b_suite* suite, const l0b
     L0B_TRY(rope_frequencies(c, &table, &m->attn_scale));
     m->rot = static_cast<int>(table.size()) * 2;
     L0B_TRY(m->alloc(&m->inv_freq, table.size()));
-    L0B_CHECK_CUDA(cudaMemcpy(m->inv_freq, table.data(), table.size() * sizeof(float), cudaMemcpyHostToDevice));
+    L0B_CHECK_CUDA(copy_sync(m->dev->stream, m->inv_freq, table.data(), table.size() * sizeof(float), cudaMemcpyHostToDevice));
 
     // Weights.
     L0B_TRY(m->alloc(&m->embed, static_cast<size_t>(c.vocab_size) * m->h));
@@ -847,13 +847,13 @@ L0B_API l0b_status l0b_model_create(l0b_device* dev, l0b_suite* suite, const l0b
     {
         const float one = 1.f;
         std::vector<float> ones(std::max(m->h, m->hd), one);
-        L0B_CHECK_CUDA(cudaMemcpy(m->final_norm, ones.data(), m->h * sizeof(float), cudaMemcpyHostToDevice));
+        L0B_CHECK_CUDA(copy_sync(m->dev->stream, m->final_norm, ones.data(), m->h * sizeof(float), cudaMemcpyHostToDevice));
         for (auto& L : m->layers) {
-            L0B_CHECK_CUDA(cudaMemcpy(L.in_norm, ones.data(), m->h * sizeof(float), cudaMemcpyHostToDevice));
-            L0B_CHECK_CUDA(cudaMemcpy(L.post_norm, ones.data(), m->h * sizeof(float), cudaMemcpyHostToDevice));
+            L0B_CHECK_CUDA(copy_sync(m->dev->stream, L.in_norm, ones.data(), m->h * sizeof(float), cudaMemcpyHostToDevice));
+            L0B_CHECK_CUDA(copy_sync(m->dev->stream, L.post_norm, ones.data(), m->h * sizeof(float), cudaMemcpyHostToDevice));
             if (L.q_norm) {
-                L0B_CHECK_CUDA(cudaMemcpy(L.q_norm, ones.data(), m->hd * sizeof(float), cudaMemcpyHostToDevice));
-                L0B_CHECK_CUDA(cudaMemcpy(L.k_norm, ones.data(), m->hd * sizeof(float), cudaMemcpyHostToDevice));
+                L0B_CHECK_CUDA(copy_sync(m->dev->stream, L.q_norm, ones.data(), m->hd * sizeof(float), cudaMemcpyHostToDevice));
+                L0B_CHECK_CUDA(copy_sync(m->dev->stream, L.k_norm, ones.data(), m->hd * sizeof(float), cudaMemcpyHostToDevice));
             }
         }
     }
@@ -925,7 +925,7 @@ L0B_API l0b_status l0b_model_set_tensor(l0b_model* m, const char* name, const fl
         float* p;
         ~Free() { cudaFree(p); }
     } guard{staging};
-    L0B_CHECK_CUDA(cudaMemcpy(staging, data, static_cast<size_t>(full) * sizeof(float), cudaMemcpyHostToDevice));
+    L0B_CHECK_CUDA(copy_sync(m->dev->stream, staging, data, static_cast<size_t>(full) * sizeof(float), cudaMemcpyHostToDevice));
     cudaStream_t st = m->dev->stream;
     const int sm = m->dev->sm_count;
     if (t.embed) {
@@ -1086,7 +1086,7 @@ L0B_API l0b_status l0b_model_generate_greedy(l0b_model* m, const int32_t* ids, i
     L0B_REQUIRE(out, L0B_ERR_ARGUMENT, "out is null");
     L0B_TRY(ingest_prompt(m, ids, count));
     int next = 0;
-    L0B_CHECK_CUDA(cudaMemcpy(&next, m->sampled, sizeof(int), cudaMemcpyDeviceToHost));
+    L0B_CHECK_CUDA(copy_sync(m->dev->stream, &next, m->sampled, sizeof(int), cudaMemcpyDeviceToHost));
     int position = count;
     int n = 0;
     while (true) {
@@ -1095,7 +1095,7 @@ L0B_API l0b_status l0b_model_generate_greedy(l0b_model* m, const int32_t* ids, i
         for (int i = 0; i < n_stop; ++i) stop = stop || stop_ids[i] == next;
         if (n >= max_new || stop) break;
         L0B_TRY(step(m, next, position));
-        L0B_CHECK_CUDA(cudaMemcpy(&next, m->sampled, sizeof(int), cudaMemcpyDeviceToHost));
+        L0B_CHECK_CUDA(copy_sync(m->dev->stream, &next, m->sampled, sizeof(int), cudaMemcpyDeviceToHost));
         ++position;
     }
     *out_count = n;
@@ -1207,7 +1207,7 @@ L0B_API l0b_status l0b_model_read_weight(l0b_model* m, int32_t layer, int32_t ki
     L0B_REQUIRE(static_cast<size_t>(bytes) == size, L0B_ERR_ARGUMENT, "storage is %zu bytes, %lld requested", size,
                 (long long)bytes);
     L0B_CHECK_CUDA(cudaStreamSynchronize(m->dev->stream));
-    L0B_CHECK_CUDA(cudaMemcpy(out, src, size, cudaMemcpyDeviceToHost));
+    L0B_CHECK_CUDA(copy_sync(m->dev->stream, out, src, size, cudaMemcpyDeviceToHost));
     return L0B_OK;
     GUARD_END
 }
@@ -1226,7 +1226,7 @@ L0B_API l0b_status l0b_model_read_kv(l0b_model* m, int32_t layer, int32_t row0, 
     L0B_CHECK_CUDA(cudaStreamSynchronize(m->dev->stream));
     for (int which = 0; which < 2; ++which) {
         const char* src = static_cast<const char*>(which ? L.vc : L.kc) + static_cast<size_t>(row0) * m->kvdim * es;
-        L0B_CHECK_CUDA(cudaMemcpy(tmp.data(), src, n * es, cudaMemcpyDeviceToHost));
+        L0B_CHECK_CUDA(copy_sync(m->dev->stream, tmp.data(), src, n * es, cudaMemcpyDeviceToHost));
         float* dst = which ? values : keys;
         for (size_t i = 0; i < n; ++i) {
             if (m->cache_dtype == L0B_F32) dst[i] = reinterpret_cast<const float*>(tmp.data())[i];

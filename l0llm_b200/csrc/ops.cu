@@ -24,7 +24,7 @@ l0b_status suite_rope_table(l0b_suite* s, int rot, double theta, const float** o
         for (int i = 0; i < rot / 2; ++i) t[i] = static_cast<float>(1.0 / std::pow(theta, 2.0 * i / rot));
         float* dptr = nullptr;
         L0B_CHECK_CUDA(cudaMalloc(&dptr, t.size() * sizeof(float)));
-        L0B_CHECK_CUDA(cudaMemcpy(dptr, t.data(), t.size() * sizeof(float), cudaMemcpyHostToDevice));
+        L0B_CHECK_CUDA(copy_sync(s->dev->stream, dptr, t.data(), t.size() * sizeof(float), cudaMemcpyHostToDevice));
         it = s->rope_tables.emplace(key, dptr).first;
     }
     *out = it->second;
@@ -91,7 +91,8 @@ L0B_API l0b_status l0b_suite_create(l0b_device* dev, l0b_suite** out) {
     s->dev = dev;
     L0B_CHECK_CUDA(cudaSetDevice(dev->index));
     L0B_CHECK_CUDA(cudaMalloc(&s->error_flag, sizeof(int)));
-    L0B_CHECK_CUDA(cudaMemset(s->error_flag, 0, sizeof(int)));
+    L0B_CHECK_CUDA(cudaMemsetAsync(s->error_flag, 0, sizeof(int), dev->stream));
+    L0B_CHECK_CUDA(cudaStreamSynchronize(dev->stream));
     *out = s.release();
     return L0B_OK;
     GUARD_END

@@ -58,6 +58,15 @@ void clear_error();
 size_t dtype_size(l0b_dtype t);
 const char* dtype_name(l0b_dtype t);
 
+// Copy ordered on `s` (the device's non-blocking stream) and waited for. A plain cudaMemcpy runs on the
+// legacy stream, which does not order against non-blocking streams, and from pageable memory it may
+// return before its DMA lands, so a kernel queued on `s` right after it could read stale bytes.
+inline cudaError_t copy_sync(cudaStream_t s, void* dst, const void* src, size_t bytes, cudaMemcpyKind kind) {
+    cudaError_t e = cudaMemcpyAsync(dst, src, bytes, kind, s);
+    if (e != cudaSuccess) return e;
+    return cudaStreamSynchronize(s);
+}
+
 // ---------------------------------------------------------------------------------------------
 // Launch records
 // ---------------------------------------------------------------------------------------------

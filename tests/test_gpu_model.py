@@ -308,7 +308,7 @@ def test_uploaded_weights_match_hf_tensors(lz, device, suite, precision):
     name = "llama3"
     cfg = hf_tiny.TINY[name]
     w = hf_tiny.weights(cfg, hf_golden(name)[0])
-    with make_model(lz, device, suite, name, precision, "f32") as model:
+    with make_model(lz, device, suite, name, precision, "f32", q8_group=32 if precision == "int8" else 0) as model:
         p = "model.layers.1."
         stacks = {0: ["self_attn.q_proj", "self_attn.k_proj", "self_attn.v_proj"], 1: ["self_attn.o_proj"],
                   2: ["mlp.gate_proj", "mlp.up_proj"], 3: ["mlp.down_proj"]}
