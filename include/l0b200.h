@@ -255,6 +255,21 @@ L0B_API l0b_status l0b_attention_execute_prefill(l0b_suite* s, l0b_device* d, l0
                                                  int32_t head_dim, int32_t n_heads, int32_t n_kv_heads,
                                                  int32_t pos0, int32_t tokens, int32_t max_seq);
 
+/* Decode attention (the l0b_attention_execute computation, one query token over cache slots
+ * [0, seq_len)) that allocates nothing, for callers that cannot allocate device memory during a call:
+ * a server that plans all of HBM at start-up, code running while a pool or another runtime owns the
+ * allocator, or a host that must never block in cudaMalloc mid-step. No counterpart in the reference.
+ * Raw device pointers; cache_dtype is L0B_F32/F16/BF16; enqueued on `stream` (a cudaStream_t).
+ * The split partials live in a fixed 4 MiB array and 4096 counters compiled into the library (every
+ * GPU that loads it holds them until exit); n_heads * (head_dim + 2) must fit 1,048,576 floats and
+ * n_kv_heads * ceil(group / 8) must fit 4096 counters, else L0B_ERR_OUT_OF_RANGE. All calls share that
+ * scratch: calls that overlap on the GPU (other streams, other threads) race and must be serialised.
+ * The first call on a device looks up the arrays' device addresses; make it before any stream capture. */
+L0B_API l0b_status l0b_attention_decode_noalloc(void* stream, const float* q, const void* kc, const void* vc,
+                                                int32_t cache_dtype, float* out, int32_t head_dim,
+                                                int32_t n_heads, int32_t n_kv_heads, int32_t seq_len,
+                                                int32_t max_seq);
+
 /* SigmoidGate.Execute(dev, x, gate, n) -- L/LlmDecoderLayer.cs:330,374. x *= sigmoid(gate). */
 L0B_API l0b_status l0b_sigmoid_gate_execute(l0b_suite* s, l0b_device* d, l0b_buffer* x, l0b_buffer* gate,
                                             int32_t n);

@@ -11,6 +11,8 @@
 // atomic counter that it resets afterwards -- merges them. With rope/store_new set the kernel also
 // applies RoPE to the query and to the new key, and the CTA owning the query position writes the
 // new key/value row into the cache, replacing the separate RoPE and KvCacheStore launches.
+#include <cmath>
+
 #include "common.cuh"
 #include "ops.cuh"
 
@@ -238,6 +240,104 @@ l0b_status attention_launch_stream(cudaStream_t stream, const AttnParams& p, int
 size_t attention_part_floats(int batch, int nh, int max_splits, int hd) {
     return static_cast<size_t>(batch) * nh * max_splits * (hd + 2);
 }
+
+// ---------------------------------------------------------------------------------------------
+// Decode attention for callers that cannot allocate device memory.
+//
+// The split-KV kernel needs scratch for its per-split partials and its merge counters. The regular
+// entry point takes it from the device's scratch, which grows with cudaMalloc. Some callers cannot let
+// a call allocate: a serving process that plans every byte of HBM at start-up, code that runs while a
+// memory pool or another runtime owns the allocator, or a host (such as a managed-language façade)
+// that must not have a call block in the allocator mid-step. This variant keeps its scratch in fixed
+// arrays compiled into the library instead: 4 MiB of partials and 4096 counters per GPU that loads the
+// library, held until the process exits.
+// ---------------------------------------------------------------------------------------------
+
+constexpr int kNoAllocPartFloats = 1 << 20;  // 4 MiB
+constexpr int kNoAllocCounters = 4096;
+
+static __device__ __align__(256) float g_noalloc_part[kNoAllocPartFloats];
+static __device__ __align__(256) unsigned g_noalloc_counters[kNoAllocCounters];
+
+}  // namespace l0b
+
+namespace {
+
+// Device addresses of the two arrays, looked up once per device (the names are host stand-ins).
+struct NoAllocAddrs {
+    bool ready = false;
+    float* part = nullptr;
+    unsigned* counters = nullptr;
+};
+NoAllocAddrs g_noalloc_addrs[64];
+
+}  // namespace
+
+extern "C" L0B_API l0b_status l0b_attention_decode_noalloc(void* stream, const float* q, const void* kc, const void* vc,
+                                                         int32_t cache_dtype, float* out, int32_t head_dim,
+                                                         int32_t n_heads, int32_t n_kv_heads, int32_t seq_len,
+                                                         int32_t max_seq) {
+    using namespace l0b;
+    L0B_REQUIRE(q && kc && vc && out, L0B_ERR_ARGUMENT, "null pointer");
+    L0B_REQUIRE(head_dim == 64 || head_dim == 128, L0B_ERR_UNSUPPORTED, "head_dim %d (64 or 128)", head_dim);
+    L0B_REQUIRE(n_kv_heads > 0 && n_heads > 0 && n_heads % n_kv_heads == 0, L0B_ERR_ARGUMENT,
+                "heads %d / kv heads %d", n_heads, n_kv_heads);
+    L0B_REQUIRE(seq_len > 0 && seq_len <= max_seq, L0B_ERR_OUT_OF_RANGE, "seqLen %d outside (0, maxSeq %d]", seq_len,
+                max_seq);
+    L0B_REQUIRE(cache_dtype == L0B_F32 || cache_dtype == L0B_F16 || cache_dtype == L0B_BF16, L0B_ERR_ARGUMENT,
+                "cache dtype %d", cache_dtype);
+    const int gparts = (n_heads / n_kv_heads + kMaxG - 1) / kMaxG;
+    const long long per_split = static_cast<long long>(n_heads) * (head_dim + 2);
+    L0B_REQUIRE(per_split <= kNoAllocPartFloats && static_cast<long long>(n_kv_heads) * gparts <= kNoAllocCounters,
+                L0B_ERR_OUT_OF_RANGE,
+                "the fixed scratch holds %d partial floats and %d counters; %d heads of dim %d need %lld and %lld",
+                kNoAllocPartFloats, kNoAllocCounters, n_heads, head_dim, per_split,
+                static_cast<long long>(n_kv_heads) * gparts);
+    int dev = 0;
+    L0B_CHECK_CUDA(cudaGetDevice(&dev));
+    L0B_REQUIRE(dev >= 0 && dev < 64, L0B_ERR_OUT_OF_RANGE, "device ordinal %d", dev);
+    NoAllocAddrs& a = g_noalloc_addrs[dev];
+    if (!a.ready) {
+        // First call on this device: resolve the arrays' device addresses (no allocation; the module is
+        // already loaded). Make this first call before any stream capture on the device.
+        L0B_CHECK_CUDA(cudaGetSymbolAddress(reinterpret_cast<void**>(&a.part), g_noalloc_part));
+        L0B_CHECK_CUDA(cudaGetSymbolAddress(reinterpret_cast<void**>(&a.counters), g_noalloc_counters));
+        a.ready = true;
+    }
+    // As many splits as fit the fixed partials (and no more than the positions need).
+    int chunk = 64;
+    while (true) {
+        const long long splits = (seq_len + chunk - 1) / chunk;
+        if (splits * per_split <= kNoAllocPartFloats) break;
+        chunk *= 2;
+    }
+    const int splits = (seq_len + chunk - 1) / chunk;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    // The counters must start at zero; a call that stopped early could have left them set.
+    L0B_CHECK_CUDA(cudaMemsetAsync(a.counters, 0, sizeof(unsigned) * n_kv_heads * gparts, s));
+    AttnParams p = {};
+    p.q = q;
+    p.q_bstride = static_cast<long long>(n_heads) * head_dim;
+    p.kc = const_cast<void*>(kc);
+    p.vc = const_cast<void*>(vc);
+    p.cache_dtype = cache_dtype;
+    p.kv_dim = n_kv_heads * head_dim;
+    p.pos_base = seq_len - 1;
+    p.out = out;
+    p.out_bstride = static_cast<long long>(n_heads) * head_dim;
+    p.part = a.part;
+    p.part_ml = a.part + static_cast<long long>(n_heads) * splits * head_dim;
+    p.counters = a.counters;
+    p.nh = n_heads;
+    p.nkv = n_kv_heads;
+    p.hd = head_dim;
+    p.chunk = chunk;
+    p.max_splits = splits;
+    p.scale = static_cast<float>(1.0 / std::sqrt(static_cast<double>(head_dim)));
+    return attention_launch_stream(s, p, 1);
+}
+
+namespace l0b {
 
 void attention_pick_split(int max_seq, int work_items, int sm_count, int* chunk, int* max_splits) {
     (void)work_items;
