@@ -227,10 +227,28 @@ def main() -> int:
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--kernel-only", action="store_true",
+                    help="only the dominant-kernel roofline loop (small device footprint, for ncu captures)")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)
     args.warmup = max(3, args.warmup)
+    if args.kernel_only:
+        import ctypes as C
+
+        import torch
+
+        from l0llm_b200 import levelzero as lz
+
+        dev = lz.ComputeDevice(0)
+        suite = lz.LlmKernelSuite.Create(dev)
+        sp = C.c_void_p()
+        lz.check(lz.load_library().l0b_device_stream(dev.handle, C.byref(sp)))
+        peak, kind = peaks()
+        print(json.dumps(dominant_kernel_roofline(lz, dev, suite, sp.value, torch, peak, kind)))
+        suite.Dispose()
+        dev.Dispose()
+        return 0
 
     world, rank, local = dist_env()
     import torch

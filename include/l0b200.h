@@ -107,6 +107,9 @@ L0B_API l0b_status l0b_device_stream(l0b_device* dev, void** stream);
 /* Number of command lists built (captured + instantiated) and reused since creation. */
 L0B_API l0b_status l0b_device_graph_stats(l0b_device* dev, int64_t* built, int64_t* reused,
                                           int64_t* updated);
+/* Reads and clears the device's error flag: nonzero when a kernel's bounded wait (a pipeline barrier
+ * that never completed) gave up instead of hanging; the results of that launch are invalid. */
+L0B_API l0b_status l0b_device_error_status(l0b_device* dev, int32_t* code);
 /* Enables (1) or disables (0) programmatic dependent launch between consecutive kernels. */
 L0B_API l0b_status l0b_device_set_pdl(l0b_device* dev, int32_t enabled);
 

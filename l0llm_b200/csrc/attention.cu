@@ -23,19 +23,33 @@ namespace {
 constexpr int kT = 32;     // positions per tile
 constexpr int kMaxG = 8;   // query heads per CTA
 
-__device__ __forceinline__ float rope_elem(const float* head, int d, int rot, int pos, const float* inv_freq,
-                                           float attn_scale) {
+// Element d of a rotated head (HF rotate-half pairs) from the per-position cos/sin table.
+__device__ __forceinline__ float rope_elem(const float* head, int d, int rot, const float* cs, const float* sn) {
     const float v = head[d];
     if (d >= rot) return v;
     const int half = rot >> 1;
     const int i = d < half ? d : d - half;
-    const float ang = __fmul_rn(static_cast<float>(pos), inv_freq[i]);
-    float s, c;
-    sincosf(ang, &s, &c);
-    c = __fmul_rn(c, attn_scale);
-    s = __fmul_rn(s, attn_scale);
+    const float c = cs[i], s = sn[i];
     if (d < half) return __fsub_rn(__fmul_rn(v, c), __fmul_rn(head[d + half], s));
     return __fadd_rn(__fmul_rn(v, c), __fmul_rn(head[d - half], s));
+}
+
+// Eight consecutive cache elements as fp32 (one 16-byte load for f16/bf16, two for f32).
+__device__ __forceinline__ void load8(const void* base, int dtype, long long off, float (&o)[8]) {
+    if (dtype == L0B_F32) {
+        const float4 a = *reinterpret_cast<const float4*>(static_cast<const float*>(base) + off);
+        const float4 b = *reinterpret_cast<const float4*>(static_cast<const float*>(base) + off + 4);
+        o[0] = a.x; o[1] = a.y; o[2] = a.z; o[3] = a.w; o[4] = b.x; o[5] = b.y; o[6] = b.z; o[7] = b.w;
+        return;
+    }
+    const uint4 u = *reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(base) + off);
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const float2 f = dtype == L0B_F16 ? half2_bits_to_float2(w[i]) : bf162_bits_to_float2(w[i]);
+        o[2 * i] = f.x;
+        o[2 * i + 1] = f.y;
+    }
 }
 
 template <int HD>
@@ -44,10 +58,11 @@ __global__ void __launch_bounds__(128) attn_kernel(const AttnParams p) {
     constexpr int JPT = kMaxG / HPT;       // heads per thread in the PV phase
     __shared__ float qs[kMaxG][HD];
     __shared__ float ks[kT][HD + 1];
-    __shared__ float vs[kT][HD];
+    __shared__ __align__(16) float vs[kT][HD];
     __shared__ float ps[kMaxG][kT];
     __shared__ float m_s[kMaxG], l_s[kMaxG], corr_s[kMaxG];
     __shared__ float knew[HD], vnew[HD];
+    __shared__ float cs_s[HD / 2], sn_s[HD / 2];
     __shared__ int last_s;
 
     const int G = p.nh / p.nkv;
@@ -65,11 +80,22 @@ __global__ void __launch_bounds__(128) attn_kernel(const AttnParams p) {
     if (split >= nact) return;
     pdl_launch_dependents();
 
+    // cos/sin of this query position, once per CTA: angle = f32(pos) * inv_freq (as RoPE.Execute).
+    if (p.rope) {
+        for (int i = tid; i < p.rot / 2; i += 128) {
+            const float ang = __fmul_rn(static_cast<float>(qpos), p.inv_freq[i]);
+            float s, c;
+            sincosf(ang, &s, &c);
+            cs_s[i] = __fmul_rn(c, p.attn_scale);
+            sn_s[i] = __fmul_rn(s, p.attn_scale);
+        }
+        __syncthreads();
+    }
     const float* qb = p.q + b * p.q_bstride + static_cast<long long>(h0) * HD;
     for (int idx = tid; idx < kMaxG * HD; idx += 128) {
         const int j = idx / HD, d = idx - (idx / HD) * HD;
         float v = 0.f;
-        if (j < ng) v = p.rope ? rope_elem(qb + j * HD, d, p.rot, qpos, p.inv_freq, p.attn_scale) : qb[j * HD + d];
+        if (j < ng) v = p.rope ? rope_elem(qb + j * HD, d, p.rot, cs_s, sn_s) : qb[j * HD + d];
         qs[j][d] = v;
     }
     if (tid < kMaxG) {
@@ -81,7 +107,7 @@ __global__ void __launch_bounds__(128) attn_kernel(const AttnParams p) {
         const float* kb = p.k_new + b * p.new_bstride + static_cast<long long>(kvh) * HD;
         const float* vb = p.v_new + b * p.new_bstride + static_cast<long long>(kvh) * HD;
         for (int d = tid; d < HD; d += 128) {
-            const float kv = p.rope ? rope_elem(kb, d, p.rot, qpos, p.inv_freq, p.attn_scale) : kb[d];
+            const float kv = p.rope ? rope_elem(kb, d, p.rot, cs_s, sn_s) : kb[d];
             knew[d] = kv;
             vnew[d] = vb[d];
             if (gp == 0) {
@@ -103,22 +129,28 @@ __global__ void __launch_bounds__(128) attn_kernel(const AttnParams p) {
     const int p_end = min(seq, p_begin + p.chunk);
     const long long cache_base = b * p.cache_bstride + static_cast<long long>(kvh) * HD;
     for (int t0 = p_begin; t0 < p_end; t0 += kT) {
-        for (int idx = tid; idx < kT * HD; idx += 128) {
-            const int t = idx / HD, d = idx - (idx / HD) * HD;
+        // 16-byte loads: HD/8 threads per row, each owning 8 consecutive dims.
+        constexpr int TPR = HD / 8;
+        for (int idx = tid; idx < kT * TPR; idx += 128) {
+            const int t = idx / TPR, d0 = (idx - t * TPR) * 8;
             const int pos = t0 + t;
-            float kv = 0.f, vv = 0.f;
-            if (pos < p_end) {
-                if (owns_new && pos == qpos) {
-                    kv = knew[d];
-                    vv = vnew[d];
-                } else {
-                    const long long off = cache_base + static_cast<long long>(pos) * p.kv_dim + d;
-                    kv = load_as_float(p.kc, p.cache_dtype, off);
-                    vv = load_as_float(p.vc, p.cache_dtype, off);
+            float kv[8], vv[8];
+            if (pos < p_end && !(owns_new && pos == qpos)) {
+                const long long off = cache_base + static_cast<long long>(pos) * p.kv_dim + d0;
+                load8(p.kc, p.cache_dtype, off, kv);
+                load8(p.vc, p.cache_dtype, off, vv);
+            } else {
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                    const bool mine = pos < p_end;
+                    kv[e] = mine ? knew[d0 + e] : 0.f;
+                    vv[e] = mine ? vnew[d0 + e] : 0.f;
                 }
             }
-            ks[t][d] = kv;
-            vs[t][d] = vv;
+#pragma unroll
+            for (int e = 0; e < 8; ++e) ks[t][d0 + e] = kv[e];
+            *reinterpret_cast<float4*>(&vs[t][d0]) = make_float4(vv[0], vv[1], vv[2], vv[3]);
+            *reinterpret_cast<float4*>(&vs[t][d0 + 4]) = make_float4(vv[4], vv[5], vv[6], vv[7]);
         }
         __syncthreads();
         for (int j = warp; j < ng; j += 4) {
@@ -342,7 +374,9 @@ namespace l0b {
 void attention_pick_split(int max_seq, int work_items, int sm_count, int* chunk, int* max_splits) {
     (void)work_items;
     (void)sm_count;
-    int c = max_seq <= 2048 ? 64 : 128;
+    // One 32-position tile per CTA up to 4096 positions (most CTAs, shortest critical path), longer
+    // splits beyond so the merge stays short.
+    int c = max_seq <= 4096 ? 32 : max_seq <= 16384 ? 64 : 128;
     *chunk = c;
     *max_splits = (max_seq + c - 1) / c;
 }

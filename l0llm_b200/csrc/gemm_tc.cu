@@ -1,0 +1,360 @@
+// Tensor-core GEMM for prefill and batched decode on sm_100a: tcgen05.mma with the accumulator in
+// tensor memory, both operands staged by TMA into 128-byte-swizzled shared memory.
+//
+// "Swap-AB" orientation: the 128-row MMA M dimension runs over weight rows and the MMA N dimension
+// (BN = 64, 128 or 256) over tokens, so one CTA computes D[128 weight rows, BN tokens] = W_tile X_tile^T
+// into BN fp32 TMEM columns. Warp 0 / lane 0 issues the TMA loads (W tile [128 x 64] and X tile
+// [BN x 64] per stage, 4 stages), warp 1 / lane 0 issues four K=16 MMAs per stage and releases the
+// stage with tcgen05.commit, and all four warps run the epilogue from TMEM (warp w owns TMEM lanes
+// 32w..32w+31 = weight rows), storing token-major fp32 rows with coalesced 128-byte writes. The SwiGLU
+// variant loads 64 gate rows and the 64 matching up rows into one tile and pairs them in the epilogue.
+// Every mbarrier wait is bounded (~2 s); a timeout sets the device error flag and the CTA exits after
+// releasing its tensor memory. No TMA multicast is used.
+#include <cuda.h>
+
+#include <cstring>
+
+#include "common.cuh"
+#include "gemm_tc.cuh"
+#include "gemv.cuh"
+
+namespace l0b {
+
+namespace {
+
+constexpr int kBM = 128;
+constexpr int kBK = 64;
+constexpr int kStages = 4;
+constexpr int kThreads = 128;
+constexpr long long kWaitCycles = 4000000000LL;
+
+struct TcParams {
+    CUtensorMap wmap;  // W [N, K] 16-bit, box {64, 128} (SwiGLU: {64, 64})
+    CUtensorMap xmap;  // X [M, K] 16-bit, box {64, BN}
+    int M, N, K, epi, ld, half_n;
+    float* out;
+    const float* bias;
+    int* error;
+};
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* b, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(b)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* b, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(b)), "r"(bytes) : "memory");
+}
+
+// Bounded wait for the phase with the given parity to complete; false after ~2 s.
+__device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity) {
+    const long long t0 = clock64();
+    while (true) {
+        uint32_t done;
+        asm volatile(
+            "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+            "selp.u32 %0, 1, 0, p;\n\t}"
+            : "=r"(done)
+            : "r"(smem_u32(b)), "r"(parity)
+            : "memory");
+        if (done) return true;
+        if (clock64() - t0 > kWaitCycles) return false;
+    }
+}
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::
+            "r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y)
+        : "memory");
+}
+
+// UMMA shared-memory descriptor of a K-major tile with 128-byte swizzle: rows of 128 bytes, 8-row
+// atoms 1024 bytes apart (stride byte offset), version 1 (sm_100), layout SWIZZLE_128B (2).
+__device__ __forceinline__ uint64_t smem_desc(const void* p) {
+    const uint32_t a = smem_u32(p);
+    return static_cast<uint64_t>((a >> 4) & 0x3FFF) | (1ull << 16) | (64ull << 32) | (1ull << 46) | (2ull << 61);
+}
+
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tc_mma(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc, uint32_t accum) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "l"(da), "l"(db), "r"(idesc), "r"(accum)
+        : "memory");
+}
+
+__device__ __forceinline__ void tc_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+    uint32_t r[16];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+          "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+template <int BN, int FMT>
+__global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const __grid_constant__ TcParams p) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    constexpr int A_BYTES = kBM * kBK * 2;
+    constexpr int B_BYTES = BN * kBK * 2;
+    uint8_t* sA = smem;
+    uint8_t* sB = smem + kStages * A_BYTES;
+    uint64_t* full = reinterpret_cast<uint64_t*>(sB + kStages * B_BYTES);
+    uint64_t* empty = full + kStages;
+    uint64_t* accum = empty + kStages;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int t0 = blockIdx.x * BN;
+    const int wt = blockIdx.y;
+    const bool swiglu = p.epi == EPI_SWIGLU;
+    const int nk = (p.K + kBK - 1) / kBK;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        mbar_init(accum, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(BN)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+        tc_fence_before();
+    }
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    pdl_wait();
+    pdl_launch_dependents();
+
+    bool ok = true;
+    if (warp == 0 && lane == 0) {
+        // TMA producer.
+        for (int kb = 0; kb < nk; ++kb) {
+            const int s = kb % kStages;
+            const uint32_t ph = (kb / kStages) & 1;
+            if (kb >= kStages && !mbar_wait(&empty[s], ph ^ 1)) {
+                ok = false;
+                break;
+            }
+            mbar_expect_tx(&full[s], A_BYTES + B_BYTES);
+            const int k0 = kb * kBK;
+            if (swiglu) {
+                tma_load_2d(sA + s * A_BYTES, &p.wmap, &full[s], k0, wt * 64);
+                tma_load_2d(sA + s * A_BYTES + A_BYTES / 2, &p.wmap, &full[s], k0, p.half_n + wt * 64);
+            } else {
+                tma_load_2d(sA + s * A_BYTES, &p.wmap, &full[s], k0, wt * kBM);
+            }
+            tma_load_2d(sB + s * B_BYTES, &p.xmap, &full[s], k0, t0);
+        }
+    } else if (warp == 1 && lane == 0) {
+        // MMA issuer: D[128, BN] (+)= A[128, 16] B[BN, 16]^T, four per stage.
+        constexpr uint32_t idesc = (1u << 4) | (static_cast<uint32_t>(FMT) << 7) | (static_cast<uint32_t>(FMT) << 10) |
+                                   (static_cast<uint32_t>(BN >> 3) << 17) | (static_cast<uint32_t>(kBM >> 4) << 24);
+        for (int kb = 0; kb < nk; ++kb) {
+            const int s = kb % kStages;
+            const uint32_t ph = (kb / kStages) & 1;
+            if (!mbar_wait(&full[s], ph)) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            const uint64_t da = smem_desc(sA + s * A_BYTES), db = smem_desc(sB + s * B_BYTES);
+#pragma unroll
+            for (int k = 0; k < kBK / 16; ++k) tc_mma(tmem, da + 2 * k, db + 2 * k, idesc, (kb | k) != 0);
+            tc_commit(&empty[s]);
+        }
+        tc_commit(accum);
+    }
+    __syncwarp();
+
+    // Epilogue: all warps.
+    const bool acc_ok = mbar_wait(accum, 0);
+    __syncwarp();
+    tc_fence_after();
+    float* xchg = reinterpret_cast<float*>(sA);  // SwiGLU: up rows handed from warps 2-3 to warps 0-1
+    for (int c0 = 0; c0 < BN; c0 += 16) {
+        float v[16];
+        tmem_ld16(tmem + (static_cast<uint32_t>(warp * 32) << 16) + c0, v);
+        if (!swiglu) {
+            const int n = wt * kBM + warp * 32 + lane;
+            if (acc_ok && n < p.N) {
+                const float b = p.bias ? p.bias[n] : 0.f;
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                    const int t = t0 + c0 + j;
+                    if (t < p.M) {
+                        float* o = p.out + static_cast<long long>(t) * p.ld + n;
+                        if (p.epi == EPI_ACCUM) *o += v[j] + b;
+                        else *o = v[j] + b;
+                    }
+                }
+            }
+        } else {
+            __syncthreads();
+            if (warp >= 2) {
+#pragma unroll
+                for (int j = 0; j < 16; ++j) xchg[((warp - 2) * 32 + lane) * 17 + j] = v[j];
+            }
+            __syncthreads();
+            if (warp < 2) {
+                const int i = wt * 64 + warp * 32 + lane;
+                if (acc_ok && i < p.half_n) {
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) {
+                        const int t = t0 + c0 + j;
+                        if (t < p.M)
+                            p.out[static_cast<long long>(t) * p.ld + i] = silu(v[j]) * xchg[(warp * 32 + lane) * 17 + j];
+                    }
+                }
+            }
+        }
+    }
+    if ((!ok || !acc_ok) && p.error) atomicExch(p.error, 1);
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(BN) : "memory");
+    }
+}
+
+__global__ void __launch_bounds__(256) cast_rows_kernel(const float* x, long long ld_x, const float* norm_w, float eps,
+                                                        void* out16, int dtype, int K) {
+    __shared__ float red[32];
+    pdl_wait();
+    const float* xr = x + blockIdx.x * ld_x;
+    float rstd = 1.f;
+    if (norm_w) {
+        float ss = 0.f;
+        for (int k = threadIdx.x; k < K; k += blockDim.x) ss += xr[k] * xr[k];
+        ss = block_sum(ss, red);
+        rstd = 1.0f / sqrtf(ss / static_cast<float>(K) + eps);
+    }
+    const long long base = static_cast<long long>(blockIdx.x) * K;
+    for (int k = threadIdx.x; k < K; k += blockDim.x) {
+        float v = xr[k];
+        if (norm_w) v = (v * rstd) * norm_w[k];
+        store_from_float(out16, dtype, base + k, v);
+    }
+}
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    if (!fn) {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+        else
+            cudaGetLastError();
+    }
+    return fn;
+}
+
+// Row-major [rows, K] 16-bit matrix, box {64 elements, box_rows}, 128-byte swizzle.
+l0b_status make_map(CUtensorMap* map, const void* base, int dtype, long long rows, long long K, int box_rows) {
+    EncodeTiledFn fn = encode_fn();
+    L0B_REQUIRE(fn, L0B_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+    L0B_REQUIRE(reinterpret_cast<uintptr_t>(base) % 16 == 0 && (K * 2) % 16 == 0, L0B_ERR_ARGUMENT,
+                "TMA needs 16-byte aligned rows (K %% 8 == 0)");
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(rows)};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(K * 2)};
+    const cuuint32_t box[2] = {static_cast<cuuint32_t>(kBK), static_cast<cuuint32_t>(box_rows)};
+    const cuuint32_t estr[2] = {1, 1};
+    CUresult r = fn(map, dtype == L0B_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+                    const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                    CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    L0B_REQUIRE(r == CUDA_SUCCESS, L0B_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", static_cast<int>(r));
+    return L0B_OK;
+}
+
+template <int BN, int FMT>
+l0b_status launch_bn(l0b_device* d, const TcParams& p, int grid_y) {
+    auto kernel = tc_gemm_kernel<BN, FMT>;
+    constexpr size_t smem = 1024 + kStages * (kBM * kBK * 2 + BN * kBK * 2) + 256;
+    static bool configured = false;
+    if (!configured) {
+        cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+        if (e != cudaSuccess) return fail(L0B_ERR_CUDA, "cudaFuncSetAttribute failed: %s", cudaGetErrorString(e));
+        configured = true;
+    }
+    dim3 grid((p.M + BN - 1) / BN, grid_y);
+    return d->launch(kernel, grid, dim3(kThreads), smem, p);
+}
+
+template <int FMT>
+l0b_status launch_fmt(l0b_device* d, const TcParams& p, int bn, int grid_y) {
+    switch (bn) {
+        case 64: return launch_bn<64, FMT>(d, p, grid_y);
+        case 128: return launch_bn<128, FMT>(d, p, grid_y);
+        default: return launch_bn<256, FMT>(d, p, grid_y);
+    }
+}
+
+}  // namespace
+
+bool tc_gemm_supported(int wdtype, int M, int N, int K, int epi) {
+    if (wdtype != L0B_F16 && wdtype != L0B_BF16) return false;
+    if (M < 1 || N < 1 || K < 64 || K % 8 != 0) return false;
+    if (epi == EPI_SWIGLU && (N % 2 != 0 || (N / 2) % 64 != 0)) return false;
+    return epi == EPI_STORE || epi == EPI_ACCUM || epi == EPI_SWIGLU;
+}
+
+l0b_status tc_gemm_launch(l0b_device* d, const TcGemmArgs& a) {
+    L0B_REQUIRE(tc_gemm_supported(a.wdtype, a.M, a.N, a.K, a.epi), L0B_ERR_UNSUPPORTED,
+                "tensor-core GEMM does not take M=%d N=%d K=%d epi=%d dtype=%d", a.M, a.N, a.K, a.epi, a.wdtype);
+    const int bn = a.M <= 64 ? 64 : a.M <= 128 ? 128 : 256;
+    TcParams p;
+    std::memset(&p, 0, sizeof(p));
+    const bool swiglu = a.epi == EPI_SWIGLU;
+    L0B_TRY(make_map(&p.wmap, a.w, a.wdtype, a.N, a.K, swiglu ? 64 : kBM));
+    L0B_TRY(make_map(&p.xmap, a.x16, a.wdtype, a.M, a.K, bn));
+    p.M = a.M;
+    p.N = a.N;
+    p.K = a.K;
+    p.epi = a.epi;
+    p.ld = a.ld;
+    p.half_n = a.N / 2;
+    p.out = a.out;
+    p.bias = a.bias;
+    p.error = d->error_flag;
+    const int grid_y = swiglu ? (a.N / 2) / 64 : (a.N + kBM - 1) / kBM;
+    if (a.wdtype == L0B_BF16) return launch_fmt<1>(d, p, bn, grid_y);
+    return launch_fmt<0>(d, p, bn, grid_y);
+}
+
+l0b_status cast_rows_launch(l0b_device* d, const float* x, long long ld_x, const float* norm_w, float eps, void* out16,
+                            int dtype, int M, int K) {
+    return d->launch(cast_rows_kernel, dim3(M), dim3(256), 0, x, ld_x, norm_w, eps, out16, dtype, K);
+}
+
+}  // namespace l0b

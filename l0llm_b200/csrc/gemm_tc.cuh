@@ -1,0 +1,29 @@
+// Tensor-core (tcgen05 / TMEM / TMA) GEMM for prefill and batched decode: Y[M, N] = X[M, K] W[N, K]^T.
+#pragma once
+
+#include "runtime.h"
+
+namespace l0b {
+
+struct TcGemmArgs {
+    int M, N, K;           // tokens, weight rows, inner dimension
+    const void* x16;       // [M, K] activations in the weight's 16-bit format (row stride K)
+    const void* w;         // [N, K] weights, f16 or bf16
+    int wdtype;            // L0B_F16 or L0B_BF16
+    int epi;               // GemvEpi: STORE, ACCUM or SWIGLU (W = [gate; up], N = 2 * I)
+    float* out;            // f32 output, row stride ld (SWIGLU: [M, N/2])
+    int ld;
+    const float* bias;     // STORE / ACCUM: f32 [N] or null
+};
+
+// Launches the GEMM on the device's stream (recorded when the device records).
+l0b_status tc_gemm_launch(l0b_device* d, const TcGemmArgs& a);
+
+// out16[m, :] = (RMSNorm(x[m, :]) if norm_w) in f16/bf16 for m < M; x row stride ld_x.
+l0b_status cast_rows_launch(l0b_device* d, const float* x, long long ld_x, const float* norm_w, float eps, void* out16,
+                            int dtype, int M, int K);
+
+// True when the tensor-core path takes this shape (16-bit weights, K % 64 == 0, N tile-aligned).
+bool tc_gemm_supported(int wdtype, int M, int N, int K, int epi);
+
+}  // namespace l0b

@@ -1,16 +1,18 @@
 // Weight-streaming linear layers for decode and small batches (sm_100a).
 //
 // Layout: W is [N, K] row-major (HuggingFace [out, in]); every output row is one contiguous stream.
-// A warp owns RPW consecutive rows; each lane reads 16 bytes per row per step with a no-L1-allocate
-// 128-bit load, so a warp step moves 512 contiguous bytes per row. int8 weights are dequantised in
-// registers (exact byte -> fp32 trick, see dequant_i8x4) and multiplied in fp32 with packed f32x2
-// FMAs; the per-lane partial sums are reduced with warp shuffles. Activations are staged once per
-// CTA in shared memory as fp32, permuted lane-major so the 128-bit shared loads are conflict-free,
-// and optionally RMS-normalised on the way in (fused input/post-attention norm).
+// A warp owns RPW rows (for SwiGLU a gate row and its up row); each lane reads 16 bytes per row per
+// step with a no-L1-allocate 128-bit load, so a warp step moves 512 contiguous bytes per row. int8
+// weights are dequantised in registers (exact byte -> fp32 trick, see dequant_i8x4) and multiplied in
+// fp32 with packed f32x2 FMAs; per-lane partial sums are reduced with warp shuffles. Activations are
+// staged once per CTA in shared memory as fp32, permuted lane-major so the 128-bit shared loads are
+// conflict-free, and optionally RMS-normalised on the way in (fused input/post-attention norm).
 //
-// The kernel is launched with programmatic dependent launch: before griddepcontrol.wait it
-// prefetches its first weight block into L2 (weights never depend on the previous kernel), so the
-// weight stream starts while the producer of x is still draining.
+// The grid is persistent (CTAs = SMs x resident CTAs per SM) and each warp walks its row blocks as one
+// flattened stream of (block, 512-byte chunk) steps through a register ring D steps deep: the loads of
+// step s + D are issued while step s is multiplied, and row-block epilogues run in the stream. The
+// first D steps are issued before griddepcontrol.wait -- weights never depend on the previous kernel
+// -- so under programmatic dependent launch the weight stream starts while the producer of x drains.
 #include "common.cuh"
 #include "gemv.cuh"
 
@@ -20,6 +22,7 @@ namespace {
 
 constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
+constexpr int kRing = 4;  // weight steps in flight per warp
 
 // Position of element r (0 <= r < 32*VEC) of a 32*VEC-element chunk in the lane-major smem layout:
 // the j-th float4 of lane l lives at j*128 + l*4.
@@ -48,6 +51,120 @@ __device__ __forceinline__ void epilogue_store(const GemvParams& p, int n, int m
     }
 }
 
+// Rows of row block `blk` owned by `warp`: RPW consecutive rows, or for SwiGLU pairs (i, i + N/2).
+template <int RPW>
+struct BlockRows {
+    int unit0;
+    int row[RPW];
+    bool valid[RPW];
+    __device__ __forceinline__ BlockRows(int blk, int warp, bool swiglu, int per_cta, int half_n, int N) {
+        unit0 = swiglu ? blk * per_cta + warp * (RPW / 2) : blk * kWarps * RPW + warp * RPW;
+#pragma unroll
+        for (int r = 0; r < RPW; ++r) {
+            row[r] = swiglu ? unit0 + (r & 1) * half_n + (r >> 1) : unit0 + r;
+            valid[r] = swiglu ? unit0 + (r >> 1) < half_n : row[r] < N;
+        }
+    }
+};
+
+// acc[r][m] += W[row r, chunk] . x[m, chunk] for one 16-byte weight vector per row. xb points at the
+// lane's first float4 of the chunk for activation row 0; rows of x are kt floats apart.
+template <typename WT, int MR, int RPW>
+__device__ __forceinline__ void mac_step(const uint4 (&w)[RPW], const float (&s)[RPW], const float* xb, int kt,
+                                         bool per_channel, float2 (&acc)[RPW][MR]) {
+#pragma unroll
+    for (int m = 0; m < MR; ++m) {
+        const float* xm = xb + m * kt;
+        if constexpr (sizeof(WT) == 1) {
+            const float4 x0 = *reinterpret_cast<const float4*>(xm);
+            const float4 x1 = *reinterpret_cast<const float4*>(xm + 128);
+            const float4 x2 = *reinterpret_cast<const float4*>(xm + 256);
+            const float4 x3 = *reinterpret_cast<const float4*>(xm + 384);
+#pragma unroll
+            for (int r = 0; r < RPW; ++r) {
+                float2 a = per_channel ? acc[r][m] : make_float2(0.f, 0.f);
+                float2 lo, hi;
+                dequant_i8x4(w[r].x, lo, hi);
+                a = ffma2(lo, make_float2(x0.x, x0.y), a);
+                a = ffma2(hi, make_float2(x0.z, x0.w), a);
+                dequant_i8x4(w[r].y, lo, hi);
+                a = ffma2(lo, make_float2(x1.x, x1.y), a);
+                a = ffma2(hi, make_float2(x1.z, x1.w), a);
+                dequant_i8x4(w[r].z, lo, hi);
+                a = ffma2(lo, make_float2(x2.x, x2.y), a);
+                a = ffma2(hi, make_float2(x2.z, x2.w), a);
+                dequant_i8x4(w[r].w, lo, hi);
+                a = ffma2(lo, make_float2(x3.x, x3.y), a);
+                a = ffma2(hi, make_float2(x3.z, x3.w), a);
+                acc[r][m] = per_channel ? a : ffma2(a, make_float2(s[r], s[r]), acc[r][m]);
+            }
+        } else if constexpr (sizeof(WT) == 2) {
+            const float4 x0 = *reinterpret_cast<const float4*>(xm);
+            const float4 x1 = *reinterpret_cast<const float4*>(xm + 128);
+#pragma unroll
+            for (int r = 0; r < RPW; ++r) {
+                float2 w0, w1, w2, w3;
+                if constexpr (DT<WT>::id == L0B_F16) {
+                    w0 = half2_bits_to_float2(w[r].x);
+                    w1 = half2_bits_to_float2(w[r].y);
+                    w2 = half2_bits_to_float2(w[r].z);
+                    w3 = half2_bits_to_float2(w[r].w);
+                } else {
+                    w0 = bf162_bits_to_float2(w[r].x);
+                    w1 = bf162_bits_to_float2(w[r].y);
+                    w2 = bf162_bits_to_float2(w[r].z);
+                    w3 = bf162_bits_to_float2(w[r].w);
+                }
+                float2 a = acc[r][m];
+                a = ffma2(w0, make_float2(x0.x, x0.y), a);
+                a = ffma2(w1, make_float2(x0.z, x0.w), a);
+                a = ffma2(w2, make_float2(x1.x, x1.y), a);
+                a = ffma2(w3, make_float2(x1.z, x1.w), a);
+                acc[r][m] = a;
+            }
+        } else {
+            const float4 x0 = *reinterpret_cast<const float4*>(xm);
+#pragma unroll
+            for (int r = 0; r < RPW; ++r) {
+                float2 a = acc[r][m];
+                a = ffma2(make_float2(__uint_as_float(w[r].x), __uint_as_float(w[r].y)), make_float2(x0.x, x0.y), a);
+                a = ffma2(make_float2(__uint_as_float(w[r].z), __uint_as_float(w[r].w)), make_float2(x0.z, x0.w), a);
+                acc[r][m] = a;
+            }
+        }
+    }
+}
+
+// Warp reduction of a finished row block and its epilogue; results spread over lanes for the stores.
+template <int MR, int RPW>
+__device__ __forceinline__ void finish_block(const GemvParams& p, float2 (&acc)[RPW][MR], const BlockRows<RPW>& g,
+                                             const float (&rscale)[RPW], bool per_channel, bool swiglu, int lane) {
+    float res[RPW][MR];
+#pragma unroll
+    for (int r = 0; r < RPW; ++r)
+#pragma unroll
+        for (int m = 0; m < MR; ++m) {
+            float v = warp_sum(acc[r][m].x + acc[r][m].y);
+            if (per_channel) v *= rscale[r];
+            res[r][m] = v;
+            acc[r][m] = make_float2(0.f, 0.f);
+        }
+    if (swiglu) {
+#pragma unroll
+        for (int r = 0; r < RPW; r += 2)
+#pragma unroll
+            for (int m = 0; m < MR; ++m)
+                if (lane == ((r * MR + m) & 31) && m < p.M && g.valid[r])
+                    epilogue_store(p, g.unit0 + (r >> 1), m, silu(res[r][m]) * res[r + 1][m]);
+    } else {
+#pragma unroll
+        for (int r = 0; r < RPW; ++r)
+#pragma unroll
+            for (int m = 0; m < MR; ++m)
+                if (lane == ((r * MR + m) & 31) && m < p.M && g.valid[r]) epilogue_store(p, g.row[r], m, res[r][m]);
+    }
+}
+
 template <typename WT, int MR, int RPW>
 __global__ void __launch_bounds__(kThreads) gemv_nk_kernel(const GemvParams p) {
     extern __shared__ float4 smem_f4[];
@@ -55,15 +172,18 @@ __global__ void __launch_bounds__(kThreads) gemv_nk_kernel(const GemvParams p) {
     __shared__ float rstd_s[MR];
     constexpr int VEC = 16 / sizeof(WT);
     constexpr int CH = 32 * VEC;  // elements per warp step
-    constexpr int ROWS = kWarps * RPW;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int N = p.N, K = p.K, M = p.M, kt = p.kt;
-    // SwiGLU: W is [gate; up] stacked, a warp owns pair i = (row i, row i + N/2); else RPW rows.
     const bool swiglu = p.epi == EPI_SWIGLU;
     const int half_n = N >> 1;
     const int units = swiglu ? half_n : N;
-    const int per_cta = swiglu ? kWarps * (RPW / 2) : ROWS;
+    const int per_cta = swiglu ? kWarps * (RPW / 2) : kWarps * RPW;
     const int nblocks = (units + per_cta - 1) / per_cta;
+    const bool per_channel = sizeof(WT) == 1 && p.group >= K;
+    const int gpr = sizeof(WT) == 1 ? K / p.group : 0;
+    const __half* scales = static_cast<const __half*>(p.scales);
+    const WT* W = static_cast<const WT*>(p.w);
+    const bool single_tile = K <= kt;
 
     if (p.prefetch && threadIdx.x == 0 && blockIdx.x < nblocks) {
         const long long u0 = static_cast<long long>(blockIdx.x) * per_cta;
@@ -78,6 +198,39 @@ __global__ void __launch_bounds__(kThreads) gemv_nk_kernel(const GemvParams p) {
             }
         }
     }
+
+    // Weight stream state (single-tile path): steps (block, chunk) of this CTA in order.
+    const int nchunks = (K + CH - 1) / CH;
+    const int my_blocks = blockIdx.x < nblocks ? (nblocks - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+    const int total = single_tile ? my_blocks * nchunks : 0;
+    uint4 ring[kRing][RPW];
+    float sring[kRing][RPW];
+    int i_step = 0, i_blk = blockIdx.x, i_c = 0;
+    auto issue = [&](uint4 (&slot)[RPW], float (&ss)[RPW]) {
+        if (i_step < total) {
+            const BlockRows<RPW> g(i_blk, warp, swiglu, per_cta, half_n, N);
+            const int kk = i_c * CH + lane * VEC;
+#pragma unroll
+            for (int r = 0; r < RPW; ++r) {
+                const bool ok = g.valid[r] && kk < K;
+                slot[r] = ok ? ld_stream_v4(W + static_cast<long long>(g.row[r]) * K + kk) : make_uint4(0, 0, 0, 0);
+                if constexpr (sizeof(WT) == 1)
+                    ss[r] = g.valid[r] ? __half2float(scales[static_cast<long long>(g.row[r]) * gpr +
+                                                             (kk < K ? kk : 0) / p.group])
+                                       : 0.f;
+                else
+                    ss[r] = 0.f;
+            }
+            if (++i_c == nchunks) {
+                i_c = 0;
+                i_blk += gridDim.x;
+            }
+        }
+        ++i_step;
+    };
+#pragma unroll
+    for (int d = 0; d < kRing; ++d) issue(ring[d], sring[d]);
+
     pdl_wait();
     pdl_launch_dependents();
 
@@ -112,150 +265,66 @@ __global__ void __launch_bounds__(kThreads) gemv_nk_kernel(const GemvParams p) {
         }
     };
 
-    const bool single_tile = K <= kt;
+    float2 acc[RPW][MR];
+#pragma unroll
+    for (int r = 0; r < RPW; ++r)
+#pragma unroll
+        for (int m = 0; m < MR; ++m) acc[r][m] = make_float2(0.f, 0.f);
+    float rscale[RPW];
+#pragma unroll
+    for (int r = 0; r < RPW; ++r) rscale[r] = 0.f;
+
     if (single_tile) {
         stage(0);
         __syncthreads();
-    }
-    const bool per_channel = sizeof(WT) == 1 && p.group >= K;
-    const int groups_per_row = sizeof(WT) == 1 ? K / p.group : 0;
-    const __half* scales = static_cast<const __half*>(p.scales);
-
-    for (int blk = blockIdx.x; blk < nblocks; blk += gridDim.x) {
-        const int unit0 = swiglu ? blk * per_cta + warp * (RPW / 2) : blk * ROWS + warp * RPW;
-        float2 acc[RPW][MR];
+        int c_blk = blockIdx.x, c_c = 0;
+        for (int s = 0; s < total; s += kRing) {
 #pragma unroll
-        for (int r = 0; r < RPW; ++r)
+            for (int d = 0; d < kRing; ++d) {
+                if (s + d < total) {
+                    mac_step<WT, MR, RPW>(ring[d], sring[d], xs + c_c * CH + lane * 4, kt, per_channel, acc);
 #pragma unroll
-            for (int m = 0; m < MR; ++m) acc[r][m] = make_float2(0.f, 0.f);
-
-        const WT* wrow[RPW];
-        int rowi[RPW];
-        bool valid[RPW];
-#pragma unroll
-        for (int r = 0; r < RPW; ++r) {
-            rowi[r] = swiglu ? unit0 + (r & 1) * half_n + (r >> 1) : unit0 + r;
-            valid[r] = swiglu ? unit0 + (r >> 1) < half_n : rowi[r] < N;
-            wrow[r] = static_cast<const WT*>(p.w) + static_cast<long long>(valid[r] ? rowi[r] : 0) * K;
-        }
-
-        for (int k0 = 0; k0 < K; k0 += kt) {
-            if (!single_tile) {
-                __syncthreads();
-                stage(k0);
-                __syncthreads();
-            }
-            const int klen = min(kt, K - k0);
-            int kk = lane * VEC;
-            uint4 cur[RPW];
-#pragma unroll
-            for (int r = 0; r < RPW; ++r)
-                cur[r] = (kk < klen && valid[r]) ? ld_stream_v4(wrow[r] + k0 + kk) : make_uint4(0, 0, 0, 0);
-            for (; kk < klen; kk += CH) {
-                uint4 nxt[RPW];
-                const bool more = kk + CH < klen;
-#pragma unroll
-                for (int r = 0; r < RPW; ++r)
-                    nxt[r] = (more && valid[r]) ? ld_stream_v4(wrow[r] + k0 + kk + CH) : make_uint4(0, 0, 0, 0);
-                const int cbase = (kk / CH) * CH;  // chunk start within the tile
-#pragma unroll
-                for (int m = 0; m < MR; ++m) {
-                    const float* xb = xs + m * kt + cbase + lane * 4;
-                    if constexpr (sizeof(WT) == 1) {
-                        const float4 x0 = *reinterpret_cast<const float4*>(xb);
-                        const float4 x1 = *reinterpret_cast<const float4*>(xb + 128);
-                        const float4 x2 = *reinterpret_cast<const float4*>(xb + 256);
-                        const float4 x3 = *reinterpret_cast<const float4*>(xb + 384);
-#pragma unroll
-                        for (int r = 0; r < RPW; ++r) {
-                            float2 a = per_channel ? acc[r][m] : make_float2(0.f, 0.f);
-                            float2 lo, hi;
-                            dequant_i8x4(cur[r].x, lo, hi);
-                            a = ffma2(lo, make_float2(x0.x, x0.y), a);
-                            a = ffma2(hi, make_float2(x0.z, x0.w), a);
-                            dequant_i8x4(cur[r].y, lo, hi);
-                            a = ffma2(lo, make_float2(x1.x, x1.y), a);
-                            a = ffma2(hi, make_float2(x1.z, x1.w), a);
-                            dequant_i8x4(cur[r].z, lo, hi);
-                            a = ffma2(lo, make_float2(x2.x, x2.y), a);
-                            a = ffma2(hi, make_float2(x2.z, x2.w), a);
-                            dequant_i8x4(cur[r].w, lo, hi);
-                            a = ffma2(lo, make_float2(x3.x, x3.y), a);
-                            a = ffma2(hi, make_float2(x3.z, x3.w), a);
-                            if (per_channel) {
-                                acc[r][m] = a;
-                            } else if (valid[r]) {
-                                const float s = __half2float(
-                                    scales[static_cast<long long>(rowi[r]) * groups_per_row + (k0 + kk) / p.group]);
-                                acc[r][m] = ffma2(a, make_float2(s, s), acc[r][m]);
-                            }
-                        }
-                    } else if constexpr (sizeof(WT) == 2) {
-                        const float4 x0 = *reinterpret_cast<const float4*>(xb);
-                        const float4 x1 = *reinterpret_cast<const float4*>(xb + 128);
-#pragma unroll
-                        for (int r = 0; r < RPW; ++r) {
-                            float2 w0, w1, w2, w3;
-                            if constexpr (DT<WT>::id == L0B_F16) {
-                                w0 = half2_bits_to_float2(cur[r].x);
-                                w1 = half2_bits_to_float2(cur[r].y);
-                                w2 = half2_bits_to_float2(cur[r].z);
-                                w3 = half2_bits_to_float2(cur[r].w);
-                            } else {
-                                w0 = bf162_bits_to_float2(cur[r].x);
-                                w1 = bf162_bits_to_float2(cur[r].y);
-                                w2 = bf162_bits_to_float2(cur[r].z);
-                                w3 = bf162_bits_to_float2(cur[r].w);
-                            }
-                            float2 a = acc[r][m];
-                            a = ffma2(w0, make_float2(x0.x, x0.y), a);
-                            a = ffma2(w1, make_float2(x0.z, x0.w), a);
-                            a = ffma2(w2, make_float2(x1.x, x1.y), a);
-                            a = ffma2(w3, make_float2(x1.z, x1.w), a);
-                            acc[r][m] = a;
-                        }
-                    } else {
-                        const float4 x0 = *reinterpret_cast<const float4*>(xb);
-#pragma unroll
-                        for (int r = 0; r < RPW; ++r) {
-                            float2 a = acc[r][m];
-                            a = ffma2(make_float2(__uint_as_float(cur[r].x), __uint_as_float(cur[r].y)),
-                                      make_float2(x0.x, x0.y), a);
-                            a = ffma2(make_float2(__uint_as_float(cur[r].z), __uint_as_float(cur[r].w)),
-                                      make_float2(x0.z, x0.w), a);
-                            acc[r][m] = a;
-                        }
+                    for (int r = 0; r < RPW; ++r) rscale[r] = sring[d][r];
+                    issue(ring[d], sring[d]);
+                    if (++c_c == nchunks) {
+                        finish_block<MR, RPW>(p, acc, BlockRows<RPW>(c_blk, warp, swiglu, per_cta, half_n, N), rscale,
+                                              per_channel, swiglu, lane);
+                        c_c = 0;
+                        c_blk += gridDim.x;
                     }
                 }
-#pragma unroll
-                for (int r = 0; r < RPW; ++r) cur[r] = nxt[r];
             }
         }
+        return;
+    }
 
-        // Reduce across the warp and run the epilogue; results are spread over lanes for the stores.
-        float res[RPW][MR];
+    // Multi-tile path (activation rows too long for shared memory): stage each K tile, then stream.
+    for (int blk = blockIdx.x; blk < nblocks; blk += gridDim.x) {
+        const BlockRows<RPW> g(blk, warp, swiglu, per_cta, half_n, N);
+        for (int k0 = 0; k0 < K; k0 += kt) {
+            __syncthreads();
+            stage(k0);
+            __syncthreads();
+            const int klen = min(kt, K - k0);
+            for (int kk = lane * VEC; kk < klen; kk += CH) {
+                uint4 w[RPW];
+                float sc[RPW];
 #pragma unroll
-        for (int r = 0; r < RPW; ++r)
-#pragma unroll
-            for (int m = 0; m < MR; ++m) {
-                float v = warp_sum(acc[r][m].x + acc[r][m].y);
-                if (per_channel && valid[r]) v *= __half2float(scales[rowi[r]]);
-                res[r][m] = v;
+                for (int r = 0; r < RPW; ++r) {
+                    w[r] = g.valid[r] ? ld_stream_v4(W + static_cast<long long>(g.row[r]) * K + k0 + kk)
+                                      : make_uint4(0, 0, 0, 0);
+                    if constexpr (sizeof(WT) == 1)
+                        sc[r] = g.valid[r]
+                                    ? __half2float(scales[static_cast<long long>(g.row[r]) * gpr + (k0 + kk) / p.group])
+                                    : 0.f;
+                    else
+                        sc[r] = 0.f;
+                    rscale[r] = sc[r];
+                }
+                mac_step<WT, MR, RPW>(w, sc, xs + (kk / CH) * CH + lane * 4, kt, per_channel, acc);
             }
-        if (swiglu) {
-#pragma unroll
-            for (int r = 0; r < RPW; r += 2)
-#pragma unroll
-                for (int m = 0; m < MR; ++m)
-                    if (lane == ((r * MR + m) & 31) && m < M && valid[r])
-                        epilogue_store(p, unit0 + (r >> 1), m, silu(res[r][m]) * res[r + 1][m]);
-        } else {
-#pragma unroll
-            for (int r = 0; r < RPW; ++r)
-#pragma unroll
-                for (int m = 0; m < MR; ++m)
-                    if (lane == ((r * MR + m) & 31) && m < M && valid[r]) epilogue_store(p, rowi[r], m, res[r][m]);
         }
+        finish_block<MR, RPW>(p, acc, g, rscale, per_channel, swiglu, lane);
     }
 }
 
@@ -318,10 +387,29 @@ l0b_status launch_on(l0b_device* dev, cudaStream_t stream, F kernel, dim3 g, dim
     return L0B_OK;
 }
 
+// Resident CTAs per SM for (kernel, dynamic smem), cached: the persistent grid is SMs x this.
+int resident_ctas(const void* func, size_t smem) {
+    struct Entry {
+        const void* func;
+        size_t smem;
+        int n;
+    };
+    static Entry cache[128];
+    static int used = 0;
+    for (int i = 0; i < used; ++i)
+        if (cache[i].func == func && cache[i].smem == smem) return cache[i].n;
+    int n = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, func, kThreads, smem) != cudaSuccess || n < 1) {
+        cudaGetLastError();
+        n = 1;
+    }
+    if (used < 128) cache[used++] = {func, smem, n};
+    return n;
+}
+
 template <typename WT, int MR>
 l0b_status launch_vec(l0b_device* dev, cudaStream_t stream, int sm_count, const GemvParams& p) {
     constexpr int RPW = 2;
-    constexpr int ROWS = kWarps * RPW;
     auto kernel = gemv_nk_kernel<WT, MR, RPW>;
     const size_t smem = static_cast<size_t>(MR) * p.kt * sizeof(float);
     static bool configured = false;
@@ -331,9 +419,10 @@ l0b_status launch_vec(l0b_device* dev, cudaStream_t stream, int sm_count, const 
         configured = true;
     }
     const int units = p.epi == EPI_SWIGLU ? p.N / 2 : p.N;
-    const int per_cta = p.epi == EPI_SWIGLU ? kWarps * (RPW / 2) : ROWS;
+    const int per_cta = p.epi == EPI_SWIGLU ? kWarps * (RPW / 2) : kWarps * RPW;
     const int nblocks = (units + per_cta - 1) / per_cta;
-    const int grid = nblocks < sm_count * 16 ? nblocks : sm_count * 16;
+    const int cap = sm_count * resident_ctas(reinterpret_cast<const void*>(kernel), smem);
+    const int grid = nblocks < cap ? nblocks : cap;
     return launch_on(dev, stream, kernel, dim3(grid), dim3(kThreads), smem, p);
 }
 

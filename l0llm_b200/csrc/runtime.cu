@@ -87,29 +87,32 @@ l0b_device::~l0b_device() {
     }
     graphs.clear();
     if (scratch.ptr) cudaFree(scratch.ptr);
+    if (scratch16.ptr) cudaFree(scratch16.ptr);
     if (counters) cudaFree(counters);
+    if (error_flag) cudaFree(error_flag);
     if (stream) cudaStreamDestroy(stream);
 }
 
-l0b_status l0b_device::ensure_scratch(size_t bytes, void** out) {
-    if (bytes > scratch.bytes) {
+l0b_status l0b_device::ensure_scratch(size_t bytes, void** out, int slot) {
+    DeviceScratch& sc = slot == 0 ? scratch : scratch16;
+    if (bytes > sc.bytes) {
         // Growing the scratch moves it: cached command lists that captured the old address no longer
         // match any new list (the address is a kernel argument), so they simply stop being reused.
         L0B_REQUIRE(!recording, L0B_ERR_INVALID_OPERATION,
                     "op scratch must grow to %zu bytes while a command list is being recorded; run the op "
                     "once outside a recording first",
                     bytes);
-        if (scratch.ptr) {
+        if (sc.ptr) {
             L0B_CHECK_CUDA(cudaStreamSynchronize(stream));
-            L0B_CHECK_CUDA(cudaFree(scratch.ptr));
-            scratch.ptr = nullptr;
-            scratch.bytes = 0;
+            L0B_CHECK_CUDA(cudaFree(sc.ptr));
+            sc.ptr = nullptr;
+            sc.bytes = 0;
         }
         size_t want = bytes < (1u << 20) ? (1u << 20) : bytes;
-        L0B_CHECK_CUDA(cudaMalloc(&scratch.ptr, want));
-        scratch.bytes = want;
+        L0B_CHECK_CUDA(cudaMalloc(&sc.ptr, want));
+        sc.bytes = want;
     }
-    *out = scratch.ptr;
+    *out = sc.ptr;
     return L0B_OK;
 }
 
@@ -364,6 +367,9 @@ L0B_API l0b_status l0b_device_create(int32_t index, l0b_device** out) {
     d->cc_major = p.major;
     d->smem_optin = p.sharedMemPerBlockOptin;
     L0B_CHECK_CUDA(cudaStreamCreateWithFlags(&d->stream, cudaStreamNonBlocking));
+    L0B_CHECK_CUDA(cudaMalloc(&d->error_flag, sizeof(int)));
+    L0B_CHECK_CUDA(cudaMemsetAsync(d->error_flag, 0, sizeof(int), d->stream));
+    L0B_CHECK_CUDA(cudaStreamSynchronize(d->stream));
     d->log.reserve(512);
     *out = d.release();
     return L0B_OK;
@@ -423,6 +429,16 @@ L0B_API l0b_status l0b_device_graph_stats(l0b_device* dev, int64_t* built, int64
     if (built) *built = dev->graphs_built;
     if (reused) *reused = dev->graphs_reused;
     if (updated) *updated = dev->graphs_updated;
+    return L0B_OK;
+}
+
+L0B_API l0b_status l0b_device_error_status(l0b_device* dev, int32_t* code) {
+    L0B_REQUIRE(dev && code, L0B_ERR_ARGUMENT, "null argument");
+    int v = 0;
+    L0B_CHECK_CUDA(cudaMemcpyAsync(&v, dev->error_flag, sizeof(int), cudaMemcpyDeviceToHost, dev->stream));
+    L0B_CHECK_CUDA(cudaMemsetAsync(dev->error_flag, 0, sizeof(int), dev->stream));
+    L0B_CHECK_CUDA(cudaStreamSynchronize(dev->stream));
+    *code = v;
     return L0B_OK;
 }
 

@@ -138,15 +138,19 @@ struct l0b_device {
     std::vector<std::unique_ptr<l0b::CachedGraph>> graphs;
     uint64_t use_clock = 0;
     int64_t graphs_built = 0, graphs_reused = 0, graphs_updated = 0;
-    // Scratch for op-level kernels that need temporary device memory (split-KV partials, counters).
+    // Scratch for op-level kernels that need temporary device memory, one slot per purpose so two ops
+    // of one command list never share it: 0 = split-KV partials, 1 = 16-bit activation copies.
     l0b::DeviceScratch scratch;
+    l0b::DeviceScratch scratch16;
     // Zeroed counters for last-block-done reductions; each user resets what it used.
     unsigned* counters = nullptr;
     size_t counter_count = 0;
+    // Set by kernels whose bounded waits gave up (read and cleared by l0b_device_error_status).
+    int* error_flag = nullptr;
 
     ~l0b_device();
 
-    l0b_status ensure_scratch(size_t bytes, void** out);
+    l0b_status ensure_scratch(size_t bytes, void** out, int slot = 0);
     l0b_status ensure_counters(size_t count, unsigned** out);
 
     // Appends (recording) or launches (immediate) one kernel.
