@@ -348,6 +348,14 @@ L0B_API l0b_status l0b_linear_fused(l0b_suite* s, l0b_device* d, int32_t m, int3
                                     l0b_buffer* w, l0b_buffer* scales, int32_t group, l0b_buffer* norm_w, float eps,
                                     int32_t epilogue, l0b_buffer* bias, l0b_buffer* out);
 
+/* Prefill-sized linear layer on the tensor cores (tcgen05.mma, accumulator in TMEM, TMA-fed): the x
+ * rows are (RMS-normalised with norm_w when given and) rounded to the weight's 16-bit format, then
+ * out = epilogue(x16 W^T) with fp32 accumulation. w: f16 or bf16 [N, K], K % 8 == 0; SwiGLU needs
+ * (N/2) % 64 == 0. The multi-row GEMV of Gemv.ExecuteRows (L/LlmMatrix.cs:149-171) replaced by a GEMM. */
+L0B_API l0b_status l0b_linear_tc(l0b_suite* s, l0b_device* d, int32_t m, int32_t n, int32_t k, l0b_buffer* x,
+                                 l0b_buffer* w, l0b_buffer* norm_w, float eps, int32_t epilogue, l0b_buffer* bias,
+                                 l0b_buffer* out);
+
 /* Raw-pointer int8 GEMV for callers that manage device memory themselves (config 0 shape:
  * y[M,N] = x[M,K] * (q * s)^T with fp16 x and y). x_dtype/y_dtype from l0b_dtype. Enqueued on
  * `stream` (a cudaStream_t, NULL = legacy default stream); returns immediately. */

@@ -67,6 +67,32 @@ struct BlockRows {
     }
 };
 
+// Exact int8 -> fp32 of the four signed bytes of a word: byte b biased to u = b ^ 0x80 (0..255) sits in
+// the mantissa of 2^23 (the float 0x4B0000uu = 8388608 + u), and subtracting 8388608 + 128 gives b.
+__device__ __forceinline__ void dequant4(uint32_t w, float& f0, float& f1, float& f2, float& f3) {
+    const uint32_t u = w ^ 0x80808080u;
+    f0 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7440)) - 8388736.0f;
+    f1 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7441)) - 8388736.0f;
+    f2 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7442)) - 8388736.0f;
+    f3 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7443)) - 8388736.0f;
+}
+
+// a += dot(4 weights of word w, x) with two independent accumulators (a.x, a.y) for ILP.
+__device__ __forceinline__ void dot4_i8(uint32_t w, const float4& x, float2& a) {
+    float f0, f1, f2, f3;
+    dequant4(w, f0, f1, f2, f3);
+    a.x = fmaf(f0, x.x, a.x);
+    a.y = fmaf(f1, x.y, a.y);
+    a.x = fmaf(f2, x.z, a.x);
+    a.y = fmaf(f3, x.w, a.y);
+}
+
+template <typename WT>
+__device__ __forceinline__ float2 w2_to_f2(uint32_t w) {
+    if constexpr (DT<WT>::id == L0B_F16) return half2_bits_to_float2(w);
+    else return bf162_bits_to_float2(w);
+}
+
 // acc[r][m] += W[row r, chunk] . x[m, chunk] for one 16-byte weight vector per row. xb points at the
 // lane's first float4 of the chunk for activation row 0; rows of x are kt floats apart.
 template <typename WT, int MR, int RPW>
@@ -82,54 +108,46 @@ __device__ __forceinline__ void mac_step(const uint4 (&w)[RPW], const float (&s)
             const float4 x3 = *reinterpret_cast<const float4*>(xm + 384);
 #pragma unroll
             for (int r = 0; r < RPW; ++r) {
-                float2 a = per_channel ? acc[r][m] : make_float2(0.f, 0.f);
-                float2 lo, hi;
-                dequant_i8x4(w[r].x, lo, hi);
-                a = ffma2(lo, make_float2(x0.x, x0.y), a);
-                a = ffma2(hi, make_float2(x0.z, x0.w), a);
-                dequant_i8x4(w[r].y, lo, hi);
-                a = ffma2(lo, make_float2(x1.x, x1.y), a);
-                a = ffma2(hi, make_float2(x1.z, x1.w), a);
-                dequant_i8x4(w[r].z, lo, hi);
-                a = ffma2(lo, make_float2(x2.x, x2.y), a);
-                a = ffma2(hi, make_float2(x2.z, x2.w), a);
-                dequant_i8x4(w[r].w, lo, hi);
-                a = ffma2(lo, make_float2(x3.x, x3.y), a);
-                a = ffma2(hi, make_float2(x3.z, x3.w), a);
-                acc[r][m] = per_channel ? a : ffma2(a, make_float2(s[r], s[r]), acc[r][m]);
+                if (per_channel) {
+                    dot4_i8(w[r].x, x0, acc[r][m]);
+                    dot4_i8(w[r].y, x1, acc[r][m]);
+                    dot4_i8(w[r].z, x2, acc[r][m]);
+                    dot4_i8(w[r].w, x3, acc[r][m]);
+                } else {
+                    float2 a = make_float2(0.f, 0.f);
+                    dot4_i8(w[r].x, x0, a);
+                    dot4_i8(w[r].y, x1, a);
+                    dot4_i8(w[r].z, x2, a);
+                    dot4_i8(w[r].w, x3, a);
+                    acc[r][m].x = fmaf(a.x + a.y, s[r], acc[r][m].x);
+                }
             }
         } else if constexpr (sizeof(WT) == 2) {
             const float4 x0 = *reinterpret_cast<const float4*>(xm);
             const float4 x1 = *reinterpret_cast<const float4*>(xm + 128);
 #pragma unroll
             for (int r = 0; r < RPW; ++r) {
-                float2 w0, w1, w2, w3;
-                if constexpr (DT<WT>::id == L0B_F16) {
-                    w0 = half2_bits_to_float2(w[r].x);
-                    w1 = half2_bits_to_float2(w[r].y);
-                    w2 = half2_bits_to_float2(w[r].z);
-                    w3 = half2_bits_to_float2(w[r].w);
-                } else {
-                    w0 = bf162_bits_to_float2(w[r].x);
-                    w1 = bf162_bits_to_float2(w[r].y);
-                    w2 = bf162_bits_to_float2(w[r].z);
-                    w3 = bf162_bits_to_float2(w[r].w);
-                }
-                float2 a = acc[r][m];
-                a = ffma2(w0, make_float2(x0.x, x0.y), a);
-                a = ffma2(w1, make_float2(x0.z, x0.w), a);
-                a = ffma2(w2, make_float2(x1.x, x1.y), a);
-                a = ffma2(w3, make_float2(x1.z, x1.w), a);
-                acc[r][m] = a;
+                const float2 w0 = w2_to_f2<WT>(w[r].x), w1 = w2_to_f2<WT>(w[r].y);
+                const float2 w2 = w2_to_f2<WT>(w[r].z), w3 = w2_to_f2<WT>(w[r].w);
+                float2& a = acc[r][m];
+                a.x = fmaf(w0.x, x0.x, a.x);
+                a.y = fmaf(w0.y, x0.y, a.y);
+                a.x = fmaf(w1.x, x0.z, a.x);
+                a.y = fmaf(w1.y, x0.w, a.y);
+                a.x = fmaf(w2.x, x1.x, a.x);
+                a.y = fmaf(w2.y, x1.y, a.y);
+                a.x = fmaf(w3.x, x1.z, a.x);
+                a.y = fmaf(w3.y, x1.w, a.y);
             }
         } else {
             const float4 x0 = *reinterpret_cast<const float4*>(xm);
 #pragma unroll
             for (int r = 0; r < RPW; ++r) {
-                float2 a = acc[r][m];
-                a = ffma2(make_float2(__uint_as_float(w[r].x), __uint_as_float(w[r].y)), make_float2(x0.x, x0.y), a);
-                a = ffma2(make_float2(__uint_as_float(w[r].z), __uint_as_float(w[r].w)), make_float2(x0.z, x0.w), a);
-                acc[r][m] = a;
+                float2& a = acc[r][m];
+                a.x = fmaf(__uint_as_float(w[r].x), x0.x, a.x);
+                a.y = fmaf(__uint_as_float(w[r].y), x0.y, a.y);
+                a.x = fmaf(__uint_as_float(w[r].z), x0.z, a.x);
+                a.y = fmaf(__uint_as_float(w[r].w), x0.w, a.y);
             }
         }
     }
@@ -166,7 +184,7 @@ __device__ __forceinline__ void finish_block(const GemvParams& p, float2 (&acc)[
 }
 
 template <typename WT, int MR, int RPW>
-__global__ void __launch_bounds__(kThreads) gemv_nk_kernel(const GemvParams p) {
+__global__ void __launch_bounds__(kThreads, MR >= 4 ? 1 : 2) gemv_nk_kernel(const GemvParams p) {
     extern __shared__ float4 smem_f4[];
     float* xs = reinterpret_cast<float*>(smem_f4);
     __shared__ float rstd_s[MR];
@@ -205,25 +223,39 @@ __global__ void __launch_bounds__(kThreads) gemv_nk_kernel(const GemvParams p) {
     const int total = single_tile ? my_blocks * nchunks : 0;
     uint4 ring[kRing][RPW];
     float sring[kRing][RPW];
+    // Row starts (null past N) and scale rows of the block being issued; updated at block changes only.
+    const WT* i_ptr[RPW];
+    const __half* i_sc[RPW];
+    const int gshift = __ffs(p.group > 0 ? p.group : 1) - 1;
+    const bool gpow2 = p.group > 0 && (1 << gshift) == p.group;
     int i_step = 0, i_blk = blockIdx.x, i_c = 0;
+    auto set_issue_block = [&](int blk) {
+        const BlockRows<RPW> g(blk, warp, swiglu, per_cta, half_n, N);
+#pragma unroll
+        for (int r = 0; r < RPW; ++r) {
+            i_ptr[r] = g.valid[r] ? W + static_cast<long long>(g.row[r]) * K : nullptr;
+            i_sc[r] = (sizeof(WT) == 1 && g.valid[r]) ? scales + static_cast<long long>(g.row[r]) * gpr : nullptr;
+        }
+    };
+    set_issue_block(blockIdx.x);
     auto issue = [&](uint4 (&slot)[RPW], float (&ss)[RPW]) {
         if (i_step < total) {
-            const BlockRows<RPW> g(i_blk, warp, swiglu, per_cta, half_n, N);
             const int kk = i_c * CH + lane * VEC;
+            const bool in_k = kk < K;
 #pragma unroll
             for (int r = 0; r < RPW; ++r) {
-                const bool ok = g.valid[r] && kk < K;
-                slot[r] = ok ? ld_stream_v4(W + static_cast<long long>(g.row[r]) * K + kk) : make_uint4(0, 0, 0, 0);
-                if constexpr (sizeof(WT) == 1)
-                    ss[r] = g.valid[r] ? __half2float(scales[static_cast<long long>(g.row[r]) * gpr +
-                                                             (kk < K ? kk : 0) / p.group])
-                                       : 0.f;
-                else
-                    ss[r] = 0.f;
+                slot[r] = (i_ptr[r] && in_k) ? ld_stream_v4(i_ptr[r] + kk) : make_uint4(0, 0, 0, 0);
+                if constexpr (sizeof(WT) == 1) {
+                    if (!per_channel)
+                        ss[r] = (i_sc[r] && in_k) ? __half2float(i_sc[r][gpow2 ? kk >> gshift : kk / p.group]) : 0.f;
+                    else if (i_c == 0)
+                        ss[r] = i_sc[r] ? __half2float(i_sc[r][0]) : 0.f;
+                }
             }
             if (++i_c == nchunks) {
                 i_c = 0;
                 i_blk += gridDim.x;
+                set_issue_block(i_blk);
             }
         }
         ++i_step;
@@ -234,23 +266,57 @@ __global__ void __launch_bounds__(kThreads) gemv_nk_kernel(const GemvParams p) {
     pdl_wait();
     pdl_launch_dependents();
 
-    // RMS of each activation row (fused norm), read straight from global memory.
+    // fp32 activations in 16-byte aligned rows take the vector path of the prologue.
+    const bool xvec = p.x_dtype == L0B_F32 && (K & 3) == 0 && (p.x_ld & 3) == 0 &&
+                      (reinterpret_cast<uintptr_t>(p.x) & 15) == 0;
+    const float* xf = static_cast<const float*>(p.x);
+
+    // RMS of each activation row (fused norm): a block-wide reduction per row.
     if (p.norm_w) {
-        for (int m = warp; m < MR; m += kWarps) {
+        __shared__ float red[32];
+        for (int m = 0; m < MR; ++m) {
             float ss = 0.f;
             if (m < M) {
-                for (int k = lane; k < K; k += 32) {
-                    const float v = load_as_float(p.x, p.x_dtype, m * p.x_ld + k);
-                    ss += v * v;
+                if (xvec) {
+                    for (int k = threadIdx.x * 4; k < K; k += kThreads * 4) {
+                        const float4 v = *reinterpret_cast<const float4*>(xf + m * p.x_ld + k);
+                        ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+                    }
+                } else {
+                    for (int k = threadIdx.x; k < K; k += kThreads) {
+                        const float v = load_as_float(p.x, p.x_dtype, m * p.x_ld + k);
+                        ss += v * v;
+                    }
                 }
             }
-            ss = warp_sum(ss);
-            if (lane == 0) rstd_s[m] = 1.0f / sqrtf(ss / static_cast<float>(K) + p.eps);
+            ss = block_sum(ss, red);
+            if (threadIdx.x == 0) rstd_s[m] = 1.0f / sqrtf(ss / static_cast<float>(K) + p.eps);
         }
         __syncthreads();
     }
 
     auto stage = [&](int k0) {
+        if (xvec) {
+            // Four consecutive elements stay consecutive in the lane-major layout (VEC is a multiple of 4).
+            const int quads = kt >> 2;
+            for (int m = 0; m < MR; ++m) {
+                for (int qi = threadIdx.x; qi < quads; qi += kThreads) {
+                    const int r = qi << 2, k = k0 + r;
+                    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+                    if (m < M && k < K) {
+                        v = *reinterpret_cast<const float4*>(xf + m * p.x_ld + k);
+                        if (p.norm_w) {
+                            const float rs = rstd_s[m];
+                            const float4 w4 = *reinterpret_cast<const float4*>(p.norm_w + k);
+                            v = make_float4((v.x * rs) * w4.x, (v.y * rs) * w4.y, (v.z * rs) * w4.z, (v.w * rs) * w4.w);
+                        }
+                    }
+                    const int c = r / CH, rr = r - c * CH;
+                    *reinterpret_cast<float4*>(xs + m * kt + c * CH + xs_perm<VEC>(rr)) = v;
+                }
+            }
+            return;
+        }
         const int span = MR * kt;
         for (int idx = threadIdx.x; idx < span; idx += kThreads) {
             const int m = idx / kt, r = idx - m * kt;
@@ -283,8 +349,10 @@ __global__ void __launch_bounds__(kThreads) gemv_nk_kernel(const GemvParams p) {
             for (int d = 0; d < kRing; ++d) {
                 if (s + d < total) {
                     mac_step<WT, MR, RPW>(ring[d], sring[d], xs + c_c * CH + lane * 4, kt, per_channel, acc);
+                    if (per_channel && c_c == 0) {
 #pragma unroll
-                    for (int r = 0; r < RPW; ++r) rscale[r] = sring[d][r];
+                        for (int r = 0; r < RPW; ++r) rscale[r] = sring[d][r];
+                    }
                     issue(ring[d], sring[d]);
                     if (++c_c == nchunks) {
                         finish_block<MR, RPW>(p, acc, BlockRows<RPW>(c_blk, warp, swiglu, per_cta, half_n, N), rscale,

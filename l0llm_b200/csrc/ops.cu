@@ -7,6 +7,7 @@
 
 #include <cuda_fp16.h>
 
+#include "gemm_tc.cuh"
 #include "gemv.cuh"
 #include "ops.cuh"
 #include "suite.h"
@@ -545,6 +546,39 @@ L0B_API l0b_status l0b_linear_fused(l0b_suite* s, l0b_device* d, int32_t m, int3
     p.seg[0].ld = out_cols;
     p.prefetch = 1;
     return gemv_nk_launch(d, wdt, p);
+}
+
+L0B_API l0b_status l0b_linear_tc(l0b_suite* s, l0b_device* d, int32_t m, int32_t n, int32_t k, l0b_buffer* x,
+                                 l0b_buffer* w, l0b_buffer* norm_w, float eps, int32_t epilogue, l0b_buffer* bias,
+                                 l0b_buffer* out) {
+    L0B_TRY(check_suite(s, d));
+    L0B_REQUIRE(m > 0 && n > 0 && k > 0, L0B_ERR_OUT_OF_RANGE, "shape M=%d N=%d K=%d", m, n, k);
+    L0B_REQUIRE(w && (w->dtype == L0B_F16 || w->dtype == L0B_BF16), L0B_ERR_ARGUMENT, "W must be f16 or bf16");
+    L0B_REQUIRE(w->count >= static_cast<long long>(n) * k, L0B_ERR_ARGUMENT, "W is smaller than N*K");
+    const int epi = epilogue == L0B_EPI_ACCUM ? EPI_ACCUM : epilogue == L0B_EPI_SWIGLU ? EPI_SWIGLU : EPI_STORE;
+    L0B_REQUIRE(tc_gemm_supported(w->dtype, m, n, k, epi), L0B_ERR_UNSUPPORTED,
+                "the tensor-core GEMM needs K %% 8 == 0, K >= 64 and for SwiGLU (N/2) %% 64 == 0");
+    L0B_REQUIRE(epi != EPI_SWIGLU || !bias, L0B_ERR_ARGUMENT, "the SwiGLU epilogue takes no bias");
+    const int out_cols = epi == EPI_SWIGLU ? n / 2 : n;
+    L0B_TRY(need(x, "x", L0B_F32, static_cast<long long>(m) * k));
+    L0B_TRY(need(out, "out", L0B_F32, static_cast<long long>(m) * out_cols));
+    if (norm_w) L0B_TRY(need(norm_w, "norm_w", L0B_F32, k));
+    if (bias) L0B_TRY(need(bias, "bias", L0B_F32, n));
+    void* x16 = nullptr;
+    L0B_TRY(d->ensure_scratch(static_cast<size_t>(m) * k * 2, &x16, 1));
+    L0B_TRY(cast_rows_launch(d, F(x), k, norm_w ? F(norm_w) : nullptr, eps, x16, w->dtype, m, k));
+    TcGemmArgs a;
+    a.M = m;
+    a.N = n;
+    a.K = k;
+    a.x16 = x16;
+    a.w = w->ptr;
+    a.wdtype = w->dtype;
+    a.epi = epi;
+    a.out = F(out);
+    a.ld = out_cols;
+    a.bias = bias ? F(bias) : nullptr;
+    return tc_gemm_launch(d, a);
 }
 
 L0B_API l0b_status l0b_gemv_w8a16_raw(void* stream, int32_t m, int32_t n, int32_t k, const void* x, int32_t x_dtype,

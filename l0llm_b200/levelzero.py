@@ -167,6 +167,9 @@ def load_library() -> C.CDLL:
         "l0b_linear": (i32, [vp, vp, i32, i32, i32, vp, vp, vp, i32, vp, vp]),
         "l0b_gemv_w8a16_raw": (i32, [vp, i32, i32, i32, vp, i32, vp, vp, i32, vp, i32]),
         "l0b_linear_fused": (i32, [vp, vp, i32, i32, i32, vp, vp, vp, i32, vp, f32, i32, vp, vp]),
+        "l0b_linear_tc": (i32, [vp, vp, i32, i32, i32, vp, vp, vp, f32, i32, vp, vp]),
+        "l0b_device_error_status": (i32, [vp, C.POINTER(i32)]),
+        "l0b_attention_decode_noalloc": (i32, [vp, vp, vp, vp, i32, vp, i32, i32, i32, i32, i32]),
         "l0b_model_config_init": (i32, [C.POINTER(ModelConfig)]),
         "l0b_rope_frequencies": (i32, [C.POINTER(ModelConfig), vp, i32, C.POINTER(i32), C.POINTER(f32)]),
         "l0b_model_create": (i32, [vp, vp, C.POINTER(ModelConfig), i32, i32, vp, pp]),
@@ -307,13 +310,17 @@ class SharedBuffer:
         if dtype is None:
             dtype = {np.dtype(np.float32): F32, np.dtype(np.float16): F16, np.dtype(np.int8): I8,
                      np.dtype(np.int32): I32, np.dtype(np.uint8): U8, np.dtype(np.uint16): BF16}[data.dtype]
-        arr = np.ascontiguousarray(data, NP_DTYPE[dtype]).ravel()
-        b = cls(device, dtype, arr.size)
-        b.Write(arr)
+        b = cls(device, dtype, np.asarray(data).size)
+        b.Write(data)
         return b
 
     def Write(self, data: np.ndarray, offset: int = 0):
-        arr = np.ascontiguousarray(data, NP_DTYPE[self.dtype]).ravel()
+        want = np.dtype(NP_DTYPE[self.dtype])
+        data = np.asarray(data)
+        if self.dtype in (F16, BF16) and data.dtype != want and data.dtype.itemsize == 2 and data.dtype.kind in "ui":
+            # 16-bit payloads given as raw bits (uint16 / int16): reinterpret, never convert.
+            data = np.ascontiguousarray(data).view(want)
+        arr = np.ascontiguousarray(data, want).ravel()
         check(load_library().l0b_buffer_write(self.handle, offset, _p(arr), arr.size))
 
     def ToArray(self, offset: int = 0, count: int | None = None) -> np.ndarray:

@@ -1,0 +1,82 @@
+"""GPU parity of the tcgen05 tensor-core GEMM (prefill linear layers) against the CPU oracle.
+
+The GEMM multiplies activations rounded to the weight's 16-bit format, so the oracle is fed the same
+rounded activations; what remains is accumulation order (fp32 in TMEM vs fp64), held to 1e-3.
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+
+def _round16(x, fmt):
+    import torch
+
+    t = torch.from_numpy(np.ascontiguousarray(x, np.float32))
+    return (t.to(torch.bfloat16) if fmt == "bf16" else t.to(torch.float16)).to(torch.float32).numpy()
+
+
+def _wbits(w, fmt):
+    import torch
+
+    t = torch.from_numpy(np.ascontiguousarray(w, np.float32))
+    return (t.to(torch.bfloat16) if fmt == "bf16" else t.to(torch.float16)).view(torch.int16).numpy().view(np.uint16)
+
+
+@pytest.mark.parametrize("fmt", ["f16", "bf16"])
+@pytest.mark.parametrize("m,n,k", [(64, 256, 896), (130, 4608, 3584), (17, 384, 512), (512, 1000, 1024),
+                                   (256, 3584, 3584), (1, 128, 64)])
+@pytest.mark.parametrize("epi", ["store", "accum"])
+def test_tc_gemm_store_accum(lz, orc, device, suite, fmt, m, n, k, epi):
+    rng = np.random.default_rng(m * 3 + n + k)
+    x = rng.standard_normal((m, k)).astype(np.float32)
+    w = ((rng.random((n, k)) * 2 - 1) * 0.05).astype(np.float32)
+    bias = (rng.standard_normal(n) * 0.1).astype(np.float32)
+    base = rng.standard_normal((m, n)).astype(np.float32)
+    wb = _wbits(w, fmt)
+    want = orc.gemv_out_in(_round16(x, fmt), wb, orc.BF16 if fmt == "bf16" else orc.F16) + bias
+    if epi == "accum":
+        want = want + base
+    code = lz.BF16 if fmt == "bf16" else lz.F16
+    with lz.SharedBuffer.from_array(device, x) as xb, lz.SharedBuffer.from_array(device, wb, code) as W, \
+            lz.SharedBuffer.from_array(device, bias) as bb, lz.SharedBuffer.from_array(device, base) as ob:
+        lz.check(lz.load_library().l0b_linear_tc(suite.handle, device.handle, m, n, k, xb.handle, W.handle, None,
+                                                  0.0, 1 if epi == "accum" else 0, bb.handle, ob.handle))
+        got = ob.ToArray().reshape(m, n)
+    err = np.abs(got - want)
+    assert np.all(err <= 1e-3 + 1e-3 * np.abs(want)), f"max err {err.max()}"
+
+
+@pytest.mark.parametrize("fmt", ["f16", "bf16"])
+@pytest.mark.parametrize("m", [5, 128, 300])
+def test_tc_gemm_norm_swiglu(lz, orc, device, suite, fmt, m):
+    rng = np.random.default_rng(m)
+    H, I = 896, 4864
+    x = rng.standard_normal((m, H)).astype(np.float32) * 2
+    nw = (1 + 0.1 * rng.standard_normal(H)).astype(np.float32)
+    w = ((rng.random((2 * I, H)) * 2 - 1) * 0.05).astype(np.float32)
+    _, normed = orc.rmsnorm(x, nw, 1e-6)
+    wb = _wbits(w, fmt)
+    y = orc.gemv_out_in(_round16(normed, fmt), wb, orc.BF16 if fmt == "bf16" else orc.F16)
+    g, u = y[:, :I], y[:, I:]
+    want = g / (1 + np.exp(-g.astype(np.float64))) * u
+    code = lz.BF16 if fmt == "bf16" else lz.F16
+    with lz.SharedBuffer.from_array(device, x) as xb, lz.SharedBuffer.from_array(device, wb, code) as W, \
+            lz.SharedBuffer.from_array(device, nw) as nb, lz.SharedBuffer(device, lz.F32, m * I) as ob:
+        lz.check(lz.load_library().l0b_linear_tc(suite.handle, device.handle, m, 2 * I, H, xb.handle, W.handle,
+                                                  nb.handle, 1e-6, 2, None, ob.handle))
+        got = ob.ToArray().reshape(m, I)
+    # The norm runs before the 16-bit rounding on both sides; a few elements may round differently.
+    err = np.abs(got - want)
+    assert np.all(err <= 2e-3 + 2e-2 * np.abs(want)), f"max err {err.max()}"
+    assert np.median(err) < 1e-3
+
+
+def test_tc_gemm_reports_no_timeouts(lz, device):
+    import ctypes as C
+
+    code = C.c_int32()
+    lz.check(lz.load_library().l0b_device_error_status(device.handle, C.byref(code)))
+    assert code.value == 0
