@@ -356,6 +356,11 @@ L0B_API l0b_status l0b_linear_tc(l0b_suite* s, l0b_device* d, int32_t m, int32_t
                                  l0b_buffer* w, l0b_buffer* norm_w, float eps, int32_t epilogue, l0b_buffer* bias,
                                  l0b_buffer* out);
 
+/* Process-wide choice of the decode GEMV kernel for shapes both take: 1 (default) = tensor-core
+ * mma.sync streaming kernel, 0 = fp32-FMA streaming kernel. Used by tests to cover both; recorded
+ * command lists keep the kernel they were recorded with. No counterpart in the reference. */
+L0B_API l0b_status l0b_set_gemv_tensor_cores(int32_t enable);
+
 /* Raw-pointer int8 GEMV for callers that manage device memory themselves (config 0 shape:
  * y[M,N] = x[M,K] * (q * s)^T with fp16 x and y). x_dtype/y_dtype from l0b_dtype. Enqueued on
  * `stream` (a cudaStream_t, NULL = legacy default stream); returns immediately. */

@@ -32,7 +32,9 @@ __device__ __forceinline__ int xs_perm(int r) {
     return j * 128 + l * 4 + e;
 }
 
-__device__ __forceinline__ void epilogue_store(const GemvParams& p, int n, int m, float v) {
+// Stores output row n of activation row m through the segment table and returns the value after the
+// bias. `fold` = false leaves the argmax to the caller (which reduces keys across lanes first).
+__device__ __forceinline__ float epilogue_store(const GemvParams& p, int n, int m, float v, bool fold = true) {
     int s = 0;
     while (s < p.nseg - 1 && n >= p.seg[s].row_end) ++s;
     const int begin = s ? p.seg[s - 1].row_end : 0;
@@ -45,10 +47,11 @@ __device__ __forceinline__ void epilogue_store(const GemvParams& p, int n, int m
         o[idx] += v;
     } else if (p.epi == EPI_ARGMAX) {
         if (g.out) store_from_float(g.out, p.out_dtype, idx, v);
-        atomicMax(p.argmax + m, argmax_key(v, n));
+        if (fold) atomicMax(p.argmax + m, argmax_key(v, n));
     } else {
         store_from_float(g.out, p.out_dtype, idx, v);
     }
+    return v;
 }
 
 // Rows of row block `blk` owned by `warp`: RPW consecutive rows, or for SwiGLU pairs (i, i + N/2).
@@ -445,6 +448,369 @@ __global__ void __launch_bounds__(kThreads) gemv_nk_scalar_kernel(const GemvPara
     if (lane == 0) epilogue_store(p, n, m, pairs ? silu(res[0]) * res[1] : res[0]);
 }
 
+// ---------------------------------------------------------------------------------------------
+// Tensor-core weight streaming for up to 8 activation rows (decode, small batches).
+//
+// One mma.sync.m16n8k16 (fp32 accumulate) takes a 16-row x 16-k weight tile as its A operand and
+// eight activation columns as B. Column 2m of B holds half(x[m] * 2^-4) and column 2m + 1 the fp16
+// residual half(x[m] * 2^-4 - hi), so the two products summed give the dot product with x to ~22
+// bits -- fp32 activations in all but name -- using B columns a single activation row leaves idle.
+// int8 weights become exact f16 integers with two byte permutes into the 0x64 exponent (1024 + u)
+// and one f16x2 subtract of 1152; f16 and bf16 weights feed the MMA as loaded. The MMA reduces
+// across the k of its tile, so no warp shuffles are needed and the instruction count per weight
+// byte is a fraction of the fp32 FMA form.
+//
+// A tile is 16 output rows (SwiGLU: 8 gate rows and their 8 up rows, so the epilogue pairs them in
+// one lane). Each row is read in 16-byte pieces (64 int8 or 32 16-bit k); four pieces make a chunk,
+// and quad lane t loads piece bytes [16 t, 16 t + 16) of rows lane / 4 and lane / 4 + 8, so every row
+// is streamed in 256-byte runs per quad -- the granularity at which the HBM keeps its pages busy (64-
+// byte runs per row measured at about half the bandwidth). Warp w of a CTA takes chunks w, w + 8, ...
+// The k order inside the MMA is a permutation of the real k, applied identically to A (weights) and B
+// (activations staged in that order), which the dot product does not see. Per-warp partial sums meet
+// in shared memory once per tile (double-buffered, one barrier) and one warp, rotating by tile, runs
+// the epilogue. Weights stream through a register ring across tiles as in the FMA kernel above.
+// ---------------------------------------------------------------------------------------------
+__device__ __forceinline__ void mma_16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                          uint32_t b0, uint32_t b1, bool bf16) {
+    if (bf16)
+        asm volatile(
+            "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+            "{%0,%1,%2,%3};"
+            : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+            : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+    else
+        asm volatile(
+            "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+            "{%0,%1,%2,%3};"
+            : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+            : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// Four signed bytes -> two f16x2 (bytes 0,1 and bytes 2,3), exact: u = b ^ 0x80 placed in the low
+// mantissa of 1024.0 (0x64uu) is 1024 + u, and subtracting 1152 leaves b.
+__device__ __forceinline__ void i8x4_to_h2x2(uint32_t w, uint32_t& lo, uint32_t& hi) {
+    const uint32_t u = w ^ 0x80808080u;
+    const uint32_t p0 = __byte_perm(u, 0x64646464u, 0x5140);
+    const uint32_t p1 = __byte_perm(u, 0x64646464u, 0x5342);
+    asm("sub.f16x2 %0, %1, %2;" : "=r"(lo) : "r"(p0), "r"(0x64806480u));
+    asm("sub.f16x2 %0, %1, %2;" : "=r"(hi) : "r"(p1), "r"(0x64806480u));
+}
+
+__device__ __forceinline__ uint32_t u4_get(const uint4& v, int i) {
+    return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w;
+}
+
+// Activation pair (hi, lo) of 8 consecutive values as two 16-byte rows of 16-bit words.
+template <bool BF16>
+__device__ __forceinline__ void split_hi_lo(const float (&v)[8], uint4& hi, uint4& lo) {
+    uint32_t h[4], l[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        if constexpr (BF16) {
+            const __nv_bfloat16 a = __float2bfloat16_rn(v[2 * i]), b = __float2bfloat16_rn(v[2 * i + 1]);
+            const __nv_bfloat16 c = __float2bfloat16_rn(v[2 * i] - __bfloat162float(a));
+            const __nv_bfloat16 d = __float2bfloat16_rn(v[2 * i + 1] - __bfloat162float(b));
+            h[i] = static_cast<uint32_t>(__bfloat16_as_ushort(a)) | (static_cast<uint32_t>(__bfloat16_as_ushort(b)) << 16);
+            l[i] = static_cast<uint32_t>(__bfloat16_as_ushort(c)) | (static_cast<uint32_t>(__bfloat16_as_ushort(d)) << 16);
+        } else {
+            const __half a = __float2half_rn(v[2 * i]), b = __float2half_rn(v[2 * i + 1]);
+            const __half c = __float2half_rn(v[2 * i] - __half2float(a));
+            const __half d = __float2half_rn(v[2 * i + 1] - __half2float(b));
+            h[i] = static_cast<uint32_t>(__half_as_ushort(a)) | (static_cast<uint32_t>(__half_as_ushort(b)) << 16);
+            l[i] = static_cast<uint32_t>(__half_as_ushort(c)) | (static_cast<uint32_t>(__half_as_ushort(d)) << 16);
+        }
+    }
+    hi = make_uint4(h[0], h[1], h[2], h[3]);
+    lo = make_uint4(l[0], l[1], l[2], l[3]);
+}
+
+// Weight pieces: int8 = 64 k (16 bytes per lane, 4 MMAs), 16-bit = 32 k (16 bytes per lane, 2 MMAs).
+template <typename WT>
+struct MmaPiece {
+    static constexpr int kK = sizeof(WT) == 1 ? 64 : 32;  // k per piece
+    static constexpr int kUnits = kK / 32;                // 32-k activation units per piece
+};
+constexpr int kMmaLoads = 4;  // pieces per chunk: 256 contiguous bytes of each row per quad
+constexpr int kMmaRing = 2;   // chunks in flight per warp
+
+// NG groups of 4 activation rows (8 B columns each). Shared memory holds the split activations in
+// 32-k units: unit u, column col, quad lane t at (u * 2M + col) * 64 + t * 16, eight 16-bit values.
+// For int8 unit u = 2p + j holds x[64 p + 16 t + 8 j, +8) (the 16 values lane t multiplies in piece p),
+// for 16-bit weights x[32 u + 8 t, +8). Lane (g, t) reads column g with conflict-free 16-byte loads;
+// columns past 2M are never read.
+template <typename WT, int NG>
+__global__ void __launch_bounds__(kThreads, 2) gemv_mma_kernel(const GemvParams p) {
+    extern __shared__ float4 smem_f4[];
+    char* xs = reinterpret_cast<char*>(smem_f4);
+    __shared__ float2 red[2][kWarps][NG][32];
+    __shared__ float rstd_s[4 * NG];
+    constexpr bool kI8 = sizeof(WT) == 1;
+    constexpr bool kBF = DT<WT>::id == L0B_BF16;
+    constexpr int PE = MmaPiece<WT>::kK;
+    // Activations are scaled by 2^-4 before the f16 split (range up to 2^20) and the sum by 2^4 after.
+    constexpr float kIn = kBF ? 1.0f : 0.0625f, kOut = kBF ? 1.0f : 16.0f;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+    const int N = p.N, K = p.K, M = p.M;
+    const int C2 = 2 * M;
+    const bool swiglu = p.epi == EPI_SWIGLU;
+    const int half_n = N >> 1;
+    const int units = swiglu ? half_n : N;
+    const int ntiles = (units + (swiglu ? 7 : 15)) / (swiglu ? 8 : 16);
+    const int npieces = K / PE;
+    const int nchunks = (npieces + kMmaLoads - 1) / kMmaLoads;
+    const int nq = warp < nchunks ? (nchunks - 1 - warp) / kWarps + 1 : 0;
+    const int nw = nchunks < kWarps ? nchunks : kWarps;  // warps holding partial sums
+    const int my_tiles = blockIdx.x < ntiles ? (ntiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+    const int total = my_tiles * nq;
+    const WT* W = static_cast<const WT*>(p.w);
+    const __half* scales = static_cast<const __half*>(p.scales);
+
+    auto tile_rows = [&](int tile, int& r0, int& r1, bool& v0, bool& v1) {
+        if (swiglu) {
+            r0 = tile * 8 + g;
+            r1 = r0 + half_n;
+            v0 = v1 = r0 < half_n;
+        } else {
+            r0 = tile * 16 + g;
+            r1 = r0 + 8;
+            v0 = r0 < N;
+            v1 = r1 < N;
+        }
+    };
+
+    if (p.prefetch && threadIdx.x == 0 && blockIdx.x < ntiles) {
+        const long long row_bytes = K * static_cast<long long>(sizeof(WT));
+        const int per = swiglu ? 8 : 16;
+        const long long u0 = static_cast<long long>(blockIdx.x) * per;
+        const long long u1 = min(u0 + per, static_cast<long long>(units));
+        for (int part = 0; part < (swiglu ? 2 : 1); ++part) {
+            const char* base = static_cast<const char*>(p.w) + (u0 + part * half_n) * row_bytes;
+            const long long bytes = (u1 - u0) * row_bytes;
+            for (long long off = 0; off < bytes; off += 32768)
+                prefetch_l2_bulk(base + off, static_cast<uint32_t>(min(32768LL, bytes - off)));
+        }
+    }
+
+    // Weight stream: steps (tile, chunk q of this warp) in order, kMmaRing steps ahead of the math.
+    // Chunk c covers pieces 4c .. 4c + 3; a piece past K (last chunk only) is neither loaded nor used.
+    uint4 ring[kMmaRing][2][kMmaLoads];
+    float sring[kMmaRing][2];
+    const WT* i_p[2];
+    const __half* i_s[2];
+    int i_step = 0, i_tile = blockIdx.x, i_q = 0;
+    auto set_issue_tile = [&](int tile) {
+        int r0, r1;
+        bool v0, v1;
+        tile_rows(tile, r0, r1, v0, v1);
+        const long long off = static_cast<long long>(warp) * (kMmaLoads * PE) + t * (PE / 4);
+        i_p[0] = v0 ? W + static_cast<long long>(r0) * K + off : nullptr;
+        i_p[1] = v1 ? W + static_cast<long long>(r1) * K + off : nullptr;
+        i_s[0] = (kI8 && v0) ? scales + r0 : nullptr;
+        i_s[1] = (kI8 && v1) ? scales + r1 : nullptr;
+    };
+    set_issue_tile(i_tile);
+    auto issue = [&](uint4 (&slot)[2][kMmaLoads], float (&ss)[2]) {
+        if (i_step < total) {
+            const int c = warp + kWarps * i_q;
+            const long long kk = static_cast<long long>(i_q) * (kWarps * kMmaLoads * PE);
+#pragma unroll
+            for (int l = 0; l < kMmaLoads; ++l) {
+                const bool in_k = kMmaLoads * c + l < npieces;
+#pragma unroll
+                for (int r = 0; r < 2; ++r)
+                    slot[r][l] = (i_p[r] && in_k) ? ld_stream_v4(i_p[r] + kk + l * PE) : make_uint4(0, 0, 0, 0);
+            }
+            if (kI8 && i_q == 0) {
+#pragma unroll
+                for (int r = 0; r < 2; ++r) ss[r] = i_s[r] ? __half2float(*i_s[r]) : 0.f;
+            }
+            if (++i_q == nq) {
+                i_q = 0;
+                i_tile += gridDim.x;
+                set_issue_tile(i_tile);
+            }
+        }
+        ++i_step;
+    };
+#pragma unroll
+    for (int d = 0; d < kMmaRing; ++d) issue(ring[d], sring[d]);
+
+    pdl_wait();
+    pdl_launch_dependents();
+
+    const bool xvec = p.x_dtype == L0B_F32 && (p.x_ld & 3) == 0 && (reinterpret_cast<uintptr_t>(p.x) & 15) == 0;
+    const float* xf = static_cast<const float*>(p.x);
+    if (p.norm_w) {
+        __shared__ float nred[32];
+        for (int m = 0; m < M; ++m) {
+            float ss = 0.f;
+            if (xvec) {
+                for (int k = threadIdx.x * 4; k < K; k += kThreads * 4) {
+                    const float4 v = *reinterpret_cast<const float4*>(xf + m * p.x_ld + k);
+                    ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+                }
+            } else {
+                for (int k = threadIdx.x; k < K; k += kThreads) {
+                    const float v = load_as_float(p.x, p.x_dtype, m * p.x_ld + k);
+                    ss += v * v;
+                }
+            }
+            ss = block_sum(ss, nred);
+            if (threadIdx.x == 0) rstd_s[m] = 1.0f / sqrtf(ss / static_cast<float>(K) + p.eps);
+        }
+        __syncthreads();
+    }
+    // Stage: item = (32-k unit u, row m, t) -> 8 consecutive k, stored as hi and lo columns.
+    {
+        const int items = (K / 32) * M * 4;
+#pragma unroll 2
+        for (int it = threadIdx.x; it < items; it += kThreads) {
+            const int u = it / (M * 4);
+            const int r = it - u * (M * 4);
+            const int m = r >> 2, tt = r & 3;
+            const int k = kI8 ? (u >> 1) * 64 + 16 * tt + 8 * (u & 1) : 32 * u + 8 * tt;
+            float v[8];
+            if (xvec) {
+                const float4 a = *reinterpret_cast<const float4*>(xf + m * p.x_ld + k);
+                const float4 b = *reinterpret_cast<const float4*>(xf + m * p.x_ld + k + 4);
+                v[0] = a.x, v[1] = a.y, v[2] = a.z, v[3] = a.w, v[4] = b.x, v[5] = b.y, v[6] = b.z, v[7] = b.w;
+            } else {
+#pragma unroll
+                for (int e = 0; e < 8; ++e) v[e] = load_as_float(p.x, p.x_dtype, m * p.x_ld + k + e);
+            }
+            if (p.norm_w) {
+                const float rs = rstd_s[m];
+#pragma unroll
+                for (int e = 0; e < 8; ++e) v[e] = (v[e] * rs) * p.norm_w[k + e];
+            }
+#pragma unroll
+            for (int e = 0; e < 8; ++e) v[e] *= kIn;
+            uint4 hi, lo;
+            split_hi_lo<kBF>(v, hi, lo);
+            char* base = xs + static_cast<size_t>(u) * C2 * 64 + tt * 16;
+            *reinterpret_cast<uint4*>(base + (2 * m) * 64) = hi;
+            *reinterpret_cast<uint4*>(base + (2 * m + 1) * 64) = lo;
+        }
+    }
+    __syncthreads();
+
+    // Epilogue of tile `tile` (iteration i) by one warp after the partials are in red[i & 1].
+    auto reduce_tile = [&](int i, int tile) {
+        int r0, r1;
+        bool v0, v1;
+        tile_rows(tile, r0, r1, v0, v1);
+#pragma unroll
+        for (int ng = 0; ng < NG; ++ng) {
+            float y0 = 0.f, y1 = 0.f;
+            for (int w = 0; w < nw; ++w) {
+                const float2 q = red[i & 1][w][ng][lane];
+                y0 += q.x;
+                y1 += q.y;
+            }
+            y0 *= kOut;
+            y1 *= kOut;
+            const int m = 4 * ng + t;
+            const bool live = m < M;
+            if (p.epi == EPI_ARGMAX) {
+                unsigned long long key = 0;
+                if (live && v0) key = argmax_key(epilogue_store(p, r0, m, y0, false), r0);
+                if (live && v1) key = max(key, argmax_key(epilogue_store(p, r1, m, y1, false), r1));
+#pragma unroll
+                for (int o = 4; o < 32; o <<= 1) key = max(key, __shfl_xor_sync(0xffffffffu, key, o));
+                if (live && g == 0 && key) atomicMax(p.argmax + m, key);
+            } else if (live) {
+                if (swiglu) {
+                    if (v0) epilogue_store(p, r0, m, silu(y0) * y1);
+                } else {
+                    if (v0) epilogue_store(p, r0, m, y0);
+                    if (v1) epilogue_store(p, r1, m, y1);
+                }
+            }
+        }
+    };
+    auto reducer = [&](int i) { return kWarps - 1 - (i & (kWarps - 1)); };
+
+    if (nq == 0) {  // no chunks for this warp (short K): barriers and epilogues only
+        for (int i = 0; i < my_tiles; ++i) {
+            __syncthreads();
+            if (warp == reducer(i)) reduce_tile(i, blockIdx.x + i * gridDim.x);
+        }
+        return;
+    }
+
+    float acc[NG][4];
+#pragma unroll
+    for (int ng = 0; ng < NG; ++ng) acc[ng][0] = acc[ng][1] = acc[ng][2] = acc[ng][3] = 0.f;
+    float rs2[2] = {1.f, 1.f};
+    int c_q = 0, c_i = 0;
+    const int col_off = g * 64 + t * 16;  // this lane's column g, quad slot t inside a unit
+    for (int s = 0; s < total; s += kMmaRing) {
+#pragma unroll
+        for (int d = 0; d < kMmaRing; ++d) {
+            if (s + d < total) {
+                const int c = warp + kWarps * c_q;
+#pragma unroll
+                for (int l = 0; l < kMmaLoads; ++l) {
+                    const int piece = kMmaLoads * c + l;
+                    if (piece < npieces) {
+                        // B fragments of this piece: MmaPiece::kUnits 16-byte loads per column group.
+                        uint32_t b[NG][8];
+#pragma unroll
+                        for (int ng = 0; ng < NG; ++ng) {
+                            const bool col_ok = 8 * ng + g < C2;
+#pragma unroll
+                            for (int j = 0; j < MmaPiece<WT>::kUnits; ++j) {
+                                uint4 q = make_uint4(0, 0, 0, 0);
+                                if (col_ok)
+                                    q = *reinterpret_cast<const uint4*>(
+                                        xs + static_cast<size_t>(piece * MmaPiece<WT>::kUnits + j) * C2 * 64 +
+                                        ng * 8 * 64 + col_off);
+                                b[ng][4 * j] = q.x, b[ng][4 * j + 1] = q.y, b[ng][4 * j + 2] = q.z, b[ng][4 * j + 3] = q.w;
+                            }
+                        }
+                        if constexpr (kI8) {
+#pragma unroll
+                            for (int jj = 0; jj < 4; ++jj) {
+                                uint32_t a0, a1, a2, a3;
+                                i8x4_to_h2x2(u4_get(ring[d][0][l], jj), a0, a2);
+                                i8x4_to_h2x2(u4_get(ring[d][1][l], jj), a1, a3);
+#pragma unroll
+                                for (int ng = 0; ng < NG; ++ng)
+                                    mma_16816(acc[ng], a0, a1, a2, a3, b[ng][2 * jj], b[ng][2 * jj + 1], false);
+                            }
+                        } else {
+#pragma unroll
+                            for (int jj = 0; jj < 2; ++jj) {
+                                const uint32_t a0 = u4_get(ring[d][0][l], 2 * jj), a2 = u4_get(ring[d][0][l], 2 * jj + 1);
+                                const uint32_t a1 = u4_get(ring[d][1][l], 2 * jj), a3 = u4_get(ring[d][1][l], 2 * jj + 1);
+#pragma unroll
+                                for (int ng = 0; ng < NG; ++ng)
+                                    mma_16816(acc[ng], a0, a1, a2, a3, b[ng][2 * jj], b[ng][2 * jj + 1], kBF);
+                            }
+                        }
+                    }
+                }
+                if (kI8 && c_q == 0) rs2[0] = sring[d][0], rs2[1] = sring[d][1];
+                issue(ring[d], sring[d]);
+                if (++c_q == nq) {
+#pragma unroll
+                    for (int ng = 0; ng < NG; ++ng) {
+                        red[c_i & 1][warp][ng][lane] =
+                            make_float2((acc[ng][0] + acc[ng][1]) * rs2[0], (acc[ng][2] + acc[ng][3]) * rs2[1]);
+                        acc[ng][0] = acc[ng][1] = acc[ng][2] = acc[ng][3] = 0.f;
+                    }
+                    __syncthreads();
+                    if (warp == reducer(c_i)) reduce_tile(c_i, blockIdx.x + c_i * gridDim.x);
+                    c_q = 0;
+                    ++c_i;
+                }
+            }
+        }
+    }
+}
+
+bool g_gemv_mma = true;
+
 template <typename F, typename... A>
 l0b_status launch_on(l0b_device* dev, cudaStream_t stream, F kernel, dim3 g, dim3 b, size_t smem, A... args) {
     if (dev) return dev->launch(kernel, g, b, smem, args...);
@@ -494,6 +860,35 @@ l0b_status launch_vec(l0b_device* dev, cudaStream_t stream, int sm_count, const 
     return launch_on(dev, stream, kernel, dim3(grid), dim3(kThreads), smem, p);
 }
 
+template <typename WT, int NG>
+l0b_status launch_mma(l0b_device* dev, cudaStream_t stream, int sm_count, const GemvParams& p) {
+    auto kernel = gemv_mma_kernel<WT, NG>;
+    const size_t smem = 4ull * p.M * p.K;  // hi and lo 16-bit copies of each activation row
+    static bool configured = false;
+    if (!configured) {
+        cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+        if (e != cudaSuccess) return fail(L0B_ERR_CUDA, "cudaFuncSetAttribute failed: %s", cudaGetErrorString(e));
+        configured = true;
+    }
+    const bool swiglu = p.epi == EPI_SWIGLU;
+    const int units = swiglu ? p.N / 2 : p.N;
+    const int ntiles = (units + (swiglu ? 7 : 15)) / (swiglu ? 8 : 16);
+    const int cap = sm_count * resident_ctas(reinterpret_cast<const void*>(kernel), smem);
+    return launch_on(dev, stream, kernel, dim3(ntiles < cap ? ntiles : cap), dim3(kThreads), smem, p);
+}
+
+// The tensor-core kernel takes 16-bit weights and per-row-scaled int8, K in whole pieces (64 / 32 k),
+// and up to 8 activation rows whose split copies fit in 200 KB of shared memory.
+template <typename WT>
+bool mma_applies(const GemvParams& p, int rows) {
+    if constexpr (sizeof(WT) > 2) {
+        return false;
+    } else {
+        return g_gemv_mma && p.K % MmaPiece<WT>::kK == 0 && reinterpret_cast<uintptr_t>(p.w) % 16 == 0 &&
+               (sizeof(WT) != 1 || p.group >= p.K) && rows <= 8 && 4ll * rows * p.K <= 200 * 1024;
+    }
+}
+
 template <typename WT>
 l0b_status launch_typed(l0b_device* dev, cudaStream_t stream, int sm_count, GemvParams p) {
     constexpr int VEC = 16 / sizeof(WT);
@@ -512,6 +907,13 @@ l0b_status launch_typed(l0b_device* dev, cudaStream_t stream, int sm_count, Gemv
             q.seg[s].out = static_cast<char*>(q.seg[s].out) + static_cast<size_t>(m0) * q.seg[s].ld * es;
         }
         if (q.argmax) q.argmax += m0;
+        if constexpr (sizeof(WT) <= 2) {
+            if (mma_applies<WT>(q, mr)) {
+                if (mr <= 4) L0B_TRY((launch_mma<WT, 1>(dev, stream, sm_count, q)));
+                else L0B_TRY((launch_mma<WT, 2>(dev, stream, sm_count, q)));
+                continue;
+            }
+        }
         if (!vec_ok) {
             const long long outs = (p.epi == EPI_SWIGLU ? p.N / 2 : p.N) * static_cast<long long>(mr);
             const int grid = static_cast<int>((outs + kWarps - 1) / kWarps);
@@ -607,6 +1009,8 @@ __global__ void __launch_bounds__(256) gemm_f32_kernel(int M, int N, int K, cons
 }
 
 }  // namespace
+
+void gemv_set_tensor_cores(bool on) { g_gemv_mma = on; }
 
 l0b_status gemv_nk_launch(l0b_device* dev, int w_dtype, GemvParams p) {
     return gemv_dispatch(dev, dev->stream, dev->sm_count, w_dtype, p);

@@ -43,6 +43,10 @@ struct GemvParams {
 // L0B_I8 / L0B_F16 / L0B_BF16 / L0B_F32. Rows of x are processed in groups of up to 8 per pass.
 l0b_status gemv_nk_launch(l0b_device* dev, int w_dtype, GemvParams p);
 
+// Process-wide choice between the tensor-core GEMV (default) and the fp32-FMA GEMV for the shapes
+// both take; launches already recorded into command lists keep the kernel they were recorded with.
+void gemv_set_tensor_cores(bool on);
+
 // Raw-stream variant (no device handle): immediate launch on `stream`.
 l0b_status gemv_nk_launch_stream(cudaStream_t stream, int sm_count, int w_dtype, GemvParams p);
 

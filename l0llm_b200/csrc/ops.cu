@@ -581,6 +581,11 @@ L0B_API l0b_status l0b_linear_tc(l0b_suite* s, l0b_device* d, int32_t m, int32_t
     return tc_gemm_launch(d, a);
 }
 
+L0B_API l0b_status l0b_set_gemv_tensor_cores(int32_t enable) {
+    gemv_set_tensor_cores(enable != 0);
+    return L0B_OK;
+}
+
 L0B_API l0b_status l0b_gemv_w8a16_raw(void* stream, int32_t m, int32_t n, int32_t k, const void* x, int32_t x_dtype,
                                       const int8_t* q, const uint16_t* scales, int32_t group, void* y,
                                       int32_t y_dtype) {

@@ -169,6 +169,7 @@ def load_library() -> C.CDLL:
         "l0b_linear_fused": (i32, [vp, vp, i32, i32, i32, vp, vp, vp, i32, vp, f32, i32, vp, vp]),
         "l0b_linear_tc": (i32, [vp, vp, i32, i32, i32, vp, vp, vp, f32, i32, vp, vp]),
         "l0b_device_error_status": (i32, [vp, C.POINTER(i32)]),
+        "l0b_set_gemv_tensor_cores": (i32, [i32]),
         "l0b_attention_decode_noalloc": (i32, [vp, vp, vp, vp, i32, vp, i32, i32, i32, i32, i32]),
         "l0b_model_config_init": (i32, [C.POINTER(ModelConfig)]),
         "l0b_rope_frequencies": (i32, [C.POINTER(ModelConfig), vp, i32, C.POINTER(i32), C.POINTER(f32)]),

@@ -1,0 +1,122 @@
+"""Both decode GEMV kernels (tensor-core mma.sync streaming and fp32-FMA streaming) against the oracle.
+
+The tensor-core kernel splits each activation into two f16 halves (hi + residual), so its result must
+stay within fp32-accumulation distance of the fp64 oracle, far tighter than a plain f16 activation
+would allow. Shapes cover a single piece of K (K = 64, most warps idle), K not a multiple of the
+eight-warp stride (896), the long down-projection row (18944), row counts that leave partial 16-row
+tiles, and 1..8 activation rows (one or two B-column groups).
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(params=["mma", "fma"])
+def path(request, lz):
+    lib = lz.load_library()
+    lib.l0b_set_gemv_tensor_cores(1 if request.param == "mma" else 0)
+    yield request.param
+    lib.l0b_set_gemv_tensor_cores(1)
+
+
+def _weights(lz, orc, wkind, hf, k):
+    import torch
+
+    if wkind == "f16":
+        w = hf.astype(np.float16)
+        return w, w.view(np.uint16), orc.F16, lz.F16, None, 0
+    if wkind == "bf16":
+        w = torch.from_numpy(hf).to(torch.bfloat16).view(torch.int16).numpy().view(np.uint16)
+        return w, w, orc.BF16, lz.BF16, None, 0
+    q, s = lz.q8_quantize_out_in(hf, k)
+    return q, q, orc.I8, lz.I8, s, k
+
+
+@pytest.mark.parametrize("wkind", ["f16", "bf16", "i8c"])
+@pytest.mark.parametrize("n,k", [(40, 64), (1000, 896), (4608, 3584), (3584, 18944), (17, 128)])
+@pytest.mark.parametrize("m", [1, 2, 5, 8])
+def test_gemv_paths_store(lz, orc, device, suite, path, wkind, n, k, m):
+    if k == 18944 and m > 2:
+        pytest.skip("shape beyond the tensor-core kernel's shared-memory budget")
+    rng = np.random.default_rng(n + 3 * k + m)
+    hf = ((rng.random((n, k)) * 2 - 1) * 0.05).astype(np.float32)
+    x = (rng.standard_normal((m, k)) * 2).astype(np.float32)
+    bias = (rng.standard_normal(n) * 0.1).astype(np.float32)
+    w_dev, w_orc, wdt, dt, scales, group = _weights(lz, orc, wkind, hf, k)
+    want = orc.gemv_out_in(x, w_orc, wdt, None if scales is None else scales.view(np.uint16), group) + bias
+    with lz.SharedBuffer.from_array(device, w_dev, dt) as W, lz.SharedBuffer.from_array(device, x) as xb, \
+            lz.SharedBuffer.from_array(device, bias) as bb, lz.SharedBuffer(device, lz.F32, m * n) as y:
+        sb = lz.SharedBuffer.from_array(device, scales) if scales is not None else None
+        suite.linear(device, m, n, k, xb, W, sb, group, bb, y)
+        got = y.ToArray().reshape(m, n)
+        if sb is not None:
+            sb.Dispose()
+    # bf16 activations split in two keep ~16 bits; f16 pairs keep ~22.
+    tol = 2e-4 if wkind == "bf16" else 2e-5
+    scale = np.abs(want).max()
+    err = np.abs(got - want).max()
+    assert err <= tol * scale, f"{path}: max err {err} vs scale {scale}"
+
+
+@pytest.mark.parametrize("wkind", ["f16", "i8c"])
+@pytest.mark.parametrize("inter", [4864, 100])
+@pytest.mark.parametrize("m", [1, 3, 8])
+def test_gemv_paths_norm_swiglu(lz, orc, device, suite, path, wkind, inter, m):
+    rng = np.random.default_rng(inter + m)
+    H = 896
+    x = (rng.standard_normal((m, H)) * 3).astype(np.float32)
+    nw = (1 + 0.1 * rng.standard_normal(H)).astype(np.float32)
+    hf = ((rng.random((2 * inter, H)) * 2 - 1) * 0.05).astype(np.float32)
+    _, normed = orc.rmsnorm(x, nw, 1e-6)
+    w_dev, w_orc, wdt, dt, scales, group = _weights(lz, orc, wkind, hf, H)
+    y = orc.gemv_out_in(normed, w_orc, wdt, None if scales is None else scales.view(np.uint16), group)
+    g, u = y[:, :inter], y[:, inter:]
+    want = g / (1 + np.exp(-g.astype(np.float64))) * u
+    with lz.SharedBuffer.from_array(device, x) as xb, lz.SharedBuffer.from_array(device, w_dev, dt) as W, \
+            lz.SharedBuffer.from_array(device, nw) as nb, lz.SharedBuffer(device, lz.F32, m * inter) as ob:
+        sb = lz.SharedBuffer.from_array(device, scales) if scales is not None else None
+        suite.linear_fused(device, m, 2 * inter, H, xb, W, sb, group, nb, 1e-6, suite.EPI_SWIGLU, None, ob)
+        got = ob.ToArray().reshape(m, inter)
+        if sb is not None:
+            sb.Dispose()
+    err = np.abs(got - want)
+    assert np.all(err <= 1e-4 + 1e-4 * np.abs(want)), f"{path}: max err {err.max()}"
+
+
+@pytest.mark.parametrize("m", [1, 2])
+def test_gemv_paths_accumulate_down_projection(lz, orc, device, suite, path, m):
+    rng = np.random.default_rng(90 + m)
+    H, I = 3584, 18944
+    hidden = rng.standard_normal((m, H)).astype(np.float32)
+    x = rng.standard_normal((m, I)).astype(np.float32)
+    hf = ((rng.random((H, I)) * 2 - 1) * 0.02).astype(np.float32)
+    q, s = lz.q8_quantize_out_in(hf, I)
+    want = hidden + orc.gemv_out_in(x, q, orc.I8, s.view(np.uint16), I)
+    with lz.SharedBuffer.from_array(device, hidden) as hb, lz.SharedBuffer.from_array(device, x) as xb, \
+            lz.SharedBuffer.from_array(device, q) as W, lz.SharedBuffer.from_array(device, s) as S:
+        suite.linear_fused(device, m, H, I, xb, W, S, I, None, 0.0, suite.EPI_ACCUM, None, hb)
+        got = hb.ToArray().reshape(m, H)
+    err = np.abs(got - want)
+    assert np.all(err <= 2e-4 + 1e-5 * np.abs(want)), f"{path}: max err {err.max()}"
+
+
+def test_gemv_paths_one_hot_reads_weights_exactly(lz, device, suite, path):
+    """x = e_c reads column c of the dequantised weights back bit-exactly on both kernels."""
+    rng = np.random.default_rng(5)
+    n, k = 272, 1024
+    hf = ((rng.random((n, k)) * 2 - 1) * 0.3).astype(np.float32)
+    q, s = lz.q8_quantize_out_in(hf, k)
+    cols = [0, 15, 16, 63, 64, 511, 512, 1023]
+    x = np.zeros((len(cols), k), np.float32)
+    for r, c in enumerate(cols):
+        x[r, c] = 1.0
+    with lz.SharedBuffer.from_array(device, q) as W, lz.SharedBuffer.from_array(device, s) as S, \
+            lz.SharedBuffer.from_array(device, x) as xb, lz.SharedBuffer(device, lz.F32, len(cols) * n) as y:
+        suite.linear(device, len(cols), n, k, xb, W, S, k, None, y)
+        got = y.ToArray().reshape(len(cols), n)
+    sf = s.astype(np.float32)
+    for r, c in enumerate(cols):
+        np.testing.assert_array_equal(got[r], q[:, c].astype(np.float32) * sf[:, 0])
