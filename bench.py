@@ -214,7 +214,7 @@ def dominant_kernel_roofline(lz, dev, suite, stream_ptr, torch, peak: float, pea
         traffic = json.loads(tf.read_text()).get("dram_bytes_per_launch")
     for b in qs + ss + [x, nw, out]:
         b.Dispose()
-    return {"kernel": "gemv_nk_kernel<int8> (RMSNorm prologue + [gate;up] 37888x3584 + SwiGLU epilogue)",
+    return {"kernel": "gemv_mma_kernel<int8> (RMSNorm prologue + [gate;up] 37888x3584 mma.sync + SwiGLU epilogue)",
             "bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
             "frac": round(achieved / peak, 4), "traffic": traffic, "algorithmic_bytes": bytes_per_launch,
             "avg_us": round(avg_ms * 1e3, 2)}

@@ -13,6 +13,8 @@
 // new key/value row into the cache, replacing the separate RoPE and KvCacheStore launches.
 #include <cmath>
 
+#include <cooperative_groups.h>
+
 #include "common.cuh"
 #include "ops.cuh"
 
@@ -235,6 +237,232 @@ __global__ void __launch_bounds__(128) attn_kernel(const AttnParams p) {
     if (tid == 0) *counter = 0u;
 }
 
+// ---------------------------------------------------------------------------------------------
+// Decode attention in thread-block clusters (no global partials, no counters).
+//
+// The S splits of one (query row, KV head group) form one cluster of (1, S, 1) CTAs, S <= 8. Each
+// CTA walks its share of the positions -- chunk = max(p.chunk, 32 * ceil(seq / (32 S))) computed from
+// the live sequence length, so short contexts leave the tail CTAs idle instead of launching more --
+// with the next 32-position K/V tile loaded into registers while the current one is scored. Its
+// (running max, running sum, unnormalised output) stay in its shared memory; after one cluster
+// barrier CTA r merges head dimensions [r HD / S, (r + 1) HD / S) of every head by reading the S
+// partials straight from the peers' shared memory (distributed shared memory over the cluster), and
+// a second barrier keeps every CTA's shared memory alive until its peers have read it.
+// ---------------------------------------------------------------------------------------------
+template <int HD>
+__global__ void __launch_bounds__(128) attn_cluster_kernel(const AttnParams p) {
+    namespace cg = cooperative_groups;
+    constexpr int HPT = 128 / HD;
+    constexpr int JPT = kMaxG / HPT;
+    constexpr int TPR = HD / 8;              // threads per cached row, 8 dims each
+    constexpr int ITEMS = kT * TPR / 128;    // row pieces per thread per tile
+    __shared__ float qs[kMaxG][HD];
+    __shared__ float ks[kT][HD + 1];
+    __shared__ __align__(16) float vs[kT][HD];
+    __shared__ float ps[kMaxG][kT];
+    __shared__ float m_s[kMaxG], l_s[kMaxG], corr_s[kMaxG];
+    __shared__ float knew[HD], vnew[HD];
+    __shared__ float cs_s[HD / 2], sn_s[HD / 2];
+    __shared__ float acc_s[kMaxG][HD];
+
+    cg::cluster_group cluster = cg::this_cluster();
+    const int G = p.nh / p.nkv;
+    const int gparts = (G + kMaxG - 1) / kMaxG;
+    const int kvh = blockIdx.x / gparts, gp = blockIdx.x - (blockIdx.x / gparts) * gparts;
+    const int h0 = kvh * G + gp * kMaxG;
+    const int ng = min(kMaxG, G - gp * kMaxG);
+    const int S = gridDim.y, split = blockIdx.y, b = blockIdx.z;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+
+    pdl_wait();
+    const int qpos = p.positions ? p.positions[b] : p.pos_base + b * p.pos_step;
+    const int seq = qpos + 1;
+    int chunk = ((seq + S - 1) / S + kT - 1) / kT * kT;
+    chunk = max(chunk, p.chunk);
+    const int nact = (seq + chunk - 1) / chunk;
+    const bool active = split < nact;
+    pdl_launch_dependents();
+    const int p_begin = split * chunk;
+    const int p_end = min(seq, p_begin + chunk);
+    const bool owns_new = p.store_new && split == nact - 1;
+    const long long cache_base = b * p.cache_bstride + static_cast<long long>(kvh) * HD;
+    const bool f32c = p.cache_dtype == L0B_F32;
+
+    // Raw 16-byte pieces of the K and V rows of one tile (two per piece for an fp32 cache).
+    uint4 kr[ITEMS][2], vr[ITEMS][2];
+    auto load_tile = [&](int t0) {
+#pragma unroll
+        for (int it = 0; it < ITEMS; ++it) {
+            const int idx = tid + it * 128;
+            const int t = idx / TPR, d0 = (idx - t * TPR) * 8;
+            const int pos = t0 + t;
+            kr[it][0] = kr[it][1] = vr[it][0] = vr[it][1] = make_uint4(0, 0, 0, 0);
+            if (pos < p_end && !(owns_new && pos == qpos)) {
+                const long long off = cache_base + static_cast<long long>(pos) * p.kv_dim + d0;
+                if (f32c) {
+                    const uint4* k4 = reinterpret_cast<const uint4*>(static_cast<const float*>(p.kc) + off);
+                    const uint4* v4 = reinterpret_cast<const uint4*>(static_cast<const float*>(p.vc) + off);
+                    kr[it][0] = k4[0], kr[it][1] = k4[1], vr[it][0] = v4[0], vr[it][1] = v4[1];
+                } else {
+                    kr[it][0] = *reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(p.kc) + off);
+                    vr[it][0] = *reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(p.vc) + off);
+                }
+            }
+        }
+    };
+    auto unpack = [&](const uint4 (&r)[2], float (&o)[8]) {
+        if (f32c) {
+            o[0] = __uint_as_float(r[0].x), o[1] = __uint_as_float(r[0].y), o[2] = __uint_as_float(r[0].z);
+            o[3] = __uint_as_float(r[0].w), o[4] = __uint_as_float(r[1].x), o[5] = __uint_as_float(r[1].y);
+            o[6] = __uint_as_float(r[1].z), o[7] = __uint_as_float(r[1].w);
+            return;
+        }
+        const uint32_t w[4] = {r[0].x, r[0].y, r[0].z, r[0].w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float2 f = p.cache_dtype == L0B_F16 ? half2_bits_to_float2(w[i]) : bf162_bits_to_float2(w[i]);
+            o[2 * i] = f.x;
+            o[2 * i + 1] = f.y;
+        }
+    };
+    if (active) load_tile(p_begin);
+
+    if (p.rope) {
+        for (int i = tid; i < p.rot / 2; i += 128) {
+            const float ang = __fmul_rn(static_cast<float>(qpos), p.inv_freq[i]);
+            float s, c;
+            sincosf(ang, &s, &c);
+            cs_s[i] = __fmul_rn(c, p.attn_scale);
+            sn_s[i] = __fmul_rn(s, p.attn_scale);
+        }
+        __syncthreads();
+    }
+    const float* qb = p.q + b * p.q_bstride + static_cast<long long>(h0) * HD;
+    for (int idx = tid; idx < kMaxG * HD; idx += 128) {
+        const int j = idx / HD, d = idx - (idx / HD) * HD;
+        float v = 0.f;
+        if (j < ng) v = p.rope ? rope_elem(qb + j * HD, d, p.rot, cs_s, sn_s) : qb[j * HD + d];
+        qs[j][d] = v;
+    }
+    if (tid < kMaxG) {
+        m_s[tid] = kNegInf;
+        l_s[tid] = 0.f;
+    }
+    if (owns_new) {
+        const float* kb = p.k_new + b * p.new_bstride + static_cast<long long>(kvh) * HD;
+        const float* vb = p.v_new + b * p.new_bstride + static_cast<long long>(kvh) * HD;
+        for (int d = tid; d < HD; d += 128) {
+            const float kv = p.rope ? rope_elem(kb, d, p.rot, cs_s, sn_s) : kb[d];
+            knew[d] = kv;
+            vnew[d] = vb[d];
+            if (gp == 0) {
+                const long long off = b * p.cache_bstride + static_cast<long long>(qpos) * p.kv_dim +
+                                      static_cast<long long>(kvh) * HD + d;
+                store_from_float(p.kc, p.cache_dtype, off, kv);
+                store_from_float(p.vc, p.cache_dtype, off, vb[d]);
+            }
+        }
+    }
+    __syncthreads();
+
+    float acc[JPT];
+#pragma unroll
+    for (int i = 0; i < JPT; ++i) acc[i] = 0.f;
+    const int dim = tid % HD, jb = tid / HD;
+    for (int t0 = p_begin; active && t0 < p_end; t0 += kT) {
+#pragma unroll
+        for (int it = 0; it < ITEMS; ++it) {
+            const int idx = tid + it * 128;
+            const int t = idx / TPR, d0 = (idx - t * TPR) * 8;
+            const int pos = t0 + t;
+            float kv[8], vv[8];
+            if (owns_new && pos == qpos) {
+#pragma unroll
+                for (int e = 0; e < 8; ++e) kv[e] = knew[d0 + e], vv[e] = vnew[d0 + e];
+            } else {
+                unpack(kr[it], kv);
+                unpack(vr[it], vv);
+            }
+#pragma unroll
+            for (int e = 0; e < 8; ++e) ks[t][d0 + e] = kv[e];
+            *reinterpret_cast<float4*>(&vs[t][d0]) = make_float4(vv[0], vv[1], vv[2], vv[3]);
+            *reinterpret_cast<float4*>(&vs[t][d0 + 4]) = make_float4(vv[4], vv[5], vv[6], vv[7]);
+        }
+        __syncthreads();
+        if (t0 + kT < p_end) load_tile(t0 + kT);  // next tile in flight during the math
+        for (int j = warp; j < ng; j += 4) {
+            float s = kNegInf;
+            if (t0 + lane < p_end) {
+                float a = 0.f;
+#pragma unroll 16
+                for (int d = 0; d < HD; ++d) a = fmaf(qs[j][d], ks[lane][d], a);
+                s = a * p.scale;
+            }
+            const float mx = warp_max(s);
+            const float m_old = m_s[j];
+            const float m_new = fmaxf(m_old, mx);
+            const float pj = s == kNegInf ? 0.f : expf(s - m_new);
+            const float sum = warp_sum(pj);
+            ps[j][lane] = pj;
+            __syncwarp();
+            if (lane == 0) {
+                const float corr = expf(m_old - m_new);
+                corr_s[j] = corr;
+                l_s[j] = l_s[j] * corr + sum;
+                m_s[j] = m_new;
+            }
+        }
+        __syncthreads();
+#pragma unroll
+        for (int i = 0; i < JPT; ++i) {
+            const int j = jb + i * HPT;
+            if (j < ng) {
+                float a = acc[i] * corr_s[j];
+#pragma unroll 8
+                for (int t = 0; t < kT; ++t) a = fmaf(ps[j][t], vs[t][dim], a);
+                acc[i] = a;
+            }
+        }
+        __syncthreads();
+    }
+#pragma unroll
+    for (int i = 0; i < JPT; ++i) acc_s[jb + i * HPT][dim] = acc[i];
+
+    // A single split needs no cluster: its own shared memory and a block barrier.
+    auto peer = [&](float* ptr, int s) { return S > 1 ? cluster.map_shared_rank(ptr, s) : ptr; };
+    if (S > 1) cluster.sync();
+    else __syncthreads();
+    // Merge this CTA's slice of head dimensions from the nact active partials of the cluster.
+    const int dper = HD / S;
+    for (int o = tid; o < ng * dper; o += 128) {
+        const int j = o / dper, d = split * dper + (o - (o / dper) * dper);
+        float mv[8], lv[8], av[8];
+        float mmax = kNegInf;
+#pragma unroll
+        for (int s = 0; s < 8; ++s) {
+            mv[s] = kNegInf, lv[s] = 0.f, av[s] = 0.f;
+            if (s < nact) {
+                mv[s] = *peer(&m_s[j], s);
+                lv[s] = *peer(&l_s[j], s);
+                av[s] = *peer(&acc_s[j][d], s);
+            }
+        }
+#pragma unroll
+        for (int s = 0; s < 8; ++s) mmax = fmaxf(mmax, mv[s]);
+        float lsum = 0.f, y = 0.f;
+#pragma unroll
+        for (int s = 0; s < 8; ++s) {
+            if (s < nact) {
+                const float w = expf(mv[s] - mmax);
+                lsum = fmaf(w, lv[s], lsum);
+                y = fmaf(w, av[s], y);
+            }
+        }
+        p.out[b * p.out_bstride + static_cast<long long>(h0 + j) * HD + d] = y / lsum;
+    }
+    if (S > 1) cluster.sync();
+}
+
 template <typename F>
 l0b_status launch_attn(l0b_device* d, cudaStream_t stream, F kernel, dim3 grid, const AttnParams& p) {
     if (d) return d->launch(kernel, grid, dim3(128), 0, p);
@@ -259,6 +487,43 @@ l0b_status attention_any(l0b_device* d, cudaStream_t stream, const AttnParams& p
     }
 }
 
+template <typename F>
+l0b_status launch_attn_cluster(l0b_device* d, cudaStream_t stream, F kernel, dim3 grid, int S, const AttnParams& p) {
+    if (d) return d->launch_cluster(kernel, grid, dim3(128), 0, S, p);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(128);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    if (S > 1) {
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = 1;
+        attr[0].val.clusterDim.y = S;
+        attr[0].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+    }
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, p);
+    if (e != cudaSuccess) return fail(L0B_ERR_CUDA, "attention launch failed: %s", cudaGetErrorString(e));
+    add_launches(1);
+    return L0B_OK;
+}
+
+l0b_status attention_cluster_any(l0b_device* d, cudaStream_t stream, const AttnParams& p, int batch, int splits) {
+    L0B_REQUIRE(p.nkv > 0 && p.nh % p.nkv == 0, L0B_ERR_ARGUMENT, "heads %d not a multiple of kv heads %d", p.nh,
+                p.nkv);
+    L0B_REQUIRE(splits == 1 || splits == 2 || splits == 4 || splits == 8, L0B_ERR_ARGUMENT,
+                "cluster splits %d (1, 2, 4 or 8)", splits);
+    const int G = p.nh / p.nkv;
+    const int gparts = (G + kMaxG - 1) / kMaxG;
+    dim3 grid(p.nkv * gparts, splits, batch);
+    switch (p.hd) {
+        case 64: return launch_attn_cluster(d, stream, attn_cluster_kernel<64>, grid, splits, p);
+        case 128: return launch_attn_cluster(d, stream, attn_cluster_kernel<128>, grid, splits, p);
+        default: return fail(L0B_ERR_UNSUPPORTED, "attention head_dim %d is not supported (64, 128)", p.hd);
+    }
+}
+
 }  // namespace
 
 l0b_status attention_launch(l0b_device* d, const AttnParams& p, int batch) {
@@ -267,6 +532,18 @@ l0b_status attention_launch(l0b_device* d, const AttnParams& p, int batch) {
 
 l0b_status attention_launch_stream(cudaStream_t stream, const AttnParams& p, int batch) {
     return attention_any(nullptr, stream, p, batch);
+}
+
+l0b_status attention_cluster_launch(l0b_device* d, const AttnParams& p, int batch, int splits) {
+    return attention_cluster_any(d, d->stream, p, batch, splits);
+}
+
+int attention_cluster_splits(int max_seq, int work_items, int sm_count) {
+    // Enough CTAs for about two per SM, and no split that the longest sequence cannot reach; at most
+    // the portable cluster size of 8.
+    int s = 8;
+    while (s > 1 && (static_cast<long long>(work_items) * s > 2LL * sm_count || 32LL * (s / 2) >= max_seq)) s >>= 1;
+    return s;
 }
 
 size_t attention_part_floats(int batch, int nh, int max_splits, int hd) {

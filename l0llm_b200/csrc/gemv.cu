@@ -464,7 +464,8 @@ __global__ void __launch_bounds__(kThreads) gemv_nk_scalar_kernel(const GemvPara
 // one lane). Each row is read in 16-byte pieces (64 int8 or 32 16-bit k); four pieces make a chunk,
 // and quad lane t loads piece bytes [16 t, 16 t + 16) of rows lane / 4 and lane / 4 + 8, so every row
 // is streamed in 256-byte runs per quad -- the granularity at which the HBM keeps its pages busy (64-
-// byte runs per row measured at about half the bandwidth). Warp w of a CTA takes chunks w, w + 8, ...
+// byte runs per row measured at about half the bandwidth). Warp w of a CTA takes the w-th eighth of
+// each row's pieces, so the warps of a CTA finish a tile together at its barrier.
 // The k order inside the MMA is a permutation of the real k, applied identically to A (weights) and B
 // (activations staged in that order), which the dot product does not see. Per-warp partial sums meet
 // in shared memory once per tile (double-buffered, one barrier) and one warp, rotating by tile, runs
@@ -556,10 +557,10 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_mma_kernel(const GemvParams 
     const int half_n = N >> 1;
     const int units = swiglu ? half_n : N;
     const int ntiles = (units + (swiglu ? 7 : 15)) / (swiglu ? 8 : 16);
+    // Warp w owns the contiguous pieces [p0, p1) of every tile (counts differ by at most one).
     const int npieces = K / PE;
-    const int nchunks = (npieces + kMmaLoads - 1) / kMmaLoads;
-    const int nq = warp < nchunks ? (nchunks - 1 - warp) / kWarps + 1 : 0;
-    const int nw = nchunks < kWarps ? nchunks : kWarps;  // warps holding partial sums
+    const int p0 = warp * npieces / kWarps, p1 = (warp + 1) * npieces / kWarps;
+    const int nq = (p1 - p0 + kMmaLoads - 1) / kMmaLoads;  // chunks of this warp per tile
     const int my_tiles = blockIdx.x < ntiles ? (ntiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
     const int total = my_tiles * nq;
     const WT* W = static_cast<const WT*>(p.w);
@@ -592,7 +593,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_mma_kernel(const GemvParams 
     }
 
     // Weight stream: steps (tile, chunk q of this warp) in order, kMmaRing steps ahead of the math.
-    // Chunk c covers pieces 4c .. 4c + 3; a piece past K (last chunk only) is neither loaded nor used.
+    // Chunk q covers pieces p0 + 4q .. p0 + 4q + 3; a piece at or past p1 is neither loaded nor used.
     uint4 ring[kMmaRing][2][kMmaLoads];
     float sring[kMmaRing][2];
     const WT* i_p[2];
@@ -602,7 +603,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_mma_kernel(const GemvParams 
         int r0, r1;
         bool v0, v1;
         tile_rows(tile, r0, r1, v0, v1);
-        const long long off = static_cast<long long>(warp) * (kMmaLoads * PE) + t * (PE / 4);
+        const long long off = static_cast<long long>(p0) * PE + t * (PE / 4);
         i_p[0] = v0 ? W + static_cast<long long>(r0) * K + off : nullptr;
         i_p[1] = v1 ? W + static_cast<long long>(r1) * K + off : nullptr;
         i_s[0] = (kI8 && v0) ? scales + r0 : nullptr;
@@ -611,11 +612,10 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_mma_kernel(const GemvParams 
     set_issue_tile(i_tile);
     auto issue = [&](uint4 (&slot)[2][kMmaLoads], float (&ss)[2]) {
         if (i_step < total) {
-            const int c = warp + kWarps * i_q;
-            const long long kk = static_cast<long long>(i_q) * (kWarps * kMmaLoads * PE);
+            const long long kk = static_cast<long long>(i_q) * (kMmaLoads * PE);
 #pragma unroll
             for (int l = 0; l < kMmaLoads; ++l) {
-                const bool in_k = kMmaLoads * c + l < npieces;
+                const bool in_k = p0 + kMmaLoads * i_q + l < p1;
 #pragma unroll
                 for (int r = 0; r < 2; ++r)
                     slot[r][l] = (i_p[r] && in_k) ? ld_stream_v4(i_p[r] + kk + l * PE) : make_uint4(0, 0, 0, 0);
@@ -702,7 +702,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_mma_kernel(const GemvParams 
 #pragma unroll
         for (int ng = 0; ng < NG; ++ng) {
             float y0 = 0.f, y1 = 0.f;
-            for (int w = 0; w < nw; ++w) {
+            for (int w = 0; w < kWarps; ++w) {
                 const float2 q = red[i & 1][w][ng][lane];
                 y0 += q.x;
                 y1 += q.y;
@@ -730,8 +730,10 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_mma_kernel(const GemvParams 
     };
     auto reducer = [&](int i) { return kWarps - 1 - (i & (kWarps - 1)); };
 
-    if (nq == 0) {  // no chunks for this warp (short K): barriers and epilogues only
+    if (nq == 0) {  // no pieces for this warp (K < 8 pieces): zero partials, barriers, epilogues
         for (int i = 0; i < my_tiles; ++i) {
+#pragma unroll
+            for (int ng = 0; ng < NG; ++ng) red[i & 1][warp][ng][lane] = make_float2(0.f, 0.f);
             __syncthreads();
             if (warp == reducer(i)) reduce_tile(i, blockIdx.x + i * gridDim.x);
         }
@@ -748,11 +750,10 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_mma_kernel(const GemvParams 
 #pragma unroll
         for (int d = 0; d < kMmaRing; ++d) {
             if (s + d < total) {
-                const int c = warp + kWarps * c_q;
 #pragma unroll
                 for (int l = 0; l < kMmaLoads; ++l) {
-                    const int piece = kMmaLoads * c + l;
-                    if (piece < npieces) {
+                    const int piece = p0 + kMmaLoads * c_q + l;
+                    if (piece < p1) {
                         // B fragments of this piece: MmaPiece::kUnits 16-byte loads per column group.
                         uint32_t b[NG][8];
 #pragma unroll

@@ -62,11 +62,7 @@ struct l0b_model {
     int* out_tokens = nullptr;  // [max_seq * batch_cap]
     int* step_idx = nullptr;
     unsigned long long* keys = nullptr;  // [batch_cap]
-    // Split-KV attention scratch.
-    float* part = nullptr;
-    float* part_ml = nullptr;
-    unsigned* counters = nullptr;
-    int chunk = 64, max_splits = 1;
+    int cluster_splits = 1;  // CTAs per cluster of the decode attention (splits merged on chip)
     // Host state.
     int* host_io = nullptr;       // pinned [2 * batch_cap]
     float* host_logits = nullptr; // pinned [batch_cap * vocab]
@@ -342,12 +338,8 @@ l0b_status record_layer_fused(l0b_model* m, int li, int rows, bool decode, int p
         a.new_bstride = m->qkv_w;
         a.cache_bstride = static_cast<long long>(m->max_seq) * m->kvdim;
         a.positions = m->pos;
-        a.part = m->part;
-        a.part_ml = m->part_ml;
-        a.counters = m->counters;
-        a.chunk = m->chunk;
-        a.max_splits = m->max_splits;
-        L0B_TRY(attention_launch(m->dev, a, rows));
+        a.chunk = 32;
+        L0B_TRY(attention_cluster_launch(m->dev, a, rows, m->cluster_splits));
     } else {
         // Prefill: rotate and store the whole chunk first (queries attend to each other's keys).
         L0B_TRY(k_rope(m->dev, m->qkv, m->qkv + m->qdim, m->prompt_pos, m->inv_freq, m->hd, m->nh, m->nkv,
@@ -425,16 +417,13 @@ l0b_status record_layer_reference(l0b_model* m, int li, int rows, bool decode, i
     a.pos_base = pos0;
     a.pos_step = 1;
     if (decode) {
-        a.chunk = m->chunk;
-        a.max_splits = m->max_splits;
-        a.part = m->part;
-        a.part_ml = m->part_ml;
-        a.counters = m->counters;
+        a.chunk = 32;
+        L0B_TRY(attention_cluster_launch(d, a, rows, m->cluster_splits));
     } else {
         a.chunk = (pos0 + rows + 31) / 32 * 32;
         a.max_splits = 1;
+        L0B_TRY(attention_launch(d, a, rows));
     }
-    L0B_TRY(attention_launch(d, a, rows));
     p = linear_params(L.o, rows, m->attn, m->qdim);
     p.seg[0] = {m->attn_proj, nullptr, m->h, m->h};
     L0B_TRY(gemv(m, L.o, p));
@@ -882,11 +871,8 @@ L0B_API l0b_status l0b_model_create(l0b_device* dev, l0b_suite* suite, const l0b
     L0B_TRY(m->alloc(&m->out_tokens, static_cast<size_t>(max_seq_len + 1) * m->batch_cap));
     L0B_TRY(m->alloc(&m->step_idx, 1));
     L0B_TRY(m->alloc(&m->keys, m->batch_cap));
-    attention_pick_split(max_seq_len, m->batch_cap * m->nkv, dev->sm_count, &m->chunk, &m->max_splits);
-    const size_t part_rows = static_cast<size_t>(m->batch_cap) * m->nh * m->max_splits;
-    L0B_TRY(m->alloc(&m->part, part_rows * m->hd));
-    L0B_TRY(m->alloc(&m->part_ml, part_rows * 2));
-    L0B_TRY(m->alloc(&m->counters, static_cast<size_t>(m->batch_cap) * m->nh));
+    m->cluster_splits = attention_cluster_splits(
+        max_seq_len, m->batch_cap * m->nkv * ((m->nh / m->nkv + 7) / 8), dev->sm_count);
     L0B_CHECK_CUDA(cudaMallocHost(&m->host_io, sizeof(int) * 2 * m->batch_cap));
     L0B_CHECK_CUDA(cudaMallocHost(&m->host_logits, sizeof(float) * m->batch_cap * m->vocab));
     L0B_CHECK_CUDA(cudaStreamSynchronize(dev->stream));

@@ -388,22 +388,11 @@ static l0b_status attention_common(l0b_suite* s, l0b_device* d, l0b_buffer* q, l
         p.max_splits = 1;
         return attention_launch(d, p, batch);
     }
+    // Decode: split-KV in thread-block clusters merged on chip (no scratch).
     const int seq = last + 1;
-    int chunk, max_splits;
-    attention_pick_split(seq, batch * nkv, d->sm_count, &chunk, &max_splits);
-    p.chunk = chunk;
-    p.max_splits = max_splits;
-    if (max_splits > 1) {
-        const size_t floats = attention_part_floats(batch, nh, max_splits, hd);
-        void* scratch = nullptr;
-        L0B_TRY(d->ensure_scratch(floats * sizeof(float), &scratch));
-        p.part = static_cast<float*>(scratch);
-        p.part_ml = p.part + static_cast<size_t>(batch) * nh * max_splits * hd;
-        unsigned* counters = nullptr;
-        L0B_TRY(d->ensure_counters(static_cast<size_t>(batch) * nh, &counters));
-        p.counters = counters;
-    }
-    return attention_launch(d, p, batch);
+    const int groups = batch * nkv * ((nh / nkv + 7) / 8);
+    p.chunk = 32;
+    return attention_cluster_launch(d, p, batch, attention_cluster_splits(seq, groups, d->sm_count));
 }
 
 L0B_API l0b_status l0b_attention_execute(l0b_suite* s, l0b_device* d, l0b_buffer* q, l0b_buffer* kc, l0b_buffer* vc,

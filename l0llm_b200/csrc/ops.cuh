@@ -66,6 +66,12 @@ struct AttnParams {
 l0b_status attention_launch(l0b_device* d, const AttnParams& p, int batch);
 // Raw-stream variant used by callers without a device handle.
 l0b_status attention_launch_stream(cudaStream_t stream, const AttnParams& p, int batch);
+// Decode attention in thread-block clusters of `splits` (1, 2, 4 or 8) CTAs per (row, KV head group) merged through
+// distributed shared memory: needs no part/part_ml/counters. p.chunk is the minimum split length
+// (a multiple of 32); the kernel derives the split length from each row's live sequence length.
+l0b_status attention_cluster_launch(l0b_device* d, const AttnParams& p, int batch, int splits);
+// Cluster size for a cache of max_seq positions and `work_items` (batch * KV head groups) rows.
+int attention_cluster_splits(int max_seq, int work_items, int sm_count);
 // Scratch floats / counters the kernel needs for (batch, nh, max_splits, hd).
 size_t attention_part_floats(int batch, int nh, int max_splits, int hd);
 // Picks the split length for a cache of max_seq positions and `work_items` (batch * nKv) rows.

@@ -143,9 +143,16 @@ static cudaLaunchConfig_t make_config(const LaunchRecord& rec, cudaStream_t stre
     cfg.attrs = attr;
     cfg.numAttrs = 0;
     if (rec.pdl) {
-        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-        attr[0].val.programmaticStreamSerializationAllowed = 1;
-        cfg.numAttrs = 1;
+        attr[cfg.numAttrs].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[cfg.numAttrs].val.programmaticStreamSerializationAllowed = 1;
+        ++cfg.numAttrs;
+    }
+    if (rec.cluster_y > 1) {
+        attr[cfg.numAttrs].id = cudaLaunchAttributeClusterDimension;
+        attr[cfg.numAttrs].val.clusterDim.x = 1;
+        attr[cfg.numAttrs].val.clusterDim.y = rec.cluster_y;
+        attr[cfg.numAttrs].val.clusterDim.z = 1;
+        ++cfg.numAttrs;
     }
     return cfg;
 }
@@ -157,7 +164,7 @@ l0b_status l0b_device::submit(LaunchRecord& rec) {
     }
     void* args[kMaxArgs];
     rec.arg_pointers(args);
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     cudaLaunchConfig_t cfg = make_config(rec, stream, attr);
     L0B_CHECK_CUDA(cudaLaunchKernelExC(&cfg, rec.func, args));
     add_launches(1);
@@ -178,7 +185,7 @@ l0b_status l0b_device::build_graph(CachedGraph& g) {
     for (auto& rec : g.log) {
         void* args[kMaxArgs];
         rec.arg_pointers(args);
-        cudaLaunchAttribute attr[1];
+        cudaLaunchAttribute attr[2];
         cudaLaunchConfig_t cfg = make_config(rec, stream, attr);
         cudaError_t e = cudaLaunchKernelExC(&cfg, rec.func, args);
         if (e != cudaSuccess) {

@@ -79,6 +79,7 @@ struct LaunchRecord {
     dim3 grid, block;
     uint32_t smem = 0;
     uint8_t pdl = 0;
+    uint8_t cluster_y = 0;  // > 1: thread-block clusters of (1, cluster_y, 1)
     uint8_t nargs = 0;
     uint16_t blob_size = 0;
     uint16_t offsets[kMaxArgs];
@@ -87,7 +88,7 @@ struct LaunchRecord {
     bool same_shape(const LaunchRecord& o) const {
         return func == o.func && grid.x == o.grid.x && grid.y == o.grid.y && grid.z == o.grid.z &&
                block.x == o.block.x && block.y == o.block.y && block.z == o.block.z && smem == o.smem &&
-               pdl == o.pdl && nargs == o.nargs && blob_size == o.blob_size &&
+               pdl == o.pdl && cluster_y == o.cluster_y && nargs == o.nargs && blob_size == o.blob_size &&
                std::memcmp(offsets, o.offsets, nargs * sizeof(uint16_t)) == 0;
     }
     bool same_args(const LaunchRecord& o) const { return std::memcmp(blob, o.blob, blob_size) == 0; }
@@ -158,6 +159,13 @@ struct l0b_device {
 
     template <typename... KArgs, typename... Args>
     l0b_status launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, Args&&... args) {
+        return launch_cluster(kernel, grid, block, smem, 0, static_cast<Args&&>(args)...);
+    }
+
+    // As launch(), in thread-block clusters of (1, cluster_y, 1) CTAs when cluster_y > 1.
+    template <typename... KArgs, typename... Args>
+    l0b_status launch_cluster(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, int cluster_y,
+                              Args&&... args) {
         static_assert(sizeof...(KArgs) == sizeof...(Args), "argument count mismatch");
         if (grid.x == 0 || grid.y == 0 || grid.z == 0) return L0B_OK;
         l0b::LaunchRecord* rec;
@@ -173,6 +181,7 @@ struct l0b_device {
         rec->block = block;
         rec->smem = static_cast<uint32_t>(smem);
         rec->pdl = pdl ? 1 : 0;
+        rec->cluster_y = static_cast<uint8_t>(cluster_y > 1 ? cluster_y : 0);
         rec->nargs = 0;
         rec->blob_size = 0;
         (rec->push(static_cast<KArgs>(args)), ...);
