@@ -24,6 +24,7 @@ namespace {
 
 constexpr int kT = 32;     // positions per tile
 constexpr int kMaxG = 8;   // query heads per CTA
+constexpr int kClusterThreads = 256;  // threads of the cluster decode kernel
 
 // Element d of a rotated head (HF rotate-half pairs) from the per-position cos/sin table.
 __device__ __forceinline__ float rope_elem(const float* head, int d, int rot, const float* cs, const float* sn) {
@@ -250,16 +251,20 @@ __global__ void __launch_bounds__(128) attn_kernel(const AttnParams p) {
 // a second barrier keeps every CTA's shared memory alive until its peers have read it.
 // ---------------------------------------------------------------------------------------------
 template <int HD>
-__global__ void __launch_bounds__(128) attn_cluster_kernel(const AttnParams p) {
+__global__ void __launch_bounds__(kClusterThreads) attn_cluster_kernel(const AttnParams p) {
     namespace cg = cooperative_groups;
-    constexpr int HPT = 128 / HD;
-    constexpr int JPT = kMaxG / HPT;
+    constexpr int NT = kClusterThreads;
+    constexpr int HPT = NT / HD;             // threads per head dimension in the PV phase
+    constexpr int JPT = kMaxG / HPT;         // heads per thread in the PV phase
     constexpr int TPR = HD / 8;              // threads per cached row, 8 dims each
-    constexpr int ITEMS = kT * TPR / 128;    // row pieces per thread per tile
-    __shared__ float qs[kMaxG][HD];
-    __shared__ float ks[kT][HD + 1];
+    constexpr int ITEMS = kT * TPR / NT;     // row pieces per thread per tile
+    // K tile as float4 columns: dims [4 c, 4 c + 4) of position t at ks4[c][t ^ kswz(c)], so a warp
+    // scoring 32 positions reads one conflict-free 16-byte word per lane and the staging stores of
+    // one row spread over the banks.
+    __shared__ __align__(16) float qs[kMaxG][HD];
+    __shared__ float4 ks4[HD / 4][kT];
     __shared__ __align__(16) float vs[kT][HD];
-    __shared__ float ps[kMaxG][kT];
+    __shared__ __align__(16) float ps[kMaxG][kT];
     __shared__ float m_s[kMaxG], l_s[kMaxG], corr_s[kMaxG];
     __shared__ float knew[HD], vnew[HD];
     __shared__ float cs_s[HD / 2], sn_s[HD / 2];
@@ -273,6 +278,7 @@ __global__ void __launch_bounds__(128) attn_cluster_kernel(const AttnParams p) {
     const int ng = min(kMaxG, G - gp * kMaxG);
     const int S = gridDim.y, split = blockIdx.y, b = blockIdx.z;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    auto kswz = [](int c) { return (c >> 1) & (kT - 1); };
 
     pdl_wait();
     const int qpos = p.positions ? p.positions[b] : p.pos_base + b * p.pos_step;
@@ -293,7 +299,7 @@ __global__ void __launch_bounds__(128) attn_cluster_kernel(const AttnParams p) {
     auto load_tile = [&](int t0) {
 #pragma unroll
         for (int it = 0; it < ITEMS; ++it) {
-            const int idx = tid + it * 128;
+            const int idx = tid + it * NT;
             const int t = idx / TPR, d0 = (idx - t * TPR) * 8;
             const int pos = t0 + t;
             kr[it][0] = kr[it][1] = vr[it][0] = vr[it][1] = make_uint4(0, 0, 0, 0);
@@ -328,7 +334,7 @@ __global__ void __launch_bounds__(128) attn_cluster_kernel(const AttnParams p) {
     if (active) load_tile(p_begin);
 
     if (p.rope) {
-        for (int i = tid; i < p.rot / 2; i += 128) {
+        for (int i = tid; i < p.rot / 2; i += NT) {
             const float ang = __fmul_rn(static_cast<float>(qpos), p.inv_freq[i]);
             float s, c;
             sincosf(ang, &s, &c);
@@ -338,7 +344,7 @@ __global__ void __launch_bounds__(128) attn_cluster_kernel(const AttnParams p) {
         __syncthreads();
     }
     const float* qb = p.q + b * p.q_bstride + static_cast<long long>(h0) * HD;
-    for (int idx = tid; idx < kMaxG * HD; idx += 128) {
+    for (int idx = tid; idx < kMaxG * HD; idx += NT) {
         const int j = idx / HD, d = idx - (idx / HD) * HD;
         float v = 0.f;
         if (j < ng) v = p.rope ? rope_elem(qb + j * HD, d, p.rot, cs_s, sn_s) : qb[j * HD + d];
@@ -347,11 +353,13 @@ __global__ void __launch_bounds__(128) attn_cluster_kernel(const AttnParams p) {
     if (tid < kMaxG) {
         m_s[tid] = kNegInf;
         l_s[tid] = 0.f;
+        corr_s[tid] = 1.f;
     }
+    for (int idx = tid; idx < kMaxG * kT; idx += NT) ps[idx / kT][idx % kT] = 0.f;  // head slots past ng stay 0
     if (owns_new) {
         const float* kb = p.k_new + b * p.new_bstride + static_cast<long long>(kvh) * HD;
         const float* vb = p.v_new + b * p.new_bstride + static_cast<long long>(kvh) * HD;
-        for (int d = tid; d < HD; d += 128) {
+        for (int d = tid; d < HD; d += NT) {
             const float kv = p.rope ? rope_elem(kb, d, p.rot, cs_s, sn_s) : kb[d];
             knew[d] = kv;
             vnew[d] = vb[d];
@@ -372,7 +380,7 @@ __global__ void __launch_bounds__(128) attn_cluster_kernel(const AttnParams p) {
     for (int t0 = p_begin; active && t0 < p_end; t0 += kT) {
 #pragma unroll
         for (int it = 0; it < ITEMS; ++it) {
-            const int idx = tid + it * 128;
+            const int idx = tid + it * NT;
             const int t = idx / TPR, d0 = (idx - t * TPR) * 8;
             const int pos = t0 + t;
             float kv[8], vv[8];
@@ -383,20 +391,29 @@ __global__ void __launch_bounds__(128) attn_cluster_kernel(const AttnParams p) {
                 unpack(kr[it], kv);
                 unpack(vr[it], vv);
             }
-#pragma unroll
-            for (int e = 0; e < 8; ++e) ks[t][d0 + e] = kv[e];
+            const int c0 = d0 >> 2;
+            ks4[c0][t ^ kswz(c0)] = make_float4(kv[0], kv[1], kv[2], kv[3]);
+            ks4[c0 + 1][t ^ kswz(c0 + 1)] = make_float4(kv[4], kv[5], kv[6], kv[7]);
             *reinterpret_cast<float4*>(&vs[t][d0]) = make_float4(vv[0], vv[1], vv[2], vv[3]);
             *reinterpret_cast<float4*>(&vs[t][d0 + 4]) = make_float4(vv[4], vv[5], vv[6], vv[7]);
         }
         __syncthreads();
         if (t0 + kT < p_end) load_tile(t0 + kT);  // next tile in flight during the math
-        for (int j = warp; j < ng; j += 4) {
+        for (int j = warp; j < ng; j += NT / 32) {
             float s = kNegInf;
             if (t0 + lane < p_end) {
-                float a = 0.f;
-#pragma unroll 16
-                for (int d = 0; d < HD; ++d) a = fmaf(qs[j][d], ks[lane][d], a);
-                s = a * p.scale;
+                float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+                const float4* q4 = reinterpret_cast<const float4*>(qs[j]);
+#pragma unroll 8
+                for (int c = 0; c < HD / 4; ++c) {
+                    const float4 kk = ks4[c][lane ^ kswz(c)];
+                    const float4 qq = q4[c];
+                    a0 = fmaf(qq.x, kk.x, a0);
+                    a1 = fmaf(qq.y, kk.y, a1);
+                    a2 = fmaf(qq.z, kk.z, a2);
+                    a3 = fmaf(qq.w, kk.w, a3);
+                }
+                s = ((a0 + a1) + (a2 + a3)) * p.scale;
             }
             const float mx = warp_max(s);
             const float m_old = m_s[j];
@@ -413,14 +430,16 @@ __global__ void __launch_bounds__(128) attn_cluster_kernel(const AttnParams p) {
             }
         }
         __syncthreads();
+        // Positions outer, heads inner: each V value is read once for all of this thread's heads.
 #pragma unroll
-        for (int i = 0; i < JPT; ++i) {
-            const int j = jb + i * HPT;
-            if (j < ng) {
-                float a = acc[i] * corr_s[j];
-#pragma unroll 8
-                for (int t = 0; t < kT; ++t) a = fmaf(ps[j][t], vs[t][dim], a);
-                acc[i] = a;
+        for (int i = 0; i < JPT; ++i) acc[i] *= corr_s[jb + i * HPT];
+#pragma unroll 2
+        for (int t = 0; t < kT; t += 4) {
+            const float v0 = vs[t][dim], v1 = vs[t + 1][dim], v2 = vs[t + 2][dim], v3 = vs[t + 3][dim];
+#pragma unroll
+            for (int i = 0; i < JPT; ++i) {
+                const float4 pp = *reinterpret_cast<const float4*>(&ps[jb + i * HPT][t]);
+                acc[i] = fmaf(pp.x, v0, fmaf(pp.y, v1, fmaf(pp.z, v2, fmaf(pp.w, v3, acc[i]))));
             }
         }
         __syncthreads();
@@ -434,7 +453,7 @@ __global__ void __launch_bounds__(128) attn_cluster_kernel(const AttnParams p) {
     else __syncthreads();
     // Merge this CTA's slice of head dimensions from the nact active partials of the cluster.
     const int dper = HD / S;
-    for (int o = tid; o < ng * dper; o += 128) {
+    for (int o = tid; o < ng * dper; o += NT) {
         const int j = o / dper, d = split * dper + (o - (o / dper) * dper);
         float mv[8], lv[8], av[8];
         float mmax = kNegInf;
@@ -489,10 +508,10 @@ l0b_status attention_any(l0b_device* d, cudaStream_t stream, const AttnParams& p
 
 template <typename F>
 l0b_status launch_attn_cluster(l0b_device* d, cudaStream_t stream, F kernel, dim3 grid, int S, const AttnParams& p) {
-    if (d) return d->launch_cluster(kernel, grid, dim3(128), 0, S, p);
+    if (d) return d->launch_cluster(kernel, grid, dim3(kClusterThreads), 0, S, p);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = grid;
-    cfg.blockDim = dim3(128);
+    cfg.blockDim = dim3(kClusterThreads);
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
     if (S > 1) {
