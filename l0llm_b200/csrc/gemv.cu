@@ -452,9 +452,10 @@ __global__ void __launch_bounds__(kThreads) gemv_nk_scalar_kernel(const GemvPara
 // Tensor-core weight streaming for up to 8 activation rows (decode, small batches).
 //
 // One mma.sync.m16n8k16 (fp32 accumulate) takes a 16-row x 16-k weight tile as its A operand and
-// eight activation columns as B. Column 2m of B holds half(x[m] * 2^-4) and column 2m + 1 the fp16
-// residual half(x[m] * 2^-4 - hi), so the two products summed give the dot product with x to ~22
-// bits -- fp32 activations in all but name -- using B columns a single activation row leaves idle.
+// eight activation columns as B. Column 2m of B holds hi = half(x[m] * 2^e) and column 2m + 1 the
+// fp16 residual half(x[m] * 2^e - hi), with 2^e a per-row power of two that puts the row's largest
+// value near 2^14; the two products summed (and scaled back by 2^-e) give the dot product with x to
+// ~22 bits -- fp32 activations in all but name -- using B columns a single row leaves idle.
 // int8 weights become exact f16 integers with two byte permutes into the 0x64 exponent (1024 + u)
 // and one f16x2 subtract of 1152; f16 and bf16 weights feed the MMA as loaded. The MMA reduces
 // across the k of its tile, so no warp shuffles are needed and the instruction count per weight
@@ -544,12 +545,11 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_mma_kernel(const GemvParams 
     extern __shared__ float4 smem_f4[];
     char* xs = reinterpret_cast<char*>(smem_f4);
     __shared__ float2 red[2][kWarps][NG][32];
-    __shared__ float rstd_s[4 * NG];
+    __shared__ float oscale_s[4 * NG];
+    __shared__ float ssq_s[4 * NG][kWarps], amax_s[4 * NG][kWarps];
     constexpr bool kI8 = sizeof(WT) == 1;
     constexpr bool kBF = DT<WT>::id == L0B_BF16;
     constexpr int PE = MmaPiece<WT>::kK;
-    // Activations are scaled by 2^-4 before the f16 split (range up to 2^20) and the sum by 2^4 after.
-    constexpr float kIn = kBF ? 1.0f : 0.0625f, kOut = kBF ? 1.0f : 16.0f;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
     const int N = p.N, K = p.K, M = p.M;
     const int C2 = 2 * M;
@@ -610,16 +610,18 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_mma_kernel(const GemvParams 
         i_s[1] = (kI8 && v1) ? scales + r1 : nullptr;
     };
     set_issue_tile(i_tile);
-    auto issue = [&](uint4 (&slot)[2][kMmaLoads], float (&ss)[2]) {
+    // Piece l of the chunk at the issue cursor (step i_step), then the cursor's scale and advance.
+    auto issue_piece = [&](uint4 (&slot)[2][kMmaLoads], int l) {
         if (i_step < total) {
             const long long kk = static_cast<long long>(i_q) * (kMmaLoads * PE);
+            const bool in_k = p0 + kMmaLoads * i_q + l < p1;
 #pragma unroll
-            for (int l = 0; l < kMmaLoads; ++l) {
-                const bool in_k = p0 + kMmaLoads * i_q + l < p1;
-#pragma unroll
-                for (int r = 0; r < 2; ++r)
-                    slot[r][l] = (i_p[r] && in_k) ? ld_stream_v4(i_p[r] + kk + l * PE) : make_uint4(0, 0, 0, 0);
-            }
+            for (int r = 0; r < 2; ++r)
+                slot[r][l] = (i_p[r] && in_k) ? ld_stream_v4(i_p[r] + kk + l * PE) : make_uint4(0, 0, 0, 0);
+        }
+    };
+    auto issue_finish = [&](float (&ss)[2]) {
+        if (i_step < total) {
             if (kI8 && i_q == 0) {
 #pragma unroll
                 for (int r = 0; r < 2; ++r) ss[r] = i_s[r] ? __half2float(*i_s[r]) : 0.f;
@@ -632,67 +634,122 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_mma_kernel(const GemvParams 
         }
         ++i_step;
     };
+    // The whole ring goes out before griddepcontrol.wait: weights never depend on the previous kernel.
+    // (Issuing the second slot only after staging, to free its registers there, measured 20-25% slower.)
 #pragma unroll
-    for (int d = 0; d < kMmaRing; ++d) issue(ring[d], sring[d]);
+    for (int d = 0; d < kMmaRing; ++d) {
+#pragma unroll
+        for (int l = 0; l < kMmaLoads; ++l) issue_piece(ring[d], l);
+        issue_finish(sring[d]);
+    }
 
     pdl_wait();
     pdl_launch_dependents();
 
     const bool xvec = p.x_dtype == L0B_F32 && (p.x_ld & 3) == 0 && (reinterpret_cast<uintptr_t>(p.x) & 15) == 0;
     const float* xf = static_cast<const float*>(p.x);
-    if (p.norm_w) {
-        __shared__ float nred[32];
+    // Stage x in two passes over shared memory, one global read. Pass 1: each thread loads its items
+    // (32-k unit u, quad lane t: 8 consecutive k), applies the RMS-norm weight, stores the fp32 values
+    // into the 32 bytes their hi/lo pair will occupy, and accumulates the row's sum of squares and
+    // largest magnitude. Pass 2 (after one barrier): the same thread rereads its values, applies the
+    // row's 1/RMS and a power-of-two scale that puts the row maximum near 2^14 (so the f16 split
+    // neither overflows nor loses the small values to subnormals), and splits them into hi + lo. The
+    // epilogue multiplies by the exact inverse of that power of two.
+    {
+        const int items = (K / 32) * 4;  // per activation row
+        constexpr int kSB = 2;
+        auto item_slot = [&](int it, int m, int& k) {
+            const int u = it >> 2, tt = it & 3;
+            k = kI8 ? (u >> 1) * 64 + 16 * tt + 8 * (u & 1) : 32 * u + 8 * tt;
+            return xs + static_cast<size_t>(u) * C2 * 64 + tt * 16 + (2 * m) * 64;  // lo slot is +64
+        };
         for (int m = 0; m < M; ++m) {
-            float ss = 0.f;
-            if (xvec) {
-                for (int k = threadIdx.x * 4; k < K; k += kThreads * 4) {
-                    const float4 v = *reinterpret_cast<const float4*>(xf + m * p.x_ld + k);
-                    ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+            float ss = 0.f, amax = 0.f;
+            for (int it0 = threadIdx.x; it0 < items; it0 += kThreads * kSB) {
+                float v[kSB][8], nw[kSB][8];
+#pragma unroll
+                for (int b = 0; b < kSB; ++b) {
+                    const int it = it0 + b * kThreads;
+                    int k;
+                    item_slot(it, m, k);
+                    if (it < items) {
+                        if (xvec) {
+                            const float4 a = *reinterpret_cast<const float4*>(xf + m * p.x_ld + k);
+                            const float4 c = *reinterpret_cast<const float4*>(xf + m * p.x_ld + k + 4);
+                            v[b][0] = a.x, v[b][1] = a.y, v[b][2] = a.z, v[b][3] = a.w;
+                            v[b][4] = c.x, v[b][5] = c.y, v[b][6] = c.z, v[b][7] = c.w;
+                        } else {
+#pragma unroll
+                            for (int e = 0; e < 8; ++e) v[b][e] = load_as_float(p.x, p.x_dtype, m * p.x_ld + k + e);
+                        }
+                        if (p.norm_w) {
+                            const float4 a = *reinterpret_cast<const float4*>(p.norm_w + k);
+                            const float4 c = *reinterpret_cast<const float4*>(p.norm_w + k + 4);
+                            nw[b][0] = a.x, nw[b][1] = a.y, nw[b][2] = a.z, nw[b][3] = a.w;
+                            nw[b][4] = c.x, nw[b][5] = c.y, nw[b][6] = c.z, nw[b][7] = c.w;
+                        }
+                    }
                 }
-            } else {
-                for (int k = threadIdx.x; k < K; k += kThreads) {
-                    const float v = load_as_float(p.x, p.x_dtype, m * p.x_ld + k);
-                    ss += v * v;
+#pragma unroll
+                for (int b = 0; b < kSB; ++b) {
+                    const int it = it0 + b * kThreads;
+                    if (it >= items) break;
+                    int k;
+                    char* slot = item_slot(it, m, k);
+                    if (p.norm_w) {
+#pragma unroll
+                        for (int e = 0; e < 8; ++e) {
+                            ss = fmaf(v[b][e], v[b][e], ss);
+                            v[b][e] *= nw[b][e];
+                        }
+                    }
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) amax = fmaxf(amax, fabsf(v[b][e]));
+                    *reinterpret_cast<float4*>(slot) = make_float4(v[b][0], v[b][1], v[b][2], v[b][3]);
+                    *reinterpret_cast<float4*>(slot + 64) = make_float4(v[b][4], v[b][5], v[b][6], v[b][7]);
                 }
             }
-            ss = block_sum(ss, nred);
-            if (threadIdx.x == 0) rstd_s[m] = 1.0f / sqrtf(ss / static_cast<float>(K) + p.eps);
+            ss = warp_sum(ss);
+            amax = warp_max(amax);
+            if (lane == 0) {
+                ssq_s[m][warp] = ss;
+                amax_s[m][warp] = amax;
+            }
         }
         __syncthreads();
-    }
-    // Stage: item = (32-k unit u, row m, t) -> 8 consecutive k, stored as hi and lo columns.
-    {
-        const int items = (K / 32) * M * 4;
-#pragma unroll 2
-        for (int it = threadIdx.x; it < items; it += kThreads) {
-            const int u = it / (M * 4);
-            const int r = it - u * (M * 4);
-            const int m = r >> 2, tt = r & 3;
-            const int k = kI8 ? (u >> 1) * 64 + 16 * tt + 8 * (u & 1) : 32 * u + 8 * tt;
-            float v[8];
-            if (xvec) {
-                const float4 a = *reinterpret_cast<const float4*>(xf + m * p.x_ld + k);
-                const float4 b = *reinterpret_cast<const float4*>(xf + m * p.x_ld + k + 4);
-                v[0] = a.x, v[1] = a.y, v[2] = a.z, v[3] = a.w, v[4] = b.x, v[5] = b.y, v[6] = b.z, v[7] = b.w;
-            } else {
+        for (int m = 0; m < M; ++m) {
+            float ss = 0.f, amax = 0.f;
 #pragma unroll
-                for (int e = 0; e < 8; ++e) v[e] = load_as_float(p.x, p.x_dtype, m * p.x_ld + k + e);
+            for (int w = 0; w < kWarps; ++w) {
+                ss += ssq_s[m][w];
+                amax = fmaxf(amax, amax_s[m][w]);
             }
-            if (p.norm_w) {
-                const float rs = rstd_s[m];
-#pragma unroll
-                for (int e = 0; e < 8; ++e) v[e] = (v[e] * rs) * p.norm_w[k + e];
+            const float rs = p.norm_w ? 1.0f / sqrtf(ss / static_cast<float>(K) + p.eps) : 1.0f;
+            // Power of two 2^e with (amax * rs) * 2^e in [2^13, 2^14); bf16 keeps the fp32 range (e = 0).
+            int e = 0;
+            if (!kBF && amax * rs > 0.f && isfinite(amax * rs)) {
+                int ex;
+                frexpf(amax * rs, &ex);  // amax * rs = f * 2^ex, f in [0.5, 1)
+                e = min(max(14 - ex, -100), 100);
             }
-#pragma unroll
-            for (int e = 0; e < 8; ++e) v[e] *= kIn;
-            uint4 hi, lo;
-            split_hi_lo<kBF>(v, hi, lo);
-            char* base = xs + static_cast<size_t>(u) * C2 * 64 + tt * 16;
-            *reinterpret_cast<uint4*>(base + (2 * m) * 64) = hi;
-            *reinterpret_cast<uint4*>(base + (2 * m + 1) * 64) = lo;
+            const float in_scale = rs * ldexpf(1.0f, e);
+            if (threadIdx.x == 0) oscale_s[m] = ldexpf(1.0f, -e);
+            for (int it = threadIdx.x; it < items; it += kThreads) {
+                int k;
+                char* slot = item_slot(it, m, k);
+                const float4 a = *reinterpret_cast<const float4*>(slot);
+                const float4 c = *reinterpret_cast<const float4*>(slot + 64);
+                float v[8] = {a.x * in_scale, a.y * in_scale, a.z * in_scale, a.w * in_scale,
+                              c.x * in_scale, c.y * in_scale, c.z * in_scale, c.w * in_scale};
+                uint4 hi, lo;
+                split_hi_lo<kBF>(v, hi, lo);
+                *reinterpret_cast<uint4*>(slot) = hi;
+                *reinterpret_cast<uint4*>(slot + 64) = lo;
+            }
         }
     }
     __syncthreads();
+    // oscale_s[m] = 2^-e of row m, applied by the epilogues.
 
     // Epilogue of tile `tile` (iteration i) by one warp after the partials are in red[i & 1].
     auto reduce_tile = [&](int i, int tile) {
@@ -707,10 +764,11 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_mma_kernel(const GemvParams 
                 y0 += q.x;
                 y1 += q.y;
             }
-            y0 *= kOut;
-            y1 *= kOut;
             const int m = 4 * ng + t;
             const bool live = m < M;
+            const float f = live ? oscale_s[m] : 1.0f;
+            y0 *= f;
+            y1 *= f;
             if (p.epi == EPI_ARGMAX) {
                 unsigned long long key = 0;
                 if (live && v0) key = argmax_key(epilogue_store(p, r0, m, y0, false), r0);
@@ -790,9 +848,10 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_mma_kernel(const GemvParams 
                             }
                         }
                     }
+                    issue_piece(ring[d], l);  // piece l of this slot is free again: refill it now
                 }
                 if (kI8 && c_q == 0) rs2[0] = sring[d][0], rs2[1] = sring[d][1];
-                issue(ring[d], sring[d]);
+                issue_finish(sring[d]);
                 if (++c_q == nq) {
 #pragma unroll
                     for (int ng = 0; ng < NG; ++ng) {

@@ -62,11 +62,10 @@ def test_gemv_paths_store(lz, orc, device, suite, path, wkind, n, k, m):
 
 
 @pytest.mark.parametrize("wkind", ["f16", "i8c"])
-@pytest.mark.parametrize("inter", [4864, 100])
+@pytest.mark.parametrize("H,inter", [(896, 4864), (896, 100), (3584, 1000)])
 @pytest.mark.parametrize("m", [1, 3, 8])
-def test_gemv_paths_norm_swiglu(lz, orc, device, suite, path, wkind, inter, m):
-    rng = np.random.default_rng(inter + m)
-    H = 896
+def test_gemv_paths_norm_swiglu(lz, orc, device, suite, path, wkind, H, inter, m):
+    rng = np.random.default_rng(inter + m + H)
     x = (rng.standard_normal((m, H)) * 3).astype(np.float32)
     nw = (1 + 0.1 * rng.standard_normal(H)).astype(np.float32)
     hf = ((rng.random((2 * inter, H)) * 2 - 1) * 0.05).astype(np.float32)
