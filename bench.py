@@ -57,58 +57,93 @@ def peaks() -> tuple[float, str]:
 
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons sampled every 200 ms during the timed region."""
+    """SM clocks and clock-event (throttle) reasons read every 20 ms through NVML (the library nvidia-smi
+    reports from; reads only) on a host thread, each sample time-stamped so that only samples taken
+    inside the timed region count. Falls back to `nvidia-smi -lms` when NVML is unavailable."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = {"hw_slowdown": 0x8, "hw_thermal_slowdown": 0x40, "sw_thermal_slowdown": 0x20, "sw_power_cap": 0x4}
 
     def __init__(self, gpu: int):
         self.gpu = gpu
-        self.rows: list[list[str]] = []
-        self.proc = None
+        self.samples: list[tuple[float, float, float, int]] = []  # (t, sm MHz, max MHz, reason bits)
+        self.stop_flag = threading.Event()
         self.thread = None
+        self.proc = None
+        self.window = (0.0, float("inf"))
 
     def start(self):
         try:
-            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
+            import pynvml
+
+            pynvml.nvmlInit()
+            h = pynvml.nvmlDeviceGetHandleByIndex(self.gpu)
+            mx = float(pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM))
+            get_reasons = getattr(pynvml, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                pynvml.nvmlDeviceGetCurrentClocksThrottleReasons
+
+            def loop():
+                while not self.stop_flag.is_set():
+                    try:
+                        sm = float(pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM))
+                        bits = int(get_reasons(h))
+                        self.samples.append((time.monotonic(), sm, mx, bits))
+                    except Exception:
+                        pass
+                    self.stop_flag.wait(0.02)
+
+            self.thread = threading.Thread(target=loop, daemon=True)
+            self.thread.start()
+        except Exception:
+            self._start_smi()
+
+    def _start_smi(self):
+        fields = ("clocks.sm,clocks.max.sm,clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+                  "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={fields}",
+                                          "--format=csv,noheader,nounits", "-lms", "50"],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except (OSError, FileNotFoundError):
             self.proc = None
             return
-        self.thread = threading.Thread(target=self._read, daemon=True)
+        bits = list(self.REASONS.values())
+
+        def read():
+            for line in self.proc.stdout:
+                r = [c.strip() for c in line.split(",")]
+                try:
+                    b = sum(bit for bit, v in zip(bits, r[2:6]) if v.lower().startswith("active"))
+                    self.samples.append((time.monotonic(), float(r[0]), float(r[1]), b))
+                except (ValueError, IndexError):
+                    continue
+
+        self.thread = threading.Thread(target=read, daemon=True)
         self.thread.start()
 
-    def _read(self):
-        for line in self.proc.stdout:
-            self.rows.append([c.strip() for c in line.split(",")])
+    def mark(self, t0: float, t1: float):
+        """The timed region, in time.monotonic() seconds."""
+        self.window = (t0, t1)
 
     def stop(self) -> dict:
-        if self.proc is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        self.proc.terminate()
-        try:
-            self.proc.wait(timeout=5)
-        except subprocess.TimeoutExpired:
-            self.proc.kill()
+        self.stop_flag.set()
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
         if self.thread:
             self.thread.join(timeout=2)
-        sm, mx, reasons = [], [], set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for r in self.rows:
-            if len(r) < 9:
-                continue
-            try:
-                sm.append(float(r[1]))
-                mx.append(float(r[2]))
-            except ValueError:
-                continue
-            for name, v in zip(names, r[5:9]):
-                if v.lower().startswith("active"):
-                    reasons.add(name)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": sorted(reasons), "samples": len(sm)}
+        t0, t1 = self.window
+        inside = [s for s in self.samples if t0 <= s[0] <= t1]
+        if not inside and self.samples:  # region shorter than one sample: take the nearest after its start
+            after = [s for s in self.samples if s[0] >= t0]
+            inside = after[:1]
+        if not inside:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no clock samples"], "samples": 0}
+        reasons = sorted(name for name, bit in self.REASONS.items() if any(s[3] & bit for s in inside))
+        return {"sm_mhz": statistics.median(s[1] for s in inside), "sm_max_mhz": max(s[2] for s in inside),
+                "reasons": reasons, "samples": len(inside)}
 
 
 def dist_env():
@@ -290,18 +325,21 @@ def main() -> int:
             pg.barrier()
         torch.cuda.synchronize()
 
-    # Warm-up (graph capture happens here), then the timed device-resident decode.
-    model.decode_greedy_device(args.warmup)
-    pos_start = model.Position
+    # Warm-up (graph capture happens here), then the timed device-resident decode. The clock sampler
+    # runs from before the warm-up and keeps only the samples taken inside the timed region.
     sampler = ClockSampler(local)
     sampler.start()
+    model.decode_greedy_device(args.warmup)
+    pos_start = model.Position
     launches0 = lz.kernel_launch_count()
     barrier()
+    t_begin = time.monotonic()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     model.decode_greedy_device(args.steps)
     e1.record(stream)
     e1.synchronize()
+    sampler.mark(t_begin, time.monotonic())
     barrier()
     ms = e0.elapsed_time(e1)
     launches = lz.kernel_launch_count() - launches0

@@ -1,10 +1,14 @@
 // Weight-streaming linear layers for decode and small batches (sm_100a).
 //
 // Layout: W is [N, K] row-major (HuggingFace [out, in]); every output row is one contiguous stream.
+// Two kernels. The tensor-core kernel further below (gemv_mma_kernel) takes 16-bit weights and int8
+// with one scale per row, up to 8 activation rows; the fp32-FMA kernel described here takes the rest
+// (fp32 weights, int8 with group scales, longer activation rows).
+//
 // A warp owns RPW rows (for SwiGLU a gate row and its up row); each lane reads 16 bytes per row per
 // step with a no-L1-allocate 128-bit load, so a warp step moves 512 contiguous bytes per row. int8
-// weights are dequantised in registers (exact byte -> fp32 trick, see dequant_i8x4) and multiplied in
-// fp32 with packed f32x2 FMAs; per-lane partial sums are reduced with warp shuffles. Activations are
+// weights are dequantised in registers (exact byte -> fp32 trick, see dequant4) and multiplied with
+// scalar fp32 FMAs; per-lane partial sums are reduced with warp shuffles. Activations are
 // staged once per CTA in shared memory as fp32, permuted lane-major so the 128-bit shared loads are
 // conflict-free, and optionally RMS-normalised on the way in (fused input/post-attention norm).
 //
