@@ -419,6 +419,7 @@ typedef struct l0b_model_config {
     int32_t q8_group;            /* int8 scale group: 32 (reference) or 0 = per output channel */
     int32_t tp_size;             /* tensor-parallel ranks (1 = none) */
     int32_t tp_rank;
+    int32_t max_batch;           /* sequences decoded together (KV cache rows); default 1, at most 64 */
 } l0b_model_config;
 
 /* Fills a config with the defaults HfModelConfig.Parse applies. */
@@ -464,6 +465,25 @@ L0B_API l0b_status l0b_model_generate_greedy(l0b_model* model, const int32_t* id
                                              int32_t max_new, const int32_t* stop_ids, int32_t n_stop,
                                              int32_t* out, int32_t* out_count);
 /* LlmModel.Position / ResetSequence / MaxSeqLen / ProjectionBytes. */
+/* Batched decoding of independent sequences (a capability the reference's engine lacks: it serialises
+ * one request at a time, L/LevelZeroLlmEngine.cs:22,55). A model created with cfg.max_batch = B keeps B
+ * KV-cache rows; sequence 0 is also the one the single-sequence calls above use.
+ *
+ * Prefill of sequence `seq` (LlmModel.Prefill semantics, L/LlmModel.cs:224-239, into cache row seq);
+ * logits (may be NULL) receive the last position's logits; the greedy next token and position are kept
+ * on the device for l0b_model_decode_greedy_device_batch. */
+L0B_API l0b_status l0b_model_prefill_sequence(l0b_model* model, int32_t seq, const int32_t* ids, int32_t count,
+                                              float* logits);
+/* One decode step of sequences 0..count-1: row b takes tokens[b] at positions[b] (cache row b).
+ * logits (may be NULL): [count, vocab]. Fused path only. */
+L0B_API l0b_status l0b_model_decode_batch(l0b_model* model, const int32_t* tokens, const int32_t* positions,
+                                          int32_t count, float* logits);
+/* `steps` greedy steps of sequences 0..count-1 entirely on the device (one CUDA graph per step), each
+ * sequence continuing from its own token and position; out (may be NULL): [steps, count] tokens. */
+L0B_API l0b_status l0b_model_decode_greedy_device_batch(l0b_model* model, int32_t steps, int32_t count,
+                                                        int32_t* out);
+/* Next position of sequence `seq` (its prefilled and decoded length). */
+L0B_API l0b_status l0b_model_sequence_position(l0b_model* model, int32_t seq, int32_t* position);
 L0B_API l0b_status l0b_model_position(l0b_model* model, int32_t* position);
 L0B_API l0b_status l0b_model_reset_sequence(l0b_model* model);
 L0B_API l0b_status l0b_model_projection_bytes(l0b_model* model, int64_t* bytes);

@@ -17,6 +17,8 @@
 // step s + D are issued while step s is multiplied, and row-block epilogues run in the stream. The
 // first D steps are issued before griddepcontrol.wait -- weights never depend on the previous kernel
 // -- so under programmatic dependent launch the weight stream starts while the producer of x drains.
+#include <cooperative_groups.h>
+
 #include "common.cuh"
 #include "gemv.cuh"
 
@@ -539,21 +541,32 @@ struct MmaPiece {
 constexpr int kMmaLoads = 4;  // pieces per chunk: 256 contiguous bytes of each row per quad
 constexpr int kMmaRing = 2;   // chunks in flight per warp
 
-// NG groups of 4 activation rows (8 B columns each). Shared memory holds the split activations in
-// 32-k units: unit u, column col, quad lane t at (u * 2M + col) * 64 + t * 16, eight 16-bit values.
-// For int8 unit u = 2p + j holds x[64 p + 16 t + 8 j, +8) (the 16 values lane t multiplies in piece p),
-// for 16-bit weights x[32 u + 8 t, +8). Lane (g, t) reads column g with conflict-free 16-byte loads;
-// columns past 2M are never read.
+// NG groups of 4 activation rows (8 B columns each, NG <= 4: up to 16 rows). Shared memory holds the
+// split activations of this CTA's K range in 32-k units: unit u (relative to the range start), column
+// col, quad lane t at (u * 2M + col) * 64 + t * 16, eight 16-bit values. For int8 unit u = 2p + j holds
+// x[64 p + 16 t + 8 j, +8) (the 16 values lane t multiplies in piece p), for 16-bit weights
+// x[32 u + 8 t, +8). Lane (g, t) reads column g with conflict-free loads; columns past 2M are never read.
+//
+// Split-K (gridDim.y = S > 1): the S CTAs of a thread-block cluster (1, S, 1) share the tiles of
+// cluster blockIdx.x and each takes the ks-th S-th of every row's pieces, so each stages only its slice
+// of x. Per-row sums of squares (for the fused RMSNorm) are exchanged through distributed shared memory
+// before the split, and per tile the ranks' partial sums meet in rank 0, which reads them from the
+// peers' shared memory in rank order one tile later (deterministic, no global scratch, no atomics).
 template <typename WT, int NG>
 __global__ void __launch_bounds__(kThreads, 2) gemv_mma_kernel(const GemvParams p) {
+    namespace cg = cooperative_groups;
     extern __shared__ float4 smem_f4[];
     char* xs = reinterpret_cast<char*>(smem_f4);
     __shared__ float2 red[2][kWarps][NG][32];
+    __shared__ float2 cpart[2][NG][32];  // this CTA's finished tile partial (split-K)
     __shared__ float oscale_s[4 * NG];
     __shared__ float ssq_s[4 * NG][kWarps], amax_s[4 * NG][kWarps];
     constexpr bool kI8 = sizeof(WT) == 1;
     constexpr bool kBF = DT<WT>::id == L0B_BF16;
     constexpr int PE = MmaPiece<WT>::kK;
+    constexpr int KU = MmaPiece<WT>::kUnits;
+    cg::cluster_group cluster = cg::this_cluster();
+    const int S = gridDim.y, ks = blockIdx.y;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
     const int N = p.N, K = p.K, M = p.M;
     const int C2 = 2 * M;
@@ -561,14 +574,20 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_mma_kernel(const GemvParams 
     const int half_n = N >> 1;
     const int units = swiglu ? half_n : N;
     const int ntiles = (units + (swiglu ? 7 : 15)) / (swiglu ? 8 : 16);
-    // Warp w owns the contiguous pieces [p0, p1) of every tile (counts differ by at most one).
+    // This CTA's pieces [kp0, kp1) of every row; warp w owns [p0, p1) of them (counts differ by <= 1).
     const int npieces = K / PE;
-    const int p0 = warp * npieces / kWarps, p1 = (warp + 1) * npieces / kWarps;
+    const int kp0 = ks * npieces / S, kp1 = (ks + 1) * npieces / S;
+    const int p0 = kp0 + warp * (kp1 - kp0) / kWarps, p1 = kp0 + (warp + 1) * (kp1 - kp0) / kWarps;
     const int nq = (p1 - p0 + kMmaLoads - 1) / kMmaLoads;  // chunks of this warp per tile
+    const int u_lo = kp0 * KU, nunits = (kp1 - kp0) * KU;
     const int my_tiles = blockIdx.x < ntiles ? (ntiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
     const int total = my_tiles * nq;
     const WT* W = static_cast<const WT*>(p.w);
     const __half* scales = static_cast<const __half*>(p.scales);
+    auto cluster_barrier = [&]() {
+        if (S > 1) cluster.sync();
+        else __syncthreads();
+    };
 
     auto tile_rows = [&](int tile, int& r0, int& r1, bool& v0, bool& v1) {
         if (swiglu) {
@@ -583,7 +602,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_mma_kernel(const GemvParams 
         }
     };
 
-    if (p.prefetch && threadIdx.x == 0 && blockIdx.x < ntiles) {
+    if (p.prefetch && S == 1 && threadIdx.x == 0 && blockIdx.x < ntiles) {
         const long long row_bytes = K * static_cast<long long>(sizeof(WT));
         const int per = swiglu ? 8 : 16;
         const long long u0 = static_cast<long long>(blockIdx.x) * per;
@@ -652,20 +671,21 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_mma_kernel(const GemvParams 
 
     const bool xvec = p.x_dtype == L0B_F32 && (p.x_ld & 3) == 0 && (reinterpret_cast<uintptr_t>(p.x) & 15) == 0;
     const float* xf = static_cast<const float*>(p.x);
-    // Stage x in two passes over shared memory, one global read. Pass 1: each thread loads its items
-    // (32-k unit u, quad lane t: 8 consecutive k), applies the RMS-norm weight, stores the fp32 values
-    // into the 32 bytes their hi/lo pair will occupy, and accumulates the row's sum of squares and
-    // largest magnitude. Pass 2 (after one barrier): the same thread rereads its values, applies the
-    // row's 1/RMS and a power-of-two scale that puts the row maximum near 2^14 (so the f16 split
-    // neither overflows nor loses the small values to subnormals), and splits them into hi + lo. The
-    // epilogue multiplies by the exact inverse of that power of two.
+    // Stage this CTA's slice of x in two passes over shared memory, one global read. Pass 1: each thread
+    // loads its items (32-k unit u, quad lane t: 8 consecutive k), applies the RMS-norm weight, stores
+    // the fp32 values into the 32 bytes their hi/lo pair will occupy, and accumulates the row's sum of
+    // squares and largest magnitude. Pass 2 (after one barrier; with split-K a cluster barrier, and the
+    // sums of squares of all ranks are added so the norm covers the whole row): the same thread rereads
+    // its values, applies the row's 1/RMS and a power-of-two scale 2^e that puts this slice's maximum
+    // near 2^14 (so the f16 split neither overflows nor loses small values to subnormals), and splits them
+    // into hi + lo. The epilogue multiplies by the exact 2^-e.
     {
-        const int items = (K / 32) * 4;  // per activation row
+        const int items = nunits * 4;  // per activation row
         constexpr int kSB = 2;
         auto item_slot = [&](int it, int m, int& k) {
-            const int u = it >> 2, tt = it & 3;
+            const int ur = it >> 2, tt = it & 3, u = u_lo + ur;
             k = kI8 ? (u >> 1) * 64 + 16 * tt + 8 * (u & 1) : 32 * u + 8 * tt;
-            return xs + static_cast<size_t>(u) * C2 * 64 + tt * 16 + (2 * m) * 64;  // lo slot is +64
+            return xs + static_cast<size_t>(ur) * C2 * 64 + tt * 16 + (2 * m) * 64;  // lo slot is +64
         };
         for (int m = 0; m < M; ++m) {
             float ss = 0.f, amax = 0.f;
@@ -720,13 +740,17 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_mma_kernel(const GemvParams 
                 amax_s[m][warp] = amax;
             }
         }
-        __syncthreads();
+        cluster_barrier();
         for (int m = 0; m < M; ++m) {
             float ss = 0.f, amax = 0.f;
 #pragma unroll
-            for (int w = 0; w < kWarps; ++w) {
-                ss += ssq_s[m][w];
-                amax = fmaxf(amax, amax_s[m][w]);
+            for (int w = 0; w < kWarps; ++w) amax = fmaxf(amax, amax_s[m][w]);
+            if (p.norm_w) {
+                for (int r = 0; r < S; ++r) {
+                    const float* q = S > 1 ? cluster.map_shared_rank(&ssq_s[m][0], r) : &ssq_s[m][0];
+#pragma unroll
+                    for (int w = 0; w < kWarps; ++w) ss += q[w];
+                }
             }
             const float rs = p.norm_w ? 1.0f / sqrtf(ss / static_cast<float>(K) + p.eps) : 1.0f;
             // Power of two 2^e with (amax * rs) * 2^e in [2^13, 2^14); bf16 keeps the fp32 range (e = 0).
@@ -753,26 +777,18 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_mma_kernel(const GemvParams 
         }
     }
     __syncthreads();
-    // oscale_s[m] = 2^-e of row m, applied by the epilogues.
+    // oscale_s[m] = 2^-e of row m, applied to this CTA's partial sums.
 
-    // Epilogue of tile `tile` (iteration i) by one warp after the partials are in red[i & 1].
-    auto reduce_tile = [&](int i, int tile) {
+    // Store / argmax / SwiGLU epilogue of a finished tile; y[ng] = (row g, row g + 8) of row 4 ng + t.
+    auto epilogue = [&](int tile, const float2 (&y)[NG]) {
         int r0, r1;
         bool v0, v1;
         tile_rows(tile, r0, r1, v0, v1);
 #pragma unroll
         for (int ng = 0; ng < NG; ++ng) {
-            float y0 = 0.f, y1 = 0.f;
-            for (int w = 0; w < kWarps; ++w) {
-                const float2 q = red[i & 1][w][ng][lane];
-                y0 += q.x;
-                y1 += q.y;
-            }
+            const float y0 = y[ng].x, y1 = y[ng].y;
             const int m = 4 * ng + t;
             const bool live = m < M;
-            const float f = live ? oscale_s[m] : 1.0f;
-            y0 *= f;
-            y1 *= f;
             if (p.epi == EPI_ARGMAX) {
                 unsigned long long key = 0;
                 if (live && v0) key = argmax_key(epilogue_store(p, r0, m, y0, false), r0);
@@ -790,86 +806,161 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_mma_kernel(const GemvParams 
             }
         }
     };
+    // This CTA's partial of tile iteration i: the warps' partials in red[i & 1], scaled back by 2^-e.
+    auto local_tile = [&](int i, float2 (&y)[NG]) {
+#pragma unroll
+        for (int ng = 0; ng < NG; ++ng) {
+            float y0 = 0.f, y1 = 0.f;
+            for (int w = 0; w < kWarps; ++w) {
+                const float2 q = red[i & 1][w][ng][lane];
+                y0 += q.x;
+                y1 += q.y;
+            }
+            const int m = 4 * ng + t;
+            const float f = m < M ? oscale_s[m] : 1.0f;
+            y[ng] = make_float2(y0 * f, y1 * f);
+        }
+    };
+    // Rank 0: tile iteration i summed over the cluster's ranks (in rank order), then its epilogue.
+    auto cluster_epilogue = [&](int i) {
+        float2 y[NG];
+#pragma unroll
+        for (int ng = 0; ng < NG; ++ng) {
+            float y0 = 0.f, y1 = 0.f;
+            for (int r = 0; r < S; ++r) {
+                const float2 q = *cluster.map_shared_rank(&cpart[i & 1][ng][lane], r);
+                y0 += q.x;
+                y1 += q.y;
+            }
+            y[ng] = make_float2(y0, y1);
+        }
+        epilogue(blockIdx.x + i * gridDim.x, y);
+    };
     auto reducer = [&](int i) { return kWarps - 1 - (i & (kWarps - 1)); };
+    // After the barrier of tile iteration i: its local partial, and (split-K, rank 0) the previous
+    // iteration's cluster sum, whose peer partials the barrier has made visible.
+    auto finish_tile = [&](int i) {
+        if (warp == reducer(i)) {
+            float2 y[NG];
+            local_tile(i, y);
+            if (S == 1) {
+                epilogue(blockIdx.x + i * gridDim.x, y);
+            } else {
+#pragma unroll
+                for (int ng = 0; ng < NG; ++ng) cpart[i & 1][ng][lane] = y[ng];
+            }
+        }
+        if (S > 1 && ks == 0 && i > 0 && warp == reducer(i - 1)) cluster_epilogue(i - 1);
+    };
 
-    if (nq == 0) {  // no pieces for this warp (K < 8 pieces): zero partials, barriers, epilogues
+    if (nq == 0) {  // no pieces for this warp (a short K range): zero partials, barriers, epilogues
         for (int i = 0; i < my_tiles; ++i) {
 #pragma unroll
             for (int ng = 0; ng < NG; ++ng) red[i & 1][warp][ng][lane] = make_float2(0.f, 0.f);
-            __syncthreads();
-            if (warp == reducer(i)) reduce_tile(i, blockIdx.x + i * gridDim.x);
+            cluster_barrier();
+            finish_tile(i);
         }
-        return;
-    }
-
-    float acc[NG][4];
+    } else {
+        float acc[NG][4];
 #pragma unroll
-    for (int ng = 0; ng < NG; ++ng) acc[ng][0] = acc[ng][1] = acc[ng][2] = acc[ng][3] = 0.f;
-    float rs2[2] = {1.f, 1.f};
-    int c_q = 0, c_i = 0;
-    const int col_off = g * 64 + t * 16;  // this lane's column g, quad slot t inside a unit
-    for (int s = 0; s < total; s += kMmaRing) {
+        for (int ng = 0; ng < NG; ++ng) acc[ng][0] = acc[ng][1] = acc[ng][2] = acc[ng][3] = 0.f;
+        float rs2[2] = {1.f, 1.f};
+        int c_q = 0, c_i = 0;
+        const int col_off = g * 64 + t * 16;  // this lane's column g, quad slot t inside a unit
+        for (int s = 0; s < total; s += kMmaRing) {
 #pragma unroll
-        for (int d = 0; d < kMmaRing; ++d) {
-            if (s + d < total) {
+            for (int d = 0; d < kMmaRing; ++d) {
+                if (s + d < total) {
 #pragma unroll
-                for (int l = 0; l < kMmaLoads; ++l) {
-                    const int piece = p0 + kMmaLoads * c_q + l;
-                    if (piece < p1) {
-                        // B fragments of this piece: MmaPiece::kUnits 16-byte loads per column group.
-                        uint32_t b[NG][8];
+                    for (int l = 0; l < kMmaLoads; ++l) {
+                        const int piece = p0 + kMmaLoads * c_q + l;
+                        if (piece < p1) {
+                            const char* ub = xs + static_cast<size_t>(piece * KU - u_lo) * C2 * 64 + col_off;
+                            if constexpr (NG <= 2) {
+                                // B fragments of the whole piece: KU 16-byte loads per column group.
+                                uint32_t b[NG][8];
+#pragma unroll
+                                for (int ng = 0; ng < NG; ++ng) {
+                                    const bool col_ok = 8 * ng + g < C2;
+#pragma unroll
+                                    for (int j = 0; j < KU; ++j) {
+                                        uint4 q = make_uint4(0, 0, 0, 0);
+                                        if (col_ok)
+                                            q = *reinterpret_cast<const uint4*>(ub + static_cast<size_t>(j) * C2 * 64 +
+                                                                                ng * 8 * 64);
+                                        b[ng][4 * j] = q.x, b[ng][4 * j + 1] = q.y, b[ng][4 * j + 2] = q.z,
+                                        b[ng][4 * j + 3] = q.w;
+                                    }
+                                }
+                                if constexpr (kI8) {
+#pragma unroll
+                                    for (int jj = 0; jj < 4; ++jj) {
+                                        uint32_t a0, a1, a2, a3;
+                                        i8x4_to_h2x2(u4_get(ring[d][0][l], jj), a0, a2);
+                                        i8x4_to_h2x2(u4_get(ring[d][1][l], jj), a1, a3);
+#pragma unroll
+                                        for (int ng = 0; ng < NG; ++ng)
+                                            mma_16816(acc[ng], a0, a1, a2, a3, b[ng][2 * jj], b[ng][2 * jj + 1], false);
+                                    }
+                                } else {
+#pragma unroll
+                                    for (int jj = 0; jj < 2; ++jj) {
+                                        const uint32_t a0 = u4_get(ring[d][0][l], 2 * jj), a2 = u4_get(ring[d][0][l], 2 * jj + 1);
+                                        const uint32_t a1 = u4_get(ring[d][1][l], 2 * jj), a3 = u4_get(ring[d][1][l], 2 * jj + 1);
+#pragma unroll
+                                        for (int ng = 0; ng < NG; ++ng)
+                                            mma_16816(acc[ng], a0, a1, a2, a3, b[ng][2 * jj], b[ng][2 * jj + 1], kBF);
+                                    }
+                                }
+                            } else {
+                                // Four column groups: B fragments loaded per MMA (8 bytes) to bound registers.
+#pragma unroll
+                                for (int jj = 0; jj < (kI8 ? 4 : 2); ++jj) {
+                                    uint32_t a0, a1, a2, a3;
+                                    if constexpr (kI8) {
+                                        i8x4_to_h2x2(u4_get(ring[d][0][l], jj), a0, a2);
+                                        i8x4_to_h2x2(u4_get(ring[d][1][l], jj), a1, a3);
+                                    } else {
+                                        a0 = u4_get(ring[d][0][l], 2 * jj), a2 = u4_get(ring[d][0][l], 2 * jj + 1);
+                                        a1 = u4_get(ring[d][1][l], 2 * jj), a3 = u4_get(ring[d][1][l], 2 * jj + 1);
+                                    }
+                                    const char* jb = ub + static_cast<size_t>(kI8 ? (jj >> 1) : 0) * C2 * 64 +
+                                                     (kI8 ? (jj & 1) : jj) * 8;
+#pragma unroll
+                                    for (int ng = 0; ng < NG; ++ng) {
+                                        uint2 q = make_uint2(0, 0);
+                                        if (8 * ng + g < C2) q = *reinterpret_cast<const uint2*>(jb + ng * 8 * 64);
+                                        mma_16816(acc[ng], a0, a1, a2, a3, q.x, q.y, kBF);
+                                    }
+                                }
+                            }
+                        }
+                        issue_piece(ring[d], l);  // piece l of this slot is free again: refill it now
+                    }
+                    if (kI8 && c_q == 0) rs2[0] = sring[d][0], rs2[1] = sring[d][1];
+                    issue_finish(sring[d]);
+                    if (++c_q == nq) {
 #pragma unroll
                         for (int ng = 0; ng < NG; ++ng) {
-                            const bool col_ok = 8 * ng + g < C2;
-#pragma unroll
-                            for (int j = 0; j < MmaPiece<WT>::kUnits; ++j) {
-                                uint4 q = make_uint4(0, 0, 0, 0);
-                                if (col_ok)
-                                    q = *reinterpret_cast<const uint4*>(
-                                        xs + static_cast<size_t>(piece * MmaPiece<WT>::kUnits + j) * C2 * 64 +
-                                        ng * 8 * 64 + col_off);
-                                b[ng][4 * j] = q.x, b[ng][4 * j + 1] = q.y, b[ng][4 * j + 2] = q.z, b[ng][4 * j + 3] = q.w;
-                            }
+                            red[c_i & 1][warp][ng][lane] =
+                                make_float2((acc[ng][0] + acc[ng][1]) * rs2[0], (acc[ng][2] + acc[ng][3]) * rs2[1]);
+                            acc[ng][0] = acc[ng][1] = acc[ng][2] = acc[ng][3] = 0.f;
                         }
-                        if constexpr (kI8) {
-#pragma unroll
-                            for (int jj = 0; jj < 4; ++jj) {
-                                uint32_t a0, a1, a2, a3;
-                                i8x4_to_h2x2(u4_get(ring[d][0][l], jj), a0, a2);
-                                i8x4_to_h2x2(u4_get(ring[d][1][l], jj), a1, a3);
-#pragma unroll
-                                for (int ng = 0; ng < NG; ++ng)
-                                    mma_16816(acc[ng], a0, a1, a2, a3, b[ng][2 * jj], b[ng][2 * jj + 1], false);
-                            }
-                        } else {
-#pragma unroll
-                            for (int jj = 0; jj < 2; ++jj) {
-                                const uint32_t a0 = u4_get(ring[d][0][l], 2 * jj), a2 = u4_get(ring[d][0][l], 2 * jj + 1);
-                                const uint32_t a1 = u4_get(ring[d][1][l], 2 * jj), a3 = u4_get(ring[d][1][l], 2 * jj + 1);
-#pragma unroll
-                                for (int ng = 0; ng < NG; ++ng)
-                                    mma_16816(acc[ng], a0, a1, a2, a3, b[ng][2 * jj], b[ng][2 * jj + 1], kBF);
-                            }
-                        }
+                        cluster_barrier();
+                        finish_tile(c_i);
+                        c_q = 0;
+                        ++c_i;
                     }
-                    issue_piece(ring[d], l);  // piece l of this slot is free again: refill it now
-                }
-                if (kI8 && c_q == 0) rs2[0] = sring[d][0], rs2[1] = sring[d][1];
-                issue_finish(sring[d]);
-                if (++c_q == nq) {
-#pragma unroll
-                    for (int ng = 0; ng < NG; ++ng) {
-                        red[c_i & 1][warp][ng][lane] =
-                            make_float2((acc[ng][0] + acc[ng][1]) * rs2[0], (acc[ng][2] + acc[ng][3]) * rs2[1]);
-                        acc[ng][0] = acc[ng][1] = acc[ng][2] = acc[ng][3] = 0.f;
-                    }
-                    __syncthreads();
-                    if (warp == reducer(c_i)) reduce_tile(c_i, blockIdx.x + c_i * gridDim.x);
-                    c_q = 0;
-                    ++c_i;
                 }
             }
         }
+    }
+    if (S > 1) {
+        // The last tile's partials are complete after this barrier; the second keeps every CTA's shared
+        // memory alive until rank 0 has read it.
+        cluster.sync();
+        if (ks == 0 && my_tiles > 0 && warp == reducer(my_tiles - 1)) cluster_epilogue(my_tiles - 1);
+        cluster.sync();
     }
 }
 
@@ -924,10 +1015,24 @@ l0b_status launch_vec(l0b_device* dev, cudaStream_t stream, int sm_count, const 
     return launch_on(dev, stream, kernel, dim3(grid), dim3(kThreads), smem, p);
 }
 
+// Split count S (cluster size) for the tensor-core kernel: the smallest of 1, 2, 4, 8 whose K slice of
+// hi/lo activations fits the shared-memory budget (100 KB keeps two CTAs per SM); 0 = does not fit.
+template <typename WT>
+int mma_splits(const GemvParams& p, int rows) {
+    const long long npieces = p.K / MmaPiece<WT>::kK;
+    for (int s = 1; s <= 8; s *= 2) {
+        const long long slice = (npieces + s - 1) / s * MmaPiece<WT>::kK;  // largest slice, in k
+        if (4ll * rows * slice <= 100 * 1024) return s;
+    }
+    const long long slice8 = (npieces + 7) / 8 * MmaPiece<WT>::kK;
+    return 4ll * rows * slice8 <= 200 * 1024 ? 8 : 0;
+}
+
 template <typename WT, int NG>
-l0b_status launch_mma(l0b_device* dev, cudaStream_t stream, int sm_count, const GemvParams& p) {
+l0b_status launch_mma(l0b_device* dev, cudaStream_t stream, int sm_count, const GemvParams& p, int S) {
     auto kernel = gemv_mma_kernel<WT, NG>;
-    const size_t smem = 4ull * p.M * p.K;  // hi and lo 16-bit copies of each activation row
+    const long long npieces = p.K / MmaPiece<WT>::kK;
+    const size_t smem = 4ull * p.M * ((npieces + S - 1) / S) * MmaPiece<WT>::kK;  // largest slice
     static bool configured = false;
     if (!configured) {
         cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
@@ -937,19 +1042,41 @@ l0b_status launch_mma(l0b_device* dev, cudaStream_t stream, int sm_count, const 
     const bool swiglu = p.epi == EPI_SWIGLU;
     const int units = swiglu ? p.N / 2 : p.N;
     const int ntiles = (units + (swiglu ? 7 : 15)) / (swiglu ? 8 : 16);
-    const int cap = sm_count * resident_ctas(reinterpret_cast<const void*>(kernel), smem);
-    return launch_on(dev, stream, kernel, dim3(ntiles < cap ? ntiles : cap), dim3(kThreads), smem, p);
+    const int cap = sm_count * resident_ctas(reinterpret_cast<const void*>(kernel), smem) / S;
+    const dim3 grid(ntiles < cap ? ntiles : (cap > 0 ? cap : 1), S);
+    if (dev) return dev->launch_cluster(kernel, grid, dim3(kThreads), smem, S, p);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    if (S > 1) {
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = 1;
+        attr[0].val.clusterDim.y = S;
+        attr[0].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+    }
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, p);
+    if (e != cudaSuccess) return fail(L0B_ERR_CUDA, "kernel launch failed: %s", cudaGetErrorString(e));
+    add_launches(1);
+    return L0B_OK;
 }
 
 // The tensor-core kernel takes 16-bit weights and per-row-scaled int8, K in whole pieces (64 / 32 k),
-// and up to 8 activation rows whose split copies fit in 200 KB of shared memory.
+// and up to 8 activation rows per pass, split over a cluster of up to 8 CTAs along K when the
+// activations of one CTA would not fit its shared memory. Returns the split count, 0 = does not apply.
 template <typename WT>
-bool mma_applies(const GemvParams& p, int rows) {
+int mma_applies(const GemvParams& p, int rows) {
     if constexpr (sizeof(WT) > 2) {
-        return false;
+        return 0;
     } else {
-        return g_gemv_mma && p.K % MmaPiece<WT>::kK == 0 && reinterpret_cast<uintptr_t>(p.w) % 16 == 0 &&
-               (sizeof(WT) != 1 || p.group >= p.K) && rows <= 8 && 4ll * rows * p.K <= 200 * 1024;
+        if (!(g_gemv_mma && p.K % MmaPiece<WT>::kK == 0 && reinterpret_cast<uintptr_t>(p.w) % 16 == 0 &&
+              (sizeof(WT) != 1 || p.group >= p.K) && rows <= 8))
+            return 0;
+        return mma_splits<WT>(p, rows);
     }
 }
 
@@ -960,9 +1087,18 @@ l0b_status launch_typed(l0b_device* dev, cudaStream_t stream, int sm_count, Gemv
     const bool vec_ok = (p.K % VEC == 0) && (reinterpret_cast<uintptr_t>(p.w) % 16 == 0) &&
                         (sizeof(WT) != 1 || (p.group % 16 == 0 && p.K % p.group == 0));
     const int M = p.M;
-    for (int m0 = 0; m0 < M; m0 += 8) {
+    for (int m0 = 0; m0 < M;) {
         GemvParams q = p;
+        // Passes of up to 8 rows. (Sixteen-row passes on four B-column groups fit shared memory only
+        // as 4-way split-K at K = 3584, where the per-tile cluster barrier dominates: measured slower than
+        // two 8-row passes, so the dispatcher does not form them.)
         const int mr = M - m0 < 8 ? M - m0 : 8;
+        int splits = 0;
+        if constexpr (sizeof(WT) <= 2) {
+            GemvParams t8 = p;
+            t8.M = mr;
+            splits = mma_applies<WT>(t8, mr);
+        }
         q.M = mr;
         q.x = static_cast<const char*>(p.x) + static_cast<size_t>(m0) * p.x_ld * dtype_size((l0b_dtype)p.x_dtype);
         for (int s = 0; s < q.nseg; ++s) {
@@ -971,10 +1107,11 @@ l0b_status launch_typed(l0b_device* dev, cudaStream_t stream, int sm_count, Gemv
             q.seg[s].out = static_cast<char*>(q.seg[s].out) + static_cast<size_t>(m0) * q.seg[s].ld * es;
         }
         if (q.argmax) q.argmax += m0;
+        m0 += mr;
         if constexpr (sizeof(WT) <= 2) {
-            if (mma_applies<WT>(q, mr)) {
-                if (mr <= 4) L0B_TRY((launch_mma<WT, 1>(dev, stream, sm_count, q)));
-                else L0B_TRY((launch_mma<WT, 2>(dev, stream, sm_count, q)));
+            if (splits) {
+                if (mr <= 4) L0B_TRY((launch_mma<WT, 1>(dev, stream, sm_count, q, splits)));
+                else L0B_TRY((launch_mma<WT, 2>(dev, stream, sm_count, q, splits)));
                 continue;
             }
         }

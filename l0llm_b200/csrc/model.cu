@@ -62,7 +62,8 @@ struct l0b_model {
     int* out_tokens = nullptr;  // [max_seq * batch_cap]
     int* step_idx = nullptr;
     unsigned long long* keys = nullptr;  // [batch_cap]
-    int cluster_splits = 1;  // CTAs per cluster of the decode attention (splits merged on chip)
+    int prefill_seq = 0;           // cache row (sequence) the prefill path writes
+    std::vector<int> seq_pos;      // host mirror of each sequence's next position
     // Host state.
     int* host_io = nullptr;       // pinned [2 * batch_cap]
     float* host_logits = nullptr; // pinned [batch_cap * vocab]
@@ -271,6 +272,17 @@ struct Synth {
 
 namespace {
 
+// Cache row of the sequence being prefilled (caches are [batch_cap, max_seq, kv_dim]).
+void* seq_cache(l0b_model* m, void* cache) {
+    const size_t off = static_cast<size_t>(m->prefill_seq) * m->max_seq * m->kvdim * dtype_size(static_cast<l0b_dtype>(m->cache_dtype));
+    return static_cast<char*>(cache) + off;
+}
+
+// Cluster size of the decode attention for `rows` sequences in this step.
+int cluster_splits(l0b_model* m, int rows) {
+    return attention_cluster_splits(m->max_seq, rows * m->nkv * ((m->nh / m->nkv + 7) / 8), m->dev->sm_count);
+}
+
 GemvParams linear_params(const ModelMatrix& w, int m_rows, const void* x, long long x_ld) {
     GemvParams p = {};
     p.w = w.w;
@@ -339,13 +351,17 @@ l0b_status record_layer_fused(l0b_model* m, int li, int rows, bool decode, int p
         a.cache_bstride = static_cast<long long>(m->max_seq) * m->kvdim;
         a.positions = m->pos;
         a.chunk = 32;
-        L0B_TRY(attention_cluster_launch(m->dev, a, rows, m->cluster_splits));
+        L0B_TRY(attention_cluster_launch(m->dev, a, rows, cluster_splits(m, rows)));
     } else {
         // Prefill: rotate and store the whole chunk first (queries attend to each other's keys).
         L0B_TRY(k_rope(m->dev, m->qkv, m->qkv + m->qdim, m->prompt_pos, m->inv_freq, m->hd, m->nh, m->nkv,
                        m->attn_scale, m->rot, rows, m->qkv_w, m->qkv_w));
-        L0B_TRY(k_kv_store(m->dev, m->qkv + m->qdim, m->qkv + m->qdim + m->kvdim, L.kc, L.vc, m->cache_dtype, pos0,
+        void* kc = seq_cache(m, L.kc);
+        void* vc = seq_cache(m, L.vc);
+        L0B_TRY(k_kv_store(m->dev, m->qkv + m->qdim, m->qkv + m->qdim + m->kvdim, kc, vc, m->cache_dtype, pos0,
                            m->kvdim, rows, m->qkv_w));
+        a.kc = kc;
+        a.vc = vc;
         a.rope = 0;
         a.store_new = 0;
         a.cache_bstride = 0;
@@ -400,12 +416,15 @@ l0b_status record_layer_reference(l0b_model* m, int li, int rows, bool decode, i
     L0B_TRY(emit(m, li, "v", m->vb, m->kvdim));
     const int* positions = decode ? m->pos : m->prompt_pos;
     L0B_TRY(k_rope(d, m->qb, m->kb, positions, m->inv_freq, m->hd, m->nh, m->nkv, m->attn_scale, m->rot, rows));
-    L0B_TRY(k_kv_store(d, m->kb, m->vb, L.kc, L.vc, m->cache_dtype, pos0, m->kvdim, rows));
+    // Decode on this path is single-sequence (row 0); prefill writes the sequence being ingested.
+    void* kc = decode ? L.kc : seq_cache(m, L.kc);
+    void* vc = decode ? L.vc : seq_cache(m, L.vc);
+    L0B_TRY(k_kv_store(d, m->kb, m->vb, kc, vc, m->cache_dtype, pos0, m->kvdim, rows));
     AttnParams a = {};
     a.q = m->qb;
     a.q_bstride = m->qdim;
-    a.kc = L.kc;
-    a.vc = L.vc;
+    a.kc = kc;
+    a.vc = vc;
     a.cache_dtype = m->cache_dtype;
     a.kv_dim = m->kvdim;
     a.out = m->attn;
@@ -418,7 +437,7 @@ l0b_status record_layer_reference(l0b_model* m, int li, int rows, bool decode, i
     a.pos_step = 1;
     if (decode) {
         a.chunk = 32;
-        L0B_TRY(attention_cluster_launch(d, a, rows, m->cluster_splits));
+        L0B_TRY(attention_cluster_launch(d, a, rows, cluster_splits(m, rows)));
     } else {
         a.chunk = (pos0 + rows + 31) / 32 * 32;
         a.max_splits = 1;
@@ -444,8 +463,9 @@ l0b_status record_layer_reference(l0b_model* m, int li, int rows, bool decode, i
     return emit(m, li, "output", m->hidden, m->h);
 }
 
-// Final norm, LM head and greedy argmax for `rows` rows starting at hidden row `row0`.
-l0b_status record_head(l0b_model* m, int row0, int rows, int advance) {
+// Final norm, LM head and greedy argmax for `rows` rows starting at hidden row `row0`; the greedy token,
+// position and argmax key of row r go to sequence slot seq0 + r.
+l0b_status record_head(l0b_model* m, int row0, int rows, int advance, int seq0 = 0) {
     const l0b_model_config& c = m->cfg;
     l0b_device* d = m->dev;
     if (m->fused && !m->probe) {
@@ -453,7 +473,7 @@ l0b_status record_head(l0b_model* m, int row0, int rows, int advance) {
         p.norm_w = m->final_norm;
         p.eps = c.rms_norm_eps;
         p.epi = EPI_ARGMAX;
-        p.argmax = m->keys;
+        p.argmax = m->keys + seq0;
         p.seg[0] = {m->logits, nullptr, m->vocab, m->vocab};
         L0B_TRY(gemv(m, m->lm_head, p));
     } else {
@@ -467,12 +487,13 @@ l0b_status record_head(l0b_model* m, int row0, int rows, int advance) {
         L0B_TRY(k_rmsnorm(d, const_cast<float*>(src), nullptr, m->final_norm, m->normed, c.rms_norm_eps, m->h, rows, 0));
         GemvParams p = linear_params(m->lm_head, rows, m->normed, m->h);
         p.epi = EPI_ARGMAX;
-        p.argmax = m->keys;
+        p.argmax = m->keys + seq0;
         p.seg[0] = {m->logits, nullptr, m->vocab, m->vocab};
         L0B_TRY(gemv(m, m->lm_head, p));
     }
-    return d->launch(step_finish_kernel, dim3(1), dim3(rows < 32 ? 32 : ((rows + 31) / 32) * 32), 0, m->keys,
-                     m->sampled, m->tok, m->pos, m->out_tokens, m->step_idx, rows, advance);
+    return d->launch(step_finish_kernel, dim3(1), dim3(rows < 32 ? 32 : ((rows + 31) / 32) * 32), 0, m->keys + seq0,
+                     m->sampled + seq0, m->tok + seq0, m->pos + seq0, seq0 ? nullptr : m->out_tokens, m->step_idx,
+                     rows, advance);
 }
 
 // One decode step for `rows` sequences whose token ids and positions are already in tok/pos.
@@ -494,12 +515,13 @@ l0b_status record_decode_step(l0b_model* m, int rows) {
 l0b_status record_prefill_chunk(l0b_model* m, int count, int pos0, bool head) {
     l0b_device* d = m->dev;
     L0B_TRY(d->launch(step_begin_kernel, dim3(grid_for(static_cast<long long>(count) * m->h, d->sm_count)),
-                      dim3(256), 0, m->prompt_tok, m->embed, m->hidden, m->h, count, m->vocab, m->keys, 1));
+                      dim3(256), 0, m->prompt_tok, m->embed, m->hidden, m->h, count, m->vocab,
+                      m->keys + m->prefill_seq, 1));
     for (int li = 0; li < static_cast<int>(m->layers.size()); ++li) {
         if (m->fused && !m->probe) L0B_TRY(record_layer_fused(m, li, count, false, pos0));
         else L0B_TRY(record_layer_reference(m, li, count, false, pos0));
     }
-    if (head) L0B_TRY(record_head(m, count - 1, 1, 0));
+    if (head) L0B_TRY(record_head(m, count - 1, 1, 0, m->prefill_seq));
     return L0B_OK;
 }
 
@@ -558,15 +580,18 @@ l0b_status step(l0b_model* m, int token, int position) {
 }
 
 // LlmModel.IngestPrompt (L/LlmModel.cs:320-333): chunks of kMaxRows tokens; a 1-token chunk is a Step.
-l0b_status ingest_prompt(l0b_model* m, const int32_t* ids, int count) {
+// `seq` selects the cache row (sequence) for a batched model; sequences other than 0 always take the
+// chunk path, whose head writes that sequence's greedy token and next position.
+l0b_status ingest_prompt(l0b_model* m, const int32_t* ids, int count, int seq = 0) {
     const int chunk = kMaxRows < m->cap ? kMaxRows : m->cap;
+    m->prefill_seq = seq;
     for (int start = 0; start < count; start += chunk) {
         const int n = count - start < chunk ? count - start : chunk;
         const bool last = start + n == count;
         for (int i = 0; i < n; ++i)
             L0B_REQUIRE(ids[start + i] >= 0 && ids[start + i] < m->vocab, L0B_ERR_OUT_OF_RANGE,
                         "Vocabulary has %d tokens (got %d).", m->vocab, ids[start + i]);
-        if (n == 1) {
+        if (n == 1 && seq == 0) {
             L0B_TRY(step(m, ids[start], start));
             continue;
         }
@@ -578,11 +603,22 @@ l0b_status ingest_prompt(l0b_model* m, const int32_t* ids, int count) {
                                        m->dev->stream));
         // The next decode step continues from the end of the prompt.
         if (last) {
-            const int next_pos = start + n;
-            L0B_TRY(write_io(m, 1, ids + start + n - 1, &next_pos));
+            // Only this sequence's slot: the others keep their device-side token and position.
+            m->host_io[seq] = ids[start + n - 1];
+            m->host_io[m->batch_cap + seq] = start + n;
+            L0B_CHECK_CUDA(cudaMemcpyAsync(m->tok + seq, &m->host_io[seq], sizeof(int), cudaMemcpyHostToDevice,
+                                           m->dev->stream));
+            L0B_CHECK_CUDA(cudaMemcpyAsync(m->pos + seq, &m->host_io[m->batch_cap + seq], sizeof(int),
+                                           cudaMemcpyHostToDevice, m->dev->stream));
         }
-        L0B_TRY(run_recorded(m, [&] { return record_prefill_chunk(m, n, start, last); }));
+        l0b_status st = run_recorded(m, [&] { return record_prefill_chunk(m, n, start, last); });
+        if (st != L0B_OK) {
+            m->prefill_seq = 0;
+            return st;
+        }
     }
+    m->prefill_seq = 0;
+    m->seq_pos[seq] = count;
     return L0B_OK;
 }
 
@@ -740,6 +776,7 @@ L0B_API l0b_status l0b_model_config_init(l0b_model_config* c) {
     c->q8_group = 32;
     c->tp_size = 1;
     c->tp_rank = 0;
+    c->max_batch = 1;
     return L0B_OK;
 }
 
@@ -797,7 +834,10 @@ L0B_API l0b_status l0b_model_create(l0b_device* dev, l0b_suite* suite, const l0b
     m->cache_dtype = c.kv_dtype;
     m->softmax_scale = static_cast<float>(1.0 / std::sqrt(static_cast<double>(c.head_dim)));
     m->fused = !c.qk_norm;
-    m->batch_cap = 1;
+    m->batch_cap = c.max_batch < 1 ? 1 : c.max_batch;
+    L0B_REQUIRE(m->batch_cap <= kMaxRows, L0B_ERR_OUT_OF_RANGE, "max_batch %d exceeds %d sequences", c.max_batch,
+                kMaxRows);
+    m->seq_pos.assign(m->batch_cap, 0);
     m->cap = kMaxRows;
     L0B_CHECK_CUDA(cudaSetDevice(dev->index));
 
@@ -871,8 +911,6 @@ L0B_API l0b_status l0b_model_create(l0b_device* dev, l0b_suite* suite, const l0b
     L0B_TRY(m->alloc(&m->out_tokens, static_cast<size_t>(max_seq_len + 1) * m->batch_cap));
     L0B_TRY(m->alloc(&m->step_idx, 1));
     L0B_TRY(m->alloc(&m->keys, m->batch_cap));
-    m->cluster_splits = attention_cluster_splits(
-        max_seq_len, m->batch_cap * m->nkv * ((m->nh / m->nkv + 7) / 8), dev->sm_count);
     L0B_CHECK_CUDA(cudaMallocHost(&m->host_io, sizeof(int) * 2 * m->batch_cap));
     L0B_CHECK_CUDA(cudaMallocHost(&m->host_logits, sizeof(float) * m->batch_cap * m->vocab));
     L0B_CHECK_CUDA(cudaStreamSynchronize(dev->stream));
@@ -1121,6 +1159,85 @@ L0B_API l0b_status l0b_model_decode_greedy_device(l0b_model* m, int32_t steps, i
     L0B_CHECK_CUDA(cudaStreamSynchronize(d->stream));
     return L0B_OK;
     GUARD_END
+}
+
+L0B_API l0b_status l0b_model_prefill_sequence(l0b_model* m, int32_t seq, const int32_t* ids, int32_t count,
+                                              float* logits) {
+    GUARD_BEGIN
+    L0B_REQUIRE(m && ids, L0B_ERR_ARGUMENT, "null argument");
+    L0B_REQUIRE(seq >= 0 && seq < m->batch_cap, L0B_ERR_OUT_OF_RANGE, "sequence %d outside the %d-sequence batch",
+                seq, m->batch_cap);
+    L0B_REQUIRE(count > 0, L0B_ERR_ARGUMENT, "The prompt must contain at least one token.");
+    L0B_REQUIRE(count <= m->max_seq, L0B_ERR_ARGUMENT, "Prompt of %d tokens exceeds the %d-token cache.", count,
+                m->max_seq);
+    L0B_TRY(ingest_prompt(m, ids, count, seq));
+    if (seq == 0) m->position = count;
+    return read_logits(m, logits, 1);
+    GUARD_END
+}
+
+L0B_API l0b_status l0b_model_decode_batch(l0b_model* m, const int32_t* tokens, const int32_t* positions,
+                                          int32_t count, float* logits) {
+    GUARD_BEGIN
+    L0B_REQUIRE(m && tokens && positions, L0B_ERR_ARGUMENT, "null argument");
+    L0B_REQUIRE(count > 0 && count <= m->batch_cap, L0B_ERR_OUT_OF_RANGE, "%d sequences (batch capacity %d)", count,
+                m->batch_cap);
+    L0B_REQUIRE(m->fused && !m->probe, L0B_ERR_UNSUPPORTED, "batched decode needs the fused path");
+    for (int b = 0; b < count; ++b) {
+        L0B_REQUIRE(tokens[b] >= 0 && tokens[b] < m->vocab, L0B_ERR_OUT_OF_RANGE, "Vocabulary has %d tokens (got %d).",
+                    m->vocab, tokens[b]);
+        L0B_REQUIRE(positions[b] >= 0 && positions[b] < m->max_seq, L0B_ERR_OUT_OF_RANGE,
+                    "Cache holds %d positions (got %d).", m->max_seq, positions[b]);
+    }
+    L0B_TRY(write_io(m, count, tokens, positions));
+    L0B_TRY(run_recorded(m, [&] { return record_decode_step(m, count); }));
+    for (int b = 0; b < count; ++b) m->seq_pos[b] = positions[b] + 1;
+    if (count >= 1) m->position = positions[0] + 1;
+    return read_logits(m, logits, count);
+    GUARD_END
+}
+
+L0B_API l0b_status l0b_model_decode_greedy_device_batch(l0b_model* m, int32_t steps, int32_t count, int32_t* out) {
+    GUARD_BEGIN
+    L0B_REQUIRE(m, L0B_ERR_ARGUMENT, "model is null");
+    L0B_REQUIRE(steps >= 0, L0B_ERR_OUT_OF_RANGE, "steps must be non-negative");
+    L0B_REQUIRE(count > 0 && count <= m->batch_cap, L0B_ERR_OUT_OF_RANGE, "%d sequences (batch capacity %d)", count,
+                m->batch_cap);
+    L0B_REQUIRE(m->fused, L0B_ERR_UNSUPPORTED, "device-resident decode needs the fused path");
+    for (int b = 0; b < count; ++b)
+        L0B_REQUIRE(m->seq_pos[b] + steps <= m->max_seq, L0B_ERR_INVALID_OPERATION,
+                    "Sequence %d: the %d-token KV cache is full.", b, m->max_seq);
+    if (steps == 0) return L0B_OK;
+    l0b_device* d = m->dev;
+    L0B_CHECK_CUDA(cudaSetDevice(d->index));
+    // Each sequence's token and position are already on the device (its prefill head or last step).
+    L0B_CHECK_CUDA(cudaMemsetAsync(m->step_idx, 0, sizeof(int), d->stream));
+    for (int i = 0; i < steps; ++i) {
+        d->recording = true;
+        d->log_used = 0;
+        l0b_status s = record_decode_step(m, count);
+        if (s != L0B_OK) {
+            d->abort_recording();
+            return s;
+        }
+        L0B_TRY(d->end_recording());
+    }
+    for (int b = 0; b < count; ++b) m->seq_pos[b] += steps;
+    m->position = m->seq_pos[0];
+    if (out) {
+        L0B_CHECK_CUDA(cudaMemcpyAsync(out, m->out_tokens, sizeof(int) * steps * count, cudaMemcpyDeviceToHost,
+                                       d->stream));
+    }
+    L0B_CHECK_CUDA(cudaStreamSynchronize(d->stream));
+    return L0B_OK;
+    GUARD_END
+}
+
+L0B_API l0b_status l0b_model_sequence_position(l0b_model* m, int32_t seq, int32_t* position) {
+    L0B_REQUIRE(m && position, L0B_ERR_ARGUMENT, "null argument");
+    L0B_REQUIRE(seq >= 0 && seq < m->batch_cap, L0B_ERR_OUT_OF_RANGE, "sequence %d", seq);
+    *position = m->seq_pos[seq];
+    return L0B_OK;
 }
 
 L0B_API l0b_status l0b_model_position(l0b_model* m, int32_t* position) {

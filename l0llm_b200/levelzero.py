@@ -84,7 +84,7 @@ class ModelConfig(C.Structure):
         ("rope_high_freq_factor", C.c_double), ("rope_beta_fast", C.c_double), ("rope_beta_slow", C.c_double),
         ("rope_attention_factor", C.c_double), ("rope_mscale", C.c_double), ("rope_mscale_all_dim", C.c_double),
         ("rope_truncate", C.c_int32), ("partial_rotary_factor", C.c_double), ("kv_dtype", C.c_int32),
-        ("q8_group", C.c_int32), ("tp_size", C.c_int32), ("tp_rank", C.c_int32),
+        ("q8_group", C.c_int32), ("tp_size", C.c_int32), ("tp_rank", C.c_int32), ("max_batch", C.c_int32),
     ]
 
 
@@ -170,6 +170,10 @@ def load_library() -> C.CDLL:
         "l0b_linear_tc": (i32, [vp, vp, i32, i32, i32, vp, vp, vp, f32, i32, vp, vp]),
         "l0b_device_error_status": (i32, [vp, C.POINTER(i32)]),
         "l0b_set_gemv_tensor_cores": (i32, [i32]),
+        "l0b_model_prefill_sequence": (i32, [vp, i32, vp, i32, vp]),
+        "l0b_model_decode_batch": (i32, [vp, vp, vp, i32, vp]),
+        "l0b_model_decode_greedy_device_batch": (i32, [vp, i32, i32, vp]),
+        "l0b_model_sequence_position": (i32, [vp, i32, C.POINTER(i32)]),
         "l0b_attention_decode_noalloc": (i32, [vp, vp, vp, vp, i32, vp, i32, i32, i32, i32, i32]),
         "l0b_model_config_init": (i32, [C.POINTER(ModelConfig)]),
         "l0b_rope_frequencies": (i32, [C.POINTER(ModelConfig), vp, i32, C.POINTER(i32), C.POINTER(f32)]),
@@ -633,6 +637,32 @@ class LlmModel:
         out = np.zeros(max(1, steps), np.int32)
         check(load_library().l0b_model_decode_greedy_device(self.handle, steps, _p(out)))
         return out[:steps]
+
+    # Batched sequences (cfg.max_batch > 1): sequence `seq` owns KV-cache row seq.
+    def PrefillSequence(self, seq: int, prompt_ids, want_logits: bool = True) -> np.ndarray | None:
+        ids = np.ascontiguousarray(prompt_ids, np.int32)
+        logits = np.zeros(self.vocab, np.float32) if want_logits else None
+        check(load_library().l0b_model_prefill_sequence(self.handle, seq, _p(ids), ids.size,
+                                                         _p(logits) if logits is not None else None))
+        return logits
+
+    def DecodeBatch(self, tokens, positions, want_logits: bool = True) -> np.ndarray | None:
+        t = np.ascontiguousarray(tokens, np.int32)
+        p = np.ascontiguousarray(positions, np.int32)
+        logits = np.zeros((t.size, self.vocab), np.float32) if want_logits else None
+        check(load_library().l0b_model_decode_batch(self.handle, _p(t), _p(p), t.size,
+                                                     _p(logits) if logits is not None else None))
+        return logits
+
+    def decode_greedy_device_batch(self, steps: int, count: int) -> np.ndarray:
+        out = np.zeros((max(1, steps), count), np.int32)
+        check(load_library().l0b_model_decode_greedy_device_batch(self.handle, steps, count, _p(out)))
+        return out[:steps]
+
+    def SequencePosition(self, seq: int) -> int:
+        v = C.c_int32()
+        check(load_library().l0b_model_sequence_position(self.handle, seq, C.byref(v)))
+        return v.value
 
     @property
     def Position(self) -> int:

@@ -1,0 +1,72 @@
+"""Batched decoding of independent sequences (cfg.max_batch > 1) against the same sequences decoded alone.
+
+Each sequence owns one KV-cache row. Prefill fills row `seq`; a batched step decodes rows 0..count-1 at
+their own positions. The reference has no multi-sequence decode (its engine serialises requests), so
+the check is consistency: sequence b decoded in a batch must give the logits and greedy tokens it gets
+when decoded alone by a single-sequence model with the same weights.
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+CFG = dict(hidden_size=256, intermediate_size=640, num_layers=2, num_attention_heads=8, num_key_value_heads=2,
+           head_dim=64, vocab_size=1000, max_position_embeddings=4096, rms_norm_eps=1e-6, rope_theta=1e6,
+           attention_bias=1, q8_group=0)
+
+
+def _model(lz, device, suite, batch, precision):
+    cfg = lz.model_config(kv_dtype=lz.F16, max_batch=batch, **CFG)
+    m = lz.LlmModel(device, suite, cfg, 96, precision)
+    m.init_synthetic(7, 0.02, 1e-3, 2e-2) if precision == "int8" else m.init_synthetic(7, 0.05, 0.0, 0.0)
+    return m
+
+
+def _prompts(n):
+    rng = np.random.default_rng(11)
+    return [rng.integers(0, CFG["vocab_size"], 3 + (7 * i) % 61).astype(np.int32) for i in range(n)]
+
+
+@pytest.mark.parametrize("precision", ["int8", "float16"])
+@pytest.mark.parametrize("batch", [5, 16])
+def test_batched_logits_match_single_sequences(lz, device, suite, precision, batch):
+    prompts = _prompts(batch)
+    with _model(lz, device, suite, batch, precision) as mb:
+        first = [mb.PrefillSequence(s, p) for s, p in enumerate(prompts)]
+        assert [mb.SequencePosition(s) for s in range(batch)] == [len(p) for p in prompts]
+        toks = np.array([int(np.argmax(f)) for f in first], np.int32)
+        pos = np.array([len(p) for p in prompts], np.int32)
+        got = mb.DecodeBatch(toks, pos)
+    with _model(lz, device, suite, 1, precision) as ms:
+        for s, p in enumerate(prompts):
+            want0 = ms.Prefill(p)
+            np.testing.assert_allclose(first[s], want0, rtol=1e-4, atol=1e-4 * np.abs(want0).max())
+            want = ms.Decode(int(toks[s]))
+            scale = np.abs(want).max()
+            err = np.abs(got[s] - want).max()
+            assert err <= 2e-3 * scale, f"sequence {s}: max err {err} (scale {scale})"
+
+
+def test_batched_device_greedy_matches_single(lz, device, suite):
+    batch, steps = 4, 6
+    prompts = _prompts(batch)
+    with _model(lz, device, suite, batch, "int8") as mb:
+        for s, p in enumerate(prompts):
+            mb.PrefillSequence(s, p, want_logits=False)
+        got = mb.decode_greedy_device_batch(steps, batch)
+        assert [mb.SequencePosition(s) for s in range(batch)] == [len(p) + steps for p in prompts]
+    with _model(lz, device, suite, 1, "int8") as ms:
+        for s, p in enumerate(prompts):
+            ms.Prefill(p)
+            want = ms.decode_greedy_device(steps)
+            np.testing.assert_array_equal(got[:, s], want)
+
+
+def test_batched_rejects_out_of_range(lz, device, suite):
+    with _model(lz, device, suite, 2, "int8") as mb:
+        with pytest.raises(lz.ArgumentOutOfRangeException):
+            mb.PrefillSequence(2, np.array([1, 2], np.int32))
+        with pytest.raises(lz.ArgumentOutOfRangeException):
+            mb.DecodeBatch(np.array([1, 2, 3], np.int32), np.array([0, 0, 0], np.int32))

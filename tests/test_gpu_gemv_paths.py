@@ -4,7 +4,9 @@ The tensor-core kernel splits each activation into two f16 halves (hi + residual
 stay within fp32-accumulation distance of the fp64 oracle, far tighter than a plain f16 activation
 would allow. Shapes cover a single piece of K (K = 64, most warps idle), K not a multiple of the
 eight-warp stride (896), the long down-projection row (18944), row counts that leave partial 16-row
-tiles, and 1..8 activation rows (one or two B-column groups).
+tiles, and 1..16 activation rows (one, two or four B-column groups). Row counts whose activations do not
+fit one CTA's shared memory run split-K across a thread-block cluster, which also exchanges the fused
+RMSNorm's sums of squares between the ranks.
 """
 from __future__ import annotations
 
@@ -37,10 +39,8 @@ def _weights(lz, orc, wkind, hf, k):
 
 @pytest.mark.parametrize("wkind", ["f16", "bf16", "i8c"])
 @pytest.mark.parametrize("n,k", [(40, 64), (1000, 896), (4608, 3584), (3584, 18944), (17, 128)])
-@pytest.mark.parametrize("m", [1, 2, 5, 8])
+@pytest.mark.parametrize("m", [1, 2, 5, 8, 13, 16])
 def test_gemv_paths_store(lz, orc, device, suite, path, wkind, n, k, m):
-    if k == 18944 and m > 2:
-        pytest.skip("shape beyond the tensor-core kernel's shared-memory budget")
     rng = np.random.default_rng(n + 3 * k + m)
     hf = ((rng.random((n, k)) * 2 - 1) * 0.05).astype(np.float32)
     x = (rng.standard_normal((m, k)) * 2).astype(np.float32)
@@ -63,7 +63,7 @@ def test_gemv_paths_store(lz, orc, device, suite, path, wkind, n, k, m):
 
 @pytest.mark.parametrize("wkind", ["f16", "i8c"])
 @pytest.mark.parametrize("H,inter", [(896, 4864), (896, 100), (3584, 1000)])
-@pytest.mark.parametrize("m", [1, 3, 8])
+@pytest.mark.parametrize("m", [1, 3, 8, 16])
 def test_gemv_paths_norm_swiglu(lz, orc, device, suite, path, wkind, H, inter, m):
     rng = np.random.default_rng(inter + m + H)
     x = (rng.standard_normal((m, H)) * 3).astype(np.float32)
@@ -85,7 +85,7 @@ def test_gemv_paths_norm_swiglu(lz, orc, device, suite, path, wkind, H, inter, m
     assert np.all(err <= 1e-4 + 1e-4 * np.abs(want)), f"{path}: max err {err.max()}"
 
 
-@pytest.mark.parametrize("m", [1, 2])
+@pytest.mark.parametrize("m", [1, 2, 9, 16])
 def test_gemv_paths_accumulate_down_projection(lz, orc, device, suite, path, m):
     rng = np.random.default_rng(90 + m)
     H, I = 3584, 18944
