@@ -356,6 +356,22 @@ L0B_API l0b_status l0b_linear_tc(l0b_suite* s, l0b_device* d, int32_t m, int32_t
                                  l0b_buffer* w, l0b_buffer* norm_w, float eps, int32_t epilogue, l0b_buffer* bias,
                                  l0b_buffer* out);
 
+/* ------------------------------------------------------------------------------------------ */
+/* Tensor parallelism (one process per GPU, NCCL over NVLink/NVSwitch)                           */
+/* ------------------------------------------------------------------------------------------ */
+
+/* A 128-byte NCCL unique id, made on one rank and handed to the others by the caller (any channel).
+ * No counterpart in the reference (single-GPU); LevelZeroLlmEngine would pass it at start-up. */
+L0B_API l0b_status l0b_comm_unique_id(uint8_t* id, int32_t bytes);
+/* Joins communicator `id` as `rank` of `nranks`, bound to `dev`'s stream. Collective: every rank
+ * calls it. Models created with cfg.tp_size = nranks, cfg.tp_rank = rank take it (l0b_model_create). */
+L0B_API l0b_status l0b_comm_create(l0b_device* dev, const uint8_t* id, int32_t bytes, int32_t nranks, int32_t rank,
+                                   l0b_comm** out);
+L0B_API l0b_status l0b_comm_free(l0b_comm* comm);
+/* In-place sum of the first `count` elements of `buf` over the ranks, on the device stream (recorded
+ * into the current command list when the device is recording). */
+L0B_API l0b_status l0b_comm_allreduce(l0b_comm* comm, l0b_buffer* buf, int64_t count);
+
 /* Process-wide choice of the decode GEMV kernel for shapes both take: 1 (default) = tensor-core
  * mma.sync streaming kernel, 0 = fp32-FMA streaming kernel. Used by tests to cover both; recorded
  * command lists keep the kernel they were recorded with. No counterpart in the reference. */

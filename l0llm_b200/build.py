@@ -68,7 +68,7 @@ def build(force: bool = False, jobs: int | None = None, verbose: bool = False) -
     newest = max(o.stat().st_mtime for o in objs)
     if force or not LIB.exists() or LIB.stat().st_mtime < newest:
         tmp = LIB.with_suffix(".so.tmp")
-        cmd = [NVCC, *ARCH, "-shared", "-o", str(tmp), *map(str, objs), "-lcuda"]
+        cmd = [NVCC, *ARCH, "-shared", "-o", str(tmp), *map(str, objs), "-lcuda", "-ldl"]
         res = subprocess.run(cmd, capture_output=True, text=True)
         if res.returncode != 0:
             raise RuntimeError(f"link failed:\n{res.stdout}\n{res.stderr}")

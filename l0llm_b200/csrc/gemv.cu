@@ -53,7 +53,7 @@ __device__ __forceinline__ float epilogue_store(const GemvParams& p, int n, int 
         o[idx] += v;
     } else if (p.epi == EPI_ARGMAX) {
         if (g.out) store_from_float(g.out, p.out_dtype, idx, v);
-        if (fold) atomicMax(p.argmax + m, argmax_key(v, n));
+        if (fold) atomicMax(p.argmax + m, argmax_key(v, n + p.argmax_base));
     } else {
         store_from_float(g.out, p.out_dtype, idx, v);
     }
@@ -791,8 +791,8 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_mma_kernel(const GemvParams 
             const bool live = m < M;
             if (p.epi == EPI_ARGMAX) {
                 unsigned long long key = 0;
-                if (live && v0) key = argmax_key(epilogue_store(p, r0, m, y0, false), r0);
-                if (live && v1) key = max(key, argmax_key(epilogue_store(p, r1, m, y1, false), r1));
+                if (live && v0) key = argmax_key(epilogue_store(p, r0, m, y0, false), r0 + p.argmax_base);
+                if (live && v1) key = max(key, argmax_key(epilogue_store(p, r1, m, y1, false), r1 + p.argmax_base));
 #pragma unroll
                 for (int o = 4; o < 32; o <<= 1) key = max(key, __shfl_xor_sync(0xffffffffu, key, o));
                 if (live && g == 0 && key) atomicMax(p.argmax + m, key);

@@ -35,6 +35,7 @@ struct GemvParams {
     int nseg;
     GemvSeg seg[4];
     unsigned long long* argmax;  // [M] keys for EPI_ARGMAX
+    int argmax_base;             // index of W's row 0 in the argmax (vocab shard offset under TP)
     int kt;                      // K elements per shared-memory tile (a multiple of 512)
     int prefetch;                // prefetch the first row block of weights into L2 before pdl_wait
 };

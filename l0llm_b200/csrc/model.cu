@@ -63,6 +63,11 @@ struct l0b_model {
     int* step_idx = nullptr;
     unsigned long long* keys = nullptr;  // [batch_cap]
     int prefill_seq = 0;           // cache row (sequence) the prefill path writes
+    // Tensor parallelism: q/k/v, gate/up and lm_head column-split, o/down row-split (partial sums
+    // all-reduced before the residual add), attention head-split, embedding replicated.
+    l0b_comm* comm = nullptr;
+    int tp = 1, tp_rank = 0;
+    float* logits_all = nullptr;   // [tp, batch_cap, vocab / tp] gathered logits
     std::vector<int> seq_pos;      // host mirror of each sequence's next position
     // Host state.
     int* host_io = nullptr;       // pinned [2 * batch_cap]
@@ -314,6 +319,14 @@ l0b_status emit(l0b_model* m, int li, const char* stage, const float* dptr, long
     return L0B_OK;
 }
 
+// Under TP: the rank's partial sum of a row-split projection, summed over the ranks, then added into
+// the residual stream.
+l0b_status reduce_into_residual(l0b_model* m, float* partial, int rows) {
+    const long long n = static_cast<long long>(rows) * m->h;
+    L0B_TRY(comm_allreduce(m->comm, partial, static_cast<size_t>(n), L0B_F32, COLL_SUM));
+    return k_add(m->dev, m->hidden, partial, n);
+}
+
 // Fused decoder layer for `rows` tokens. decode: each row is its own sequence (cache row b, position
 // pos[b]); prefill: the rows are consecutive positions of sequence 0 starting at pos0.
 l0b_status record_layer_fused(l0b_model* m, int li, int rows, bool decode, int pos0) {
@@ -370,11 +383,17 @@ l0b_status record_layer_fused(l0b_model* m, int li, int rows, bool decode, int p
         a.max_splits = 1;
         L0B_TRY(attention_launch(m->dev, a, rows));
     }
-    // 3. o_proj, added into the residual stream.
+    // 3. o_proj, added into the residual stream (under TP: this rank's partial, summed over ranks).
     p = linear_params(L.o, rows, m->attn, m->qdim);
-    p.epi = EPI_ACCUM;
-    p.seg[0] = {m->hidden, nullptr, m->h, m->h};
-    L0B_TRY(gemv(m, L.o, p));
+    if (m->comm) {
+        p.seg[0] = {m->attn_proj, nullptr, m->h, m->h};
+        L0B_TRY(gemv(m, L.o, p));
+        L0B_TRY(reduce_into_residual(m, m->attn_proj, rows));
+    } else {
+        p.epi = EPI_ACCUM;
+        p.seg[0] = {m->hidden, nullptr, m->h, m->h};
+        L0B_TRY(gemv(m, L.o, p));
+    }
     // 4. gate/up with the post-attention RMSNorm prologue and the SwiGLU epilogue.
     p = linear_params(L.gate_up, rows, m->hidden, m->h);
     p.norm_w = L.post_norm;
@@ -384,6 +403,11 @@ l0b_status record_layer_fused(l0b_model* m, int li, int rows, bool decode, int p
     L0B_TRY(gemv(m, L.gate_up, p));
     // 5. down, added into the residual stream.
     p = linear_params(L.down, rows, m->act, m->inter);
+    if (m->comm) {
+        p.seg[0] = {m->down, nullptr, m->h, m->h};
+        L0B_TRY(gemv(m, L.down, p));
+        return reduce_into_residual(m, m->down, rows);
+    }
     p.epi = EPI_ACCUM;
     p.seg[0] = {m->hidden, nullptr, m->h, m->h};
     return gemv(m, L.down, p);
@@ -446,6 +470,7 @@ l0b_status record_layer_reference(l0b_model* m, int li, int rows, bool decode, i
     p = linear_params(L.o, rows, m->attn, m->qdim);
     p.seg[0] = {m->attn_proj, nullptr, m->h, m->h};
     L0B_TRY(gemv(m, L.o, p));
+    if (m->comm) L0B_TRY(comm_allreduce(m->comm, m->attn_proj, static_cast<size_t>(rows) * m->h, L0B_F32, COLL_SUM));
     L0B_TRY(emit(m, li, "attn_out", m->attn_proj, m->h));
     L0B_TRY(k_rmsnorm(d, m->hidden, m->attn_proj, L.post_norm, m->normed, c.rms_norm_eps, m->h, rows, 1));
     L0B_TRY(emit(m, li, "post_norm", m->normed, m->h));
@@ -458,6 +483,7 @@ l0b_status record_layer_reference(l0b_model* m, int li, int rows, bool decode, i
     p = linear_params(L.down, rows, m->gate, m->inter);
     p.seg[0] = {m->down, nullptr, m->h, m->h};
     L0B_TRY(gemv(m, L.down, p));
+    if (m->comm) L0B_TRY(comm_allreduce(m->comm, m->down, static_cast<size_t>(rows) * m->h, L0B_F32, COLL_SUM));
     L0B_TRY(emit(m, li, "mlp_out", m->down, m->h));
     L0B_TRY(k_add(d, m->hidden, m->down, static_cast<long long>(rows) * m->h));
     return emit(m, li, "output", m->hidden, m->h);
@@ -474,6 +500,7 @@ l0b_status record_head(l0b_model* m, int row0, int rows, int advance, int seq0 =
         p.eps = c.rms_norm_eps;
         p.epi = EPI_ARGMAX;
         p.argmax = m->keys + seq0;
+        p.argmax_base = m->tp_rank * m->vocab;
         p.seg[0] = {m->logits, nullptr, m->vocab, m->vocab};
         L0B_TRY(gemv(m, m->lm_head, p));
     } else {
@@ -488,9 +515,12 @@ l0b_status record_head(l0b_model* m, int row0, int rows, int advance, int seq0 =
         GemvParams p = linear_params(m->lm_head, rows, m->normed, m->h);
         p.epi = EPI_ARGMAX;
         p.argmax = m->keys + seq0;
+        p.argmax_base = m->tp_rank * m->vocab;
         p.seg[0] = {m->logits, nullptr, m->vocab, m->vocab};
         L0B_TRY(gemv(m, m->lm_head, p));
     }
+    // Under TP each rank holds the argmax of its vocab shard (global indices): the largest key wins.
+    if (m->comm) L0B_TRY(comm_allreduce(m->comm, m->keys + seq0, rows, kDtypeU64, COLL_MAX));
     return d->launch(step_finish_kernel, dim3(1), dim3(rows < 32 ? 32 : ((rows + 31) / 32) * 32), 0, m->keys + seq0,
                      m->sampled + seq0, m->tok + seq0, m->pos + seq0, seq0 ? nullptr : m->out_tokens, m->step_idx,
                      rows, advance);
@@ -560,6 +590,19 @@ l0b_status write_io(l0b_model* m, int rows, const int* tokens, const int* positi
 l0b_status read_logits(l0b_model* m, float* out, int rows) {
     if (!out) return L0B_OK;
     const size_t bytes = static_cast<size_t>(rows) * m->vocab * sizeof(float);
+    if (m->comm) {
+        // Every rank joins the gather (each holds a vocab shard); rows come back as [rank][row][shard].
+        L0B_TRY(comm_allgather(m->comm, m->logits, m->logits_all, static_cast<size_t>(rows) * m->vocab, L0B_F32));
+        L0B_CHECK_CUDA(cudaMemcpyAsync(m->host_logits, m->logits_all, bytes * m->tp, cudaMemcpyDeviceToHost,
+                                       m->dev->stream));
+        L0B_CHECK_CUDA(cudaStreamSynchronize(m->dev->stream));
+        const size_t full = static_cast<size_t>(m->vocab) * m->tp;
+        for (int r = 0; r < m->tp; ++r)
+            for (int b = 0; b < rows; ++b)
+                std::memcpy(out + b * full + static_cast<size_t>(r) * m->vocab,
+                            m->host_logits + (static_cast<size_t>(r) * rows + b) * m->vocab, m->vocab * sizeof(float));
+        return L0B_OK;
+    }
     L0B_CHECK_CUDA(cudaMemcpyAsync(m->host_logits, m->logits, bytes, cudaMemcpyDeviceToHost, m->dev->stream));
     L0B_CHECK_CUDA(cudaStreamSynchronize(m->dev->stream));
     std::memcpy(out, m->host_logits, bytes);
@@ -801,6 +844,9 @@ L0B_API l0b_status l0b_model_create(l0b_device* dev, l0b_suite* suite, const l0b
                 "kv_dtype must be f32, f16 or bf16");
     const int tp = c.tp_size > 1 ? c.tp_size : 1;
     L0B_REQUIRE(tp == 1 || comm, L0B_ERR_ARGUMENT, "tensor parallelism needs a communicator");
+    L0B_REQUIRE(tp == 1 || (comm_size(comm) == tp && comm_rank(comm) == c.tp_rank), L0B_ERR_ARGUMENT,
+                "communicator is rank %d of %d, the config says %d of %d", comm_rank(comm), comm_size(comm),
+                c.tp_rank, tp);
     L0B_REQUIRE(c.num_key_value_heads % tp == 0 && c.intermediate_size % tp == 0 && c.vocab_size % tp == 0,
                 L0B_ERR_UNSUPPORTED, "kv heads, intermediate size and vocab must divide by tp_size %d", tp);
     L0B_REQUIRE(c.head_dim == 64 || c.head_dim == 128, L0B_ERR_UNSUPPORTED, "head_dim %d (64 or 128 are supported)",
@@ -834,6 +880,9 @@ L0B_API l0b_status l0b_model_create(l0b_device* dev, l0b_suite* suite, const l0b
     m->cache_dtype = c.kv_dtype;
     m->softmax_scale = static_cast<float>(1.0 / std::sqrt(static_cast<double>(c.head_dim)));
     m->fused = !c.qk_norm;
+    m->tp = tp;
+    m->tp_rank = tp > 1 ? c.tp_rank : 0;
+    m->comm = tp > 1 ? comm : nullptr;
     m->batch_cap = c.max_batch < 1 ? 1 : c.max_batch;
     L0B_REQUIRE(m->batch_cap <= kMaxRows, L0B_ERR_OUT_OF_RANGE, "max_batch %d exceeds %d sequences", c.max_batch,
                 kMaxRows);
@@ -912,7 +961,8 @@ L0B_API l0b_status l0b_model_create(l0b_device* dev, l0b_suite* suite, const l0b
     L0B_TRY(m->alloc(&m->step_idx, 1));
     L0B_TRY(m->alloc(&m->keys, m->batch_cap));
     L0B_CHECK_CUDA(cudaMallocHost(&m->host_io, sizeof(int) * 2 * m->batch_cap));
-    L0B_CHECK_CUDA(cudaMallocHost(&m->host_logits, sizeof(float) * m->batch_cap * m->vocab));
+    if (m->tp > 1) L0B_TRY(m->alloc(&m->logits_all, static_cast<size_t>(m->tp) * m->batch_cap * m->vocab));
+    L0B_CHECK_CUDA(cudaMallocHost(&m->host_logits, sizeof(float) * m->batch_cap * m->vocab * m->tp));
     L0B_CHECK_CUDA(cudaStreamSynchronize(dev->stream));
     *out = m.release();
     return L0B_OK;

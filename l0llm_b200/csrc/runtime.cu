@@ -171,6 +171,32 @@ l0b_status l0b_device::submit(LaunchRecord& rec) {
     return L0B_OK;
 }
 
+l0b_status l0b_device::collective(int kind, const CollArgs& a) {
+    LaunchRecord* rec;
+    LaunchRecord local;
+    if (recording) {
+        if (log_used == log.size()) log.emplace_back();
+        rec = &log[log_used];
+    } else {
+        rec = &local;
+    }
+    rec->func = nullptr;
+    rec->grid = dim3(0, 0, 0);
+    rec->block = dim3(0, 0, 0);
+    rec->smem = 0;
+    rec->pdl = 0;
+    rec->cluster_y = 0;
+    rec->kind = static_cast<uint8_t>(kind);
+    rec->nargs = 0;
+    rec->blob_size = 0;
+    rec->push(a);
+    if (recording) {
+        ++log_used;
+        return L0B_OK;
+    }
+    return collective_issue(kind, a, stream);
+}
+
 l0b_status l0b_device::build_graph(CachedGraph& g) {
     if (g.exec) {
         cudaGraphExecDestroy(g.exec);
@@ -183,6 +209,19 @@ l0b_status l0b_device::build_graph(CachedGraph& g) {
     g.nodes.clear();
     L0B_CHECK_CUDA(cudaStreamBeginCapture(stream, cudaStreamCaptureModeThreadLocal));
     for (auto& rec : g.log) {
+        if (rec.kind != REC_KERNEL) {
+            CollArgs a;
+            std::memcpy(&a, rec.blob + rec.offsets[0], sizeof(a));
+            l0b_status st = collective_issue(rec.kind, a, stream);
+            if (st != L0B_OK) {
+                cudaGraph_t junk = nullptr;
+                cudaStreamEndCapture(stream, &junk);
+                if (junk) cudaGraphDestroy(junk);
+                return st;
+            }
+            g.nodes.push_back(nullptr);  // never patched: collectives only match with equal arguments
+            continue;
+        }
         void* args[kMaxArgs];
         rec.arg_pointers(args);
         cudaLaunchAttribute attr[2];

@@ -74,12 +74,28 @@ inline cudaError_t copy_sync(cudaStream_t s, void* dst, const void* src, size_t 
 constexpr int kMaxArgBytes = 768;
 constexpr int kMaxArgs = 24;
 
+// A command-list entry is a kernel launch or a collective on the device stream (tensor parallelism).
+enum RecordKind : uint8_t { REC_KERNEL = 0, REC_ALLREDUCE = 1, REC_ALLGATHER = 2 };
+enum CollOp : int { COLL_SUM = 0, COLL_MAX = 1 };
+constexpr int kDtypeU64 = 100;  // collective element type for 64-bit argmax keys (internal)
+struct CollArgs {
+    const void* send;
+    void* recv;
+    size_t count;
+    int dtype;
+    int op;
+    void* comm;  // ncclComm_t
+};
+// Issues a collective on `stream` (comm.cu; NCCL is loaded when the first communicator is made).
+l0b_status collective_issue(int kind, const CollArgs& a, cudaStream_t stream);
+
 struct LaunchRecord {
     const void* func = nullptr;
     dim3 grid, block;
     uint32_t smem = 0;
     uint8_t pdl = 0;
     uint8_t cluster_y = 0;  // > 1: thread-block clusters of (1, cluster_y, 1)
+    uint8_t kind = REC_KERNEL;
     uint8_t nargs = 0;
     uint16_t blob_size = 0;
     uint16_t offsets[kMaxArgs];
@@ -88,8 +104,9 @@ struct LaunchRecord {
     bool same_shape(const LaunchRecord& o) const {
         return func == o.func && grid.x == o.grid.x && grid.y == o.grid.y && grid.z == o.grid.z &&
                block.x == o.block.x && block.y == o.block.y && block.z == o.block.z && smem == o.smem &&
-               pdl == o.pdl && cluster_y == o.cluster_y && nargs == o.nargs && blob_size == o.blob_size &&
-               std::memcmp(offsets, o.offsets, nargs * sizeof(uint16_t)) == 0;
+               pdl == o.pdl && cluster_y == o.cluster_y && kind == o.kind && nargs == o.nargs &&
+               blob_size == o.blob_size && std::memcmp(offsets, o.offsets, nargs * sizeof(uint16_t)) == 0 &&
+               (kind == REC_KERNEL || same_args(o));  // a captured collective cannot be patched
     }
     bool same_args(const LaunchRecord& o) const { return std::memcmp(blob, o.blob, blob_size) == 0; }
 
@@ -182,11 +199,15 @@ struct l0b_device {
         rec->smem = static_cast<uint32_t>(smem);
         rec->pdl = pdl ? 1 : 0;
         rec->cluster_y = static_cast<uint8_t>(cluster_y > 1 ? cluster_y : 0);
+        rec->kind = l0b::REC_KERNEL;
         rec->nargs = 0;
         rec->blob_size = 0;
         (rec->push(static_cast<KArgs>(args)), ...);
         return submit(*rec);
     }
+
+    // Appends (recording) or issues (immediate) one collective.
+    l0b_status collective(int kind, const l0b::CollArgs& a);
 
     l0b_status end_recording();
     void abort_recording();
@@ -201,7 +222,14 @@ struct l0b_buffer {
     size_t bytes() const { return static_cast<size_t>(count) * l0b::dtype_size(dtype); }
 };
 
+struct l0b_comm;
+
 namespace l0b {
+// Tensor-parallel collectives on the communicator's device stream (recorded like kernels).
+l0b_status comm_allreduce(l0b_comm* c, void* buf, size_t count, int dtype, int op);
+l0b_status comm_allgather(l0b_comm* c, const void* send, void* recv, size_t count, int dtype);
+int comm_size(const l0b_comm* c);
+int comm_rank(const l0b_comm* c);
 // Process-wide counter of kernels launched (immediate + graph kernel nodes).
 void add_launches(int64_t n);
 // Checks that the current device is an sm_100-class GPU. Cached.

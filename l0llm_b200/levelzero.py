@@ -170,6 +170,10 @@ def load_library() -> C.CDLL:
         "l0b_linear_tc": (i32, [vp, vp, i32, i32, i32, vp, vp, vp, f32, i32, vp, vp]),
         "l0b_device_error_status": (i32, [vp, C.POINTER(i32)]),
         "l0b_set_gemv_tensor_cores": (i32, [i32]),
+        "l0b_comm_unique_id": (i32, [vp, i32]),
+        "l0b_comm_create": (i32, [vp, vp, i32, i32, i32, pp]),
+        "l0b_comm_free": (i32, [vp]),
+        "l0b_comm_allreduce": (i32, [vp, vp, i64]),
         "l0b_model_prefill_sequence": (i32, [vp, i32, vp, i32, vp]),
         "l0b_model_decode_batch": (i32, [vp, vp, vp, i32, vp]),
         "l0b_model_decode_greedy_device_batch": (i32, [vp, i32, i32, vp]),
@@ -588,6 +592,40 @@ def model_config(**kw) -> ModelConfig:
     return cfg
 
 
+class Communicator:
+    """Tensor-parallel communicator (NCCL), one per rank. Rank 0 makes the id with unique_id() and the
+    caller hands it to every rank (any channel, e.g. torch.distributed over gloo)."""
+
+    ID_BYTES = 128
+
+    @staticmethod
+    def unique_id() -> bytes:
+        buf = (C.c_uint8 * Communicator.ID_BYTES)()
+        check(load_library().l0b_comm_unique_id(buf, Communicator.ID_BYTES))
+        return bytes(buf)
+
+    def __init__(self, device: ComputeDevice, uid: bytes, nranks: int, rank: int):
+        buf = (C.c_uint8 * len(uid)).from_buffer_copy(uid)
+        h = C.c_void_p()
+        check(load_library().l0b_comm_create(device.handle, buf, len(uid), nranks, rank, C.byref(h)))
+        self.handle = h
+        self.nranks, self.rank = nranks, rank
+
+    def AllReduce(self, buf: "SharedBuffer", count: int | None = None):
+        check(load_library().l0b_comm_allreduce(self.handle, buf.handle, buf.Count if count is None else count))
+
+    def Dispose(self):
+        if self.handle:
+            load_library().l0b_comm_free(self.handle)
+            self.handle = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.Dispose()
+
+
 class LlmModel:
     """LlmModel: prefill / decode / greedy generation on the device."""
 
@@ -595,10 +633,11 @@ class LlmModel:
                  precision: str = "auto", comm=None):
         h = C.c_void_p()
         check(load_library().l0b_model_create(device.handle, suite.handle, C.byref(cfg), max_seq_len,
-                                              PRECISION[precision], comm, C.byref(h)))
+                                              PRECISION[precision], _h(comm) if comm is not None else None,
+                                              C.byref(h)))
         self.handle = h
         self.cfg = cfg
-        self.vocab = cfg.vocab_size // max(1, cfg.tp_size)
+        self.vocab = cfg.vocab_size  # under TP the logits are gathered to the full vocabulary
         self.MaxSeqLen = max_seq_len
 
     def init_synthetic(self, seed: int, std: float = 0.02, scale_lo: float = 1e-3, scale_hi: float = 2e-2):
