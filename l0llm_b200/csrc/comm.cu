@@ -128,6 +128,25 @@ L0B_API l0b_status l0b_comm_create(l0b_device* dev, const uint8_t* id, int32_t b
         delete c;
         return fail(L0B_ERR_NCCL, "ncclCommInitRank failed: %s", g_nccl.error_string(r));
     }
+    // One small all-reduce and all-gather outside any stream capture, waited for: NCCL sets up its
+    // connections on first use, which must not happen inside the capture of a command list.
+    void* scratch = nullptr;
+    cudaError_t e = cudaMalloc(&scratch, 64 * sizeof(float) * (nranks + 1));
+    if (e == cudaSuccess) {
+        float* f = static_cast<float*>(scratch);
+        cudaMemsetAsync(f, 0, 64 * sizeof(float) * (nranks + 1), dev->stream);
+        r = g_nccl.all_reduce(f, f, 64, ncclFloat32, ncclSum, c->comm, dev->stream);
+        if (r == ncclSuccess) r = g_nccl.all_gather(f, f + 64, 64, ncclFloat32, c->comm, dev->stream);
+        if (r == ncclSuccess) r = g_nccl.all_reduce(f, f, 32, ncclUint64, ncclMax, c->comm, dev->stream);
+        e = cudaStreamSynchronize(dev->stream);
+        cudaFree(scratch);
+    }
+    if (e != cudaSuccess || r != ncclSuccess) {
+        g_nccl.comm_destroy(c->comm);
+        delete c;
+        if (e != cudaSuccess) return fail(L0B_ERR_CUDA, "communicator warm-up failed: %s", cudaGetErrorString(e));
+        return fail(L0B_ERR_NCCL, "communicator warm-up failed: %s", g_nccl.error_string(r));
+    }
     *out = c;
     return L0B_OK;
 }
@@ -136,7 +155,8 @@ L0B_API l0b_status l0b_comm_free(l0b_comm* c) {
     if (!c) return L0B_OK;
     if (c->comm && g_nccl.handle) {
         cudaSetDevice(c->dev->index);
-        cudaStreamSynchronize(c->dev->stream);
+        // Captured collectives keep the communicator busy: release the device's graphs first.
+        c->dev->drop_graphs();
         g_nccl.comm_destroy(c->comm);
     }
     delete c;

@@ -67,6 +67,7 @@ struct l0b_model {
     // all-reduced before the residual add), attention head-split, embedding replicated.
     l0b_comm* comm = nullptr;
     int tp = 1, tp_rank = 0;
+    int vocab_full = 0;            // tokens in the (replicated) embedding; vocab is this rank's lm_head shard
     float* logits_all = nullptr;   // [tp, batch_cap, vocab / tp] gathered logits
     std::vector<int> seq_pos;      // host mirror of each sequence's next position
     // Host state.
@@ -256,12 +257,14 @@ struct Synth {
         if (mat.dtype == L0B_I8) {
             int8_t* q = static_cast<int8_t*>(mat.w) + static_cast<long long>(dst_row) * mat.k;
             L0B_TRY(fill(q, L0B_I8, count, id, SYN_I8, 0.f, 0.f, cols, full_k, row0, col0));
-            // Scales: one per (row, group) of the full tensor; a column shard takes its groups.
-            const int gpr_full = full_k / mat.group;
-            const int gpr = cols / mat.group;
+            // Scales: one per (row, group) of the full tensor; a column shard takes its groups. With one
+            // scale per output row (group = this shard's K) every column shard takes the row's only scale.
+            const bool per_row = mat.group >= mat.k;
+            const int gpr_full = per_row ? 1 : full_k / mat.group;
+            const int gpr = per_row ? 1 : cols / mat.group;
             __half* s = mat.scales + static_cast<long long>(dst_row) * gpr;
             return fill(s, L0B_F16, static_cast<long long>(rows) * gpr, scale_id, SYN_UNIFORM, lo, hi, gpr, gpr_full,
-                        row0, col0 / mat.group);
+                        row0, per_row ? 0 : col0 / mat.group);
         }
         char* w = static_cast<char*>(mat.w) +
                   static_cast<long long>(dst_row) * mat.k * dtype_size(static_cast<l0b_dtype>(mat.dtype));
@@ -530,7 +533,7 @@ l0b_status record_head(l0b_model* m, int row0, int rows, int advance, int seq0 =
 l0b_status record_decode_step(l0b_model* m, int rows) {
     l0b_device* d = m->dev;
     L0B_TRY(d->launch(step_begin_kernel, dim3(grid_for(static_cast<long long>(rows) * m->h, d->sm_count)), dim3(256),
-                      0, m->tok, m->embed, m->hidden, m->h, rows, m->vocab, m->keys, rows));
+                      0, m->tok, m->embed, m->hidden, m->h, rows, m->vocab_full, m->keys, rows));
     for (int li = 0; li < static_cast<int>(m->layers.size()); ++li) {
         if (m->fused && !m->probe) L0B_TRY(record_layer_fused(m, li, rows, true, 0));
         else {
@@ -545,7 +548,7 @@ l0b_status record_decode_step(l0b_model* m, int rows) {
 l0b_status record_prefill_chunk(l0b_model* m, int count, int pos0, bool head) {
     l0b_device* d = m->dev;
     L0B_TRY(d->launch(step_begin_kernel, dim3(grid_for(static_cast<long long>(count) * m->h, d->sm_count)),
-                      dim3(256), 0, m->prompt_tok, m->embed, m->hidden, m->h, count, m->vocab,
+                      dim3(256), 0, m->prompt_tok, m->embed, m->hidden, m->h, count, m->vocab_full,
                       m->keys + m->prefill_seq, 1));
     for (int li = 0; li < static_cast<int>(m->layers.size()); ++li) {
         if (m->fused && !m->probe) L0B_TRY(record_layer_fused(m, li, count, false, pos0));
@@ -611,7 +614,7 @@ l0b_status read_logits(l0b_model* m, float* out, int rows) {
 
 // LlmModel.Step (L/LlmModel.cs:402-444): one token at `position`.
 l0b_status step(l0b_model* m, int token, int position) {
-    L0B_REQUIRE(token >= 0 && token < m->vocab, L0B_ERR_OUT_OF_RANGE, "Vocabulary has %d tokens (got %d).", m->vocab,
+    L0B_REQUIRE(token >= 0 && token < m->vocab_full, L0B_ERR_OUT_OF_RANGE, "Vocabulary has %d tokens (got %d).", m->vocab_full,
                 token);
     L0B_REQUIRE(position >= 0 && position < m->max_seq, L0B_ERR_OUT_OF_RANGE, "Cache holds %d positions.", m->max_seq);
     L0B_TRY(write_io(m, 1, &token, &position));
@@ -632,8 +635,8 @@ l0b_status ingest_prompt(l0b_model* m, const int32_t* ids, int count, int seq = 
         const int n = count - start < chunk ? count - start : chunk;
         const bool last = start + n == count;
         for (int i = 0; i < n; ++i)
-            L0B_REQUIRE(ids[start + i] >= 0 && ids[start + i] < m->vocab, L0B_ERR_OUT_OF_RANGE,
-                        "Vocabulary has %d tokens (got %d).", m->vocab, ids[start + i]);
+            L0B_REQUIRE(ids[start + i] >= 0 && ids[start + i] < m->vocab_full, L0B_ERR_OUT_OF_RANGE,
+                        "Vocabulary has %d tokens (got %d).", m->vocab_full, ids[start + i]);
         if (n == 1 && seq == 0) {
             L0B_TRY(step(m, ids[start], start));
             continue;
@@ -877,6 +880,7 @@ L0B_API l0b_status l0b_model_create(l0b_device* dev, l0b_suite* suite, const l0b
     m->kvdim = m->nkv * m->hd;
     m->qkv_w = m->qdim + 2 * m->kvdim;
     m->vocab = c.vocab_size / tp;
+    m->vocab_full = c.vocab_size;
     m->cache_dtype = c.kv_dtype;
     m->softmax_scale = static_cast<float>(1.0 / std::sqrt(static_cast<double>(c.head_dim)));
     m->fused = !c.qk_norm;
@@ -1234,8 +1238,8 @@ L0B_API l0b_status l0b_model_decode_batch(l0b_model* m, const int32_t* tokens, c
                 m->batch_cap);
     L0B_REQUIRE(m->fused && !m->probe, L0B_ERR_UNSUPPORTED, "batched decode needs the fused path");
     for (int b = 0; b < count; ++b) {
-        L0B_REQUIRE(tokens[b] >= 0 && tokens[b] < m->vocab, L0B_ERR_OUT_OF_RANGE, "Vocabulary has %d tokens (got %d).",
-                    m->vocab, tokens[b]);
+        L0B_REQUIRE(tokens[b] >= 0 && tokens[b] < m->vocab_full, L0B_ERR_OUT_OF_RANGE,
+                    "Vocabulary has %d tokens (got %d).", m->vocab_full, tokens[b]);
         L0B_REQUIRE(positions[b] >= 0 && positions[b] < m->max_seq, L0B_ERR_OUT_OF_RANGE,
                     "Cache holds %d positions (got %d).", m->max_seq, positions[b]);
     }

@@ -326,6 +326,15 @@ l0b_status l0b_device::end_recording() {
     return L0B_OK;
 }
 
+void l0b_device::drop_graphs() {
+    cudaStreamSynchronize(stream);
+    for (auto& g : graphs) {
+        if (g->exec) cudaGraphExecDestroy(g->exec);
+        if (g->graph) cudaGraphDestroy(g->graph);
+    }
+    graphs.clear();
+}
+
 void l0b_device::abort_recording() {
     recording = false;
     log_used = 0;

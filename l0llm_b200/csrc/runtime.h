@@ -209,6 +209,10 @@ struct l0b_device {
     // Appends (recording) or issues (immediate) one collective.
     l0b_status collective(int kind, const l0b::CollArgs& a);
 
+    // Destroys every cached command-list graph (after the stream drains); lists are captured anew
+    // when next recorded. Graphs holding collectives must go before their communicator.
+    void drop_graphs();
+
     l0b_status end_recording();
     void abort_recording();
     l0b_status build_graph(l0b::CachedGraph& g);
