@@ -43,6 +43,12 @@ ORC2 = dict(hidden=3584, inter=18944, layers=28, heads=28, kv_heads=4, head_dim=
             eps=1e-6, theta=1e6, tie=0, bias=1, qk_norm=0, rope_type=0, rope_factor=1.0, rope_original_max=0,
             rope_low=1.0, rope_high=4.0, rope_beta_fast=32.0, rope_beta_slow=1.0, rope_attention=0.0)
 SEED = 2
+# Config 4: Llama-3-70B shape, bf16, llama3 RoPE scaling, tensor-parallel over the torchrun ranks.
+CFG4 = dict(hidden_size=8192, intermediate_size=28672, num_layers=80, num_attention_heads=64, num_key_value_heads=8,
+            head_dim=128, vocab_size=128256, max_position_embeddings=131072, rms_norm_eps=1e-5, rope_theta=5e5,
+            tie_word_embeddings=0, attention_bias=0, rope_type=3, rope_factor=8.0, rope_low_freq_factor=1.0,
+            rope_high_freq_factor=4.0, rope_original_max_position=8192)
+CFG4_PROMPT = 2048
 BS16 = 16  # the metric's second batch size (decode at batch 1 and batch 16)
 CONTEXT = 512
 
@@ -256,6 +262,95 @@ def dominant_kernel_roofline(lz, dev, suite, stream_ptr, torch, peak: float, pea
             "avg_us": round(avg_ms * 1e3, 2)}
 
 
+def run_cfg4_tp(args) -> int:
+    """Config 4: one sequence decoded tensor-parallel over all ranks (strong scaling): q/k/v, gate/up
+    and lm_head column-split, o_proj/down row-split with an all-reduce each, KV heads split."""
+    world, rank, local = dist_env()
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    from l0llm_b200 import levelzero as lz
+
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600))
+    dev = lz.ComputeDevice(local)
+    suite = lz.LlmKernelSuite.Create(dev)
+    import ctypes as C
+
+    sp = C.c_void_p()
+    lz.check(lz.load_library().l0b_device_stream(dev.handle, C.byref(sp)))
+    stream = torch.cuda.ExternalStream(sp.value)
+    comm = None
+    if world > 1:
+        box = [lz.Communicator.unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(box, src=0)
+        comm = lz.Communicator(dev, box[0], world, rank)
+    cfg = lz.model_config(kv_dtype=lz.BF16, tp_size=world, tp_rank=rank, **CFG4)
+    model = lz.LlmModel(dev, suite, cfg, CFG4_PROMPT + 2 * args.warmup + args.steps + 16, "bfloat16", comm=comm)
+    model.init_synthetic(4, 0.02)
+    prompt = np.random.default_rng(4).integers(0, CFG4["vocab_size"], CFG4_PROMPT).astype(np.int32)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    barrier()
+    t0 = time.perf_counter()
+    model.Prefill(prompt)
+    barrier()
+    prefill_s = time.perf_counter() - t0
+    sampler = ClockSampler(local)
+    sampler.start()
+    model.decode_greedy_device(args.warmup)
+    barrier()
+    t_begin = time.monotonic()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    toks = model.decode_greedy_device(args.steps)
+    e1.record(stream)
+    e1.synchronize()
+    sampler.mark(t_begin, time.monotonic())
+    barrier()
+    ms = e0.elapsed_time(e1)
+    clocks = sampler.stop()
+    proj = model.ProjectionBytes
+    t = torch.tensor([ms, prefill_s], dtype=torch.float64, device="cuda")
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        same = torch.tensor(toks.astype(np.int64), device="cuda")
+        ref = same.clone()
+        dist.broadcast(ref, src=0)
+        assert bool((same == ref).all()), "ranks disagree on the greedy tokens"
+    ms, prefill_s = float(t[0]), float(t[1])
+    model.Dispose()
+    if comm is not None:
+        comm.Dispose()  # releases the device's captured graphs first
+    suite.Dispose()
+    dev.Dispose()
+    if rank == 0:
+        step_bytes = proj * world  # every rank streams its shard each step
+        line = {
+            "metric": "decode tok/s (Llama-3-70B bf16, TP, bs1)", "value": round(args.steps / (ms / 1e3), 2),
+            "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": f"config 4: Llama-3-70B-shape bf16, TP{world}, bs1, {CFG4_PROMPT}-token prompt",
+                       "global_batch": 1, "seq_len": CFG4_PROMPT, "parallelism": f"tp{world}",
+                       "l2": "inputs larger than L2: every rank streams its weight shard each step"},
+            "step_roofline": {"weight_bytes_per_step_all_ranks": int(step_bytes),
+                              "per_rank_gbs": round(proj / (ms / args.steps * 1e-3) / 1e9, 1)},
+            "clocks": clocks, "prefill_s": round(prefill_s, 3),
+        }
+        print(json.dumps(line))
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
 def main() -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -265,10 +360,15 @@ def main() -> int:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--kernel-only", action="store_true",
                     help="only the dominant-kernel roofline loop (small device footprint, for ncu captures)")
+    ap.add_argument("--workload", default="cfg2", choices=["cfg2", "cfg4"],
+                    help="cfg2: the headline (Qwen2.5-7B int8, one GPU, replicas over N); cfg4: Llama-3-70B bf16 "
+                         "tensor-parallel over the N ranks")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)
     args.warmup = max(3, args.warmup)
+    if args.workload == "cfg4":
+        return run_cfg4_tp(args)
     if args.kernel_only:
         import ctypes as C
 

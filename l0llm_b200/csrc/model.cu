@@ -322,12 +322,15 @@ l0b_status emit(l0b_model* m, int li, const char* stage, const float* dptr, long
     return L0B_OK;
 }
 
-// Under TP: the rank's partial sum of a row-split projection, summed over the ranks, then added into
-// the residual stream.
-l0b_status reduce_into_residual(l0b_model* m, float* partial, int rows) {
-    const long long n = static_cast<long long>(rows) * m->h;
-    L0B_TRY(comm_allreduce(m->comm, partial, static_cast<size_t>(n), L0B_F32, COLL_SUM));
-    return k_add(m->dev, m->hidden, partial, n);
+// A row-split projection under TP, folded into the residual stream with one in-place all-reduce:
+// rank 0 accumulates its partial product into `hidden`, the other ranks store theirs there, so the
+// sum over ranks is hidden + sum of the partials on every rank (no separate add kernel).
+l0b_status project_into_residual(l0b_model* m, const ModelMatrix& w, GemvParams p, int rows) {
+    p.epi = m->tp_rank == 0 ? EPI_ACCUM : EPI_STORE;
+    p.out_dtype = L0B_F32;
+    p.seg[0] = {m->hidden, nullptr, m->h, m->h};
+    L0B_TRY(gemv(m, w, p));
+    return comm_allreduce(m->comm, m->hidden, static_cast<size_t>(rows) * m->h, L0B_F32, COLL_SUM);
 }
 
 // Fused decoder layer for `rows` tokens. decode: each row is its own sequence (cache row b, position
@@ -389,9 +392,7 @@ l0b_status record_layer_fused(l0b_model* m, int li, int rows, bool decode, int p
     // 3. o_proj, added into the residual stream (under TP: this rank's partial, summed over ranks).
     p = linear_params(L.o, rows, m->attn, m->qdim);
     if (m->comm) {
-        p.seg[0] = {m->attn_proj, nullptr, m->h, m->h};
-        L0B_TRY(gemv(m, L.o, p));
-        L0B_TRY(reduce_into_residual(m, m->attn_proj, rows));
+        L0B_TRY(project_into_residual(m, L.o, p, rows));
     } else {
         p.epi = EPI_ACCUM;
         p.seg[0] = {m->hidden, nullptr, m->h, m->h};
@@ -406,11 +407,7 @@ l0b_status record_layer_fused(l0b_model* m, int li, int rows, bool decode, int p
     L0B_TRY(gemv(m, L.gate_up, p));
     // 5. down, added into the residual stream.
     p = linear_params(L.down, rows, m->act, m->inter);
-    if (m->comm) {
-        p.seg[0] = {m->down, nullptr, m->h, m->h};
-        L0B_TRY(gemv(m, L.down, p));
-        return reduce_into_residual(m, m->down, rows);
-    }
+    if (m->comm) return project_into_residual(m, L.down, p, rows);
     p.epi = EPI_ACCUM;
     p.seg[0] = {m->hidden, nullptr, m->h, m->h};
     return gemv(m, L.down, p);
