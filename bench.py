@@ -262,6 +262,125 @@ def dominant_kernel_roofline(lz, dev, suite, stream_ptr, torch, peak: float, pea
             "avg_us": round(avg_ms * 1e3, 2)}
 
 
+def run_cfg3_deltanet(args) -> int:
+    """Config 3: one Gated DeltaNet layer (Qwen3.5 shape, bf16 projections) driven through the library's
+    ops as LlmDecoderLayer.MixLinear calls them: in_proj (q, k, v | z) and (b | a) projections, causal
+    conv + SiLU, the gated delta recurrence with its gated RMSNorm, out_proj. Decode: one token per
+    step for bs sequences (projections batched over the rows, conv and recurrence per sequence), one
+    recorded command list per step. Prefill: 4096 tokens, projections on the tcgen05 GEMM."""
+    import ctypes as C
+
+    import torch
+
+    from l0llm_b200 import levelzero as lz
+
+    H, HK, HV, DK, DV, KC, T = 2048, 16, 32, 128, 128, 4, 4096
+    CONV = 2 * HK * DK + HV * DV
+    ZD = HV * DV
+    dev = lz.ComputeDevice(0)
+    suite = lz.LlmKernelSuite.Create(dev)
+    lib = lz.load_library()
+    sp = C.c_void_p()
+    lz.check(lib.l0b_device_stream(dev.handle, C.byref(sp)))
+    stream = torch.cuda.ExternalStream(sp.value)
+    rng = np.random.default_rng(3)
+
+    def bf16(shape, std):
+        w = torch.from_numpy((rng.standard_normal(shape) * std).astype(np.float32)).to(torch.bfloat16)
+        return lz.SharedBuffer.from_array(dev, w.view(torch.int16).numpy().view(np.uint16), lz.BF16)
+
+    def f32(a):
+        return lz.SharedBuffer.from_array(dev, np.ascontiguousarray(a, np.float32))
+
+    w_qkv, w_z, w_b, w_a, w_o = bf16((CONV, H), 0.02), bf16((ZD, H), 0.02), bf16((HV, H), 0.02), \
+        bf16((HV, H), 0.02), bf16((H, ZD), 0.02)
+    conv_w = f32(rng.standard_normal((CONV, KC)) * 0.3)
+    a_log = f32(np.log(rng.uniform(1, 16, HV)))
+    dt_bias = f32(rng.standard_normal(HV) * 0.1)
+    norm_w = f32(1 + 0.1 * rng.standard_normal(DV))
+
+    def layer_buffers(rows):
+        return dict(x=f32(rng.standard_normal((rows, H))), qkv=lz.SharedBuffer(dev, lz.F32, rows * CONV),
+                    z=lz.SharedBuffer(dev, lz.F32, rows * ZD), b=lz.SharedBuffer(dev, lz.F32, rows * HV),
+                    a=lz.SharedBuffer(dev, lz.F32, rows * HV), conv=lz.SharedBuffer(dev, lz.F32, rows * CONV),
+                    o=lz.SharedBuffer(dev, lz.F32, rows * ZD), y=lz.SharedBuffer(dev, lz.F32, rows * H))
+
+    def timed(fn, reps):
+        for _ in range(args.warmup):
+            fn()
+        dev.Synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(reps):
+            fn()
+        e1.record(stream)
+        e1.synchronize()
+        return e0.elapsed_time(e1) / reps
+
+    results = {}
+    for bs in (1, 8):
+        buf = layer_buffers(bs)
+        states = [lz.SharedBuffer(dev, lz.F32, HV * DK * DV) for _ in range(bs)]
+        conv_states = [lz.SharedBuffer(dev, lz.F32, CONV * (KC - 1)) for _ in range(bs)]
+        # Row q of each batched buffer, as its own (non-owning) buffer for the per-sequence ops.
+        row = {k: [buf[k].View(q * n, n) for q in range(bs)]
+               for k, n in (("qkv", CONV), ("conv", CONV), ("z", ZD), ("b", HV), ("a", HV), ("o", ZD))}
+
+        def step():
+            dev.BeginRecording()
+            suite.linear(dev, bs, CONV, H, buf["x"], w_qkv, None, 0, None, buf["qkv"])
+            suite.linear(dev, bs, ZD, H, buf["x"], w_z, None, 0, None, buf["z"])
+            suite.linear(dev, bs, HV, H, buf["x"], w_b, None, 0, None, buf["b"])
+            suite.linear(dev, bs, HV, H, buf["x"], w_a, None, 0, None, buf["a"])
+            for q in range(bs):
+                # Sequence q: its conv window and its recurrent state.
+                suite.CausalConv.Execute(dev, row["qkv"][q], conv_states[q], conv_w, row["conv"][q], CONV, KC, 1)
+                suite.GatedDelta.ExecuteGrouped(dev, row["conv"][q], row["z"][q], row["b"][q], row["a"][q], a_log,
+                                                dt_bias, norm_w, states[q], row["o"][q], HK, HV, DK, DV, 1, 1e-6)
+            suite.linear(dev, bs, H, ZD, buf["o"], w_o, None, 0, None, buf["y"])
+            dev.EndRecording()
+
+        ms = timed(step, 256 if bs == 1 else 64)
+        proj = (CONV + ZD + 2 * HV) * H * 2 + H * ZD * 2
+        step_bytes = proj + bs * (2 * HV * DK * DV * 4 + 2 * CONV * (KC - 1) * 4)
+        results[f"bs{bs}"] = {"us_per_step": round(ms * 1e3, 2), "tok_s": round(bs / (ms / 1e3), 1),
+                              "bytes_per_step": step_bytes, "achieved_gbs": round(step_bytes / (ms * 1e-3) / 1e9, 1)}
+    # Prefill: 4096 tokens of one sequence.
+    pre = layer_buffers(T)
+    state = lz.SharedBuffer(dev, lz.F32, HV * DK * DV)
+    conv_state = lz.SharedBuffer(dev, lz.F32, CONV * (KC - 1))
+    phases = {}
+
+    def tc(m, n, k, x, w, out):
+        lz.check(lib.l0b_linear_tc(suite.handle, dev.handle, m, n, k, x.handle, w.handle, None, 0.0, 0, None,
+                                   out.handle))
+
+    phases["projections_in"] = timed(lambda: (tc(T, CONV, H, pre["x"], w_qkv, pre["qkv"]),
+                                              tc(T, ZD, H, pre["x"], w_z, pre["z"]),
+                                              tc(T, HV, H, pre["x"], w_b, pre["b"]),
+                                              tc(T, HV, H, pre["x"], w_a, pre["a"])), 3)
+    phases["causal_conv"] = timed(lambda: suite.CausalConv.Execute(dev, pre["qkv"], conv_state, conv_w, pre["conv"],
+                                                                   CONV, KC, T), 3)
+    phases["gated_delta"] = timed(lambda: suite.GatedDelta.ExecuteGrouped(
+        dev, pre["conv"], pre["z"], pre["b"], pre["a"], a_log, dt_bias, norm_w, state, pre["o"], HK, HV, DK, DV, T,
+        1e-6), 3)
+    phases["out_proj"] = timed(lambda: tc(T, H, ZD, pre["o"], w_o, pre["y"]), 3)
+    total = sum(phases.values())
+    suite.Dispose()
+    dev.Dispose()
+    line = {"metric": "Gated DeltaNet layer decode tok/s (Qwen3.5 shape, bf16, bs1)", "value": results["bs1"]["tok_s"],
+            "unit": "tok/s", "n_gpus": 1, "steps": 256, "warmup": args.warmup,
+            "ms_per_step": round(results["bs1"]["us_per_step"] / 1e3, 5), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "config 3: Gated DeltaNet layer alone, hidden 2048, 16 key / 32 value heads of "
+                                   "128, conv 4, fp32 state [32,128,128] per sequence",
+                       "l2": "weights 67 MB per step: below L2, so the decode figures are L2-assisted"},
+            "decode": results,
+            "prefill_4096_ms": {k: round(v, 3) for k, v in phases.items()} | {"total": round(total, 3)}}
+    print(json.dumps(line))
+    return 0
+
+
 def run_cfg4_tp(args) -> int:
     """Config 4: one sequence decoded tensor-parallel over all ranks (strong scaling): q/k/v, gate/up
     and lm_head column-split, o_proj/down row-split with an all-reduce each, KV heads split."""
@@ -360,15 +479,17 @@ def main() -> int:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--kernel-only", action="store_true",
                     help="only the dominant-kernel roofline loop (small device footprint, for ncu captures)")
-    ap.add_argument("--workload", default="cfg2", choices=["cfg2", "cfg4"],
-                    help="cfg2: the headline (Qwen2.5-7B int8, one GPU, replicas over N); cfg4: Llama-3-70B bf16 "
-                         "tensor-parallel over the N ranks")
+    ap.add_argument("--workload", default="cfg2", choices=["cfg2", "cfg3", "cfg4"],
+                    help="cfg2: the headline (Qwen2.5-7B int8, one GPU, replicas over N); cfg3: the Gated DeltaNet "
+                         "layer alone (bf16, one GPU); cfg4: Llama-3-70B bf16 tensor-parallel over the N ranks")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)
     args.warmup = max(3, args.warmup)
     if args.workload == "cfg4":
         return run_cfg4_tp(args)
+    if args.workload == "cfg3":
+        return run_cfg3_deltanet(args)
     if args.kernel_only:
         import ctypes as C
 

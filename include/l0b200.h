@@ -122,6 +122,9 @@ L0B_API l0b_status l0b_buffer_alloc(l0b_device* dev, l0b_dtype dtype, int64_t co
 /* ComputeDevice.AllocShared<T>(T[] data). */
 L0B_API l0b_status l0b_buffer_alloc_from(l0b_device* dev, l0b_dtype dtype, int64_t count,
                                          const void* host, l0b_buffer** out);
+/* A buffer naming elements [offset, offset + count) of `base` (the C# side's Pointer + offset): it
+ * owns nothing, l0b_buffer_free releases only the handle, and it must not outlive `base`. */
+L0B_API l0b_status l0b_buffer_view(l0b_buffer* base, int64_t offset, int64_t count, l0b_buffer** out);
 L0B_API l0b_status l0b_buffer_free(l0b_buffer* buf);
 /* SharedBuffer.Write(T[]) at an element offset (Marshal.Copy into Pointer + offset). */
 L0B_API l0b_status l0b_buffer_write(l0b_buffer* buf, int64_t offset, const void* host, int64_t count);

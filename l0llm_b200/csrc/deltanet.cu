@@ -36,6 +36,44 @@ __global__ void causal_conv_kernel(const float* x, float* state, const float* w,
     for (int j = 0; j < hist; ++j) state[static_cast<long long>(c) * hist + j] = win[j];
 }
 
+// Many tokens, input and output apart: every (token, channel) output at once. Input at time tau < 0
+// comes from the conv window (state holds times -hist .. -1); the window is rolled by the next kernel.
+__global__ void causal_conv_tokens_kernel(const float* __restrict__ x, const float* __restrict__ state,
+                                          const float* __restrict__ w, float* __restrict__ out, int conv_dim,
+                                          int kernel, int tokens) {
+    pdl_wait();
+    const int hist = kernel - 1;
+    const long long total = static_cast<long long>(tokens) * conv_dim;
+    for (long long e = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; e < total;
+         e += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const int t = static_cast<int>(e / conv_dim), c = static_cast<int>(e - static_cast<long long>(t) * conv_dim);
+        float acc = 0.f;
+        for (int j = 0; j < kernel; ++j) {
+            const int tau = t - hist + j;
+            const float v = tau >= 0 ? x[static_cast<long long>(tau) * conv_dim + c]
+                                     : state[static_cast<long long>(c) * hist + hist + tau];
+            acc = fmaf(w[static_cast<long long>(c) * kernel + j], v, acc);
+        }
+        out[e] = silu(acc);
+    }
+}
+
+// The conv window after `tokens` inputs: times tokens - hist .. tokens - 1, each channel read whole
+// before it is written.
+__global__ void causal_conv_window_kernel(const float* __restrict__ x, float* state, int conv_dim, int kernel,
+                                          int tokens) {
+    pdl_wait();
+    const int c = blockIdx.x * blockDim.x + threadIdx.x;
+    const int hist = kernel - 1;
+    if (c >= conv_dim || hist == 0) return;
+    float nw[8];
+    for (int j = 0; j < hist; ++j) {
+        const int tau = tokens - hist + j;
+        nw[j] = tau >= 0 ? x[static_cast<long long>(tau) * conv_dim + c] : state[static_cast<long long>(c) * hist + hist + tau];
+    }
+    for (int j = 0; j < hist; ++j) state[static_cast<long long>(c) * hist + j] = nw[j];
+}
+
 template <int DK>
 __global__ void __launch_bounds__(256) gated_delta_kernel(const float* conv, const float* z, const float* b,
                                                           const float* a, const float* a_log, const float* dt_bias,
@@ -111,10 +149,127 @@ __global__ void __launch_bounds__(256) gated_delta_kernel(const float* conv, con
     }
 }
 
+// Prefill form of the recurrence: the columns of a head's state are independent given the token's
+// normalised q and k, beta and decay, so one warp owns 16 columns of one value head (grid: value head x
+// column group) and walks the tokens with no block barrier. Lane l holds rows [(l / 16) DK/2, +DK/2) of
+// column l % 16 in registers; the two halves of each dot product meet with one shuffle. The warp
+// L2-normalises q and k itself (shuffles) and loads the next token while computing this one. It writes
+// the raw output o; gated_norm_kernel applies the gated RMSNorm afterwards over all tokens at once.
+template <int DK>
+__global__ void __launch_bounds__(32) gated_delta_scan_kernel(const float* __restrict__ conv, const float* __restrict__ b,
+                                                              const float* __restrict__ a, const float* __restrict__ a_log,
+                                                              const float* __restrict__ dt_bias, float* state,
+                                                              float* __restrict__ out, int hk, int hv, int dv, int tokens) {
+    constexpr int PER = DK / 32;  // q/k elements each lane loads
+    constexpr int HR = DK / 2;    // state rows per lane
+    __shared__ float qs[2][DK], ks[2][DK];
+    pdl_wait();
+    const int h = blockIdx.x, lane = threadIdx.x;
+    const int j = blockIdx.y * 16 + (lane & 15), r0 = (lane >> 4) * HR;
+    const bool live = j < dv;
+    const int rep = hv / hk, kh = h / rep;
+    const int conv_dim = 2 * hk * DK + hv * dv;
+    float* S = state + static_cast<long long>(h) * DK * dv;
+    float s[HR];
+#pragma unroll
+    for (int i = 0; i < HR; ++i) s[i] = live ? S[static_cast<long long>(r0 + i) * dv + j] : 0.f;
+    const float A = -expf(a_log[h]);
+    const float bias = dt_bias[h];
+    const float qscale = rsqrtf(static_cast<float>(DK));
+    // Token t's inputs, loaded one token ahead.
+    float qv[PER], kv[PER], vv = 0.f, bv = 0.f, av = 0.f;
+    auto load = [&](int t) {
+        const float* row = conv + static_cast<long long>(t) * conv_dim;
+#pragma unroll
+        for (int e = 0; e < PER; ++e) {
+            qv[e] = row[kh * DK + lane + 32 * e];
+            kv[e] = row[hk * DK + kh * DK + lane + 32 * e];
+        }
+        vv = live ? row[2 * hk * DK + h * dv + j] : 0.f;
+        bv = b[static_cast<long long>(t) * hv + h];
+        av = a[static_cast<long long>(t) * hv + h];
+    };
+    if (tokens > 0) load(0);
+    for (int t = 0; t < tokens; ++t) {
+        const int buf = t & 1;
+        float pq = 0.f, pk = 0.f;
+#pragma unroll
+        for (int e = 0; e < PER; ++e) {
+            pq = fmaf(qv[e], qv[e], pq);
+            pk = fmaf(kv[e], kv[e], pk);
+        }
+        pq = warp_sum(pq);
+        pk = warp_sum(pk);
+        const float iq = rsqrtf(pq + 1e-6f) * qscale, ik = rsqrtf(pk + 1e-6f);
+#pragma unroll
+        for (int e = 0; e < PER; ++e) {
+            qs[buf][lane + 32 * e] = qv[e] * iq;
+            ks[buf][lane + 32 * e] = kv[e] * ik;
+        }
+        const float beta = 1.f / (1.f + expf(-bv));
+        const float xa = av + bias;
+        const float decay = expf(A * (xa > 20.f ? xa : log1pf(expf(xa))));
+        const float v = vv;
+        __syncwarp();
+        if (t + 1 < tokens) load(t + 1);
+        const float* kb = &ks[buf][r0];
+        const float* qb = &qs[buf][r0];
+        float m0 = 0.f, m1 = 0.f;
+#pragma unroll
+        for (int i = 0; i < HR; i += 2) {
+            s[i] *= decay;
+            s[i + 1] *= decay;
+            m0 = fmaf(s[i], kb[i], m0);
+            m1 = fmaf(s[i + 1], kb[i + 1], m1);
+        }
+        float mem = m0 + m1;
+        mem += __shfl_xor_sync(0xffffffffu, mem, 16);
+        const float delta = (v - mem) * beta;
+        float o0 = 0.f, o1 = 0.f;
+#pragma unroll
+        for (int i = 0; i < HR; i += 2) {
+            s[i] = fmaf(kb[i], delta, s[i]);
+            s[i + 1] = fmaf(kb[i + 1], delta, s[i + 1]);
+            o0 = fmaf(s[i], qb[i], o0);
+            o1 = fmaf(s[i + 1], qb[i + 1], o1);
+        }
+        float o = o0 + o1;
+        o += __shfl_xor_sync(0xffffffffu, o, 16);
+        if (live && lane < 16) out[static_cast<long long>(t) * hv * dv + static_cast<long long>(h) * dv + j] = o;
+    }
+    if (live) {
+#pragma unroll
+        for (int i = 0; i < HR; ++i) S[static_cast<long long>(r0 + i) * dv + j] = s[i];
+    }
+}
+
+// out[t, h, :] = rmsnorm(o) * w * silu(z), in place over the raw outputs of every (token, value head).
+__global__ void __launch_bounds__(256) gated_norm_kernel(float* out, const float* __restrict__ z,
+                                                         const float* __restrict__ norm_w, int dv, float eps) {
+    __shared__ float red[32];
+    pdl_wait();
+    const long long base = static_cast<long long>(blockIdx.x) * dv;
+    const int j = threadIdx.x;
+    const float o = j < dv ? out[base + j] : 0.f;
+    const float ss = block_sum(o * o, red);
+    const float rstd = rsqrtf(ss / static_cast<float>(dv) + eps);
+    if (j < dv) out[base + j] = (o * rstd) * norm_w[j] * silu(z[base + j]);
+}
+
 }  // namespace
 
 l0b_status k_causal_conv(l0b_device* d, const float* x, float* state, const float* w, float* out, int conv_dim,
                          int kernel, int tokens) {
+    if (tokens >= 16 && x != out) {
+        // Prefill: token-parallel outputs, then the window roll.
+        const long long total = static_cast<long long>(tokens) * conv_dim;
+        long long blocks = (total + 255) / 256;
+        if (blocks > d->sm_count * 16LL) blocks = d->sm_count * 16LL;
+        L0B_TRY(d->launch(causal_conv_tokens_kernel, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, x,
+                          static_cast<const float*>(state), w, out, conv_dim, kernel, tokens));
+        return d->launch(causal_conv_window_kernel, dim3((conv_dim + 127) / 128), dim3(128), 0, x, state, conv_dim,
+                         kernel, tokens);
+    }
     return d->launch(causal_conv_kernel, dim3((conv_dim + 127) / 128), dim3(128), 0, x, state, w, out, conv_dim, kernel,
                      tokens);
 }
@@ -123,6 +278,17 @@ l0b_status k_gated_delta(l0b_device* d, const float* conv, const float* z, const
                          const float* a_log, const float* dt_bias, const float* norm_w, float* state, float* out, int hk,
                          int hv, int dk, int dv, int tokens, float eps) {
     const int threads = ((dv + 31) / 32) * 32;
+    if (tokens >= 16 && (dk == 128 || dk == 64)) {
+        // Prefill: the warp-level scan, then the gated norm over all tokens.
+        const dim3 grid(hv, (dv + 15) / 16);
+        if (dk == 128)
+            L0B_TRY(d->launch(gated_delta_scan_kernel<128>, grid, dim3(32), 0, conv, b, a, a_log, dt_bias, state, out,
+                              hk, hv, dv, tokens));
+        else
+            L0B_TRY(d->launch(gated_delta_scan_kernel<64>, grid, dim3(32), 0, conv, b, a, a_log, dt_bias, state, out,
+                              hk, hv, dv, tokens));
+        return d->launch(gated_norm_kernel, dim3(tokens * hv), dim3(threads), 0, out, z, norm_w, dv, eps);
+    }
     if (dk == 128)
         return d->launch(gated_delta_kernel<128>, dim3(hv), dim3(threads), 0, conv, z, b, a, a_log, dt_bias, norm_w,
                          state, out, hk, hv, dv, tokens, eps);

@@ -540,9 +540,24 @@ L0B_API l0b_status l0b_buffer_alloc_from(l0b_device* dev, l0b_dtype dtype, int64
     return L0B_OK;
 }
 
+L0B_API l0b_status l0b_buffer_view(l0b_buffer* base, int64_t offset, int64_t count, l0b_buffer** out) {
+    L0B_REQUIRE(base && out, L0B_ERR_ARGUMENT, "null argument");
+    L0B_REQUIRE(offset >= 0 && count >= 0 && offset + count <= base->count, L0B_ERR_OUT_OF_RANGE,
+                "view [%lld, %lld) outside a %lld-element buffer", (long long)offset, (long long)(offset + count),
+                (long long)base->count);
+    l0b_buffer* v = new l0b_buffer();
+    v->dev = base->dev;
+    v->dtype = base->dtype;
+    v->count = count;
+    v->ptr = static_cast<char*>(base->ptr) + offset * dtype_size(base->dtype);
+    v->owns = false;
+    *out = v;
+    return L0B_OK;
+}
+
 L0B_API l0b_status l0b_buffer_free(l0b_buffer* buf) {
     if (!buf) return L0B_OK;
-    if (buf->ptr) {
+    if (buf->ptr && buf->owns) {
         cudaSetDevice(buf->dev->index);
         // The buffer may still be read by queued work.
         cudaStreamSynchronize(buf->dev->stream);

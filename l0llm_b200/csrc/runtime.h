@@ -223,6 +223,7 @@ struct l0b_buffer {
     l0b_dtype dtype = L0B_F32;
     int64_t count = 0;
     void* ptr = nullptr;
+    bool owns = true;  // false for a view into another buffer's memory
     size_t bytes() const { return static_cast<size_t>(count) * l0b::dtype_size(dtype); }
 };
 

@@ -122,6 +122,7 @@ def load_library() -> C.CDLL:
         "l0b_device_set_pdl": (i32, [vp, i32]),
         "l0b_buffer_alloc": (i32, [vp, i32, i64, pp]),
         "l0b_buffer_alloc_from": (i32, [vp, i32, i64, vp, pp]),
+        "l0b_buffer_view": (i32, [vp, i64, i64, pp]),
         "l0b_buffer_free": (i32, [vp]),
         "l0b_buffer_write": (i32, [vp, i64, vp, i64]),
         "l0b_buffer_read": (i32, [vp, i64, vp, i64]),
@@ -313,6 +314,12 @@ class SharedBuffer:
             check(load_library().l0b_buffer_alloc(device.handle, dtype, self.Count, C.byref(h)))
             _handle = h
         self.handle = _handle
+
+    def View(self, offset: int, count: int) -> "SharedBuffer":
+        """Elements [offset, offset + count) of this buffer (no copy, owns nothing; must not outlive it)."""
+        h = C.c_void_p()
+        check(load_library().l0b_buffer_view(self.handle, offset, count, C.byref(h)))
+        return SharedBuffer(self.device, self.dtype, count, _handle=h)
 
     @classmethod
     def from_array(cls, device: ComputeDevice, data: np.ndarray, dtype: int | None = None) -> "SharedBuffer":

@@ -414,7 +414,8 @@ def test_sampling_temperature_matches_cdf(lz, orc, device, suite, r):
 # ----------------------------------------------------------------------------------------------
 
 @pytest.mark.parametrize("hk,hv,dk,dv,tokens", [(2, 4, 128, 128, 1), (2, 4, 128, 128, 7), (4, 4, 64, 64, 5),
-                                                (16, 32, 128, 128, 2)])
+                                                (16, 32, 128, 128, 2), (2, 4, 128, 128, 16),
+                                                (4, 8, 64, 64, 100)])
 def test_causal_conv_and_gated_delta(lz, orc, device, suite, hk, hv, dk, dv, tokens):
     rng = RNG(hk * 100 + tokens)
     K = 4
@@ -535,3 +536,18 @@ def test_fused_residual_accumulate(lz, orc, device, suite, m):
     with buf(lz, device, hidden) as hb, buf(lz, device, x) as xb, buf(lz, device, q) as W, buf(lz, device, s) as S:
         suite.linear_fused(device, m, H, I, xb, W, S, I, None, 0.0, suite.EPI_ACCUM, None, hb)
         close(hb.ToArray().reshape(m, H), want, atol=1e-3, rtol=1e-4)
+
+
+def test_buffer_view_reads_and_writes_the_base(lz, device):
+    """A view names a sub-range of its base buffer: no copy, and freeing it leaves the base intact."""
+    base = lz.SharedBuffer.from_array(device, np.arange(40, dtype=np.float32))
+    v = base.View(5, 10)
+    np.testing.assert_array_equal(v.ToArray(), np.arange(5, 15, dtype=np.float32))
+    v.Write(np.full(10, -1.0, np.float32))
+    v.Dispose()
+    got = base.ToArray()
+    np.testing.assert_array_equal(got[5:15], -1.0)
+    np.testing.assert_array_equal(got[:5], np.arange(5, dtype=np.float32))
+    with pytest.raises(lz.ArgumentOutOfRangeException):
+        base.View(35, 10)
+    base.Dispose()
