@@ -340,7 +340,11 @@ L0B_API l0b_status l0b_linear(l0b_suite* s, l0b_device* d, int32_t m, int32_t n,
 typedef enum l0b_epilogue {
     L0B_EPI_STORE = 0,  /* out[m, n] = y[m, n] (+ bias) */
     L0B_EPI_ACCUM = 1,  /* out[m, n] += y[m, n] (+ bias): the residual add of o_proj / down_proj */
-    L0B_EPI_SWIGLU = 2  /* W = [gate; up] (N = 2 * I rows): out[m, i] = silu(y[m, i]) * y[m, i + I] */
+    L0B_EPI_SWIGLU = 2, /* W = [gate; up] (N = 2 * I rows): out[m, i] = silu(y[m, i]) * y[m, i + I] */
+    /* l0b_linear_tc only, OR'ed into the epilogue: the x rows enter as hi + lo 16-bit halves (each row
+     * scaled by a power of two for f16's range) so the products keep about f32 activation precision,
+     * at twice the tensor-core work; the mode the model's prefill uses. */
+    L0B_EPI_F32_ACTIVATIONS = 0x100
 } l0b_epilogue;
 
 /* Fused linear layer of the decode path: optional RMSNorm of each x row with norm_w (eps) as the
@@ -514,6 +518,10 @@ L0B_API l0b_status l0b_model_decode_greedy_device(l0b_model* model, int32_t step
 L0B_API l0b_status l0b_model_set_recording(l0b_model* model, int32_t enabled);
 /* Selects the fused decode kernels (1, default) or the one-op-per-reference-call sequence (0). */
 L0B_API l0b_status l0b_model_set_fused(l0b_model* model, int32_t enabled);
+/* Projections over at least `min_rows` activation rows (prefill chunks) with f16/bf16 weights run on
+ * the tcgen05 GEMM (weights read once per chunk, activations as hi + lo 16-bit halves); fewer rows,
+ * int8 weights and min_rows = 0 use the GEMV. Default 16. No effect on int8 models. */
+L0B_API l0b_status l0b_model_set_gemm_rows(l0b_model* model, int32_t min_rows);
 /* LlmDecoderLayer.Probe (L/LlmDecoderLayer.cs:113-119): when set, steps run the reference op sequence
  * without command-list recording and call `fn` after each stage of each layer with a host copy of the
  * stage's buffer (row 0 of the step). Stages: input_norm, q, k, v (after bias, before RoPE), attn_out

@@ -35,6 +35,8 @@ struct TcParams {
     float* out;
     const float* bias;
     int* error;
+    int split, kpad;       // split activations: 2 x nk stages, lo half at column kpad
+    const float* rscale;   // per-token result scale (split mode) or null
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -127,6 +129,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const __grid_const
     const int wt = blockIdx.y;
     const bool swiglu = p.epi == EPI_SWIGLU;
     const int nk = (p.K + kBK - 1) / kBK;
+    const int nst = p.split ? 2 * nk : nk;  // split: stage 2k + part is weight tile k against half `part`
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStages; ++s) {
@@ -153,7 +156,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const __grid_const
     bool ok = true;
     if (warp == 0 && lane == 0) {
         // TMA producer.
-        for (int kb = 0; kb < nk; ++kb) {
+        for (int kb = 0; kb < nst; ++kb) {
             const int s = kb % kStages;
             const uint32_t ph = (kb / kStages) & 1;
             if (kb >= kStages && !mbar_wait(&empty[s], ph ^ 1)) {
@@ -161,20 +164,21 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const __grid_const
                 break;
             }
             mbar_expect_tx(&full[s], A_BYTES + B_BYTES);
-            const int k0 = kb * kBK;
+            const int k0 = (p.split ? kb >> 1 : kb) * kBK;
+            const int kx = p.split ? (kb & 1) * p.kpad + k0 : k0;
             if (swiglu) {
                 tma_load_2d(sA + s * A_BYTES, &p.wmap, &full[s], k0, wt * 64);
                 tma_load_2d(sA + s * A_BYTES + A_BYTES / 2, &p.wmap, &full[s], k0, p.half_n + wt * 64);
             } else {
                 tma_load_2d(sA + s * A_BYTES, &p.wmap, &full[s], k0, wt * kBM);
             }
-            tma_load_2d(sB + s * B_BYTES, &p.xmap, &full[s], k0, t0);
+            tma_load_2d(sB + s * B_BYTES, &p.xmap, &full[s], kx, t0);
         }
     } else if (warp == 1 && lane == 0) {
         // MMA issuer: D[128, BN] (+)= A[128, 16] B[BN, 16]^T, four per stage.
         constexpr uint32_t idesc = (1u << 4) | (static_cast<uint32_t>(FMT) << 7) | (static_cast<uint32_t>(FMT) << 10) |
                                    (static_cast<uint32_t>(BN >> 3) << 17) | (static_cast<uint32_t>(kBM >> 4) << 24);
-        for (int kb = 0; kb < nk; ++kb) {
+        for (int kb = 0; kb < nst; ++kb) {
             const int s = kb % kStages;
             const uint32_t ph = (kb / kStages) & 1;
             if (!mbar_wait(&full[s], ph)) {
@@ -208,13 +212,21 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const __grid_const
                     const int t = t0 + c0 + j;
                     if (t < p.M) {
                         float* o = p.out + static_cast<long long>(t) * p.ld + n;
-                        if (p.epi == EPI_ACCUM) *o += v[j] + b;
-                        else *o = v[j] + b;
+                        const float y = p.rscale ? v[j] * p.rscale[t] : v[j];
+                        if (p.epi == EPI_ACCUM) *o += y + b;
+                        else *o = y + b;
                     }
                 }
             }
         } else {
             __syncthreads();
+            if (p.rscale) {
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                    const int t = t0 + c0 + j;
+                    v[j] *= t < p.M ? p.rscale[t] : 1.f;
+                }
+            }
             if (warp >= 2) {
 #pragma unroll
                 for (int j = 0; j < 16; ++j) xchg[((warp - 2) * 32 + lane) * 17 + j] = v[j];
@@ -259,6 +271,56 @@ __global__ void __launch_bounds__(256) cast_rows_kernel(const float* x, long lon
         float v = xr[k];
         if (norm_w) v = (v * rstd) * norm_w[k];
         store_from_float(out16, dtype, base + k, v);
+    }
+}
+
+// One block per row: RMS norm (optional) and the row maximum, then the [hi | lo] split.
+__global__ void __launch_bounds__(256) cast_rows_split_kernel(const float* x, long long ld_x, const float* norm_w,
+                                                              float eps, void* out16, float* rscale, int dtype, int K,
+                                                              int kpad) {
+    __shared__ float red[32];
+    __shared__ float mx[32];
+    pdl_wait();
+    const float* xr = x + blockIdx.x * ld_x;
+    float ss = 0.f, am = 0.f;
+    for (int k = threadIdx.x; k < K; k += blockDim.x) {
+        const float v = xr[k];
+        ss += v * v;
+        am = fmaxf(am, fabsf(norm_w ? v * norm_w[k] : v));
+    }
+    const float rstd = norm_w ? 1.0f / sqrtf(block_sum(ss, red) / static_cast<float>(K) + eps) : 1.0f;
+    am = warp_max(am);
+    if ((threadIdx.x & 31) == 0) mx[threadIdx.x >> 5] = am;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        float t = threadIdx.x < (blockDim.x >> 5) ? mx[threadIdx.x] : 0.f;
+        t = warp_max(t);
+        if (threadIdx.x == 0) mx[0] = t;
+    }
+    __syncthreads();
+    const float top = mx[0] * rstd;
+    int e = 0;
+    if (dtype == L0B_F16 && top > 0.f && isfinite(top)) {
+        int ex;
+        frexpf(top, &ex);
+        e = min(max(14 - ex, -100), 100);
+    }
+    const float sc = rstd * ldexpf(1.0f, e);
+    if (threadIdx.x == 0) rscale[blockIdx.x] = ldexpf(1.0f, -e);
+    const long long base = static_cast<long long>(blockIdx.x) * 2 * kpad;
+    for (int k = threadIdx.x; k < kpad; k += blockDim.x) {
+        float hi = 0.f, lo = 0.f;
+        if (k < K) {
+            const float v = (norm_w ? xr[k] * norm_w[k] : xr[k]) * sc;
+            if (dtype == L0B_F16) {
+                hi = __half2float(__float2half_rn(v));
+            } else {
+                hi = __bfloat162float(__float2bfloat16_rn(v));
+            }
+            lo = v - hi;
+        }
+        store_from_float(out16, dtype, base + k, hi);
+        store_from_float(out16, dtype, base + kpad + k, lo);
     }
 }
 
@@ -337,7 +399,11 @@ l0b_status tc_gemm_launch(l0b_device* d, const TcGemmArgs& a) {
     std::memset(&p, 0, sizeof(p));
     const bool swiglu = a.epi == EPI_SWIGLU;
     L0B_TRY(make_map(&p.wmap, a.w, a.wdtype, a.N, a.K, swiglu ? 64 : kBM));
-    L0B_TRY(make_map(&p.xmap, a.x16, a.wdtype, a.M, a.K, bn));
+    const int kpad = (a.K + kBK - 1) / kBK * kBK;
+    L0B_TRY(make_map(&p.xmap, a.x16, a.wdtype, a.M, a.split ? 2 * kpad : a.K, bn));
+    p.split = a.split;
+    p.kpad = kpad;
+    p.rscale = a.rscale;
     p.M = a.M;
     p.N = a.N;
     p.K = a.K;
@@ -355,6 +421,13 @@ l0b_status tc_gemm_launch(l0b_device* d, const TcGemmArgs& a) {
 l0b_status cast_rows_launch(l0b_device* d, const float* x, long long ld_x, const float* norm_w, float eps, void* out16,
                             int dtype, int M, int K) {
     return d->launch(cast_rows_kernel, dim3(M), dim3(256), 0, x, ld_x, norm_w, eps, out16, dtype, K);
+}
+
+l0b_status cast_rows_split_launch(l0b_device* d, const float* x, long long ld_x, const float* norm_w, float eps,
+                                  void* out16, float* rscale, int dtype, int M, int K) {
+    const int kpad = (K + kBK - 1) / kBK * kBK;
+    return d->launch(cast_rows_split_kernel, dim3(M), dim3(256), 0, x, ld_x, norm_w, eps, out16, rscale, dtype, K,
+                     kpad);
 }
 
 }  // namespace l0b

@@ -19,6 +19,7 @@
 #include <vector>
 
 #include "common.cuh"
+#include "gemm_tc.cuh"
 #include "gemv.cuh"
 #include "model.h"
 #include "ops.cuh"
@@ -52,6 +53,11 @@ struct l0b_model {
     float *attn = nullptr, *attn_proj = nullptr, *gate = nullptr, *up = nullptr, *act = nullptr, *down = nullptr;
     float* logits = nullptr;  // [batch_cap, vocab]
     float* head_in = nullptr; // [h] last prompt row (reference sequence: Copy.Execute)
+    // Tensor-core GEMM for projections of >= tc_rows activation rows (16-bit weights; 0 = off): the
+    // rows are split into [hi | lo] 16-bit halves in x16 with a per-row scale in rscale.
+    int tc_rows = 0;
+    void* x16 = nullptr;      // [cap, 2 * pad64(max K)] 16-bit
+    float* rscale = nullptr;  // [cap]
     // Device-side step state: io = [tok(batch_cap) | pos(batch_cap)] written in one copy.
     int* io = nullptr;
     int* tok = nullptr;
@@ -309,7 +315,38 @@ GemvParams linear_params(const ModelMatrix& w, int m_rows, const void* x, long l
     return p;
 }
 
-l0b_status gemv(l0b_model* m, const ModelMatrix& w, const GemvParams& p) { return gemv_nk_launch(m->dev, w.dtype, p); }
+// Projections over many rows (prefill chunks) with 16-bit weights run on the tcgen05 GEMM, which reads
+// the weights once; the f32 activations go in as hi + lo 16-bit halves so the products keep about the
+// precision of the f32-activation GEMV. Everything else runs on the GEMV.
+bool tc_takes(const l0b_model* m, const ModelMatrix& w, const GemvParams& p) {
+    if (!m->x16 || m->tc_rows <= 0 || p.M < m->tc_rows) return false;
+    if (w.dtype != L0B_F16 && w.dtype != L0B_BF16) return false;
+    if (p.nseg != 1 || p.x_dtype != L0B_F32 || p.out_dtype != L0B_F32) return false;
+    if (p.epi != EPI_STORE && p.epi != EPI_ACCUM && p.epi != EPI_SWIGLU) return false;
+    const int cols = p.epi == EPI_SWIGLU ? w.n / 2 : w.n;
+    if (p.seg[0].row_end != cols) return false;
+    return tc_gemm_supported(w.dtype, p.M, w.n, w.k, p.epi);
+}
+
+l0b_status gemv(l0b_model* m, const ModelMatrix& w, const GemvParams& p) {
+    if (!tc_takes(m, w, p)) return gemv_nk_launch(m->dev, w.dtype, p);
+    L0B_TRY(cast_rows_split_launch(m->dev, static_cast<const float*>(p.x), p.x_ld, p.norm_w, p.eps, m->x16,
+                                   m->rscale, w.dtype, p.M, w.k));
+    TcGemmArgs a;
+    a.M = p.M;
+    a.N = w.n;
+    a.K = w.k;
+    a.x16 = m->x16;
+    a.w = w.w;
+    a.wdtype = w.dtype;
+    a.epi = p.epi;
+    a.out = static_cast<float*>(p.seg[0].out);
+    a.ld = p.seg[0].ld;
+    a.bias = p.seg[0].bias;
+    a.split = 1;
+    a.rscale = m->rscale;
+    return tc_gemm_launch(m->dev, a);
+}
 
 // Probe (LlmDecoderLayer.Emit, L/LlmDecoderLayer.cs:427): hand a host copy of row 0 of a stage buffer to
 // the callback. Only reached when the step runs unrecorded.
@@ -951,6 +988,16 @@ L0B_API l0b_status l0b_model_create(l0b_device* dev, l0b_suite* suite, const l0b
     L0B_TRY(m->alloc(&m->act, cap * m->inter));
     L0B_TRY(m->alloc(&m->down, cap * m->h));
     L0B_TRY(m->alloc(&m->head_in, static_cast<size_t>(m->batch_cap) * m->h));
+    if (m->wdtype == L0B_F16 || m->wdtype == L0B_BF16) {
+        int kmax = m->h > m->inter ? m->h : m->inter;
+        if (m->qdim > kmax) kmax = m->qdim;
+        const size_t kpad = (static_cast<size_t>(kmax) + 63) / 64 * 64;
+        uint16_t* x16 = nullptr;
+        L0B_TRY(m->alloc(&x16, cap * 2 * kpad));
+        m->x16 = x16;
+        L0B_TRY(m->alloc(&m->rscale, cap));
+        m->tc_rows = 16;
+    }
     L0B_TRY(m->alloc(&m->logits, static_cast<size_t>(m->batch_cap) * m->vocab));
     L0B_TRY(m->alloc(&m->io, 2 * static_cast<size_t>(m->batch_cap)));
     m->tok = m->io;
@@ -1321,6 +1368,13 @@ L0B_API l0b_status l0b_model_set_fused(l0b_model* m, int32_t enabled) {
     L0B_REQUIRE(m, L0B_ERR_ARGUMENT, "model is null");
     L0B_REQUIRE(!enabled || !m->cfg.qk_norm, L0B_ERR_UNSUPPORTED, "the fused layer has no QK-norm");
     m->fused = enabled != 0;
+    return L0B_OK;
+}
+
+L0B_API l0b_status l0b_model_set_gemm_rows(l0b_model* m, int32_t min_rows) {
+    L0B_REQUIRE(m, L0B_ERR_ARGUMENT, "model is null");
+    L0B_REQUIRE(min_rows >= 0, L0B_ERR_OUT_OF_RANGE, "min_rows %d", min_rows);
+    m->tc_rows = m->x16 ? min_rows : 0;
     return L0B_OK;
 }
 

@@ -541,6 +541,8 @@ L0B_API l0b_status l0b_linear_tc(l0b_suite* s, l0b_device* d, int32_t m, int32_t
                                  l0b_buffer* w, l0b_buffer* norm_w, float eps, int32_t epilogue, l0b_buffer* bias,
                                  l0b_buffer* out) {
     L0B_TRY(check_suite(s, d));
+    const bool split = (epilogue & L0B_EPI_F32_ACTIVATIONS) != 0;
+    epilogue &= ~L0B_EPI_F32_ACTIVATIONS;
     L0B_REQUIRE(m > 0 && n > 0 && k > 0, L0B_ERR_OUT_OF_RANGE, "shape M=%d N=%d K=%d", m, n, k);
     L0B_REQUIRE(w && (w->dtype == L0B_F16 || w->dtype == L0B_BF16), L0B_ERR_ARGUMENT, "W must be f16 or bf16");
     L0B_REQUIRE(w->count >= static_cast<long long>(n) * k, L0B_ERR_ARGUMENT, "W is smaller than N*K");
@@ -554,9 +556,19 @@ L0B_API l0b_status l0b_linear_tc(l0b_suite* s, l0b_device* d, int32_t m, int32_t
     if (norm_w) L0B_TRY(need(norm_w, "norm_w", L0B_F32, k));
     if (bias) L0B_TRY(need(bias, "bias", L0B_F32, n));
     void* x16 = nullptr;
-    L0B_TRY(d->ensure_scratch(static_cast<size_t>(m) * k * 2, &x16, 1));
-    L0B_TRY(cast_rows_launch(d, F(x), k, norm_w ? F(norm_w) : nullptr, eps, x16, w->dtype, m, k));
+    float* rscale = nullptr;
+    if (split) {
+        const size_t x_bytes = static_cast<size_t>(m) * 2 * ((k + 63) / 64 * 64) * 2;
+        L0B_TRY(d->ensure_scratch(x_bytes + static_cast<size_t>(m) * sizeof(float), &x16, 1));
+        rscale = reinterpret_cast<float*>(static_cast<char*>(x16) + x_bytes);
+        L0B_TRY(cast_rows_split_launch(d, F(x), k, norm_w ? F(norm_w) : nullptr, eps, x16, rscale, w->dtype, m, k));
+    } else {
+        L0B_TRY(d->ensure_scratch(static_cast<size_t>(m) * k * 2, &x16, 1));
+        L0B_TRY(cast_rows_launch(d, F(x), k, norm_w ? F(norm_w) : nullptr, eps, x16, w->dtype, m, k));
+    }
     TcGemmArgs a;
+    a.split = split ? 1 : 0;
+    a.rscale = rscale;
     a.M = m;
     a.N = n;
     a.K = k;

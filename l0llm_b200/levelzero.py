@@ -196,6 +196,7 @@ def load_library() -> C.CDLL:
         "l0b_model_decode_greedy_device": (i32, [vp, i32, vp]),
         "l0b_model_set_recording": (i32, [vp, i32]),
         "l0b_model_set_fused": (i32, [vp, i32]),
+        "l0b_model_set_gemm_rows": (i32, [vp, i32]),
         "l0b_model_read_kv": (i32, [vp, i32, i32, i32, vp, vp]),
         "l0b_model_set_probe": (i32, [vp, PROBE_FN, vp]),
         "l0b_model_read_weight": (i32, [vp, i32, i32, vp, i64]),
@@ -543,6 +544,7 @@ class LlmKernelSuite:
                                         _h(bias), y.handle))
 
     EPI_STORE, EPI_ACCUM, EPI_SWIGLU = 0, 1, 2
+    EPI_F32_ACTIVATIONS = 0x100  # linear_tc only: x enters as hi + lo 16-bit halves
 
     def linear_fused(self, dev, M, N, K, x, W, scales, group, norm_w, eps, epilogue, bias, out):
         """RMSNorm prologue (norm_w) + projection + store / residual-add / SwiGLU epilogue, one kernel."""
@@ -730,6 +732,10 @@ class LlmModel:
 
     def set_fused(self, on: bool):
         check(load_library().l0b_model_set_fused(self.handle, 1 if on else 0))
+
+    def set_gemm_rows(self, min_rows: int):
+        """Projections over >= min_rows rows with 16-bit weights use the tcgen05 GEMM (0 = GEMV only)."""
+        check(load_library().l0b_model_set_gemm_rows(self.handle, int(min_rows)))
 
     @property
     def Probe(self):

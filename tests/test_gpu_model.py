@@ -109,6 +109,25 @@ def test_prefill_matches_token_by_token(lz, device, suite, length):
         assert max_diff(seq_after, batched_after) < 2e-3
 
 
+@pytest.mark.parametrize("precision,kv", [("float16", "f16"), ("bfloat16", "bf16")])
+@pytest.mark.parametrize("name", ["qwen2", "llama3"])
+def test_prefill_tensor_core_gemm_matches_gemv(lz, device, suite, name, precision, kv):
+    """Prefill chunks of >= 16 rows run their projections on the tcgen05 GEMM with the activations split
+    into hi + lo 16-bit halves; the logits agree with the GEMV-only prefill up to f32 summation order."""
+    rng = np.random.default_rng(7)
+    prompt = rng.integers(0, hf_tiny.TINY[name]["vocab"], 100).astype(np.int32)  # chunks of 64 and 36
+    with make_model(lz, device, suite, name, precision, kv) as model:
+        model.set_gemm_rows(0)
+        want = model.Prefill(prompt)
+        want_next = model.Decode(int(np.argmax(want)))
+        model.set_gemm_rows(16)
+        got = model.Prefill(prompt)
+        got_next = model.Decode(int(np.argmax(got)))
+    assert int(np.argmax(got)) == int(np.argmax(want))
+    assert max_diff(got, want) < 2e-3
+    assert max_diff(got_next, want_next) < 2e-3
+
+
 def test_prefill_restarts_from_position_zero(lz, device, suite):
     rng = np.random.default_rng(1)
     prompt = rng.integers(0, 384, 20).astype(np.int32)

@@ -74,6 +74,59 @@ def test_tc_gemm_norm_swiglu(lz, orc, device, suite, fmt, m):
     assert np.median(err) < 1e-3
 
 
+@pytest.mark.parametrize("fmt", ["f16", "bf16"])
+@pytest.mark.parametrize("m,n,k,epi", [(64, 512, 896, 0), (100, 4608, 3584, 1), (17, 384, 200, 0), (1, 128, 64, 1)])
+def test_tc_gemm_f32_activations(lz, orc, device, suite, fmt, m, n, k, epi):
+    """Split activations (x = hi + lo in the weight's 16-bit format, rows scaled by powers of two): the
+    result is the product of the UNROUNDED f32 rows with the 16-bit weights. Row magnitudes span 2^+-17,
+    beyond f16's range without the row scale; K = 200 leaves a zero-padded partial K tile."""
+    rng = np.random.default_rng(m * 7 + n + k)
+    x = (rng.standard_normal((m, k)) * np.exp2(rng.uniform(-17, 17, (m, 1)))).astype(np.float32)
+    w = ((rng.random((n, k)) * 2 - 1) * 0.05).astype(np.float32)
+    bias = (rng.standard_normal(n) * 0.1).astype(np.float32)
+    base = rng.standard_normal((m, n)).astype(np.float32)
+    wb = _wbits(w, fmt)
+    w16 = _round16(w, fmt).astype(np.float64)
+    want = x.astype(np.float64) @ w16.T + bias
+    if epi == 1:
+        want = want + base
+    # hi + lo keeps 16 (bf16) or 22 (f16) bits of each x; fp32 accumulation over K adds ~sqrt(K) ulps.
+    bound = np.abs(x).astype(np.float64) @ np.abs(w16).T
+    code = lz.BF16 if fmt == "bf16" else lz.F16
+    with lz.SharedBuffer.from_array(device, x) as xb, lz.SharedBuffer.from_array(device, wb, code) as W, \
+            lz.SharedBuffer.from_array(device, bias) as bb, lz.SharedBuffer.from_array(device, base) as ob:
+        lz.check(lz.load_library().l0b_linear_tc(suite.handle, device.handle, m, n, k, xb.handle, W.handle, None,
+                                                  0.0, epi | lz.LlmKernelSuite.EPI_F32_ACTIVATIONS, bb.handle,
+                                                  ob.handle))
+        got = ob.ToArray().reshape(m, n)
+    err = np.abs(got - want)
+    assert np.all(err <= 3e-5 * bound + 1e-6 * np.abs(want) + 1e-6), f"max err {err.max()}"
+
+
+@pytest.mark.parametrize("fmt", ["f16", "bf16"])
+def test_tc_gemm_f32_activations_norm_swiglu(lz, orc, device, suite, fmt):
+    rng = np.random.default_rng(11)
+    m, H, I = 48, 896, 4864
+    x = rng.standard_normal((m, H)).astype(np.float32) * 2
+    nw = (1 + 0.1 * rng.standard_normal(H)).astype(np.float32)
+    w = ((rng.random((2 * I, H)) * 2 - 1) * 0.05).astype(np.float32)
+    _, normed = orc.rmsnorm(x, nw, 1e-6)
+    wb = _wbits(w, fmt)
+    y = np.asarray(normed, np.float64) @ _round16(w, fmt).astype(np.float64).T
+    g, u = y[:, :I], y[:, I:]
+    want = g / (1 + np.exp(-g)) * u
+    code = lz.BF16 if fmt == "bf16" else lz.F16
+    with lz.SharedBuffer.from_array(device, x) as xb, lz.SharedBuffer.from_array(device, wb, code) as W, \
+            lz.SharedBuffer.from_array(device, nw) as nb, lz.SharedBuffer(device, lz.F32, m * I) as ob:
+        lz.check(lz.load_library().l0b_linear_tc(suite.handle, device.handle, m, 2 * I, H, xb.handle, W.handle,
+                                                  nb.handle, 1e-6, 2 | lz.LlmKernelSuite.EPI_F32_ACTIVATIONS, None,
+                                                  ob.handle))
+        got = ob.ToArray().reshape(m, I)
+    # Twenty times tighter than the rounded-activation bound of test_tc_gemm_norm_swiglu.
+    err = np.abs(got - want)
+    assert np.all(err <= 1e-4 + 1e-3 * np.abs(want)), f"max err {err.max()}"
+
+
 def test_tc_gemm_reports_no_timeouts(lz, device):
     import ctypes as C
 
