@@ -331,8 +331,8 @@ L0B_API l0b_status l0b_gated_delta_execute_grouped(l0b_suite* s, l0b_device* d, 
 
 /* Y[M, N] = X[M, K] * W^T (+ bias). X f32/f16/bf16, Y f32/f16/bf16; bias f32 [N] or NULL.
  * group: int8 scale group (32, or K for per-channel); ignored for 16/32-bit weights.
- * M of any size: small M streams the weights once per 8 rows on the CUDA cores, large M runs the
- * tcgen05 tensor-core GEMM (16-bit weights). */
+ * Any M: the weights stream once per 8 rows (tensor-core GEMV); l0b_linear_tc runs a prefill-sized M
+ * as one tcgen05 GEMM. */
 L0B_API l0b_status l0b_linear(l0b_suite* s, l0b_device* d, int32_t m, int32_t n, int32_t k, l0b_buffer* x,
                               l0b_buffer* w, l0b_buffer* scales, int32_t group, l0b_buffer* bias,
                               l0b_buffer* y);
@@ -362,6 +362,14 @@ L0B_API l0b_status l0b_linear_fused(l0b_suite* s, l0b_device* d, int32_t m, int3
 L0B_API l0b_status l0b_linear_tc(l0b_suite* s, l0b_device* d, int32_t m, int32_t n, int32_t k, l0b_buffer* x,
                                  l0b_buffer* w, l0b_buffer* norm_w, float eps, int32_t epilogue, l0b_buffer* bias,
                                  l0b_buffer* out);
+/* l0b_linear_tc for int8 weights: W int8 [N, K] (K % 16 == 0) with one f16 scale per row (scales [N],
+ * group = K or <= 0). TMA stages the raw bytes, two warps convert them to f16 in shared memory (exact),
+ * the MMA runs in f16 (activations rounded to f16, or split into hi + lo f16 halves with
+ * L0B_EPI_F32_ACTIVATIONS), and the epilogue applies the row scale. Group-wise scales are refused
+ * (L0B_ERR_UNSUPPORTED): they stay on the GEMV. f16/bf16 W are accepted and scales ignored. */
+L0B_API l0b_status l0b_linear_tc_scaled(l0b_suite* s, l0b_device* d, int32_t m, int32_t n, int32_t k, l0b_buffer* x,
+                                        l0b_buffer* w, l0b_buffer* scales, int32_t group, l0b_buffer* norm_w,
+                                        float eps, int32_t epilogue, l0b_buffer* bias, l0b_buffer* out);
 
 /* ------------------------------------------------------------------------------------------ */
 /* Tensor parallelism (one process per GPU, NCCL over NVLink/NVSwitch)                           */
@@ -518,9 +526,9 @@ L0B_API l0b_status l0b_model_decode_greedy_device(l0b_model* model, int32_t step
 L0B_API l0b_status l0b_model_set_recording(l0b_model* model, int32_t enabled);
 /* Selects the fused decode kernels (1, default) or the one-op-per-reference-call sequence (0). */
 L0B_API l0b_status l0b_model_set_fused(l0b_model* model, int32_t enabled);
-/* Projections over at least `min_rows` activation rows (prefill chunks) with f16/bf16 weights run on
- * the tcgen05 GEMM (weights read once per chunk, activations as hi + lo 16-bit halves); fewer rows,
- * int8 weights and min_rows = 0 use the GEMV. Default 16. No effect on int8 models. */
+/* Projections over at least `min_rows` activation rows (prefill chunks) with f16/bf16 weights, or int8
+ * weights with one scale per row, run on the tcgen05 GEMM (weights read once per chunk, activations as
+ * hi + lo 16-bit halves); fewer rows, group-wise int8 and min_rows = 0 use the GEMV. Default 16. */
 L0B_API l0b_status l0b_model_set_gemm_rows(l0b_model* model, int32_t min_rows);
 /* LlmDecoderLayer.Probe (L/LlmDecoderLayer.cs:113-119): when set, steps run the reference op sequence
  * without command-list recording and call `fn` after each stage of each layer with a host copy of the

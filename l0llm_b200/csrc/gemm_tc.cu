@@ -10,6 +10,9 @@
 // variant loads 64 gate rows and the 64 matching up rows into one tile and pairs them in the epilogue.
 // Every mbarrier wait is bounded (~2 s); a timeout sets the device error flag and the CTA exits after
 // releasing its tensor memory. No TMA multicast is used.
+// int8 weights (one scale per weight row): TMA brings the raw [128 x 64] byte tile, warps 2-3 turn it
+// into the swizzled f16 A tile (exact: |q| <= 128) and hand it to the MMA issuer through a third
+// mbarrier; the epilogue multiplies by the row's scale.
 #include <cuda.h>
 
 #include <cstring>
@@ -29,7 +32,7 @@ constexpr int kThreads = 128;
 constexpr long long kWaitCycles = 4000000000LL;
 
 struct TcParams {
-    CUtensorMap wmap;  // W [N, K] 16-bit, box {64, 128} (SwiGLU: {64, 64})
+    CUtensorMap wmap;  // W [N, K] 16-bit (int8: bytes, no swizzle), box {64, 128} (SwiGLU: {64, 64})
     CUtensorMap xmap;  // X [M, K] 16-bit, box {64, BN}
     int M, N, K, epi, ld, half_n;
     float* out;
@@ -37,7 +40,18 @@ struct TcParams {
     int* error;
     int split, kpad;       // split activations: 2 x nk stages, lo half at column kpad
     const float* rscale;   // per-token result scale (split mode) or null
+    const __half* wscale;  // int8: f16 scale per weight row
 };
+
+// Four signed bytes -> two f16x2 (bytes 0,1 and bytes 2,3), exact: u = b ^ 0x80 placed in the low
+// mantissa of 1024.0 (0x64uu) is 1024 + u, and subtracting 1152 leaves b.
+__device__ __forceinline__ void i8x4_to_h2x2(uint32_t w, uint32_t& lo, uint32_t& hi) {
+    const uint32_t u = w ^ 0x80808080u;
+    const uint32_t p0 = __byte_perm(u, 0x64646464u, 0x5140);
+    const uint32_t p1 = __byte_perm(u, 0x64646464u, 0x5342);
+    asm("sub.f16x2 %0, %1, %2;" : "=r"(lo) : "r"(p0), "r"(0x64806480u));
+    asm("sub.f16x2 %0, %1, %2;" : "=r"(hi) : "r"(p1), "r"(0x64806480u));
+}
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -45,6 +59,10 @@ __device__ __forceinline__ uint32_t smem_u32(const void* p) {
 
 __device__ __forceinline__ void mbar_init(uint64_t* b, uint32_t count) {
     asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(b)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* b) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(b)) : "memory");
 }
 
 __device__ __forceinline__ void mbar_expect_tx(uint64_t* b, uint32_t bytes) {
@@ -111,17 +129,23 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
     for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// FMT: 0 = f16, 1 = bf16 (weights and activations), 2 = int8 weights converted to f16 in shared memory.
 template <int BN, int FMT>
 __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const __grid_constant__ TcParams p) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    constexpr bool kQ8 = FMT == 2;
+    constexpr uint32_t MMA_FMT = FMT == 1 ? 1 : 0;
     constexpr int A_BYTES = kBM * kBK * 2;
     constexpr int B_BYTES = BN * kBK * 2;
+    constexpr int Q_BYTES = kQ8 ? kBM * kBK : 0;
     uint8_t* sA = smem;
     uint8_t* sB = smem + kStages * A_BYTES;
-    uint64_t* full = reinterpret_cast<uint64_t*>(sB + kStages * B_BYTES);
+    uint8_t* sQ = sB + kStages * B_BYTES;  // int8: raw weight tiles [128][64] bytes
+    uint64_t* full = reinterpret_cast<uint64_t*>(sQ + kStages * Q_BYTES);
     uint64_t* empty = full + kStages;
-    uint64_t* accum = empty + kStages;
+    uint64_t* conv = empty + kStages;  // int8: the converted A tile of stage s is ready
+    uint64_t* accum = conv + kStages;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -135,6 +159,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const __grid_const
         for (int s = 0; s < kStages; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1);
+            mbar_init(&conv[s], 64);
         }
         mbar_init(accum, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -163,25 +188,26 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const __grid_const
                 ok = false;
                 break;
             }
-            mbar_expect_tx(&full[s], A_BYTES + B_BYTES);
+            mbar_expect_tx(&full[s], (kQ8 ? Q_BYTES : A_BYTES) + B_BYTES);
             const int k0 = (p.split ? kb >> 1 : kb) * kBK;
             const int kx = p.split ? (kb & 1) * p.kpad + k0 : k0;
+            uint8_t* wdst = kQ8 ? sQ + s * Q_BYTES : sA + s * A_BYTES;
             if (swiglu) {
-                tma_load_2d(sA + s * A_BYTES, &p.wmap, &full[s], k0, wt * 64);
-                tma_load_2d(sA + s * A_BYTES + A_BYTES / 2, &p.wmap, &full[s], k0, p.half_n + wt * 64);
+                tma_load_2d(wdst, &p.wmap, &full[s], k0, wt * 64);
+                tma_load_2d(wdst + (kQ8 ? Q_BYTES : A_BYTES) / 2, &p.wmap, &full[s], k0, p.half_n + wt * 64);
             } else {
-                tma_load_2d(sA + s * A_BYTES, &p.wmap, &full[s], k0, wt * kBM);
+                tma_load_2d(wdst, &p.wmap, &full[s], k0, wt * kBM);
             }
             tma_load_2d(sB + s * B_BYTES, &p.xmap, &full[s], kx, t0);
         }
     } else if (warp == 1 && lane == 0) {
         // MMA issuer: D[128, BN] (+)= A[128, 16] B[BN, 16]^T, four per stage.
-        constexpr uint32_t idesc = (1u << 4) | (static_cast<uint32_t>(FMT) << 7) | (static_cast<uint32_t>(FMT) << 10) |
+        constexpr uint32_t idesc = (1u << 4) | (MMA_FMT << 7) | (MMA_FMT << 10) |
                                    (static_cast<uint32_t>(BN >> 3) << 17) | (static_cast<uint32_t>(kBM >> 4) << 24);
         for (int kb = 0; kb < nst; ++kb) {
             const int s = kb % kStages;
             const uint32_t ph = (kb / kStages) & 1;
-            if (!mbar_wait(&full[s], ph)) {
+            if (!mbar_wait(&full[s], ph) || (kQ8 && !mbar_wait(&conv[s], ph))) {
                 ok = false;
                 break;
             }
@@ -192,6 +218,36 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const __grid_const
             tc_commit(&empty[s]);
         }
         tc_commit(accum);
+    } else if (kQ8 && warp >= 2) {
+        // Converters: 512 16-byte pieces of int8 per stage, 8 per thread; row r's f16 chunk c goes to
+        // 16-byte slot c ^ (r & 7) of its 128-byte row (the TMA / UMMA 128-byte swizzle).
+        const int ct = threadIdx.x - 64;
+        for (int kb = 0; kb < nst; ++kb) {
+            const int s = kb % kStages;
+            const uint32_t ph = (kb / kStages) & 1;
+            if (!mbar_wait(&full[s], ph)) {
+                ok = false;
+                break;
+            }
+            const uint8_t* q = sQ + s * Q_BYTES;
+            uint8_t* a = sA + s * A_BYTES;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const int c = ct + 64 * i;
+                const int r = c >> 2, j = c & 3;
+                const uint4 w = *reinterpret_cast<const uint4*>(q + r * 64 + j * 16);
+                uint4 o0, o1;
+                i8x4_to_h2x2(w.x, o0.x, o0.y);
+                i8x4_to_h2x2(w.y, o0.z, o0.w);
+                i8x4_to_h2x2(w.z, o1.x, o1.y);
+                i8x4_to_h2x2(w.w, o1.z, o1.w);
+                *reinterpret_cast<uint4*>(a + r * 128 + (((2 * j) ^ (r & 7)) << 4)) = o0;
+                *reinterpret_cast<uint4*>(a + r * 128 + (((2 * j + 1) ^ (r & 7)) << 4)) = o1;
+            }
+            // Generic-proxy writes become visible to the tensor core's (async proxy) reads.
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            mbar_arrive(&conv[s]);
+        }
     }
     __syncwarp();
 
@@ -203,6 +259,13 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const __grid_const
     for (int c0 = 0; c0 < BN; c0 += 16) {
         float v[16];
         tmem_ld16(tmem + (static_cast<uint32_t>(warp * 32) << 16) + c0, v);
+        if (kQ8) {
+            const int row = swiglu ? (warp < 2 ? 0 : p.half_n) + wt * 64 + (warp & 1) * 32 + lane
+                                   : wt * kBM + warp * 32 + lane;
+            const float ws = row < p.N ? __half2float(p.wscale[row]) : 0.f;
+#pragma unroll
+            for (int j = 0; j < 16; ++j) v[j] *= ws;
+        }
         if (!swiglu) {
             const int n = wt * kBM + warp * 32 + lane;
             if (acc_ok && n < p.N) {
@@ -342,19 +405,24 @@ EncodeTiledFn encode_fn() {
     return fn;
 }
 
-// Row-major [rows, K] 16-bit matrix, box {64 elements, box_rows}, 128-byte swizzle.
+// Row-major [rows, K] matrix, box {64 elements, box_rows}: 16-bit with the 128-byte swizzle, or int8
+// bytes unswizzled (the converter warps read them as plain 64-byte rows).
 l0b_status make_map(CUtensorMap* map, const void* base, int dtype, long long rows, long long K, int box_rows) {
     EncodeTiledFn fn = encode_fn();
     L0B_REQUIRE(fn, L0B_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
-    L0B_REQUIRE(reinterpret_cast<uintptr_t>(base) % 16 == 0 && (K * 2) % 16 == 0, L0B_ERR_ARGUMENT,
-                "TMA needs 16-byte aligned rows (K %% 8 == 0)");
+    const long long esize = dtype == L0B_I8 ? 1 : 2;
+    L0B_REQUIRE(reinterpret_cast<uintptr_t>(base) % 16 == 0 && (K * esize) % 16 == 0, L0B_ERR_ARGUMENT,
+                "TMA needs 16-byte aligned rows (K * element size %% 16 == 0)");
     const cuuint64_t dims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(rows)};
-    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(K * 2)};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(K * esize)};
     const cuuint32_t box[2] = {static_cast<cuuint32_t>(kBK), static_cast<cuuint32_t>(box_rows)};
     const cuuint32_t estr[2] = {1, 1};
-    CUresult r = fn(map, dtype == L0B_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
-                    const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                    CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    const CUtensorMapDataType type = dtype == L0B_I8     ? CU_TENSOR_MAP_DATA_TYPE_UINT8
+                                     : dtype == L0B_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                         : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    CUresult r = fn(map, type, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                    dtype == L0B_I8 ? CU_TENSOR_MAP_SWIZZLE_NONE : CU_TENSOR_MAP_SWIZZLE_128B,
+                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     L0B_REQUIRE(r == CUDA_SUCCESS, L0B_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", static_cast<int>(r));
     return L0B_OK;
 }
@@ -362,7 +430,7 @@ l0b_status make_map(CUtensorMap* map, const void* base, int dtype, long long row
 template <int BN, int FMT>
 l0b_status launch_bn(l0b_device* d, const TcParams& p, int grid_y) {
     auto kernel = tc_gemm_kernel<BN, FMT>;
-    constexpr size_t smem = 1024 + kStages * (kBM * kBK * 2 + BN * kBK * 2) + 256;
+    constexpr size_t smem = 1024 + kStages * (kBM * kBK * 2 + BN * kBK * 2 + (FMT == 2 ? kBM * kBK : 0)) + 256;
     static bool configured = false;
     if (!configured) {
         cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
@@ -385,8 +453,8 @@ l0b_status launch_fmt(l0b_device* d, const TcParams& p, int bn, int grid_y) {
 }  // namespace
 
 bool tc_gemm_supported(int wdtype, int M, int N, int K, int epi) {
-    if (wdtype != L0B_F16 && wdtype != L0B_BF16) return false;
-    if (M < 1 || N < 1 || K < 64 || K % 8 != 0) return false;
+    if (wdtype != L0B_F16 && wdtype != L0B_BF16 && wdtype != L0B_I8) return false;
+    if (M < 1 || N < 1 || K < 64 || K % (wdtype == L0B_I8 ? 16 : 8) != 0) return false;
     if (epi == EPI_SWIGLU && (N % 2 != 0 || (N / 2) % 64 != 0)) return false;
     return epi == EPI_STORE || epi == EPI_ACCUM || epi == EPI_SWIGLU;
 }
@@ -398,9 +466,12 @@ l0b_status tc_gemm_launch(l0b_device* d, const TcGemmArgs& a) {
     TcParams p;
     std::memset(&p, 0, sizeof(p));
     const bool swiglu = a.epi == EPI_SWIGLU;
+    const bool q8 = a.wdtype == L0B_I8;
+    L0B_REQUIRE(!q8 || a.wscale, L0B_ERR_ARGUMENT, "int8 weights need their row scales");
     L0B_TRY(make_map(&p.wmap, a.w, a.wdtype, a.N, a.K, swiglu ? 64 : kBM));
     const int kpad = (a.K + kBK - 1) / kBK * kBK;
-    L0B_TRY(make_map(&p.xmap, a.x16, a.wdtype, a.M, a.split ? 2 * kpad : a.K, bn));
+    L0B_TRY(make_map(&p.xmap, a.x16, q8 ? L0B_F16 : a.wdtype, a.M, a.split ? 2 * kpad : a.K, bn));
+    p.wscale = static_cast<const __half*>(a.wscale);
     p.split = a.split;
     p.kpad = kpad;
     p.rscale = a.rscale;
@@ -414,6 +485,7 @@ l0b_status tc_gemm_launch(l0b_device* d, const TcGemmArgs& a) {
     p.bias = a.bias;
     p.error = d->error_flag;
     const int grid_y = swiglu ? (a.N / 2) / 64 : (a.N + kBM - 1) / kBM;
+    if (q8) return launch_fmt<2>(d, p, bn, grid_y);
     if (a.wdtype == L0B_BF16) return launch_fmt<1>(d, p, bn, grid_y);
     return launch_fmt<0>(d, p, bn, grid_y);
 }

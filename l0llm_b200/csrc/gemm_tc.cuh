@@ -8,8 +8,8 @@ namespace l0b {
 struct TcGemmArgs {
     int M, N, K;           // tokens, weight rows, inner dimension
     const void* x16;       // [M, K] activations in the weight's 16-bit format (row stride K)
-    const void* w;         // [N, K] weights, f16 or bf16
-    int wdtype;            // L0B_F16 or L0B_BF16
+    const void* w;         // [N, K] weights, f16, bf16 or int8
+    int wdtype;            // L0B_F16, L0B_BF16 or L0B_I8 (activations then f16)
     int epi;               // GemvEpi: STORE, ACCUM or SWIGLU (W = [gate; up], N = 2 * I)
     float* out;            // f32 output, row stride ld (SWIGLU: [M, N/2])
     int ld;
@@ -19,6 +19,7 @@ struct TcGemmArgs {
     // same accumulator, and row t of the result is multiplied by rscale[t].
     int split = 0;
     const float* rscale = nullptr;
+    const void* wscale = nullptr;  // int8: f16 [N], one scale per weight row
 };
 
 // Launches the GEMM on the device's stream (recorded when the device records).
@@ -34,7 +35,8 @@ l0b_status cast_rows_launch(l0b_device* d, const float* x, long long ld_x, const
 l0b_status cast_rows_split_launch(l0b_device* d, const float* x, long long ld_x, const float* norm_w, float eps,
                                   void* out16, float* rscale, int dtype, int M, int K);
 
-// True when the tensor-core path takes this shape (16-bit weights, K % 64 == 0, N tile-aligned).
+// True when the tensor-core path takes this shape: f16/bf16 weights with K % 8 == 0 or int8 weights
+// (per-row scales) with K % 16 == 0, K >= 64; SwiGLU needs (N / 2) % 64 == 0.
 bool tc_gemm_supported(int wdtype, int M, int N, int K, int epi);
 
 }  // namespace l0b

@@ -53,8 +53,9 @@ struct l0b_model {
     float *attn = nullptr, *attn_proj = nullptr, *gate = nullptr, *up = nullptr, *act = nullptr, *down = nullptr;
     float* logits = nullptr;  // [batch_cap, vocab]
     float* head_in = nullptr; // [h] last prompt row (reference sequence: Copy.Execute)
-    // Tensor-core GEMM for projections of >= tc_rows activation rows (16-bit weights; 0 = off): the
-    // rows are split into [hi | lo] 16-bit halves in x16 with a per-row scale in rscale.
+    // Tensor-core GEMM for projections of >= tc_rows activation rows (16-bit weights, or int8 with one
+    // scale per row; 0 = off): the rows are split into [hi | lo] 16-bit halves in x16 with a per-row
+    // scale in rscale.
     int tc_rows = 0;
     void* x16 = nullptr;      // [cap, 2 * pad64(max K)] 16-bit
     float* rscale = nullptr;  // [cap]
@@ -315,12 +316,13 @@ GemvParams linear_params(const ModelMatrix& w, int m_rows, const void* x, long l
     return p;
 }
 
-// Projections over many rows (prefill chunks) with 16-bit weights run on the tcgen05 GEMM, which reads
-// the weights once; the f32 activations go in as hi + lo 16-bit halves so the products keep about the
-// precision of the f32-activation GEMV. Everything else runs on the GEMV.
+// Projections over many rows (prefill chunks) run on the tcgen05 GEMM, which reads the weights once; the
+// f32 activations go in as hi + lo 16-bit halves so the products keep about the precision of the
+// f32-activation GEMV. int8 weights qualify with one scale per row (exact f16 integers times the row
+// scale in the epilogue, as on the GEMV); group-wise int8 and everything else runs on the GEMV.
 bool tc_takes(const l0b_model* m, const ModelMatrix& w, const GemvParams& p) {
     if (!m->x16 || m->tc_rows <= 0 || p.M < m->tc_rows) return false;
-    if (w.dtype != L0B_F16 && w.dtype != L0B_BF16) return false;
+    if (w.dtype != L0B_F16 && w.dtype != L0B_BF16 && !(w.dtype == L0B_I8 && w.group >= w.k)) return false;
     if (p.nseg != 1 || p.x_dtype != L0B_F32 || p.out_dtype != L0B_F32) return false;
     if (p.epi != EPI_STORE && p.epi != EPI_ACCUM && p.epi != EPI_SWIGLU) return false;
     const int cols = p.epi == EPI_SWIGLU ? w.n / 2 : w.n;
@@ -331,7 +333,7 @@ bool tc_takes(const l0b_model* m, const ModelMatrix& w, const GemvParams& p) {
 l0b_status gemv(l0b_model* m, const ModelMatrix& w, const GemvParams& p) {
     if (!tc_takes(m, w, p)) return gemv_nk_launch(m->dev, w.dtype, p);
     L0B_TRY(cast_rows_split_launch(m->dev, static_cast<const float*>(p.x), p.x_ld, p.norm_w, p.eps, m->x16,
-                                   m->rscale, w.dtype, p.M, w.k));
+                                   m->rscale, w.dtype == L0B_I8 ? L0B_F16 : w.dtype, p.M, w.k));
     TcGemmArgs a;
     a.M = p.M;
     a.N = w.n;
@@ -345,6 +347,7 @@ l0b_status gemv(l0b_model* m, const ModelMatrix& w, const GemvParams& p) {
     a.bias = p.seg[0].bias;
     a.split = 1;
     a.rscale = m->rscale;
+    a.wscale = w.dtype == L0B_I8 ? w.scales : nullptr;
     return tc_gemm_launch(m->dev, a);
 }
 
@@ -988,7 +991,7 @@ L0B_API l0b_status l0b_model_create(l0b_device* dev, l0b_suite* suite, const l0b
     L0B_TRY(m->alloc(&m->act, cap * m->inter));
     L0B_TRY(m->alloc(&m->down, cap * m->h));
     L0B_TRY(m->alloc(&m->head_in, static_cast<size_t>(m->batch_cap) * m->h));
-    if (m->wdtype == L0B_F16 || m->wdtype == L0B_BF16) {
+    if (m->wdtype == L0B_F16 || m->wdtype == L0B_BF16 || m->wdtype == L0B_I8) {
         int kmax = m->h > m->inter ? m->h : m->inter;
         if (m->qdim > kmax) kmax = m->qdim;
         const size_t kpad = (static_cast<size_t>(kmax) + 63) / 64 * 64;

@@ -537,38 +537,49 @@ L0B_API l0b_status l0b_linear_fused(l0b_suite* s, l0b_device* d, int32_t m, int3
     return gemv_nk_launch(d, wdt, p);
 }
 
-L0B_API l0b_status l0b_linear_tc(l0b_suite* s, l0b_device* d, int32_t m, int32_t n, int32_t k, l0b_buffer* x,
-                                 l0b_buffer* w, l0b_buffer* norm_w, float eps, int32_t epilogue, l0b_buffer* bias,
-                                 l0b_buffer* out) {
+namespace {
+
+l0b_status linear_tc(l0b_suite* s, l0b_device* d, int32_t m, int32_t n, int32_t k, l0b_buffer* x, l0b_buffer* w,
+                     l0b_buffer* scales, int32_t group, l0b_buffer* norm_w, float eps, int32_t epilogue,
+                     l0b_buffer* bias, l0b_buffer* out) {
     L0B_TRY(check_suite(s, d));
     const bool split = (epilogue & L0B_EPI_F32_ACTIVATIONS) != 0;
     epilogue &= ~L0B_EPI_F32_ACTIVATIONS;
     L0B_REQUIRE(m > 0 && n > 0 && k > 0, L0B_ERR_OUT_OF_RANGE, "shape M=%d N=%d K=%d", m, n, k);
-    L0B_REQUIRE(w && (w->dtype == L0B_F16 || w->dtype == L0B_BF16), L0B_ERR_ARGUMENT, "W must be f16 or bf16");
+    L0B_REQUIRE(w && (w->dtype == L0B_F16 || w->dtype == L0B_BF16 || w->dtype == L0B_I8), L0B_ERR_ARGUMENT,
+                "W must be f16, bf16 or int8");
     L0B_REQUIRE(w->count >= static_cast<long long>(n) * k, L0B_ERR_ARGUMENT, "W is smaller than N*K");
+    const bool q8 = w->dtype == L0B_I8;
+    if (q8) {
+        L0B_REQUIRE(group <= 0 || group >= k, L0B_ERR_UNSUPPORTED,
+                    "the tensor-core GEMM takes int8 weights with one scale per row (group = K), not group %d", group);
+        L0B_TRY(need(scales, "scales", L0B_F16, n));
+    }
     const int epi = epilogue == L0B_EPI_ACCUM ? EPI_ACCUM : epilogue == L0B_EPI_SWIGLU ? EPI_SWIGLU : EPI_STORE;
     L0B_REQUIRE(tc_gemm_supported(w->dtype, m, n, k, epi), L0B_ERR_UNSUPPORTED,
-                "the tensor-core GEMM needs K %% 8 == 0, K >= 64 and for SwiGLU (N/2) %% 64 == 0");
+                "the tensor-core GEMM needs K >= 64, K %% 8 == 0 (int8: %% 16) and for SwiGLU (N/2) %% 64 == 0");
     L0B_REQUIRE(epi != EPI_SWIGLU || !bias, L0B_ERR_ARGUMENT, "the SwiGLU epilogue takes no bias");
     const int out_cols = epi == EPI_SWIGLU ? n / 2 : n;
     L0B_TRY(need(x, "x", L0B_F32, static_cast<long long>(m) * k));
     L0B_TRY(need(out, "out", L0B_F32, static_cast<long long>(m) * out_cols));
     if (norm_w) L0B_TRY(need(norm_w, "norm_w", L0B_F32, k));
     if (bias) L0B_TRY(need(bias, "bias", L0B_F32, n));
+    const int xdtype = q8 ? L0B_F16 : w->dtype;  // int8 weights meet f16 activations
     void* x16 = nullptr;
     float* rscale = nullptr;
     if (split) {
         const size_t x_bytes = static_cast<size_t>(m) * 2 * ((k + 63) / 64 * 64) * 2;
         L0B_TRY(d->ensure_scratch(x_bytes + static_cast<size_t>(m) * sizeof(float), &x16, 1));
         rscale = reinterpret_cast<float*>(static_cast<char*>(x16) + x_bytes);
-        L0B_TRY(cast_rows_split_launch(d, F(x), k, norm_w ? F(norm_w) : nullptr, eps, x16, rscale, w->dtype, m, k));
+        L0B_TRY(cast_rows_split_launch(d, F(x), k, norm_w ? F(norm_w) : nullptr, eps, x16, rscale, xdtype, m, k));
     } else {
         L0B_TRY(d->ensure_scratch(static_cast<size_t>(m) * k * 2, &x16, 1));
-        L0B_TRY(cast_rows_launch(d, F(x), k, norm_w ? F(norm_w) : nullptr, eps, x16, w->dtype, m, k));
+        L0B_TRY(cast_rows_launch(d, F(x), k, norm_w ? F(norm_w) : nullptr, eps, x16, xdtype, m, k));
     }
     TcGemmArgs a;
     a.split = split ? 1 : 0;
     a.rscale = rscale;
+    a.wscale = q8 ? scales->ptr : nullptr;
     a.M = m;
     a.N = n;
     a.K = k;
@@ -580,6 +591,21 @@ L0B_API l0b_status l0b_linear_tc(l0b_suite* s, l0b_device* d, int32_t m, int32_t
     a.ld = out_cols;
     a.bias = bias ? F(bias) : nullptr;
     return tc_gemm_launch(d, a);
+}
+
+}  // namespace
+
+L0B_API l0b_status l0b_linear_tc(l0b_suite* s, l0b_device* d, int32_t m, int32_t n, int32_t k, l0b_buffer* x,
+                                 l0b_buffer* w, l0b_buffer* norm_w, float eps, int32_t epilogue, l0b_buffer* bias,
+                                 l0b_buffer* out) {
+    L0B_REQUIRE(!w || w->dtype != L0B_I8, L0B_ERR_ARGUMENT, "int8 weights go through l0b_linear_tc_scaled");
+    return linear_tc(s, d, m, n, k, x, w, nullptr, 0, norm_w, eps, epilogue, bias, out);
+}
+
+L0B_API l0b_status l0b_linear_tc_scaled(l0b_suite* s, l0b_device* d, int32_t m, int32_t n, int32_t k, l0b_buffer* x,
+                                        l0b_buffer* w, l0b_buffer* scales, int32_t group, l0b_buffer* norm_w,
+                                        float eps, int32_t epilogue, l0b_buffer* bias, l0b_buffer* out) {
+    return linear_tc(s, d, m, n, k, x, w, scales, group, norm_w, eps, epilogue, bias, out);
 }
 
 L0B_API l0b_status l0b_set_gemv_tensor_cores(int32_t enable) {

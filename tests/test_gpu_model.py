@@ -109,11 +109,12 @@ def test_prefill_matches_token_by_token(lz, device, suite, length):
         assert max_diff(seq_after, batched_after) < 2e-3
 
 
-@pytest.mark.parametrize("precision,kv", [("float16", "f16"), ("bfloat16", "bf16")])
+@pytest.mark.parametrize("precision,kv", [("float16", "f16"), ("bfloat16", "bf16"), ("int8", "f16")])
 @pytest.mark.parametrize("name", ["qwen2", "llama3"])
 def test_prefill_tensor_core_gemm_matches_gemv(lz, device, suite, name, precision, kv):
     """Prefill chunks of >= 16 rows run their projections on the tcgen05 GEMM with the activations split
-    into hi + lo 16-bit halves; the logits agree with the GEMV-only prefill up to f32 summation order."""
+    into hi + lo 16-bit halves (int8: per-row scales, bytes converted to f16 in shared memory); the
+    logits agree with the GEMV-only prefill up to f32 summation order."""
     rng = np.random.default_rng(7)
     prompt = rng.integers(0, hf_tiny.TINY[name]["vocab"], 100).astype(np.int32)  # chunks of 64 and 36
     with make_model(lz, device, suite, name, precision, kv) as model:

@@ -127,6 +127,70 @@ def test_tc_gemm_f32_activations_norm_swiglu(lz, orc, device, suite, fmt):
     assert np.all(err <= 1e-4 + 1e-3 * np.abs(want)), f"max err {err.max()}"
 
 
+def _q8_rows(rng, n, k):
+    q = rng.integers(-127, 128, (n, k)).astype(np.int8)
+    q[:, 0] = -128  # the full int8 range converts exactly
+    s16 = (rng.random(n) * 2e-3 + 1e-4).astype(np.float16)
+    return q, s16
+
+
+@pytest.mark.parametrize("split", [False, True])
+@pytest.mark.parametrize("m,n,k,epi", [(64, 512, 896, 0), (100, 4608, 3584, 1), (17, 384, 208, 0), (300, 256, 512, 1)])
+def test_tc_gemm_int8_row_scales(lz, device, suite, split, m, n, k, epi):
+    """int8 weights with one f16 scale per row: raw bytes by TMA, converted to f16 in shared memory by
+    two warps, row scale in the epilogue. The integers are exact in f16, so against the f64 product the
+    only differences are the activation rounding (none in split mode past 22 bits) and fp32 sums."""
+    rng = np.random.default_rng(m + n * 3 + k)
+    x = (rng.standard_normal((m, k)) * np.exp2(rng.uniform(-8, 8, (m, 1)))).astype(np.float32)
+    q, s16 = _q8_rows(rng, n, k)
+    bias = (rng.standard_normal(n) * 0.1).astype(np.float32)
+    base = rng.standard_normal((m, n)).astype(np.float32)
+    xa = x.astype(np.float64) if split else _round16(x, "f16").astype(np.float64)
+    sc = s16.astype(np.float64)
+    want = (xa @ q.astype(np.float64).T) * sc + bias
+    if epi == 1:
+        want = want + base
+    bound = (np.abs(xa) @ np.abs(q.astype(np.float64)).T) * sc
+    flag = lz.LlmKernelSuite.EPI_F32_ACTIVATIONS if split else 0
+    with lz.SharedBuffer.from_array(device, x) as xb, lz.SharedBuffer.from_array(device, q, lz.I8) as W, \
+            lz.SharedBuffer.from_array(device, s16.view(np.uint16), lz.F16) as S, \
+            lz.SharedBuffer.from_array(device, bias) as bb, lz.SharedBuffer.from_array(device, base) as ob:
+        lz.check(lz.load_library().l0b_linear_tc_scaled(suite.handle, device.handle, m, n, k, xb.handle, W.handle,
+                                                         S.handle, k, None, 0.0, epi | flag, bb.handle, ob.handle))
+        got = ob.ToArray().reshape(m, n)
+    err = np.abs(got - want)
+    assert np.all(err <= 1e-5 * bound + 1e-6 * np.abs(want) + 1e-6), f"max err {err.max()}"
+
+
+def test_tc_gemm_int8_norm_swiglu(lz, orc, device, suite):
+    rng = np.random.default_rng(21)
+    m, H, I = 48, 896, 4864
+    x = rng.standard_normal((m, H)).astype(np.float32) * 2
+    nw = (1 + 0.1 * rng.standard_normal(H)).astype(np.float32)
+    q, s16 = _q8_rows(rng, 2 * I, H)
+    _, normed = orc.rmsnorm(x, nw, 1e-6)
+    y = (np.asarray(normed, np.float64) @ q.astype(np.float64).T) * s16.astype(np.float64)
+    g, u = y[:, :I], y[:, I:]
+    want = g / (1 + np.exp(-g)) * u
+    with lz.SharedBuffer.from_array(device, x) as xb, lz.SharedBuffer.from_array(device, q, lz.I8) as W, \
+            lz.SharedBuffer.from_array(device, s16.view(np.uint16), lz.F16) as S, \
+            lz.SharedBuffer.from_array(device, nw) as nb, lz.SharedBuffer(device, lz.F32, m * I) as ob:
+        lz.check(lz.load_library().l0b_linear_tc_scaled(suite.handle, device.handle, m, 2 * I, H, xb.handle,
+                                                         W.handle, S.handle, 0, nb.handle, 1e-6,
+                                                         2 | lz.LlmKernelSuite.EPI_F32_ACTIVATIONS, None, ob.handle))
+        got = ob.ToArray().reshape(m, I)
+    err = np.abs(got - want)
+    assert np.all(err <= 1e-4 + 1e-3 * np.abs(want)), f"max err {err.max()}"
+
+
+def test_tc_gemm_int8_refuses_group_scales(lz, device, suite):
+    with lz.SharedBuffer(device, lz.F32, 64 * 128) as xb, lz.SharedBuffer(device, lz.I8, 128 * 128) as W, \
+            lz.SharedBuffer(device, lz.F16, 128 * 4) as S, lz.SharedBuffer(device, lz.F32, 64 * 128) as ob:
+        st = lz.load_library().l0b_linear_tc_scaled(suite.handle, device.handle, 64, 128, 128, xb.handle, W.handle,
+                                                     S.handle, 32, None, 0.0, 0, None, ob.handle)
+    assert st != 0
+
+
 def test_tc_gemm_reports_no_timeouts(lz, device):
     import ctypes as C
 
