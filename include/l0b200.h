@@ -528,7 +528,7 @@ L0B_API l0b_status l0b_model_set_recording(l0b_model* model, int32_t enabled);
 L0B_API l0b_status l0b_model_set_fused(l0b_model* model, int32_t enabled);
 /* Projections over at least `min_rows` activation rows (prefill chunks) with f16/bf16 weights, or int8
  * weights with one scale per row, run on the tcgen05 GEMM (weights read once per chunk, activations as
- * hi + lo 16-bit halves); fewer rows, group-wise int8 and min_rows = 0 use the GEMV. Default 16. */
+ * hi + lo 16-bit halves); fewer rows, group-wise int8 and min_rows = 0 use the GEMV. Default 8. */
 L0B_API l0b_status l0b_model_set_gemm_rows(l0b_model* model, int32_t min_rows);
 /* LlmDecoderLayer.Probe (L/LlmDecoderLayer.cs:113-119): when set, steps run the reference op sequence
  * without command-list recording and call `fn` after each stage of each layer with a host copy of the

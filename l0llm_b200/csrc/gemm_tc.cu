@@ -2,17 +2,29 @@
 // tensor memory, both operands staged by TMA into 128-byte-swizzled shared memory.
 //
 // "Swap-AB" orientation: the 128-row MMA M dimension runs over weight rows and the MMA N dimension
-// (BN = 64, 128 or 256) over tokens, so one CTA computes D[128 weight rows, BN tokens] = W_tile X_tile^T
-// into BN fp32 TMEM columns. Warp 0 / lane 0 issues the TMA loads (W tile [128 x 64] and X tile
-// [BN x 64] per stage, 4 stages), warp 1 / lane 0 issues four K=16 MMAs per stage and releases the
-// stage with tcgen05.commit, and all four warps run the epilogue from TMEM (warp w owns TMEM lanes
-// 32w..32w+31 = weight rows), storing token-major fp32 rows with coalesced 128-byte writes. The SwiGLU
-// variant loads 64 gate rows and the 64 matching up rows into one tile and pairs them in the epilogue.
+// (BN = 32, 64, 128 or 256) over activation rows, so one CTA computes D[128 weight rows, BN] =
+// W_tile X_tile^T into BN fp32 TMEM columns. Warp 0 / lane 0 issues the TMA loads (W tile [128 x 64] and
+// X tile [BN x 64] per stage, a ring of 4-8 stages filling ~100 KB, two CTAs per SM, for BN <= 64, or
+// ~196 KB above), warp 1 / lane 0 issues four K=16 MMAs per stage and releases the stage with
+// tcgen05.commit, and all four warps run the epilogue from TMEM (warp w owns TMEM lanes 32w..32w+31 =
+// weight rows), storing token-major fp32 rows with coalesced 128-byte writes. The SwiGLU variant loads
+// 64 gate rows and the 64 matching up rows into one tile and pairs them in the epilogue.
+//
+// f32 activations enter as hi / lo pairs of 16-bit rows (the lo row the rounding residual of the hi),
+// so one tile's BN columns hold BN / 2 tokens twice and the epilogue adds the pair: about 22 bits (f16)
+// or 16 bits (bf16) of each activation for one pass over K.
+//
+// Few tiles (decode batches, narrow projections) would leave most SMs idle, so K is split S ways across
+// CTAs (blockIdx.z): each split writes its partial tile to global scratch, and the last split of a tile
+// to arrive (an atomic counter per tile, no waiting) sums the S partials in split order — deterministic
+// — runs the epilogue and re-arms the counter.
+//
+// int8 weights (one scale per weight row): TMA brings the raw [128 x 64] byte tile per stage, warps 2-3
+// turn it into one of two swizzled f16 A tiles (exact: |q| <= 128) and hand it to the MMA issuer through
+// an mbarrier; the epilogue multiplies by the row's scale.
+//
 // Every mbarrier wait is bounded (~2 s); a timeout sets the device error flag and the CTA exits after
 // releasing its tensor memory. No TMA multicast is used.
-// int8 weights (one scale per weight row): TMA brings the raw [128 x 64] byte tile, warps 2-3 turn it
-// into the swizzled f16 A tile (exact: |q| <= 128) and hand it to the MMA issuer through a third
-// mbarrier; the epilogue multiplies by the row's scale.
 #include <cuda.h>
 
 #include <cstring>
@@ -27,20 +39,21 @@ namespace {
 
 constexpr int kBM = 128;
 constexpr int kBK = 64;
-constexpr int kStages = 4;
 constexpr int kThreads = 128;
 constexpr long long kWaitCycles = 4000000000LL;
 
 struct TcParams {
     CUtensorMap wmap;  // W [N, K] 16-bit (int8: bytes, no swizzle), box {64, 128} (SwiGLU: {64, 64})
-    CUtensorMap xmap;  // X [M, K] 16-bit, box {64, BN}
+    CUtensorMap xmap;  // X 16-bit, row stride K, box {64, BN}: [M, K], or the paired hi / lo layout
     int M, N, K, epi, ld, half_n;
     float* out;
     const float* bias;
     int* error;
-    int split, kpad;       // split activations: 2 x nk stages, lo half at column kpad
-    const float* rscale;   // per-token result scale (split mode) or null
+    int pair;              // x rows come as hi / lo pairs: token columns BN / 2, summed in the epilogue
+    const float* rscale;   // per-token result scale or null
     const __half* wscale;  // int8: f16 scale per weight row
+    float* part;           // split-K partial tiles (gridDim.z > 1)
+    unsigned* counters;    // split-K tile counters, zero at rest
 };
 
 // Four signed bytes -> two f16x2 (bytes 0,1 and bytes 2,3), exact: u = b ^ 0x80 placed in the low
@@ -129,38 +142,64 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
     for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// Shared-memory plan of one instantiation: 16-bit weights take an A tile per stage; int8 weights take a
+// raw byte tile per stage plus two converted A tiles. Stages fill ~100 KB (two CTAs per SM) for BN <= 64
+// and ~196 KB (one CTA per SM) above, at most 8.
+template <int BN, int FMT>
+struct TcCfg {
+    static constexpr bool kQ8 = FMT == 2;
+    static constexpr int A_BYTES = kBM * kBK * 2;
+    static constexpr int B_BYTES = BN * kBK * 2;
+    static constexpr int Q_BYTES = kQ8 ? kBM * kBK : 0;
+    static constexpr int A_TILES_FIXED = kQ8 ? 2 : 0;
+    static constexpr int STAGE_BYTES = (kQ8 ? Q_BYTES : A_BYTES) + B_BYTES;
+    static constexpr int TARGET = BN <= 64 ? 100 * 1024 : 196 * 1024;
+    static constexpr int STAGES_FIT = (TARGET - A_TILES_FIXED * A_BYTES) / STAGE_BYTES;
+    static constexpr int STAGES = STAGES_FIT > 8 ? 8 : STAGES_FIT;
+    static constexpr int A_TILES = kQ8 ? 2 : STAGES;
+    static constexpr size_t SMEM = 1024 + static_cast<size_t>(A_TILES) * A_BYTES +
+                                   static_cast<size_t>(STAGES) * (B_BYTES + Q_BYTES) + 256;
+    static_assert(STAGES >= 3, "the int8 converter's release of A tiles needs three or more stages");
+};
+
 // FMT: 0 = f16, 1 = bf16 (weights and activations), 2 = int8 weights converted to f16 in shared memory.
 template <int BN, int FMT>
 __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const __grid_constant__ TcParams p) {
-    extern __shared__ uint8_t smem_raw[];
-    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    constexpr bool kQ8 = FMT == 2;
+    using Cfg = TcCfg<BN, FMT>;
+    constexpr bool kQ8 = Cfg::kQ8;
+    constexpr int ST = Cfg::STAGES;
+    constexpr int A_BYTES = Cfg::A_BYTES, B_BYTES = Cfg::B_BYTES, Q_BYTES = Cfg::Q_BYTES;
     constexpr uint32_t MMA_FMT = FMT == 1 ? 1 : 0;
-    constexpr int A_BYTES = kBM * kBK * 2;
-    constexpr int B_BYTES = BN * kBK * 2;
-    constexpr int Q_BYTES = kQ8 ? kBM * kBK : 0;
-    uint8_t* sA = smem;
-    uint8_t* sB = smem + kStages * A_BYTES;
-    uint8_t* sQ = sB + kStages * B_BYTES;  // int8: raw weight tiles [128][64] bytes
-    uint64_t* full = reinterpret_cast<uint64_t*>(sQ + kStages * Q_BYTES);
-    uint64_t* empty = full + kStages;
-    uint64_t* conv = empty + kStages;  // int8: the converted A tile of stage s is ready
-    uint64_t* accum = conv + kStages;
+    extern __shared__ uint8_t smem_raw[];
+    __shared__ int last_split;
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* sA = smem;                        // 16-bit: one A tile per stage; int8: two converted tiles
+    uint8_t* sB = sA + Cfg::A_TILES * A_BYTES;
+    uint8_t* sQ = sB + ST * B_BYTES;           // int8: raw weight tiles [128][64] bytes per stage
+    uint64_t* full = reinterpret_cast<uint64_t*>(sQ + ST * Q_BYTES);
+    uint64_t* empty = full + ST;
+    uint64_t* conv = empty + ST;               // int8: converted A tile a (= stage index & 1) is ready
+    uint64_t* accum = conv + 2;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int t0 = blockIdx.x * BN;
+    const int tb = p.pair ? BN / 2 : BN;       // tokens per tile
+    const int t0 = blockIdx.x * tb;
+    const int xrow0 = blockIdx.x * BN;         // first x16 row of this token tile
     const int wt = blockIdx.y;
+    const int z = blockIdx.z, S = gridDim.z;
     const bool swiglu = p.epi == EPI_SWIGLU;
     const int nk = (p.K + kBK - 1) / kBK;
-    const int nst = p.split ? 2 * nk : nk;  // split: stage 2k + part is weight tile k against half `part`
+    const int kb0 = z * nk / S;
+    const int nst = (z + 1) * nk / S - kb0;    // >= 1: the host keeps S <= nk
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < kStages; ++s) {
+        for (int s = 0; s < ST; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1);
-            mbar_init(&conv[s], 64);
         }
+        mbar_init(&conv[0], 64);
+        mbar_init(&conv[1], 64);
         mbar_init(accum, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -181,16 +220,15 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const __grid_const
     bool ok = true;
     if (warp == 0 && lane == 0) {
         // TMA producer.
-        for (int kb = 0; kb < nst; ++kb) {
-            const int s = kb % kStages;
-            const uint32_t ph = (kb / kStages) & 1;
-            if (kb >= kStages && !mbar_wait(&empty[s], ph ^ 1)) {
+        for (int i = 0; i < nst; ++i) {
+            const int s = i % ST;
+            const uint32_t ph = (i / ST) & 1;
+            if (i >= ST && !mbar_wait(&empty[s], ph ^ 1)) {
                 ok = false;
                 break;
             }
             mbar_expect_tx(&full[s], (kQ8 ? Q_BYTES : A_BYTES) + B_BYTES);
-            const int k0 = (p.split ? kb >> 1 : kb) * kBK;
-            const int kx = p.split ? (kb & 1) * p.kpad + k0 : k0;
+            const int k0 = (kb0 + i) * kBK;
             uint8_t* wdst = kQ8 ? sQ + s * Q_BYTES : sA + s * A_BYTES;
             if (swiglu) {
                 tma_load_2d(wdst, &p.wmap, &full[s], k0, wt * 64);
@@ -198,42 +236,43 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const __grid_const
             } else {
                 tma_load_2d(wdst, &p.wmap, &full[s], k0, wt * kBM);
             }
-            tma_load_2d(sB + s * B_BYTES, &p.xmap, &full[s], kx, t0);
+            tma_load_2d(sB + s * B_BYTES, &p.xmap, &full[s], k0, xrow0);
         }
     } else if (warp == 1 && lane == 0) {
         // MMA issuer: D[128, BN] (+)= A[128, 16] B[BN, 16]^T, four per stage.
         constexpr uint32_t idesc = (1u << 4) | (MMA_FMT << 7) | (MMA_FMT << 10) |
                                    (static_cast<uint32_t>(BN >> 3) << 17) | (static_cast<uint32_t>(kBM >> 4) << 24);
-        for (int kb = 0; kb < nst; ++kb) {
-            const int s = kb % kStages;
-            const uint32_t ph = (kb / kStages) & 1;
-            if (!mbar_wait(&full[s], ph) || (kQ8 && !mbar_wait(&conv[s], ph))) {
+        for (int i = 0; i < nst; ++i) {
+            const int s = i % ST;
+            const uint32_t ph = (i / ST) & 1;
+            if (!mbar_wait(&full[s], ph) || (kQ8 && !mbar_wait(&conv[i & 1], (i >> 1) & 1))) {
                 ok = false;
                 break;
             }
             tc_fence_after();
-            const uint64_t da = smem_desc(sA + s * A_BYTES), db = smem_desc(sB + s * B_BYTES);
+            const uint64_t da = smem_desc(kQ8 ? sA + (i & 1) * A_BYTES : sA + s * A_BYTES);
+            const uint64_t db = smem_desc(sB + s * B_BYTES);
 #pragma unroll
-            for (int k = 0; k < kBK / 16; ++k) tc_mma(tmem, da + 2 * k, db + 2 * k, idesc, (kb | k) != 0);
+            for (int k = 0; k < kBK / 16; ++k) tc_mma(tmem, da + 2 * k, db + 2 * k, idesc, (i | k) != 0);
             tc_commit(&empty[s]);
         }
         tc_commit(accum);
     } else if (kQ8 && warp >= 2) {
-        // Converters: 512 16-byte pieces of int8 per stage, 8 per thread; row r's f16 chunk c goes to
-        // 16-byte slot c ^ (r & 7) of its 128-byte row (the TMA / UMMA 128-byte swizzle).
+        // Converters: stage i's bytes go to A tile i & 1 once the MMAs of stage i - 2 (the tile's last
+        // reader) have completed. 512 16-byte pieces of int8 per stage, 8 per thread; row r's f16 chunk
+        // c goes to 16-byte slot c ^ (r & 7) of its 128-byte row (the TMA / UMMA 128-byte swizzle).
         const int ct = threadIdx.x - 64;
-        for (int kb = 0; kb < nst; ++kb) {
-            const int s = kb % kStages;
-            const uint32_t ph = (kb / kStages) & 1;
-            if (!mbar_wait(&full[s], ph)) {
+        for (int i = 0; i < nst; ++i) {
+            const int s = i % ST;
+            if (!mbar_wait(&full[s], (i / ST) & 1) || (i >= 2 && !mbar_wait(&empty[(i - 2) % ST], ((i - 2) / ST) & 1))) {
                 ok = false;
                 break;
             }
             const uint8_t* q = sQ + s * Q_BYTES;
-            uint8_t* a = sA + s * A_BYTES;
+            uint8_t* a = sA + (i & 1) * A_BYTES;
 #pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                const int c = ct + 64 * i;
+            for (int it = 0; it < 8; ++it) {
+                const int c = ct + 64 * it;
                 const int r = c >> 2, j = c & 3;
                 const uint4 w = *reinterpret_cast<const uint4*>(q + r * 64 + j * 16);
                 uint4 o0, o1;
@@ -246,57 +285,59 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const __grid_const
             }
             // Generic-proxy writes become visible to the tensor core's (async proxy) reads.
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            mbar_arrive(&conv[s]);
+            mbar_arrive(&conv[i & 1]);
         }
     }
     __syncwarp();
 
-    // Epilogue: all warps.
+    // Epilogue: all warps. Thread (warp, lane) owns TMEM lane rl = weight row `row` of the tile.
     const bool acc_ok = mbar_wait(accum, 0);
     __syncwarp();
     tc_fence_after();
+    const int rl = warp * 32 + lane;
+    const int row = swiglu ? (warp < 2 ? 0 : p.half_n - 64) + wt * 64 + rl : wt * kBM + rl;
+    const float wsc = (kQ8 && row < p.N) ? __half2float(p.wscale[row]) : 1.f;
+    const uint32_t tl = tmem + (static_cast<uint32_t>(warp * 32) << 16);
     float* xchg = reinterpret_cast<float*>(sA);  // SwiGLU: up rows handed from warps 2-3 to warps 0-1
-    for (int c0 = 0; c0 < BN; c0 += 16) {
-        float v[16];
-        tmem_ld16(tmem + (static_cast<uint32_t>(warp * 32) << 16) + c0, v);
-        if (kQ8) {
-            const int row = swiglu ? (warp < 2 ? 0 : p.half_n) + wt * 64 + (warp & 1) * 32 + lane
-                                   : wt * kBM + warp * 32 + lane;
-            const float ws = row < p.N ? __half2float(p.wscale[row]) : 0.f;
+    // Accumulator columns c0..c0+15 of this lane: the token's hi column plus (paired) its lo column.
+    auto load_acc = [&](int c0, float (&v)[16]) {
+        tmem_ld16(tl + c0, v);
+        if (p.pair) {
+            float u[16];
+            tmem_ld16(tl + BN / 2 + c0, u);
 #pragma unroll
-            for (int j = 0; j < 16; ++j) v[j] *= ws;
+            for (int j = 0; j < 16; ++j) v[j] += u[j];
+        }
+    };
+    // Scales, bias and the epilogue of tokens t0 + c0 .. t0 + c0 + 15 (uniform across the CTA).
+    auto finish = [&](int c0, float (&v)[16]) {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+            const int t = t0 + c0 + j;
+            v[j] *= wsc * ((p.rscale && t < p.M) ? p.rscale[t] : 1.f);
         }
         if (!swiglu) {
-            const int n = wt * kBM + warp * 32 + lane;
-            if (acc_ok && n < p.N) {
-                const float b = p.bias ? p.bias[n] : 0.f;
+            if (acc_ok && row < p.N) {
+                const float b = p.bias ? p.bias[row] : 0.f;
 #pragma unroll
                 for (int j = 0; j < 16; ++j) {
                     const int t = t0 + c0 + j;
                     if (t < p.M) {
-                        float* o = p.out + static_cast<long long>(t) * p.ld + n;
-                        const float y = p.rscale ? v[j] * p.rscale[t] : v[j];
-                        if (p.epi == EPI_ACCUM) *o += y + b;
-                        else *o = y + b;
+                        float* o = p.out + static_cast<long long>(t) * p.ld + row;
+                        if (p.epi == EPI_ACCUM) *o += v[j] + b;
+                        else *o = v[j] + b;
                     }
                 }
             }
         } else {
             __syncthreads();
-            if (p.rscale) {
-#pragma unroll
-                for (int j = 0; j < 16; ++j) {
-                    const int t = t0 + c0 + j;
-                    v[j] *= t < p.M ? p.rscale[t] : 1.f;
-                }
-            }
             if (warp >= 2) {
 #pragma unroll
                 for (int j = 0; j < 16; ++j) xchg[((warp - 2) * 32 + lane) * 17 + j] = v[j];
             }
             __syncthreads();
             if (warp < 2) {
-                const int i = wt * 64 + warp * 32 + lane;
+                const int i = wt * 64 + rl;
                 if (acc_ok && i < p.half_n) {
 #pragma unroll
                     for (int j = 0; j < 16; ++j) {
@@ -305,6 +346,45 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const __grid_const
                             p.out[static_cast<long long>(t) * p.ld + i] = silu(v[j]) * xchg[(warp * 32 + lane) * 17 + j];
                     }
                 }
+            }
+        }
+    };
+    if (S == 1) {
+        for (int c0 = 0; c0 < tb; c0 += 16) {
+            float v[16];
+            load_acc(c0, v);
+            finish(c0, v);
+        }
+    } else {
+        // Split-K: partial tile [tb columns][128 rows] of split z; the last split to arrive sums the
+        // splits in order 0..S-1 (deterministic) and finishes; it also re-arms the tile's counter.
+        const int tile = blockIdx.y * gridDim.x + blockIdx.x;
+        float* base = p.part + static_cast<size_t>(tile) * S * tb * kBM;
+        for (int c0 = 0; c0 < tb; c0 += 16) {
+            float v[16];
+            load_acc(c0, v);
+#pragma unroll
+            for (int j = 0; j < 16; ++j) base[(static_cast<size_t>(z) * tb + c0 + j) * kBM + rl] = v[j];
+        }
+        __threadfence();
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            const unsigned prev = atomicAdd(&p.counters[tile], 1u);
+            last_split = prev == static_cast<unsigned>(S - 1);
+            if (last_split) p.counters[tile] = 0;
+        }
+        __syncthreads();
+        if (last_split) {
+            __threadfence();
+            for (int c0 = 0; c0 < tb; c0 += 16) {
+                float v[16];
+#pragma unroll
+                for (int j = 0; j < 16; ++j) v[j] = 0.f;
+                for (int zz = 0; zz < S; ++zz) {
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) v[j] += __ldcg(&base[(static_cast<size_t>(zz) * tb + c0 + j) * kBM + rl]);
+                }
+                finish(c0, v);
             }
         }
     }
@@ -337,10 +417,11 @@ __global__ void __launch_bounds__(256) cast_rows_kernel(const float* x, long lon
     }
 }
 
-// One block per row: RMS norm (optional) and the row maximum, then the [hi | lo] split.
+// One block per token: RMS norm (optional) and the row maximum, then the hi / lo pair, written to rows
+// (t / tb) * bn + t % tb (hi) and that + tb (lo) of the paired layout, row stride K.
 __global__ void __launch_bounds__(256) cast_rows_split_kernel(const float* x, long long ld_x, const float* norm_w,
                                                               float eps, void* out16, float* rscale, int dtype, int K,
-                                                              int kpad) {
+                                                              int bn, int tb) {
     __shared__ float red[32];
     __shared__ float mx[32];
     pdl_wait();
@@ -370,20 +451,14 @@ __global__ void __launch_bounds__(256) cast_rows_split_kernel(const float* x, lo
     }
     const float sc = rstd * ldexpf(1.0f, e);
     if (threadIdx.x == 0) rscale[blockIdx.x] = ldexpf(1.0f, -e);
-    const long long base = static_cast<long long>(blockIdx.x) * 2 * kpad;
-    for (int k = threadIdx.x; k < kpad; k += blockDim.x) {
-        float hi = 0.f, lo = 0.f;
-        if (k < K) {
-            const float v = (norm_w ? xr[k] * norm_w[k] : xr[k]) * sc;
-            if (dtype == L0B_F16) {
-                hi = __half2float(__float2half_rn(v));
-            } else {
-                hi = __bfloat162float(__float2bfloat16_rn(v));
-            }
-            lo = v - hi;
-        }
-        store_from_float(out16, dtype, base + k, hi);
-        store_from_float(out16, dtype, base + kpad + k, lo);
+    const int t = blockIdx.x;
+    const long long hi_row = static_cast<long long>(t / tb) * bn + t % tb;
+    const long long hbase = hi_row * K, lbase = (hi_row + tb) * K;
+    for (int k = threadIdx.x; k < K; k += blockDim.x) {
+        const float v = (norm_w ? xr[k] * norm_w[k] : xr[k]) * sc;
+        const float hi = dtype == L0B_F16 ? __half2float(__float2half_rn(v)) : __bfloat162float(__float2bfloat16_rn(v));
+        store_from_float(out16, dtype, hbase + k, hi);
+        store_from_float(out16, dtype, lbase + k, v - hi);
     }
 }
 
@@ -428,25 +503,25 @@ l0b_status make_map(CUtensorMap* map, const void* base, int dtype, long long row
 }
 
 template <int BN, int FMT>
-l0b_status launch_bn(l0b_device* d, const TcParams& p, int grid_y) {
+l0b_status launch_bn(l0b_device* d, const TcParams& p, const TcPlan& plan) {
     auto kernel = tc_gemm_kernel<BN, FMT>;
-    constexpr size_t smem = 1024 + kStages * (kBM * kBK * 2 + BN * kBK * 2 + (FMT == 2 ? kBM * kBK : 0)) + 256;
+    constexpr size_t smem = TcCfg<BN, FMT>::SMEM;
     static bool configured = false;
     if (!configured) {
         cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
         if (e != cudaSuccess) return fail(L0B_ERR_CUDA, "cudaFuncSetAttribute failed: %s", cudaGetErrorString(e));
         configured = true;
     }
-    dim3 grid((p.M + BN - 1) / BN, grid_y);
-    return d->launch(kernel, grid, dim3(kThreads), smem, p);
+    return d->launch(kernel, dim3(plan.tiles_x, plan.tiles_y, plan.S), dim3(kThreads), smem, p);
 }
 
 template <int FMT>
-l0b_status launch_fmt(l0b_device* d, const TcParams& p, int bn, int grid_y) {
-    switch (bn) {
-        case 64: return launch_bn<64, FMT>(d, p, grid_y);
-        case 128: return launch_bn<128, FMT>(d, p, grid_y);
-        default: return launch_bn<256, FMT>(d, p, grid_y);
+l0b_status launch_fmt(l0b_device* d, const TcParams& p, const TcPlan& plan) {
+    switch (plan.bn) {
+        case 32: return launch_bn<32, FMT>(d, p, plan);
+        case 64: return launch_bn<64, FMT>(d, p, plan);
+        case 128: return launch_bn<128, FMT>(d, p, plan);
+        default: return launch_bn<256, FMT>(d, p, plan);
     }
 }
 
@@ -459,22 +534,57 @@ bool tc_gemm_supported(int wdtype, int M, int N, int K, int epi) {
     return epi == EPI_STORE || epi == EPI_ACCUM || epi == EPI_SWIGLU;
 }
 
+size_t tc_gemm_part_floats(int sm_count) { return static_cast<size_t>(2) * sm_count * 128 * kBM; }
+
+// Token columns: the smallest BN in {32, 64, 128, 256} that holds the tile's columns (hi and lo when
+// paired). Weight tiles: 128 rows (SwiGLU: 64 gate + 64 up). K splits: when the tiles fill fewer than the
+// resident slots (two CTAs per SM at BN <= 64), split K so tiles x S comes close to the slots, each
+// split keeping two or more K blocks of 64 and the partial tiles within the scratch bound.
+TcPlan tc_gemm_plan(int M, int N, int K, int epi, bool pair, int sm_count) {
+    TcPlan pl;
+    const int cols = pair ? 2 * M : M;
+    pl.bn = cols <= 32 ? 32 : cols <= 64 ? 64 : cols <= 128 ? 128 : 256;
+    pl.tb = pair ? pl.bn / 2 : pl.bn;
+    pl.tiles_x = (M + pl.tb - 1) / pl.tb;
+    pl.tiles_y = epi == EPI_SWIGLU ? (N / 2) / 64 : (N + kBM - 1) / kBM;
+    const long long tiles = static_cast<long long>(pl.tiles_x) * pl.tiles_y;
+    const int slots = sm_count * (pl.bn <= 64 ? 2 : 1);
+    const int nk = (K + kBK - 1) / kBK;
+    int S = tiles >= slots ? 1 : static_cast<int>(slots / tiles);
+    if (S > nk / 2) S = nk / 2;
+    if (S > 16) S = 16;
+    if (S < 1) S = 1;
+    while (S > 1 && (tiles * S * pl.tb * kBM > static_cast<long long>(tc_gemm_part_floats(sm_count)) ||
+                     tiles > kTcCounters))
+        --S;
+    pl.S = S;
+    pl.part_floats = S > 1 ? static_cast<size_t>(tiles) * S * pl.tb * kBM : 0;
+    pl.counters = S > 1 ? static_cast<int>(tiles) : 0;
+    return pl;
+}
+
 l0b_status tc_gemm_launch(l0b_device* d, const TcGemmArgs& a) {
     L0B_REQUIRE(tc_gemm_supported(a.wdtype, a.M, a.N, a.K, a.epi), L0B_ERR_UNSUPPORTED,
                 "tensor-core GEMM does not take M=%d N=%d K=%d epi=%d dtype=%d", a.M, a.N, a.K, a.epi, a.wdtype);
-    const int bn = a.M <= 64 ? 64 : a.M <= 128 ? 128 : 256;
+    TcPlan plan = tc_gemm_plan(a.M, a.N, a.K, a.epi, a.split != 0, d->sm_count);
+    if (plan.S > 1 && (!a.part || !a.counters || a.part_floats < plan.part_floats || a.counter_count < plan.counters)) {
+        plan.S = 1;  // no scratch for the split: one CTA per tile
+        plan.part_floats = 0;
+        plan.counters = 0;
+    }
     TcParams p;
     std::memset(&p, 0, sizeof(p));
     const bool swiglu = a.epi == EPI_SWIGLU;
     const bool q8 = a.wdtype == L0B_I8;
     L0B_REQUIRE(!q8 || a.wscale, L0B_ERR_ARGUMENT, "int8 weights need their row scales");
     L0B_TRY(make_map(&p.wmap, a.w, a.wdtype, a.N, a.K, swiglu ? 64 : kBM));
-    const int kpad = (a.K + kBK - 1) / kBK * kBK;
-    L0B_TRY(make_map(&p.xmap, a.x16, q8 ? L0B_F16 : a.wdtype, a.M, a.split ? 2 * kpad : a.K, bn));
+    const long long xrows = a.split ? tc_pair_rows(plan) : a.M;
+    L0B_TRY(make_map(&p.xmap, a.x16, q8 ? L0B_F16 : a.wdtype, xrows, a.K, plan.bn));
     p.wscale = static_cast<const __half*>(a.wscale);
-    p.split = a.split;
-    p.kpad = kpad;
+    p.pair = a.split ? 1 : 0;
     p.rscale = a.rscale;
+    p.part = plan.S > 1 ? a.part : nullptr;
+    p.counters = plan.S > 1 ? a.counters : nullptr;
     p.M = a.M;
     p.N = a.N;
     p.K = a.K;
@@ -484,10 +594,9 @@ l0b_status tc_gemm_launch(l0b_device* d, const TcGemmArgs& a) {
     p.out = a.out;
     p.bias = a.bias;
     p.error = d->error_flag;
-    const int grid_y = swiglu ? (a.N / 2) / 64 : (a.N + kBM - 1) / kBM;
-    if (q8) return launch_fmt<2>(d, p, bn, grid_y);
-    if (a.wdtype == L0B_BF16) return launch_fmt<1>(d, p, bn, grid_y);
-    return launch_fmt<0>(d, p, bn, grid_y);
+    if (q8) return launch_fmt<2>(d, p, plan);
+    if (a.wdtype == L0B_BF16) return launch_fmt<1>(d, p, plan);
+    return launch_fmt<0>(d, p, plan);
 }
 
 l0b_status cast_rows_launch(l0b_device* d, const float* x, long long ld_x, const float* norm_w, float eps, void* out16,
@@ -496,10 +605,9 @@ l0b_status cast_rows_launch(l0b_device* d, const float* x, long long ld_x, const
 }
 
 l0b_status cast_rows_split_launch(l0b_device* d, const float* x, long long ld_x, const float* norm_w, float eps,
-                                  void* out16, float* rscale, int dtype, int M, int K) {
-    const int kpad = (K + kBK - 1) / kBK * kBK;
+                                  void* out16, float* rscale, int dtype, int M, int K, const TcPlan& plan) {
     return d->launch(cast_rows_split_kernel, dim3(M), dim3(256), 0, x, ld_x, norm_w, eps, out16, rscale, dtype, K,
-                     kpad);
+                     plan.bn, plan.tb);
 }
 
 }  // namespace l0b

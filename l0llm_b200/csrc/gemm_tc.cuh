@@ -5,22 +5,45 @@
 
 namespace l0b {
 
+// Tile plan of one GEMM: BN accumulator columns per CTA, of which TB are tokens (TB = BN / 2 when the
+// activations come as hi / lo pairs); tiles_x token tiles x tiles_y weight tiles, each split S ways
+// along K. With S > 1 every split writes its partial tile to `part` and the last split of a tile to
+// finish (an atomic counter per tile) sums them in split order and runs the epilogue.
+struct TcPlan {
+    int bn = 64, tb = 64, tiles_x = 1, tiles_y = 1, S = 1;
+    size_t part_floats = 0;  // scratch the split needs (tiles * S * TB * 128)
+    int counters = 0;        // tile counters the split needs
+};
+
 struct TcGemmArgs {
     int M, N, K;           // tokens, weight rows, inner dimension
-    const void* x16;       // [M, K] activations in the weight's 16-bit format (row stride K)
+    const void* x16;       // activations in the GEMM's 16-bit format (layout below)
     const void* w;         // [N, K] weights, f16, bf16 or int8
     int wdtype;            // L0B_F16, L0B_BF16 or L0B_I8 (activations then f16)
     int epi;               // GemvEpi: STORE, ACCUM or SWIGLU (W = [gate; up], N = 2 * I)
     float* out;            // f32 output, row stride ld (SWIGLU: [M, N/2])
     int ld;
     const float* bias;     // STORE / ACCUM: f32 [N] or null
-    // Split activations (cast_rows_split_launch): x16 is [M, 2 Kp], hi in columns [0, K) and the f16
-    // residual lo in [Kp, Kp + K), Kp = 64 * ceil(K / 64); every weight tile meets both halves in the
-    // same accumulator, and row t of the result is multiplied by rscale[t].
+    // Paired activations (cast_rows_split_launch): token t of token tile j = t / TB has its hi half in
+    // x16 row j * BN + t % TB and its lo residual in row j * BN + TB + t % TB (row stride K); the two
+    // accumulator columns are summed, and the result of token t is multiplied by rscale[t].
+    // Unpaired: x16 is [M, K], one rounded row per token.
     int split = 0;
     const float* rscale = nullptr;
     const void* wscale = nullptr;  // int8: f16 [N], one scale per weight row
+    // Split-K scratch (may be null: no split): f32 partial tiles and zeroed tile counters, which the
+    // GEMM leaves zeroed again.
+    float* part = nullptr;
+    size_t part_floats = 0;
+    unsigned* counters = nullptr;
+    int counter_count = 0;
 };
+
+// The tile plan tc_gemm_launch uses for this shape on `sm_count` SMs (pair = split activations).
+TcPlan tc_gemm_plan(int M, int N, int K, int epi, bool pair, int sm_count);
+
+// Rows of the paired x16 matrix for M tokens under `plan` (tiles_x * BN).
+inline long long tc_pair_rows(const TcPlan& plan) { return static_cast<long long>(plan.tiles_x) * plan.bn; }
 
 // Launches the GEMM on the device's stream (recorded when the device records).
 l0b_status tc_gemm_launch(l0b_device* d, const TcGemmArgs& a);
@@ -29,14 +52,18 @@ l0b_status tc_gemm_launch(l0b_device* d, const TcGemmArgs& a);
 l0b_status cast_rows_launch(l0b_device* d, const float* x, long long ld_x, const float* norm_w, float eps, void* out16,
                             int dtype, int M, int K);
 
-// out16 = the rows of x (RMS-normalised with norm_w when given) split as [hi | lo] in f16/bf16 with
-// row stride 2 Kp (Kp = 64 * ceil(K / 64), padding zeroed); for f16 each row is first scaled by a power
-// of two putting its largest value near 2^14, and rscale[m] receives the inverse.
+// out16 = the rows of x (RMS-normalised with norm_w when given) as hi / lo pairs in f16/bf16 in the
+// paired layout of `plan` (row stride K); for f16 each token is first scaled by a power of two putting
+// its largest value near 2^14, and rscale[m] receives the inverse (bf16: 1).
 l0b_status cast_rows_split_launch(l0b_device* d, const float* x, long long ld_x, const float* norm_w, float eps,
-                                  void* out16, float* rscale, int dtype, int M, int K);
+                                  void* out16, float* rscale, int dtype, int M, int K, const TcPlan& plan);
 
 // True when the tensor-core path takes this shape: f16/bf16 weights with K % 8 == 0 or int8 weights
 // (per-row scales) with K % 16 == 0, K >= 64; SwiGLU needs (N / 2) % 64 == 0.
 bool tc_gemm_supported(int wdtype, int M, int N, int K, int epi);
+
+// Split-K scratch that covers every plan on `sm_count` SMs: floats and counters.
+size_t tc_gemm_part_floats(int sm_count);
+constexpr int kTcCounters = 4096;
 
 }  // namespace l0b

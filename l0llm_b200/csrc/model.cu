@@ -57,8 +57,10 @@ struct l0b_model {
     // scale per row; 0 = off): the rows are split into [hi | lo] 16-bit halves in x16 with a per-row
     // scale in rscale.
     int tc_rows = 0;
-    void* x16 = nullptr;      // [cap, 2 * pad64(max K)] 16-bit
+    void* x16 = nullptr;      // paired hi / lo rows, [2 * cap + 256, max K] 16-bit
     float* rscale = nullptr;  // [cap]
+    float* tc_part = nullptr; // split-K partial tiles (tc_gemm_part_floats)
+    unsigned* tc_counters = nullptr;  // [kTcCounters], zero at rest
     // Device-side step state: io = [tok(batch_cap) | pos(batch_cap)] written in one copy.
     int* io = nullptr;
     int* tok = nullptr;
@@ -332,9 +334,14 @@ bool tc_takes(const l0b_model* m, const ModelMatrix& w, const GemvParams& p) {
 
 l0b_status gemv(l0b_model* m, const ModelMatrix& w, const GemvParams& p) {
     if (!tc_takes(m, w, p)) return gemv_nk_launch(m->dev, w.dtype, p);
+    const TcPlan plan = tc_gemm_plan(p.M, w.n, w.k, p.epi, true, m->dev->sm_count);
     L0B_TRY(cast_rows_split_launch(m->dev, static_cast<const float*>(p.x), p.x_ld, p.norm_w, p.eps, m->x16,
-                                   m->rscale, w.dtype == L0B_I8 ? L0B_F16 : w.dtype, p.M, w.k));
+                                   m->rscale, w.dtype == L0B_I8 ? L0B_F16 : w.dtype, p.M, w.k, plan));
     TcGemmArgs a;
+    a.part = m->tc_part;
+    a.part_floats = tc_gemm_part_floats(m->dev->sm_count);
+    a.counters = m->tc_counters;
+    a.counter_count = kTcCounters;
     a.M = p.M;
     a.N = w.n;
     a.K = w.k;
@@ -994,12 +1001,13 @@ L0B_API l0b_status l0b_model_create(l0b_device* dev, l0b_suite* suite, const l0b
     if (m->wdtype == L0B_F16 || m->wdtype == L0B_BF16 || m->wdtype == L0B_I8) {
         int kmax = m->h > m->inter ? m->h : m->inter;
         if (m->qdim > kmax) kmax = m->qdim;
-        const size_t kpad = (static_cast<size_t>(kmax) + 63) / 64 * 64;
         uint16_t* x16 = nullptr;
-        L0B_TRY(m->alloc(&x16, cap * 2 * kpad));
+        L0B_TRY(m->alloc(&x16, (2 * cap + 256) * static_cast<size_t>(kmax)));
         m->x16 = x16;
         L0B_TRY(m->alloc(&m->rscale, cap));
-        m->tc_rows = 16;
+        L0B_TRY(m->alloc(&m->tc_part, tc_gemm_part_floats(m->dev->sm_count)));
+        L0B_TRY(m->alloc(&m->tc_counters, kTcCounters));
+        m->tc_rows = 8;
     }
     L0B_TRY(m->alloc(&m->logits, static_cast<size_t>(m->batch_cap) * m->vocab));
     L0B_TRY(m->alloc(&m->io, 2 * static_cast<size_t>(m->batch_cap)));

@@ -735,7 +735,8 @@ class LlmModel:
         check(load_library().l0b_model_set_fused(self.handle, 1 if on else 0))
 
     def set_gemm_rows(self, min_rows: int):
-        """Projections over >= min_rows rows with 16-bit weights use the tcgen05 GEMM (0 = GEMV only)."""
+        """Projections over >= min_rows rows (16-bit or per-row-scaled int8 weights) use the tcgen05 GEMM
+        (0 = GEMV only; default 8)."""
         check(load_library().l0b_model_set_gemm_rows(self.handle, int(min_rows)))
 
     @property
