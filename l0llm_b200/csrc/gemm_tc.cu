@@ -54,6 +54,8 @@ struct TcParams {
     const __half* wscale;  // int8: f16 scale per weight row
     float* part;           // split-K partial tiles (gridDim.z > 1)
     unsigned* counters;    // split-K tile counters, zero at rest
+    unsigned long long* argmax;  // EPI_ARGMAX: per-token keys (atomicMax), index = row + argmax_base
+    int argmax_base;
 };
 
 // Four signed bytes -> two f16x2 (bytes 0,1 and bytes 2,3), exact: u = b ^ 0x80 placed in the low
@@ -172,6 +174,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const __grid_const
     constexpr uint32_t MMA_FMT = FMT == 1 ? 1 : 0;
     extern __shared__ uint8_t smem_raw[];
     __shared__ int last_split;
+    __shared__ unsigned long long amax_keys[4][16];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* sA = smem;                        // 16-bit: one A tile per stage; int8: two converted tiles
     uint8_t* sB = sA + Cfg::A_TILES * A_BYTES;
@@ -316,7 +319,35 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const __grid_const
             const int t = t0 + c0 + j;
             v[j] *= wsc * ((p.rscale && t < p.M) ? p.rscale[t] : 1.f);
         }
-        if (!swiglu) {
+        if (p.epi == EPI_ARGMAX) {
+            // Logits (when stored) and one atomicMax per token per CTA: the largest of the tile's rows.
+            const bool live = acc_ok && row < p.N;
+            const float b = (live && p.bias) ? p.bias[row] : 0.f;
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+                const int t = t0 + c0 + j;
+                unsigned long long key = 0;
+                if (live && t < p.M) {
+                    if (p.out) p.out[static_cast<long long>(t) * p.ld + row] = v[j] + b;
+                    key = argmax_key(v[j] + b, row + p.argmax_base);
+                }
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) {
+                    const unsigned long long other = __shfl_xor_sync(0xffffffffu, key, o);
+                    key = other > key ? other : key;
+                }
+                if (lane == 0) amax_keys[warp][j] = key;
+            }
+            __syncthreads();
+            if (threadIdx.x < 16) {
+                unsigned long long key = amax_keys[0][threadIdx.x];
+#pragma unroll
+                for (int w = 1; w < 4; ++w) key = amax_keys[w][threadIdx.x] > key ? amax_keys[w][threadIdx.x] : key;
+                if (key && t0 + c0 + static_cast<int>(threadIdx.x) < p.M)
+                    atomicMax(p.argmax + t0 + c0 + threadIdx.x, key);
+            }
+            __syncthreads();
+        } else if (!swiglu) {
             if (acc_ok && row < p.N) {
                 const float b = p.bias ? p.bias[row] : 0.f;
 #pragma unroll
@@ -462,6 +493,88 @@ __global__ void __launch_bounds__(256) cast_rows_split_kernel(const float* x, lo
     }
 }
 
+// Register-resident variant of cast_rows_split_kernel for K % 4 == 0 and K <= 4 * VPT * blockDim.x:
+// every thread loads its VPT float4 of the row at once (one read of x, all loads in flight), and the
+// hi / lo halves are written from registers, four 16-bit values per store.
+template <int VPT>
+__global__ void __launch_bounds__(512) cast_rows_split_reg_kernel(const float* x, long long ld_x, const float* norm_w,
+                                                                  float eps, void* out16, float* rscale, int dtype,
+                                                                  int K, int bn, int tb) {
+    __shared__ float red[32];
+    __shared__ float mx[32];
+    pdl_wait();
+    const int t = blockIdx.x;
+    const int K4 = K >> 2;
+    const float4* xr = reinterpret_cast<const float4*>(x + t * ld_x);
+    const float4* nw = reinterpret_cast<const float4*>(norm_w);
+    float4 v[VPT];
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+        const int k4 = threadIdx.x + i * blockDim.x;
+        v[i] = k4 < K4 ? xr[k4] : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    float ss = 0.f, am = 0.f;
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+        const int k4 = threadIdx.x + i * blockDim.x;
+        ss += v[i].x * v[i].x + v[i].y * v[i].y + v[i].z * v[i].z + v[i].w * v[i].w;
+        if (norm_w && k4 < K4) {
+            const float4 w = nw[k4];
+            v[i].x *= w.x;
+            v[i].y *= w.y;
+            v[i].z *= w.z;
+            v[i].w *= w.w;
+        }
+        am = fmaxf(am, fmaxf(fmaxf(fabsf(v[i].x), fabsf(v[i].y)), fmaxf(fabsf(v[i].z), fabsf(v[i].w))));
+    }
+    const float rstd = norm_w ? 1.0f / sqrtf(block_sum(ss, red) / static_cast<float>(K) + eps) : 1.0f;
+    am = warp_max(am);
+    if ((threadIdx.x & 31) == 0) mx[threadIdx.x >> 5] = am;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        float m = threadIdx.x < (blockDim.x >> 5) ? mx[threadIdx.x] : 0.f;
+        m = warp_max(m);
+        if (threadIdx.x == 0) mx[0] = m;
+    }
+    __syncthreads();
+    const float top = mx[0] * rstd;
+    int e = 0;
+    if (dtype == L0B_F16 && top > 0.f && isfinite(top)) {
+        int ex;
+        frexpf(top, &ex);
+        e = min(max(14 - ex, -100), 100);
+    }
+    const float sc = rstd * ldexpf(1.0f, e);
+    if (threadIdx.x == 0) rscale[t] = ldexpf(1.0f, -e);
+    const long long hi_row = static_cast<long long>(t / tb) * bn + t % tb;
+    uint2* hrow = reinterpret_cast<uint2*>(static_cast<uint16_t*>(out16) + hi_row * K);
+    uint2* lrow = reinterpret_cast<uint2*>(static_cast<uint16_t*>(out16) + (hi_row + tb) * K);
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+        const int k4 = threadIdx.x + i * blockDim.x;
+        if (k4 < K4) {
+            const float a0 = v[i].x * sc, a1 = v[i].y * sc, a2 = v[i].z * sc, a3 = v[i].w * sc;
+            uint2 h, l;
+            if (dtype == L0B_F16) {
+                const __half2 h01 = __floats2half2_rn(a0, a1), h23 = __floats2half2_rn(a2, a3);
+                const float2 f01 = __half22float2(h01), f23 = __half22float2(h23);
+                const __half2 l01 = __floats2half2_rn(a0 - f01.x, a1 - f01.y), l23 = __floats2half2_rn(a2 - f23.x, a3 - f23.y);
+                h = make_uint2(*reinterpret_cast<const uint32_t*>(&h01), *reinterpret_cast<const uint32_t*>(&h23));
+                l = make_uint2(*reinterpret_cast<const uint32_t*>(&l01), *reinterpret_cast<const uint32_t*>(&l23));
+            } else {
+                const __nv_bfloat162 h01 = __floats2bfloat162_rn(a0, a1), h23 = __floats2bfloat162_rn(a2, a3);
+                const float2 f01 = __bfloat1622float2(h01), f23 = __bfloat1622float2(h23);
+                const __nv_bfloat162 l01 = __floats2bfloat162_rn(a0 - f01.x, a1 - f01.y),
+                                     l23 = __floats2bfloat162_rn(a2 - f23.x, a3 - f23.y);
+                h = make_uint2(*reinterpret_cast<const uint32_t*>(&h01), *reinterpret_cast<const uint32_t*>(&h23));
+                l = make_uint2(*reinterpret_cast<const uint32_t*>(&l01), *reinterpret_cast<const uint32_t*>(&l23));
+            }
+            hrow[k4] = h;
+            lrow[k4] = l;
+        }
+    }
+}
+
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
@@ -531,7 +644,7 @@ bool tc_gemm_supported(int wdtype, int M, int N, int K, int epi) {
     if (wdtype != L0B_F16 && wdtype != L0B_BF16 && wdtype != L0B_I8) return false;
     if (M < 1 || N < 1 || K < 64 || K % (wdtype == L0B_I8 ? 16 : 8) != 0) return false;
     if (epi == EPI_SWIGLU && (N % 2 != 0 || (N / 2) % 64 != 0)) return false;
-    return epi == EPI_STORE || epi == EPI_ACCUM || epi == EPI_SWIGLU;
+    return epi == EPI_STORE || epi == EPI_ACCUM || epi == EPI_SWIGLU || epi == EPI_ARGMAX;
 }
 
 size_t tc_gemm_part_floats(int sm_count) { return static_cast<size_t>(2) * sm_count * 128 * kBM; }
@@ -583,6 +696,9 @@ l0b_status tc_gemm_launch(l0b_device* d, const TcGemmArgs& a) {
     p.wscale = static_cast<const __half*>(a.wscale);
     p.pair = a.split ? 1 : 0;
     p.rscale = a.rscale;
+    L0B_REQUIRE(a.epi != EPI_ARGMAX || a.argmax, L0B_ERR_ARGUMENT, "the argmax epilogue needs its key array");
+    p.argmax = a.argmax;
+    p.argmax_base = a.argmax_base;
     p.part = plan.S > 1 ? a.part : nullptr;
     p.counters = plan.S > 1 ? a.counters : nullptr;
     p.M = a.M;
@@ -606,6 +722,15 @@ l0b_status cast_rows_launch(l0b_device* d, const float* x, long long ld_x, const
 
 l0b_status cast_rows_split_launch(l0b_device* d, const float* x, long long ld_x, const float* norm_w, float eps,
                                   void* out16, float* rscale, int dtype, int M, int K, const TcPlan& plan) {
+    const bool vec = K % 4 == 0 && ld_x % 4 == 0 && reinterpret_cast<uintptr_t>(x) % 16 == 0 &&
+                     (!norm_w || reinterpret_cast<uintptr_t>(norm_w) % 16 == 0) &&
+                     reinterpret_cast<uintptr_t>(out16) % 8 == 0;
+    if (vec && K <= 4 * 4 * 256)
+        return d->launch(cast_rows_split_reg_kernel<4>, dim3(M), dim3(256), 0, x, ld_x, norm_w, eps, out16, rscale,
+                         dtype, K, plan.bn, plan.tb);
+    if (vec && K <= 4 * 10 * 512)
+        return d->launch(cast_rows_split_reg_kernel<10>, dim3(M), dim3(512), 0, x, ld_x, norm_w, eps, out16, rscale,
+                         dtype, K, plan.bn, plan.tb);
     return d->launch(cast_rows_split_kernel, dim3(M), dim3(256), 0, x, ld_x, norm_w, eps, out16, rscale, dtype, K,
                      plan.bn, plan.tb);
 }

@@ -20,7 +20,7 @@ struct TcGemmArgs {
     const void* x16;       // activations in the GEMM's 16-bit format (layout below)
     const void* w;         // [N, K] weights, f16, bf16 or int8
     int wdtype;            // L0B_F16, L0B_BF16 or L0B_I8 (activations then f16)
-    int epi;               // GemvEpi: STORE, ACCUM or SWIGLU (W = [gate; up], N = 2 * I)
+    int epi;               // GemvEpi: STORE, ACCUM, SWIGLU (W = [gate; up], N = 2 * I) or ARGMAX
     float* out;            // f32 output, row stride ld (SWIGLU: [M, N/2])
     int ld;
     const float* bias;     // STORE / ACCUM: f32 [N] or null
@@ -31,6 +31,10 @@ struct TcGemmArgs {
     int split = 0;
     const float* rscale = nullptr;
     const void* wscale = nullptr;  // int8: f16 [N], one scale per weight row
+    // EPI_ARGMAX: logits to out (when not null) and, per token t, atomicMax of
+    // argmax_key(value, row + argmax_base) into argmax[t].
+    unsigned long long* argmax = nullptr;
+    int argmax_base = 0;
     // Split-K scratch (may be null: no split): f32 partial tiles and zeroed tile counters, which the
     // GEMM leaves zeroed again.
     float* part = nullptr;
@@ -59,7 +63,8 @@ l0b_status cast_rows_split_launch(l0b_device* d, const float* x, long long ld_x,
                                   void* out16, float* rscale, int dtype, int M, int K, const TcPlan& plan);
 
 // True when the tensor-core path takes this shape: f16/bf16 weights with K % 8 == 0 or int8 weights
-// (per-row scales) with K % 16 == 0, K >= 64; SwiGLU needs (N / 2) % 64 == 0.
+// (per-row scales) with K % 16 == 0, K >= 64; SwiGLU needs (N / 2) % 64 == 0. Epilogues: store,
+// residual add, SwiGLU, argmax.
 bool tc_gemm_supported(int wdtype, int M, int N, int K, int epi);
 
 // Split-K scratch that covers every plan on `sm_count` SMs: floats and counters.

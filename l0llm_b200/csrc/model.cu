@@ -326,7 +326,7 @@ bool tc_takes(const l0b_model* m, const ModelMatrix& w, const GemvParams& p) {
     if (!m->x16 || m->tc_rows <= 0 || p.M < m->tc_rows) return false;
     if (w.dtype != L0B_F16 && w.dtype != L0B_BF16 && !(w.dtype == L0B_I8 && w.group >= w.k)) return false;
     if (p.nseg != 1 || p.x_dtype != L0B_F32 || p.out_dtype != L0B_F32) return false;
-    if (p.epi != EPI_STORE && p.epi != EPI_ACCUM && p.epi != EPI_SWIGLU) return false;
+    if (p.epi != EPI_STORE && p.epi != EPI_ACCUM && p.epi != EPI_SWIGLU && p.epi != EPI_ARGMAX) return false;
     const int cols = p.epi == EPI_SWIGLU ? w.n / 2 : w.n;
     if (p.seg[0].row_end != cols) return false;
     return tc_gemm_supported(w.dtype, p.M, w.n, w.k, p.epi);
@@ -355,6 +355,8 @@ l0b_status gemv(l0b_model* m, const ModelMatrix& w, const GemvParams& p) {
     a.split = 1;
     a.rscale = m->rscale;
     a.wscale = w.dtype == L0B_I8 ? w.scales : nullptr;
+    a.argmax = p.argmax;
+    a.argmax_base = p.argmax_base;
     return tc_gemm_launch(m->dev, a);
 }
 

@@ -49,8 +49,10 @@ def test_batched_logits_match_single_sequences(lz, device, suite, precision, bat
             assert err <= 2e-3 * scale, f"sequence {s}: max err {err} (scale {scale})"
 
 
-def test_batched_device_greedy_matches_single(lz, device, suite):
-    batch, steps = 4, 6
+@pytest.mark.parametrize("batch", [4, 12])
+def test_batched_device_greedy_matches_single(lz, device, suite, batch):
+    """Batch 12 runs its projections and the LM head's argmax on the tensor-core GEMM (8+ rows)."""
+    steps = 6
     prompts = _prompts(batch)
     with _model(lz, device, suite, batch, "int8") as mb:
         for s, p in enumerate(prompts):
