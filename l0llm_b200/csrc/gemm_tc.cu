@@ -19,9 +19,11 @@
 // to arrive (an atomic counter per tile, no waiting) sums the S partials in split order — deterministic
 // — runs the epilogue and re-arms the counter.
 //
-// int8 weights (one scale per weight row): TMA brings the raw [128 x 64] byte tile per stage, warps 2-3
-// turn it into one of two swizzled f16 A tiles (exact: |q| <= 128) and hand it to the MMA issuer through
-// an mbarrier; the epilogue multiplies by the row's scale.
+// int8 weights (one scale per weight row) run on the integer tensor-core MMA (kind::i8, s8 x s8 -> s32)
+// straight from TMA: no conversion pass. Their f32 activations enter as four balanced base-128 int8
+// digits per token (x * 2^s = d0 + 128 d1 + 128^2 d2 + 128^3 d3, |x * 2^s| < 2^26: ~27 bits of each
+// token's largest value), four accumulator columns per token summed exactly in the epilogue, then times
+// 2^-s and the row's scale. The integer sums are exact (|sum| < 2^31 for K < 2^17).
 //
 // Every mbarrier wait is bounded (~2 s); a timeout sets the device error flag and the CTA exits after
 // releasing its tensor memory. No TMA multicast is used.
@@ -44,12 +46,12 @@ constexpr long long kWaitCycles = 4000000000LL;
 
 struct TcParams {
     CUtensorMap wmap;  // W [N, K] 16-bit (int8: bytes, no swizzle), box {64, 128} (SwiGLU: {64, 64})
-    CUtensorMap xmap;  // X 16-bit, row stride K, box {64, BN}: [M, K], or the paired hi / lo layout
+    CUtensorMap xmap;  // X row stride K, box {64 (int8: 128), BN}: [M, K], paired hi / lo, or int8 digits
     int M, N, K, epi, ld, half_n;
     float* out;
     const float* bias;
     int* error;
-    int pair;              // x rows come as hi / lo pairs: token columns BN / 2, summed in the epilogue
+    int mode;              // x rows per token: 0 one, 1 hi / lo pair (BN / 2 tokens), 2 four int8 digits (BN / 4)
     const float* rscale;   // per-token result scale or null
     const __half* wscale;  // int8: f16 scale per weight row
     float* part;           // split-K partial tiles (gridDim.z > 1)
@@ -57,16 +59,6 @@ struct TcParams {
     unsigned long long* argmax;  // EPI_ARGMAX: per-token keys (atomicMax), index = row + argmax_base
     int argmax_base;
 };
-
-// Four signed bytes -> two f16x2 (bytes 0,1 and bytes 2,3), exact: u = b ^ 0x80 placed in the low
-// mantissa of 1024.0 (0x64uu) is 1024 + u, and subtracting 1152 leaves b.
-__device__ __forceinline__ void i8x4_to_h2x2(uint32_t w, uint32_t& lo, uint32_t& hi) {
-    const uint32_t u = w ^ 0x80808080u;
-    const uint32_t p0 = __byte_perm(u, 0x64646464u, 0x5140);
-    const uint32_t p1 = __byte_perm(u, 0x64646464u, 0x5342);
-    asm("sub.f16x2 %0, %1, %2;" : "=r"(lo) : "r"(p0), "r"(0x64806480u));
-    asm("sub.f16x2 %0, %1, %2;" : "=r"(hi) : "r"(p1), "r"(0x64806480u));
-}
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -126,6 +118,14 @@ __device__ __forceinline__ void tc_mma(uint32_t tmem_d, uint64_t da, uint64_t db
         : "memory");
 }
 
+__device__ __forceinline__ void tc_mma_i8(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc, uint32_t accum) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "l"(da), "l"(db), "r"(idesc), "r"(accum)
+        : "memory");
+}
+
 __device__ __forceinline__ void tc_commit(uint64_t* bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
                  : "memory");
@@ -144,55 +144,50 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
     for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-// Shared-memory plan of one instantiation: 16-bit weights take an A tile per stage; int8 weights take a
-// raw byte tile per stage plus two converted A tiles. Stages fill ~100 KB (two CTAs per SM) for BN <= 64
-// and ~196 KB (one CTA per SM) above, at most 8.
+// Shared-memory plan of one instantiation: an A tile [128 rows x 128 bytes] and a B tile [BN x 128 bytes]
+// per stage (64 k of 16-bit values or 128 k of int8), stages filling ~100 KB (two CTAs per SM) for
+// BN <= 64, ~196 KB (one CTA per SM) above, at most 8.
 template <int BN, int FMT>
 struct TcCfg {
     static constexpr bool kQ8 = FMT == 2;
-    static constexpr int A_BYTES = kBM * kBK * 2;
-    static constexpr int B_BYTES = BN * kBK * 2;
-    static constexpr int Q_BYTES = kQ8 ? kBM * kBK : 0;
-    static constexpr int A_TILES_FIXED = kQ8 ? 2 : 0;
-    static constexpr int STAGE_BYTES = (kQ8 ? Q_BYTES : A_BYTES) + B_BYTES;
+    static constexpr int KB = kQ8 ? 128 : kBK;  // k per stage (128-byte rows)
+    static constexpr int A_BYTES = kBM * 128;
+    static constexpr int B_BYTES = BN * 128;
+    static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
     static constexpr int TARGET = BN <= 64 ? 100 * 1024 : 196 * 1024;
-    static constexpr int STAGES_FIT = (TARGET - A_TILES_FIXED * A_BYTES) / STAGE_BYTES;
+    static constexpr int CTAS_PER_SM = BN <= 64 ? 2 : 1;
+    static constexpr int STAGES_FIT = TARGET / STAGE_BYTES;
     static constexpr int STAGES = STAGES_FIT > 8 ? 8 : STAGES_FIT;
-    static constexpr int A_TILES = kQ8 ? 2 : STAGES;
-    static constexpr size_t SMEM = 1024 + static_cast<size_t>(A_TILES) * A_BYTES +
-                                   static_cast<size_t>(STAGES) * (B_BYTES + Q_BYTES) + 256;
-    static_assert(STAGES >= 3, "the int8 converter's release of A tiles needs three or more stages");
+    static constexpr size_t SMEM = 1024 + static_cast<size_t>(STAGES) * STAGE_BYTES + 256;
+    static_assert(STAGES >= 3, "three or more stages");
 };
 
-// FMT: 0 = f16, 1 = bf16 (weights and activations), 2 = int8 weights converted to f16 in shared memory.
+// FMT: 0 = f16, 1 = bf16 (kind::f16, f32 accumulators), 2 = int8 weights and digits (kind::i8, s32).
 template <int BN, int FMT>
 __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const __grid_constant__ TcParams p) {
     using Cfg = TcCfg<BN, FMT>;
     constexpr bool kQ8 = Cfg::kQ8;
-    constexpr int ST = Cfg::STAGES;
-    constexpr int A_BYTES = Cfg::A_BYTES, B_BYTES = Cfg::B_BYTES, Q_BYTES = Cfg::Q_BYTES;
-    constexpr uint32_t MMA_FMT = FMT == 1 ? 1 : 0;
+    constexpr int ST = Cfg::STAGES, KB = Cfg::KB;
+    constexpr int A_BYTES = Cfg::A_BYTES, B_BYTES = Cfg::B_BYTES;
     extern __shared__ uint8_t smem_raw[];
     __shared__ int last_split;
     __shared__ unsigned long long amax_keys[4][16];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint8_t* sA = smem;                        // 16-bit: one A tile per stage; int8: two converted tiles
-    uint8_t* sB = sA + Cfg::A_TILES * A_BYTES;
-    uint8_t* sQ = sB + ST * B_BYTES;           // int8: raw weight tiles [128][64] bytes per stage
-    uint64_t* full = reinterpret_cast<uint64_t*>(sQ + ST * Q_BYTES);
+    uint8_t* sA = smem;
+    uint8_t* sB = sA + ST * A_BYTES;
+    uint64_t* full = reinterpret_cast<uint64_t*>(sB + ST * B_BYTES);
     uint64_t* empty = full + ST;
-    uint64_t* conv = empty + ST;               // int8: converted A tile a (= stage index & 1) is ready
-    uint64_t* accum = conv + 2;
+    uint64_t* accum = empty + ST;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int tb = p.pair ? BN / 2 : BN;       // tokens per tile
+    const int tb = p.mode == 2 ? BN / 4 : p.mode == 1 ? BN / 2 : BN;  // tokens per tile
     const int t0 = blockIdx.x * tb;
-    const int xrow0 = blockIdx.x * BN;         // first x16 row of this token tile
+    const int xrow0 = blockIdx.x * BN;         // first x row of this token tile
     const int wt = blockIdx.y;
     const int z = blockIdx.z, S = gridDim.z;
     const bool swiglu = p.epi == EPI_SWIGLU;
-    const int nk = (p.K + kBK - 1) / kBK;
+    const int nk = (p.K + KB - 1) / KB;
     const int kb0 = z * nk / S;
     const int nst = (z + 1) * nk / S - kb0;    // >= 1: the host keeps S <= nk
 
@@ -201,8 +196,6 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const __grid_const
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1);
         }
-        mbar_init(&conv[0], 64);
-        mbar_init(&conv[1], 64);
         mbar_init(accum, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -230,66 +223,41 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const __grid_const
                 ok = false;
                 break;
             }
-            mbar_expect_tx(&full[s], (kQ8 ? Q_BYTES : A_BYTES) + B_BYTES);
-            const int k0 = (kb0 + i) * kBK;
-            uint8_t* wdst = kQ8 ? sQ + s * Q_BYTES : sA + s * A_BYTES;
+            mbar_expect_tx(&full[s], A_BYTES + B_BYTES);
+            const int k0 = (kb0 + i) * KB;
             if (swiglu) {
-                tma_load_2d(wdst, &p.wmap, &full[s], k0, wt * 64);
-                tma_load_2d(wdst + (kQ8 ? Q_BYTES : A_BYTES) / 2, &p.wmap, &full[s], k0, p.half_n + wt * 64);
+                tma_load_2d(sA + s * A_BYTES, &p.wmap, &full[s], k0, wt * 64);
+                tma_load_2d(sA + s * A_BYTES + A_BYTES / 2, &p.wmap, &full[s], k0, p.half_n + wt * 64);
             } else {
-                tma_load_2d(wdst, &p.wmap, &full[s], k0, wt * kBM);
+                tma_load_2d(sA + s * A_BYTES, &p.wmap, &full[s], k0, wt * kBM);
             }
             tma_load_2d(sB + s * B_BYTES, &p.xmap, &full[s], k0, xrow0);
         }
     } else if (warp == 1 && lane == 0) {
-        // MMA issuer: D[128, BN] (+)= A[128, 16] B[BN, 16]^T, four per stage.
-        constexpr uint32_t idesc = (1u << 4) | (MMA_FMT << 7) | (MMA_FMT << 10) |
-                                   (static_cast<uint32_t>(BN >> 3) << 17) | (static_cast<uint32_t>(kBM >> 4) << 24);
+        // MMA issuer: D[128, BN] (+)= A[128, 32 bytes] B[BN, 32 bytes]^T (k = 16 values of 16 bits, or
+        // 32 of int8), four per stage.
+        constexpr uint32_t idesc = kQ8 ? ((2u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(BN >> 3) << 17) |
+                                          (static_cast<uint32_t>(kBM >> 4) << 24))
+                                       : ((1u << 4) | (static_cast<uint32_t>(FMT) << 7) |
+                                          (static_cast<uint32_t>(FMT) << 10) | (static_cast<uint32_t>(BN >> 3) << 17) |
+                                          (static_cast<uint32_t>(kBM >> 4) << 24));
         for (int i = 0; i < nst; ++i) {
             const int s = i % ST;
             const uint32_t ph = (i / ST) & 1;
-            if (!mbar_wait(&full[s], ph) || (kQ8 && !mbar_wait(&conv[i & 1], (i >> 1) & 1))) {
+            if (!mbar_wait(&full[s], ph)) {
                 ok = false;
                 break;
             }
             tc_fence_after();
-            const uint64_t da = smem_desc(kQ8 ? sA + (i & 1) * A_BYTES : sA + s * A_BYTES);
-            const uint64_t db = smem_desc(sB + s * B_BYTES);
+            const uint64_t da = smem_desc(sA + s * A_BYTES), db = smem_desc(sB + s * B_BYTES);
 #pragma unroll
-            for (int k = 0; k < kBK / 16; ++k) tc_mma(tmem, da + 2 * k, db + 2 * k, idesc, (i | k) != 0);
+            for (int k = 0; k < 4; ++k) {
+                if constexpr (kQ8) tc_mma_i8(tmem, da + 2 * k, db + 2 * k, idesc, (i | k) != 0);
+                else tc_mma(tmem, da + 2 * k, db + 2 * k, idesc, (i | k) != 0);
+            }
             tc_commit(&empty[s]);
         }
         tc_commit(accum);
-    } else if (kQ8 && warp >= 2) {
-        // Converters: stage i's bytes go to A tile i & 1 once the MMAs of stage i - 2 (the tile's last
-        // reader) have completed. 512 16-byte pieces of int8 per stage, 8 per thread; row r's f16 chunk
-        // c goes to 16-byte slot c ^ (r & 7) of its 128-byte row (the TMA / UMMA 128-byte swizzle).
-        const int ct = threadIdx.x - 64;
-        for (int i = 0; i < nst; ++i) {
-            const int s = i % ST;
-            if (!mbar_wait(&full[s], (i / ST) & 1) || (i >= 2 && !mbar_wait(&empty[(i - 2) % ST], ((i - 2) / ST) & 1))) {
-                ok = false;
-                break;
-            }
-            const uint8_t* q = sQ + s * Q_BYTES;
-            uint8_t* a = sA + (i & 1) * A_BYTES;
-#pragma unroll
-            for (int it = 0; it < 8; ++it) {
-                const int c = ct + 64 * it;
-                const int r = c >> 2, j = c & 3;
-                const uint4 w = *reinterpret_cast<const uint4*>(q + r * 64 + j * 16);
-                uint4 o0, o1;
-                i8x4_to_h2x2(w.x, o0.x, o0.y);
-                i8x4_to_h2x2(w.y, o0.z, o0.w);
-                i8x4_to_h2x2(w.z, o1.x, o1.y);
-                i8x4_to_h2x2(w.w, o1.z, o1.w);
-                *reinterpret_cast<uint4*>(a + r * 128 + (((2 * j) ^ (r & 7)) << 4)) = o0;
-                *reinterpret_cast<uint4*>(a + r * 128 + (((2 * j + 1) ^ (r & 7)) << 4)) = o1;
-            }
-            // Generic-proxy writes become visible to the tensor core's (async proxy) reads.
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            mbar_arrive(&conv[i & 1]);
-        }
     }
     __syncwarp();
 
@@ -302,10 +270,25 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const __grid_const
     const float wsc = (kQ8 && row < p.N) ? __half2float(p.wscale[row]) : 1.f;
     const uint32_t tl = tmem + (static_cast<uint32_t>(warp * 32) << 16);
     float* xchg = reinterpret_cast<float*>(sA);  // SwiGLU: up rows handed from warps 2-3 to warps 0-1
-    // Accumulator columns c0..c0+15 of this lane: the token's hi column plus (paired) its lo column.
+    // Accumulator columns c0..c0+15 of this lane: the token's hi column plus (paired) its lo column,
+    // or its four digit columns (s32, exact) combined in f64 and rounded once.
     auto load_acc = [&](int c0, float (&v)[16]) {
         tmem_ld16(tl + c0, v);
-        if (p.pair) {
+        if (kQ8) {
+            double acc[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) acc[j] = static_cast<double>(__float_as_int(v[j]));
+#pragma unroll
+            for (int dg = 1; dg < 4; ++dg) {
+                float u[16];
+                tmem_ld16(tl + dg * (BN / 4) + c0, u);
+                const double w = static_cast<double>(1 << (7 * dg));
+#pragma unroll
+                for (int j = 0; j < 16; ++j) acc[j] += w * static_cast<double>(__float_as_int(u[j]));
+            }
+#pragma unroll
+            for (int j = 0; j < 16; ++j) v[j] = static_cast<float>(acc[j]);
+        } else if (p.mode == 1) {
             float u[16];
             tmem_ld16(tl + BN / 2 + c0, u);
 #pragma unroll
@@ -575,6 +558,91 @@ __global__ void __launch_bounds__(512) cast_rows_split_reg_kernel(const float* x
     }
 }
 
+// Four balanced base-128 digits of a scaled activation: X = rint(v) (|X| < 2^26) = d0 + 128 d1 + 128^2 d2
+// + 128^3 d3 with d0..d2 in [-64, 64); packed into byte `lane` of each digit's word.
+__device__ __forceinline__ void digits4(float v, int lane, uint32_t (&w)[4]) {
+    int X = __float2int_rn(v);
+#pragma unroll
+    for (int dg = 0; dg < 3; ++dg) {
+        const int d = ((X + 64) & 127) - 64;
+        w[dg] |= (static_cast<uint32_t>(d) & 0xFFu) << (8 * lane);
+        X = (X - d) >> 7;
+    }
+    w[3] |= (static_cast<uint32_t>(X) & 0xFFu) << (8 * lane);
+}
+
+// Per token: RMS norm (optional) and the row maximum, then int8 digits of x * 2^s with the largest |x|
+// * 2^s just below 2^26, to rows (t / tb) * bn + dg * tb + t % tb (digit dg) of the digit layout; rscale =
+// 2^-s. Register-resident: each thread holds VPT float4 of the row (K % 4 == 0, K <= 4 * VPT * threads).
+template <int VPT>
+__global__ void __launch_bounds__(512) cast_rows_digits_kernel(const float* x, long long ld_x, const float* norm_w,
+                                                               float eps, uint8_t* out8, float* rscale, int K, int bn,
+                                                               int tb) {
+    __shared__ float red[32];
+    __shared__ float mx[32];
+    pdl_wait();
+    const int t = blockIdx.x;
+    const int K4 = K >> 2;
+    const float4* xr = reinterpret_cast<const float4*>(x + t * ld_x);
+    const float4* nw = reinterpret_cast<const float4*>(norm_w);
+    float4 v[VPT];
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+        const int k4 = threadIdx.x + i * blockDim.x;
+        v[i] = k4 < K4 ? xr[k4] : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    float ss = 0.f, am = 0.f;
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+        const int k4 = threadIdx.x + i * blockDim.x;
+        ss += v[i].x * v[i].x + v[i].y * v[i].y + v[i].z * v[i].z + v[i].w * v[i].w;
+        if (norm_w && k4 < K4) {
+            const float4 w = nw[k4];
+            v[i].x *= w.x;
+            v[i].y *= w.y;
+            v[i].z *= w.z;
+            v[i].w *= w.w;
+        }
+        am = fmaxf(am, fmaxf(fmaxf(fabsf(v[i].x), fabsf(v[i].y)), fmaxf(fabsf(v[i].z), fabsf(v[i].w))));
+    }
+    const float rstd = norm_w ? 1.0f / sqrtf(block_sum(ss, red) / static_cast<float>(K) + eps) : 1.0f;
+    am = warp_max(am);
+    if ((threadIdx.x & 31) == 0) mx[threadIdx.x >> 5] = am;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        float m = threadIdx.x < (blockDim.x >> 5) ? mx[threadIdx.x] : 0.f;
+        m = warp_max(m);
+        if (threadIdx.x == 0) mx[0] = m;
+    }
+    __syncthreads();
+    const float top = mx[0] * rstd;
+    int e = 0;
+    if (top > 0.f && isfinite(top)) {
+        int ex;
+        frexpf(top, &ex);  // top = f 2^ex, f in [0.5, 1): top 2^(26 - ex) < 2^26
+        e = min(max(26 - ex, -120), 120);
+    }
+    const float sc = rstd * ldexpf(1.0f, e);
+    if (threadIdx.x == 0) rscale[t] = ldexpf(1.0f, -e);
+    const long long row0 = static_cast<long long>(t / tb) * bn + t % tb;
+    uint32_t* rows[4];
+#pragma unroll
+    for (int dg = 0; dg < 4; ++dg) rows[dg] = reinterpret_cast<uint32_t*>(out8 + (row0 + dg * tb) * K);
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+        const int k4 = threadIdx.x + i * blockDim.x;
+        if (k4 < K4) {
+            uint32_t w[4] = {0u, 0u, 0u, 0u};
+            digits4(v[i].x * sc, 0, w);
+            digits4(v[i].y * sc, 1, w);
+            digits4(v[i].z * sc, 2, w);
+            digits4(v[i].w * sc, 3, w);
+#pragma unroll
+            for (int dg = 0; dg < 4; ++dg) rows[dg][k4] = w[dg];
+        }
+    }
+}
+
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
@@ -593,8 +661,8 @@ EncodeTiledFn encode_fn() {
     return fn;
 }
 
-// Row-major [rows, K] matrix, box {64 elements, box_rows}: 16-bit with the 128-byte swizzle, or int8
-// bytes unswizzled (the converter warps read them as plain 64-byte rows).
+// Row-major [rows, K] matrix with the 128-byte swizzle, box {128 bytes of k, box_rows}: 64 values of 16
+// bits or 128 of int8.
 l0b_status make_map(CUtensorMap* map, const void* base, int dtype, long long rows, long long K, int box_rows) {
     EncodeTiledFn fn = encode_fn();
     L0B_REQUIRE(fn, L0B_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
@@ -603,13 +671,13 @@ l0b_status make_map(CUtensorMap* map, const void* base, int dtype, long long row
                 "TMA needs 16-byte aligned rows (K * element size %% 16 == 0)");
     const cuuint64_t dims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(rows)};
     const cuuint64_t strides[1] = {static_cast<cuuint64_t>(K * esize)};
-    const cuuint32_t box[2] = {static_cast<cuuint32_t>(kBK), static_cast<cuuint32_t>(box_rows)};
+    const cuuint32_t box[2] = {static_cast<cuuint32_t>(128 / esize), static_cast<cuuint32_t>(box_rows)};
     const cuuint32_t estr[2] = {1, 1};
     const CUtensorMapDataType type = dtype == L0B_I8     ? CU_TENSOR_MAP_DATA_TYPE_UINT8
                                      : dtype == L0B_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
                                                          : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
     CUresult r = fn(map, type, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                    dtype == L0B_I8 ? CU_TENSOR_MAP_SWIZZLE_NONE : CU_TENSOR_MAP_SWIZZLE_128B,
+                    CU_TENSOR_MAP_SWIZZLE_128B,
                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     L0B_REQUIRE(r == CUDA_SUCCESS, L0B_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", static_cast<int>(r));
     return L0B_OK;
@@ -653,16 +721,17 @@ size_t tc_gemm_part_floats(int sm_count) { return static_cast<size_t>(2) * sm_co
 // paired). Weight tiles: 128 rows (SwiGLU: 64 gate + 64 up). K splits: when the tiles fill fewer than the
 // resident slots (two CTAs per SM at BN <= 64), split K so tiles x S comes close to the slots, each
 // split keeping two or more K blocks of 64 and the partial tiles within the scratch bound.
-TcPlan tc_gemm_plan(int M, int N, int K, int epi, bool pair, int sm_count) {
+TcPlan tc_gemm_plan(int M, int N, int K, int epi, bool pair, int wdtype, int sm_count) {
     TcPlan pl;
-    const int cols = pair ? 2 * M : M;
-    pl.bn = cols <= 32 ? 32 : cols <= 64 ? 64 : cols <= 128 ? 128 : 256;
-    pl.tb = pair ? pl.bn / 2 : pl.bn;
+    const bool q8 = wdtype == L0B_I8;  // int8 weights: four digit columns per token, BN >= 64
+    const int cols = q8 ? 4 * M : pair ? 2 * M : M;
+    pl.bn = (cols <= 32 && !q8) ? 32 : cols <= 64 ? 64 : cols <= 128 ? 128 : 256;
+    pl.tb = q8 ? pl.bn / 4 : pair ? pl.bn / 2 : pl.bn;
     pl.tiles_x = (M + pl.tb - 1) / pl.tb;
     pl.tiles_y = epi == EPI_SWIGLU ? (N / 2) / 64 : (N + kBM - 1) / kBM;
     const long long tiles = static_cast<long long>(pl.tiles_x) * pl.tiles_y;
     const int slots = sm_count * (pl.bn <= 64 ? 2 : 1);
-    const int nk = (K + kBK - 1) / kBK;
+    const int nk = (K + (q8 ? 127 : kBK - 1)) / (q8 ? 128 : kBK);
     int S = tiles >= slots ? 1 : static_cast<int>(slots / tiles);
     if (S > nk / 2) S = nk / 2;
     if (S > 16) S = 16;
@@ -679,7 +748,7 @@ TcPlan tc_gemm_plan(int M, int N, int K, int epi, bool pair, int sm_count) {
 l0b_status tc_gemm_launch(l0b_device* d, const TcGemmArgs& a) {
     L0B_REQUIRE(tc_gemm_supported(a.wdtype, a.M, a.N, a.K, a.epi), L0B_ERR_UNSUPPORTED,
                 "tensor-core GEMM does not take M=%d N=%d K=%d epi=%d dtype=%d", a.M, a.N, a.K, a.epi, a.wdtype);
-    TcPlan plan = tc_gemm_plan(a.M, a.N, a.K, a.epi, a.split != 0, d->sm_count);
+    TcPlan plan = tc_gemm_plan(a.M, a.N, a.K, a.epi, a.split != 0, a.wdtype, d->sm_count);
     if (plan.S > 1 && (!a.part || !a.counters || a.part_floats < plan.part_floats || a.counter_count < plan.counters)) {
         plan.S = 1;  // no scratch for the split: one CTA per tile
         plan.part_floats = 0;
@@ -691,10 +760,10 @@ l0b_status tc_gemm_launch(l0b_device* d, const TcGemmArgs& a) {
     const bool q8 = a.wdtype == L0B_I8;
     L0B_REQUIRE(!q8 || a.wscale, L0B_ERR_ARGUMENT, "int8 weights need their row scales");
     L0B_TRY(make_map(&p.wmap, a.w, a.wdtype, a.N, a.K, swiglu ? 64 : kBM));
-    const long long xrows = a.split ? tc_pair_rows(plan) : a.M;
-    L0B_TRY(make_map(&p.xmap, a.x16, q8 ? L0B_F16 : a.wdtype, xrows, a.K, plan.bn));
+    const long long xrows = (a.split || q8) ? tc_pair_rows(plan) : a.M;
+    L0B_TRY(make_map(&p.xmap, a.x16, a.wdtype, xrows, a.K, plan.bn));
     p.wscale = static_cast<const __half*>(a.wscale);
-    p.pair = a.split ? 1 : 0;
+    p.mode = q8 ? 2 : a.split ? 1 : 0;
     p.rscale = a.rscale;
     L0B_REQUIRE(a.epi != EPI_ARGMAX || a.argmax, L0B_ERR_ARGUMENT, "the argmax epilogue needs its key array");
     p.argmax = a.argmax;
@@ -725,6 +794,16 @@ l0b_status cast_rows_split_launch(l0b_device* d, const float* x, long long ld_x,
     const bool vec = K % 4 == 0 && ld_x % 4 == 0 && reinterpret_cast<uintptr_t>(x) % 16 == 0 &&
                      (!norm_w || reinterpret_cast<uintptr_t>(norm_w) % 16 == 0) &&
                      reinterpret_cast<uintptr_t>(out16) % 8 == 0;
+    if (dtype == L0B_I8) {
+        L0B_REQUIRE(vec && K <= 4 * 10 * 512, L0B_ERR_UNSUPPORTED,
+                    "int8 digits need 16-byte aligned f32 rows with K %% 4 == 0 and K <= 20480");
+        uint8_t* o = static_cast<uint8_t*>(out16);
+        if (K <= 4 * 4 * 256)
+            return d->launch(cast_rows_digits_kernel<4>, dim3(M), dim3(256), 0, x, ld_x, norm_w, eps, o, rscale, K,
+                             plan.bn, plan.tb);
+        return d->launch(cast_rows_digits_kernel<10>, dim3(M), dim3(512), 0, x, ld_x, norm_w, eps, o, rscale, K,
+                         plan.bn, plan.tb);
+    }
     if (vec && K <= 4 * 4 * 256)
         return d->launch(cast_rows_split_reg_kernel<4>, dim3(M), dim3(256), 0, x, ld_x, norm_w, eps, out16, rscale,
                          dtype, K, plan.bn, plan.tb);

@@ -19,7 +19,7 @@ struct TcGemmArgs {
     int M, N, K;           // tokens, weight rows, inner dimension
     const void* x16;       // activations in the GEMM's 16-bit format (layout below)
     const void* w;         // [N, K] weights, f16, bf16 or int8
-    int wdtype;            // L0B_F16, L0B_BF16 or L0B_I8 (activations then f16)
+    int wdtype;            // L0B_F16, L0B_BF16 or L0B_I8 (activations then int8 digits)
     int epi;               // GemvEpi: STORE, ACCUM, SWIGLU (W = [gate; up], N = 2 * I) or ARGMAX
     float* out;            // f32 output, row stride ld (SWIGLU: [M, N/2])
     int ld;
@@ -27,7 +27,9 @@ struct TcGemmArgs {
     // Paired activations (cast_rows_split_launch): token t of token tile j = t / TB has its hi half in
     // x16 row j * BN + t % TB and its lo residual in row j * BN + TB + t % TB (row stride K); the two
     // accumulator columns are summed, and the result of token t is multiplied by rscale[t].
-    // Unpaired: x16 is [M, K], one rounded row per token.
+    // Unpaired: x16 is [M, K], one rounded row per token. int8 weights (split ignored): x16 holds four
+    // int8 digit rows per token, digit dg of token t in row j * BN + dg * TB + t % TB (TB = BN / 4), and
+    // rscale[t] = 2^-s of the token's scaling (cast_rows_split_launch with dtype L0B_I8).
     int split = 0;
     const float* rscale = nullptr;
     const void* wscale = nullptr;  // int8: f16 [N], one scale per weight row
@@ -43,8 +45,9 @@ struct TcGemmArgs {
     int counter_count = 0;
 };
 
-// The tile plan tc_gemm_launch uses for this shape on `sm_count` SMs (pair = split activations).
-TcPlan tc_gemm_plan(int M, int N, int K, int epi, bool pair, int sm_count);
+// The tile plan tc_gemm_launch uses for this shape and weight type on `sm_count` SMs (pair = split
+// 16-bit activations; int8 weights always take four digit columns per token).
+TcPlan tc_gemm_plan(int M, int N, int K, int epi, bool pair, int wdtype, int sm_count);
 
 // Rows of the paired x16 matrix for M tokens under `plan` (tiles_x * BN).
 inline long long tc_pair_rows(const TcPlan& plan) { return static_cast<long long>(plan.tiles_x) * plan.bn; }
@@ -58,7 +61,8 @@ l0b_status cast_rows_launch(l0b_device* d, const float* x, long long ld_x, const
 
 // out16 = the rows of x (RMS-normalised with norm_w when given) as hi / lo pairs in f16/bf16 in the
 // paired layout of `plan` (row stride K); for f16 each token is first scaled by a power of two putting
-// its largest value near 2^14, and rscale[m] receives the inverse (bf16: 1).
+// its largest value near 2^14, and rscale[m] receives the inverse (bf16: 1). dtype L0B_I8: four int8
+// digit rows per token (the int8-weight layout), rscale[m] = 2^-s.
 l0b_status cast_rows_split_launch(l0b_device* d, const float* x, long long ld_x, const float* norm_w, float eps,
                                   void* out16, float* rscale, int dtype, int M, int K, const TcPlan& plan);
 

@@ -334,9 +334,9 @@ bool tc_takes(const l0b_model* m, const ModelMatrix& w, const GemvParams& p) {
 
 l0b_status gemv(l0b_model* m, const ModelMatrix& w, const GemvParams& p) {
     if (!tc_takes(m, w, p)) return gemv_nk_launch(m->dev, w.dtype, p);
-    const TcPlan plan = tc_gemm_plan(p.M, w.n, w.k, p.epi, true, m->dev->sm_count);
+    const TcPlan plan = tc_gemm_plan(p.M, w.n, w.k, p.epi, true, w.dtype, m->dev->sm_count);
     L0B_TRY(cast_rows_split_launch(m->dev, static_cast<const float*>(p.x), p.x_ld, p.norm_w, p.eps, m->x16,
-                                   m->rscale, w.dtype == L0B_I8 ? L0B_F16 : w.dtype, p.M, w.k, plan));
+                                   m->rscale, w.dtype, p.M, w.k, plan));
     TcGemmArgs a;
     a.part = m->tc_part;
     a.part_floats = tc_gemm_part_floats(m->dev->sm_count);

@@ -564,12 +564,12 @@ l0b_status linear_tc(l0b_suite* s, l0b_device* d, int32_t m, int32_t n, int32_t 
     L0B_TRY(need(out, "out", L0B_F32, static_cast<long long>(m) * out_cols));
     if (norm_w) L0B_TRY(need(norm_w, "norm_w", L0B_F32, k));
     if (bias) L0B_TRY(need(bias, "bias", L0B_F32, n));
-    const int xdtype = q8 ? L0B_F16 : w->dtype;  // int8 weights meet f16 activations
-    const TcPlan plan = tc_gemm_plan(m, n, k, epi, split, d->sm_count);
+    const int xdtype = w->dtype;  // int8 weights: the activations as int8 digits (always near-f32)
+    const TcPlan plan = tc_gemm_plan(m, n, k, epi, split, w->dtype, d->sm_count);
     void* x16 = nullptr;
     float* rscale = nullptr;
-    if (split) {
-        const size_t x_bytes = (static_cast<size_t>(tc_pair_rows(plan)) * k * 2 + 255) / 256 * 256;
+    if (split || q8) {
+        const size_t x_bytes = (static_cast<size_t>(tc_pair_rows(plan)) * k * (q8 ? 1 : 2) + 255) / 256 * 256;
         L0B_TRY(d->ensure_scratch(x_bytes + static_cast<size_t>(m) * sizeof(float), &x16, 1));
         rscale = reinterpret_cast<float*>(static_cast<char*>(x16) + x_bytes);
         L0B_TRY(cast_rows_split_launch(d, F(x), k, norm_w ? F(norm_w) : nullptr, eps, x16, rscale, xdtype, m, k,

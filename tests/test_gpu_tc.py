@@ -135,17 +135,19 @@ def _q8_rows(rng, n, k):
 
 
 @pytest.mark.parametrize("split", [False, True])
-@pytest.mark.parametrize("m,n,k,epi", [(64, 512, 896, 0), (100, 4608, 3584, 1), (17, 384, 208, 0), (300, 256, 512, 1)])
+@pytest.mark.parametrize("m,n,k,epi", [(64, 512, 896, 0), (100, 4608, 3584, 1), (17, 384, 208, 0), (300, 256, 512, 1),
+                                       (8, 640, 3584, 1), (5, 256, 208, 0), (16, 3584, 18944, 1)])
 def test_tc_gemm_int8_row_scales(lz, device, suite, split, m, n, k, epi):
-    """int8 weights with one f16 scale per row: raw bytes by TMA, converted to f16 in shared memory by
-    two warps, row scale in the epilogue. The integers are exact in f16, so against the f64 product the
-    only differences are the activation rounding (none in split mode past 22 bits) and fp32 sums."""
+    """int8 weights with one f16 scale per row on the integer MMA (kind::i8): the activations go in as four
+    int8 digits of x * 2^s (~27 bits of each token's largest value, with or without the f32 flag), the
+    s32 sums are exact, so against the f64 product only the digit rounding and the final f32 rounding
+    remain. K = 208 leaves a partial 128-k stage; K = 18944 checks the s32 range."""
     rng = np.random.default_rng(m + n * 3 + k)
     x = (rng.standard_normal((m, k)) * np.exp2(rng.uniform(-8, 8, (m, 1)))).astype(np.float32)
     q, s16 = _q8_rows(rng, n, k)
     bias = (rng.standard_normal(n) * 0.1).astype(np.float32)
     base = rng.standard_normal((m, n)).astype(np.float32)
-    xa = x.astype(np.float64) if split else _round16(x, "f16").astype(np.float64)
+    xa = x.astype(np.float64)
     sc = s16.astype(np.float64)
     want = (xa @ q.astype(np.float64).T) * sc + bias
     if epi == 1:
