@@ -387,6 +387,9 @@ L0B_API l0b_status l0b_comm_free(l0b_comm* comm);
  * into the current command list when the device is recording). */
 L0B_API l0b_status l0b_comm_allreduce(l0b_comm* comm, l0b_buffer* buf, int64_t count);
 
+/* Tuning: the largest K split the tensor-core GEMM may use for narrow projections (1..16, default 16;
+ * <= 0 restores the default). Affects plans made after the call. */
+L0B_API l0b_status l0b_tc_set_max_splits(int32_t splits);
 /* Process-wide choice of the decode GEMV kernel for shapes both take: 1 (default) = tensor-core
  * mma.sync streaming kernel, 0 = fp32-FMA streaming kernel. Used by tests to cover both; recorded
  * command lists keep the kernel they were recorded with. No counterpart in the reference. */

@@ -209,6 +209,10 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const __grid_const
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    if (warp == 0 && lane == 0) {
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&p.wmap)) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&p.xmap)) : "memory");
+    }
 
     pdl_wait();
     pdl_launch_dependents();
@@ -394,9 +398,21 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const __grid_const
                 float v[16];
 #pragma unroll
                 for (int j = 0; j < 16; ++j) v[j] = 0.f;
-                for (int zz = 0; zz < S; ++zz) {
+                // Four splits' loads in flight at a time; the sum still runs in split order.
+                for (int z0 = 0; z0 < S; z0 += 4) {
+                    float q[4][16];
 #pragma unroll
-                    for (int j = 0; j < 16; ++j) v[j] += __ldcg(&base[(static_cast<size_t>(zz) * tb + c0 + j) * kBM + rl]);
+                    for (int dz = 0; dz < 4; ++dz) {
+#pragma unroll
+                        for (int j = 0; j < 16; ++j)
+                            q[dz][j] = z0 + dz < S ? __ldcg(&base[(static_cast<size_t>(z0 + dz) * tb + c0 + j) * kBM + rl])
+                                                   : 0.f;
+                    }
+#pragma unroll
+                    for (int dz = 0; dz < 4; ++dz) {
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) v[j] += q[dz][j];
+                    }
                 }
                 finish(c0, v);
             }
@@ -717,6 +733,12 @@ bool tc_gemm_supported(int wdtype, int M, int N, int K, int epi) {
 
 size_t tc_gemm_part_floats(int sm_count) { return static_cast<size_t>(2) * sm_count * 128 * kBM; }
 
+namespace {
+int g_max_splits = 16;  // upper bound on the K split (l0b_tc_set_max_splits)
+}
+
+void tc_gemm_set_max_splits(int s) { g_max_splits = s < 1 ? 16 : (s > 16 ? 16 : s); }
+
 // Token columns: the smallest BN in {32, 64, 128, 256} that holds the tile's columns (hi and lo when
 // paired). Weight tiles: 128 rows (SwiGLU: 64 gate + 64 up). K splits: when the tiles fill fewer than the
 // resident slots (two CTAs per SM at BN <= 64), split K so tiles x S comes close to the slots, each
@@ -734,7 +756,7 @@ TcPlan tc_gemm_plan(int M, int N, int K, int epi, bool pair, int wdtype, int sm_
     const int nk = (K + (q8 ? 127 : kBK - 1)) / (q8 ? 128 : kBK);
     int S = tiles >= slots ? 1 : static_cast<int>(slots / tiles);
     if (S > nk / 2) S = nk / 2;
-    if (S > 16) S = 16;
+    if (S > g_max_splits) S = g_max_splits;
     if (S < 1) S = 1;
     while (S > 1 && (tiles * S * pl.tb * kBM > static_cast<long long>(tc_gemm_part_floats(sm_count)) ||
                      tiles > kTcCounters))

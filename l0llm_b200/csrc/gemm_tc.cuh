@@ -71,6 +71,10 @@ l0b_status cast_rows_split_launch(l0b_device* d, const float* x, long long ld_x,
 // residual add, SwiGLU, argmax.
 bool tc_gemm_supported(int wdtype, int M, int N, int K, int epi);
 
+// Upper bound on the K split of later plans (1..16; <= 0 restores 16). Launches already recorded into
+// command lists keep their plan.
+void tc_gemm_set_max_splits(int s);
+
 // Split-K scratch that covers every plan on `sm_count` SMs: floats and counters.
 size_t tc_gemm_part_floats(int sm_count);
 constexpr int kTcCounters = 4096;

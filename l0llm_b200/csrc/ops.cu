@@ -618,6 +618,11 @@ L0B_API l0b_status l0b_linear_tc_scaled(l0b_suite* s, l0b_device* d, int32_t m, 
     return linear_tc(s, d, m, n, k, x, w, scales, group, norm_w, eps, epilogue, bias, out);
 }
 
+L0B_API l0b_status l0b_tc_set_max_splits(int32_t splits) {
+    tc_gemm_set_max_splits(splits);
+    return L0B_OK;
+}
+
 L0B_API l0b_status l0b_set_gemv_tensor_cores(int32_t enable) {
     gemv_set_tensor_cores(enable != 0);
     return L0B_OK;

@@ -170,6 +170,7 @@ def load_library() -> C.CDLL:
         "l0b_linear_fused": (i32, [vp, vp, i32, i32, i32, vp, vp, vp, i32, vp, f32, i32, vp, vp]),
         "l0b_linear_tc": (i32, [vp, vp, i32, i32, i32, vp, vp, vp, f32, i32, vp, vp]),
         "l0b_linear_tc_scaled": (i32, [vp, vp, i32, i32, i32, vp, vp, vp, i32, vp, f32, i32, vp, vp]),
+        "l0b_tc_set_max_splits": (i32, [i32]),
         "l0b_device_error_status": (i32, [vp, C.POINTER(i32)]),
         "l0b_set_gemv_tensor_cores": (i32, [i32]),
         "l0b_comm_unique_id": (i32, [vp, i32]),
