@@ -470,6 +470,77 @@ def run_cfg4_tp(args) -> int:
     return 0
 
 
+def run_profile_case(case: str) -> int:
+    """Small, self-contained launches for ncu captures (the commands in profiles/ run these).
+
+    decode-bs1 / decode-bs16: the config-2 model (int8, seed 2) after its prompt(s) and three warm-up
+    steps; one more decode step runs inside the NVTX range "step" (capture with --nvtx-include "step/").
+    gemm-gateup-16: the config-2 gate/up projection (int8 [37888, 3584], SwiGLU) at 16 activation rows on
+    the tensor-core GEMM, 3 rotating weight copies (408 MB > L2), 6 warm-up launches then 30 timed.
+    """
+    import ctypes as C
+
+    import torch
+
+    from l0llm_b200 import levelzero as lz
+
+    dev = lz.ComputeDevice(0)
+    suite = lz.LlmKernelSuite.Create(dev)
+    sp = C.c_void_p()
+    lz.check(lz.load_library().l0b_device_stream(dev.handle, C.byref(sp)))
+    rng = np.random.default_rng(SEED)
+    if case in ("decode-bs1", "decode-bs16"):
+        batch = 1 if case == "decode-bs1" else BS16
+        mc = lz.model_config(kv_dtype=lz.F16, max_batch=batch, **CFG2)
+        with lz.LlmModel(dev, suite, mc, CONTEXT + 64, "int8") as model:
+            model.init_synthetic(SEED, 0.02, 1e-3, 2e-2)
+            for sq in range(batch):
+                model.PrefillSequence(sq, rng.integers(0, CFG2["vocab_size"], CONTEXT).astype(np.int32),
+                                      want_logits=False)
+            step = (lambda n: model.decode_greedy_device(n)) if batch == 1 else \
+                (lambda n: model.decode_greedy_device_batch(n, batch))
+            step(3)
+            dev.Synchronize()
+            torch.cuda.nvtx.range_push("step")
+            step(1)
+            dev.Synchronize()
+            torch.cuda.nvtx.range_pop()
+        print(json.dumps({"profile_case": case, "ok": True}))
+    elif case == "gemm-gateup-16":
+        H, I, M, copies = CFG2["hidden_size"], CFG2["intermediate_size"], BS16, 3
+        N = 2 * I
+        qs = [lz.SharedBuffer.from_array(dev, rng.integers(-127, 128, (N, H), dtype=np.int8)) for _ in range(copies)]
+        ss = [lz.SharedBuffer.from_array(dev, rng.uniform(1e-3, 2e-2, N).astype(np.float16)) for _ in range(copies)]
+        x = lz.SharedBuffer.from_array(dev, rng.standard_normal(M * H).astype(np.float32))
+        out = lz.SharedBuffer(dev, lz.F32, M * I)
+        L = lz.load_library()
+
+        def run(i):
+            lz.check(L.l0b_linear_tc_scaled(suite.handle, dev.handle, M, N, H, x.handle, qs[i % copies].handle,
+                                            ss[i % copies].handle, H, None, 0.0, 2 | 0x100, None, out.handle))
+
+        for i in range(6):
+            run(i)
+        stream = torch.cuda.ExternalStream(sp.value)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        dev.Synchronize()
+        e0.record(stream)
+        for i in range(30):
+            run(i)
+        e1.record(stream)
+        e1.synchronize()
+        us = e0.elapsed_time(e1) / 30 * 1e3
+        print(json.dumps({"profile_case": case, "us_per_call_with_cast": round(us, 2),
+                          "weight_gbs": round(N * H / us / 1e3, 1)}))
+        for b in qs + ss + [x, out]:
+            b.Dispose()
+    else:
+        raise SystemExit(f"unknown profile case {case}")
+    suite.Dispose()
+    dev.Dispose()
+    return 0
+
+
 def main() -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -482,7 +553,11 @@ def main() -> int:
     ap.add_argument("--workload", default="cfg2", choices=["cfg2", "cfg3", "cfg4"],
                     help="cfg2: the headline (Qwen2.5-7B int8, one GPU, replicas over N); cfg3: the Gated DeltaNet "
                          "layer alone (bf16, one GPU); cfg4: Llama-3-70B bf16 tensor-parallel over the N ranks")
+    ap.add_argument("--profile-case", choices=["decode-bs1", "decode-bs16", "gemm-gateup-16"],
+                    help="run one small case for an ncu capture instead of the benchmark")
     args = ap.parse_args()
+    if args.profile_case:
+        return run_profile_case(args.profile_case)
     if args.impl == "reference":
         return run_reference(args)
     args.warmup = max(3, args.warmup)

@@ -294,6 +294,17 @@ L0B_API l0b_status l0b_copy_execute(l0b_suite* s, l0b_device* d, l0b_buffer* src
 L0B_API l0b_status l0b_sampling_execute(l0b_suite* s, l0b_device* d, l0b_buffer* logits,
                                         l0b_buffer* sampled, float temperature, float random_val,
                                         int32_t vocab);
+/* LlmSampler.Sample (src/HFLabs.ML.LLM.LevelZero/LlmAbstractions.cs:40-165) on the device, the token
+ * written to out_token (i32 [1]) with no logits readback: repetition penalty over the distinct ids of
+ * `context` (i32 [n_context], may be NULL), greedy when temperature <= 0, else softmax(logits / T) cut to
+ * the top_k most likely tokens and to the shortest prefix reaching top_p, sampled at random_value * (kept
+ * mass) (random_value in [0, 1): the reference's Random.NextDouble()). Ties order by token index. top_k
+ * must lie in [1, 1024] when temperature > 0 (L0B_ERR_UNSUPPORTED otherwise); vocab may be smaller than
+ * the logits buffer (the reference's usable tokenizer vocabulary). */
+L0B_API l0b_status l0b_sample_execute(l0b_suite* s, l0b_device* d, l0b_buffer* logits, int32_t vocab,
+                                      l0b_buffer* context, int32_t n_context, float temperature, float top_p,
+                                      int32_t top_k, float repetition_penalty, double random_value,
+                                      l0b_buffer* out_token);
 
 /* CausalConv.Execute(dev, qkv, convState, convW, out, convDim, k, tokens) -- L/LlmDecoderLayer.cs:392.
  * Depthwise causal conv1d over [history (k-1 taps, oldest first) ++ tokens], then SiLU; the history

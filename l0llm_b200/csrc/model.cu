@@ -71,6 +71,16 @@ struct l0b_model {
     int* out_tokens = nullptr;  // [max_seq * batch_cap]
     int* step_idx = nullptr;
     unsigned long long* keys = nullptr;  // [batch_cap]
+    // Device sampling of sequence 0 (LlmSampler.Sample): the context bitmap for the repetition penalty,
+    // key scratch, the context ids of the last l0b_model_sample_logits call, and the active parameters
+    // while a sampled decode records its steps.
+    uint32_t* seen = nullptr;     // [ceil(vocab_full / 32)]
+    uint32_t* skeys = nullptr;    // [vocab_full]
+    int* ctx_ids = nullptr;       // [max_seq + 1]
+    bool sampling = false;
+    float s_temperature = 0.f, s_top_p = 1.f, s_penalty = 1.f;
+    int s_top_k = 0;
+    unsigned long long s_seed = 0;
     int prefill_seq = 0;           // cache row (sequence) the prefill path writes
     // Tensor parallelism: q/k/v, gate/up and lm_head column-split, o/down row-split (partial sums
     // all-reduced before the residual add), attention head-split, embedding replicated.
@@ -570,6 +580,11 @@ l0b_status record_head(l0b_model* m, int row0, int rows, int advance, int seq0 =
     }
     // Under TP each rank holds the argmax of its vocab shard (global indices): the largest key wins.
     if (m->comm) L0B_TRY(comm_allreduce(m->comm, m->keys + seq0, rows, kDtypeU64, COLL_MAX));
+    // A sampled decode replaces the greedy key with the drawn token's (position of the new token:
+    // the input position + 1), and records the token in the context bitmap.
+    if (m->sampling && seq0 == 0 && rows == 1)
+        L0B_TRY(sample_step(d, m->logits, m->vocab_full, m->seen, m->s_temperature, m->s_top_p, m->s_top_k,
+                            m->s_penalty, m->skeys, 0.0, m->s_seed, m->pos, 1, nullptr, m->keys, m->seen));
     return d->launch(step_finish_kernel, dim3(1), dim3(rows < 32 ? 32 : ((rows + 31) / 32) * 32), 0, m->keys + seq0,
                      m->sampled + seq0, m->tok + seq0, m->pos + seq0, seq0 ? nullptr : m->out_tokens, m->step_idx,
                      rows, advance);
@@ -1020,6 +1035,9 @@ L0B_API l0b_status l0b_model_create(l0b_device* dev, l0b_suite* suite, const l0b
     L0B_TRY(m->alloc(&m->sampled, m->batch_cap));
     L0B_TRY(m->alloc(&m->out_tokens, static_cast<size_t>(max_seq_len + 1) * m->batch_cap));
     L0B_TRY(m->alloc(&m->step_idx, 1));
+    L0B_TRY(m->alloc(&m->seen, sample_seen_words(m->vocab_full)));
+    L0B_TRY(m->alloc(&m->skeys, sample_keys_words(m->vocab_full)));  // zeroed: the max word starts at 0
+    L0B_TRY(m->alloc(&m->ctx_ids, static_cast<size_t>(max_seq_len) + 1));
     L0B_TRY(m->alloc(&m->keys, m->batch_cap));
     L0B_CHECK_CUDA(cudaMallocHost(&m->host_io, sizeof(int) * 2 * m->batch_cap));
     if (m->tp > 1) L0B_TRY(m->alloc(&m->logits_all, static_cast<size_t>(m->tp) * m->batch_cap * m->vocab));
@@ -1235,6 +1253,62 @@ L0B_API l0b_status l0b_model_generate_greedy(l0b_model* m, const int32_t* ids, i
     }
     *out_count = n;
     return L0B_OK;
+    GUARD_END
+}
+
+// Samples the token after the last processed position from the last step's logits on the device (no
+// logits readback), as LevelZeroLlmEngine.PickToken -> LlmSampler.Sample does on the host
+// (src/HFLabs.ML.LLM.LevelZero/LevelZeroLlmEngine.cs:292-310), and makes it the next input token. The
+// repetition context (prompt and generated ids) is given here once; later sampled decode steps add
+// their tokens to it on the device.
+L0B_API l0b_status l0b_model_sample_logits(l0b_model* m, float temperature, float top_p, int32_t top_k,
+                                           float repetition_penalty, uint64_t seed, const int32_t* context,
+                                           int32_t n_context, int32_t* token) {
+    GUARD_BEGIN
+    L0B_REQUIRE(m, L0B_ERR_ARGUMENT, "model is null");
+    L0B_REQUIRE(m->tp == 1, L0B_ERR_UNSUPPORTED, "device sampling runs on single-GPU models");
+    L0B_REQUIRE(m->position > 0, L0B_ERR_INVALID_OPERATION, "no logits yet: prefill or decode first");
+    L0B_REQUIRE(n_context >= 0 && n_context <= m->max_seq + 1 && (n_context == 0 || context), L0B_ERR_OUT_OF_RANGE,
+                "context of %d ids (at most %d)", n_context, m->max_seq + 1);
+    L0B_TRY(sample_check(temperature, top_p, top_k, repetition_penalty, m->vocab_full));
+    l0b_device* d = m->dev;
+    L0B_CHECK_CUDA(cudaSetDevice(d->index));
+    if (n_context > 0)
+        L0B_CHECK_CUDA(cudaMemcpyAsync(m->ctx_ids, context, sizeof(int) * n_context, cudaMemcpyHostToDevice, d->stream));
+    m->host_io[0] = m->position;
+    L0B_CHECK_CUDA(cudaMemcpyAsync(m->pos, &m->host_io[0], sizeof(int), cudaMemcpyHostToDevice, d->stream));
+    L0B_TRY(seen_build(d, m->ctx_ids, n_context, m->vocab_full, m->seen));
+    L0B_TRY(sample_step(d, m->logits, m->vocab_full, m->seen, temperature, top_p, top_k, repetition_penalty, m->skeys,
+                        0.0, seed, m->pos, 0, m->sampled, nullptr, m->seen));
+    L0B_CHECK_CUDA(cudaMemcpyAsync(m->tok, m->sampled, sizeof(int), cudaMemcpyDeviceToDevice, d->stream));
+    int t = 0;
+    L0B_CHECK_CUDA(cudaMemcpyAsync(&m->host_io[0], m->sampled, sizeof(int), cudaMemcpyDeviceToHost, d->stream));
+    L0B_CHECK_CUDA(cudaStreamSynchronize(d->stream));
+    t = m->host_io[0];
+    if (token) *token = t;
+    return L0B_OK;
+    GUARD_END
+}
+
+// Device-resident sampled decode of sequence 0: `steps` times, decode the pending token and sample the
+// next from its logits with the given parameters (the draw of the token at position p is seeded by
+// (seed, p)); the context bitmap of the last l0b_model_sample_logits call grows with every token.
+L0B_API l0b_status l0b_model_decode_sample_device(l0b_model* m, int32_t steps, float temperature, float top_p,
+                                                  int32_t top_k, float repetition_penalty, uint64_t seed,
+                                                  int32_t* out) {
+    GUARD_BEGIN
+    L0B_REQUIRE(m, L0B_ERR_ARGUMENT, "model is null");
+    L0B_REQUIRE(m->tp == 1, L0B_ERR_UNSUPPORTED, "device sampling runs on single-GPU models");
+    L0B_TRY(sample_check(temperature, top_p, top_k, repetition_penalty, m->vocab_full));
+    m->sampling = true;
+    m->s_temperature = temperature;
+    m->s_top_p = top_p;
+    m->s_top_k = top_k;
+    m->s_penalty = repetition_penalty;
+    m->s_seed = seed;
+    const l0b_status st = l0b_model_decode_greedy_device(m, steps, out);
+    m->sampling = false;
+    return st;
     GUARD_END
 }
 

@@ -452,6 +452,34 @@ L0B_API l0b_status l0b_sampling_execute(l0b_suite* s, l0b_device* d, l0b_buffer*
     return k_sampling(d, F(logits), static_cast<int*>(sampled->ptr), temperature, random_val, vocab);
 }
 
+L0B_API l0b_status l0b_sample_execute(l0b_suite* s, l0b_device* d, l0b_buffer* logits, int32_t vocab,
+                                      l0b_buffer* context, int32_t n_context, float temperature, float top_p,
+                                      int32_t top_k, float repetition_penalty, double random_value,
+                                      l0b_buffer* out_token) {
+    L0B_TRY(check_suite(s, d));
+    L0B_REQUIRE(vocab > 0, L0B_ERR_ARGUMENT, "Logits array cannot be null or empty.");
+    L0B_REQUIRE(random_value >= 0.0 && random_value < 1.0, L0B_ERR_OUT_OF_RANGE, "random value %g outside [0, 1)",
+                random_value);
+    L0B_TRY(need(logits, "logits", L0B_F32, vocab));
+    L0B_TRY(need(out_token, "out_token", L0B_I32, 1));
+    L0B_REQUIRE(n_context >= 0, L0B_ERR_OUT_OF_RANGE, "n_context %d", n_context);
+    if (n_context > 0) L0B_TRY(need(context, "context", L0B_I32, n_context));
+    L0B_TRY(sample_check(temperature, top_p, top_k, repetition_penalty, vocab));
+    const size_t words = sample_seen_words(vocab), kwords = sample_keys_words(vocab);
+    void* scratch = nullptr;
+    L0B_TRY(d->ensure_scratch((kwords + words) * sizeof(uint32_t), &scratch, 0));
+    uint32_t* keys = static_cast<uint32_t*>(scratch);
+    // The max word starts at zero (the scratch may hold anything); the select kernel leaves it zero.
+    L0B_TRY(k_fill_u32(d, keys + vocab, 0u, 1));
+    uint32_t* seen = nullptr;
+    if (n_context > 0 && repetition_penalty != 1.0f) {
+        seen = keys + kwords;
+        L0B_TRY(seen_build(d, static_cast<const int*>(context->ptr), n_context, vocab, seen));
+    }
+    return sample_step(d, F(logits), vocab, seen, temperature, top_p, top_k, repetition_penalty, keys, random_value,
+                       0, nullptr, 0, static_cast<int*>(out_token->ptr), nullptr, nullptr);
+}
+
 L0B_API l0b_status l0b_linear(l0b_suite* s, l0b_device* d, int32_t m, int32_t n, int32_t k, l0b_buffer* x,
                               l0b_buffer* w, l0b_buffer* scales, int32_t group, l0b_buffer* bias, l0b_buffer* y) {
     L0B_TRY(check_suite(s, d));

@@ -77,4 +77,25 @@ size_t attention_part_floats(int batch, int nh, int max_splits, int hd);
 // Picks the split length for a cache of max_seq positions and `work_items` (batch * nKv) rows.
 void attention_pick_split(int max_seq, int work_items, int sm_count, int* chunk, int* max_splits);
 
+// Device sampling (LlmSampler.Sample): validates the parameters (top_k within the select's 1024
+// candidates when T > 0).
+l0b_status sample_check(float temperature, float top_p, int top_k, float penalty, int vocab);
+// p[0..n) = v.
+l0b_status k_fill_u32(l0b_device* d, uint32_t* p, uint32_t v, int n);
+// 32-bit words of a context bitmap over `vocab` tokens.
+size_t sample_seen_words(int vocab);
+// 32-bit words of the key scratch sample_step takes for `vocab` tokens (keys, the max word, which must
+// be zero before the first draw and is left zero, and the normaliser partials).
+size_t sample_keys_words(int vocab);
+// bits = the set of ids[0..n) (one CTA; zeroes the bitmap first).
+l0b_status seen_build(l0b_device* d, const int* ids, int n, int vocab, uint32_t* bits);
+// One draw: keys scratch [vocab]; `seen` (or null) drives the repetition penalty. The draw is `u`, or
+// when pos is given the seeded draw of the token at position *pos + pos_offset: 53 bits of
+// splitmix64(seed ^ ((p + 1) * 0x9E3779B97F4A7C15)) scaled to [0, 1). The token goes to out_token and/or
+// as an argmax key to out_key; seen_update (or null) records it.
+l0b_status sample_step(l0b_device* d, const float* logits, int vocab, const uint32_t* seen, float temperature,
+                       float top_p, int top_k, float penalty, uint32_t* keys, double u, unsigned long long seed,
+                       const int* pos, int pos_offset, int* out_token, unsigned long long* out_key,
+                       uint32_t* seen_update);
+
 }  // namespace l0b

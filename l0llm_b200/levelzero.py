@@ -171,6 +171,9 @@ def load_library() -> C.CDLL:
         "l0b_linear_tc": (i32, [vp, vp, i32, i32, i32, vp, vp, vp, f32, i32, vp, vp]),
         "l0b_linear_tc_scaled": (i32, [vp, vp, i32, i32, i32, vp, vp, vp, i32, vp, f32, i32, vp, vp]),
         "l0b_tc_set_max_splits": (i32, [i32]),
+        "l0b_sample_execute": (i32, [vp, vp, vp, i32, vp, i32, f32, f32, i32, f32, C.c_double, vp]),
+        "l0b_model_sample_logits": (i32, [vp, f32, f32, i32, f32, C.c_uint64, vp, i32, C.POINTER(i32)]),
+        "l0b_model_decode_sample_device": (i32, [vp, i32, f32, f32, i32, f32, C.c_uint64, vp]),
         "l0b_device_error_status": (i32, [vp, C.POINTER(i32)]),
         "l0b_set_gemv_tensor_cores": (i32, [i32]),
         "l0b_comm_unique_id": (i32, [vp, i32]),
@@ -486,6 +489,16 @@ class _Sampling(_Op):
                                           randomVal, vocab))
 
 
+class _Sampler(_Op):
+    """LlmSampler.Sample on the device: the token goes to `out` (i32 [1])."""
+
+    def Execute(self, dev, logits, vocab, context, n_context, temperature, top_p, top_k, repetition_penalty,
+                random_value, out):
+        check(self.L.l0b_sample_execute(self._s(), dev.handle, logits.handle, vocab,
+                                        context.handle if context is not None else None, n_context, temperature,
+                                        top_p, top_k, repetition_penalty, random_value, out.handle))
+
+
 class _CausalConv(_Op):
     def Execute(self, dev, qkv, convState, convW, out, convDim, k, tokens):
         check(self.L.l0b_causal_conv_execute(self._s(), dev.handle, qkv.handle, convState.handle, convW.handle,
@@ -526,6 +539,7 @@ class LlmKernelSuite:
         self.Add = _Unary(self, "l0b_add_execute")
         self.Copy = _Copy(self)
         self.Sampling = _Sampling(self)
+        self.Sampler = _Sampler(self)
         self.CausalConv = _CausalConv(self)
         self.GatedDelta = _GatedDelta(self)
 
@@ -686,6 +700,24 @@ class LlmModel:
     def decode_greedy_device(self, steps: int) -> np.ndarray:
         out = np.zeros(max(1, steps), np.int32)
         check(load_library().l0b_model_decode_greedy_device(self.handle, steps, _p(out)))
+        return out[:steps]
+
+    # Device sampling (LlmSampler.Sample on the GPU; no logits readback).
+    def sample_logits(self, temperature: float, top_p: float, top_k: int, repetition_penalty: float, seed: int,
+                      context) -> int:
+        """Samples the next token from the last step's logits; it becomes the next input token."""
+        ctx = np.ascontiguousarray(context if context is not None else [], np.int32)
+        tok = C.c_int32()
+        check(load_library().l0b_model_sample_logits(self.handle, temperature, top_p, top_k, repetition_penalty,
+                                                     seed, _p(ctx) if ctx.size else None, ctx.size, C.byref(tok)))
+        return tok.value
+
+    def decode_sample_device(self, steps: int, temperature: float, top_p: float, top_k: int,
+                             repetition_penalty: float, seed: int) -> np.ndarray:
+        """`steps` device-resident decode steps, each sampling the next token (draws seeded by position)."""
+        out = np.zeros(max(1, steps), np.int32)
+        check(load_library().l0b_model_decode_sample_device(self.handle, steps, temperature, top_p, top_k,
+                                                            repetition_penalty, seed, _p(out)))
         return out[:steps]
 
     # Batched sequences (cfg.max_batch > 1): sequence `seq` owns KV-cache row seq.

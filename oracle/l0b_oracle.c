@@ -371,6 +371,95 @@ int orc_sample(const float* logits, int vocab, float temperature, float random_v
     return vocab - 1;
 }
 
+typedef struct {
+    double p;
+    int idx;
+} orc_prob;
+
+/* Descending probability, then ascending index. */
+static int orc_prob_cmp(const void* a, const void* b) {
+    const orc_prob* x = (const orc_prob*)a;
+    const orc_prob* y = (const orc_prob*)b;
+    if (x->p > y->p) return -1;
+    if (x->p < y->p) return 1;
+    return x->idx < y->idx ? -1 : (x->idx > y->idx ? 1 : 0);
+}
+
+int orc_sampler(const float* logits, int vocab, const int* ctx, int n_ctx, float temperature, float top_p, int top_k,
+                float repetition_penalty, double u) {
+    if (!logits || vocab <= 0) return -1;
+    float* c = (float*)malloc(sizeof(float) * (size_t)vocab);
+    memcpy(c, logits, sizeof(float) * (size_t)vocab);
+    /* 1. Repetition penalty, once per distinct context id (LlmAbstractions.cs:60-78). */
+    if (repetition_penalty != 1.0f && ctx && n_ctx > 0) {
+        unsigned char* done = (unsigned char*)calloc((size_t)vocab, 1);
+        for (int i = 0; i < n_ctx; ++i) {
+            const int t = ctx[i];
+            if (t < 0 || t >= vocab || done[t]) continue;
+            done[t] = 1;
+            const float l = c[t];
+            c[t] = l >= 0.0f ? l / repetition_penalty : l * repetition_penalty;
+        }
+        free(done);
+    }
+    /* 2. Greedy when T <= 0 (:81-94). */
+    if (temperature <= 0.0f) {
+        int best = 0;
+        for (int i = 1; i < vocab; ++i)
+            if (c[i] > c[best]) best = i;
+        free(c);
+        return best;
+    }
+    /* 3-4. Temperature, softmax in double (:97-113). */
+    for (int i = 0; i < vocab; ++i) c[i] /= temperature;
+    float mx = c[0];
+    for (int i = 1; i < vocab; ++i)
+        if (c[i] > mx) mx = c[i];
+    orc_prob* pr = (orc_prob*)malloc(sizeof(orc_prob) * (size_t)vocab);
+    double sum = 0.0;
+    for (int i = 0; i < vocab; ++i) {
+        const float d = c[i] - mx;
+        pr[i].p = exp((double)d);
+        pr[i].idx = i;
+        sum += pr[i].p;
+    }
+    for (int i = 0; i < vocab; ++i) pr[i].p /= sum;
+    /* 5. Sort, top-k, top-p (:116-146). */
+    qsort(pr, (size_t)vocab, sizeof(orc_prob), orc_prob_cmp);
+    int count = vocab;
+    if (top_k > 0 && top_k < count) count = top_k;
+    if (top_p > 0.0f && top_p < 1.0f) {
+        double cum = 0.0;
+        int keep = 0;
+        for (int i = 0; i < count; ++i) {
+            cum += pr[i].p;
+            ++keep;
+            if (cum >= (double)top_p) break;
+        }
+        if (keep < count) count = keep;
+    }
+    /* 6. Inverse CDF over the kept mass (:148-164). */
+    double kept = 0.0;
+    for (int i = 0; i < count; ++i) kept += pr[i].p;
+    int chosen = pr[count - 1].idx;
+    if (kept <= 0.0) {
+        chosen = pr[0].idx;
+    } else {
+        const double r = u * kept;
+        double cur = 0.0;
+        for (int i = 0; i < count; ++i) {
+            cur += pr[i].p;
+            if (r <= cur) {
+                chosen = pr[i].idx;
+                break;
+            }
+        }
+    }
+    free(pr);
+    free(c);
+    return chosen;
+}
+
 /* ------------------------------------------------------------------------------------------------ */
 /* Synthetic tensors (restates synth_kernel of the CUDA model)                                        */
 /* ------------------------------------------------------------------------------------------------ */
@@ -383,6 +472,11 @@ static uint64_t splitmix64(uint64_t x) {
 }
 
 uint64_t orc_tensor_stream(uint64_t seed, uint64_t id) { return splitmix64(seed ^ (id * 0x9E3779B97F4A7C15ULL)); }
+
+double orc_sample_uniform(uint64_t seed, int p) {
+    const uint64_t h = splitmix64(seed ^ ((uint64_t)(p + 1) * 0x9E3779B97F4A7C15ULL));
+    return (double)(h >> 11) * (1.0 / 9007199254740992.0);
+}
 
 void orc_synth_fill(void* dst, int dtype, int64_t count, uint64_t stream, int mode, float a, float b, int64_t row_len,
                     int64_t full_len, int64_t row0, int64_t col0) {

@@ -70,6 +70,15 @@ void orc_attention(const float* q, const void* kc, const void* vc, int cache_dty
 /* Sampling.Execute (L/LlmModel.cs:398): argmax (first maximum) or inverse-CDF sample. */
 int orc_argmax(const float* x, int n);
 int orc_sample(const float* logits, int vocab, float temperature, float random_val);
+/* LlmSampler.Sample (src/HFLabs.ML.LLM.LevelZero/LlmAbstractions.cs:40-165) with its random draw passed
+ * in (u = Random.NextDouble()): repetition penalty on the distinct ids of ctx, greedy argmax when T <= 0,
+ * logits / T, softmax in double, descending sort (ties: lower index first; the reference's List.Sort is
+ * unstable), top-k, top-p (shortest prefix reaching top_p), inverse CDF of the kept mass at u * mass. */
+int orc_sampler(const float* logits, int vocab, const int* ctx, int n_ctx, float temperature, float top_p, int top_k,
+                float repetition_penalty, double u);
+/* The seeded draw the device sampled decode uses for the token at position p: 53 bits of
+ * splitmix64(seed ^ ((p + 1) * 0x9E3779B97F4A7C15)) scaled to [0, 1). */
+double orc_sample_uniform(uint64_t seed, int p);
 
 /* Seeded synthetic tensors: restates the generator of the CUDA model (splitmix64 hashing, exactly
  * rounded float steps), so both sides hold identical weights. */

@@ -80,6 +80,10 @@ def lib() -> C.CDLL:
     L.orc_argmax.argtypes = [_f32p, C.c_int]
     L.orc_sample.restype = C.c_int
     L.orc_sample.argtypes = [_f32p, C.c_int, C.c_float, C.c_float]
+    L.orc_sampler.restype = C.c_int
+    L.orc_sampler.argtypes = [_f32p, C.c_int, vp, C.c_int, C.c_float, C.c_float, C.c_int, C.c_float, C.c_double]
+    L.orc_sample_uniform.restype = C.c_double
+    L.orc_sample_uniform.argtypes = [C.c_uint64, C.c_int]
     L.orc_tensor_stream.restype = C.c_uint64
     L.orc_tensor_stream.argtypes = [C.c_uint64, C.c_uint64]
     L.orc_synth_fill.argtypes = [vp, C.c_int, C.c_int64, C.c_uint64, C.c_int, C.c_float, C.c_float, C.c_int64,
@@ -114,6 +118,18 @@ def f16_bits(x: np.ndarray) -> np.ndarray:
     x = np.ascontiguousarray(x, np.float32).ravel()
     L = lib()
     return np.array([L.orc_f32_to_f16(float(v)) for v in x], np.uint16)
+
+
+def sampler(logits: np.ndarray, ctx, temperature: float, top_p: float, top_k: int, penalty: float, u: float) -> int:
+    """LlmSampler.Sample (src/HFLabs.ML.LLM.LevelZero/LlmAbstractions.cs:40-165) with the draw u given."""
+    lg = np.ascontiguousarray(logits, np.float32)
+    c = None if ctx is None or len(ctx) == 0 else np.ascontiguousarray(ctx, np.int32)
+    return lib().orc_sampler(lg, lg.size, _ptr(c), 0 if c is None else c.size, temperature, top_p, top_k, penalty, u)
+
+
+def sample_uniform(seed: int, p: int) -> float:
+    """The device sampled decode's draw for the token at position p."""
+    return lib().orc_sample_uniform(seed, p)
 
 
 def gemv_out_in(x: np.ndarray, w: np.ndarray, wdtype: int, scales: np.ndarray | None = None,
