@@ -976,6 +976,396 @@ l0b_status launch_on(l0b_device* dev, cudaStream_t stream, F kernel, dim3 g, dim
     return L0B_OK;
 }
 
+// ---------------------------------------------------------------------------------------------
+// Bulk-streamed tensor-core GEMV for one activation row (decode at batch 1).
+//
+// The weights of a tile (16 rows; SwiGLU: 8 gate + their 8 up rows) are streamed as 512-byte segments of
+// each row (8 pieces of 64 bytes) by one-dimensional bulk copies (cp.async.bulk, completing on an
+// mbarrier) into a 12-stage shared-memory ring: every copy is one contiguous run of a row, so the HBM
+// serves long runs, and ~100 KB per SM stay in flight (a read-only probe of this pattern measured
+// 7.1-7.3 TB/s on B200, against ~5.5 TB/s for register loads of 256-byte runs). Rows sit 576 bytes apart
+// in a stage (an odd multiple of 64 modulo 128), so the 16-byte fragment reads of the two rows served in
+// one shared-memory phase fall in disjoint banks. A producer warp issues
+// the copies (before the dependency wait: weights never depend on the previous kernel); eight consumer
+// warps stage the hi/lo activations once (as the kernel above) and then take one piece each per stage,
+// with the same k permutation, int8 conversion and mma.sync as above.
+//
+// Work is split stream-K: the (tile, segment) units are cut into equal contiguous ranges, one per CTA
+// (one CTA per SM), so every SM streams the same number of bytes whatever the tile count. A CTA that
+// holds a whole tile runs its epilogue; a tile shared by CTAs has each contributor write its partial to
+// a per-CTA slot, and the last to arrive (an atomic counter per tile, no waiting) sums the contributors'
+// partials in CTA order (deterministic) and runs the epilogue. Each tile's counter is left at zero.
+// ---------------------------------------------------------------------------------------------
+constexpr int kBulkPieces = 8;                      // 64-byte pieces per segment: one per consumer warp
+constexpr int kBulkStride = kBulkPieces * 64 + 64;  // row stride inside a stage: rows 2j, 2j+1 64 bytes apart
+constexpr int kBulkStageBytes = 16 * kBulkStride;
+constexpr int kBulkStages = 12;
+constexpr int kBulkThreads = kThreads + 32;         // 8 consumer warps + 1 producer warp
+constexpr int kBulkMaxCtas = 1024;
+constexpr int kBulkMaxTiles = 1 << 16;
+constexpr long long kBulkWaitCycles = 4000000000LL;
+
+__device__ float g_bulk_part[kBulkMaxCtas][2][16];  // split tiles: each CTA's first / last tile partial
+__device__ unsigned g_bulk_count[kBulkMaxTiles];    // per-tile arrivals, zero at rest
+
+__device__ __forceinline__ uint32_t bulk_smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// Bounded mbarrier wait (~2 s): false on timeout.
+__device__ __forceinline__ bool bulk_wait(uint64_t* bar, uint32_t parity) {
+    const long long t0 = clock64();
+    while (true) {
+        uint32_t done;
+        asm volatile(
+            "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+            : "=r"(done)
+            : "r"(bulk_smem_u32(bar)), "r"(parity)
+            : "memory");
+        if (done) return true;
+        if (clock64() - t0 > kBulkWaitCycles) return false;
+    }
+}
+
+__device__ __forceinline__ void bulk_consumer_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kThreads) : "memory"); }
+
+template <typename WT>
+__global__ void __launch_bounds__(kBulkThreads, 1) gemv_bulk_kernel(const GemvParams p, int* error) {
+    extern __shared__ __align__(1024) char bulk_smem[];
+    constexpr bool kI8 = sizeof(WT) == 1;
+    constexpr bool kBF = DT<WT>::id == L0B_BF16;
+    constexpr int PE = MmaPiece<WT>::kK;  // k per 64-byte piece
+    constexpr int KU = MmaPiece<WT>::kUnits;
+    constexpr int C2 = 2;                 // B columns: hi, lo of the one activation row
+    __shared__ float2 red[kWarps][32];
+    __shared__ float ssq_s[kWarps], amax_s[kWarps];
+    __shared__ float oscale_s;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+    const int N = p.N, K = p.K;
+    const bool swiglu = p.epi == EPI_SWIGLU;
+    const int half_n = N >> 1;
+    const int npieces = K / PE;
+    const int nseg = (npieces + kBulkPieces - 1) / kBulkPieces;
+    const int ntiles = swiglu ? (half_n + 7) / 8 : (N + 15) / 16;
+    const long long U = static_cast<long long>(ntiles) * nseg;
+    const int G = gridDim.x;
+    const long long u_begin = U * blockIdx.x / G, u_end = U * (blockIdx.x + 1) / G;
+    const size_t xs_bytes = (static_cast<size_t>(npieces) * KU * C2 * 64 + 1023) & ~static_cast<size_t>(1023);
+    char* xs = bulk_smem;
+    char* stages = bulk_smem + xs_bytes;
+    uint64_t* full = reinterpret_cast<uint64_t*>(stages + kBulkStages * kBulkStageBytes);
+    uint64_t* empty = full + kBulkStages;
+    const char* W = static_cast<const char*>(p.w);
+    const long long row_bytes = static_cast<long long>(K) * sizeof(WT);
+
+    // Weight row rr (0..15) of a tile: rows g / g + 8 of the MMA.
+    auto tile_row = [&](int tile, int rr, bool& valid) {
+        if (swiglu) {
+            const int r = tile * 8 + (rr & 7);
+            valid = r < half_n;
+            return rr < 8 ? r : r + half_n;
+        }
+        const int r = tile * 16 + rr;
+        valid = r < N;
+        return r;
+    };
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kBulkStages; ++s) {
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(bulk_smem_u32(&full[s])) : "memory");
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bulk_smem_u32(&empty[s])), "r"(kWarps)
+                         : "memory");
+        }
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncthreads();
+
+    if (warp == kWarps) {
+        // Producer: one lane issues every row's copy of every unit in this CTA's range.
+        if (lane == 0) {
+            long long i = 0;
+            for (long long u = u_begin; u < u_end; ++u, ++i) {
+                const int s = static_cast<int>(i % kBulkStages);
+                const uint32_t ph = static_cast<uint32_t>((i / kBulkStages) & 1);
+                if (i >= kBulkStages && !bulk_wait(&empty[s], ph ^ 1)) {
+                    atomicExch(error, 1);
+                    break;
+                }
+                const int tile = static_cast<int>(u / nseg), seg = static_cast<int>(u % nseg);
+                const int pc0 = seg * kBulkPieces;
+                const int npc = min(kBulkPieces, npieces - pc0);
+                const uint32_t bytes = static_cast<uint32_t>(npc) * 64;
+                uint32_t total = 0;
+#pragma unroll 1
+                for (int rr = 0; rr < 16; ++rr) {
+                    bool v;
+                    tile_row(tile, rr, v);
+                    total += v ? bytes : 0;
+                }
+                asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bulk_smem_u32(&full[s])),
+                             "r"(total)
+                             : "memory");
+                char* dst = stages + s * kBulkStageBytes;
+#pragma unroll 1
+                for (int rr = 0; rr < 16; ++rr) {
+                    bool v;
+                    const int row = tile_row(tile, rr, v);
+                    if (!v) continue;
+                    asm volatile(
+                        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                            bulk_smem_u32(dst + rr * kBulkStride)),
+                        "l"(W + static_cast<long long>(row) * row_bytes + static_cast<long long>(pc0) * 64), "r"(bytes),
+                        "r"(bulk_smem_u32(&full[s]))
+                        : "memory");
+                }
+            }
+        }
+        return;
+    }
+
+    // Consumers.
+    pdl_wait();
+    pdl_launch_dependents();
+    // Stage x as hi / lo pairs in the piece order of the kernel above (one row: 32-k unit u, quad lane t).
+    {
+        const int items = npieces * KU * 4;
+        const float* xf = static_cast<const float*>(p.x);
+        const bool xvec = p.x_dtype == L0B_F32 && (reinterpret_cast<uintptr_t>(p.x) & 15) == 0;
+        auto item_slot = [&](int it, int& k) {
+            const int u = it >> 2, tt = it & 3;
+            k = kI8 ? (u >> 1) * 64 + 16 * tt + 8 * (u & 1) : 32 * u + 8 * tt;
+            return xs + static_cast<size_t>(u) * C2 * 64 + tt * 16;  // lo slot is +64
+        };
+        float ss = 0.f, amax = 0.f;
+        for (int it = threadIdx.x; it < items; it += kThreads) {
+            int k;
+            char* slot = item_slot(it, k);
+            float v[8];
+            if (xvec) {
+                const float4 a = *reinterpret_cast<const float4*>(xf + k);
+                const float4 c = *reinterpret_cast<const float4*>(xf + k + 4);
+                v[0] = a.x, v[1] = a.y, v[2] = a.z, v[3] = a.w, v[4] = c.x, v[5] = c.y, v[6] = c.z, v[7] = c.w;
+            } else {
+#pragma unroll
+                for (int e = 0; e < 8; ++e) v[e] = load_as_float(p.x, p.x_dtype, k + e);
+            }
+            if (p.norm_w) {
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                    ss = fmaf(v[e], v[e], ss);
+                    v[e] *= p.norm_w[k + e];
+                }
+            }
+#pragma unroll
+            for (int e = 0; e < 8; ++e) amax = fmaxf(amax, fabsf(v[e]));
+            *reinterpret_cast<float4*>(slot) = make_float4(v[0], v[1], v[2], v[3]);
+            *reinterpret_cast<float4*>(slot + 64) = make_float4(v[4], v[5], v[6], v[7]);
+        }
+        ss = warp_sum(ss);
+        amax = warp_max(amax);
+        if (lane == 0) {
+            ssq_s[warp] = ss;
+            amax_s[warp] = amax;
+        }
+        bulk_consumer_sync();
+        float sst = 0.f, am = 0.f;
+#pragma unroll
+        for (int w = 0; w < kWarps; ++w) {
+            sst += ssq_s[w];
+            am = fmaxf(am, amax_s[w]);
+        }
+        const float rs = p.norm_w ? 1.0f / sqrtf(sst / static_cast<float>(K) + p.eps) : 1.0f;
+        int e = 0;
+        if (!kBF && am * rs > 0.f && isfinite(am * rs)) {
+            int ex;
+            frexpf(am * rs, &ex);
+            e = min(max(14 - ex, -100), 100);
+        }
+        const float in_scale = rs * ldexpf(1.0f, e);
+        if (threadIdx.x == 0) oscale_s = ldexpf(1.0f, -e);
+        for (int it = threadIdx.x; it < items; it += kThreads) {
+            int k;
+            char* slot = item_slot(it, k);
+            const float4 a = *reinterpret_cast<const float4*>(slot);
+            const float4 c = *reinterpret_cast<const float4*>(slot + 64);
+            float v[8] = {a.x * in_scale, a.y * in_scale, a.z * in_scale, a.w * in_scale,
+                          c.x * in_scale, c.y * in_scale, c.z * in_scale, c.w * in_scale};
+            uint4 hi, lo;
+            split_hi_lo<kBF>(v, hi, lo);
+            *reinterpret_cast<uint4*>(slot) = hi;
+            *reinterpret_cast<uint4*>(slot + 64) = lo;
+        }
+        bulk_consumer_sync();
+    }
+
+    // Epilogue of tile `tile` from y = (row g, row g + 8) sums (lanes with t == 0 hold the real ones).
+    auto epilogue = [&](int tile, float y0, float y1) {
+        bool v0, v1;
+        const int r0 = tile_row(tile, g, v0), r1 = tile_row(tile, g + 8, v1);
+        if (kI8) {
+            const __half* sc = static_cast<const __half*>(p.scales);
+            y0 *= v0 ? __half2float(sc[r0]) : 0.f;
+            y1 *= v1 ? __half2float(sc[r1]) : 0.f;
+        }
+        const bool live = t == 0;
+        if (p.epi == EPI_ARGMAX) {
+            unsigned long long key = 0;
+            if (live && v0) key = argmax_key(epilogue_store(p, r0, 0, y0, false), r0 + p.argmax_base);
+            if (live && v1) key = max(key, argmax_key(epilogue_store(p, r1, 0, y1, false), r1 + p.argmax_base));
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) key = max(key, __shfl_xor_sync(0xffffffffu, key, o));
+            if (lane == 0 && key) atomicMax(p.argmax, key);
+        } else if (live) {
+            if (swiglu) {
+                if (v0) epilogue_store(p, r0, 0, silu(y0) * y1);
+            } else {
+                if (v0) epilogue_store(p, r0, 0, y0);
+                if (v1) epilogue_store(p, r1, 0, y1);
+            }
+        }
+    };
+
+    const int first_tile = static_cast<int>(u_begin / nseg);
+    auto cta_of = [&](long long x) { return static_cast<int>(((x + 1) * G + U - 1) / U) - 1; };
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    long long tile_u0 = u_begin;  // first unit of the current tile inside this CTA's range
+    const int col_off = g * 64 + t * 16;
+    long long i = 0;
+    for (long long u = u_begin; u < u_end; ++u, ++i) {
+        const int s = static_cast<int>(i % kBulkStages);
+        const uint32_t ph = static_cast<uint32_t>((i / kBulkStages) & 1);
+        if (!bulk_wait(&full[s], ph)) {
+            if (lane == 0) atomicExch(error, 1);
+        }
+        const int tile = static_cast<int>(u / nseg), seg = static_cast<int>(u % nseg);
+        const int piece = seg * kBulkPieces + warp;
+        if (piece < npieces) {
+            const char* st = stages + s * kBulkStageBytes + warp * 64 + t * 16;
+            const uint4 w0 = *reinterpret_cast<const uint4*>(st + g * kBulkStride);
+            const uint4 w1 = *reinterpret_cast<const uint4*>(st + (g + 8) * kBulkStride);
+            const char* ub = xs + static_cast<size_t>(piece * KU) * C2 * 64 + col_off;
+            uint32_t b[8];
+#pragma unroll
+            for (int j = 0; j < KU; ++j) {
+                uint4 q = make_uint4(0, 0, 0, 0);
+                if (g < C2) q = *reinterpret_cast<const uint4*>(ub + static_cast<size_t>(j) * C2 * 64);
+                b[4 * j] = q.x, b[4 * j + 1] = q.y, b[4 * j + 2] = q.z, b[4 * j + 3] = q.w;
+            }
+            if constexpr (kI8) {
+#pragma unroll
+                for (int jj = 0; jj < 4; ++jj) {
+                    uint32_t a0, a1, a2, a3;
+                    i8x4_to_h2x2(u4_get(w0, jj), a0, a2);
+                    i8x4_to_h2x2(u4_get(w1, jj), a1, a3);
+                    mma_16816(acc, a0, a1, a2, a3, b[2 * jj], b[2 * jj + 1], false);
+                }
+            } else {
+#pragma unroll
+                for (int jj = 0; jj < 2; ++jj) {
+                    const uint32_t a0 = u4_get(w0, 2 * jj), a2 = u4_get(w0, 2 * jj + 1);
+                    const uint32_t a1 = u4_get(w1, 2 * jj), a3 = u4_get(w1, 2 * jj + 1);
+                    mma_16816(acc, a0, a1, a2, a3, b[2 * jj], b[2 * jj + 1], kBF);
+                }
+            }
+        }
+        __syncwarp();
+        if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bulk_smem_u32(&empty[s])) : "memory");
+        if (seg == nseg - 1 || u == u_end - 1) {
+            // This CTA's share of the tile is complete: reduce the warps.
+            red[warp][lane] = make_float2(acc[0] + acc[1], acc[2] + acc[3]);
+            acc[0] = acc[1] = acc[2] = acc[3] = 0.f;
+            bulk_consumer_sync();
+            if (warp == 0) {
+                float y0 = 0.f, y1 = 0.f;
+#pragma unroll
+                for (int w = 0; w < kWarps; ++w) {
+                    y0 += red[w][lane].x;
+                    y1 += red[w][lane].y;
+                }
+                y0 *= oscale_s;
+                y1 *= oscale_s;
+                const long long t0u = static_cast<long long>(tile) * nseg;
+                if (tile_u0 == t0u && seg == nseg - 1) {
+                    epilogue(tile, y0, y1);
+                } else {
+                    // Shared tile: this CTA's partial (rows g, g + 8 from the lanes with t == 0).
+                    const int slot = tile == first_tile ? 0 : 1;
+                    if (t == 0) {
+                        g_bulk_part[blockIdx.x][slot][g] = y0;
+                        g_bulk_part[blockIdx.x][slot][g + 8] = y1;
+                    }
+                    __threadfence();
+                    __syncwarp();
+                    const int c0 = cta_of(t0u), c1 = cta_of(t0u + nseg - 1);
+                    unsigned prev = 0;
+                    if (lane == 0) {
+                        prev = atomicAdd(&g_bulk_count[tile], 1u);
+                        if (prev == static_cast<unsigned>(c1 - c0)) g_bulk_count[tile] = 0u;
+                    }
+                    prev = __shfl_sync(0xffffffffu, prev, 0);
+                    if (prev == static_cast<unsigned>(c1 - c0)) {
+                        __threadfence();
+                        float s0 = 0.f, s1 = 0.f;
+                        for (int c = c0; c <= c1; ++c) {
+                            const long long cb = U * c / G;
+                            const int cs = static_cast<int>(cb / nseg) == tile ? 0 : 1;
+                            s0 += __ldcg(&g_bulk_part[c][cs][g]);
+                            s1 += __ldcg(&g_bulk_part[c][cs][g + 8]);
+                        }
+                        epilogue(tile, s0, s1);
+                    }
+                }
+            }
+            bulk_consumer_sync();
+            tile_u0 = u + 1;
+        }
+    }
+}
+
+template <typename WT>
+size_t bulk_smem_bytes(int K) {
+    const int npieces = K / MmaPiece<WT>::kK;
+    const size_t xs = (static_cast<size_t>(npieces) * MmaPiece<WT>::kUnits * 2 * 64 + 1023) & ~static_cast<size_t>(1023);
+    return 1024 + xs + static_cast<size_t>(kBulkStages) * kBulkStageBytes + 2 * kBulkStages * 8;
+}
+
+// One activation row, 16-byte aligned rows of whole pieces, int8 with one scale per row; shared memory
+// for the staged activations (4 K bytes) and the ring within one CTA per SM.
+template <typename WT>
+bool bulk_applies(const GemvParams& p) {
+    if constexpr (sizeof(WT) > 2) {
+        return false;
+    } else {
+        if (!g_gemv_mma || p.M != 1 || p.nseg < 1 || p.K % MmaPiece<WT>::kK != 0) return false;
+        if (reinterpret_cast<uintptr_t>(p.w) % 16 != 0 || (p.x_dtype == L0B_F32 && (reinterpret_cast<uintptr_t>(p.x) & 15)))
+            return false;
+        if (sizeof(WT) == 1 && p.group < p.K) return false;
+        if (p.norm_w && (reinterpret_cast<uintptr_t>(p.norm_w) & 15)) return false;
+        const int ntiles = p.epi == EPI_SWIGLU ? (p.N / 2 + 7) / 8 : (p.N + 15) / 16;
+        if (ntiles > kBulkMaxTiles) return false;
+        return bulk_smem_bytes<WT>(p.K) <= 220 * 1024;
+    }
+}
+
+template <typename WT>
+l0b_status launch_bulk(l0b_device* dev, cudaStream_t stream, int sm_count, const GemvParams& p) {
+    auto kernel = gemv_bulk_kernel<WT>;
+    static bool configured = false;
+    if (!configured) {
+        cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
+        if (e != cudaSuccess) return fail(L0B_ERR_CUDA, "cudaFuncSetAttribute failed: %s", cudaGetErrorString(e));
+        configured = true;
+    }
+    const size_t smem = bulk_smem_bytes<WT>(p.K);
+    const int npieces = p.K / MmaPiece<WT>::kK;
+    const long long U = static_cast<long long>(p.epi == EPI_SWIGLU ? (p.N / 2 + 7) / 8 : (p.N + 15) / 16) *
+                        ((npieces + kBulkPieces - 1) / kBulkPieces);
+    int grid = sm_count < kBulkMaxCtas ? sm_count : kBulkMaxCtas;
+    if (U < grid) grid = static_cast<int>(U);
+    int* err = dev ? dev->error_flag : nullptr;
+    return launch_on(dev, stream, kernel, dim3(grid), dim3(kBulkThreads), smem, p, err);
+}
+
 // Resident CTAs per SM for (kernel, dynamic smem), cached: the persistent grid is SMs x this.
 int resident_ctas(const void* func, size_t smem) {
     struct Entry {
@@ -1087,6 +1477,9 @@ l0b_status launch_typed(l0b_device* dev, cudaStream_t stream, int sm_count, Gemv
     const bool vec_ok = (p.K % VEC == 0) && (reinterpret_cast<uintptr_t>(p.w) % 16 == 0) &&
                         (sizeof(WT) != 1 || (p.group % 16 == 0 && p.K % p.group == 0));
     const int M = p.M;
+    if constexpr (sizeof(WT) <= 2) {
+        if (bulk_applies<WT>(p)) return launch_bulk<WT>(dev, stream, sm_count, p);
+    }
     for (int m0 = 0; m0 < M;) {
         GemvParams q = p;
         // Passes of up to 8 rows. (Sixteen-row passes on four B-column groups fit shared memory only
