@@ -1088,7 +1088,7 @@ __global__ void __launch_bounds__(kBulkThreads, 1) gemv_bulk_kernel(const GemvPa
                 const int s = static_cast<int>(i % kBulkStages);
                 const uint32_t ph = static_cast<uint32_t>((i / kBulkStages) & 1);
                 if (i >= kBulkStages && !bulk_wait(&empty[s], ph ^ 1)) {
-                    atomicExch(error, 1);
+                    if (error) atomicExch(error, 1);
                     break;
                 }
                 const int tile = static_cast<int>(u / nseg), seg = static_cast<int>(u % nseg);
@@ -1235,7 +1235,7 @@ __global__ void __launch_bounds__(kBulkThreads, 1) gemv_bulk_kernel(const GemvPa
         const int s = static_cast<int>(i % kBulkStages);
         const uint32_t ph = static_cast<uint32_t>((i / kBulkStages) & 1);
         if (!bulk_wait(&full[s], ph)) {
-            if (lane == 0) atomicExch(error, 1);
+            if (lane == 0 && error) atomicExch(error, 1);
         }
         const int tile = static_cast<int>(u / nseg), seg = static_cast<int>(u % nseg);
         const int piece = seg * kBulkPieces + warp;
