@@ -18,8 +18,10 @@
 // first D steps are issued before griddepcontrol.wait -- weights never depend on the previous kernel
 // -- so under programmatic dependent launch the weight stream starts while the producer of x drains.
 #include <cooperative_groups.h>
+#include <cstring>
 
 #include "common.cuh"
+#include "gemm_tc.cuh"
 #include "gemv.cuh"
 
 namespace l0b {
@@ -965,6 +967,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_mma_kernel(const GemvParams 
 }
 
 bool g_gemv_mma = true;
+bool g_gemv_bulk = false;  // the TMA-streamed one-row kernel (l0b_set_gemv_bulk)
 
 template <typename F, typename... A>
 l0b_status launch_on(l0b_device* dev, cudaStream_t stream, F kernel, dim3 g, dim3 b, size_t smem, A... args) {
@@ -980,12 +983,12 @@ l0b_status launch_on(l0b_device* dev, cudaStream_t stream, F kernel, dim3 g, dim
 // Bulk-streamed tensor-core GEMV for one activation row (decode at batch 1).
 //
 // The weights of a tile (16 rows; SwiGLU: 8 gate + their 8 up rows) are streamed as 512-byte segments of
-// each row (8 pieces of 64 bytes) by one-dimensional bulk copies (cp.async.bulk, completing on an
-// mbarrier) into a 12-stage shared-memory ring: every copy is one contiguous run of a row, so the HBM
-// serves long runs, and ~100 KB per SM stay in flight (a read-only probe of this pattern measured
-// 7.1-7.3 TB/s on B200, against ~5.5 TB/s for register loads of 256-byte runs). Rows sit 576 bytes apart
-// in a stage (an odd multiple of 64 modulo 128), so the 16-byte fragment reads of the two rows served in
-// one shared-memory phase fall in disjoint banks. A producer warp issues
+// each row (8 pieces of 64 bytes): one TMA per stage (a 3-D tensor map of 128-byte chunks, box 16 rows x
+// 4 chunks, 128-byte swizzle) brings the 8 KB block into a 14-stage shared-memory ring, ~112 KB per SM in
+// flight. (One 1-D bulk copy per row and segment moved the same bytes at under 0.6 TB/s: the copy engine's
+// cost per operation, not bytes, set the rate; a single 8 KB operation per stage does not pay it 16
+// times.) The swizzle puts the 16-byte fragment reads of the two rows served in one shared-memory phase
+// in disjoint banks. A producer warp issues
 // the copies (before the dependency wait: weights never depend on the previous kernel); eight consumer
 // warps stage the hi/lo activations once (as the kernel above) and then take one piece each per stage,
 // with the same k permutation, int8 conversion and mma.sync as above.
@@ -997,9 +1000,9 @@ l0b_status launch_on(l0b_device* dev, cudaStream_t stream, F kernel, dim3 g, dim
 // partials in CTA order (deterministic) and runs the epilogue. Each tile's counter is left at zero.
 // ---------------------------------------------------------------------------------------------
 constexpr int kBulkPieces = 8;                      // 64-byte pieces per segment: one per consumer warp
-constexpr int kBulkStride = kBulkPieces * 64 + 64;  // row stride inside a stage: rows 2j, 2j+1 64 bytes apart
-constexpr int kBulkStageBytes = 16 * kBulkStride;
-constexpr int kBulkStages = 12;
+constexpr int kBulkChunks = kBulkPieces / 2;        // 128-byte chunks per row per stage
+constexpr int kBulkStageBytes = 16 * kBulkPieces * 64;
+constexpr int kBulkStages = 14;
 constexpr int kBulkThreads = kThreads + 32;         // 8 consumer warps + 1 producer warp
 constexpr int kBulkMaxCtas = 1024;
 constexpr int kBulkMaxTiles = 1 << 16;
@@ -1029,8 +1032,16 @@ __device__ __forceinline__ bool bulk_wait(uint64_t* bar, uint32_t parity) {
 
 __device__ __forceinline__ void bulk_consumer_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kThreads) : "memory"); }
 
+struct BulkArgs {
+    CUtensorMap wmap;  // rows x 128-byte chunks, box (SwiGLU: 8, else 16) rows x kBulkChunks chunks
+    GemvParams p;
+    int* error;
+};
+
 template <typename WT>
-__global__ void __launch_bounds__(kBulkThreads, 1) gemv_bulk_kernel(const GemvParams p, int* error) {
+__global__ void __launch_bounds__(kBulkThreads, 1) gemv_bulk_kernel(const __grid_constant__ BulkArgs ba) {
+    const GemvParams& p = ba.p;
+    int* error = ba.error;
     extern __shared__ __align__(1024) char bulk_smem[];
     constexpr bool kI8 = sizeof(WT) == 1;
     constexpr bool kBF = DT<WT>::id == L0B_BF16;
@@ -1051,12 +1062,12 @@ __global__ void __launch_bounds__(kBulkThreads, 1) gemv_bulk_kernel(const GemvPa
     const int G = gridDim.x;
     const long long u_begin = U * blockIdx.x / G, u_end = U * (blockIdx.x + 1) / G;
     const size_t xs_bytes = (static_cast<size_t>(npieces) * KU * C2 * 64 + 1023) & ~static_cast<size_t>(1023);
-    char* xs = bulk_smem;
-    char* stages = bulk_smem + xs_bytes;
+    // 1024-byte aligned base: the swizzled stages need it (the size includes the slack).
+    char* const base = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(bulk_smem) + 1023) & ~uintptr_t(1023));
+    char* xs = base;
+    char* stages = base + xs_bytes;
     uint64_t* full = reinterpret_cast<uint64_t*>(stages + kBulkStages * kBulkStageBytes);
     uint64_t* empty = full + kBulkStages;
-    const char* W = static_cast<const char*>(p.w);
-    const long long row_bytes = static_cast<long long>(K) * sizeof(WT);
 
     // Weight row rr (0..15) of a tile: rows g / g + 8 of the MMA.
     auto tile_row = [&](int tile, int rr, bool& valid) {
@@ -1092,30 +1103,26 @@ __global__ void __launch_bounds__(kBulkThreads, 1) gemv_bulk_kernel(const GemvPa
                     break;
                 }
                 const int tile = static_cast<int>(u / nseg), seg = static_cast<int>(u % nseg);
-                const int pc0 = seg * kBulkPieces;
-                const int npc = min(kBulkPieces, npieces - pc0);
-                const uint32_t bytes = static_cast<uint32_t>(npc) * 64;
-                uint32_t total = 0;
-#pragma unroll 1
-                for (int rr = 0; rr < 16; ++rr) {
-                    bool v;
-                    tile_row(tile, rr, v);
-                    total += v ? bytes : 0;
-                }
-                asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bulk_smem_u32(&full[s])),
-                             "r"(total)
+                const uint32_t bar = bulk_smem_u32(&full[s]);
+                asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "n"(kBulkStageBytes)
                              : "memory");
                 char* dst = stages + s * kBulkStageBytes;
-#pragma unroll 1
-                for (int rr = 0; rr < 16; ++rr) {
-                    bool v;
-                    const int row = tile_row(tile, rr, v);
-                    if (!v) continue;
+                const uint64_t map = reinterpret_cast<uint64_t>(&ba.wmap);
+                // Rows past the matrix read as zeros; the chunks past K too.
+                if (swiglu) {
                     asm volatile(
-                        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                            bulk_smem_u32(dst + rr * kBulkStride)),
-                        "l"(W + static_cast<long long>(row) * row_bytes + static_cast<long long>(pc0) * 64), "r"(bytes),
-                        "r"(bulk_smem_u32(&full[s]))
+                        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];" ::
+                            "r"(bulk_smem_u32(dst)), "l"(map), "r"(bar), "r"(0), "r"(seg * kBulkChunks), "r"(tile * 8)
+                        : "memory");
+                    asm volatile(
+                        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];" ::
+                            "r"(bulk_smem_u32(dst + kBulkStageBytes / 2)), "l"(map), "r"(bar), "r"(0),
+                            "r"(seg * kBulkChunks), "r"(half_n + tile * 8)
+                        : "memory");
+                } else {
+                    asm volatile(
+                        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];" ::
+                            "r"(bulk_smem_u32(dst)), "l"(map), "r"(bar), "r"(0), "r"(seg * kBulkChunks), "r"(tile * 16)
                         : "memory");
                 }
             }
@@ -1240,9 +1247,13 @@ __global__ void __launch_bounds__(kBulkThreads, 1) gemv_bulk_kernel(const GemvPa
         const int tile = static_cast<int>(u / nseg), seg = static_cast<int>(u % nseg);
         const int piece = seg * kBulkPieces + warp;
         if (piece < npieces) {
-            const char* st = stages + s * kBulkStageBytes + warp * 64 + t * 16;
-            const uint4 w0 = *reinterpret_cast<const uint4*>(st + g * kBulkStride);
-            const uint4 w1 = *reinterpret_cast<const uint4*>(st + (g + 8) * kBulkStride);
+            // Row r's 16-byte chunk c of piece `warp`: 128-byte line r * 4 + warp / 2, chunk position
+            // ((warp & 1) * 4 + t) XOR (line & 7) (the TMA 128-byte swizzle).
+            const char* st = stages + s * kBulkStageBytes;
+            const int l0 = g * kBulkChunks + (warp >> 1), l1 = (g + 8) * kBulkChunks + (warp >> 1);
+            const int c = (warp & 1) * 4 + t;
+            const uint4 w0 = *reinterpret_cast<const uint4*>(st + l0 * 128 + ((c ^ (l0 & 7)) << 4));
+            const uint4 w1 = *reinterpret_cast<const uint4*>(st + l1 * 128 + ((c ^ (l1 & 7)) << 4));
             const char* ub = xs + static_cast<size_t>(piece * KU) * C2 * 64 + col_off;
             uint32_t b[8];
 #pragma unroll
@@ -1336,7 +1347,8 @@ bool bulk_applies(const GemvParams& p) {
     if constexpr (sizeof(WT) > 2) {
         return false;
     } else {
-        if (!g_gemv_mma || p.M != 1 || p.nseg < 1 || p.K % MmaPiece<WT>::kK != 0) return false;
+        if (!g_gemv_mma || !g_gemv_bulk || p.M != 1 || p.nseg < 1 || p.K % MmaPiece<WT>::kK != 0) return false;
+        if ((static_cast<long long>(p.K) * sizeof(WT)) % 128 != 0) return false;
         if (reinterpret_cast<uintptr_t>(p.w) % 16 != 0 || (p.x_dtype == L0B_F32 && (reinterpret_cast<uintptr_t>(p.x) & 15)))
             return false;
         if (sizeof(WT) == 1 && p.group < p.K) return false;
@@ -1362,8 +1374,13 @@ l0b_status launch_bulk(l0b_device* dev, cudaStream_t stream, int sm_count, const
                         ((npieces + kBulkPieces - 1) / kBulkPieces);
     int grid = sm_count < kBulkMaxCtas ? sm_count : kBulkMaxCtas;
     if (U < grid) grid = static_cast<int>(U);
-    int* err = dev ? dev->error_flag : nullptr;
-    return launch_on(dev, stream, kernel, dim3(grid), dim3(kBulkThreads), smem, p, err);
+    BulkArgs ba;
+    std::memset(&ba, 0, sizeof(ba));
+    L0B_TRY(make_rows_map(&ba.wmap, p.w, p.N, static_cast<long long>(p.K) * sizeof(WT), p.epi == EPI_SWIGLU ? 8 : 16,
+                          kBulkChunks));
+    ba.p = p;
+    ba.error = dev ? dev->error_flag : nullptr;
+    return launch_on(dev, stream, kernel, dim3(grid), dim3(kBulkThreads), smem, ba);
 }
 
 // Resident CTAs per SM for (kernel, dynamic smem), cached: the persistent grid is SMs x this.
@@ -1605,6 +1622,7 @@ __global__ void __launch_bounds__(256) gemm_f32_kernel(int M, int N, int K, cons
 }  // namespace
 
 void gemv_set_tensor_cores(bool on) { g_gemv_mma = on; }
+void gemv_set_bulk(bool on) { g_gemv_bulk = on; }
 
 l0b_status gemv_nk_launch(l0b_device* dev, int w_dtype, GemvParams p) {
     return gemv_dispatch(dev, dev->stream, dev->sm_count, w_dtype, p);

@@ -651,6 +651,11 @@ L0B_API l0b_status l0b_tc_set_max_splits(int32_t splits) {
     return L0B_OK;
 }
 
+L0B_API l0b_status l0b_set_gemv_bulk(int32_t enable) {
+    gemv_set_bulk(enable != 0);
+    return L0B_OK;
+}
+
 L0B_API l0b_status l0b_set_gemv_tensor_cores(int32_t enable) {
     gemv_set_tensor_cores(enable != 0);
     return L0B_OK;

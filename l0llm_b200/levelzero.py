@@ -171,6 +171,7 @@ def load_library() -> C.CDLL:
         "l0b_linear_tc": (i32, [vp, vp, i32, i32, i32, vp, vp, vp, f32, i32, vp, vp]),
         "l0b_linear_tc_scaled": (i32, [vp, vp, i32, i32, i32, vp, vp, vp, i32, vp, f32, i32, vp, vp]),
         "l0b_tc_set_max_splits": (i32, [i32]),
+        "l0b_set_gemv_bulk": (i32, [i32]),
         "l0b_sample_execute": (i32, [vp, vp, vp, i32, vp, i32, f32, f32, i32, f32, C.c_double, vp]),
         "l0b_model_sample_logits": (i32, [vp, f32, f32, i32, f32, C.c_uint64, vp, i32, C.POINTER(i32)]),
         "l0b_model_decode_sample_device": (i32, [vp, i32, f32, f32, i32, f32, C.c_uint64, vp]),
