@@ -16,12 +16,16 @@ import pytest
 pytestmark = pytest.mark.gpu
 
 
-@pytest.fixture(params=["mma", "fma"])
+@pytest.fixture(params=["mma", "fma", "bulk"])
 def path(request, lz):
+    """mma: register-streamed tensor-core GEMV; fma: fp32 FMA; bulk: the TMA-streamed tensor-core GEMV
+    for one activation row (other row counts fall back to mma)."""
     lib = lz.load_library()
-    lib.l0b_set_gemv_tensor_cores(1 if request.param == "mma" else 0)
+    lib.l0b_set_gemv_tensor_cores(0 if request.param == "fma" else 1)
+    lib.l0b_set_gemv_bulk(1 if request.param == "bulk" else 0)
     yield request.param
     lib.l0b_set_gemv_tensor_cores(1)
+    lib.l0b_set_gemv_bulk(0)
 
 
 def _weights(lz, orc, wkind, hf, k):
