@@ -21,7 +21,6 @@
 #include <cstring>
 
 #include "common.cuh"
-#include "gemm_tc.cuh"
 #include "gemv.cuh"
 
 namespace l0b {
@@ -980,36 +979,25 @@ l0b_status launch_on(l0b_device* dev, cudaStream_t stream, F kernel, dim3 g, dim
 }
 
 // ---------------------------------------------------------------------------------------------
-// Bulk-streamed tensor-core GEMV for one activation row (decode at batch 1).
+// Bulk-streamed tensor-core GEMV for one activation row (decode at batch 1), int8 weights.
 //
-// The weights of a tile (16 rows; SwiGLU: 8 gate + their 8 up rows) are streamed as 512-byte segments of
-// each row (8 pieces of 64 bytes): one TMA per stage (a 3-D tensor map of 128-byte chunks, box 16 rows x
-// 4 chunks, 128-byte swizzle) brings the 8 KB block into a 14-stage shared-memory ring, ~112 KB per SM in
-// flight. (One 1-D bulk copy per row and segment moved the same bytes at under 0.6 TB/s: the copy engine's
-// cost per operation, not bytes, set the rate; a single 8 KB operation per stage does not pay it 16
-// times.) The swizzle puts the 16-byte fragment reads of the two rows served in one shared-memory phase
-// in disjoint banks. A producer warp issues
-// the copies (before the dependency wait: weights never depend on the previous kernel); eight consumer
-// warps stage the hi/lo activations once (as the kernel above) and then take one piece each per stage,
-// with the same k permutation, int8 conversion and mma.sync as above.
-//
-// Work is split stream-K: the (tile, segment) units are cut into equal contiguous ranges, one per CTA
-// (one CTA per SM), so every SM streams the same number of bytes whatever the tile count. A CTA that
-// holds a whole tile runs its epilogue; a tile shared by CTAs has each contributor write its partial to
-// a per-CTA slot, and the last to arrive (an atomic counter per tile, no waiting) sums the contributors'
-// partials in CTA order (deterministic) and runs the epilogue. Each tile's counter is left at zero.
+// A tile's 16 weight rows are one contiguous block of HBM (8 gate + 8 up rows for SwiGLU: two blocks),
+// so a whole tile arrives in shared memory with one 1-D bulk copy (cp.async.bulk, completing on an
+// mbarrier) of 16 K bytes (57 KB at K = 3584). Large contiguous copies are what the copy engine streams
+// fastest: a read-only probe of 8-64 KB copies measured 7.1-7.3 TB/s on B200, while copies of 512-byte
+// row segments (one per row) and 3-D tensor-map boxes of 128-byte lines were bound by the engine's cost
+// per operation and per line (0.5 and 2 TB/s). A producer warp keeps 2-3 tiles in flight per SM
+// (issued before the dependency wait: weights never depend on the previous kernel); eight consumer
+// warps stage the hi/lo activations once (as the register-streamed kernel) and split each tile's pieces
+// between them with the same k permutation, int8 conversion and mma.sync. The warps' partial sums meet
+// in double-buffered shared memory; a reducer warp rotating by tile runs the epilogue while the others
+// go on with the next tile. Each CTA (one per SM) takes a contiguous range of whole tiles, so the kernel
+// serves projections with many tiles per SM (gate/up, LM head); the others stay on the register GEMV.
 // ---------------------------------------------------------------------------------------------
-constexpr int kBulkPieces = 8;                      // 64-byte pieces per segment: one per consumer warp
-constexpr int kBulkChunks = kBulkPieces / 2;        // 128-byte chunks per row per stage
-constexpr int kBulkStageBytes = 16 * kBulkPieces * 64;
-constexpr int kBulkStages = 14;
-constexpr int kBulkThreads = kThreads + 32;         // 8 consumer warps + 1 producer warp
-constexpr int kBulkMaxCtas = 1024;
-constexpr int kBulkMaxTiles = 1 << 16;
+constexpr int kBulkThreads = kThreads + 32;  // 8 consumer warps + 1 producer warp
+constexpr int kBulkMaxStages = 4;
+constexpr int kBulkSmemBudget = 220 * 1024;
 constexpr long long kBulkWaitCycles = 4000000000LL;
-
-__device__ float g_bulk_part[kBulkMaxCtas][2][16];  // split tiles: each CTA's first / last tile partial
-__device__ unsigned g_bulk_count[kBulkMaxTiles];    // per-tile arrivals, zero at rest
 
 __device__ __forceinline__ uint32_t bulk_smem_u32(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -1032,23 +1020,28 @@ __device__ __forceinline__ bool bulk_wait(uint64_t* bar, uint32_t parity) {
 
 __device__ __forceinline__ void bulk_consumer_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kThreads) : "memory"); }
 
-struct BulkArgs {
-    CUtensorMap wmap;  // rows x 128-byte chunks, box (SwiGLU: 8, else 16) rows x kBulkChunks chunks
-    GemvParams p;
-    int* error;
-};
+__device__ __forceinline__ void bulk_copy(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     bulk_smem_u32(dst)),
+                 "l"(src), "r"(bytes), "r"(bulk_smem_u32(bar))
+                 : "memory");
+}
 
-template <typename WT>
-__global__ void __launch_bounds__(kBulkThreads, 1) gemv_bulk_kernel(const __grid_constant__ BulkArgs ba) {
-    const GemvParams& p = ba.p;
-    int* error = ba.error;
-    extern __shared__ __align__(1024) char bulk_smem[];
-    constexpr bool kI8 = sizeof(WT) == 1;
-    constexpr bool kBF = DT<WT>::id == L0B_BF16;
-    constexpr int PE = MmaPiece<WT>::kK;  // k per 64-byte piece
-    constexpr int KU = MmaPiece<WT>::kUnits;
-    constexpr int C2 = 2;                 // B columns: hi, lo of the one activation row
-    __shared__ float2 red[kWarps][32];
+// Activations staged as hi/lo pairs (bytes) and the tile ring for K and `stages`.
+__host__ __device__ inline size_t bulk_xs_bytes(int K) { return (static_cast<size_t>(K) * 4 + 1023) & ~static_cast<size_t>(1023); }
+inline size_t bulk_smem_bytes(int K, int stages) {
+    return 1024 + bulk_xs_bytes(K) + static_cast<size_t>(stages) * 16 * K + 2 * kBulkMaxStages * 8;
+}
+inline int bulk_stages(int K) {
+    for (int s = kBulkMaxStages; s >= 2; --s)
+        if (bulk_smem_bytes(K, s) <= static_cast<size_t>(kBulkSmemBudget)) return s;
+    return 0;
+}
+
+__global__ void __launch_bounds__(kBulkThreads, 1) gemv_bulk_kernel(const GemvParams p, int stages, int* error) {
+    extern __shared__ char bulk_smem[];
+    constexpr int PE = 64, KU = 2, C2 = 2;  // int8: 64 k per piece, two 32-k units; B columns hi, lo
+    __shared__ float2 red[2][kWarps][32];
     __shared__ float ssq_s[kWarps], amax_s[kWarps];
     __shared__ float oscale_s;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
@@ -1056,33 +1049,19 @@ __global__ void __launch_bounds__(kBulkThreads, 1) gemv_bulk_kernel(const __grid
     const bool swiglu = p.epi == EPI_SWIGLU;
     const int half_n = N >> 1;
     const int npieces = K / PE;
-    const int nseg = (npieces + kBulkPieces - 1) / kBulkPieces;
     const int ntiles = swiglu ? (half_n + 7) / 8 : (N + 15) / 16;
-    const long long U = static_cast<long long>(ntiles) * nseg;
-    const int G = gridDim.x;
-    const long long u_begin = U * blockIdx.x / G, u_end = U * (blockIdx.x + 1) / G;
-    const size_t xs_bytes = (static_cast<size_t>(npieces) * KU * C2 * 64 + 1023) & ~static_cast<size_t>(1023);
-    // 1024-byte aligned base: the swizzled stages need it (the size includes the slack).
+    const int t_begin = static_cast<int>(static_cast<long long>(ntiles) * blockIdx.x / gridDim.x);
+    const int t_end = static_cast<int>(static_cast<long long>(ntiles) * (blockIdx.x + 1) / gridDim.x);
     char* const base = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(bulk_smem) + 1023) & ~uintptr_t(1023));
     char* xs = base;
-    char* stages = base + xs_bytes;
-    uint64_t* full = reinterpret_cast<uint64_t*>(stages + kBulkStages * kBulkStageBytes);
-    uint64_t* empty = full + kBulkStages;
-
-    // Weight row rr (0..15) of a tile: rows g / g + 8 of the MMA.
-    auto tile_row = [&](int tile, int rr, bool& valid) {
-        if (swiglu) {
-            const int r = tile * 8 + (rr & 7);
-            valid = r < half_n;
-            return rr < 8 ? r : r + half_n;
-        }
-        const int r = tile * 16 + rr;
-        valid = r < N;
-        return r;
-    };
+    char* ring = base + bulk_xs_bytes(K);
+    const size_t stage_bytes = static_cast<size_t>(16) * K;
+    uint64_t* full = reinterpret_cast<uint64_t*>(ring + stages * stage_bytes);
+    uint64_t* empty = full + kBulkMaxStages;
+    const char* W = static_cast<const char*>(p.w);
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < kBulkStages; ++s) {
+        for (int s = 0; s < stages; ++s) {
             asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(bulk_smem_u32(&full[s])) : "memory");
             asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bulk_smem_u32(&empty[s])), "r"(kWarps)
                          : "memory");
@@ -1092,38 +1071,31 @@ __global__ void __launch_bounds__(kBulkThreads, 1) gemv_bulk_kernel(const __grid
     __syncthreads();
 
     if (warp == kWarps) {
-        // Producer: one lane issues every row's copy of every unit in this CTA's range.
+        // Producer: tile i's rows as one (SwiGLU: two) contiguous copies; rows past the matrix are not
+        // copied (their stage bytes are stale and their outputs are never stored).
         if (lane == 0) {
-            long long i = 0;
-            for (long long u = u_begin; u < u_end; ++u, ++i) {
-                const int s = static_cast<int>(i % kBulkStages);
-                const uint32_t ph = static_cast<uint32_t>((i / kBulkStages) & 1);
-                if (i >= kBulkStages && !bulk_wait(&empty[s], ph ^ 1)) {
+            for (int tile = t_begin, i = 0; tile < t_end; ++tile, ++i) {
+                const int s = i % stages;
+                if (i >= stages && !bulk_wait(&empty[s], ((i / stages) & 1) ^ 1)) {
                     if (error) atomicExch(error, 1);
                     break;
                 }
-                const int tile = static_cast<int>(u / nseg), seg = static_cast<int>(u % nseg);
-                const uint32_t bar = bulk_smem_u32(&full[s]);
-                asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "n"(kBulkStageBytes)
-                             : "memory");
-                char* dst = stages + s * kBulkStageBytes;
-                const uint64_t map = reinterpret_cast<uint64_t>(&ba.wmap);
-                // Rows past the matrix read as zeros; the chunks past K too.
+                char* dst = ring + s * stage_bytes;
                 if (swiglu) {
-                    asm volatile(
-                        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];" ::
-                            "r"(bulk_smem_u32(dst)), "l"(map), "r"(bar), "r"(0), "r"(seg * kBulkChunks), "r"(tile * 8)
-                        : "memory");
-                    asm volatile(
-                        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];" ::
-                            "r"(bulk_smem_u32(dst + kBulkStageBytes / 2)), "l"(map), "r"(bar), "r"(0),
-                            "r"(seg * kBulkChunks), "r"(half_n + tile * 8)
-                        : "memory");
+                    const int r0 = tile * 8, nr = min(8, half_n - r0);
+                    const uint32_t bytes = static_cast<uint32_t>(nr) * K;
+                    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bulk_smem_u32(&full[s])),
+                                 "r"(2 * bytes)
+                                 : "memory");
+                    bulk_copy(dst, W + static_cast<long long>(r0) * K, bytes, &full[s]);
+                    bulk_copy(dst + 8 * K, W + static_cast<long long>(half_n + r0) * K, bytes, &full[s]);
                 } else {
-                    asm volatile(
-                        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];" ::
-                            "r"(bulk_smem_u32(dst)), "l"(map), "r"(bar), "r"(0), "r"(seg * kBulkChunks), "r"(tile * 16)
-                        : "memory");
+                    const int r0 = tile * 16, nr = min(16, N - r0);
+                    const uint32_t bytes = static_cast<uint32_t>(nr) * K;
+                    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bulk_smem_u32(&full[s])),
+                                 "r"(bytes)
+                                 : "memory");
+                    bulk_copy(dst, W + static_cast<long long>(r0) * K, bytes, &full[s]);
                 }
             }
         }
@@ -1133,14 +1105,14 @@ __global__ void __launch_bounds__(kBulkThreads, 1) gemv_bulk_kernel(const __grid
     // Consumers.
     pdl_wait();
     pdl_launch_dependents();
-    // Stage x as hi / lo pairs in the piece order of the kernel above (one row: 32-k unit u, quad lane t).
+    // Stage x as hi / lo pairs in the piece order of the register-streamed kernel (32-k unit u, lane t).
     {
         const int items = npieces * KU * 4;
         const float* xf = static_cast<const float*>(p.x);
         const bool xvec = p.x_dtype == L0B_F32 && (reinterpret_cast<uintptr_t>(p.x) & 15) == 0;
         auto item_slot = [&](int it, int& k) {
             const int u = it >> 2, tt = it & 3;
-            k = kI8 ? (u >> 1) * 64 + 16 * tt + 8 * (u & 1) : 32 * u + 8 * tt;
+            k = (u >> 1) * 64 + 16 * tt + 8 * (u & 1);
             return xs + static_cast<size_t>(u) * C2 * 64 + tt * 16;  // lo slot is +64
         };
         float ss = 0.f, amax = 0.f;
@@ -1183,7 +1155,7 @@ __global__ void __launch_bounds__(kBulkThreads, 1) gemv_bulk_kernel(const __grid
         }
         const float rs = p.norm_w ? 1.0f / sqrtf(sst / static_cast<float>(K) + p.eps) : 1.0f;
         int e = 0;
-        if (!kBF && am * rs > 0.f && isfinite(am * rs)) {
+        if (am * rs > 0.f && isfinite(am * rs)) {
             int ex;
             frexpf(am * rs, &ex);
             e = min(max(14 - ex, -100), 100);
@@ -1198,22 +1170,29 @@ __global__ void __launch_bounds__(kBulkThreads, 1) gemv_bulk_kernel(const __grid
             float v[8] = {a.x * in_scale, a.y * in_scale, a.z * in_scale, a.w * in_scale,
                           c.x * in_scale, c.y * in_scale, c.z * in_scale, c.w * in_scale};
             uint4 hi, lo;
-            split_hi_lo<kBF>(v, hi, lo);
+            split_hi_lo<false>(v, hi, lo);
             *reinterpret_cast<uint4*>(slot) = hi;
             *reinterpret_cast<uint4*>(slot + 64) = lo;
         }
         bulk_consumer_sync();
     }
 
-    // Epilogue of tile `tile` from y = (row g, row g + 8) sums (lanes with t == 0 hold the real ones).
-    auto epilogue = [&](int tile, float y0, float y1) {
+    // Epilogue of tile `tile` from the (row g, row g + 8) sums; the lanes with t == 0 hold the real ones.
+    // Rows (g, g + 8) of a tile and their scales; the reducer loads the scales when the tile starts so
+    // the epilogue does not wait for them.
+    auto tile_rows2 = [&](int tile, int& r0, int& r1, bool& v0, bool& v1) {
+        r0 = swiglu ? tile * 8 + g : tile * 16 + g;
+        r1 = swiglu ? r0 + half_n : r0 + 8;
+        v0 = swiglu ? r0 < half_n : r0 < N;
+        v1 = swiglu ? v0 : r1 < N;
+    };
+    const __half* sc = static_cast<const __half*>(p.scales);
+    auto epilogue = [&](int tile, float y0, float y1, float s0, float s1) {
+        int r0, r1;
         bool v0, v1;
-        const int r0 = tile_row(tile, g, v0), r1 = tile_row(tile, g + 8, v1);
-        if (kI8) {
-            const __half* sc = static_cast<const __half*>(p.scales);
-            y0 *= v0 ? __half2float(sc[r0]) : 0.f;
-            y1 *= v1 ? __half2float(sc[r1]) : 0.f;
-        }
+        tile_rows2(tile, r0, r1, v0, v1);
+        y0 *= s0;
+        y1 *= s1;
         const bool live = t == 0;
         if (p.epi == EPI_ARGMAX) {
             unsigned long long key = 0;
@@ -1232,28 +1211,26 @@ __global__ void __launch_bounds__(kBulkThreads, 1) gemv_bulk_kernel(const __grid
         }
     };
 
-    const int first_tile = static_cast<int>(u_begin / nseg);
-    auto cta_of = [&](long long x) { return static_cast<int>(((x + 1) * G + U - 1) / U) - 1; };
-    float acc[4] = {0.f, 0.f, 0.f, 0.f};
-    long long tile_u0 = u_begin;  // first unit of the current tile inside this CTA's range
+    // This warp's pieces of every tile.
+    const int p0 = warp * npieces / kWarps, p1 = (warp + 1) * npieces / kWarps;
     const int col_off = g * 64 + t * 16;
-    long long i = 0;
-    for (long long u = u_begin; u < u_end; ++u, ++i) {
-        const int s = static_cast<int>(i % kBulkStages);
-        const uint32_t ph = static_cast<uint32_t>((i / kBulkStages) & 1);
-        if (!bulk_wait(&full[s], ph)) {
-            if (lane == 0 && error) atomicExch(error, 1);
+    float sc0 = 0.f, sc1 = 0.f;  // the row scales of the tile this warp reduces next
+    for (int tile = t_begin, i = 0; tile < t_end; ++tile, ++i) {
+        const int s = i % stages;
+        const bool reducer = warp == kWarps - 1 - (i & (kWarps - 1));
+        if (reducer) {
+            int r0, r1;
+            bool v0, v1;
+            tile_rows2(tile, r0, r1, v0, v1);
+            sc0 = v0 ? __half2float(sc[r0]) : 0.f;
+            sc1 = v1 ? __half2float(sc[r1]) : 0.f;
         }
-        const int tile = static_cast<int>(u / nseg), seg = static_cast<int>(u % nseg);
-        const int piece = seg * kBulkPieces + warp;
-        if (piece < npieces) {
-            // Row r's 16-byte chunk c of piece `warp`: 128-byte line r * 4 + warp / 2, chunk position
-            // ((warp & 1) * 4 + t) XOR (line & 7) (the TMA 128-byte swizzle).
-            const char* st = stages + s * kBulkStageBytes;
-            const int l0 = g * kBulkChunks + (warp >> 1), l1 = (g + 8) * kBulkChunks + (warp >> 1);
-            const int c = (warp & 1) * 4 + t;
-            const uint4 w0 = *reinterpret_cast<const uint4*>(st + l0 * 128 + ((c ^ (l0 & 7)) << 4));
-            const uint4 w1 = *reinterpret_cast<const uint4*>(st + l1 * 128 + ((c ^ (l1 & 7)) << 4));
+        if (!bulk_wait(&full[s], (i / stages) & 1) && lane == 0 && error) atomicExch(error, 1);
+        const char* st = ring + s * stage_bytes + t * 16;
+        float acc[4] = {0.f, 0.f, 0.f, 0.f}, acc2[4] = {0.f, 0.f, 0.f, 0.f};
+        for (int piece = p0; piece < p1; ++piece) {
+            const uint4 w0 = *reinterpret_cast<const uint4*>(st + static_cast<size_t>(g) * K + piece * PE);
+            const uint4 w1 = *reinterpret_cast<const uint4*>(st + static_cast<size_t>(g + 8) * K + piece * PE);
             const char* ub = xs + static_cast<size_t>(piece * KU) * C2 * 64 + col_off;
             uint32_t b[8];
 #pragma unroll
@@ -1262,125 +1239,60 @@ __global__ void __launch_bounds__(kBulkThreads, 1) gemv_bulk_kernel(const __grid
                 if (g < C2) q = *reinterpret_cast<const uint4*>(ub + static_cast<size_t>(j) * C2 * 64);
                 b[4 * j] = q.x, b[4 * j + 1] = q.y, b[4 * j + 2] = q.z, b[4 * j + 3] = q.w;
             }
-            if constexpr (kI8) {
 #pragma unroll
-                for (int jj = 0; jj < 4; ++jj) {
-                    uint32_t a0, a1, a2, a3;
-                    i8x4_to_h2x2(u4_get(w0, jj), a0, a2);
-                    i8x4_to_h2x2(u4_get(w1, jj), a1, a3);
-                    mma_16816(acc, a0, a1, a2, a3, b[2 * jj], b[2 * jj + 1], false);
-                }
-            } else {
-#pragma unroll
-                for (int jj = 0; jj < 2; ++jj) {
-                    const uint32_t a0 = u4_get(w0, 2 * jj), a2 = u4_get(w0, 2 * jj + 1);
-                    const uint32_t a1 = u4_get(w1, 2 * jj), a3 = u4_get(w1, 2 * jj + 1);
-                    mma_16816(acc, a0, a1, a2, a3, b[2 * jj], b[2 * jj + 1], kBF);
-                }
+            for (int jj = 0; jj < 4; ++jj) {
+                uint32_t a0, a1, a2, a3;
+                i8x4_to_h2x2(u4_get(w0, jj), a0, a2);
+                i8x4_to_h2x2(u4_get(w1, jj), a1, a3);
+                // Two accumulators: independent MMA chains.
+                mma_16816((jj & 1) ? acc2 : acc, a0, a1, a2, a3, b[2 * jj], b[2 * jj + 1], false);
             }
         }
+#pragma unroll
+        for (int e = 0; e < 4; ++e) acc[e] += acc2[e];
         __syncwarp();
         if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bulk_smem_u32(&empty[s])) : "memory");
-        if (seg == nseg - 1 || u == u_end - 1) {
-            // This CTA's share of the tile is complete: reduce the warps.
-            red[warp][lane] = make_float2(acc[0] + acc[1], acc[2] + acc[3]);
-            acc[0] = acc[1] = acc[2] = acc[3] = 0.f;
-            bulk_consumer_sync();
-            if (warp == 0) {
-                float y0 = 0.f, y1 = 0.f;
+        red[i & 1][warp][lane] = make_float2(acc[0] + acc[1], acc[2] + acc[3]);
+        bulk_consumer_sync();
+        // Tile i's partials are complete; its reducer sums them while the other warps go on (the next
+        // write to red[i & 1] comes after the next barrier, which the reducer reaches only when done).
+        if (reducer) {
+            float y0 = 0.f, y1 = 0.f;
 #pragma unroll
-                for (int w = 0; w < kWarps; ++w) {
-                    y0 += red[w][lane].x;
-                    y1 += red[w][lane].y;
-                }
-                y0 *= oscale_s;
-                y1 *= oscale_s;
-                const long long t0u = static_cast<long long>(tile) * nseg;
-                if (tile_u0 == t0u && seg == nseg - 1) {
-                    epilogue(tile, y0, y1);
-                } else {
-                    // Shared tile: this CTA's partial (rows g, g + 8 from the lanes with t == 0).
-                    const int slot = tile == first_tile ? 0 : 1;
-                    if (t == 0) {
-                        g_bulk_part[blockIdx.x][slot][g] = y0;
-                        g_bulk_part[blockIdx.x][slot][g + 8] = y1;
-                    }
-                    __threadfence();
-                    __syncwarp();
-                    const int c0 = cta_of(t0u), c1 = cta_of(t0u + nseg - 1);
-                    unsigned prev = 0;
-                    if (lane == 0) {
-                        prev = atomicAdd(&g_bulk_count[tile], 1u);
-                        if (prev == static_cast<unsigned>(c1 - c0)) g_bulk_count[tile] = 0u;
-                    }
-                    prev = __shfl_sync(0xffffffffu, prev, 0);
-                    if (prev == static_cast<unsigned>(c1 - c0)) {
-                        __threadfence();
-                        float s0 = 0.f, s1 = 0.f;
-                        for (int c = c0; c <= c1; ++c) {
-                            const long long cb = U * c / G;
-                            const int cs = static_cast<int>(cb / nseg) == tile ? 0 : 1;
-                            s0 += __ldcg(&g_bulk_part[c][cs][g]);
-                            s1 += __ldcg(&g_bulk_part[c][cs][g + 8]);
-                        }
-                        epilogue(tile, s0, s1);
-                    }
-                }
+            for (int w = 0; w < kWarps; ++w) {
+                y0 += red[i & 1][w][lane].x;
+                y1 += red[i & 1][w][lane].y;
             }
-            bulk_consumer_sync();
-            tile_u0 = u + 1;
+            epilogue(tile, y0 * oscale_s, y1 * oscale_s, sc0, sc1);
         }
     }
 }
 
-template <typename WT>
-size_t bulk_smem_bytes(int K) {
-    const int npieces = K / MmaPiece<WT>::kK;
-    const size_t xs = (static_cast<size_t>(npieces) * MmaPiece<WT>::kUnits * 2 * 64 + 1023) & ~static_cast<size_t>(1023);
-    return 1024 + xs + static_cast<size_t>(kBulkStages) * kBulkStageBytes + 2 * kBulkStages * 8;
-}
-
-// One activation row, 16-byte aligned rows of whole pieces, int8 with one scale per row; shared memory
-// for the staged activations (4 K bytes) and the ring within one CTA per SM.
-template <typename WT>
-bool bulk_applies(const GemvParams& p) {
-    if constexpr (sizeof(WT) > 2) {
+// One activation row, int8 with one scale per row, 16-byte aligned; at least two whole-tile stages in
+// shared memory beside the staged activations, and at least 8 tiles per SM (whole tiles per CTA).
+bool bulk_applies(int w_dtype, const GemvParams& p, int sm_count) {
+    if (!g_gemv_mma || !g_gemv_bulk || w_dtype != L0B_I8 || p.M != 1 || p.nseg < 1) return false;
+    if (p.group < p.K || p.K % 64 != 0) return false;
+    if (reinterpret_cast<uintptr_t>(p.w) % 16 != 0 || (p.x_dtype == L0B_F32 && (reinterpret_cast<uintptr_t>(p.x) & 15)))
         return false;
-    } else {
-        if (!g_gemv_mma || !g_gemv_bulk || p.M != 1 || p.nseg < 1 || p.K % MmaPiece<WT>::kK != 0) return false;
-        if ((static_cast<long long>(p.K) * sizeof(WT)) % 128 != 0) return false;
-        if (reinterpret_cast<uintptr_t>(p.w) % 16 != 0 || (p.x_dtype == L0B_F32 && (reinterpret_cast<uintptr_t>(p.x) & 15)))
-            return false;
-        if (sizeof(WT) == 1 && p.group < p.K) return false;
-        if (p.norm_w && (reinterpret_cast<uintptr_t>(p.norm_w) & 15)) return false;
-        const int ntiles = p.epi == EPI_SWIGLU ? (p.N / 2 + 7) / 8 : (p.N + 15) / 16;
-        if (ntiles > kBulkMaxTiles) return false;
-        return bulk_smem_bytes<WT>(p.K) <= 220 * 1024;
-    }
+    if (p.norm_w && (reinterpret_cast<uintptr_t>(p.norm_w) & 15)) return false;
+    if (bulk_stages(p.K) < 2) return false;
+    const int ntiles = p.epi == EPI_SWIGLU ? (p.N / 2 + 7) / 8 : (p.N + 15) / 16;
+    return ntiles >= 8 * sm_count;
 }
 
-template <typename WT>
 l0b_status launch_bulk(l0b_device* dev, cudaStream_t stream, int sm_count, const GemvParams& p) {
-    auto kernel = gemv_bulk_kernel<WT>;
     static bool configured = false;
     if (!configured) {
-        cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
+        cudaError_t e = cudaFuncSetAttribute(gemv_bulk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             kBulkSmemBudget);
         if (e != cudaSuccess) return fail(L0B_ERR_CUDA, "cudaFuncSetAttribute failed: %s", cudaGetErrorString(e));
         configured = true;
     }
-    const size_t smem = bulk_smem_bytes<WT>(p.K);
-    const int npieces = p.K / MmaPiece<WT>::kK;
-    const long long U = static_cast<long long>(p.epi == EPI_SWIGLU ? (p.N / 2 + 7) / 8 : (p.N + 15) / 16) *
-                        ((npieces + kBulkPieces - 1) / kBulkPieces);
-    int grid = sm_count < kBulkMaxCtas ? sm_count : kBulkMaxCtas;
-    if (U < grid) grid = static_cast<int>(U);
-    BulkArgs ba;
-    std::memset(&ba, 0, sizeof(ba));
-    L0B_TRY(make_rows_map(&ba.wmap, p.w, p.N, static_cast<long long>(p.K) * sizeof(WT), p.epi == EPI_SWIGLU ? 8 : 16,
-                          kBulkChunks));
-    ba.p = p;
-    ba.error = dev ? dev->error_flag : nullptr;
-    return launch_on(dev, stream, kernel, dim3(grid), dim3(kBulkThreads), smem, ba);
+    const int stages = bulk_stages(p.K);
+    const size_t smem = bulk_smem_bytes(p.K, stages);
+    int* err = dev ? dev->error_flag : nullptr;
+    return launch_on(dev, stream, gemv_bulk_kernel, dim3(sm_count), dim3(kBulkThreads), smem, p, stages, err);
 }
 
 // Resident CTAs per SM for (kernel, dynamic smem), cached: the persistent grid is SMs x this.
@@ -1494,8 +1406,8 @@ l0b_status launch_typed(l0b_device* dev, cudaStream_t stream, int sm_count, Gemv
     const bool vec_ok = (p.K % VEC == 0) && (reinterpret_cast<uintptr_t>(p.w) % 16 == 0) &&
                         (sizeof(WT) != 1 || (p.group % 16 == 0 && p.K % p.group == 0));
     const int M = p.M;
-    if constexpr (sizeof(WT) <= 2) {
-        if (bulk_applies<WT>(p)) return launch_bulk<WT>(dev, stream, sm_count, p);
+    if constexpr (sizeof(WT) == 1) {
+        if (bulk_applies(L0B_I8, p, sm_count)) return launch_bulk(dev, stream, sm_count, p);
     }
     for (int m0 = 0; m0 < M;) {
         GemvParams q = p;

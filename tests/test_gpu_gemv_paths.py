@@ -123,3 +123,76 @@ def test_gemv_paths_one_hot_reads_weights_exactly(lz, device, suite, path):
     sf = s.astype(np.float32)
     for r, c in enumerate(cols):
         np.testing.assert_array_equal(got[r], q[:, c].astype(np.float32) * sf[:, 0])
+
+
+@pytest.fixture
+def bulk(lz):
+    lib = lz.load_library()
+    lib.l0b_set_gemv_bulk(1)
+    yield
+    lib.l0b_set_gemv_bulk(0)
+
+
+@pytest.mark.parametrize("n,k,epi", [(20003, 896, "store"), (19000, 3584, "accum")])
+def test_gemv_bulk_many_tiles(lz, orc, device, suite, bulk, n, k, epi):
+    """The whole-tile bulk kernel serves one-row int8 projections with at least 8 tiles per SM: a partial
+    last tile, the store and residual-add epilogues, against the oracle."""
+    rng = np.random.default_rng(n + k)
+    hf = ((rng.random((n, k)) * 2 - 1) * 0.05).astype(np.float32)
+    x = (rng.standard_normal((1, k)) * 2).astype(np.float32)
+    base = rng.standard_normal((1, n)).astype(np.float32)
+    q, s = lz.q8_quantize_out_in(hf, k)
+    want = orc.gemv_out_in(x, q, orc.I8, s.view(np.uint16), k)
+    if epi == "accum":
+        want = want + base
+    with lz.SharedBuffer.from_array(device, q) as W, lz.SharedBuffer.from_array(device, s) as S, \
+            lz.SharedBuffer.from_array(device, x) as xb, lz.SharedBuffer.from_array(device, base) as ob:
+        suite.linear_fused(device, 1, n, k, xb, W, S, k, None, 0.0,
+                           suite.EPI_ACCUM if epi == "accum" else suite.EPI_STORE, None, ob)
+        got = ob.ToArray().reshape(1, n)
+    err = np.abs(got - want)
+    assert np.all(err <= 1e-4 + 1e-5 * np.abs(want)), f"max err {err.max()}"
+
+
+def test_gemv_bulk_norm_swiglu_many_tiles(lz, orc, device, suite, bulk):
+    rng = np.random.default_rng(77)
+    H, inter = 3584, 9500  # 1188 SwiGLU tiles, the last one partial
+    x = (rng.standard_normal((1, H)) * 3).astype(np.float32)
+    nw = (1 + 0.1 * rng.standard_normal(H)).astype(np.float32)
+    hf = ((rng.random((2 * inter, H)) * 2 - 1) * 0.05).astype(np.float32)
+    _, normed = orc.rmsnorm(x, nw, 1e-6)
+    q, s = lz.q8_quantize_out_in(hf, H)
+    y = orc.gemv_out_in(normed, q, orc.I8, s.view(np.uint16), H)
+    g, u = y[:, :inter], y[:, inter:]
+    want = g / (1 + np.exp(-g.astype(np.float64))) * u
+    with lz.SharedBuffer.from_array(device, x) as xb, lz.SharedBuffer.from_array(device, q) as W, \
+            lz.SharedBuffer.from_array(device, s) as S, lz.SharedBuffer.from_array(device, nw) as nb, \
+            lz.SharedBuffer(device, lz.F32, inter) as ob:
+        suite.linear_fused(device, 1, 2 * inter, H, xb, W, S, H, nb, 1e-6, suite.EPI_SWIGLU, None, ob)
+        got = ob.ToArray().reshape(1, inter)
+    err = np.abs(got - want)
+    assert np.all(err <= 1e-4 + 1e-4 * np.abs(want)), f"max err {err.max()}"
+
+
+def test_gemv_bulk_model_matches_register_path(lz, device, suite):
+    """Config-2 widths, two layers: greedy decode with the bulk kernel on the gate/up projections and the
+    152,064-row LM head (argmax epilogue) gives the register path's tokens and logits."""
+    cfgd = dict(hidden_size=3584, intermediate_size=18944, num_layers=2, num_attention_heads=28,
+                num_key_value_heads=4, head_dim=128, vocab_size=152064, max_position_embeddings=32768,
+                rms_norm_eps=1e-6, rope_theta=1e6, attention_bias=1, q8_group=0)
+    prompt = np.random.default_rng(2).integers(0, 152064, 16).astype(np.int32)
+    lib = lz.load_library()
+    out = {}
+    for on in (0, 1):
+        lib.l0b_set_gemv_bulk(on)
+        try:
+            with lz.LlmModel(device, suite, lz.model_config(kv_dtype=lz.F16, **cfgd), 64, "int8") as model:
+                model.init_synthetic(2, 0.02, 1e-3, 2e-2)
+                model.Prefill(prompt)
+                toks = model.decode_greedy_device(6)
+                out[on] = (toks, model.Decode(int(toks[-1])))
+        finally:
+            lib.l0b_set_gemv_bulk(0)
+    np.testing.assert_array_equal(out[0][0], out[1][0])
+    scale = float(np.abs(out[0][1]).max())
+    assert float(np.abs(out[0][1] - out[1][1]).max()) <= 1e-4 * scale
