@@ -401,8 +401,9 @@ L0B_API l0b_status l0b_comm_allreduce(l0b_comm* comm, l0b_buffer* buf, int64_t c
 /* Tuning: the largest K split the tensor-core GEMM may use for narrow projections (1..16, default 16;
  * <= 0 restores the default). Affects plans made after the call. */
 L0B_API l0b_status l0b_tc_set_max_splits(int32_t splits);
-/* Tuning: one-row projections (batch-1 decode) on the TMA-streamed tensor-core GEMV (1) or on the
- * register-streamed one (0, default). Affects launches made after the call. */
+/* Tuning: one-row int8 projections with at least 8 tiles of 16 rows per SM (the gate/up projection and
+ * LM head at batch 1) on the GEMV that streams whole tiles by bulk copies (1, default) or on the
+ * register-streamed one (0). Affects launches made after the call. */
 L0B_API l0b_status l0b_set_gemv_bulk(int32_t enable);
 /* Process-wide choice of the decode GEMV kernel for shapes both take: 1 (default) = tensor-core
  * mma.sync streaming kernel, 0 = fp32-FMA streaming kernel. Used by tests to cover both; recorded

@@ -966,7 +966,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_mma_kernel(const GemvParams 
 }
 
 bool g_gemv_mma = true;
-bool g_gemv_bulk = false;  // the TMA-streamed one-row kernel (l0b_set_gemv_bulk)
+bool g_gemv_bulk = true;  // the bulk-copy one-row kernel where it applies (l0b_set_gemv_bulk)
 
 template <typename F, typename... A>
 l0b_status launch_on(l0b_device* dev, cudaStream_t stream, F kernel, dim3 g, dim3 b, size_t smem, A... args) {
@@ -994,9 +994,11 @@ l0b_status launch_on(l0b_device* dev, cudaStream_t stream, F kernel, dim3 g, dim
 // go on with the next tile. Each CTA (one per SM) takes a contiguous range of whole tiles, so the kernel
 // serves projections with many tiles per SM (gate/up, LM head); the others stay on the register GEMV.
 // ---------------------------------------------------------------------------------------------
-constexpr int kBulkThreads = kThreads + 32;  // 8 consumer warps + 1 producer warp
+constexpr int kBulkCW = 16;                      // consumer warps
+constexpr int kBulkConsumers = kBulkCW * 32;
+constexpr int kBulkThreads = kBulkConsumers + 32;  // consumers + 1 producer warp
 constexpr int kBulkMaxStages = 4;
-constexpr int kBulkSmemBudget = 220 * 1024;
+constexpr int kBulkSmemBudget = 212 * 1024;  // dynamic; the static arrays take ~8 KB of the 227 KB
 constexpr long long kBulkWaitCycles = 4000000000LL;
 
 __device__ __forceinline__ uint32_t bulk_smem_u32(const void* p) {
@@ -1018,7 +1020,7 @@ __device__ __forceinline__ bool bulk_wait(uint64_t* bar, uint32_t parity) {
     }
 }
 
-__device__ __forceinline__ void bulk_consumer_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kThreads) : "memory"); }
+__device__ __forceinline__ void bulk_consumer_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kBulkConsumers) : "memory"); }
 
 __device__ __forceinline__ void bulk_copy(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
     asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
@@ -1041,8 +1043,8 @@ inline int bulk_stages(int K) {
 __global__ void __launch_bounds__(kBulkThreads, 1) gemv_bulk_kernel(const GemvParams p, int stages, int* error) {
     extern __shared__ char bulk_smem[];
     constexpr int PE = 64, KU = 2, C2 = 2;  // int8: 64 k per piece, two 32-k units; B columns hi, lo
-    __shared__ float2 red[2][kWarps][32];
-    __shared__ float ssq_s[kWarps], amax_s[kWarps];
+    __shared__ float2 red[2][kBulkCW][32];
+    __shared__ float ssq_s[kBulkCW], amax_s[kBulkCW];
     __shared__ float oscale_s;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
     const int N = p.N, K = p.K;
@@ -1063,14 +1065,14 @@ __global__ void __launch_bounds__(kBulkThreads, 1) gemv_bulk_kernel(const GemvPa
     if (threadIdx.x == 0) {
         for (int s = 0; s < stages; ++s) {
             asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(bulk_smem_u32(&full[s])) : "memory");
-            asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bulk_smem_u32(&empty[s])), "r"(kWarps)
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bulk_smem_u32(&empty[s])), "r"(kBulkCW)
                          : "memory");
         }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     __syncthreads();
 
-    if (warp == kWarps) {
+    if (warp == kBulkCW) {
         // Producer: tile i's rows as one (SwiGLU: two) contiguous copies; rows past the matrix are not
         // copied (their stage bytes are stale and their outputs are never stored).
         if (lane == 0) {
@@ -1116,7 +1118,7 @@ __global__ void __launch_bounds__(kBulkThreads, 1) gemv_bulk_kernel(const GemvPa
             return xs + static_cast<size_t>(u) * C2 * 64 + tt * 16;  // lo slot is +64
         };
         float ss = 0.f, amax = 0.f;
-        for (int it = threadIdx.x; it < items; it += kThreads) {
+        for (int it = threadIdx.x; it < items; it += kBulkConsumers) {
             int k;
             char* slot = item_slot(it, k);
             float v[8];
@@ -1149,7 +1151,7 @@ __global__ void __launch_bounds__(kBulkThreads, 1) gemv_bulk_kernel(const GemvPa
         bulk_consumer_sync();
         float sst = 0.f, am = 0.f;
 #pragma unroll
-        for (int w = 0; w < kWarps; ++w) {
+        for (int w = 0; w < kBulkCW; ++w) {
             sst += ssq_s[w];
             am = fmaxf(am, amax_s[w]);
         }
@@ -1162,7 +1164,7 @@ __global__ void __launch_bounds__(kBulkThreads, 1) gemv_bulk_kernel(const GemvPa
         }
         const float in_scale = rs * ldexpf(1.0f, e);
         if (threadIdx.x == 0) oscale_s = ldexpf(1.0f, -e);
-        for (int it = threadIdx.x; it < items; it += kThreads) {
+        for (int it = threadIdx.x; it < items; it += kBulkConsumers) {
             int k;
             char* slot = item_slot(it, k);
             const float4 a = *reinterpret_cast<const float4*>(slot);
@@ -1212,12 +1214,12 @@ __global__ void __launch_bounds__(kBulkThreads, 1) gemv_bulk_kernel(const GemvPa
     };
 
     // This warp's pieces of every tile.
-    const int p0 = warp * npieces / kWarps, p1 = (warp + 1) * npieces / kWarps;
+    const int p0 = warp * npieces / kBulkCW, p1 = (warp + 1) * npieces / kBulkCW;
     const int col_off = g * 64 + t * 16;
     float sc0 = 0.f, sc1 = 0.f;  // the row scales of the tile this warp reduces next
     for (int tile = t_begin, i = 0; tile < t_end; ++tile, ++i) {
         const int s = i % stages;
-        const bool reducer = warp == kWarps - 1 - (i & (kWarps - 1));
+        const bool reducer = warp == kBulkCW - 1 - (i & (kBulkCW - 1));
         if (reducer) {
             int r0, r1;
             bool v0, v1;
@@ -1259,7 +1261,7 @@ __global__ void __launch_bounds__(kBulkThreads, 1) gemv_bulk_kernel(const GemvPa
         if (reducer) {
             float y0 = 0.f, y1 = 0.f;
 #pragma unroll
-            for (int w = 0; w < kWarps; ++w) {
+            for (int w = 0; w < kBulkCW; ++w) {
                 y0 += red[i & 1][w][lane].x;
                 y1 += red[i & 1][w][lane].y;
             }

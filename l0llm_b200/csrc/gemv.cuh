@@ -47,8 +47,8 @@ l0b_status gemv_nk_launch(l0b_device* dev, int w_dtype, GemvParams p);
 // Process-wide choice between the tensor-core GEMV (default) and the fp32-FMA GEMV for the shapes
 // both take; launches already recorded into command lists keep the kernel they were recorded with.
 void gemv_set_tensor_cores(bool on);
-// Process-wide choice of the TMA-streamed kernel for one activation row (tensor cores on); launches
-// already recorded keep their kernel.
+// Process-wide choice of the bulk-copy kernel for one activation row where it applies (default on);
+// launches already recorded keep their kernel.
 void gemv_set_bulk(bool on);
 
 // Raw-stream variant (no device handle): immediate launch on `stream`.

@@ -22,10 +22,10 @@ def path(request, lz):
     for one activation row (other row counts fall back to mma)."""
     lib = lz.load_library()
     lib.l0b_set_gemv_tensor_cores(0 if request.param == "fma" else 1)
-    lib.l0b_set_gemv_bulk(1 if request.param == "bulk" else 0)
+    lib.l0b_set_gemv_bulk(1 if request.param == "bulk" else 0)  # mma: the register-streamed kernel only
     yield request.param
     lib.l0b_set_gemv_tensor_cores(1)
-    lib.l0b_set_gemv_bulk(0)
+    lib.l0b_set_gemv_bulk(1)
 
 
 def _weights(lz, orc, wkind, hf, k):
@@ -130,7 +130,6 @@ def bulk(lz):
     lib = lz.load_library()
     lib.l0b_set_gemv_bulk(1)
     yield
-    lib.l0b_set_gemv_bulk(0)
 
 
 @pytest.mark.parametrize("n,k,epi", [(20003, 896, "store"), (19000, 3584, "accum")])
@@ -192,7 +191,7 @@ def test_gemv_bulk_model_matches_register_path(lz, device, suite):
                 toks = model.decode_greedy_device(6)
                 out[on] = (toks, model.Decode(int(toks[-1])))
         finally:
-            lib.l0b_set_gemv_bulk(0)
+            lib.l0b_set_gemv_bulk(1)
     np.testing.assert_array_equal(out[0][0], out[1][0])
     scale = float(np.abs(out[0][1]).max())
     assert float(np.abs(out[0][1] - out[1][1]).max()) <= 1e-4 * scale
