@@ -224,7 +224,8 @@ def run_reference(args) -> int:
 # ------------------------------------------------------------------------------------------------
 
 def dominant_kernel_roofline(lz, dev, suite, stream_ptr, torch, peak: float, peak_kind: str) -> dict:
-    """The fused RMSNorm + [gate; up] int8 GEMV + SwiGLU of config 2, over 4 rotating weight copies."""
+    """The fused RMSNorm + [gate; up] int8 GEMV + SwiGLU of config 2 (gemv_bulk_kernel), over 4 rotating
+    weight copies."""
     H, I = 3584, 18944
     N = 2 * I
     copies = 4
@@ -256,7 +257,8 @@ def dominant_kernel_roofline(lz, dev, suite, stream_ptr, torch, peak: float, pea
         traffic = json.loads(tf.read_text()).get("dram_bytes_per_launch")
     for b in qs + ss + [x, nw, out]:
         b.Dispose()
-    return {"kernel": "gemv_mma_kernel<int8> (RMSNorm prologue + [gate;up] 37888x3584 mma.sync + SwiGLU epilogue)",
+    return {"kernel": "gemv_bulk_kernel (int8 [gate;up] 37888x3584: whole 16-row tiles by bulk copy, RMSNorm "
+                      "prologue, mma.sync, SwiGLU epilogue)",
             "bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
             "frac": round(achieved / peak, 4), "traffic": traffic, "algorithmic_bytes": bytes_per_launch,
             "avg_us": round(avg_ms * 1e3, 2)}
