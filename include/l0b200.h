@@ -533,6 +533,12 @@ L0B_API l0b_status l0b_model_decode_greedy_device_batch(l0b_model* model, int32_
                                                         int32_t* out);
 /* Next position of sequence `seq` (its prefilled and decoded length). */
 L0B_API l0b_status l0b_model_sequence_position(l0b_model* model, int32_t seq, int32_t* position);
+/* Device-side fork for beam search (replaces LlmModel.CaptureState + RestoreState,
+ * src/HFLabs.ML.LLM.LevelZero/LlmModel.cs:257-306, which copy the KV tail through host arrays): sequence
+ * dst becomes a copy of sequence src. KV-cache rows [base_position, length of src) of every layer are
+ * copied device to device (rows below base_position, a shared prompt, are assumed equal), and dst takes
+ * src's length and its device-side next token and position. Stream-ordered: no host synchronisation. */
+L0B_API l0b_status l0b_model_fork_sequence(l0b_model* model, int32_t src, int32_t dst, int32_t base_position);
 L0B_API l0b_status l0b_model_position(l0b_model* model, int32_t* position);
 L0B_API l0b_status l0b_model_reset_sequence(l0b_model* model);
 L0B_API l0b_status l0b_model_projection_bytes(l0b_model* model, int64_t* bytes);

@@ -1425,6 +1425,44 @@ L0B_API l0b_status l0b_model_sequence_position(l0b_model* m, int32_t seq, int32_
     return L0B_OK;
 }
 
+// Device-side fork (the reference's CaptureState + RestoreState, src/HFLabs.ML.LLM.LevelZero/LlmModel.cs:
+// 257-306, which round-trips the KV tail through host arrays): sequence dst becomes a copy of sequence
+// src. Cache rows [base_position, length) of every layer are copied on the device (rows below
+// base_position are taken to be equal already, the shared prompt), and so are the device token,
+// position and last sampled token that the device-resident decode continues from.
+L0B_API l0b_status l0b_model_fork_sequence(l0b_model* m, int32_t src, int32_t dst, int32_t base_position) {
+    GUARD_BEGIN
+    L0B_REQUIRE(m, L0B_ERR_ARGUMENT, "model is null");
+    L0B_REQUIRE(src >= 0 && src < m->batch_cap && dst >= 0 && dst < m->batch_cap, L0B_ERR_OUT_OF_RANGE,
+                "sequences %d -> %d outside the %d-sequence batch", src, dst, m->batch_cap);
+    L0B_REQUIRE(src != dst, L0B_ERR_ARGUMENT, "a sequence cannot be forked onto itself");
+    // Sequence 0's length is kept by the single-sequence calls in `position`.
+    const int length = src == 0 ? m->position : m->seq_pos[src];
+    L0B_REQUIRE(base_position >= 0 && base_position <= length, L0B_ERR_OUT_OF_RANGE,
+                "base position %d outside [0, %d]", base_position, length);
+    l0b_device* d = m->dev;
+    L0B_CHECK_CUDA(cudaSetDevice(d->index));
+    const size_t row = static_cast<size_t>(m->kvdim) * dtype_size(static_cast<l0b_dtype>(m->cache_dtype));
+    const size_t bytes = static_cast<size_t>(length - base_position) * row;
+    if (bytes > 0) {
+        for (ModelLayer& L : m->layers) {
+            for (int which = 0; which < 2; ++which) {
+                char* cache = static_cast<char*>(which ? L.vc : L.kc);
+                const size_t s_off = (static_cast<size_t>(src) * m->max_seq + base_position) * row;
+                const size_t d_off = (static_cast<size_t>(dst) * m->max_seq + base_position) * row;
+                L0B_CHECK_CUDA(cudaMemcpyAsync(cache + d_off, cache + s_off, bytes, cudaMemcpyDeviceToDevice, d->stream));
+            }
+        }
+    }
+    L0B_CHECK_CUDA(cudaMemcpyAsync(m->tok + dst, m->tok + src, sizeof(int), cudaMemcpyDeviceToDevice, d->stream));
+    L0B_CHECK_CUDA(cudaMemcpyAsync(m->pos + dst, m->pos + src, sizeof(int), cudaMemcpyDeviceToDevice, d->stream));
+    L0B_CHECK_CUDA(cudaMemcpyAsync(m->sampled + dst, m->sampled + src, sizeof(int), cudaMemcpyDeviceToDevice, d->stream));
+    m->seq_pos[dst] = length;
+    if (dst == 0) m->position = length;
+    return L0B_OK;
+    GUARD_END
+}
+
 L0B_API l0b_status l0b_model_position(l0b_model* m, int32_t* position) {
     L0B_REQUIRE(m && position, L0B_ERR_ARGUMENT, "null argument");
     *position = m->position;

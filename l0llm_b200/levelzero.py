@@ -175,6 +175,7 @@ def load_library() -> C.CDLL:
         "l0b_sample_execute": (i32, [vp, vp, vp, i32, vp, i32, f32, f32, i32, f32, C.c_double, vp]),
         "l0b_model_sample_logits": (i32, [vp, f32, f32, i32, f32, C.c_uint64, vp, i32, C.POINTER(i32)]),
         "l0b_model_decode_sample_device": (i32, [vp, i32, f32, f32, i32, f32, C.c_uint64, vp]),
+        "l0b_model_fork_sequence": (i32, [vp, i32, i32, i32]),
         "l0b_device_error_status": (i32, [vp, C.POINTER(i32)]),
         "l0b_set_gemv_tensor_cores": (i32, [i32]),
         "l0b_comm_unique_id": (i32, [vp, i32]),
@@ -702,6 +703,10 @@ class LlmModel:
         out = np.zeros(max(1, steps), np.int32)
         check(load_library().l0b_model_decode_greedy_device(self.handle, steps, _p(out)))
         return out[:steps]
+
+    def ForkSequence(self, src: int, dst: int, base_position: int = 0):
+        """Sequence dst becomes a device-side copy of sequence src (KV rows from base_position on)."""
+        check(load_library().l0b_model_fork_sequence(self.handle, src, dst, base_position))
 
     # Device sampling (LlmSampler.Sample on the GPU; no logits readback).
     def sample_logits(self, temperature: float, top_p: float, top_k: int, repetition_penalty: float, seed: int,

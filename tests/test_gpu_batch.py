@@ -72,3 +72,28 @@ def test_batched_rejects_out_of_range(lz, device, suite):
             mb.PrefillSequence(2, np.array([1, 2], np.int32))
         with pytest.raises(lz.ArgumentOutOfRangeException):
             mb.DecodeBatch(np.array([1, 2, 3], np.int32), np.array([0, 0, 0], np.int32))
+
+
+def test_fork_sequence_on_device(lz, device, suite):
+    """ForkSequence copies a sequence's KV rows and its next-token state device to device (the
+    reference's CaptureState / RestoreState go through host arrays): forked rows then decode exactly as
+    the source, both through DecodeBatch and the device-resident greedy loop."""
+    a = _prompts(3)[2]
+    b = a.copy()
+    b[5:] = (b[5:] + 1) % CFG["vocab_size"]  # shares a's first 5 tokens only
+    with _model(lz, device, suite, 3, "int8") as mb:
+        mb.PrefillSequence(0, a, want_logits=False)
+        mb.PrefillSequence(1, b, want_logits=False)
+        mb.ForkSequence(0, 1, 5)  # the first 5 rows are shared: only the tail is copied
+        mb.ForkSequence(0, 2, 0)
+        assert [mb.SequencePosition(s) for s in range(3)] == [len(a)] * 3
+        got = mb.DecodeBatch(np.full(3, 7, np.int32), np.full(3, len(a), np.int32))
+        np.testing.assert_array_equal(got[0], got[1])
+        np.testing.assert_array_equal(got[0], got[2])
+        toks = mb.decode_greedy_device_batch(4, 3)
+        np.testing.assert_array_equal(toks[:, 0], toks[:, 1])
+        np.testing.assert_array_equal(toks[:, 0], toks[:, 2])
+        with pytest.raises(lz.ArgumentException):
+            mb.ForkSequence(1, 1, 0)
+        with pytest.raises(lz.ArgumentOutOfRangeException):
+            mb.ForkSequence(0, 3, 0)
