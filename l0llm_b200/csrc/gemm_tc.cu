@@ -724,24 +724,6 @@ l0b_status launch_fmt(l0b_device* d, const TcParams& p, const TcPlan& plan) {
 
 }  // namespace
 
-l0b_status make_rows_map(CUtensorMap* map, const void* base, long long rows, long long row_bytes, int box_rows,
-                         int chunks) {
-    EncodeTiledFn fn = encode_fn();
-    L0B_REQUIRE(fn, L0B_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
-    L0B_REQUIRE(reinterpret_cast<uintptr_t>(base) % 16 == 0 && row_bytes % 128 == 0, L0B_ERR_ARGUMENT,
-                "row map needs 16-byte aligned rows of whole 128-byte chunks");
-    // dims: byte in chunk (128), chunk in row, row; a box is box_rows rows x `chunks` chunks.
-    const cuuint64_t dims[3] = {128, static_cast<cuuint64_t>(row_bytes / 128), static_cast<cuuint64_t>(rows)};
-    const cuuint64_t strides[2] = {128, static_cast<cuuint64_t>(row_bytes)};
-    const cuuint32_t box[3] = {128, static_cast<cuuint32_t>(chunks), static_cast<cuuint32_t>(box_rows)};
-    const cuuint32_t estr[3] = {1, 1, 1};
-    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base), dims, strides, box, estr,
-                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    L0B_REQUIRE(r == CUDA_SUCCESS, L0B_ERR_CUDA, "cuTensorMapEncodeTiled (rows) failed (%d)", static_cast<int>(r));
-    return L0B_OK;
-}
-
 bool tc_gemm_supported(int wdtype, int M, int N, int K, int epi) {
     if (wdtype != L0B_F16 && wdtype != L0B_BF16 && wdtype != L0B_I8) return false;
     if (M < 1 || N < 1 || K < 64 || K % (wdtype == L0B_I8 ? 16 : 8) != 0) return false;

@@ -1,8 +1,6 @@
 // Tensor-core (tcgen05 / TMEM / TMA) GEMM for prefill and batched decode: Y[M, N] = X[M, K] W[N, K]^T.
 #pragma once
 
-#include <cuda.h>
-
 #include "runtime.h"
 
 namespace l0b {
@@ -76,11 +74,6 @@ bool tc_gemm_supported(int wdtype, int M, int N, int K, int epi);
 // Upper bound on the K split of later plans (1..16; <= 0 restores 16). Launches already recorded into
 // command lists keep their plan.
 void tc_gemm_set_max_splits(int s);
-
-// Tensor map over `rows` rows of row_bytes bytes (a multiple of 128) for boxes of box_rows rows x
-// `chunks` 128-byte chunks, 128-byte swizzle: one TMA brings a [box_rows, 128 * chunks] byte block.
-l0b_status make_rows_map(CUtensorMap* map, const void* base, long long rows, long long row_bytes, int box_rows,
-                         int chunks);
 
 // Split-K scratch that covers every plan on `sm_count` SMs: floats and counters.
 size_t tc_gemm_part_floats(int sm_count);
