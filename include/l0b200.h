@@ -340,7 +340,12 @@ L0B_API l0b_status l0b_gated_delta_execute_grouped(l0b_suite* s, l0b_device* d, 
 /* w dtype: L0B_F32, L0B_F16, L0B_BF16 or L0B_I8 (then `scales` f16 [N, K/group]).             */
 /* ------------------------------------------------------------------------------------------ */
 
-/* Y[M, N] = X[M, K] * W^T (+ bias). X f32/f16/bf16, Y f32/f16/bf16; bias f32 [N] or NULL.
+/* Ordering note for the linear ops below: the decode GEMVs start streaming W before they wait for the
+ * previous kernel on the stream (weights are parameters), and the GEMVs, GEMMs and attention let the
+ * next kernel start early. So W must not be an output of the linear / attention op launched just before
+ * on the same stream; weights written by uploads, l0b_q8_quantize_device or the other ops are ordered.
+ *
+ * Y[M, N] = X[M, K] * W^T (+ bias). X f32/f16/bf16, Y f32/f16/bf16; bias f32 [N] or NULL.
  * group: int8 scale group (32, or K for per-channel); ignored for 16/32-bit weights.
  * Any M: the weights stream once per 8 rows (tensor-core GEMV); l0b_linear_tc runs a prefill-sized M
  * as one tcgen05 GEMM. */
