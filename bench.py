@@ -223,7 +223,7 @@ def run_reference(args) -> int:
 # GPU
 # ------------------------------------------------------------------------------------------------
 
-def dominant_kernel_roofline(lz, dev, suite, stream_ptr, torch, peak: float, peak_kind: str) -> dict:
+def dominant_kernel_roofline(lz, dev, suite, stream_ptr, torch, peak: float, peak_kind: str, bulk: bool = True) -> dict:
     """The fused RMSNorm + [gate; up] int8 GEMV + SwiGLU of config 2 (gemv_bulk_kernel), over 4 rotating
     weight copies."""
     H, I = 3584, 18944
@@ -253,12 +253,14 @@ def dominant_kernel_roofline(lz, dev, suite, stream_ptr, torch, peak: float, pea
     achieved = bytes_per_launch / (avg_ms * 1e-3) / 1e9
     traffic = None
     tf = ROOT / "profiles" / "gemv_i8_swiglu_cfg2.traffic.json"
-    if tf.exists():
+    if tf.exists() and bulk:
         traffic = json.loads(tf.read_text()).get("dram_bytes_per_launch")
     for b in qs + ss + [x, nw, out]:
         b.Dispose()
-    return {"kernel": "gemv_bulk_kernel (int8 [gate;up] 37888x3584: whole 16-row tiles by bulk copy, RMSNorm "
-                      "prologue, mma.sync, SwiGLU epilogue)",
+    name = ("gemv_bulk_kernel (int8 [gate;up] 37888x3584: whole 16-row tiles by bulk copy, RMSNorm prologue, "
+            "mma.sync, SwiGLU epilogue)" if bulk else
+            "gemv_mma_kernel<int8> (register-streamed; RMSNorm prologue + [gate;up] 37888x3584 mma.sync + SwiGLU)")
+    return {"kernel": name,
             "bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
             "frac": round(achieved / peak, 4), "traffic": traffic, "algorithmic_bytes": bytes_per_launch,
             "avg_us": round(avg_ms * 1e3, 2)}
@@ -479,6 +481,8 @@ def run_profile_case(case: str) -> int:
     steps; one more decode step runs inside the NVTX range "step" (capture with --nvtx-include "step/").
     gemm-gateup-16: the config-2 gate/up projection (int8 [37888, 3584], SwiGLU) at 16 activation rows on
     the tensor-core GEMM, 3 rotating weight copies (408 MB > L2), 6 warm-up launches then 30 timed.
+    attention-512: Attention.Execute at the config-2 head shape (hd 128, 28 query / 4 KV heads, f32
+    caches of 4096 rows, 512 live positions), 5 warm-up launches then 50 timed.
     """
     import ctypes as C
 
@@ -536,6 +540,25 @@ def run_profile_case(case: str) -> int:
                           "weight_gbs": round(N * H / us / 1e3, 1)}))
         for b in qs + ss + [x, out]:
             b.Dispose()
+    elif case == "attention-512":
+        hd, nh, nkv, seq, max_seq = 128, 28, 4, 512, 4096
+        q = lz.SharedBuffer.from_array(dev, rng.standard_normal(nh * hd).astype(np.float32))
+        kc = lz.SharedBuffer.from_array(dev, rng.standard_normal(max_seq * nkv * hd).astype(np.float32))
+        vc = lz.SharedBuffer.from_array(dev, rng.standard_normal(max_seq * nkv * hd).astype(np.float32))
+        out = lz.SharedBuffer(dev, lz.F32, nh * hd)
+        for _ in range(5):
+            suite.Attention.Execute(dev, q, kc, vc, out, hd, nh, nkv, seq, max_seq)
+        stream = torch.cuda.ExternalStream(sp.value)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        dev.Synchronize()
+        e0.record(stream)
+        for _ in range(50):
+            suite.Attention.Execute(dev, q, kc, vc, out, hd, nh, nkv, seq, max_seq)
+        e1.record(stream)
+        e1.synchronize()
+        print(json.dumps({"profile_case": case, "us_per_call": round(e0.elapsed_time(e1) / 50 * 1e3, 2)}))
+        for b in (q, kc, vc, out):
+            b.Dispose()
     else:
         raise SystemExit(f"unknown profile case {case}")
     suite.Dispose()
@@ -555,9 +578,15 @@ def main() -> int:
     ap.add_argument("--workload", default="cfg2", choices=["cfg2", "cfg3", "cfg4"],
                     help="cfg2: the headline (Qwen2.5-7B int8, one GPU, replicas over N); cfg3: the Gated DeltaNet "
                          "layer alone (bf16, one GPU); cfg4: Llama-3-70B bf16 tensor-parallel over the N ranks")
-    ap.add_argument("--profile-case", choices=["decode-bs1", "decode-bs16", "gemm-gateup-16"],
+    ap.add_argument("--no-bulk-gemv", action="store_true",
+                    help="one-row projections on the register-streamed GEMV only (l0b_set_gemv_bulk(0))")
+    ap.add_argument("--profile-case", choices=["decode-bs1", "decode-bs16", "gemm-gateup-16", "attention-512"],
                     help="run one small case for an ncu capture instead of the benchmark")
     args = ap.parse_args()
+    if args.no_bulk_gemv:
+        from l0llm_b200 import levelzero as lz
+
+        lz.load_library().l0b_set_gemv_bulk(0)
     if args.profile_case:
         return run_profile_case(args.profile_case)
     if args.impl == "reference":
@@ -579,7 +608,8 @@ def main() -> int:
         sp = C.c_void_p()
         lz.check(lz.load_library().l0b_device_stream(dev.handle, C.byref(sp)))
         peak, kind = peaks()
-        print(json.dumps(dominant_kernel_roofline(lz, dev, suite, sp.value, torch, peak, kind)))
+        print(json.dumps(dominant_kernel_roofline(lz, dev, suite, sp.value, torch, peak, kind,
+                                                  bulk=not args.no_bulk_gemv)))
         suite.Dispose()
         dev.Dispose()
         return 0
@@ -674,7 +704,7 @@ def main() -> int:
     barrier()
     bs16_ms = g0.elapsed_time(g1)
 
-    roof = dominant_kernel_roofline(lz, dev, suite, sp.value, torch, peak, peak_kind)
+    roof = dominant_kernel_roofline(lz, dev, suite, sp.value, torch, peak, peak_kind, bulk=not args.no_bulk_gemv)
 
     if pg is not None:
         t = torch.tensor([ms, e2e_ms, bs16_ms], dtype=torch.float64, device="cuda")
