@@ -214,7 +214,11 @@ L0B_API l0b_status l0b_gemm_execute(l0b_suite* s, l0b_device* d, int32_t m, int3
  * keeps the activations exact (f32) instead of quantizing them. */
 L0B_API l0b_status l0b_gemv_q8_quantize(l0b_suite* s, l0b_device* d, int32_t rows, int32_t k, l0b_buffer* x);
 /* GemvQ8.Execute / ExecuteRows(dev, [M,] N, K, scratch, words, scales, y) -- L/LlmMatrix.cs:130,157,
- * 235,239. words: i8 (or i32-packed) [N, K]; scales f16 [N, K/32]. Y [M, N] f32. */
+ * 235,239. words: i8 (or i32-packed) [N, K]; scales f16 [N, K/32]. Y [M, N] f32.
+ * The reference's `scratch` argument is not taken: every reference call passes the suite's own
+ * LlmQ8Activations (suite.Q8Scratch, via RequireScratch, L/LlmMatrix.cs:243-253), and these entries
+ * always read the suite's scratch, i.e. the rows the last l0b_gemv_q8_quantize on this suite staged.
+ * A facade holding any other LlmQ8Activations must quantize into the suite before calling. */
 L0B_API l0b_status l0b_gemv_q8_execute(l0b_suite* s, l0b_device* d, int32_t n, int32_t k,
                                        l0b_buffer* words, l0b_buffer* scales, l0b_buffer* y);
 L0B_API l0b_status l0b_gemv_q8_execute_rows(l0b_suite* s, l0b_device* d, int32_t m, int32_t n, int32_t k,

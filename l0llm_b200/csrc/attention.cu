@@ -12,6 +12,7 @@
 // applies RoPE to the query and to the new key, and the CTA owning the query position writes the
 // new key/value row into the cache, replacing the separate RoPE and KvCacheStore launches.
 #include <cmath>
+#include <mutex>
 
 #include <cooperative_groups.h>
 
@@ -591,13 +592,15 @@ static __device__ __align__(256) unsigned g_noalloc_counters[kNoAllocCounters];
 
 namespace {
 
-// Device addresses of the two arrays, looked up once per device (the names are host stand-ins).
+// Device addresses of the two arrays, looked up once per device (the names are host stand-ins). The
+// lookup runs under a mutex so two host threads making their first call on one device do not race.
 struct NoAllocAddrs {
     bool ready = false;
     float* part = nullptr;
     unsigned* counters = nullptr;
 };
 NoAllocAddrs g_noalloc_addrs[64];
+std::mutex g_noalloc_mutex;
 
 }  // namespace
 
@@ -624,13 +627,22 @@ extern "C" L0B_API l0b_status l0b_attention_decode_noalloc(void* stream, const f
     int dev = 0;
     L0B_CHECK_CUDA(cudaGetDevice(&dev));
     L0B_REQUIRE(dev >= 0 && dev < 64, L0B_ERR_OUT_OF_RANGE, "device ordinal %d", dev);
-    NoAllocAddrs& a = g_noalloc_addrs[dev];
-    if (!a.ready) {
-        // First call on this device: resolve the arrays' device addresses (no allocation; the module is
-        // already loaded). Make this first call before any stream capture on the device.
-        L0B_CHECK_CUDA(cudaGetSymbolAddress(reinterpret_cast<void**>(&a.part), g_noalloc_part));
-        L0B_CHECK_CUDA(cudaGetSymbolAddress(reinterpret_cast<void**>(&a.counters), g_noalloc_counters));
-        a.ready = true;
+    NoAllocAddrs a;
+    {
+        std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+        NoAllocAddrs& slot = g_noalloc_addrs[dev];
+        if (!slot.ready) {
+            // First call on this device: resolve the arrays' device addresses (no allocation; the module
+            // is already loaded). Make this first call before any stream capture on the device.
+            float* part = nullptr;
+            unsigned* counters = nullptr;
+            L0B_CHECK_CUDA(cudaGetSymbolAddress(reinterpret_cast<void**>(&part), g_noalloc_part));
+            L0B_CHECK_CUDA(cudaGetSymbolAddress(reinterpret_cast<void**>(&counters), g_noalloc_counters));
+            slot.part = part;
+            slot.counters = counters;
+            slot.ready = true;
+        }
+        a = slot;
     }
     // As many splits as fit the fixed partials (and no more than the positions need).
     int chunk = 64;

@@ -17,6 +17,8 @@
 // step s + D are issued while step s is multiplied, and row-block epilogues run in the stream. The
 // first D steps are issued before griddepcontrol.wait -- weights never depend on the previous kernel
 // -- so under programmatic dependent launch the weight stream starts while the producer of x drains.
+#include <climits>
+#include <cstdlib>
 #include <cooperative_groups.h>
 #include <cstring>
 
@@ -1029,35 +1031,51 @@ __device__ __forceinline__ void bulk_copy(void* dst, const void* src, uint32_t b
                  : "memory");
 }
 
-// Activations staged as hi/lo pairs (bytes) and the tile ring for K and `stages`.
+// Activations staged as hi/lo pairs (bytes) and the ring of `stages` units of 16 rows x KS bytes.
 __host__ __device__ inline size_t bulk_xs_bytes(int K) { return (static_cast<size_t>(K) * 4 + 1023) & ~static_cast<size_t>(1023); }
-inline size_t bulk_smem_bytes(int K, int stages) {
-    return 1024 + bulk_xs_bytes(K) + static_cast<size_t>(stages) * 16 * K + 2 * kBulkMaxStages * 8;
+inline size_t bulk_smem_bytes(int K, int stages, int KS) {
+    return 1024 + bulk_xs_bytes(K) + static_cast<size_t>(stages) * 16 * KS + 2 * kBulkMaxStages * 8;
 }
-inline int bulk_stages(int K) {
+inline int bulk_stages(int K, int KS) {
     for (int s = kBulkMaxStages; s >= 2; --s)
-        if (bulk_smem_bytes(K, s) <= static_cast<size_t>(kBulkSmemBudget)) return s;
+        if (bulk_smem_bytes(K, s, KS) <= static_cast<size_t>(kBulkSmemBudget)) return s;
     return 0;
 }
 
+// Split-K units (p.ksplit = S > 1, for projections with few row tiles: o_proj, down, q/k/v): a unit is
+// the 16 rows of a tile times one S-th of K (16 row copies of K/S bytes into one stage), units are taken
+// in (tile, segment) order, and each CTA a contiguous range of them, so the work per SM differs by at most
+// one unit. A warp keeps its sums across the segments of a tile in registers; at the end of the tile (or
+// of the CTA's range) the warps' sums meet once. A tile whose segments two CTAs share (the host keeps
+// every range at least S - 1 units long, so never more than two) is finished by the second CTA to get
+// there: each writes its 16 partial sums to p.part[tile][first segment == 0 ? 0 : 1] and bumps
+// p.counters[tile]; the one that finds the other's partial adds the two (a + b == b + a: the result does
+// not depend on arrival order), runs the epilogue and re-arms the counter.
 __global__ void __launch_bounds__(kBulkThreads, 1) gemv_bulk_kernel(const GemvParams p, int stages, int* error) {
     extern __shared__ char bulk_smem[];
     constexpr int PE = 64, KU = 2, C2 = 2;  // int8: 64 k per piece, two 32-k units; B columns hi, lo
     __shared__ float2 red[2][kBulkCW][32];
     __shared__ float ssq_s[kBulkCW], amax_s[kBulkCW];
     __shared__ float oscale_s;
+    // After one timed-out wait the rest of the launch only drains: abort_s is set and units from
+    // issued_s on (never copied, or stuck) are not waited for, so the kernel returns after one timeout.
+    __shared__ int abort_s, issued_s;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
     const int N = p.N, K = p.K;
     const bool swiglu = p.epi == EPI_SWIGLU;
     const int half_n = N >> 1;
-    const int npieces = K / PE;
+    const int S = p.ksplit > 1 ? p.ksplit : 1;
+    const int KS = K / S;                 // k per unit (a multiple of PE)
+    const int npieces = K / PE;           // pieces of a whole row (x staging)
+    const int npu = KS / PE;              // pieces per unit
     const int ntiles = swiglu ? (half_n + 7) / 8 : (N + 15) / 16;
-    const int t_begin = static_cast<int>(static_cast<long long>(ntiles) * blockIdx.x / gridDim.x);
-    const int t_end = static_cast<int>(static_cast<long long>(ntiles) * (blockIdx.x + 1) / gridDim.x);
+    const int nunits = ntiles * S;
+    const int u_begin = static_cast<int>(static_cast<long long>(nunits) * blockIdx.x / gridDim.x);
+    const int u_end = static_cast<int>(static_cast<long long>(nunits) * (blockIdx.x + 1) / gridDim.x);
     char* const base = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(bulk_smem) + 1023) & ~uintptr_t(1023));
     char* xs = base;
     char* ring = base + bulk_xs_bytes(K);
-    const size_t stage_bytes = static_cast<size_t>(16) * K;
+    const size_t stage_bytes = static_cast<size_t>(16) * KS;
     uint64_t* full = reinterpret_cast<uint64_t*>(ring + stages * stage_bytes);
     uint64_t* empty = full + kBulkMaxStages;
     const char* W = static_cast<const char*>(p.w);
@@ -1069,20 +1087,27 @@ __global__ void __launch_bounds__(kBulkThreads, 1) gemv_bulk_kernel(const GemvPa
                          : "memory");
         }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        abort_s = 0;
+        issued_s = INT_MAX;
     }
     __syncthreads();
 
     if (warp == kBulkCW) {
-        // Producer: tile i's rows as one (SwiGLU: two) contiguous copies; rows past the matrix are not
-        // copied (their stage bytes are stale and their outputs are never stored).
+        // Producer: unit i's rows as one contiguous copy (S = 1; SwiGLU: two), or one copy per row of its
+        // segment (S > 1). Rows past the matrix are not copied (their stage bytes are stale and their
+        // outputs are never stored).
         if (lane == 0) {
-            for (int tile = t_begin, i = 0; tile < t_end; ++tile, ++i) {
+            for (int u = u_begin, i = 0; u < u_end; ++u, ++i) {
                 const int s = i % stages;
                 if (i >= stages && !bulk_wait(&empty[s], ((i / stages) & 1) ^ 1)) {
                     if (error) atomicExch(error, 1);
+                    atomicMin(&issued_s, i);
+                    __threadfence_block();
+                    atomicExch(&abort_s, 1);
                     break;
                 }
                 char* dst = ring + s * stage_bytes;
+                const int tile = u / S, seg = u - tile * S;
                 if (swiglu) {
                     const int r0 = tile * 8, nr = min(8, half_n - r0);
                     const uint32_t bytes = static_cast<uint32_t>(nr) * K;
@@ -1091,13 +1116,21 @@ __global__ void __launch_bounds__(kBulkThreads, 1) gemv_bulk_kernel(const GemvPa
                                  : "memory");
                     bulk_copy(dst, W + static_cast<long long>(r0) * K, bytes, &full[s]);
                     bulk_copy(dst + 8 * K, W + static_cast<long long>(half_n + r0) * K, bytes, &full[s]);
-                } else {
+                } else if (S == 1) {
                     const int r0 = tile * 16, nr = min(16, N - r0);
                     const uint32_t bytes = static_cast<uint32_t>(nr) * K;
                     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bulk_smem_u32(&full[s])),
                                  "r"(bytes)
                                  : "memory");
                     bulk_copy(dst, W + static_cast<long long>(r0) * K, bytes, &full[s]);
+                } else {
+                    const int r0 = tile * 16, nr = min(16, N - r0);
+                    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bulk_smem_u32(&full[s])),
+                                 "r"(static_cast<uint32_t>(nr * KS))
+                                 : "memory");
+                    const char* src = W + static_cast<long long>(r0) * K + static_cast<long long>(seg) * KS;
+                    for (int r = 0; r < nr; ++r)
+                        bulk_copy(dst + r * KS, src + static_cast<long long>(r) * K, static_cast<uint32_t>(KS), &full[s]);
                 }
             }
         }
@@ -1189,12 +1222,10 @@ __global__ void __launch_bounds__(kBulkThreads, 1) gemv_bulk_kernel(const GemvPa
         v1 = swiglu ? v0 : r1 < N;
     };
     const __half* sc = static_cast<const __half*>(p.scales);
-    auto epilogue = [&](int tile, float y0, float y1, float s0, float s1) {
+    auto epilogue = [&](int tile, float y0, float y1) {
         int r0, r1;
         bool v0, v1;
         tile_rows2(tile, r0, r1, v0, v1);
-        y0 *= s0;
-        y1 *= s1;
         const bool live = t == 0;
         if (p.epi == EPI_ARGMAX) {
             unsigned long long key = 0;
@@ -1212,34 +1243,74 @@ __global__ void __launch_bounds__(kBulkThreads, 1) gemv_bulk_kernel(const GemvPa
             }
         }
     };
+    // A tile two CTAs share: publish this CTA's part; the second to arrive adds the other's and finishes.
+    auto fixup = [&](int tile, int slot, float y0, float y1) {
+        float* mine = p.part + (static_cast<long long>(tile) * 2 + slot) * 16;
+        if (t == 0) {
+            mine[g] = y0;
+            mine[g + 8] = y1;
+        }
+        __threadfence();
+        __syncwarp();
+        unsigned old = 0;
+        if (lane == 0) old = atomicAdd(p.counters + tile, 1u);
+        old = __shfl_sync(0xffffffffu, old, 0);
+        if (old == 0) return;
+        __threadfence();
+        const float* other = p.part + (static_cast<long long>(tile) * 2 + (slot ^ 1)) * 16;
+        if (t == 0) {
+            y0 += __ldcg(other + g);
+            y1 += __ldcg(other + g + 8);
+        }
+        if (lane == 0) p.counters[tile] = 0u;
+        epilogue(tile, y0, y1);
+    };
 
-    // This warp's pieces of every tile.
-    const int p0 = warp * npieces / kBulkCW, p1 = (warp + 1) * npieces / kBulkCW;
+    // This warp's pieces of every unit.
+    const int p0 = warp * npu / kBulkCW, p1 = (warp + 1) * npu / kBulkCW;
     const int col_off = g * 64 + t * 16;
     float sc0 = 0.f, sc1 = 0.f;  // the row scales of the tile this warp reduces next
-    for (int tile = t_begin, i = 0; tile < t_end; ++tile, ++i) {
+    float acc[4] = {0.f, 0.f, 0.f, 0.f}, acc2[4] = {0.f, 0.f, 0.f, 0.f};
+    int seg_first = 0;  // first segment of the current tile in this CTA's range
+    int j = 0;          // tiles finished by this CTA (reducer rotation, red[] buffer parity)
+    for (int u = u_begin, i = 0; u < u_end; ++u, ++i) {
         const int s = i % stages;
-        const bool reducer = warp == kBulkCW - 1 - (i & (kBulkCW - 1));
-        if (reducer) {
-            int r0, r1;
-            bool v0, v1;
-            tile_rows2(tile, r0, r1, v0, v1);
-            sc0 = v0 ? __half2float(sc[r0]) : 0.f;
-            sc1 = v1 ? __half2float(sc[r1]) : 0.f;
+        const int tile = u / S, seg = u - tile * S;
+        const bool first = i == 0 || seg == 0;
+        const bool last = u + 1 == u_end || seg == S - 1;
+        const bool reducer = warp == kBulkCW - 1 - (j & (kBulkCW - 1));
+        if (first) {
+            seg_first = seg;
+#pragma unroll
+            for (int e = 0; e < 4; ++e) acc[e] = acc2[e] = 0.f;
+            if (reducer) {
+                int r0, r1;
+                bool v0, v1;
+                tile_rows2(tile, r0, r1, v0, v1);
+                sc0 = v0 ? __half2float(sc[r0]) : 0.f;
+                sc1 = v1 ? __half2float(sc[r1]) : 0.f;
+            }
         }
-        if (!bulk_wait(&full[s], (i / stages) & 1) && lane == 0 && error) atomicExch(error, 1);
+        // Units issued before an abort are still waited for (their copies land in this CTA's memory).
+        const bool skip = *reinterpret_cast<volatile int*>(&abort_s) && i >= *reinterpret_cast<volatile int*>(&issued_s);
+        if (!skip && !bulk_wait(&full[s], (i / stages) & 1) && lane == 0) {
+            if (error) atomicExch(error, 1);
+            atomicMin(&issued_s, i);
+            __threadfence_block();
+            atomicExch(&abort_s, 1);
+        }
         const char* st = ring + s * stage_bytes + t * 16;
-        float acc[4] = {0.f, 0.f, 0.f, 0.f}, acc2[4] = {0.f, 0.f, 0.f, 0.f};
+        const int xpiece0 = seg * npu;  // this unit's first piece in the staged activations
         for (int piece = p0; piece < p1; ++piece) {
-            const uint4 w0 = *reinterpret_cast<const uint4*>(st + static_cast<size_t>(g) * K + piece * PE);
-            const uint4 w1 = *reinterpret_cast<const uint4*>(st + static_cast<size_t>(g + 8) * K + piece * PE);
-            const char* ub = xs + static_cast<size_t>(piece * KU) * C2 * 64 + col_off;
+            const uint4 w0 = *reinterpret_cast<const uint4*>(st + static_cast<size_t>(g) * KS + piece * PE);
+            const uint4 w1 = *reinterpret_cast<const uint4*>(st + static_cast<size_t>(g + 8) * KS + piece * PE);
+            const char* ub = xs + static_cast<size_t>((xpiece0 + piece) * KU) * C2 * 64 + col_off;
             uint32_t b[8];
 #pragma unroll
-            for (int j = 0; j < KU; ++j) {
+            for (int jj = 0; jj < KU; ++jj) {
                 uint4 q = make_uint4(0, 0, 0, 0);
-                if (g < C2) q = *reinterpret_cast<const uint4*>(ub + static_cast<size_t>(j) * C2 * 64);
-                b[4 * j] = q.x, b[4 * j + 1] = q.y, b[4 * j + 2] = q.z, b[4 * j + 3] = q.w;
+                if (g < C2) q = *reinterpret_cast<const uint4*>(ub + static_cast<size_t>(jj) * C2 * 64);
+                b[4 * jj] = q.x, b[4 * jj + 1] = q.y, b[4 * jj + 2] = q.z, b[4 * jj + 3] = q.w;
             }
 #pragma unroll
             for (int jj = 0; jj < 4; ++jj) {
@@ -1250,40 +1321,71 @@ __global__ void __launch_bounds__(kBulkThreads, 1) gemv_bulk_kernel(const GemvPa
                 mma_16816((jj & 1) ? acc2 : acc, a0, a1, a2, a3, b[2 * jj], b[2 * jj + 1], false);
             }
         }
-#pragma unroll
-        for (int e = 0; e < 4; ++e) acc[e] += acc2[e];
         __syncwarp();
         if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bulk_smem_u32(&empty[s])) : "memory");
-        red[i & 1][warp][lane] = make_float2(acc[0] + acc[1], acc[2] + acc[3]);
+        if (!last) continue;
+        red[j & 1][warp][lane] = make_float2(acc[0] + acc[1] + acc2[0] + acc2[1], acc[2] + acc[3] + acc2[2] + acc2[3]);
         bulk_consumer_sync();
-        // Tile i's partials are complete; its reducer sums them while the other warps go on (the next
-        // write to red[i & 1] comes after the next barrier, which the reducer reaches only when done).
+        // Tile j's partials are complete; its reducer sums them while the other warps go on (the next
+        // write to red[j & 1] comes after the next barrier, which the reducer reaches only when done).
         if (reducer) {
             float y0 = 0.f, y1 = 0.f;
 #pragma unroll
             for (int w = 0; w < kBulkCW; ++w) {
-                y0 += red[i & 1][w][lane].x;
-                y1 += red[i & 1][w][lane].y;
+                y0 += red[j & 1][w][lane].x;
+                y1 += red[j & 1][w][lane].y;
             }
-            epilogue(tile, y0 * oscale_s, y1 * oscale_s, sc0, sc1);
+            y0 *= oscale_s * sc0;
+            y1 *= oscale_s * sc1;
+            if (seg_first == 0 && seg == S - 1) epilogue(tile, y0, y1);
+            else fixup(tile, seg_first == 0 ? 0 : 1, y0, y1);
         }
+        ++j;
     }
 }
 
-// One activation row, int8 with one scale per row, 16-byte aligned; at least two whole-tile stages in
-// shared memory beside the staged activations, and at least 8 tiles per SM (whole tiles per CTA).
+// Split count of the one-row bulk GEMV: 1 (whole 16-row tiles per CTA) when there are at least 8 tiles
+// per SM. Otherwise S > 1 dividing K's 64-k pieces such that a unit keeps >= 3 stages in shared memory,
+// >= 8 pieces and >= 512 bytes per row copy, and every CTA's range is >= S - 1 units long (a tile then
+// spans at most two CTAs): the smallest such S giving every SM >= 6 units, else the largest giving >= 2;
+// 0 = no bulk GEMV.
+int bulk_split(const GemvParams& p, int sm_count) {
+    const int ntiles = p.epi == EPI_SWIGLU ? (p.N / 2 + 7) / 8 : (p.N + 15) / 16;
+    if (ntiles >= 8 * sm_count) return bulk_stages(p.K, p.K) >= 2 ? 1 : 0;
+    if (p.epi == EPI_SWIGLU || !p.part || !p.counters || p.counter_count < ntiles) return 0;
+    const int npieces = p.K / 64;
+    static const int forced = [] {
+        const char* e = getenv("L0B_BULK_SPLIT");
+        return e ? atoi(e) : -1;
+    }();
+    int best = 0;
+    for (int S = 2; S <= 32; ++S) {
+        if (npieces % S != 0) continue;
+        const int KS = p.K / S;
+        const long long units = static_cast<long long>(ntiles) * S;
+        if (npieces / S < 8 || KS < 512) break;
+        if (bulk_stages(p.K, KS) < 3 || units / sm_count < S - 1 || units < 2LL * sm_count) continue;
+        if (forced >= 0) {
+            if (S == forced) return S;
+            continue;
+        }
+        best = S;
+        if (units >= 6LL * sm_count) return S;
+    }
+    return forced >= 0 ? 0 : best;
+}
+
+// One activation row, int8 with one scale per row, 16-byte aligned, and a split (above) that applies.
 bool bulk_applies(int w_dtype, const GemvParams& p, int sm_count) {
     if (!g_gemv_mma || !g_gemv_bulk || w_dtype != L0B_I8 || p.M != 1 || p.nseg < 1) return false;
     if (p.group < p.K || p.K % 64 != 0) return false;
     if (reinterpret_cast<uintptr_t>(p.w) % 16 != 0 || (p.x_dtype == L0B_F32 && (reinterpret_cast<uintptr_t>(p.x) & 15)))
         return false;
     if (p.norm_w && (reinterpret_cast<uintptr_t>(p.norm_w) & 15)) return false;
-    if (bulk_stages(p.K) < 2) return false;
-    const int ntiles = p.epi == EPI_SWIGLU ? (p.N / 2 + 7) / 8 : (p.N + 15) / 16;
-    return ntiles >= 8 * sm_count;
+    return bulk_split(p, sm_count) > 0;
 }
 
-l0b_status launch_bulk(l0b_device* dev, cudaStream_t stream, int sm_count, const GemvParams& p) {
+l0b_status launch_bulk(l0b_device* dev, cudaStream_t stream, int sm_count, GemvParams p) {
     static bool configured = false;
     if (!configured) {
         cudaError_t e = cudaFuncSetAttribute(gemv_bulk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -1291,8 +1393,10 @@ l0b_status launch_bulk(l0b_device* dev, cudaStream_t stream, int sm_count, const
         if (e != cudaSuccess) return fail(L0B_ERR_CUDA, "cudaFuncSetAttribute failed: %s", cudaGetErrorString(e));
         configured = true;
     }
-    const int stages = bulk_stages(p.K);
-    const size_t smem = bulk_smem_bytes(p.K, stages);
+    p.ksplit = bulk_split(p, sm_count);
+    const int KS = p.K / p.ksplit;
+    const int stages = bulk_stages(p.K, KS);
+    const size_t smem = bulk_smem_bytes(p.K, stages, KS);
     int* err = dev ? dev->error_flag : nullptr;
     return launch_on(dev, stream, gemv_bulk_kernel, dim3(sm_count), dim3(kBulkThreads), smem, p, stages, err);
 }

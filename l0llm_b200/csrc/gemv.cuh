@@ -38,6 +38,13 @@ struct GemvParams {
     int argmax_base;             // index of W's row 0 in the argmax (vocab shard offset under TP)
     int kt;                      // K elements per shared-memory tile (a multiple of 512)
     int prefetch;                // prefetch the first row block of weights into L2 before pdl_wait
+    // Split-K scratch of the one-row bulk GEMV (null: no split): part >= 32 floats per 16-row tile,
+    // counters >= one per tile, zero at rest (every launch leaves them zero). ksplit is set by the
+    // dispatcher.
+    float* part;
+    unsigned* counters;
+    int counter_count;
+    int ksplit;
 };
 
 // Launches y = x * W^T with the fused options in `p` (fills kt and the grid). `w_dtype` is

@@ -328,6 +328,16 @@ GemvParams linear_params(const ModelMatrix& w, int m_rows, const void* x, long l
     return p;
 }
 
+// The model's split-K scratch (shared with the tensor-core GEMM: kernels on the stream run in order and
+// every user leaves the counters at zero).
+GemvParams model_linear_params(const l0b_model* m, const ModelMatrix& w, int m_rows, const void* x, long long x_ld) {
+    GemvParams p = linear_params(w, m_rows, x, x_ld);
+    p.part = m->tc_part;
+    p.counters = m->tc_counters;
+    p.counter_count = m->tc_counters ? kTcCounters : 0;
+    return p;
+}
+
 // Projections over many rows (prefill chunks) run on the tcgen05 GEMM, which reads the weights once; the
 // f32 activations go in as hi + lo 16-bit halves so the products keep about the precision of the
 // f32-activation GEMV. int8 weights qualify with one scale per row (exact f16 integers times the row
@@ -398,7 +408,7 @@ l0b_status record_layer_fused(l0b_model* m, int li, int rows, bool decode, int p
     ModelLayer& L = m->layers[li];
     const l0b_model_config& c = m->cfg;
     // 1. QKV projection with the input RMSNorm prologue and the bias epilogue.
-    GemvParams p = linear_params(L.qkv, rows, m->hidden, m->h);
+    GemvParams p = model_linear_params(m, L.qkv, rows, m->hidden, m->h);
     p.norm_w = L.in_norm;
     p.eps = c.rms_norm_eps;
     p.seg[0] = {m->qkv, L.qkv_bias, m->qkv_w, m->qkv_w};
@@ -449,7 +459,7 @@ l0b_status record_layer_fused(l0b_model* m, int li, int rows, bool decode, int p
         L0B_TRY(attention_launch(m->dev, a, rows));
     }
     // 3. o_proj, added into the residual stream (under TP: this rank's partial, summed over ranks).
-    p = linear_params(L.o, rows, m->attn, m->qdim);
+    p = model_linear_params(m, L.o, rows, m->attn, m->qdim);
     if (m->comm) {
         L0B_TRY(project_into_residual(m, L.o, p, rows));
     } else {
@@ -458,14 +468,14 @@ l0b_status record_layer_fused(l0b_model* m, int li, int rows, bool decode, int p
         L0B_TRY(gemv(m, L.o, p));
     }
     // 4. gate/up with the post-attention RMSNorm prologue and the SwiGLU epilogue.
-    p = linear_params(L.gate_up, rows, m->hidden, m->h);
+    p = model_linear_params(m, L.gate_up, rows, m->hidden, m->h);
     p.norm_w = L.post_norm;
     p.eps = c.rms_norm_eps;
     p.epi = EPI_SWIGLU;
     p.seg[0] = {m->act, nullptr, m->inter, m->inter};
     L0B_TRY(gemv(m, L.gate_up, p));
     // 5. down, added into the residual stream.
-    p = linear_params(L.down, rows, m->act, m->inter);
+    p = model_linear_params(m, L.down, rows, m->act, m->inter);
     if (m->comm) return project_into_residual(m, L.down, p, rows);
     p.epi = EPI_ACCUM;
     p.seg[0] = {m->hidden, nullptr, m->h, m->h};
@@ -479,7 +489,7 @@ l0b_status record_layer_reference(l0b_model* m, int li, int rows, bool decode, i
     l0b_device* d = m->dev;
     L0B_TRY(k_rmsnorm(d, m->hidden, nullptr, L.in_norm, m->normed, c.rms_norm_eps, m->h, rows, 0));
     L0B_TRY(emit(m, li, "input_norm", m->normed, m->h));
-    GemvParams p = linear_params(L.qkv, rows, m->normed, m->h);
+    GemvParams p = model_linear_params(m, L.qkv, rows, m->normed, m->h);
     p.nseg = 3;
     p.seg[0] = {m->qb, nullptr, m->qdim, m->qdim};
     p.seg[1] = {m->kb, nullptr, m->qdim + m->kvdim, m->kvdim};
@@ -526,20 +536,20 @@ l0b_status record_layer_reference(l0b_model* m, int li, int rows, bool decode, i
         a.max_splits = 1;
         L0B_TRY(attention_launch(d, a, rows));
     }
-    p = linear_params(L.o, rows, m->attn, m->qdim);
+    p = model_linear_params(m, L.o, rows, m->attn, m->qdim);
     p.seg[0] = {m->attn_proj, nullptr, m->h, m->h};
     L0B_TRY(gemv(m, L.o, p));
     if (m->comm) L0B_TRY(comm_allreduce(m->comm, m->attn_proj, static_cast<size_t>(rows) * m->h, L0B_F32, COLL_SUM));
     L0B_TRY(emit(m, li, "attn_out", m->attn_proj, m->h));
     L0B_TRY(k_rmsnorm(d, m->hidden, m->attn_proj, L.post_norm, m->normed, c.rms_norm_eps, m->h, rows, 1));
     L0B_TRY(emit(m, li, "post_norm", m->normed, m->h));
-    p = linear_params(L.gate_up, rows, m->normed, m->h);
+    p = model_linear_params(m, L.gate_up, rows, m->normed, m->h);
     p.nseg = 2;
     p.seg[0] = {m->gate, nullptr, m->inter, m->inter};
     p.seg[1] = {m->up, nullptr, 2 * m->inter, m->inter};
     L0B_TRY(gemv(m, L.gate_up, p));
     L0B_TRY(k_swiglu(d, m->gate, m->up, static_cast<long long>(rows) * m->inter));
-    p = linear_params(L.down, rows, m->gate, m->inter);
+    p = model_linear_params(m, L.down, rows, m->gate, m->inter);
     p.seg[0] = {m->down, nullptr, m->h, m->h};
     L0B_TRY(gemv(m, L.down, p));
     if (m->comm) L0B_TRY(comm_allreduce(m->comm, m->down, static_cast<size_t>(rows) * m->h, L0B_F32, COLL_SUM));
@@ -554,7 +564,7 @@ l0b_status record_head(l0b_model* m, int row0, int rows, int advance, int seq0 =
     const l0b_model_config& c = m->cfg;
     l0b_device* d = m->dev;
     if (m->fused && !m->probe) {
-        GemvParams p = linear_params(m->lm_head, rows, m->hidden + static_cast<long long>(row0) * m->h, m->h);
+        GemvParams p = model_linear_params(m, m->lm_head, rows, m->hidden + static_cast<long long>(row0) * m->h, m->h);
         p.norm_w = m->final_norm;
         p.eps = c.rms_norm_eps;
         p.epi = EPI_ARGMAX;
@@ -571,7 +581,7 @@ l0b_status record_head(l0b_model* m, int row0, int rows, int advance, int seq0 =
             src = m->head_in;
         }
         L0B_TRY(k_rmsnorm(d, const_cast<float*>(src), nullptr, m->final_norm, m->normed, c.rms_norm_eps, m->h, rows, 0));
-        GemvParams p = linear_params(m->lm_head, rows, m->normed, m->h);
+        GemvParams p = model_linear_params(m, m->lm_head, rows, m->normed, m->h);
         p.epi = EPI_ARGMAX;
         p.argmax = m->keys + seq0;
         p.argmax_base = m->tp_rank * m->vocab;
@@ -641,14 +651,24 @@ l0b_status run_recorded(l0b_model* m, Body body, bool wait = true) {
     return L0B_OK;
 }
 
+// Tokens and positions of sequences 0..rows-1 to the device. Only those rows are copied: the other
+// sequences keep their device-side token and position (a batched device decode continues from them).
 l0b_status write_io(l0b_model* m, int rows, const int* tokens, const int* positions) {
     for (int b = 0; b < rows; ++b) {
         m->host_io[b] = tokens[b];
         m->host_io[m->batch_cap + b] = positions[b];
     }
-    L0B_CHECK_CUDA(cudaMemcpyAsync(m->io, m->host_io, sizeof(int) * 2 * m->batch_cap, cudaMemcpyHostToDevice,
+    L0B_CHECK_CUDA(cudaMemcpyAsync(m->tok, m->host_io, sizeof(int) * rows, cudaMemcpyHostToDevice, m->dev->stream));
+    L0B_CHECK_CUDA(cudaMemcpyAsync(m->pos, m->host_io + m->batch_cap, sizeof(int) * rows, cudaMemcpyHostToDevice,
                                    m->dev->stream));
     return L0B_OK;
+}
+
+// Sequence 0's length: the single-sequence calls keep it in `position`, the batched ones in seq_pos[0].
+// Every change goes through here so the two never drift apart.
+void set_position0(l0b_model* m, int position) {
+    m->position = position;
+    m->seq_pos[0] = position;
 }
 
 l0b_status read_logits(l0b_model* m, float* out, int rows) {
@@ -1200,9 +1220,9 @@ L0B_API l0b_status l0b_model_prefill(l0b_model* m, const int32_t* ids, int32_t c
     L0B_REQUIRE(count > 0, L0B_ERR_ARGUMENT, "The prompt must contain at least one token.");
     L0B_REQUIRE(count <= m->max_seq, L0B_ERR_ARGUMENT, "Prompt of %d tokens exceeds the %d-token cache.", count,
                 m->max_seq);
-    m->position = 0;
+    set_position0(m, 0);
     L0B_TRY(ingest_prompt(m, ids, count));
-    m->position = count;
+    set_position0(m, count);
     return read_logits(m, logits, 1);
     GUARD_END
 }
@@ -1212,7 +1232,7 @@ L0B_API l0b_status l0b_model_decode(l0b_model* m, int32_t token, float* logits) 
     L0B_REQUIRE(m, L0B_ERR_ARGUMENT, "model is null");
     L0B_REQUIRE(m->position < m->max_seq, L0B_ERR_INVALID_OPERATION, "The %d-token KV cache is full.", m->max_seq);
     L0B_TRY(step(m, token, m->position));
-    m->position += 1;
+    set_position0(m, m->position + 1);
     return read_logits(m, logits, 1);
     GUARD_END
 }
@@ -1337,7 +1357,7 @@ L0B_API l0b_status l0b_model_decode_greedy_device(l0b_model* m, int32_t steps, i
         }
         L0B_TRY(d->end_recording());
     }
-    m->position += steps;
+    set_position0(m, m->position + steps);
     if (out) {
         L0B_CHECK_CUDA(cudaMemcpyAsync(out, m->out_tokens, sizeof(int) * steps, cudaMemcpyDeviceToHost, d->stream));
     }
@@ -1356,7 +1376,7 @@ L0B_API l0b_status l0b_model_prefill_sequence(l0b_model* m, int32_t seq, const i
     L0B_REQUIRE(count <= m->max_seq, L0B_ERR_ARGUMENT, "Prompt of %d tokens exceeds the %d-token cache.", count,
                 m->max_seq);
     L0B_TRY(ingest_prompt(m, ids, count, seq));
-    if (seq == 0) m->position = count;
+    if (seq == 0) set_position0(m, count);
     return read_logits(m, logits, 1);
     GUARD_END
 }
@@ -1377,7 +1397,7 @@ L0B_API l0b_status l0b_model_decode_batch(l0b_model* m, const int32_t* tokens, c
     L0B_TRY(write_io(m, count, tokens, positions));
     L0B_TRY(run_recorded(m, [&] { return record_decode_step(m, count); }));
     for (int b = 0; b < count; ++b) m->seq_pos[b] = positions[b] + 1;
-    if (count >= 1) m->position = positions[0] + 1;
+    set_position0(m, positions[0] + 1);
     return read_logits(m, logits, count);
     GUARD_END
 }
@@ -1408,7 +1428,7 @@ L0B_API l0b_status l0b_model_decode_greedy_device_batch(l0b_model* m, int32_t st
         L0B_TRY(d->end_recording());
     }
     for (int b = 0; b < count; ++b) m->seq_pos[b] += steps;
-    m->position = m->seq_pos[0];
+    set_position0(m, m->seq_pos[0]);
     if (out) {
         L0B_CHECK_CUDA(cudaMemcpyAsync(out, m->out_tokens, sizeof(int) * steps * count, cudaMemcpyDeviceToHost,
                                        d->stream));
@@ -1436,8 +1456,7 @@ L0B_API l0b_status l0b_model_fork_sequence(l0b_model* m, int32_t src, int32_t ds
     L0B_REQUIRE(src >= 0 && src < m->batch_cap && dst >= 0 && dst < m->batch_cap, L0B_ERR_OUT_OF_RANGE,
                 "sequences %d -> %d outside the %d-sequence batch", src, dst, m->batch_cap);
     L0B_REQUIRE(src != dst, L0B_ERR_ARGUMENT, "a sequence cannot be forked onto itself");
-    // Sequence 0's length is kept by the single-sequence calls in `position`.
-    const int length = src == 0 ? m->position : m->seq_pos[src];
+    const int length = m->seq_pos[src];
     L0B_REQUIRE(base_position >= 0 && base_position <= length, L0B_ERR_OUT_OF_RANGE,
                 "base position %d outside [0, %d]", base_position, length);
     l0b_device* d = m->dev;
@@ -1458,7 +1477,7 @@ L0B_API l0b_status l0b_model_fork_sequence(l0b_model* m, int32_t src, int32_t ds
     L0B_CHECK_CUDA(cudaMemcpyAsync(m->pos + dst, m->pos + src, sizeof(int), cudaMemcpyDeviceToDevice, d->stream));
     L0B_CHECK_CUDA(cudaMemcpyAsync(m->sampled + dst, m->sampled + src, sizeof(int), cudaMemcpyDeviceToDevice, d->stream));
     m->seq_pos[dst] = length;
-    if (dst == 0) m->position = length;
+    if (dst == 0) set_position0(m, length);
     return L0B_OK;
     GUARD_END
 }
@@ -1471,7 +1490,7 @@ L0B_API l0b_status l0b_model_position(l0b_model* m, int32_t* position) {
 
 L0B_API l0b_status l0b_model_reset_sequence(l0b_model* m) {
     L0B_REQUIRE(m, L0B_ERR_ARGUMENT, "model is null");
-    m->position = 0;
+    set_position0(m, 0);
     return L0B_OK;
 }
 

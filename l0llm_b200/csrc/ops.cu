@@ -40,6 +40,8 @@ l0b_suite::~l0b_suite() {
     for (auto& kv : rope_tables) cudaFree(kv.second);
     if (q8_x) cudaFree(q8_x);
     if (error_flag) cudaFree(error_flag);
+    if (split_part) cudaFree(split_part);
+    if (split_counters) cudaFree(split_counters);
 }
 
 namespace {
@@ -93,6 +95,9 @@ L0B_API l0b_status l0b_suite_create(l0b_device* dev, l0b_suite** out) {
     L0B_CHECK_CUDA(cudaSetDevice(dev->index));
     L0B_CHECK_CUDA(cudaMalloc(&s->error_flag, sizeof(int)));
     L0B_CHECK_CUDA(cudaMemsetAsync(s->error_flag, 0, sizeof(int), dev->stream));
+    L0B_CHECK_CUDA(cudaMalloc(&s->split_part, sizeof(float) * 32 * kSuiteSplitTiles));
+    L0B_CHECK_CUDA(cudaMalloc(&s->split_counters, sizeof(unsigned) * kSuiteSplitTiles));
+    L0B_CHECK_CUDA(cudaMemsetAsync(s->split_counters, 0, sizeof(unsigned) * kSuiteSplitTiles, dev->stream));
     L0B_CHECK_CUDA(cudaStreamSynchronize(dev->stream));
     *out = s.release();
     return L0B_OK;
@@ -273,6 +278,9 @@ static l0b_status q8_exec(l0b_suite* s, l0b_device* d, int32_t m, int32_t n, int
     p.seg[0].row_end = n;
     p.seg[0].ld = n;
     p.prefetch = 1;
+    p.part = s->split_part;
+    p.counters = s->split_counters;
+    p.counter_count = kSuiteSplitTiles;
     return gemv_nk_launch(d, L0B_I8, p);
 }
 
@@ -516,6 +524,9 @@ L0B_API l0b_status l0b_linear(l0b_suite* s, l0b_device* d, int32_t m, int32_t n,
     p.seg[0].row_end = n;
     p.seg[0].ld = n;
     p.prefetch = 1;
+    p.part = s->split_part;
+    p.counters = s->split_counters;
+    p.counter_count = kSuiteSplitTiles;
     return gemv_nk_launch(d, wdt, p);
 }
 
@@ -562,6 +573,9 @@ L0B_API l0b_status l0b_linear_fused(l0b_suite* s, l0b_device* d, int32_t m, int3
     p.seg[0].row_end = out_cols;
     p.seg[0].ld = out_cols;
     p.prefetch = 1;
+    p.part = s->split_part;
+    p.counters = s->split_counters;
+    p.counter_count = kSuiteSplitTiles;
     return gemv_nk_launch(d, wdt, p);
 }
 

@@ -9,6 +9,8 @@
 namespace l0b {
 // LlmGemvKernel.MaxRows: rows per ExecuteRows call and per prefill chunk of the model.
 constexpr int kMaxRows = 64;
+// 16-row tiles the suite's split-K GEMV scratch covers (N <= 65536 output rows).
+constexpr int kSuiteSplitTiles = 4096;
 }  // namespace l0b
 
 struct l0b_suite {
@@ -18,6 +20,9 @@ struct l0b_suite {
     int q8_width = 0;
     int q8_k = 0;
     int* error_flag = nullptr;  // set by kernels that meet an out-of-range index (embedding ids)
+    // Split-K scratch of the one-row bulk GEMV (l0b::kSuiteSplitTiles tiles), counters zero at rest.
+    float* split_part = nullptr;
+    unsigned* split_counters = nullptr;
     std::map<std::pair<int, double>, float*> rope_tables;
     ~l0b_suite();
 };

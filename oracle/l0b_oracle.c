@@ -5,6 +5,7 @@
  */
 #include "l0b_oracle.h"
 
+#include <immintrin.h>
 #include <math.h>
 #include <stdio.h>
 #include <stdlib.h>
@@ -164,6 +165,123 @@ void orc_gemv_in_out(int M, int N, int K, const float* x, int w_is_half, const v
             }
             y[(int64_t)m * N + n] = (float)acc;
         }
+}
+
+/* Timing build of orc_gemv_out_in: the same products accumulated in fp32 with fused multiply-adds in
+ * eight AVX2 lanes per (row, token) pair (each lane sums K/8 products; the lanes meet in double), two
+ * weight rows x up to six activation rows per register block, activation rows in blocks of 24 so a
+ * block stays in the core's L2 while the weights stream. Relative error ~sqrt(K/8) * 2^-24 per output
+ * (about 1e-6 at K = 18944), far below the 1e-2 parity tolerance. */
+#define ORC_RB 2
+#define ORC_TB 6
+#define ORC_TBIG 24
+
+static inline __attribute__((always_inline)) __m256 ld8w(const void* w, int dt, int64_t i) {
+    if (dt == ORC_I8) return _mm256_cvtepi32_ps(_mm256_cvtepi8_epi32(_mm_loadl_epi64((const __m128i*)((const int8_t*)w + i))));
+    if (dt == ORC_F16) return _mm256_cvtph_ps(_mm_loadu_si128((const __m128i*)((const uint16_t*)w + i)));
+    if (dt == ORC_BF16)
+        return _mm256_castsi256_ps(
+            _mm256_slli_epi32(_mm256_cvtepu16_epi32(_mm_loadu_si128((const __m128i*)((const uint16_t*)w + i))), 16));
+    return _mm256_loadu_ps((const float*)w + i);
+}
+
+static inline double hsum8(__m256 v) {
+    const __m256d a = _mm256_add_pd(_mm256_cvtps_pd(_mm256_castps256_ps128(v)), _mm256_cvtps_pd(_mm256_extractf128_ps(v, 1)));
+    const __m128d s = _mm_add_pd(_mm256_castpd256_pd128(a), _mm256_extractf128_pd(a, 1));
+    return _mm_cvtsd_f64(_mm_add_sd(s, _mm_unpackhi_pd(s, s)));
+}
+
+/* Rows n0 and n1 (n1 may repeat n0 when N is odd; its result is then not stored) x tokens [t0, t0 + tb). */
+static inline __attribute__((always_inline)) void fast_block(int dt, int K, int group, const void* w,
+                                                             const uint16_t* sc, int n0, int n1, int store1,
+                                                             const float* x, int t0, int tb, int N, float* y) {
+    __m256 acc[ORC_RB][ORC_TB];
+    double tail[ORC_RB][ORC_TB];
+    for (int r = 0; r < ORC_RB; ++r)
+        for (int t = 0; t < tb; ++t) {
+            acc[r][t] = _mm256_setzero_ps();
+            tail[r][t] = 0.0;
+        }
+    const int64_t w0 = (int64_t)n0 * K, w1 = (int64_t)n1 * K;
+    const int grouped = dt == ORC_I8 && group < K;
+    const int kv = K & ~7;
+    if (!grouped) {
+        for (int k = 0; k < kv; k += 8) {
+            const __m256 a0 = ld8w(w, dt, w0 + k), a1 = ld8w(w, dt, w1 + k);
+            for (int t = 0; t < tb; ++t) {
+                const __m256 xv = _mm256_loadu_ps(x + (int64_t)(t0 + t) * K + k);
+                acc[0][t] = _mm256_fmadd_ps(a0, xv, acc[0][t]);
+                acc[1][t] = _mm256_fmadd_ps(a1, xv, acc[1][t]);
+            }
+        }
+        for (int k = kv; k < K; ++k)
+            for (int t = 0; t < tb; ++t) {
+                const double xv = x[(int64_t)(t0 + t) * K + k];
+                tail[0][t] += (double)load_elem(w, dt, w0 + k) * xv;
+                tail[1][t] += (double)load_elem(w, dt, w1 + k) * xv;
+            }
+        const double s0 = dt == ORC_I8 ? (double)orc_f16_to_f32(sc[n0]) : 1.0;
+        const double s1 = dt == ORC_I8 ? (double)orc_f16_to_f32(sc[n1]) : 1.0;
+        for (int t = 0; t < tb; ++t) {
+            y[(int64_t)(t0 + t) * N + n0] = (float)((hsum8(acc[0][t]) + tail[0][t]) * s0);
+            if (store1) y[(int64_t)(t0 + t) * N + n1] = (float)((hsum8(acc[1][t]) + tail[1][t]) * s1);
+        }
+        return;
+    }
+    /* int8 with group-wise scales (group a multiple of 8): each group's partial sum times its scale. */
+    const int gpr = K / group;
+    for (int g = 0; g < gpr; ++g) {
+        __m256 part[ORC_RB][ORC_TB];
+        for (int r = 0; r < ORC_RB; ++r)
+            for (int t = 0; t < tb; ++t) part[r][t] = _mm256_setzero_ps();
+        for (int k = g * group; k < (g + 1) * group; k += 8) {
+            const __m256 a0 = ld8w(w, dt, w0 + k), a1 = ld8w(w, dt, w1 + k);
+            for (int t = 0; t < tb; ++t) {
+                const __m256 xv = _mm256_loadu_ps(x + (int64_t)(t0 + t) * K + k);
+                part[0][t] = _mm256_fmadd_ps(a0, xv, part[0][t]);
+                part[1][t] = _mm256_fmadd_ps(a1, xv, part[1][t]);
+            }
+        }
+        const __m256 s0 = _mm256_set1_ps(orc_f16_to_f32(sc[(int64_t)n0 * gpr + g]));
+        const __m256 s1 = _mm256_set1_ps(orc_f16_to_f32(sc[(int64_t)n1 * gpr + g]));
+        for (int t = 0; t < tb; ++t) {
+            acc[0][t] = _mm256_fmadd_ps(part[0][t], s0, acc[0][t]);
+            acc[1][t] = _mm256_fmadd_ps(part[1][t], s1, acc[1][t]);
+        }
+    }
+    for (int t = 0; t < tb; ++t) {
+        y[(int64_t)(t0 + t) * N + n0] = (float)hsum8(acc[0][t]);
+        if (store1) y[(int64_t)(t0 + t) * N + n1] = (float)hsum8(acc[1][t]);
+    }
+}
+
+static void fast_rows(int dt, int M, int N, int K, const float* x, const void* w, const uint16_t* sc, int group,
+                      float* y) {
+    for (int m0 = 0; m0 < M; m0 += ORC_TBIG) {
+        const int mb = M - m0 < ORC_TBIG ? M - m0 : ORC_TBIG;
+#pragma omp parallel for schedule(static)
+        for (int np = 0; np < (N + 1) / 2; ++np) {
+            const int n0 = 2 * np, has1 = n0 + 1 < N, n1 = has1 ? n0 + 1 : n0;
+            int t = m0;
+            for (; t + ORC_TB <= m0 + mb; t += ORC_TB) fast_block(dt, K, group, w, sc, n0, n1, has1, x, t, ORC_TB, N, y);
+            for (; t < m0 + mb; ++t) fast_block(dt, K, group, w, sc, n0, n1, has1, x, t, 1, N, y);
+        }
+    }
+}
+
+void orc_gemm_fast(int M, int N, int K, const float* x, int wdtype, const void* w, const uint16_t* scales, int group,
+                   float* y) {
+    if (wdtype == ORC_I8 && group <= 0) group = K;
+    if (wdtype == ORC_I8 && group < K && group % 8 != 0) {
+        orc_gemv_out_in(M, N, K, x, wdtype, w, scales, group, y);
+        return;
+    }
+    switch (wdtype) {
+        case ORC_I8: fast_rows(ORC_I8, M, N, K, x, w, scales, group, y); break;
+        case ORC_F16: fast_rows(ORC_F16, M, N, K, x, w, scales, group, y); break;
+        case ORC_BF16: fast_rows(ORC_BF16, M, N, K, x, w, scales, group, y); break;
+        default: fast_rows(ORC_F32, M, N, K, x, w, scales, group, y); break;
+    }
 }
 
 void orc_q8_quantize(const float* w, int N, int K, int group, int8_t* q, uint16_t* scales) {
@@ -612,13 +730,16 @@ typedef struct {
 struct orc_model {
     orc_config c;
     int max_seq, qd, kvd, rot, layer_limit;
+    int batch;  /* sequences: KV caches are [batch, max_seq, kv_dim] */
+    int fast;   /* 1: projections on the fp32 timing GEMM (orc_gemm_fast); 0: double accumulation */
     float attn_scale;
     float* inv_freq;
     float* embed;
     float* final_norm;
     orc_mat lm_head;
     orc_layer* L;
-    /* scratch */
+    /* row scratch, [rows_cap, width] */
+    int rows_cap;
     float *hidden, *normed, *q, *k, *v, *attn, *proj, *gate, *up, *down;
     orc_probe_fn probe;
     void* probe_user;
@@ -653,15 +774,62 @@ static void mat_set_f32(orc_mat* m, const float* src) {
     else orc_convert(src, m->w, m->dtype, (int64_t)m->n * m->k);
 }
 
-static void mat_apply(const orc_mat* m, const float* x, float* y) {
-    orc_gemv_out_in(1, m->n, m->k, x, m->dtype, m->w, m->s, m->group, y);
+static void mat_apply_rows(const orc_model* om, const orc_mat* m, int rows, const float* x, float* y) {
+    if (om->fast) orc_gemm_fast(rows, m->n, m->k, x, m->dtype, m->w, m->s, m->group, y);
+    else orc_gemv_out_in(rows, m->n, m->k, x, m->dtype, m->w, m->s, m->group, y);
 }
 
-orc_model* orc_model_create(const orc_config* cfg, int max_seq) {
+static void free_rows(orc_model* m) {
+    free(m->hidden);
+    free(m->normed);
+    free(m->q);
+    free(m->k);
+    free(m->v);
+    free(m->attn);
+    free(m->proj);
+    free(m->gate);
+    free(m->up);
+    free(m->down);
+    m->hidden = m->normed = m->q = m->k = m->v = m->attn = m->proj = m->gate = m->up = m->down = NULL;
+    m->rows_cap = 0;
+}
+
+static int ensure_rows(orc_model* m, int rows) {
+    if (rows <= m->rows_cap) return 0;
+    free_rows(m);
+    const size_t r = (size_t)rows, H = (size_t)m->c.hidden, I = (size_t)m->c.inter;
+    m->hidden = (float*)calloc(r * H, sizeof(float));
+    m->normed = (float*)calloc(r * H, sizeof(float));
+    m->q = (float*)calloc(r * (size_t)m->qd, sizeof(float));
+    m->k = (float*)calloc(r * (size_t)m->kvd, sizeof(float));
+    m->v = (float*)calloc(r * (size_t)m->kvd, sizeof(float));
+    m->attn = (float*)calloc(r * (size_t)m->qd, sizeof(float));
+    m->proj = (float*)calloc(r * H, sizeof(float));
+    m->gate = (float*)calloc(r * I, sizeof(float));
+    m->up = (float*)calloc(r * I, sizeof(float));
+    m->down = (float*)calloc(r * H, sizeof(float));
+    if (!m->hidden || !m->normed || !m->q || !m->k || !m->v || !m->attn || !m->proj || !m->gate || !m->up || !m->down) {
+        free_rows(m);
+        return -1;
+    }
+    m->rows_cap = rows;
+    return 0;
+}
+
+/* KV cache rows of sequence `seq`. */
+static void* seq_cache(const orc_model* m, void* cache, int seq) {
+    return (char*)cache + (size_t)seq * m->max_seq * m->kvd * dtype_bytes(m->c.kv_dtype);
+}
+
+orc_model* orc_model_create(const orc_config* cfg, int max_seq) { return orc_model_create_batch(cfg, max_seq, 1); }
+
+orc_model* orc_model_create_batch(const orc_config* cfg, int max_seq, int batch) {
+    if (batch < 1) return NULL;
     orc_model* m = (orc_model*)calloc(1, sizeof(orc_model));
     if (!m) return NULL;
     m->c = *cfg;
     m->max_seq = max_seq;
+    m->batch = batch;
     m->qd = cfg->heads * cfg->head_dim;
     m->kvd = cfg->kv_heads * cfg->head_dim;
     m->inv_freq = (float*)calloc((size_t)cfg->head_dim, sizeof(float));
@@ -697,21 +865,23 @@ orc_model* orc_model_create(const orc_config* cfg, int max_seq) {
             L->kn = (float*)malloc(sizeof(float) * (size_t)cfg->head_dim);
             for (int i = 0; i < cfg->head_dim; ++i) L->qn[i] = L->kn[i] = 1.f;
         }
-        L->kc = calloc((size_t)max_seq * m->kvd, kvb);
-        L->vc = calloc((size_t)max_seq * m->kvd, kvb);
+        L->kc = calloc((size_t)batch * max_seq * m->kvd, kvb);
+        L->vc = calloc((size_t)batch * max_seq * m->kvd, kvb);
+        if (!L->kc || !L->vc || !L->q.w || !L->gate.w || !L->down.w) {
+            m->c.layers = l + 1;
+            orc_model_free(m);
+            return NULL;
+        }
     }
-    m->hidden = (float*)calloc((size_t)H, sizeof(float));
-    m->normed = (float*)calloc((size_t)H, sizeof(float));
-    m->q = (float*)calloc((size_t)m->qd, sizeof(float));
-    m->k = (float*)calloc((size_t)m->kvd, sizeof(float));
-    m->v = (float*)calloc((size_t)m->kvd, sizeof(float));
-    m->attn = (float*)calloc((size_t)m->qd, sizeof(float));
-    m->proj = (float*)calloc((size_t)H, sizeof(float));
-    m->gate = (float*)calloc((size_t)I, sizeof(float));
-    m->up = (float*)calloc((size_t)I, sizeof(float));
-    m->down = (float*)calloc((size_t)H, sizeof(float));
+    (void)I;
+    if (!m->embed || !m->lm_head.w || ensure_rows(m, 1) != 0) {
+        orc_model_free(m);
+        return NULL;
+    }
     return m;
 }
+
+void orc_model_set_fast(orc_model* m, int fast) { m->fast = fast != 0; }
 
 void orc_model_free(orc_model* m) {
     if (!m) return;
@@ -739,16 +909,7 @@ void orc_model_free(orc_model* m) {
     free(m->embed);
     free(m->final_norm);
     free(m->inv_freq);
-    free(m->hidden);
-    free(m->normed);
-    free(m->q);
-    free(m->k);
-    free(m->v);
-    free(m->attn);
-    free(m->proj);
-    free(m->gate);
-    free(m->up);
-    free(m->down);
+    free_rows(m);
     free(m);
 }
 
@@ -835,49 +996,100 @@ int orc_model_set_tensor(orc_model* m, const char* name, const float* data, int6
     return 0;
 }
 
-/* LlmModel.Step + LlmDecoderLayer.Forward (L/LlmModel.cs:402-444, L/LlmDecoderLayer.cs:129-196, 291-334). */
-int orc_model_step(orc_model* m, int token, int position, float* logits) {
+/* LlmModel.Step / StepBatch / IngestPrompt + LlmDecoderLayer.Forward / ForwardBatch (L/LlmModel.cs:156-251,
+ * 320-444; L/LlmDecoderLayer.cs:129-196, 290-378): `rows` tokens through the decoder at once. Row r feeds
+ * tokens[r] at positions[r] of sequence seqs[r] (NULL: sequence 0). Every row's K/V is stored before any
+ * attention, so consecutive positions of one sequence form a causal prefill chunk and rows of distinct
+ * sequences a decode batch. logits: [rows, vocab], or only the last row's when last_only; may be NULL. */
+int orc_model_forward(orc_model* m, int rows, const int* tokens, const int* positions, const int* seqs,
+                      float* logits, int last_only) {
     const orc_config* c = &m->c;
     const int H = c->hidden, I = c->inter, hd = c->head_dim;
-    if (token < 0 || token >= c->vocab || position < 0 || position >= m->max_seq) return -1;
-    memcpy(m->hidden, m->embed + (int64_t)token * H, sizeof(float) * (size_t)H);
+    if (rows < 1) return -1;
+    for (int r = 0; r < rows; ++r) {
+        const int sq = seqs ? seqs[r] : 0;
+        if (tokens[r] < 0 || tokens[r] >= c->vocab || positions[r] < 0 || positions[r] >= m->max_seq || sq < 0 ||
+            sq >= m->batch)
+            return -1;
+    }
+    if (ensure_rows(m, rows) != 0) return -2;
+    for (int r = 0; r < rows; ++r)
+        memcpy(m->hidden + (int64_t)r * H, m->embed + (int64_t)tokens[r] * H, sizeof(float) * (size_t)H);
     const int nl = m->layer_limit > 0 && m->layer_limit < c->layers ? m->layer_limit : c->layers;
     for (int l = 0; l < nl; ++l) {
         orc_layer* L = &m->L[l];
-        orc_rmsnorm(m->hidden, NULL, L->in_norm, m->normed, c->eps, H, 1, 0);
+        orc_rmsnorm(m->hidden, NULL, L->in_norm, m->normed, c->eps, H, rows, 0);
         emit(m, l, "input_norm", m->normed, H);
-        mat_apply(&L->q, m->normed, m->q);
-        mat_apply(&L->k, m->normed, m->k);
-        mat_apply(&L->v, m->normed, m->v);
+        mat_apply_rows(m, &L->q, rows, m->normed, m->q);
+        mat_apply_rows(m, &L->k, rows, m->normed, m->k);
+        mat_apply_rows(m, &L->v, rows, m->normed, m->v);
         if (c->bias) {
-            orc_bias_add(m->q, L->qb, m->qd, 1);
-            orc_bias_add(m->k, L->kb, m->kvd, 1);
-            orc_bias_add(m->v, L->vb, m->kvd, 1);
+            orc_bias_add(m->q, L->qb, m->qd, rows);
+            orc_bias_add(m->k, L->kb, m->kvd, rows);
+            orc_bias_add(m->v, L->vb, m->kvd, rows);
         }
         if (c->qk_norm) {
-            orc_rmsnorm(m->q, NULL, L->qn, m->q, c->eps, hd, c->heads, 0);
-            orc_rmsnorm(m->k, NULL, L->kn, m->k, c->eps, hd, c->kv_heads, 0);
+            orc_rmsnorm(m->q, NULL, L->qn, m->q, c->eps, hd, rows * c->heads, 0);
+            orc_rmsnorm(m->k, NULL, L->kn, m->k, c->eps, hd, rows * c->kv_heads, 0);
         }
         emit(m, l, "q", m->q, m->qd);
         emit(m, l, "k", m->k, m->kvd);
         emit(m, l, "v", m->v, m->kvd);
-        orc_rope(m->q, m->k, &position, m->inv_freq, hd, c->heads, c->kv_heads, m->attn_scale, m->rot, 1);
-        orc_kv_store(m->k, m->v, L->kc, L->vc, c->kv_dtype, position, m->kvd, 1);
-        orc_attention(m->q, L->kc, L->vc, c->kv_dtype, m->attn, hd, c->heads, c->kv_heads, position, 1);
-        mat_apply(&L->o, m->attn, m->proj);
+        orc_rope(m->q, m->k, positions, m->inv_freq, hd, c->heads, c->kv_heads, m->attn_scale, m->rot, rows);
+        for (int r = 0; r < rows; ++r) {
+            const int sq = seqs ? seqs[r] : 0;
+            orc_kv_store(m->k + (int64_t)r * m->kvd, m->v + (int64_t)r * m->kvd, seq_cache(m, L->kc, sq),
+                         seq_cache(m, L->vc, sq), c->kv_dtype, positions[r], m->kvd, 1);
+        }
+        for (int r = 0; r < rows; ++r) {
+            const int sq = seqs ? seqs[r] : 0;
+            orc_attention(m->q + (int64_t)r * m->qd, seq_cache(m, L->kc, sq), seq_cache(m, L->vc, sq), c->kv_dtype,
+                          m->attn + (int64_t)r * m->qd, hd, c->heads, c->kv_heads, positions[r], 1);
+        }
+        mat_apply_rows(m, &L->o, rows, m->attn, m->proj);
         emit(m, l, "attn_out", m->proj, H);
-        orc_rmsnorm(m->hidden, m->proj, L->post_norm, m->normed, c->eps, H, 1, 1);
+        orc_rmsnorm(m->hidden, m->proj, L->post_norm, m->normed, c->eps, H, rows, 1);
         emit(m, l, "post_norm", m->normed, H);
-        mat_apply(&L->gate, m->normed, m->gate);
-        mat_apply(&L->up, m->normed, m->up);
-        orc_swiglu(m->gate, m->up, I);
-        mat_apply(&L->down, m->gate, m->down);
+        mat_apply_rows(m, &L->gate, rows, m->normed, m->gate);
+        mat_apply_rows(m, &L->up, rows, m->normed, m->up);
+        orc_swiglu(m->gate, m->up, (int64_t)rows * I);
+        mat_apply_rows(m, &L->down, rows, m->gate, m->down);
         emit(m, l, "mlp_out", m->down, H);
-        orc_add(m->hidden, m->down, H);
+        orc_add(m->hidden, m->down, (int64_t)rows * H);
         emit(m, l, "output", m->hidden, H);
     }
-    orc_rmsnorm(m->hidden, NULL, m->final_norm, m->normed, c->eps, H, 1, 0);
-    if (logits) mat_apply(&m->lm_head, m->normed, logits);
+    if (!logits) return 0;
+    if (last_only) {
+        orc_rmsnorm(m->hidden + (int64_t)(rows - 1) * H, NULL, m->final_norm, m->normed, c->eps, H, 1, 0);
+        mat_apply_rows(m, &m->lm_head, 1, m->normed, logits);
+    } else {
+        orc_rmsnorm(m->hidden, NULL, m->final_norm, m->normed, c->eps, H, rows, 0);
+        mat_apply_rows(m, &m->lm_head, rows, m->normed, logits);
+    }
+    return 0;
+}
+
+/* LlmModel.Step (L/LlmModel.cs:402-444): one token of sequence 0. */
+int orc_model_step(orc_model* m, int token, int position, float* logits) {
+    return orc_model_forward(m, 1, &token, &position, NULL, logits, 0);
+}
+
+int orc_model_read_kv_seq(orc_model* m, int layer, int seq, int row0, int rows, float* keys, float* values) {
+    if (layer < 0 || layer >= m->c.layers || seq < 0 || seq >= m->batch || row0 < 0 || row0 + rows > m->max_seq) return -1;
+    const void* kc = seq_cache(m, m->L[layer].kc, seq);
+    const void* vc = seq_cache(m, m->L[layer].vc, seq);
+    for (int64_t i = 0; i < (int64_t)rows * m->kvd; ++i) {
+        keys[i] = load_elem(kc, m->c.kv_dtype, (int64_t)row0 * m->kvd + i);
+        values[i] = load_elem(vc, m->c.kv_dtype, (int64_t)row0 * m->kvd + i);
+    }
+    return 0;
+}
+
+int orc_model_write_kv_seq(orc_model* m, int layer, int seq, int row0, int rows, const float* keys,
+                           const float* values) {
+    if (layer < 0 || layer >= m->c.layers || seq < 0 || seq >= m->batch || row0 < 0 || row0 + rows > m->max_seq) return -1;
+    orc_kv_store(keys, values, seq_cache(m, m->L[layer].kc, seq), seq_cache(m, m->L[layer].vc, seq), m->c.kv_dtype, row0,
+                 m->kvd, rows);
     return 0;
 }
 

@@ -14,7 +14,9 @@
  * T/LlmMatrixInt8Tests.cs:45-119 (int8 sizes and error bound). The int8 word/scale packing and the
  * quantizer rounding of LevelZero.NET are not visible in any source: that layout is an assumption
  * (documented in l0b200.h) and its parity is unpinned. Dot products accumulate in double, as the
- * reference's CPU checks do (T/LlmMatrixTests.cs:71-79).
+ * reference's CPU checks do (T/LlmMatrixTests.cs:71-79); orc_gemm_fast (a model's fast mode) is the
+ * fp32-accumulate timing build of the same products, used for the CPU baseline and to ingest long
+ * prompts into the checker, with its error bound stated where it is defined.
  */
 #ifndef L0B_ORACLE_H
 #define L0B_ORACLE_H
@@ -40,6 +42,9 @@ void orc_convert(const float* src, void* dst, int dtype, int64_t n);
  * [N, K/group]. L/LlmMatrix.cs:122-171 (GemvQ8 for int8, Gemv for 16/32-bit). */
 void orc_gemv_out_in(int M, int N, int K, const float* x, int wdtype, const void* w, const uint16_t* scales,
                      int group, float* y);
+/* orc_gemv_out_in with fp32 fused multiply-add accumulation (AVX2, eight lanes per output), for timing. */
+void orc_gemm_fast(int M, int N, int K, const float* x, int wdtype, const void* w, const uint16_t* scales, int group,
+                   float* y);
 /* Reference layout W [K, N] (f32 or f16): y[m, n] = sum_k x[m, k] * W[k, n]. T/LlmMatrixTests.cs:71-79. */
 void orc_gemv_in_out(int M, int N, int K, const float* x, int w_is_half, const void* w, float* y);
 /* Symmetric int8 quantisation of [N, K] with one scale per `group` inputs (L/LlmMatrix.cs:89-93). */
@@ -112,11 +117,21 @@ typedef struct orc_config {
 
 typedef struct orc_model orc_model;
 orc_model* orc_model_create(const orc_config* cfg, int max_seq);
+/* `batch` sequences, each with its own KV cache rows [max_seq, kv_dim] per layer. */
+orc_model* orc_model_create_batch(const orc_config* cfg, int max_seq, int batch);
+/* 1: projections accumulate in fp32 (orc_gemm_fast); 0 (default): in double. */
+void orc_model_set_fast(orc_model* m, int fast);
 void orc_model_free(orc_model* m);
 int orc_model_init_synthetic(orc_model* m, uint64_t seed, float std, float scale_lo, float scale_hi);
 int orc_model_set_tensor(orc_model* m, const char* name, const float* data, int64_t count);
 /* Feeds token `token` at `position` and writes the vocab logits of the next token. */
 int orc_model_step(orc_model* m, int token, int position, float* logits);
+/* `rows` tokens at once: row r is token tokens[r] at positions[r] of sequence seqs[r] (NULL: 0). All rows'
+ * K/V are stored before attention, so consecutive positions of one sequence are a causal prefill chunk
+ * (LlmModel.IngestPrompt) and rows of different sequences a decode batch (LlmModel.StepBatch).
+ * logits: [rows, vocab], or the last row's only when last_only; may be NULL. */
+int orc_model_forward(orc_model* m, int rows, const int* tokens, const int* positions, const int* seqs,
+                      float* logits, int last_only);
 /* Runs only `layers_to_run` layers (<= cfg.layers) for timing samples; 0 = all. */
 void orc_model_set_layer_limit(orc_model* m, int layers_to_run);
 /* Stage callback with the reference's probe stage names (L/LlmDecoderLayer.cs:113-119). */
@@ -124,6 +139,10 @@ typedef void (*orc_probe_fn)(void* user, int layer, const char* stage, const flo
 void orc_model_set_probe(orc_model* m, orc_probe_fn fn, void* user);
 /* Reads the K/V cache rows of a layer as f32. */
 int orc_model_read_kv(orc_model* m, int layer, int row0, int rows, float* keys, float* values);
+int orc_model_read_kv_seq(orc_model* m, int layer, int seq, int row0, int rows, float* keys, float* values);
+/* Writes K/V cache rows (rounded to the cache dtype), e.g. a context filled by another prefill. */
+int orc_model_write_kv_seq(orc_model* m, int layer, int seq, int row0, int rows, const float* keys,
+                           const float* values);
 /* Threads used by the oracle's parallel loops (OpenMP). */
 int orc_num_threads(void);
 void orc_set_num_threads(int n);

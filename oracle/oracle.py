@@ -91,8 +91,18 @@ def lib() -> C.CDLL:
     L.orc_causal_conv.argtypes = [_f32p, _f32p, _f32p, _f32p, C.c_int, C.c_int, C.c_int]
     L.orc_gated_delta.argtypes = [_f32p, _f32p, _f32p, _f32p, _f32p, _f32p, _f32p, _f32p, _f32p, C.c_int, C.c_int,
                                   C.c_int, C.c_int, C.c_int, C.c_float]
+    L.orc_gemm_fast.argtypes = [C.c_int, C.c_int, C.c_int, _f32p, C.c_int, vp, vp, C.c_int, _f32p]
     L.orc_model_create.restype = vp
     L.orc_model_create.argtypes = [C.POINTER(OrcConfig), C.c_int]
+    L.orc_model_create_batch.restype = vp
+    L.orc_model_create_batch.argtypes = [C.POINTER(OrcConfig), C.c_int, C.c_int]
+    L.orc_model_set_fast.argtypes = [vp, C.c_int]
+    L.orc_model_forward.restype = C.c_int
+    L.orc_model_forward.argtypes = [vp, C.c_int, _i32p, _i32p, vp, vp, C.c_int]
+    L.orc_model_read_kv_seq.restype = C.c_int
+    L.orc_model_read_kv_seq.argtypes = [vp, C.c_int, C.c_int, C.c_int, C.c_int, _f32p, _f32p]
+    L.orc_model_write_kv_seq.restype = C.c_int
+    L.orc_model_write_kv_seq.argtypes = [vp, C.c_int, C.c_int, C.c_int, C.c_int, _f32p, _f32p]
     L.orc_model_free.argtypes = [vp]
     L.orc_model_init_synthetic.argtypes = [vp, C.c_uint64, C.c_float, C.c_float, C.c_float]
     L.orc_model_set_tensor.restype = C.c_int
@@ -141,6 +151,18 @@ def gemv_out_in(x: np.ndarray, w: np.ndarray, wdtype: int, scales: np.ndarray | 
     y = np.zeros((M, N), np.float32)
     lib().orc_gemv_out_in(M, N, K, x.reshape(M, K), wdtype, _ptr(np.ascontiguousarray(w)),
                           _ptr(None if scales is None else np.ascontiguousarray(scales)), group, y)
+    return y
+
+
+def gemm_fast(x: np.ndarray, w: np.ndarray, wdtype: int, scales: np.ndarray | None = None,
+              group: int = 0) -> np.ndarray:
+    """gemv_out_in accumulated in fp32 with FMA (the timing build)."""
+    x = np.ascontiguousarray(x, np.float32)
+    M, K = x.reshape(-1, x.shape[-1]).shape
+    N = w.shape[0]
+    y = np.zeros((M, N), np.float32)
+    lib().orc_gemm_fast(M, N, K, x.reshape(M, K), wdtype, _ptr(np.ascontiguousarray(w)),
+                        _ptr(None if scales is None else np.ascontiguousarray(scales)), group, y)
     return y
 
 
@@ -211,15 +233,47 @@ def synth_fill(count, dtype, seed, tensor_id, mode, a, b=0.0, row_len=0, full_le
 class OracleModel:
     """The whole decoder on the CPU, one token per step (LlmModel.Step semantics)."""
 
-    def __init__(self, cfg: dict, max_seq: int):
+    def __init__(self, cfg: dict, max_seq: int, batch: int = 1):
         c = OrcConfig()
         for k, v in cfg.items():
             setattr(c, k, v)
         self.cfg = cfg
-        self._h = lib().orc_model_create(C.byref(c), max_seq)
+        self._h = lib().orc_model_create_batch(C.byref(c), max_seq, batch)
         if not self._h:
             raise MemoryError("oracle model allocation failed")
         self.vocab = cfg["vocab"]
+        self.kv_dim = cfg["kv_heads"] * cfg["head_dim"]
+
+    def set_fast(self, fast: bool):
+        """fp32-accumulate projections (timing build, relative error ~1e-6) instead of double."""
+        lib().orc_model_set_fast(self._h, 1 if fast else 0)
+
+    def forward(self, tokens, positions, seqs=None, last_only: bool = False) -> np.ndarray:
+        """Rows of (token, position, sequence) at once: a causal prefill chunk or a decode batch."""
+        t = np.ascontiguousarray(tokens, np.int32)
+        p = np.ascontiguousarray(positions, np.int32)
+        sq = None if seqs is None else np.ascontiguousarray(seqs, np.int32)
+        logits = np.zeros((1 if last_only else t.size, self.vocab), np.float32)
+        rc = lib().orc_model_forward(self._h, t.size, t, p, _ptr(sq), _ptr(logits), 1 if last_only else 0)
+        if rc != 0:
+            raise ValueError(f"oracle forward failed ({rc})")
+        return logits[0] if last_only else logits
+
+    def prefill(self, prompt, seq: int = 0, chunk: int = 512) -> np.ndarray:
+        """LlmModel.Prefill of sequence `seq` from position 0; the last position's logits."""
+        prompt = np.asarray(prompt, np.int32)
+        lg = None
+        for s0 in range(0, prompt.size, chunk):
+            part = prompt[s0:s0 + chunk]
+            last = s0 + part.size == prompt.size
+            lg = self.forward(part, np.arange(s0, s0 + part.size), np.full(part.size, seq), last_only=True)
+        return lg
+
+    def write_kv(self, layer: int, row0: int, keys: np.ndarray, values: np.ndarray, seq: int = 0):
+        k = np.ascontiguousarray(keys, np.float32).reshape(-1, self.kv_dim)
+        v = np.ascontiguousarray(values, np.float32).reshape(-1, self.kv_dim)
+        if lib().orc_model_write_kv_seq(self._h, layer, seq, row0, k.shape[0], k, v) != 0:
+            raise ValueError("oracle write_kv failed")
 
     def close(self):
         if self._h:
@@ -258,10 +312,10 @@ class OracleModel:
     def set_layer_limit(self, n: int):
         lib().orc_model_set_layer_limit(self._h, n)
 
-    def read_kv(self, layer: int, row0: int, rows: int, kv_dim: int):
+    def read_kv(self, layer: int, row0: int, rows: int, kv_dim: int, seq: int = 0):
         k = np.zeros(rows * kv_dim, np.float32)
         v = np.zeros(rows * kv_dim, np.float32)
-        lib().orc_model_read_kv(self._h, layer, row0, rows, k, v)
+        lib().orc_model_read_kv_seq(self._h, layer, seq, row0, rows, k, v)
         return k.reshape(rows, kv_dim), v.reshape(rows, kv_dim)
 
 

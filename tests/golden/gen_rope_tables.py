@@ -80,7 +80,8 @@ def reference_tables(ref: Path) -> dict[str, list[float]]:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", required=True,
+                    help="checkout of the l0llm repository whose T/golden/rope.golden.json pins the tables")
     args = ap.parse_args()
     ref = reference_tables(Path(args.reference))
     doc = {"generator": "transformers " + __import__("transformers").__version__ + ", torch " + torch.__version__,

@@ -314,3 +314,102 @@ def test_no_device_is_reported_without_gpu(lz):
 def test_quantizer_rejects_bad_shapes(lz):
     with pytest.raises(lz.ArgumentException):
         lz.q8_quantize_out_in(np.zeros((4, 50), np.float32), 32)
+
+
+# ----------------------------------------------------------------------------------------------
+# The oracle's fp32 timing GEMM and its batched forward (prefill chunks, decode batches)
+# ----------------------------------------------------------------------------------------------
+
+@pytest.mark.parametrize("m,n,k,wdtype,group", [(1, 97, 896, 3, 0), (13, 64, 896, 3, 32), (7, 33, 72, 1, 0),
+                                                 (5, 10, 19, 0, 0), (30, 65, 256, 2, 0)])
+def test_gemm_fast_matches_double_accumulation(orc, m, n, k, wdtype, group):
+    rng = np.random.default_rng(m * 1000 + n)
+    x = rng.standard_normal((m, k)).astype(np.float32)
+    s = None
+    if wdtype == orc.I8:
+        w = rng.integers(-127, 128, (n, k)).astype(np.int8)
+        g = group or k
+        s = orc.f16_bits(rng.uniform(1e-3, 2e-2, n * (k // g)).astype(np.float32)).reshape(n, k // g)
+    elif wdtype == orc.F32:
+        w = rng.standard_normal((n, k)).astype(np.float32)
+    else:
+        wf = rng.standard_normal((n, k)).astype(np.float32)
+        w = (orc.f16_bits(wf) if wdtype == orc.F16 else (wf.view(np.uint32) >> 16).astype(np.uint16)).reshape(n, k)
+    exact = orc.gemv_out_in(x, w, wdtype, s, group)
+    fast = orc.gemm_fast(x, w, wdtype, s, group)
+    assert np.abs(fast - exact).max() <= 1e-5 * np.abs(exact).max()
+
+
+def _tiny_oracle(orc, name, batch):
+    cfg = hf_tiny.TINY[name]
+    om = orc.OracleModel(hf_tiny.oracle_config(cfg, orc.F32, 0, orc.F16), 32, batch)
+    for key, v in hf_tiny.weights(cfg, 7).items():
+        om.set_tensor(key, v)
+    return om, hf_tiny.prompt(cfg, 7)
+
+
+@pytest.mark.parametrize("name", ["qwen2", "llama3", "qwen3"])
+def test_oracle_prefill_chunk_equals_token_steps(orc, name):
+    """IngestPrompt as one causal chunk equals one Step per token, bit for bit in double accumulation
+    (the reference's chunked-prefill == sequential test, T/Qwen25PrefillTests.cs:41-75)."""
+    a, prompt = _tiny_oracle(orc, name, 1)
+    for t, tok in enumerate(prompt[:9]):
+        want = a.step(int(tok), t)
+    b, _ = _tiny_oracle(orc, name, 3)
+    got = b.prefill(prompt[:9], seq=2)
+    np.testing.assert_array_equal(got, want)
+    ka, va = a.read_kv(1, 0, 9, a.kv_dim)
+    kb, vb = b.read_kv(1, 0, 9, b.kv_dim, seq=2)
+    np.testing.assert_array_equal(ka, kb)
+    np.testing.assert_array_equal(va, vb)
+    c, _ = _tiny_oracle(orc, name, 1)
+    c.set_fast(True)
+    np.testing.assert_allclose(c.prefill(prompt[:9]), want, rtol=0, atol=1e-4 * np.abs(want).max())
+    for m in (a, b, c):
+        m.close()
+
+
+def test_oracle_decode_batch_equals_separate_sequences(orc):
+    """StepBatch: rows of different sequences, each at its own position, equal separate single steps."""
+    om, prompt = _tiny_oracle(orc, "qwen2", 2)
+    om.prefill(prompt[:5], seq=0)
+    om.prefill(prompt[3:10], seq=1)
+    got = om.forward([11, 12], [5, 7], [0, 1])
+    for seq, (p, off) in enumerate(((prompt[:5], 5), (prompt[3:10], 7))):
+        ref, _ = _tiny_oracle(orc, "qwen2", 1)
+        ref.prefill(p)
+        np.testing.assert_array_equal(got[seq], ref.step(11 + seq, off))
+        ref.close()
+    # A context written from outside (another prefill's K/V rows) is what the next step attends to.
+    other, _ = _tiny_oracle(orc, "qwen2", 1)
+    for layer in range(hf_tiny.TINY["qwen2"]["layers"]):
+        k, v = om.read_kv(layer, 0, 7, om.kv_dim, seq=1)
+        other.write_kv(layer, 0, k, v)
+    np.testing.assert_array_equal(other.step(12, 7), got[1])
+    om.close()
+    other.close()
+
+
+def test_config2_weights_amplify_rounding(orc):
+    """Config 2's synthetic int8 weights amplify rounding differences: four layers of config-2 width
+    in the oracle's fp32 build and in its double build (each projection agreeing to ~1e-7 relative)
+    already disagree by more than the elementwise max-abs 1e-2 + rel 1e-2 bar on part of the logits,
+    while staying within 1e-2 of the logit range. This is why the full-depth config-2 GPU tests hold the
+    elementwise bar on the decisive (top) logits and the range-relative bar on the rest. (A 32-token
+    prompt: the spread grows with the number of attended positions.)"""
+    cfg = dict(hidden=3584, inter=18944, layers=4, heads=28, kv_heads=4, head_dim=128, vocab=152064, max_pos=32768,
+               eps=1e-6, theta=1e6, tie=0, bias=1, qk_norm=0, rope_type=0, rope_factor=1.0, rope_original_max=0,
+               rope_low=1.0, rope_high=4.0, rope_beta_fast=32.0, rope_beta_slow=1.0, rope_attention=0.0,
+               wdtype=orc.I8, group=0, kv_dtype=orc.F16)
+    prompt = np.random.default_rng(2).integers(0, 152064, 32).astype(np.int32)
+    out = []
+    for fast in (False, True):
+        om = orc.OracleModel(cfg, 34)
+        om.init_synthetic(2, 0.02, 1e-3, 2e-2)
+        om.set_fast(fast)
+        out.append(om.prefill(prompt))
+        om.close()
+    exact, fast = out
+    err = np.abs(fast.astype(np.float64) - exact)
+    assert (err > 1e-2 + 1e-2 * np.abs(exact)).sum() > 0
+    assert err.max() <= 1e-2 * np.abs(exact).max()

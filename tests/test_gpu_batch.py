@@ -97,3 +97,35 @@ def test_fork_sequence_on_device(lz, device, suite):
             mb.ForkSequence(1, 1, 0)
         with pytest.raises(lz.ArgumentOutOfRangeException):
             mb.ForkSequence(0, 3, 0)
+
+
+def test_sequence0_length_is_one_value_across_single_and_batched_calls(lz, device, suite):
+    """Decode on sequence 0 advances the length the batched calls check: a batched device decode that
+    would run past the cache after single-sequence decodes is refused, not written past the rows."""
+    prompts = _prompts(2)
+    with _model(lz, device, suite, 2, "int8") as mb:
+        mb.PrefillSequence(1, prompts[1], want_logits=False)
+        mb.Prefill(np.arange(80, dtype=np.int32))
+        for t in range(10):
+            mb.Decode(t)
+        assert mb.Position == 90 and mb.SequencePosition(0) == 90
+        with pytest.raises(lz.InvalidOperationException):
+            mb.decode_greedy_device_batch(7, 1)  # 90 + 7 > 96 rows
+        toks = mb.decode_greedy_device_batch(6, 1)
+        assert toks.shape == (6, 1) and mb.Position == 96 and mb.SequencePosition(0) == 96
+
+
+def test_single_sequence_step_keeps_other_rows_device_state(lz, device, suite):
+    """A one-token step of sequence 0 writes only row 0's token and position: rows prefilled before it
+    still continue from their own device state in a later batched greedy decode."""
+    steps = 5
+    prompts = _prompts(3)
+    with _model(lz, device, suite, 3, "int8") as mb:
+        mb.PrefillSequence(1, prompts[1], want_logits=False)
+        mb.PrefillSequence(2, prompts[2], want_logits=False)
+        mb.Prefill(np.array([5], np.int32))  # a one-token prompt of sequence 0 runs as a Step
+        got = mb.decode_greedy_device_batch(steps, 3)
+    with _model(lz, device, suite, 1, "int8") as ms:
+        for s, p in ((0, np.array([5], np.int32)), (1, prompts[1]), (2, prompts[2])):
+            ms.Prefill(p)
+            np.testing.assert_array_equal(got[:, s], ms.decode_greedy_device(steps))

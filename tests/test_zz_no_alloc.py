@@ -3,9 +3,9 @@
 It exists for callers that cannot let a call allocate device memory (a server that plans all of HBM
 at start-up, code running while another runtime owns the allocator, a host that must not block in
 cudaMalloc mid-step). Its scratch is a fixed array inside the library, so two calls in a row must both
-agree with the regular entry point (l0b_attention_execute), the second one reusing what the first
-left in that scratch. Kept in its own file so a run that stops at the first failure has run every
-other test first.
+agree with the regular entry point (l0b_attention_execute) and with the CPU oracle's attention
+(oracle/l0b_oracle.c orc_attention), the second call reusing what the first left in that scratch.
+Kept in its own file so a run that stops at the first failure has run every other test first.
 """
 from __future__ import annotations
 
@@ -28,6 +28,8 @@ def _noalloc(lz, stream, q, kc, vc, cache_dtype, out, hd, nh, nkv, seq, max_seq)
 
 
 def test_noalloc_attention_matches_regular_entry_twice(lz, device, suite):
+    from oracle import oracle as orc
+
     stream = C.c_void_p()
     lz.check(lz.load_library().l0b_device_stream(device.handle, C.byref(stream)))
     hd, nh, nkv, max_seq = 128, 28, 4, 4096
@@ -44,6 +46,8 @@ def test_noalloc_attention_matches_regular_entry_twice(lz, device, suite):
             device.Synchronize()
             a, b = got.ToArray(), want.ToArray()
         np.testing.assert_allclose(a, b, atol=1e-4, rtol=1e-3)
+        ref = orc.attention(q[None, :], kc.view(np.uint16), vc.view(np.uint16), orc.F16, hd, nh, nkv, seq - 1, 1)[0]
+        np.testing.assert_allclose(a, ref, atol=1e-4, rtol=1e-3)
 
 
 def test_noalloc_rejects_sizes_beyond_its_scratch(lz, device):
