@@ -410,10 +410,17 @@ L0B_API l0b_status l0b_comm_allreduce(l0b_comm* comm, l0b_buffer* buf, int64_t c
 /* Tuning: the largest K split the tensor-core GEMM may use for narrow projections (1..16, default 16;
  * <= 0 restores the default). Affects plans made after the call. */
 L0B_API l0b_status l0b_tc_set_max_splits(int32_t splits);
-/* Tuning: one-row int8 projections with at least 8 tiles of 16 rows per SM (the gate/up projection and
- * LM head at batch 1) on the GEMV that streams whole tiles by bulk copies (1, default) or on the
- * register-streamed one (0). Affects launches made after the call. */
+/* Tuning: one-row int8 projections on the GEMV that streams weights by bulk copies (1, default) -- whole
+ * 16-row tiles for projections with at least 8 tiles per SM (gate/up, LM head), units of up to four
+ * 512-k blocks of a tile for projections stored in the blocked layout (q/k/v, o_proj, down) -- or on the
+ * register-streamed one (0). Affects launches made after the call. No counterpart in the reference. */
 L0B_API l0b_status l0b_set_gemv_bulk(int32_t enable);
+/* Layout of the int8 weights of models created after the call: with blocking on (1, default), int8
+ * projections with one scale per row, K % 512 == 0, N % 16 == 0 and fewer than 8 tiles of 16 rows per
+ * SM (q/k/v, o_proj, down at Qwen2.5-7B widths) are stored as [N/16][K/512][16][512] bytes, so the k
+ * blocks of a 16-row tile are contiguous 8 KB blocks; 0 keeps every matrix row-major [N, K].
+ * l0b_model_read_weight returns the [out, in] order either way. No counterpart in the reference. */
+L0B_API l0b_status l0b_set_weight_blocking(int32_t enable);
 /* Process-wide choice of the decode GEMV kernel for shapes both take: 1 (default) = tensor-core
  * mma.sync streaming kernel, 0 = fp32-FMA streaming kernel. Used by tests to cover both; recorded
  * command lists keep the kernel they were recorded with. No counterpart in the reference. */

@@ -58,6 +58,7 @@ struct TcParams {
     unsigned* counters;    // split-K tile counters, zero at rest
     unsigned long long* argmax;  // EPI_ARGMAX: per-token keys (atomicMax), index = row + argmax_base
     int argmax_base;
+    int wkb;  // > 0: wmap is the 4-D map of the blocked int8 layout {kb, 16, K / kb, N / 16}
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -98,6 +99,23 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, u
             "r"(smem_u32(dst)),
         "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y)
         : "memory");
+}
+
+__device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1, int c2,
+                                            int c3) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5, %6}], "
+        "[%2];" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+        : "memory");
+}
+
+// The weight tile [rows row0 .. + box rows, k0 .. + 128 bytes): row-major 2-D map, or the blocked
+// layout's 4-D map (the box {128 bytes, 16 rows, 1 block, rows / 16 tiles} lands in shared memory in the
+// same row order, 128 bytes per row, as the 2-D box).
+__device__ __forceinline__ void tma_load_w(void* dst, const TcParams& p, uint64_t* bar, int k0, int row0) {
+    if (p.wkb > 0) tma_load_4d(dst, &p.wmap, bar, k0 % p.wkb, 0, k0 / p.wkb, row0 >> 4);
+    else tma_load_2d(dst, &p.wmap, bar, k0, row0);
 }
 
 // UMMA shared-memory descriptor of a K-major tile with 128-byte swizzle: rows of 128 bytes, 8-row
@@ -230,10 +248,10 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const __grid_const
             mbar_expect_tx(&full[s], A_BYTES + B_BYTES);
             const int k0 = (kb0 + i) * KB;
             if (swiglu) {
-                tma_load_2d(sA + s * A_BYTES, &p.wmap, &full[s], k0, wt * 64);
-                tma_load_2d(sA + s * A_BYTES + A_BYTES / 2, &p.wmap, &full[s], k0, p.half_n + wt * 64);
+                tma_load_w(sA + s * A_BYTES, p, &full[s], k0, wt * 64);
+                tma_load_w(sA + s * A_BYTES + A_BYTES / 2, p, &full[s], k0, p.half_n + wt * 64);
             } else {
-                tma_load_2d(sA + s * A_BYTES, &p.wmap, &full[s], k0, wt * kBM);
+                tma_load_w(sA + s * A_BYTES, p, &full[s], k0, wt * kBM);
             }
             tma_load_2d(sB + s * B_BYTES, &p.xmap, &full[s], k0, xrow0);
         }
@@ -699,6 +717,27 @@ l0b_status make_map(CUtensorMap* map, const void* base, int dtype, long long row
     return L0B_OK;
 }
 
+// int8 weights in the blocked layout [N / 16][K / kb][16][kb]: a 4-D map {kb, 16, K / kb, N / 16} with the
+// 128-byte swizzle and box {128, 16, 1, box_rows / 16}.
+l0b_status make_map_blocked(CUtensorMap* map, const void* base, long long rows, long long K, int kb, int box_rows) {
+    EncodeTiledFn fn = encode_fn();
+    L0B_REQUIRE(fn, L0B_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+    L0B_REQUIRE(reinterpret_cast<uintptr_t>(base) % 16 == 0 && rows % 16 == 0 && K % kb == 0 && kb % 128 == 0 &&
+                    box_rows % 16 == 0,
+                L0B_ERR_ARGUMENT, "blocked weight map: rows %lld, K %lld, kb %d", rows, K, kb);
+    const cuuint64_t dims[4] = {static_cast<cuuint64_t>(kb), 16, static_cast<cuuint64_t>(K / kb),
+                                static_cast<cuuint64_t>(rows / 16)};
+    const cuuint64_t strides[3] = {static_cast<cuuint64_t>(kb), static_cast<cuuint64_t>(16) * kb,
+                                   static_cast<cuuint64_t>(16) * K};
+    const cuuint32_t box[4] = {128, 16, 1, static_cast<cuuint32_t>(box_rows / 16)};
+    const cuuint32_t estr[4] = {1, 1, 1, 1};
+    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, const_cast<void*>(base), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    L0B_REQUIRE(r == CUDA_SUCCESS, L0B_ERR_CUDA, "cuTensorMapEncodeTiled (blocked) failed (%d)", static_cast<int>(r));
+    return L0B_OK;
+}
+
 template <int BN, int FMT>
 l0b_status launch_bn(l0b_device* d, const TcParams& p, const TcPlan& plan) {
     auto kernel = tc_gemm_kernel<BN, FMT>;
@@ -781,7 +820,13 @@ l0b_status tc_gemm_launch(l0b_device* d, const TcGemmArgs& a) {
     const bool swiglu = a.epi == EPI_SWIGLU;
     const bool q8 = a.wdtype == L0B_I8;
     L0B_REQUIRE(!q8 || a.wscale, L0B_ERR_ARGUMENT, "int8 weights need their row scales");
-    L0B_TRY(make_map(&p.wmap, a.w, a.wdtype, a.N, a.K, swiglu ? 64 : kBM));
+    if (q8 && a.kb > 0) {
+        L0B_REQUIRE(!swiglu, L0B_ERR_UNSUPPORTED, "the SwiGLU epilogue takes row-major weights");
+        L0B_TRY(make_map_blocked(&p.wmap, a.w, a.N, a.K, a.kb, kBM));
+        p.wkb = a.kb;
+    } else {
+        L0B_TRY(make_map(&p.wmap, a.w, a.wdtype, a.N, a.K, swiglu ? 64 : kBM));
+    }
     const long long xrows = (a.split || q8) ? tc_pair_rows(plan) : a.M;
     L0B_TRY(make_map(&p.xmap, a.x16, a.wdtype, xrows, a.K, plan.bn));
     p.wscale = static_cast<const __half*>(a.wscale);

@@ -33,6 +33,7 @@ struct TcGemmArgs {
     int split = 0;
     const float* rscale = nullptr;
     const void* wscale = nullptr;  // int8: f16 [N], one scale per weight row
+    int kb = 0;                    // int8: > 0 when w is in the blocked layout (gemv.cuh), k per block
     // EPI_ARGMAX: logits to out (when not null) and, per token t, atomicMax of
     // argmax_key(value, row + argmax_base) into argmax[t].
     unsigned long long* argmax = nullptr;

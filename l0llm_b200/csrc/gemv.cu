@@ -18,7 +18,6 @@
 // first D steps are issued before griddepcontrol.wait -- weights never depend on the previous kernel
 // -- so under programmatic dependent launch the weight stream starts while the producer of x drains.
 #include <climits>
-#include <cstdlib>
 #include <cooperative_groups.h>
 #include <cstring>
 
@@ -625,13 +624,22 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_mma_kernel(const GemvParams 
     const WT* i_p[2];
     const __half* i_s[2];
     int i_step = 0, i_tile = blockIdx.x, i_q = 0;
+    // Blocked int8 layout (p.kb > 0): piece pc of row r lies in block pc / ppb of the row's tile, at
+    // (r % 16) * kb + (pc % ppb) * PE within it.
+    const int kbk = kI8 ? p.kb : 0;  // 0 or kWeightBlock (8 pieces of 64 k)
     auto set_issue_tile = [&](int tile) {
         int r0, r1;
         bool v0, v1;
         tile_rows(tile, r0, r1, v0, v1);
-        const long long off = static_cast<long long>(p0) * PE + t * (PE / 4);
-        i_p[0] = v0 ? W + static_cast<long long>(r0) * K + off : nullptr;
-        i_p[1] = v1 ? W + static_cast<long long>(r1) * K + off : nullptr;
+        if (kbk > 0) {
+            const long long tb = static_cast<long long>(t) * (PE / 4);
+            i_p[0] = v0 ? W + static_cast<long long>(r0 >> 4) * 16 * K + (r0 & 15) * kbk + tb : nullptr;
+            i_p[1] = v1 ? W + static_cast<long long>(r1 >> 4) * 16 * K + (r1 & 15) * kbk + tb : nullptr;
+        } else {
+            const long long off = static_cast<long long>(p0) * PE + t * (PE / 4);
+            i_p[0] = v0 ? W + static_cast<long long>(r0) * K + off : nullptr;
+            i_p[1] = v1 ? W + static_cast<long long>(r1) * K + off : nullptr;
+        }
         i_s[0] = (kI8 && v0) ? scales + r0 : nullptr;
         i_s[1] = (kI8 && v1) ? scales + r1 : nullptr;
     };
@@ -639,11 +647,13 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_mma_kernel(const GemvParams 
     // Piece l of the chunk at the issue cursor (step i_step), then the cursor's scale and advance.
     auto issue_piece = [&](uint4 (&slot)[2][kMmaLoads], int l) {
         if (i_step < total) {
-            const long long kk = static_cast<long long>(i_q) * (kMmaLoads * PE);
-            const bool in_k = p0 + kMmaLoads * i_q + l < p1;
+            const int pc = p0 + kMmaLoads * i_q + l;
+            const bool in_k = pc < p1;
+            const long long off = kbk > 0 ? static_cast<long long>(pc >> 3) * (16 * kWeightBlock) + (pc & 7) * PE
+                                          : static_cast<long long>(i_q) * (kMmaLoads * PE) + l * PE;
 #pragma unroll
             for (int r = 0; r < 2; ++r)
-                slot[r][l] = (i_p[r] && in_k) ? ld_stream_v4(i_p[r] + kk + l * PE) : make_uint4(0, 0, 0, 0);
+                slot[r][l] = (i_p[r] && in_k) ? ld_stream_v4(i_p[r] + off) : make_uint4(0, 0, 0, 0);
         }
     };
     auto issue_finish = [&](float (&ss)[2]) {
@@ -999,7 +1009,7 @@ l0b_status launch_on(l0b_device* dev, cudaStream_t stream, F kernel, dim3 g, dim
 constexpr int kBulkCW = 16;                      // consumer warps
 constexpr int kBulkConsumers = kBulkCW * 32;
 constexpr int kBulkThreads = kBulkConsumers + 32;  // consumers + 1 producer warp
-constexpr int kBulkMaxStages = 4;
+constexpr int kBulkMaxStages = 8;
 constexpr int kBulkSmemBudget = 212 * 1024;  // dynamic; the static arrays take ~8 KB of the 227 KB
 constexpr long long kBulkWaitCycles = 4000000000LL;
 
@@ -1031,26 +1041,31 @@ __device__ __forceinline__ void bulk_copy(void* dst, const void* src, uint32_t b
                  : "memory");
 }
 
-// Activations staged as hi/lo pairs (bytes) and the ring of `stages` units of 16 rows x KS bytes.
+// Activations staged as hi/lo pairs (bytes) and the ring of `stages` units of 16 rows x UK bytes.
 __host__ __device__ inline size_t bulk_xs_bytes(int K) { return (static_cast<size_t>(K) * 4 + 1023) & ~static_cast<size_t>(1023); }
-inline size_t bulk_smem_bytes(int K, int stages, int KS) {
-    return 1024 + bulk_xs_bytes(K) + static_cast<size_t>(stages) * 16 * KS + 2 * kBulkMaxStages * 8;
+inline size_t bulk_smem_bytes(int K, int stages, int UK) {
+    return 1024 + bulk_xs_bytes(K) + static_cast<size_t>(stages) * 16 * UK + 2 * kBulkMaxStages * 8;
 }
-inline int bulk_stages(int K, int KS) {
+inline int bulk_stages(int K, int UK) {
     for (int s = kBulkMaxStages; s >= 2; --s)
-        if (bulk_smem_bytes(K, s, KS) <= static_cast<size_t>(kBulkSmemBudget)) return s;
+        if (bulk_smem_bytes(K, s, UK) <= static_cast<size_t>(kBulkSmemBudget)) return s;
     return 0;
 }
 
-// Split-K units (p.ksplit = S > 1, for projections with few row tiles: o_proj, down, q/k/v): a unit is
-// the 16 rows of a tile times one S-th of K (16 row copies of K/S bytes into one stage), units are taken
-// in (tile, segment) order, and each CTA a contiguous range of them, so the work per SM differs by at most
-// one unit. A warp keeps its sums across the segments of a tile in registers; at the end of the tile (or
-// of the CTA's range) the warps' sums meet once. A tile whose segments two CTAs share (the host keeps
-// every range at least S - 1 units long, so never more than two) is finished by the second CTA to get
-// there: each writes its 16 partial sums to p.part[tile][first segment == 0 ? 0 : 1] and bumps
-// p.counters[tile]; the one that finds the other's partial adds the two (a + b == b + a: the result does
-// not depend on arrival order), runs the epilogue and re-arms the counter.
+// Split-K units (projections with few row tiles -- o_proj, down, q/k/v -- stored in the blocked layout,
+// p.kb > 0): a unit is up to p.ugroup consecutive k blocks of one 16-row tile, which the blocked layout
+// keeps contiguous, so a unit is one bulk copy of up to ugroup * 16 * kb bytes. A CTA's copies complete
+// one stage at a time, at about one DRAM latency each (a probe of copies alone: 8 KB stages 3.0 TB/s,
+// 16 KB 6.0, 32 KB and more 7.0 on B200), so units are made large enough to stream at full rate.
+// Units are taken in (tile, group) order -- their order in HBM -- and each CTA a contiguous range of
+// them, so the work per SM differs by at most one unit. A warp keeps its sums across the units of a
+// tile in registers; at the end of the tile (or of the CTA's range) the warps' sums meet once. A tile
+// whose units two CTAs share (the host keeps every range at least units-per-tile - 1 long, so never
+// more than two) is finished by the second CTA to get there: each writes its 16 partial sums to
+// p.part[tile][first unit == 0 ? 0 : 1] and bumps p.counters[tile]; the one that finds the other's
+// partial adds the two (a + b == b + a: the result does not depend on arrival order), runs the
+// epilogue and re-arms the counter.
+template <bool BLK>
 __global__ void __launch_bounds__(kBulkThreads, 1) gemv_bulk_kernel(const GemvParams p, int stages, int* error) {
     extern __shared__ char bulk_smem[];
     constexpr int PE = 64, KU = 2, C2 = 2;  // int8: 64 k per piece, two 32-k units; B columns hi, lo
@@ -1064,18 +1079,21 @@ __global__ void __launch_bounds__(kBulkThreads, 1) gemv_bulk_kernel(const GemvPa
     const int N = p.N, K = p.K;
     const bool swiglu = p.epi == EPI_SWIGLU;
     const int half_n = N >> 1;
-    const int S = p.ksplit > 1 ? p.ksplit : 1;
-    const int KS = K / S;                 // k per unit (a multiple of PE)
-    const int npieces = K / PE;           // pieces of a whole row (x staging)
-    const int npu = KS / PE;              // pieces per unit
+    constexpr bool blocked = BLK;
+    const int kb = blocked ? kWeightBlock : K;  // k per block (row-major: the whole row)
+    const int nb = K / kb;                      // blocks per row
+    const int G = blocked ? p.ugroup : 1;       // blocks per unit
+    const int ug = blocked ? (nb + G - 1) / G : 1;  // units per tile
+    const int ppb = kb / PE;                    // pieces per block
+    const int npieces = K / PE;                // pieces of a whole row (x staging)
     const int ntiles = swiglu ? (half_n + 7) / 8 : (N + 15) / 16;
-    const int nunits = ntiles * S;
+    const int nunits = ntiles * ug;
     const int u_begin = static_cast<int>(static_cast<long long>(nunits) * blockIdx.x / gridDim.x);
     const int u_end = static_cast<int>(static_cast<long long>(nunits) * (blockIdx.x + 1) / gridDim.x);
     char* const base = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(bulk_smem) + 1023) & ~uintptr_t(1023));
     char* xs = base;
     char* ring = base + bulk_xs_bytes(K);
-    const size_t stage_bytes = static_cast<size_t>(16) * KS;
+    const size_t stage_bytes = static_cast<size_t>(16) * kb * G;
     uint64_t* full = reinterpret_cast<uint64_t*>(ring + stages * stage_bytes);
     uint64_t* empty = full + kBulkMaxStages;
     const char* W = static_cast<const char*>(p.w);
@@ -1107,7 +1125,7 @@ __global__ void __launch_bounds__(kBulkThreads, 1) gemv_bulk_kernel(const GemvPa
                     break;
                 }
                 char* dst = ring + s * stage_bytes;
-                const int tile = u / S, seg = u - tile * S;
+                const int tile = u / ug, uj = u - tile * ug;
                 if (swiglu) {
                     const int r0 = tile * 8, nr = min(8, half_n - r0);
                     const uint32_t bytes = static_cast<uint32_t>(nr) * K;
@@ -1116,7 +1134,7 @@ __global__ void __launch_bounds__(kBulkThreads, 1) gemv_bulk_kernel(const GemvPa
                                  : "memory");
                     bulk_copy(dst, W + static_cast<long long>(r0) * K, bytes, &full[s]);
                     bulk_copy(dst + 8 * K, W + static_cast<long long>(half_n + r0) * K, bytes, &full[s]);
-                } else if (S == 1) {
+                } else if constexpr (!blocked) {
                     const int r0 = tile * 16, nr = min(16, N - r0);
                     const uint32_t bytes = static_cast<uint32_t>(nr) * K;
                     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bulk_smem_u32(&full[s])),
@@ -1124,13 +1142,14 @@ __global__ void __launch_bounds__(kBulkThreads, 1) gemv_bulk_kernel(const GemvPa
                                  : "memory");
                     bulk_copy(dst, W + static_cast<long long>(r0) * K, bytes, &full[s]);
                 } else {
-                    const int r0 = tile * 16, nr = min(16, N - r0);
+                    // Blocks [uj * G, uj * G + nblk) of the tile: contiguous in the blocked layout.
+                    const int nblk = min(G, nb - uj * G);
+                    const uint32_t bytes = static_cast<uint32_t>(nblk) * 16 * kb;
                     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bulk_smem_u32(&full[s])),
-                                 "r"(static_cast<uint32_t>(nr * KS))
+                                 "r"(bytes)
                                  : "memory");
-                    const char* src = W + static_cast<long long>(r0) * K + static_cast<long long>(seg) * KS;
-                    for (int r = 0; r < nr; ++r)
-                        bulk_copy(dst + r * KS, src + static_cast<long long>(r) * K, static_cast<uint32_t>(KS), &full[s]);
+                    bulk_copy(dst, W + static_cast<long long>(tile) * 16 * K + static_cast<long long>(uj) * G * 16 * kb,
+                              bytes, &full[s]);
                 }
             }
         }
@@ -1266,21 +1285,22 @@ __global__ void __launch_bounds__(kBulkThreads, 1) gemv_bulk_kernel(const GemvPa
         epilogue(tile, y0, y1);
     };
 
-    // This warp's pieces of every unit.
-    const int p0 = warp * npu / kBulkCW, p1 = (warp + 1) * npu / kBulkCW;
     const int col_off = g * 64 + t * 16;
     float sc0 = 0.f, sc1 = 0.f;  // the row scales of the tile this warp reduces next
     float acc[4] = {0.f, 0.f, 0.f, 0.f}, acc2[4] = {0.f, 0.f, 0.f, 0.f};
-    int seg_first = 0;  // first segment of the current tile in this CTA's range
+    int seg_first = 0;  // first unit of the current tile in this CTA's range
     int j = 0;          // tiles finished by this CTA (reducer rotation, red[] buffer parity)
     for (int u = u_begin, i = 0; u < u_end; ++u, ++i) {
         const int s = i % stages;
-        const int tile = u / S, seg = u - tile * S;
-        const bool first = i == 0 || seg == 0;
-        const bool last = u + 1 == u_end || seg == S - 1;
+        const int tile = u / ug, uj = u - tile * ug;
+        const bool first = i == 0 || uj == 0;
+        const bool last = u + 1 == u_end || uj == ug - 1;
+        // This warp's pieces of the unit (a unit of nblk blocks has nblk * ppb pieces).
+        const int npu = blocked ? min(G, nb - uj * G) * ppb : npieces;
+        const int p0 = warp * npu / kBulkCW, p1 = (warp + 1) * npu / kBulkCW;
         const bool reducer = warp == kBulkCW - 1 - (j & (kBulkCW - 1));
         if (first) {
-            seg_first = seg;
+            seg_first = uj;
 #pragma unroll
             for (int e = 0; e < 4; ++e) acc[e] = acc2[e] = 0.f;
             if (reducer) {
@@ -1300,10 +1320,16 @@ __global__ void __launch_bounds__(kBulkThreads, 1) gemv_bulk_kernel(const GemvPa
             atomicExch(&abort_s, 1);
         }
         const char* st = ring + s * stage_bytes + t * 16;
-        const int xpiece0 = seg * npu;  // this unit's first piece in the staged activations
+        const int xpiece0 = uj * G * ppb;  // this unit's first piece in the staged activations
+        // Rows g and g + 8 of piece `piece`: blocked, block piece / 8 of the stage (kWeightBlock = 512 =
+        // 8 pieces), row r of the block; row-major, the stage is the tile with rows K apart.
+        const char* wg0 = st + static_cast<size_t>(g) * kb;
+        const char* wg1 = st + static_cast<size_t>(g + 8) * kb;
         for (int piece = p0; piece < p1; ++piece) {
-            const uint4 w0 = *reinterpret_cast<const uint4*>(st + static_cast<size_t>(g) * KS + piece * PE);
-            const uint4 w1 = *reinterpret_cast<const uint4*>(st + static_cast<size_t>(g + 8) * KS + piece * PE);
+            const size_t off = blocked ? static_cast<size_t>(piece >> 3) * (16 * kWeightBlock) + (piece & 7) * PE
+                                       : static_cast<size_t>(piece) * PE;
+            const uint4 w0 = *reinterpret_cast<const uint4*>(wg0 + off);
+            const uint4 w1 = *reinterpret_cast<const uint4*>(wg1 + off);
             const char* ub = xs + static_cast<size_t>((xpiece0 + piece) * KU) * C2 * 64 + col_off;
             uint32_t b[8];
 #pragma unroll
@@ -1337,42 +1363,35 @@ __global__ void __launch_bounds__(kBulkThreads, 1) gemv_bulk_kernel(const GemvPa
             }
             y0 *= oscale_s * sc0;
             y1 *= oscale_s * sc1;
-            if (seg_first == 0 && seg == S - 1) epilogue(tile, y0, y1);
+            if constexpr (!blocked) epilogue(tile, y0, y1);
+            else if (seg_first == 0 && uj == ug - 1) epilogue(tile, y0, y1);
             else fixup(tile, seg_first == 0 ? 0 : 1, y0, y1);
         }
         ++j;
     }
 }
 
-// Split count of the one-row bulk GEMV: 1 (whole 16-row tiles per CTA) when there are at least 8 tiles
-// per SM. Otherwise S > 1 dividing K's 64-k pieces such that a unit keeps >= 3 stages in shared memory,
-// >= 8 pieces and >= 512 bytes per row copy, and every CTA's range is >= S - 1 units long (a tile then
-// spans at most two CTAs): the smallest such S giving every SM >= 6 units, else the largest giving >= 2;
-// 0 = no bulk GEMV.
-int bulk_split(const GemvParams& p, int sm_count) {
+// Unit size of the one-row bulk GEMV, in k blocks (0 = the kernel does not apply): row-major weights
+// take whole 16-row tiles when there are at least 8 tiles per SM (returns 1); blocked weights take the
+// largest group of G <= 4 blocks that still gives every SM >= 6 units (smaller units balance the SMs,
+// larger ones stream faster), keeps >= 3 stages in shared memory and every CTA's range at least
+// units-per-tile - 1 long (a tile then spans at most two CTAs).
+int bulk_group(const GemvParams& p, int sm_count) {
     const int ntiles = p.epi == EPI_SWIGLU ? (p.N / 2 + 7) / 8 : (p.N + 15) / 16;
-    if (ntiles >= 8 * sm_count) return bulk_stages(p.K, p.K) >= 2 ? 1 : 0;
-    if (p.epi == EPI_SWIGLU || !p.part || !p.counters || p.counter_count < ntiles) return 0;
-    const int npieces = p.K / 64;
-    static const int forced = [] {
-        const char* e = getenv("L0B_BULK_SPLIT");
-        return e ? atoi(e) : -1;
-    }();
-    int best = 0;
-    for (int S = 2; S <= 32; ++S) {
-        if (npieces % S != 0) continue;
-        const int KS = p.K / S;
-        const long long units = static_cast<long long>(ntiles) * S;
-        if (npieces / S < 8 || KS < 512) break;
-        if (bulk_stages(p.K, KS) < 3 || units / sm_count < S - 1 || units < 2LL * sm_count) continue;
-        if (forced >= 0) {
-            if (S == forced) return S;
-            continue;
-        }
-        best = S;
-        if (units >= 6LL * sm_count) return S;
+    if (p.kb <= 0) return ntiles >= 8 * sm_count && bulk_stages(p.K, p.K) >= 2 ? 1 : 0;
+    if (p.epi == EPI_SWIGLU || p.N % 16 != 0 || p.K % p.kb != 0 || p.kb != kWeightBlock) return 0;
+    if (!p.part || !p.counters || p.counter_count < ntiles) return 0;
+    const int nb = p.K / p.kb;
+    // Short rows (q/k/v and o_proj at K = 3584: 7 blocks) stream faster on the register GEMV, whose
+    // consumers need no stage round trip; long ones (down at K = 18944: 37 blocks) on the bulk GEMV.
+    if (nb < 16) return 0;
+    for (int G = 4; G >= 1; --G) {
+        const int ug = (nb + G - 1) / G;
+        const long long units = static_cast<long long>(ntiles) * ug;
+        if (bulk_stages(p.K, G * p.kb) < 3 || units / sm_count < ug - 1) continue;
+        if (units >= 6LL * sm_count || G == 1) return G;
     }
-    return forced >= 0 ? 0 : best;
+    return 0;
 }
 
 // One activation row, int8 with one scale per row, 16-byte aligned, and a split (above) that applies.
@@ -1382,23 +1401,27 @@ bool bulk_applies(int w_dtype, const GemvParams& p, int sm_count) {
     if (reinterpret_cast<uintptr_t>(p.w) % 16 != 0 || (p.x_dtype == L0B_F32 && (reinterpret_cast<uintptr_t>(p.x) & 15)))
         return false;
     if (p.norm_w && (reinterpret_cast<uintptr_t>(p.norm_w) & 15)) return false;
-    return bulk_split(p, sm_count) > 0;
+    return bulk_group(p, sm_count) > 0;
 }
 
 l0b_status launch_bulk(l0b_device* dev, cudaStream_t stream, int sm_count, GemvParams p) {
     static bool configured = false;
     if (!configured) {
-        cudaError_t e = cudaFuncSetAttribute(gemv_bulk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             kBulkSmemBudget);
-        if (e != cudaSuccess) return fail(L0B_ERR_CUDA, "cudaFuncSetAttribute failed: %s", cudaGetErrorString(e));
+        for (const void* f : {reinterpret_cast<const void*>(gemv_bulk_kernel<true>),
+                              reinterpret_cast<const void*>(gemv_bulk_kernel<false>)}) {
+            cudaError_t e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, kBulkSmemBudget);
+            if (e != cudaSuccess) return fail(L0B_ERR_CUDA, "cudaFuncSetAttribute failed: %s", cudaGetErrorString(e));
+        }
         configured = true;
     }
-    p.ksplit = bulk_split(p, sm_count);
-    const int KS = p.K / p.ksplit;
-    const int stages = bulk_stages(p.K, KS);
-    const size_t smem = bulk_smem_bytes(p.K, stages, KS);
+    p.ugroup = bulk_group(p, sm_count);
+    const int UK = p.kb > 0 ? p.ugroup * p.kb : p.K;  // k per stage
+    const int stages = bulk_stages(p.K, UK);
+    const size_t smem = bulk_smem_bytes(p.K, stages, UK);
     int* err = dev ? dev->error_flag : nullptr;
-    return launch_on(dev, stream, gemv_bulk_kernel, dim3(sm_count), dim3(kBulkThreads), smem, p, stages, err);
+    if (p.kb > 0)
+        return launch_on(dev, stream, gemv_bulk_kernel<true>, dim3(sm_count), dim3(kBulkThreads), smem, p, stages, err);
+    return launch_on(dev, stream, gemv_bulk_kernel<false>, dim3(sm_count), dim3(kBulkThreads), smem, p, stages, err);
 }
 
 // Resident CTAs per SM for (kernel, dynamic smem), cached: the persistent grid is SMs x this.
@@ -1514,6 +1537,17 @@ l0b_status launch_typed(l0b_device* dev, cudaStream_t stream, int sm_count, Gemv
     const int M = p.M;
     if constexpr (sizeof(WT) == 1) {
         if (bulk_applies(L0B_I8, p, sm_count)) return launch_bulk(dev, stream, sm_count, p);
+    }
+    L0B_REQUIRE(p.kb == 0 || p.kb == kWeightBlock, L0B_ERR_ARGUMENT, "blocked layout with %d k per block", p.kb);
+    if (p.kb > 0) {
+        // Blocked weights are read by the tensor-core kernels only (the fp32-FMA kernel has no blocked
+        // addressing): refuse rather than read the bytes in the wrong order.
+        GemvParams t8 = p;
+        t8.M = M < 8 ? M : 8;
+        int ok = 0;
+        if constexpr (sizeof(WT) == 1) ok = mma_applies<WT>(t8, t8.M);
+        L0B_REQUIRE(ok > 0, L0B_ERR_UNSUPPORTED,
+                    "int8 weights in the blocked layout need the tensor-core GEMV (N=%d K=%d M=%d)", p.N, p.K, M);
     }
     for (int m0 = 0; m0 < M;) {
         GemvParams q = p;
@@ -1641,6 +1675,13 @@ __global__ void __launch_bounds__(256) gemm_f32_kernel(int M, int N, int K, cons
 
 void gemv_set_tensor_cores(bool on) { g_gemv_mma = on; }
 void gemv_set_bulk(bool on) { g_gemv_bulk = on; }
+
+namespace {
+bool g_weight_blocking = true;  // l0b_set_weight_blocking
+}  // namespace
+
+bool weight_blocking() { return g_weight_blocking; }
+void set_weight_blocking(bool on) { g_weight_blocking = on; }
 
 l0b_status gemv_nk_launch(l0b_device* dev, int w_dtype, GemvParams p) {
     return gemv_dispatch(dev, dev->stream, dev->sm_count, w_dtype, p);

@@ -20,8 +20,17 @@ struct GemvSeg {
     int ld;             // output row stride in elements
 };
 
+// Blocked int8 weight layout (kb > 0): [N / 16][K / kb][16][kb] bytes, so the 16 rows x kb columns of
+// one (row tile, k block) are one contiguous block and consecutive blocks of a tile are adjacent; a
+// 16-row tile keeps the byte range it has in the row-major layout. Byte offset of element (r, c) of an
+// N x K matrix:
+__host__ __device__ inline long long blocked_index(long long r, long long c, long long K, int kb) {
+    return ((r >> 4) * (K / kb) + c / kb) * 16LL * kb + (r & 15) * kb + c % kb;
+}
+constexpr int kWeightBlock = 512;  // k per block of the blocked layout
+
 struct GemvParams {
-    const void* w;         // [N, K] row-major weights
+    const void* w;         // [N, K] row-major weights (or blocked, see kb)
     const void* scales;    // int8: f16 [N, K / group]
     int group;             // int8 scale group; >= K means one scale per output row
     int N, K, M;           // W rows, inner dim, activation rows
@@ -38,13 +47,13 @@ struct GemvParams {
     int argmax_base;             // index of W's row 0 in the argmax (vocab shard offset under TP)
     int kt;                      // K elements per shared-memory tile (a multiple of 512)
     int prefetch;                // prefetch the first row block of weights into L2 before pdl_wait
-    // Split-K scratch of the one-row bulk GEMV (null: no split): part >= 32 floats per 16-row tile,
-    // counters >= one per tile, zero at rest (every launch leaves them zero). ksplit is set by the
-    // dispatcher.
+    // Split-K scratch of the one-row bulk GEMV over blocked weights (null: no split): part >= 32 floats
+    // per 16-row tile, counters >= one per tile, zero at rest (every launch leaves them zero).
     float* part;
     unsigned* counters;
     int counter_count;
-    int ksplit;
+    int kb;      // > 0: int8 W in the blocked layout with this k per block (N % 16 == 0, K % kb == 0)
+    int ugroup;  // bulk GEMV: k blocks per unit (set by the dispatcher)
 };
 
 // Launches y = x * W^T with the fused options in `p` (fills kt and the grid). `w_dtype` is
@@ -57,6 +66,10 @@ void gemv_set_tensor_cores(bool on);
 // Process-wide choice of the bulk-copy kernel for one activation row where it applies (default on);
 // launches already recorded keep their kernel.
 void gemv_set_bulk(bool on);
+// Process-wide: models created afterwards store their int8 per-row-scaled projections with few row
+// tiles in the blocked layout (default on).
+bool weight_blocking();
+void set_weight_blocking(bool on);
 
 // Raw-stream variant (no device handle): immediate launch on `stream`.
 l0b_status gemv_nk_launch_stream(cudaStream_t stream, int sm_count, int w_dtype, GemvParams p);

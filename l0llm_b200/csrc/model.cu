@@ -120,11 +120,17 @@ struct l0b_model {
         *out = static_cast<T*>(p);
         return L0B_OK;
     }
-    l0b_status alloc_matrix(ModelMatrix& m, int n, int k) {
+    // Int8 per-row-scaled projections with few 16-row tiles (under 8 per SM: q/k/v, o_proj, down) go in
+    // the blocked layout, whose units of contiguous k blocks the one-row bulk GEMV streams as whole copies.
+    l0b_status alloc_matrix(ModelMatrix& m, int n, int k, bool may_block = true) {
         m.n = n;
         m.k = k;
         m.dtype = wdtype;
         m.group = wdtype == L0B_I8 ? (group > 0 ? group : k) : 0;
+        m.kb = (may_block && weight_blocking() && wdtype == L0B_I8 && m.group >= k && k % kWeightBlock == 0 &&
+                n % 16 == 0 && n / 16 < 8 * dev->sm_count)
+                   ? kWeightBlock
+                   : 0;
         if (wdtype == L0B_I8) {
             L0B_REQUIRE(k % m.group == 0, L0B_ERR_UNSUPPORTED, "int8 scale group %d does not divide K %d", m.group, k);
             int8_t* w;
@@ -158,8 +164,11 @@ enum SynthMode { SYN_NORMAL = 0, SYN_CONST = 1, SYN_I8 = 2, SYN_UNIFORM = 3 };
 
 // Element i of the destination maps to index (row0 + i / row_len) * full_len + col0 + i % row_len of the
 // full HuggingFace tensor, so a tensor-parallel shard holds exactly the values of the full tensor.
+// int8 destinations in the blocked layout (blk_kb > 0): element i goes to row blk_row0 + i / row_len,
+// column i % row_len of a blocked matrix with blk_k columns.
 __global__ void synth_kernel(void* dst, int dtype, long long count, uint64_t stream, int mode, float a, float b,
-                             long long row_len, long long full_len, long long row0, long long col0) {
+                             long long row_len, long long full_len, long long row0, long long col0, long long blk_k,
+                             int blk_kb, long long blk_row0) {
     pdl_wait();
     for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < count;
          i += static_cast<long long>(gridDim.x) * blockDim.x) {
@@ -167,7 +176,8 @@ __global__ void synth_kernel(void* dst, int dtype, long long count, uint64_t str
         const long long idx = (row0 + r) * full_len + col0 + (i - r * row_len);
         const uint64_t bits = splitmix64(stream + static_cast<uint64_t>(idx) * 0xD1B54A32D192ED03ULL);
         if (mode == SYN_I8) {
-            static_cast<int8_t*>(dst)[i] = static_cast<int8_t>(static_cast<int>(bits % 255ULL) - 127);
+            const long long di = blk_kb > 0 ? blocked_index(blk_row0 + r, i - r * row_len, blk_k, blk_kb) : i;
+            static_cast<int8_t*>(dst)[di] = static_cast<int8_t>(static_cast<int>(bits % 255ULL) - 127);
             continue;
         }
         float v;
@@ -183,6 +193,17 @@ __global__ void synth_kernel(void* dst, int dtype, long long count, uint64_t str
             v = a;
         }
         store_from_float(dst, dtype, i, v);
+    }
+}
+
+// Columns [col0, col0 + cols) of `rows` row-major int8 rows (row stride src_ld) into rows
+// [dst_row0, dst_row0 + rows) of an int8 matrix in the blocked layout (K columns, kb per block).
+__global__ void scatter_blocked_kernel(const int8_t* src, long long src_ld, long long col0, long long rows, long long cols,
+                                       int8_t* dst, long long K, int kb, long long dst_row0) {
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < rows * cols;
+         i += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const long long r = i / cols, c = i - r * cols;
+        dst[blocked_index(dst_row0 + r, c, K, kb)] = src[r * src_ld + col0 + c];
     }
 }
 
@@ -259,12 +280,14 @@ struct Synth {
     float std;
     float lo, hi;
     l0b_status fill(void* dst, int dtype, long long count, uint64_t id, int mode, float a, float b,
-                    long long row_len = 0, long long full_len = 0, long long row0 = 0, long long col0 = 0) {
+                    long long row_len = 0, long long full_len = 0, long long row0 = 0, long long col0 = 0,
+                    long long blk_k = 0, int blk_kb = 0, long long blk_row0 = 0) {
         if (count == 0) return L0B_OK;
         if (row_len <= 0) row_len = count;
         if (full_len <= 0) full_len = row_len;
         synth_kernel<<<grid_for(count, m->dev->sm_count), 256, 0, m->dev->stream>>>(
-            dst, dtype, count, tensor_stream(seed, id), mode, a, b, row_len, full_len, row0, col0);
+            dst, dtype, count, tensor_stream(seed, id), mode, a, b, row_len, full_len, row0, col0, blk_k, blk_kb,
+            blk_row0);
         L0B_CHECK_CUDA(cudaGetLastError());
         return L0B_OK;
     }
@@ -274,8 +297,13 @@ struct Synth {
                       int row0, int col0) {
         const long long count = static_cast<long long>(rows) * cols;
         if (mat.dtype == L0B_I8) {
-            int8_t* q = static_cast<int8_t*>(mat.w) + static_cast<long long>(dst_row) * mat.k;
-            L0B_TRY(fill(q, L0B_I8, count, id, SYN_I8, 0.f, 0.f, cols, full_k, row0, col0));
+            if (mat.kb > 0) {
+                L0B_TRY(fill(mat.w, L0B_I8, count, id, SYN_I8, 0.f, 0.f, cols, full_k, row0, col0, mat.k, mat.kb,
+                             dst_row));
+            } else {
+                int8_t* q = static_cast<int8_t*>(mat.w) + static_cast<long long>(dst_row) * mat.k;
+                L0B_TRY(fill(q, L0B_I8, count, id, SYN_I8, 0.f, 0.f, cols, full_k, row0, col0));
+            }
             // Scales: one per (row, group) of the full tensor; a column shard takes its groups. With one
             // scale per output row (group = this shard's K) every column shard takes the row's only scale.
             const bool per_row = mat.group >= mat.k;
@@ -325,6 +353,7 @@ GemvParams linear_params(const ModelMatrix& w, int m_rows, const void* x, long l
     p.out_dtype = L0B_F32;
     p.nseg = 1;
     p.prefetch = 1;
+    p.kb = w.kb;
     return p;
 }
 
@@ -375,6 +404,7 @@ l0b_status gemv(l0b_model* m, const ModelMatrix& w, const GemvParams& p) {
     a.split = 1;
     a.rscale = m->rscale;
     a.wscale = w.dtype == L0B_I8 ? w.scales : nullptr;
+    a.kb = w.kb;
     a.argmax = p.argmax;
     a.argmax_base = p.argmax_base;
     return tc_gemm_launch(m->dev, a);
@@ -984,7 +1014,7 @@ L0B_API l0b_status l0b_model_create(l0b_device* dev, l0b_suite* suite, const l0b
     // Weights.
     L0B_TRY(m->alloc(&m->embed, static_cast<size_t>(c.vocab_size) * m->h));
     L0B_TRY(m->alloc(&m->final_norm, m->h));
-    L0B_TRY(m->alloc_matrix(m->lm_head, m->vocab, m->h));
+    L0B_TRY(m->alloc_matrix(m->lm_head, m->vocab, m->h, false));
     m->layers.resize(c.num_layers);
     const size_t cache_elems = static_cast<size_t>(m->batch_cap) * max_seq_len * m->kvdim;
     for (auto& L : m->layers) {
@@ -1133,9 +1163,17 @@ L0B_API l0b_status l0b_model_set_tensor(l0b_model* m, const char* name, const fl
             l0b_status s = k_quantize(m->dev, rows_f, L0B_F32, t.rows, t.full_cols, gfull, q_full, s_full);
             m->dev->recording = was;
             L0B_TRY(s);
-            int8_t* qdst = static_cast<int8_t*>(mat.w) + static_cast<long long>(t.dst_row) * mat.k;
-            L0B_CHECK_CUDA(cudaMemcpy2DAsync(qdst, mat.k, q_full + t.col0, t.full_cols, t.cols, t.rows,
-                                             cudaMemcpyDeviceToDevice, st));
+            if (mat.kb > 0) {
+                const long long n = static_cast<long long>(t.rows) * t.cols;
+                scatter_blocked_kernel<<<grid_for(n, sm), 256, 0, st>>>(q_full, t.full_cols, t.col0, t.rows, t.cols,
+                                                                        static_cast<int8_t*>(mat.w), mat.k, mat.kb,
+                                                                        t.dst_row);
+                L0B_CHECK_CUDA(cudaGetLastError());
+            } else {
+                int8_t* qdst = static_cast<int8_t*>(mat.w) + static_cast<long long>(t.dst_row) * mat.k;
+                L0B_CHECK_CUDA(cudaMemcpy2DAsync(qdst, mat.k, q_full + t.col0, t.full_cols, t.cols, t.rows,
+                                                 cudaMemcpyDeviceToDevice, st));
+            }
             if (gfull == t.full_cols) {
                 L0B_REQUIRE(t.cols == t.full_cols || mat.group == mat.k, L0B_ERR_UNSUPPORTED, "scale layout");
                 L0B_CHECK_CUDA(cudaMemcpyAsync(mat.scales + t.dst_row, s_full, static_cast<size_t>(t.rows) * sizeof(__half),
@@ -1559,6 +1597,15 @@ L0B_API l0b_status l0b_model_read_weight(l0b_model* m, int32_t layer, int32_t ki
     L0B_REQUIRE(static_cast<size_t>(bytes) == size, L0B_ERR_ARGUMENT, "storage is %zu bytes, %lld requested", size,
                 (long long)bytes);
     L0B_CHECK_CUDA(cudaStreamSynchronize(m->dev->stream));
+    if (kind < 4 && mat.kb > 0) {
+        // Back to the [out, in] order.
+        std::vector<int8_t> tmp(size);
+        L0B_CHECK_CUDA(copy_sync(m->dev->stream, tmp.data(), src, size, cudaMemcpyDeviceToHost));
+        int8_t* o = static_cast<int8_t*>(out);
+        for (long long r = 0; r < mat.n; ++r)
+            for (long long c = 0; c < mat.k; ++c) o[r * mat.k + c] = tmp[blocked_index(r, c, mat.k, mat.kb)];
+        return L0B_OK;
+    }
     L0B_CHECK_CUDA(copy_sync(m->dev->stream, out, src, size, cudaMemcpyDeviceToHost));
     return L0B_OK;
     GUARD_END

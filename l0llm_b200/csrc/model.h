@@ -18,6 +18,7 @@ struct ModelMatrix {
     void* w = nullptr;
     __half* scales = nullptr;
     int group = 0;  // int8 scale group (k = per output channel)
+    int kb = 0;     // > 0: int8 weights in the blocked layout (gemv.cuh blocked_index), 0: row-major
     size_t bytes() const {
         size_t b = static_cast<size_t>(n) * k * dtype_size(static_cast<l0b_dtype>(dtype));
         if (dtype == L0B_I8) b += static_cast<size_t>(n) * (k / group) * 2;

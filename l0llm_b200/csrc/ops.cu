@@ -670,6 +670,11 @@ L0B_API l0b_status l0b_set_gemv_bulk(int32_t enable) {
     return L0B_OK;
 }
 
+L0B_API l0b_status l0b_set_weight_blocking(int32_t enable) {
+    set_weight_blocking(enable != 0);
+    return L0B_OK;
+}
+
 L0B_API l0b_status l0b_set_gemv_tensor_cores(int32_t enable) {
     gemv_set_tensor_cores(enable != 0);
     return L0B_OK;

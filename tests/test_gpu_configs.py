@@ -17,12 +17,13 @@ synthetic int8 weights (codes uniform in +-127 times scales up to 0.02: weights 
 activations reach ~1e7 and attention scores ~1e3, so attention is nearly one-hot and a 1e-7 relative
 perturbation of any projection grows, through near-ties between attended positions, to ~1e-3 of the
 logit range (tests/test_cpu_oracle.py::test_config2_weights_amplify_rounding shows the oracle's fp32
-and double builds failing the elementwise bar against each other; over 64 decode steps after a
-128-token prompt they differ by 3.4e-4 of the range at the median and 4.3e-3 at worst). A full-depth
-config-2 comparison therefore holds: every greedy token (teacher-forced argmax and the free-running
-device decode) equal to the oracle's unless the oracle's top-2 margin is inside the step's measured
-error; the per-step maximum error at a median of <= 2e-3 of the logit range; and no step above 3e-2 of
-it.
+and double builds failing the elementwise bar against each other; over 64 decode steps they differ by
+3.4e-4 of the range at the median and 4.3e-3 at worst after a 128-token prompt, and by 1.9e-4 at the
+median but 7.2e-2 at worst after a 32-token prompt, where fewer attended positions make a flipped
+near-tie weigh more). A full-depth config-2 comparison therefore holds: every greedy token
+(teacher-forced argmax and the free-running device decode) equal to the oracle's unless the oracle's
+top-2 margin is inside the step's measured error; the per-step maximum error at a median of <= 2e-3 of
+the logit range; and no step above 0.15 of it (twice the oracle's own worst spread).
 """
 from __future__ import annotations
 
@@ -128,7 +129,7 @@ def config2_check(got_rows, want_rows, tf_tokens, dev_tokens, oracle_tokens, wha
                 f"{what} device greedy step {i}: {dev_tokens[i]} != {oracle_tokens[i]} with margin {margin:.3e}")
     med, worst = float(np.median(rel)), max(rel)
     assert med <= 2e-3, f"{what}: median per-step max error {med:.3e} of the logit range (> 2e-3)"
-    assert worst <= 3e-2, f"{what}: a step's max error reached {worst:.3e} of the logit range (> 3e-2)"
+    assert worst <= 0.15, f"{what}: a step's max error reached {worst:.3e} of the logit range (> 0.15)"
     return med, worst, first_mismatch
 
 

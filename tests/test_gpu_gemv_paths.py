@@ -195,3 +195,64 @@ def test_gemv_bulk_model_matches_register_path(lz, device, suite):
     np.testing.assert_array_equal(out[0][0], out[1][0])
     scale = float(np.abs(out[0][1]).max())
     assert float(np.abs(out[0][1] - out[1][1]).max()) <= 1e-4 * scale
+
+
+CFG2_W = dict(hidden_size=3584, intermediate_size=18944, num_attention_heads=28, num_key_value_heads=4, head_dim=128,
+              vocab_size=152064, max_position_embeddings=32768, rms_norm_eps=1e-6, rope_theta=1e6, attention_bias=1,
+              q8_group=0)
+
+
+def test_blocked_layout_model_matches_row_major(lz, device, suite):
+    """q/k/v, o_proj and down of config-2 widths are stored in the blocked layout ([N/16][K/512][16][512]):
+    the same model built row-major gives the same prefill logits (tcgen05 GEMM, 4-D tensor map), the same
+    one-row decode (bulk GEMV over units of contiguous blocks, with the two-CTA tile fixup), the same
+    batch-5 decode (register-streamed GEMV, blocked addressing) and batch-12 decode (tcgen05 GEMM)."""
+    lib = lz.load_library()
+    prompts = [np.random.default_rng(40 + s).integers(0, 152064, 9 + 3 * s).astype(np.int32) for s in range(12)]
+    out = {}
+    for blocked in (1, 0):
+        lib.l0b_set_weight_blocking(blocked)
+        try:
+            mc = lz.model_config(kv_dtype=lz.F16, num_layers=2, max_batch=12, **CFG2_W)
+            with lz.LlmModel(device, suite, mc, 96, "int8") as model:
+                model.init_synthetic(2, 0.02, 1e-3, 2e-2)
+                r = {"prefill": model.Prefill(prompts[0]), "greedy": model.decode_greedy_device(6)}
+                firsts = [model.PrefillSequence(s, p) for s, p in enumerate(prompts)]
+                toks = np.array([int(np.argmax(f)) for f in firsts], np.int32)
+                pos = np.array([len(p) for p in prompts], np.int32)
+                r["batch5"] = model.DecodeBatch(toks[:5], pos[:5])
+                for s, p in enumerate(prompts):
+                    model.PrefillSequence(s, p, want_logits=False)
+                r["batch12"] = model.DecodeBatch(toks, pos)
+                r["o_proj"] = model.read_weight(1, 1, np.int8, 3584 * 3584)
+                out[blocked] = r
+        finally:
+            lib.l0b_set_weight_blocking(1)
+    a, b = out[1], out[0]
+    np.testing.assert_array_equal(a["greedy"], b["greedy"])
+    np.testing.assert_array_equal(a["o_proj"], b["o_proj"])
+    for key in ("prefill", "batch5", "batch12"):
+        scale = float(np.abs(b[key]).max())
+        err = float(np.abs(a[key] - b[key]).max())
+        assert err <= 1e-4 * scale, f"{key}: blocked vs row-major max err {err} (scale {scale})"
+
+
+def test_blocked_layout_set_tensor_round_trip(lz, device, suite):
+    """Uploaded HF tensors land in the blocked layout and read back in [out, in] order as the host
+    quantizer's codes; the stacked q/k/v rows keep their offsets."""
+    mc = lz.model_config(kv_dtype=lz.F16, num_layers=1, **CFG2_W)
+    rng = np.random.default_rng(9)
+    with lz.LlmModel(device, suite, mc, 8, "int8") as model:
+        want = {}
+        for name, (n, k) in {"self_attn.q_proj": (3584, 3584), "self_attn.k_proj": (512, 3584),
+                             "self_attn.v_proj": (512, 3584), "self_attn.o_proj": (3584, 3584),
+                             "mlp.down_proj": (3584, 18944)}.items():
+            hf = ((rng.random((n, k)) * 2 - 1) * 0.05).astype(np.float32)
+            model.set_tensor(f"model.layers.0.{name}.weight", hf)
+            want[name] = lz.q8_quantize_out_in(hf, k)
+        qkv = np.concatenate([want[n][0] for n in ("self_attn.q_proj", "self_attn.k_proj", "self_attn.v_proj")])
+        np.testing.assert_array_equal(model.read_weight(0, 0, np.int8, qkv.size).reshape(qkv.shape), qkv)
+        np.testing.assert_array_equal(model.read_weight(0, 1, np.int8, 3584 * 3584).reshape(3584, 3584),
+                                      want["self_attn.o_proj"][0])
+        np.testing.assert_array_equal(model.read_weight(0, 3, np.int8, 3584 * 18944).reshape(3584, 18944),
+                                      want["mlp.down_proj"][0])
