@@ -334,6 +334,12 @@ L0B_API l0b_status l0b_gated_delta_execute_grouped(l0b_suite* s, l0b_device* d, 
                                                    l0b_buffer* norm_w, l0b_buffer* state, l0b_buffer* out,
                                                    int32_t n_k_heads, int32_t n_v_heads, int32_t key_dim,
                                                    int32_t value_dim, int32_t tokens, float eps);
+/* Tuning: calls of 16 or more tokens (prefill) run the recurrence in chunks of 64 tokens (1, default:
+ * the WY form -- per-chunk products built for every chunk in parallel, then one pass over the chunks
+ * per group of state columns; key head dim 64 or 128, value head dim a multiple of 32; scratch of
+ * ~150 KB per (value head, chunk) kept by the suite, grown outside recording) or token by token (0).
+ * No counterpart in the reference. */
+L0B_API l0b_status l0b_set_gated_delta_chunked(int32_t enable);
 
 /* ------------------------------------------------------------------------------------------ */
 /* Linear layers in the [out, in] layout, and the fused decode ops                              */

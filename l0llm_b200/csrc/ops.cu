@@ -41,6 +41,7 @@ l0b_suite::~l0b_suite() {
     if (q8_x) cudaFree(q8_x);
     if (error_flag) cudaFree(error_flag);
     if (split_part) cudaFree(split_part);
+    if (gdn_rec) cudaFree(gdn_rec);
     if (split_counters) cudaFree(split_counters);
 }
 

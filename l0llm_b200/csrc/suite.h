@@ -21,6 +21,9 @@ struct l0b_suite {
     int q8_k = 0;
     int* error_flag = nullptr;  // set by kernels that meet an out-of-range index (embedding ids)
     // Split-K scratch of the one-row bulk GEMV (l0b::kSuiteSplitTiles tiles), counters zero at rest.
+    // Records of the chunked Gated DeltaNet prefill (floats), grown on demand.
+    float* gdn_rec = nullptr;
+    long long gdn_floats = 0;
     float* split_part = nullptr;
     unsigned* split_counters = nullptr;
     std::map<std::pair<int, double>, float*> rope_tables;

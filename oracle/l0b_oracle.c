@@ -655,13 +655,16 @@ void orc_gated_delta(const float* conv, const float* z, const float* b, const fl
     const int conv_dim = 2 * hk * dk + hv * dv;
     const int rep = hv / hk;
     const double qscale = 1.0 / sqrt((double)dk);
-    double* q = (double*)malloc(sizeof(double) * (size_t)dk);
-    double* k = (double*)malloc(sizeof(double) * (size_t)dk);
-    double* o = (double*)malloc(sizeof(double) * (size_t)dv);
-    double* kv = (double*)malloc(sizeof(double) * (size_t)dv);
-    for (int t = 0; t < tokens; ++t) {
-        const float* row = conv + (int64_t)t * conv_dim;
-        for (int h = 0; h < hv; ++h) {
+    /* Value heads are independent (each owns its state and output columns): one per OpenMP iteration,
+     * its tokens in order. */
+#pragma omp parallel for schedule(dynamic)
+    for (int h = 0; h < hv; ++h) {
+        double* q = (double*)malloc(sizeof(double) * (size_t)dk);
+        double* k = (double*)malloc(sizeof(double) * (size_t)dk);
+        double* o = (double*)malloc(sizeof(double) * (size_t)dv);
+        double* kv = (double*)malloc(sizeof(double) * (size_t)dv);
+        for (int t = 0; t < tokens; ++t) {
+            const float* row = conv + (int64_t)t * conv_dim;
             const int kh = h / rep;
             const float* qs = row + (int64_t)kh * dk;
             const float* ks = row + (int64_t)hk * dk + (int64_t)kh * dk;
@@ -704,11 +707,11 @@ void orc_gated_delta(const float* conv, const float* z, const float* b, const fl
                 out[(int64_t)t * hv * dv + (int64_t)h * dv + j] = (float)((double)(float)(o[j] * rstd) * norm_w[j] * gate);
             }
         }
+        free(q);
+        free(k);
+        free(o);
+        free(kv);
     }
-    free(q);
-    free(k);
-    free(o);
-    free(kv);
 }
 
 /* ------------------------------------------------------------------------------------------------ */
