@@ -63,6 +63,16 @@ def peaks() -> tuple[float, str]:
     return 6650.0, "fallback"
 
 
+def tflops_peak() -> float:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return float(json.loads(p.read_text())["bf16_tflops"])
+        except Exception:
+            pass
+    return 1590.0
+
+
 class ClockSampler:
     """SM clocks and clock-event (throttle) reasons read every 20 ms through NVML (the library nvidia-smi
     reports from; reads only) on a host thread, each sample time-stamped so that only samples taken
@@ -292,35 +302,113 @@ def dominant_kernel_roofline(lz, dev, suite, stream_ptr, torch, peak: float, pea
             "avg_us": round(avg_ms * 1e3, 2)}
 
 
-def run_cfg3_deltanet(args) -> int:
+def measure_cfg0(lz, dev, suite, stream_ptr, torch, peak: float, peak_kind: str, tflops_peak: float) -> dict:
+    """Config 0: the single linear op y = x W^T with W int8 [4864, 896] (codes uniform in [-127, 127],
+    fp16 per-row scales U[1e-3, 2e-2]) and x from N(0, 1) (fp16 values, f32 storage), seed 0: one row
+    (decode GEMV, l0b_linear) and 128 rows (prefill GEMM on the tcgen05 kernel, l0b_linear_tc), each over
+    40 rotating weight copies (174 MB > L2), CUDA events."""
+    N, K, copies = 4864, 896, 40
+    rng = np.random.default_rng(0)
+    stream = torch.cuda.ExternalStream(stream_ptr)
+    qs = [lz.SharedBuffer.from_array(dev, rng.integers(-127, 128, (N, K), dtype=np.int8)) for _ in range(copies)]
+    ss = [lz.SharedBuffer.from_array(dev, rng.uniform(1e-3, 2e-2, N).astype(np.float16)) for _ in range(copies)]
+    out = {}
+    lib = lz.load_library()
+    for M in (1, 128):
+        x = lz.SharedBuffer.from_array(dev, rng.standard_normal((M, K)).astype(np.float16).astype(np.float32))
+        y = lz.SharedBuffer(dev, lz.F32, M * N)
+
+        def run(i):
+            if M == 1:
+                suite.linear(dev, 1, N, K, x, qs[i % copies], ss[i % copies], K, None, y)
+            else:
+                lz.check(lib.l0b_linear_tc_scaled(suite.handle, dev.handle, M, N, K, x.handle, qs[i % copies].handle,
+                                                  ss[i % copies].handle, K, None, 0.0, 0, None, y.handle))
+
+        for i in range(2 * copies):
+            run(i)
+        dev.Synchronize()
+        reps = 10 * copies
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for i in range(reps):
+            run(i)
+        e1.record(stream)
+        e1.synchronize()
+        us = e0.elapsed_time(e1) / reps * 1e3
+        byt = N * K + N * 2 + M * K * 4 + M * N * 4
+        flops = 2.0 * M * N * K
+        r = {"us_per_call": round(us, 3), "algorithmic_bytes": byt, "achieved_gbs": round(byt / us / 1e3, 1),
+             "hbm_frac": round(byt / us / 1e3 / peak, 4), "tflops": round(flops / us / 1e6, 2)}
+        if M > 1:
+            r["tensor_frac"] = round(flops / us / 1e6 / tflops_peak, 4)
+        out["gemv_m1" if M == 1 else "gemm_m128"] = r
+        x.Dispose()
+        y.Dispose()
+    for b in qs + ss:
+        b.Dispose()
+    out["note"] = (f"peak {peak} GB/s ({peak_kind}) and {tflops_peak} TFLOP/s bf16 (measured burst); the 4.4 MB "
+                   "weight of one call fits L2, so the copies rotate; M=1 on the register-streamed tensor-core GEMV, "
+                   "M=128 on tcgen05 kind::i8 with the activation digit cast included")
+    return out
+
+
+def measure_cfg1(lz, dev, suite, stream_ptr, torch, peak: float, steps: int, warmup: int) -> dict:
+    """Config 1: Qwen2.5-0.5B shape, fp16 weights N(0, 0.02) seed 1 (tied embeddings), 128-token prompt,
+    device-resident greedy decode at bs1 timed with CUDA events."""
+    stream = torch.cuda.ExternalStream(stream_ptr)
+    cfg = dict(hidden_size=896, intermediate_size=4864, num_layers=24, num_attention_heads=14, num_key_value_heads=2,
+               head_dim=64, vocab_size=151936, max_position_embeddings=32768, rms_norm_eps=1e-6, rope_theta=1e6,
+               tie_word_embeddings=1, attention_bias=1)
+    prompt = np.random.default_rng(1).integers(0, 151936, 128).astype(np.int32)
+    with lz.LlmModel(dev, suite, lz.model_config(kv_dtype=lz.F16, **cfg), 128 + warmup + steps + 8, "float16") as m:
+        m.init_synthetic(1, 0.02)
+        t0 = time.perf_counter()
+        m.Prefill(prompt)
+        prefill_s = time.perf_counter() - t0
+        m.decode_greedy_device(warmup)
+        dev.Synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        m.decode_greedy_device(steps)
+        e1.record(stream)
+        e1.synchronize()
+        ms = e0.elapsed_time(e1)
+        proj = m.ProjectionBytes
+    pos_mid = 128 + warmup + steps / 2
+    step_bytes = proj + 24 * 2 * 128 * 2 * pos_mid  # fp16 KV: 2 kv heads x 64 = 128 wide, K and V
+    return {"workload": "config 1: Qwen2.5-0.5B-shape fp16 decode, bs1, 128-token prompt", "value": round(
+        steps / (ms / 1e3), 1), "unit": "tok/s", "ms_per_step": round(ms / steps, 4), "prefill_s": round(prefill_s, 3),
+        "bytes_per_step": int(step_bytes), "achieved_gbs": round(step_bytes / (ms / steps * 1e-3) / 1e9, 1),
+        "frac": round(step_bytes / (ms / steps * 1e-3) / 1e9 / peak, 4)}
+
+
+def measure_cfg3(lz, dev, suite, stream_ptr, torch, warmup: int) -> dict:
     """Config 3: one Gated DeltaNet layer (Qwen3.5 shape, bf16 projections) driven through the library's
     ops as LlmDecoderLayer.MixLinear calls them: in_proj (q, k, v | z) and (b | a) projections, causal
     conv + SiLU, the gated delta recurrence with its gated RMSNorm, out_proj. Decode: one token per
-    step for bs sequences (projections batched over the rows, conv and recurrence per sequence), one
-    recorded command list per step. Prefill: 4096 tokens, projections on the tcgen05 GEMM."""
-    import ctypes as C
-
-    import torch
-
-    from l0llm_b200 import levelzero as lz
-
+    step for bs sequences (projections, conv and recurrence each one launch over all rows), one recorded
+    command list per step. Prefill: 4096 tokens, projections on the tcgen05 GEMM, the recurrence chunked."""
     H, HK, HV, DK, DV, KC, T = 2048, 16, 32, 128, 128, 4, 4096
     CONV = 2 * HK * DK + HV * DV
     ZD = HV * DV
-    dev = lz.ComputeDevice(0)
-    suite = lz.LlmKernelSuite.Create(dev)
     lib = lz.load_library()
-    sp = C.c_void_p()
-    lz.check(lib.l0b_device_stream(dev.handle, C.byref(sp)))
-    stream = torch.cuda.ExternalStream(sp.value)
+    stream = torch.cuda.ExternalStream(stream_ptr)
     rng = np.random.default_rng(3)
+    owned = []
 
     def bf16(shape, std):
         w = torch.from_numpy((rng.standard_normal(shape) * std).astype(np.float32)).to(torch.bfloat16)
-        return lz.SharedBuffer.from_array(dev, w.view(torch.int16).numpy().view(np.uint16), lz.BF16)
+        owned.append(lz.SharedBuffer.from_array(dev, w.view(torch.int16).numpy().view(np.uint16), lz.BF16))
+        return owned[-1]
 
     def f32(a):
-        return lz.SharedBuffer.from_array(dev, np.ascontiguousarray(a, np.float32))
+        owned.append(lz.SharedBuffer.from_array(dev, np.ascontiguousarray(a, np.float32)))
+        return owned[-1]
+
+    def f32n(n):
+        owned.append(lz.SharedBuffer(dev, lz.F32, n))
+        return owned[-1]
 
     w_qkv, w_z, w_b, w_a, w_o = bf16((CONV, H), 0.02), bf16((ZD, H), 0.02), bf16((HV, H), 0.02), \
         bf16((HV, H), 0.02), bf16((H, ZD), 0.02)
@@ -330,13 +418,11 @@ def run_cfg3_deltanet(args) -> int:
     norm_w = f32(1 + 0.1 * rng.standard_normal(DV))
 
     def layer_buffers(rows):
-        return dict(x=f32(rng.standard_normal((rows, H))), qkv=lz.SharedBuffer(dev, lz.F32, rows * CONV),
-                    z=lz.SharedBuffer(dev, lz.F32, rows * ZD), b=lz.SharedBuffer(dev, lz.F32, rows * HV),
-                    a=lz.SharedBuffer(dev, lz.F32, rows * HV), conv=lz.SharedBuffer(dev, lz.F32, rows * CONV),
-                    o=lz.SharedBuffer(dev, lz.F32, rows * ZD), y=lz.SharedBuffer(dev, lz.F32, rows * H))
+        return dict(x=f32(rng.standard_normal((rows, H))), qkv=f32n(rows * CONV), z=f32n(rows * ZD), b=f32n(rows * HV),
+                    a=f32n(rows * HV), conv=f32n(rows * CONV), o=f32n(rows * ZD), y=f32n(rows * H))
 
     def timed(fn, reps):
-        for _ in range(args.warmup):
+        for _ in range(warmup):
             fn()
         dev.Synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -350,11 +436,9 @@ def run_cfg3_deltanet(args) -> int:
     results = {}
     for bs in (1, 8):
         buf = layer_buffers(bs)
-        states = [lz.SharedBuffer(dev, lz.F32, HV * DK * DV) for _ in range(bs)]
-        conv_states = [lz.SharedBuffer(dev, lz.F32, CONV * (KC - 1)) for _ in range(bs)]
-        # Row q of each batched buffer, as its own (non-owning) buffer for the per-sequence ops.
-        row = {k: [buf[k].View(q * n, n) for q in range(bs)]
-               for k, n in (("qkv", CONV), ("conv", CONV), ("z", ZD), ("b", HV), ("a", HV), ("o", ZD))}
+        # Every sequence's recurrent state and conv window, batched: one launch each for all sequences.
+        states = f32n(bs * HV * DK * DV)
+        conv_states = f32n(bs * CONV * (KC - 1))
 
         def step():
             dev.BeginRecording()
@@ -362,11 +446,9 @@ def run_cfg3_deltanet(args) -> int:
             suite.linear(dev, bs, ZD, H, buf["x"], w_z, None, 0, None, buf["z"])
             suite.linear(dev, bs, HV, H, buf["x"], w_b, None, 0, None, buf["b"])
             suite.linear(dev, bs, HV, H, buf["x"], w_a, None, 0, None, buf["a"])
-            for q in range(bs):
-                # Sequence q: its conv window and its recurrent state.
-                suite.CausalConv.Execute(dev, row["qkv"][q], conv_states[q], conv_w, row["conv"][q], CONV, KC, 1)
-                suite.GatedDelta.ExecuteGrouped(dev, row["conv"][q], row["z"][q], row["b"][q], row["a"][q], a_log,
-                                                dt_bias, norm_w, states[q], row["o"][q], HK, HV, DK, DV, 1, 1e-6)
+            suite.CausalConv.ExecuteBatch(dev, buf["qkv"], conv_states, conv_w, buf["conv"], CONV, KC, bs)
+            suite.GatedDelta.ExecuteBatch(dev, buf["conv"], buf["z"], buf["b"], buf["a"], a_log, dt_bias, norm_w,
+                                          states, buf["o"], HK, HV, DK, DV, bs, 1e-6)
             suite.linear(dev, bs, H, ZD, buf["o"], w_o, None, 0, None, buf["y"])
             dev.EndRecording()
 
@@ -377,8 +459,8 @@ def run_cfg3_deltanet(args) -> int:
                               "bytes_per_step": step_bytes, "achieved_gbs": round(step_bytes / (ms * 1e-3) / 1e9, 1)}
     # Prefill: 4096 tokens of one sequence.
     pre = layer_buffers(T)
-    state = lz.SharedBuffer(dev, lz.F32, HV * DK * DV)
-    conv_state = lz.SharedBuffer(dev, lz.F32, CONV * (KC - 1))
+    state = f32n(HV * DK * DV)
+    conv_state = f32n(CONV * (KC - 1))
     phases = {}
 
     def tc(m, n, k, x, w, out):
@@ -396,49 +478,54 @@ def run_cfg3_deltanet(args) -> int:
         1e-6), 3)
     phases["out_proj"] = timed(lambda: tc(T, H, ZD, pre["o"], w_o, pre["y"]), 3)
     total = sum(phases.values())
+    for bb in owned:
+        bb.Dispose()
+    return {"decode": results, "prefill_4096_ms": {k: round(v, 3) for k, v in phases.items()} | {"total": round(total, 3)},
+            "config": "config 3: Gated DeltaNet layer alone, hidden 2048, 16 key / 32 value heads of 128, conv 4, "
+                      "fp32 state [32,128,128] per sequence; bf16 weights 67 MB per step (below L2: decode figures "
+                      "are L2-assisted)"}
+
+
+def run_cfg3_deltanet(args) -> int:
+    """Config 3 on its own (bench.py --workload cfg3)."""
+    import ctypes as C
+
+    import torch
+
+    from l0llm_b200 import levelzero as lz
+
+    dev = lz.ComputeDevice(0)
+    suite = lz.LlmKernelSuite.Create(dev)
+    sp = C.c_void_p()
+    lz.check(lz.load_library().l0b_device_stream(dev.handle, C.byref(sp)))
+    r = measure_cfg3(lz, dev, suite, sp.value, torch, args.warmup)
     suite.Dispose()
     dev.Dispose()
-    line = {"metric": "Gated DeltaNet layer decode tok/s (Qwen3.5 shape, bf16, bs1)", "value": results["bs1"]["tok_s"],
+    bs1 = r["decode"]["bs1"]
+    line = {"metric": "Gated DeltaNet layer decode tok/s (Qwen3.5 shape, bf16, bs1)", "value": bs1["tok_s"],
             "unit": "tok/s", "n_gpus": 1, "steps": 256, "warmup": args.warmup,
-            "ms_per_step": round(results["bs1"]["us_per_step"] / 1e3, 5), "higher_is_better": True,
+            "ms_per_step": round(bs1["us_per_step"] / 1e3, 5), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": "config 3: Gated DeltaNet layer alone, hidden 2048, 16 key / 32 value heads of "
-                                   "128, conv 4, fp32 state [32,128,128] per sequence",
-                       "l2": "weights 67 MB per step: below L2, so the decode figures are L2-assisted"},
-            "decode": results,
-            "prefill_4096_ms": {k: round(v, 3) for k, v in phases.items()} | {"total": round(total, 3)}}
+            "config": {"workload": r["config"]}, "decode": r["decode"], "prefill_4096_ms": r["prefill_4096_ms"]}
     print(json.dumps(line))
     return 0
 
 
-def run_cfg4_tp(args) -> int:
-    """Config 4: one sequence decoded tensor-parallel over all ranks (strong scaling): q/k/v, gate/up
-    and lm_head column-split, o_proj/down row-split with an all-reduce each, KV heads split."""
-    world, rank, local = dist_env()
-    import datetime
-
-    import torch
-    import torch.distributed as dist
-
-    from l0llm_b200 import levelzero as lz
-
-    torch.cuda.set_device(local)
-    if world > 1:
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600))
-    dev = lz.ComputeDevice(local)
-    suite = lz.LlmKernelSuite.Create(dev)
-    import ctypes as C
-
-    sp = C.c_void_p()
-    lz.check(lz.load_library().l0b_device_stream(dev.handle, C.byref(sp)))
-    stream = torch.cuda.ExternalStream(sp.value)
+def measure_cfg4_tp(lz, dev, suite, stream_ptr, torch, dist, world: int, rank: int, local: int, steps: int,
+                    warmup: int) -> dict:
+    """Config 4 (Llama-3-70B shape, bf16, llama3 RoPE) decoded tensor-parallel over the `world` ranks of the
+    job (world = 1: the whole 139 GB model on one GPU, the scaling anchor): q/k/v, gate/up and lm_head
+    column-split, o_proj/down row-split with an all-reduce after each, KV heads split. A 2048-token prompt,
+    then `warmup` + `steps` device-resident greedy steps at bs1; CUDA events on the model stream, max
+    over ranks. Every rank takes the same collective steps; returns the result on every rank."""
+    stream = torch.cuda.ExternalStream(stream_ptr)
     comm = None
     if world > 1:
         box = [lz.Communicator.unique_id() if rank == 0 else None]
         dist.broadcast_object_list(box, src=0)
         comm = lz.Communicator(dev, box[0], world, rank)
     cfg = lz.model_config(kv_dtype=lz.BF16, tp_size=world, tp_rank=rank, **CFG4)
-    model = lz.LlmModel(dev, suite, cfg, CFG4_PROMPT + 2 * args.warmup + args.steps + 16, "bfloat16", comm=comm)
+    model = lz.LlmModel(dev, suite, cfg, CFG4_PROMPT + 2 * warmup + steps + 16, "bfloat16", comm=comm)
     model.init_synthetic(4, 0.02)
     prompt = np.random.default_rng(4).integers(0, CFG4["vocab_size"], CFG4_PROMPT).astype(np.int32)
 
@@ -452,48 +539,72 @@ def run_cfg4_tp(args) -> int:
     model.Prefill(prompt)
     barrier()
     prefill_s = time.perf_counter() - t0
-    sampler = ClockSampler(local)
-    sampler.start()
-    model.decode_greedy_device(args.warmup)
+    model.decode_greedy_device(warmup)
     barrier()
-    t_begin = time.monotonic()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
-    toks = model.decode_greedy_device(args.steps)
+    toks = model.decode_greedy_device(steps)
     e1.record(stream)
     e1.synchronize()
-    sampler.mark(t_begin, time.monotonic())
     barrier()
     ms = e0.elapsed_time(e1)
-    clocks = sampler.stop()
     proj = model.ProjectionBytes
     t = torch.tensor([ms, prefill_s], dtype=torch.float64, device="cuda")
+    agree = True
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         same = torch.tensor(toks.astype(np.int64), device="cuda")
         ref = same.clone()
         dist.broadcast(ref, src=0)
-        assert bool((same == ref).all()), "ranks disagree on the greedy tokens"
+        agree = bool((same == ref).all())
     ms, prefill_s = float(t[0]), float(t[1])
     model.Dispose()
     if comm is not None:
         comm.Dispose()  # releases the device's captured graphs first
+    return {"workload": f"config 4: Llama-3-70B-shape bf16 (80 layers, hidden 8192, 64/8 heads, inter 28672, vocab "
+                        f"128256, llama3 RoPE), TP{world}, bs1, {CFG4_PROMPT}-token prompt",
+            "value": round(steps / (ms / 1e3), 2), "unit": "tok/s", "ms_per_step": round(ms / steps, 4),
+            "scaling": "strong", "parallelism": f"tp{world}", "prefill_s": round(prefill_s, 3),
+            "per_rank_weight_gbs": round(proj / (ms / steps * 1e-3) / 1e9, 1),
+            "weight_bytes_per_rank": int(proj), "ranks_agree_on_tokens": agree, "steps": steps, "warmup": warmup}
+
+
+def run_cfg4_tp(args) -> int:
+    """Config 4 on its own (bench.py --workload cfg4, under torchrun for N > 1)."""
+    world, rank, local = dist_env()
+    import ctypes as C
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    from l0llm_b200 import levelzero as lz
+
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600))
+    dev = lz.ComputeDevice(local)
+    suite = lz.LlmKernelSuite.Create(dev)
+    sp = C.c_void_p()
+    lz.check(lz.load_library().l0b_device_stream(dev.handle, C.byref(sp)))
+    sampler = ClockSampler(local)
+    sampler.start()
+    t_begin = time.monotonic()
+    r = measure_cfg4_tp(lz, dev, suite, sp.value, torch, dist, world, rank, local, args.steps, args.warmup)
+    sampler.mark(t_begin, time.monotonic())
+    clocks = sampler.stop()
     suite.Dispose()
     dev.Dispose()
     if rank == 0:
-        step_bytes = proj * world  # every rank streams its shard each step
         line = {
-            "metric": "decode tok/s (Llama-3-70B bf16, TP, bs1)", "value": round(args.steps / (ms / 1e3), 2),
-            "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True, "scaling": "strong",
-            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": f"config 4: Llama-3-70B-shape bf16, TP{world}, bs1, {CFG4_PROMPT}-token prompt",
-                       "global_batch": 1, "seq_len": CFG4_PROMPT, "parallelism": f"tp{world}",
+            "metric": "decode tok/s (Llama-3-70B bf16, TP, bs1)", "value": r["value"], "unit": "tok/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": r["ms_per_step"],
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": r["workload"], "global_batch": 1, "seq_len": CFG4_PROMPT,
+                       "parallelism": r["parallelism"],
                        "l2": "inputs larger than L2: every rank streams its weight shard each step"},
-            "step_roofline": {"weight_bytes_per_step_all_ranks": int(step_bytes),
-                              "per_rank_gbs": round(proj / (ms / args.steps * 1e-3) / 1e9, 1)},
-            "clocks": clocks, "prefill_s": round(prefill_s, 3),
-        }
+            "per_rank_weight_gbs": r["per_rank_weight_gbs"], "clocks": clocks, "prefill_s": r["prefill_s"],
+            "ranks_agree_on_tokens": r["ranks_agree_on_tokens"]}
         print(json.dumps(line))
     if world > 1:
         dist.destroy_process_group()
@@ -606,6 +717,8 @@ def main() -> int:
                          "layer alone (bf16, one GPU); cfg4: Llama-3-70B bf16 tensor-parallel over the N ranks")
     ap.add_argument("--no-bulk-gemv", action="store_true",
                     help="one-row projections on the register-streamed GEMV only (l0b_set_gemv_bulk(0))")
+    ap.add_argument("--no-legs", action="store_true", help="skip the config 0 / 1 / 3 legs of the bench line")
+    ap.add_argument("--no-tp", action="store_true", help="skip the config 4 tensor-parallel leg (tp)")
     ap.add_argument("--profile-case", choices=["decode-bs1", "decode-bs16", "gemm-gateup-16", "attention-512"],
                     help="run one small case for an ncu capture instead of the benchmark")
     args = ap.parse_args()
@@ -736,17 +849,31 @@ def main() -> int:
         t = torch.tensor([ms, e2e_ms, bs16_ms], dtype=torch.float64, device="cuda")
         pg.all_reduce(t, op=pg.ReduceOp.MAX)
         ms, e2e_ms, bs16_ms = float(t[0]), float(t[1]), float(t[2])
+    proj_bytes_cfg2 = model.ProjectionBytes
+    model.Dispose()
+
+    # The other BASELINE configurations (one GPU, rank 0 of a single-rank run) and config 4 tensor-parallel
+    # over all ranks of the job.
+    legs = {}
+    if world == 1 and not args.no_legs:
+        tf_peak = tflops_peak()
+        legs["cfg0"] = measure_cfg0(lz, dev, suite, sp.value, torch, peak, peak_kind, tf_peak)
+        legs["cfg1"] = measure_cfg1(lz, dev, suite, sp.value, torch, peak, args.steps, args.warmup)
+        legs["cfg3"] = measure_cfg3(lz, dev, suite, sp.value, torch, args.warmup)
+    tp = None
+    if not args.no_tp:
+        barrier()
+        tp = measure_cfg4_tp(lz, dev, suite, sp.value, torch, pg, world, rank, local, args.steps, args.warmup)
 
     tokens = world * args.steps
     value = tokens / (ms / 1e3)
     e2e = tokens / (e2e_ms / 1e3)
     kv_bytes = 28 * 2 * 512 * 2 * (pos_start + args.steps / 2)
-    step_bytes = proj_bytes + kv_bytes
+    step_bytes = proj_bytes_cfg2 + kv_bytes
     step_gbs = step_bytes / (ms / args.steps * 1e-3) / 1e9
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline(budget_s=25.0)
-    model.Dispose()
     suite.Dispose()
     dev.Dispose()
     if rank == 0:
@@ -772,6 +899,9 @@ def main() -> int:
                      "ms_per_step": round(bs16_ms / args.steps, 4), "sequences": BS16 * world,
                      "context": f"{CONTEXT}-token prompts, positions {CONTEXT}..{CONTEXT + args.warmup + args.steps}"},
         }
+        line.update(legs)
+        if tp is not None:
+            line["tp"] = tp
         print(json.dumps(line))
     if pg is not None:
         pg.destroy_process_group()

@@ -340,6 +340,26 @@ L0B_API l0b_status l0b_gated_delta_execute_grouped(l0b_suite* s, l0b_device* d, 
  * ~150 KB per (value head, chunk) kept by the suite, grown outside recording) or token by token (0).
  * No counterpart in the reference. */
 L0B_API l0b_status l0b_set_gated_delta_chunked(int32_t enable);
+/* Batched decode of the DeltaNet ops (no counterpart in the reference, whose MixLinear runs one sequence
+ * at a time, L/LlmDecoderLayer.cs:381-397): one token of each of `batch` sequences in one launch.
+ * CausalConv: qkv / out [batch, convDim], convStates [batch, convDim, kernel - 1]. GatedDelta: conv
+ * [batch, convDim], z / out [batch, Hv * dv], b / a [batch, Hv], states [batch, Hv, dk, dv]. Row b of
+ * each equals the single-sequence op on sequence b's buffers. */
+L0B_API l0b_status l0b_causal_conv_execute_batch(l0b_suite* s, l0b_device* d, l0b_buffer* qkv,
+                                                 l0b_buffer* conv_states, l0b_buffer* conv_w, l0b_buffer* out,
+                                                 int32_t conv_dim, int32_t kernel, int32_t batch);
+L0B_API l0b_status l0b_gated_delta_execute_batch(l0b_suite* s, l0b_device* d, l0b_buffer* conv, l0b_buffer* z,
+                                                 l0b_buffer* b, l0b_buffer* a, l0b_buffer* a_log,
+                                                 l0b_buffer* dt_bias, l0b_buffer* norm_w, l0b_buffer* states,
+                                                 l0b_buffer* out, int32_t n_k_heads, int32_t n_v_heads,
+                                                 int32_t key_dim, int32_t value_dim, int32_t batch, float eps);
+/* The DeltaNet part of the device-side fork (replaces the LlmLinearState half of LlmModel.CaptureState +
+ * RestoreState, L/LlmModel.cs:257-306 and L/LlmSequenceState.cs:14-80, which copy the conv window and the
+ * recurrent state through host arrays): sequence dst's conv window and recurrent state in the batched
+ * state buffers become device copies of sequence src's. Stream-ordered; not while recording. */
+L0B_API l0b_status l0b_linear_state_fork(l0b_suite* s, l0b_device* d, l0b_buffer* conv_states, l0b_buffer* states,
+                                         int32_t conv_dim, int32_t kernel, int32_t n_v_heads, int32_t key_dim,
+                                         int32_t value_dim, int32_t src, int32_t dst);
 
 /* ------------------------------------------------------------------------------------------ */
 /* Linear layers in the [out, in] layout, and the fused decode ops                              */

@@ -16,11 +16,16 @@ bool g_gdn_chunked = true;  // chunked prefill of the recurrence (l0b_set_gated_
 
 namespace {
 
+// blockIdx.y selects a sequence of a batch: its rows of x / out start seq_x floats apart and its conv
+// window seq_state floats apart (0 for one sequence).
 __global__ void causal_conv_kernel(const float* x, float* state, const float* w, float* out, int conv_dim, int kernel,
-                                   int tokens) {
+                                   int tokens, long long seq_x, long long seq_state) {
     pdl_wait();
     const int c = blockIdx.x * blockDim.x + threadIdx.x;
     if (c >= conv_dim) return;
+    x += blockIdx.y * seq_x;
+    out += blockIdx.y * seq_x;
+    state += blockIdx.y * seq_state;
     const int hist = kernel - 1;
     float win[8];  // kernel <= 8
     float wc[8];
@@ -76,6 +81,8 @@ __global__ void causal_conv_window_kernel(const float* __restrict__ x, float* st
     for (int j = 0; j < hist; ++j) state[static_cast<long long>(c) * hist + j] = nw[j];
 }
 
+// blockIdx.y selects a sequence of a batch (one token each): its conv / z / out / b / a rows and its state
+// lie seq (its index) rows and seq * hv * DK * dv floats further on.
 template <int DK>
 __global__ void __launch_bounds__(256) gated_delta_kernel(const float* conv, const float* z, const float* b,
                                                           const float* a, const float* a_log, const float* dt_bias,
@@ -88,6 +95,15 @@ __global__ void __launch_bounds__(256) gated_delta_kernel(const float* conv, con
     const int j = threadIdx.x;  // value column
     const int rep = hv / hk, kh = h / rep;
     const int conv_dim = 2 * hk * DK + hv * dv;
+    {
+        const long long sq = blockIdx.y;
+        conv += sq * conv_dim;
+        z += sq * hv * dv;
+        out += sq * hv * dv;
+        b += sq * hv;
+        a += sq * hv;
+        state += sq * hv * static_cast<long long>(DK) * dv;
+    }
     float* S = state + static_cast<long long>(h) * DK * dv;
     float s[DK];
 #pragma unroll
@@ -603,7 +619,28 @@ l0b_status k_causal_conv(l0b_device* d, const float* x, float* state, const floa
                          kernel, tokens);
     }
     return d->launch(causal_conv_kernel, dim3((conv_dim + 127) / 128), dim3(128), 0, x, state, w, out, conv_dim, kernel,
-                     tokens);
+                     tokens, 0LL, 0LL);
+}
+
+// One token of each of `batch` sequences: rows b of x / out, window b of the [batch, conv_dim, kernel - 1] states.
+l0b_status k_causal_conv_batch(l0b_device* d, const float* x, float* states, const float* w, float* out, int conv_dim,
+                               int kernel, int batch) {
+    return d->launch(causal_conv_kernel, dim3((conv_dim + 127) / 128, batch), dim3(128), 0, x, states, w, out, conv_dim,
+                     kernel, 1, static_cast<long long>(conv_dim), static_cast<long long>(conv_dim) * (kernel - 1));
+}
+
+// One token of each of `batch` sequences, states [batch, hv, dk, dv].
+l0b_status k_gated_delta_batch(l0b_device* d, const float* conv, const float* z, const float* b, const float* a,
+                               const float* a_log, const float* dt_bias, const float* norm_w, float* states, float* out,
+                               int hk, int hv, int dk, int dv, int batch, float eps) {
+    const int threads = ((dv + 31) / 32) * 32;
+    if (dk == 128)
+        return d->launch(gated_delta_kernel<128>, dim3(hv, batch), dim3(threads), 0, conv, z, b, a, a_log, dt_bias,
+                         norm_w, states, out, hk, hv, dv, 1, eps);
+    if (dk == 64)
+        return d->launch(gated_delta_kernel<64>, dim3(hv, batch), dim3(threads), 0, conv, z, b, a, a_log, dt_bias,
+                         norm_w, states, out, hk, hv, dv, 1, eps);
+    return fail(L0B_ERR_UNSUPPORTED, "gated delta key head dim %d (64 or 128 are supported)", dk);
 }
 
 // Scratch of the chunked prefill: one record per (value head, chunk), grown on demand outside a
@@ -716,6 +753,70 @@ L0B_API l0b_status l0b_gated_delta_execute_grouped(l0b_suite* s, l0b_device* d, 
     L0B_TRY(need_f32(out, "out", tokens * vd));
     return k_gated_delta(s, d, P(conv), P(z), P(b), P(a), P(a_log), P(dt_bias), P(norm_w), P(state), P(out), n_k_heads,
                          n_v_heads, key_dim, value_dim, tokens, eps);
+}
+
+L0B_API l0b_status l0b_causal_conv_execute_batch(l0b_suite* s, l0b_device* d, l0b_buffer* qkv, l0b_buffer* conv_states,
+                                                 l0b_buffer* conv_w, l0b_buffer* out, int32_t conv_dim, int32_t kernel,
+                                                 int32_t batch) {
+    L0B_REQUIRE(s && d && s->dev == d, L0B_ERR_ARGUMENT, "suite/device mismatch");
+    L0B_REQUIRE(conv_dim > 0 && kernel >= 1 && kernel <= 8 && batch > 0 && batch <= 65535, L0B_ERR_OUT_OF_RANGE,
+                "convDim %d kernel %d batch %d (kernel 1..8)", conv_dim, kernel, batch);
+    const long long n = static_cast<long long>(batch) * conv_dim;
+    L0B_TRY(need_f32(qkv, "qkv", n));
+    L0B_TRY(need_f32(out, "out", n));
+    L0B_TRY(need_f32(conv_states, "convStates", n * (kernel - 1)));
+    L0B_TRY(need_f32(conv_w, "convW", static_cast<long long>(conv_dim) * kernel));
+    return k_causal_conv_batch(d, P(qkv), P(conv_states), P(conv_w), P(out), conv_dim, kernel, batch);
+}
+
+L0B_API l0b_status l0b_gated_delta_execute_batch(l0b_suite* s, l0b_device* d, l0b_buffer* conv, l0b_buffer* z,
+                                                 l0b_buffer* b, l0b_buffer* a, l0b_buffer* a_log, l0b_buffer* dt_bias,
+                                                 l0b_buffer* norm_w, l0b_buffer* states, l0b_buffer* out,
+                                                 int32_t n_k_heads, int32_t n_v_heads, int32_t key_dim,
+                                                 int32_t value_dim, int32_t batch, float eps) {
+    L0B_REQUIRE(s && d && s->dev == d, L0B_ERR_ARGUMENT, "suite/device mismatch");
+    L0B_REQUIRE(n_k_heads > 0 && n_v_heads > 0 && n_v_heads % n_k_heads == 0, L0B_ERR_ARGUMENT,
+                "value heads %d must be a multiple of key heads %d", n_v_heads, n_k_heads);
+    L0B_REQUIRE(value_dim > 0 && value_dim <= 256 && batch > 0 && batch <= 65535, L0B_ERR_OUT_OF_RANGE,
+                "value dim %d batch %d", value_dim, batch);
+    const long long conv_dim = 2LL * n_k_heads * key_dim + static_cast<long long>(n_v_heads) * value_dim;
+    const long long vd = static_cast<long long>(n_v_heads) * value_dim;
+    L0B_TRY(need_f32(conv, "conv", batch * conv_dim));
+    L0B_TRY(need_f32(z, "z", batch * vd));
+    L0B_TRY(need_f32(b, "b", static_cast<long long>(batch) * n_v_heads));
+    L0B_TRY(need_f32(a, "a", static_cast<long long>(batch) * n_v_heads));
+    L0B_TRY(need_f32(a_log, "A_log", n_v_heads));
+    L0B_TRY(need_f32(dt_bias, "dt_bias", n_v_heads));
+    L0B_TRY(need_f32(norm_w, "normW", value_dim));
+    L0B_TRY(need_f32(states, "states", batch * vd * key_dim));
+    L0B_TRY(need_f32(out, "out", batch * vd));
+    return k_gated_delta_batch(d, P(conv), P(z), P(b), P(a), P(a_log), P(dt_bias), P(norm_w), P(states), P(out),
+                               n_k_heads, n_v_heads, key_dim, value_dim, batch, eps);
+}
+
+// The DeltaNet part of the device-side fork: sequence dst's conv window and recurrent state become copies
+// of sequence src's, in batched state buffers ([batch, conv_dim, kernel - 1] and [batch, hv, dk, dv]).
+L0B_API l0b_status l0b_linear_state_fork(l0b_suite* s, l0b_device* d, l0b_buffer* conv_states, l0b_buffer* states,
+                                         int32_t conv_dim, int32_t kernel, int32_t n_v_heads, int32_t key_dim,
+                                         int32_t value_dim, int32_t src, int32_t dst) {
+    L0B_REQUIRE(s && d && s->dev == d, L0B_ERR_ARGUMENT, "suite/device mismatch");
+    L0B_REQUIRE(conv_dim > 0 && kernel >= 1 && n_v_heads > 0 && key_dim > 0 && value_dim > 0, L0B_ERR_OUT_OF_RANGE,
+                "state shape");
+    L0B_REQUIRE(src >= 0 && dst >= 0, L0B_ERR_OUT_OF_RANGE, "sequences %d -> %d", src, dst);
+    L0B_REQUIRE(src != dst, L0B_ERR_ARGUMENT, "a sequence cannot be forked onto itself");
+    const long long cw = static_cast<long long>(conv_dim) * (kernel - 1);
+    const long long rs = static_cast<long long>(n_v_heads) * key_dim * value_dim;
+    const long long hi = src > dst ? src : dst;
+    L0B_TRY(need_f32(conv_states, "convStates", (hi + 1) * cw));
+    L0B_TRY(need_f32(states, "states", (hi + 1) * rs));
+    L0B_REQUIRE(!d->recording, L0B_ERR_INVALID_OPERATION, "fork the state outside a recording");
+    L0B_CHECK_CUDA(cudaSetDevice(d->index));
+    if (cw > 0)
+        L0B_CHECK_CUDA(cudaMemcpyAsync(P(conv_states) + dst * cw, P(conv_states) + src * cw, cw * sizeof(float),
+                                       cudaMemcpyDeviceToDevice, d->stream));
+    L0B_CHECK_CUDA(cudaMemcpyAsync(P(states) + dst * rs, P(states) + src * rs, rs * sizeof(float),
+                                   cudaMemcpyDeviceToDevice, d->stream));
+    return L0B_OK;
 }
 
 L0B_API l0b_status l0b_set_gated_delta_chunked(int32_t enable) {

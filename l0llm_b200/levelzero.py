@@ -165,6 +165,11 @@ def load_library() -> C.CDLL:
         "l0b_causal_conv_execute": (i32, [vp, vp, vp, vp, vp, vp, i32, i32, i32]),
         "l0b_gated_delta_execute": (i32, [vp, vp] + [vp] * 9 + [i32, i32, i32, i32, f32]),
         "l0b_gated_delta_execute_grouped": (i32, [vp, vp] + [vp] * 9 + [i32, i32, i32, i32, i32, f32]),
+        "l0b_causal_conv_execute_batch": (i32, [vp, vp, vp, vp, vp, vp, i32, i32, i32]),
+        "l0b_gated_delta_execute_batch": (i32, [vp, vp] + [vp] * 9 + [i32, i32, i32, i32, i32, f32]),
+        "l0b_linear_state_fork": (i32, [vp, vp, vp, vp] + [i32] * 7),
+        "l0b_set_gated_delta_chunked": (i32, [i32]),
+        "l0b_set_weight_blocking": (i32, [i32]),
         "l0b_linear": (i32, [vp, vp, i32, i32, i32, vp, vp, vp, i32, vp, vp]),
         "l0b_gemv_w8a16_raw": (i32, [vp, i32, i32, i32, vp, i32, vp, vp, i32, vp, i32]),
         "l0b_linear_fused": (i32, [vp, vp, i32, i32, i32, vp, vp, vp, i32, vp, f32, i32, vp, vp]),
@@ -507,6 +512,12 @@ class _CausalConv(_Op):
                                              out.handle, convDim, k, tokens))
 
 
+    def ExecuteBatch(self, dev, qkv, convStates, convW, out, convDim, k, batch):
+        """One token of each of `batch` sequences (rows of qkv/out, windows of convStates)."""
+        check(self.L.l0b_causal_conv_execute_batch(self._s(), dev.handle, qkv.handle, convStates.handle, convW.handle,
+                                                   out.handle, convDim, k, batch))
+
+
 class _GatedDelta(_Op):
     def Execute(self, dev, conv, z, b, a, A_log, dt_bias, normW, S, out, Hv, dk, dv, tokens, eps):
         check(self.L.l0b_gated_delta_execute(self._s(), dev.handle, conv.handle, z.handle, b.handle, a.handle,
@@ -517,6 +528,17 @@ class _GatedDelta(_Op):
         check(self.L.l0b_gated_delta_execute_grouped(self._s(), dev.handle, conv.handle, z.handle, b.handle, a.handle,
                                                      A_log.handle, dt_bias.handle, normW.handle, S.handle, out.handle,
                                                      Hk, Hv, dk, dv, tokens, eps))
+
+    def ExecuteBatch(self, dev, conv, z, b, a, A_log, dt_bias, normW, states, out, Hk, Hv, dk, dv, batch, eps):
+        """One token of each of `batch` sequences, states [batch, Hv, dk, dv]."""
+        check(self.L.l0b_gated_delta_execute_batch(self._s(), dev.handle, conv.handle, z.handle, b.handle, a.handle,
+                                                   A_log.handle, dt_bias.handle, normW.handle, states.handle,
+                                                   out.handle, Hk, Hv, dk, dv, batch, eps))
+
+    def ForkState(self, dev, convStates, states, convDim, k, Hv, dk, dv, src, dst):
+        """Sequence dst's conv window and recurrent state become device copies of sequence src's."""
+        check(self.L.l0b_linear_state_fork(self._s(), dev.handle, convStates.handle, states.handle, convDim, k, Hv, dk,
+                                           dv, src, dst))
 
 
 class LlmKernelSuite:

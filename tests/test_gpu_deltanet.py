@@ -157,3 +157,57 @@ def test_mix_linear_layer_against_oracle(lz, orc, device, suite):
     got = np.concatenate(got)
     _close(got[:pre], y_o[:pre], 2e-3, "prefill output")
     _close(got[pre:], y_o[pre:], 2e-3, "decode outputs")
+
+
+def test_batched_decode_equals_per_sequence_and_fork(lz, device, suite):
+    """The batched decode ops (one launch for all sequences) give each sequence exactly what the
+    single-sequence ops give it; a forked sequence (conv window and recurrent state copied on the device)
+    then decodes exactly as its source."""
+    hk, hv, dk, dv, kc, bs, steps = 16, 32, 128, 128, 4, 5, 3
+    conv_dim = 2 * hk * dk + hv * dv
+    rng = RNG(11)
+    conv_w = (rng.standard_normal((conv_dim, kc)) * 0.3).astype(np.float32)
+    a_log = np.zeros(hv, np.float32)
+    dt = np.zeros(hv, np.float32)
+    nw = (1 + 0.1 * rng.standard_normal(dv)).astype(np.float32)
+    hist0 = rng.standard_normal((bs, conv_dim, kc - 1)).astype(np.float32)
+    S0 = (rng.standard_normal((bs, hv, dk, dv)) * 0.1).astype(np.float32)
+    xs = rng.standard_normal((steps, bs, conv_dim)).astype(np.float32)
+    zs = rng.standard_normal((steps, bs, hv * dv)).astype(np.float32)
+    bb_ = rng.standard_normal((steps, bs, hv)).astype(np.float32)
+    aa_ = rng.standard_normal((steps, bs, hv)).astype(np.float32)
+    with _buf(lz, device, conv_w) as cw, _buf(lz, device, a_log) as alb, _buf(lz, device, dt) as dtb, \
+            _buf(lz, device, nw) as nwb, _buf(lz, device, hist0) as H, _buf(lz, device, S0) as S:
+        batched = []
+        for t in range(steps):
+            with _buf(lz, device, xs[t]) as xb, _buf(lz, device, zs[t]) as zb, _buf(lz, device, bb_[t]) as bb, \
+                    _buf(lz, device, aa_[t]) as ab, lz.SharedBuffer(device, lz.F32, bs * conv_dim) as cb, \
+                    lz.SharedBuffer(device, lz.F32, bs * hv * dv) as ob:
+                suite.CausalConv.ExecuteBatch(device, xb, H, cw, cb, conv_dim, kc, bs)
+                suite.GatedDelta.ExecuteBatch(device, cb, zb, bb, ab, alb, dtb, nwb, S, ob, hk, hv, dk, dv, bs, 1e-6)
+                batched.append(ob.ToArray().reshape(bs, -1))
+        S_b, H_b = S.ToArray().reshape(S0.shape), H.ToArray().reshape(hist0.shape)
+        # Fork sequence 1 onto 3, then one more batched step with equal inputs for both.
+        suite.GatedDelta.ForkState(device, H, S, conv_dim, kc, hv, dk, dv, 1, 3)
+        x1 = np.repeat(xs[0][1:2], bs, 0)
+        z1 = np.repeat(zs[0][1:2], bs, 0)
+        with _buf(lz, device, x1) as xb, _buf(lz, device, z1) as zb, _buf(lz, device, np.repeat(bb_[0][1:2], bs, 0)) as bb, \
+                _buf(lz, device, np.repeat(aa_[0][1:2], bs, 0)) as ab, \
+                lz.SharedBuffer(device, lz.F32, bs * conv_dim) as cb, lz.SharedBuffer(device, lz.F32, bs * hv * dv) as ob:
+            suite.CausalConv.ExecuteBatch(device, xb, H, cw, cb, conv_dim, kc, bs)
+            suite.GatedDelta.ExecuteBatch(device, cb, zb, bb, ab, alb, dtb, nwb, S, ob, hk, hv, dk, dv, bs, 1e-6)
+            after = ob.ToArray().reshape(bs, -1)
+        np.testing.assert_array_equal(after[1], after[3])
+        for q in range(bs):
+            with _buf(lz, device, hist0[q]) as H1, _buf(lz, device, S0[q]) as S1:
+                for t in range(steps):
+                    with _buf(lz, device, xs[t][q]) as xb, _buf(lz, device, zs[t][q]) as zb, \
+                            _buf(lz, device, bb_[t][q]) as bb, _buf(lz, device, aa_[t][q]) as ab, \
+                            lz.SharedBuffer(device, lz.F32, conv_dim) as cb, \
+                            lz.SharedBuffer(device, lz.F32, hv * dv) as ob:
+                        suite.CausalConv.Execute(device, xb, H1, cw, cb, conv_dim, kc, 1)
+                        suite.GatedDelta.ExecuteGrouped(device, cb, zb, bb, ab, alb, dtb, nwb, S1, ob, hk, hv, dk, dv,
+                                                        1, 1e-6)
+                        np.testing.assert_array_equal(ob.ToArray(), batched[t][q])
+                np.testing.assert_array_equal(S1.ToArray().reshape(S0.shape[1:]), S_b[q])
+                np.testing.assert_array_equal(H1.ToArray().reshape(hist0.shape[1:]), H_b[q])
