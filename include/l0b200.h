@@ -280,6 +280,11 @@ L0B_API l0b_status l0b_attention_decode_noalloc(void* stream, const float* q, co
                                                 int32_t n_heads, int32_t n_kv_heads, int32_t seq_len,
                                                 int32_t max_seq);
 
+/* Tuning: prefill attention (a block of query rows over f16 / bf16 caches, head dim 64 or 128) on the
+ * tensor cores (1, default: flash-attention tiles on mma.sync with hi + lo 16-bit queries and
+ * probabilities, about fp32 accuracy) or on the scalar kernel (0). No counterpart in the reference. */
+L0B_API l0b_status l0b_set_attention_prefill_tensor_cores(int32_t enable);
+
 /* SigmoidGate.Execute(dev, x, gate, n) -- L/LlmDecoderLayer.cs:330,374. x *= sigmoid(gate). */
 L0B_API l0b_status l0b_sigmoid_gate_execute(l0b_suite* s, l0b_device* d, l0b_buffer* x, l0b_buffer* gate,
                                             int32_t n);

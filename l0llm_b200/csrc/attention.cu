@@ -15,6 +15,8 @@
 #include <mutex>
 
 #include <cooperative_groups.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
 
 #include "common.cuh"
 #include "ops.cuh"
@@ -493,10 +495,291 @@ l0b_status launch_attn(l0b_device* d, cudaStream_t stream, F kernel, dim3 grid, 
     return L0B_OK;
 }
 
+// ---------------------------------------------------------------------------------------------
+// Prefill attention on the tensor cores (mma.sync m16n8k16, fp32 accumulators), flash-attention style.
+//
+// A CTA takes 64 query rows of one query head (four warps of 16 rows) and walks the key tiles of its
+// KV head up to the largest position among its rows, 64 slots a tile, double-buffered in shared memory
+// by cp.async (16-byte chunks of a row XOR-swizzled by the row index, so the fragment reads hit 32
+// distinct banks). S = Q K^T: the query rows are scaled by softmax_scale * log2(e) and split into hi +
+// lo 16-bit halves held in registers for the whole walk, each against the exact 16-bit key, so the
+// scores keep about 22 bits (f16) or 16 bits (bf16) of the f32 query. The mask keeps slot <= the row's
+// position; the softmax is online in exp2 (running max and sum per row, rows with nothing seen yet
+// kept at zero). O += P V: P enters as the A operand straight from the score registers, again as hi +
+// lo halves; V fragments come transposed by ldmatrix. Finally O / sum goes to the row's output.
+// K / V caches f16 or bf16 (f32 caches take the scalar kernel).
+// ---------------------------------------------------------------------------------------------
+constexpr int kPfBM = 64, kPfBN = 64;
+bool g_attn_prefill_mma = true;  // l0b_set_attention_prefill_tensor_cores
+
+__device__ __forceinline__ uint32_t pf_pack(float a, float b, bool bf) {
+    if (bf) {
+        const __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
+        return *reinterpret_cast<const uint32_t*>(&v);
+    }
+    const __half2 v = __floats2half2_rn(a, b);
+    return *reinterpret_cast<const uint32_t*>(&v);
+}
+__device__ __forceinline__ float2 pf_unpack(uint32_t u, bool bf) {
+    if (bf) return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u));
+    return __half22float2(*reinterpret_cast<const __half2*>(&u));
+}
+// hi = 16-bit (a, b); lo = 16-bit residuals.
+__device__ __forceinline__ void pf_split(float a, float b, bool bf, uint32_t& hi, uint32_t& lo) {
+    hi = pf_pack(a, b, bf);
+    const float2 h = pf_unpack(hi, bf);
+    lo = pf_pack(a - h.x, b - h.y, bf);
+}
+__device__ __forceinline__ void pf_mma(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                       uint32_t b1, bool bf) {
+    if (bf)
+        asm volatile(
+            "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+            : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+            : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+    else
+        asm volatile(
+            "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+            : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+            : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+template <int HD, bool BF>
+__global__ void __launch_bounds__(128) attn_prefill_mma_kernel(const AttnParams p, int rows) {
+    constexpr int NT = HD / 8;    // 8-column tiles of the output
+    constexpr int KS = HD / 16;   // 16-deep steps of Q K^T
+    constexpr int RB = HD * 2;    // bytes per tile row
+    constexpr int TILE = kPfBN * RB;
+    extern __shared__ __align__(128) unsigned char pf_smem[];
+    unsigned char* Ks = pf_smem;             // [2][kPfBN][HD] 16-bit, swizzled
+    unsigned char* Vs = pf_smem + 2 * TILE;  // [2][kPfBN][HD]
+    __shared__ int pmax_s[4];
+    pdl_wait();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+    const int h = blockIdx.y, kvh = h / (p.nh / p.nkv);
+    const int r0 = blockIdx.x * kPfBM, wr = r0 + warp * 16;
+    auto pos_of = [&](int b) { return b < rows ? (p.positions ? p.positions[b] : p.pos_base + b * p.pos_step) : -1; };
+    // The largest position among the CTA's rows bounds the key walk.
+    {
+        int pm = -1;
+        for (int b = r0 + threadIdx.x; b < r0 + kPfBM; b += 128) pm = max(pm, pos_of(b));
+        for (int o = 16; o > 0; o >>= 1) pm = max(pm, __shfl_xor_sync(0xffffffffu, pm, o));
+        if (lane == 0) pmax_s[warp] = pm;
+    }
+    __syncthreads();
+    const int pmax = max(max(pmax_s[0], pmax_s[1]), max(pmax_s[2], pmax_s[3]));
+    if (pmax < 0) return;
+    const int pa = pos_of(wr + g), pb = pos_of(wr + g + 8);
+    const int ntiles = pmax / kPfBN + 1;
+    const char* kbase = static_cast<const char*>(p.kc) + static_cast<long long>(kvh) * HD * 2;
+    const char* vbase = static_cast<const char*>(p.vc) + static_cast<long long>(kvh) * HD * 2;
+    const long long row_stride = static_cast<long long>(p.kv_dim) * 2;
+    // One key tile (and value tile) into stage st: 16-byte chunks, rows past pmax zero-filled.
+    auto load_tile = [&](int j, int st) {
+        for (int e = threadIdx.x; e < kPfBN * (HD / 8); e += 128) {
+            const int r = e / (HD / 8), c = e - r * (HD / 8);
+            const int slot = j * kPfBN + r;
+            const uint32_t off = static_cast<uint32_t>(r * RB + ((c ^ (r & 7)) * 16));
+            unsigned char* kd = Ks + st * TILE + off;
+            unsigned char* vd = Vs + st * TILE + off;
+            if (slot <= pmax) {
+                const long long go = static_cast<long long>(slot) * row_stride + c * 16;
+                asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(static_cast<uint32_t>(
+                                 __cvta_generic_to_shared(kd))),
+                             "l"(kbase + go)
+                             : "memory");
+                asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(static_cast<uint32_t>(
+                                 __cvta_generic_to_shared(vd))),
+                             "l"(vbase + go)
+                             : "memory");
+            } else {
+                *reinterpret_cast<uint4*>(kd) = make_uint4(0, 0, 0, 0);
+                *reinterpret_cast<uint4*>(vd) = make_uint4(0, 0, 0, 0);
+            }
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+    load_tile(0, 0);
+    // Query fragments (rows g and g + 8 of this warp), scaled for exp2 and split into hi / lo halves.
+    const float qs = p.scale * 1.4426950408889634f;
+    uint32_t qh[KS][4], ql[KS][4];
+    {
+        const float* qa = pa >= 0 ? p.q + static_cast<long long>(wr + g) * p.q_bstride + static_cast<long long>(h) * HD : nullptr;
+        const float* qb = pb >= 0 ? p.q + static_cast<long long>(wr + g + 8) * p.q_bstride + static_cast<long long>(h) * HD : nullptr;
+#pragma unroll
+        for (int kk = 0; kk < KS; ++kk) {
+            const int c0 = 16 * kk + 2 * t, c1 = c0 + 8;
+            const float2 x0 = qa ? *reinterpret_cast<const float2*>(qa + c0) : make_float2(0.f, 0.f);
+            const float2 x1 = qb ? *reinterpret_cast<const float2*>(qb + c0) : make_float2(0.f, 0.f);
+            const float2 x2 = qa ? *reinterpret_cast<const float2*>(qa + c1) : make_float2(0.f, 0.f);
+            const float2 x3 = qb ? *reinterpret_cast<const float2*>(qb + c1) : make_float2(0.f, 0.f);
+            pf_split(x0.x * qs, x0.y * qs, BF, qh[kk][0], ql[kk][0]);
+            pf_split(x1.x * qs, x1.y * qs, BF, qh[kk][1], ql[kk][1]);
+            pf_split(x2.x * qs, x2.y * qs, BF, qh[kk][2], ql[kk][2]);
+            pf_split(x3.x * qs, x3.y * qs, BF, qh[kk][3], ql[kk][3]);
+        }
+    }
+    float o[NT][4];
+#pragma unroll
+    for (int n = 0; n < NT; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+    float ma = -INFINITY, mb = -INFINITY, la = 0.f, lb = 0.f;
+    // This warp's rows need tiles up to wmax / kPfBN. The skip test must be the same for every lane: the
+    // MMA and ldmatrix below are warp-collective (.sync.aligned), so the bound is the warp-wide maximum.
+    int wmax = max(pa, pb);
+    for (int o = 16; o > 0; o >>= 1) wmax = max(wmax, __shfl_xor_sync(0xffffffffu, wmax, o));
+    for (int j = 0; j < ntiles; ++j) {
+        const int st = j & 1;
+        if (j + 1 < ntiles) {
+            load_tile(j + 1, st ^ 1);
+            asm volatile("cp.async.wait_group 1;" ::: "memory");
+        } else {
+            asm volatile("cp.async.wait_group 0;" ::: "memory");
+        }
+        __syncthreads();
+        if (j * kPfBN <= wmax) {
+            const unsigned char* kt = Ks + st * TILE;
+            const unsigned char* vt = Vs + st * TILE;
+            // S = Q K^T for the 64 slots of the tile: 8 tiles of 8 slots.
+            float sc[8][4];
+#pragma unroll
+            for (int nt = 0; nt < 8; ++nt) {
+                sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.f;
+                const int r = nt * 8 + g;
+#pragma unroll
+                for (int kk = 0; kk < KS; ++kk) {
+                    const uint32_t b0 = *reinterpret_cast<const uint32_t*>(kt + r * RB + (((2 * kk) ^ (r & 7)) * 16) + 4 * t);
+                    const uint32_t b1 =
+                        *reinterpret_cast<const uint32_t*>(kt + r * RB + (((2 * kk + 1) ^ (r & 7)) * 16) + 4 * t);
+                    pf_mma(sc[nt], qh[kk][0], qh[kk][1], qh[kk][2], qh[kk][3], b0, b1, BF);
+                    pf_mma(sc[nt], ql[kk][0], ql[kk][1], ql[kk][2], ql[kk][3], b0, b1, BF);
+                }
+            }
+            // Mask and online softmax (rows g: sc[.][0..1], g + 8: sc[.][2..3]).
+            float ta = -INFINITY, tb = -INFINITY;
+#pragma unroll
+            for (int nt = 0; nt < 8; ++nt) {
+                const int s0 = j * kPfBN + nt * 8 + 2 * t;
+                if (s0 > pa) sc[nt][0] = -INFINITY;
+                if (s0 + 1 > pa) sc[nt][1] = -INFINITY;
+                if (s0 > pb) sc[nt][2] = -INFINITY;
+                if (s0 + 1 > pb) sc[nt][3] = -INFINITY;
+                ta = fmaxf(ta, fmaxf(sc[nt][0], sc[nt][1]));
+                tb = fmaxf(tb, fmaxf(sc[nt][2], sc[nt][3]));
+            }
+            ta = fmaxf(ta, __shfl_xor_sync(0xffffffffu, ta, 1));
+            ta = fmaxf(ta, __shfl_xor_sync(0xffffffffu, ta, 2));
+            tb = fmaxf(tb, __shfl_xor_sync(0xffffffffu, tb, 1));
+            tb = fmaxf(tb, __shfl_xor_sync(0xffffffffu, tb, 2));
+            const float na = fmaxf(ma, ta), nb = fmaxf(mb, tb);
+            const float aa = na == -INFINITY ? 1.f : exp2f(ma - na);
+            const float ab = nb == -INFINITY ? 1.f : exp2f(mb - nb);
+            ma = na;
+            mb = nb;
+            float sa = 0.f, sb = 0.f;
+#pragma unroll
+            for (int nt = 0; nt < 8; ++nt) {
+                sc[nt][0] = na == -INFINITY ? 0.f : exp2f(sc[nt][0] - na);
+                sc[nt][1] = na == -INFINITY ? 0.f : exp2f(sc[nt][1] - na);
+                sc[nt][2] = nb == -INFINITY ? 0.f : exp2f(sc[nt][2] - nb);
+                sc[nt][3] = nb == -INFINITY ? 0.f : exp2f(sc[nt][3] - nb);
+                sa += sc[nt][0] + sc[nt][1];
+                sb += sc[nt][2] + sc[nt][3];
+            }
+            la = la * aa + sa;
+            lb = lb * ab + sb;
+#pragma unroll
+            for (int n = 0; n < NT; ++n) {
+                o[n][0] *= aa;
+                o[n][1] *= aa;
+                o[n][2] *= ab;
+                o[n][3] *= ab;
+            }
+            // O += P V: P of slots 16 kk .. 16 kk + 15 from score tiles 2 kk and 2 kk + 1.
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk) {
+                uint32_t ph[4], pl[4];
+                pf_split(sc[2 * kk][0], sc[2 * kk][1], BF, ph[0], pl[0]);
+                pf_split(sc[2 * kk][2], sc[2 * kk][3], BF, ph[1], pl[1]);
+                pf_split(sc[2 * kk + 1][0], sc[2 * kk + 1][1], BF, ph[2], pl[2]);
+                pf_split(sc[2 * kk + 1][2], sc[2 * kk + 1][3], BF, ph[3], pl[3]);
+#pragma unroll
+                for (int n = 0; n < NT; n += 2) {
+                    // Transposed fragments of V rows 16 kk .. + 15, columns of output tiles n and n + 1.
+                    const int r = 16 * kk + (lane & 7) + ((lane >> 3) & 1) * 8;
+                    const int c = n + (lane >> 4);
+                    const uint32_t addr = static_cast<uint32_t>(__cvta_generic_to_shared(vt + r * RB + ((c ^ (r & 7)) * 16)));
+                    uint32_t v0, v1, v2, v3;
+                    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                                 : "=r"(v0), "=r"(v1), "=r"(v2), "=r"(v3)
+                                 : "r"(addr));
+                    pf_mma(o[n], ph[0], ph[1], ph[2], ph[3], v0, v1, BF);
+                    pf_mma(o[n], pl[0], pl[1], pl[2], pl[3], v0, v1, BF);
+                    pf_mma(o[n + 1], ph[0], ph[1], ph[2], ph[3], v2, v3, BF);
+                    pf_mma(o[n + 1], pl[0], pl[1], pl[2], pl[3], v2, v3, BF);
+                }
+            }
+        }
+        __syncthreads();  // stage st is refilled by the next iteration's prefetch
+    }
+    la += __shfl_xor_sync(0xffffffffu, la, 1);
+    la += __shfl_xor_sync(0xffffffffu, la, 2);
+    lb += __shfl_xor_sync(0xffffffffu, lb, 1);
+    lb += __shfl_xor_sync(0xffffffffu, lb, 2);
+    const float ia = la > 0.f ? 1.f / la : 0.f, ib = lb > 0.f ? 1.f / lb : 0.f;
+    float* oa = pa >= 0 ? p.out + static_cast<long long>(wr + g) * p.out_bstride + static_cast<long long>(h) * HD : nullptr;
+    float* ob = pb >= 0 ? p.out + static_cast<long long>(wr + g + 8) * p.out_bstride + static_cast<long long>(h) * HD : nullptr;
+#pragma unroll
+    for (int n = 0; n < NT; ++n) {
+        const int c = n * 8 + 2 * t;
+        if (oa) *reinterpret_cast<float2*>(oa + c) = make_float2(o[n][0] * ia, o[n][1] * ia);
+        if (ob) *reinterpret_cast<float2*>(ob + c) = make_float2(o[n][2] * ib, o[n][3] * ib);
+    }
+}
+
+template <int HD, bool BF>
+l0b_status launch_prefill_mma(l0b_device* d, cudaStream_t stream, const AttnParams& p, int rows) {
+    constexpr size_t smem = 4ull * kPfBN * HD * 2;
+    auto kernel = attn_prefill_mma_kernel<HD, BF>;
+    static bool configured = false;
+    if (!configured) {
+        cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+        if (e != cudaSuccess) return fail(L0B_ERR_CUDA, "cudaFuncSetAttribute failed: %s", cudaGetErrorString(e));
+        configured = true;
+    }
+    const dim3 grid((rows + kPfBM - 1) / kPfBM, p.nh);
+    if (d) return d->launch(kernel, grid, dim3(128), smem, p, rows);
+    kernel<<<grid, 128, smem, stream>>>(p, rows);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return fail(L0B_ERR_CUDA, "attention launch failed: %s", cudaGetErrorString(e));
+    add_launches(1);
+    return L0B_OK;
+}
+
+// The tensor-core prefill kernel applies: f16 / bf16 caches with 16-byte aligned rows, head dim 64 or
+// 128, query rows 8-byte aligned (float2 reads), and a query block (prefill, not one decode row).
+bool prefill_mma_applies(const AttnParams& p, int rows) {
+    if (!g_attn_prefill_mma || rows < 2 || p.rope || p.store_new || p.cache_bstride != 0) return false;
+    if (p.cache_dtype != L0B_F16 && p.cache_dtype != L0B_BF16) return false;
+    if (p.hd != 64 && p.hd != 128) return false;
+    if ((p.kv_dim * 2) % 16 != 0 || reinterpret_cast<uintptr_t>(p.kc) % 16 || reinterpret_cast<uintptr_t>(p.vc) % 16)
+        return false;
+    if (reinterpret_cast<uintptr_t>(p.q) % 8 || p.q_bstride % 2 || reinterpret_cast<uintptr_t>(p.out) % 8 ||
+        p.out_bstride % 2)
+        return false;
+    return true;
+}
+
+l0b_status attention_prefill_mma(l0b_device* d, cudaStream_t stream, const AttnParams& p, int rows) {
+    const bool bf = p.cache_dtype == L0B_BF16;
+    if (p.hd == 64) return bf ? launch_prefill_mma<64, true>(d, stream, p, rows) : launch_prefill_mma<64, false>(d, stream, p, rows);
+    return bf ? launch_prefill_mma<128, true>(d, stream, p, rows) : launch_prefill_mma<128, false>(d, stream, p, rows);
+}
+
 l0b_status attention_any(l0b_device* d, cudaStream_t stream, const AttnParams& p, int batch) {
     L0B_REQUIRE(p.nkv > 0 && p.nh % p.nkv == 0, L0B_ERR_ARGUMENT, "heads %d not a multiple of kv heads %d", p.nh,
                 p.nkv);
     L0B_REQUIRE(p.chunk > 0 && p.max_splits > 0, L0B_ERR_ARGUMENT, "bad split configuration");
+    if (p.max_splits == 1 && prefill_mma_applies(p, batch)) return attention_prefill_mma(d, stream, p, batch);
     const int G = p.nh / p.nkv;
     const int gparts = (G + kMaxG - 1) / kMaxG;
     dim3 grid(p.nkv * gparts, p.max_splits, batch);
@@ -603,6 +886,11 @@ NoAllocAddrs g_noalloc_addrs[64];
 std::mutex g_noalloc_mutex;
 
 }  // namespace
+
+extern "C" L0B_API l0b_status l0b_set_attention_prefill_tensor_cores(int32_t enable) {
+    l0b::g_attn_prefill_mma = enable != 0;
+    return L0B_OK;
+}
 
 extern "C" L0B_API l0b_status l0b_attention_decode_noalloc(void* stream, const float* q, const void* kc, const void* vc,
                                                          int32_t cache_dtype, float* out, int32_t head_dim,
