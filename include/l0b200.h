@@ -548,8 +548,9 @@ L0B_API l0b_status l0b_model_set_tensor(l0b_model* model, const char* name, cons
  * with fp16 scales uniform on [scale_lo, scale_hi]; biases N(0, std); norms 1. */
 L0B_API l0b_status l0b_model_init_synthetic(l0b_model* model, uint64_t seed, float std, float scale_lo,
                                             float scale_hi);
-/* LlmModel.Prefill(promptIds): resets the sequence, ingests the prompt in chunks of
- * l0b_gemv_max_rows() tokens and writes the logits of the next token (vocab f32, may be NULL). */
+/* LlmModel.Prefill(promptIds): resets the sequence, ingests the prompt in chunks of up to 512 tokens
+ * (each projection of a chunk one tensor-core GEMM that reads the weights once; the reference chunks by
+ * LlmGemvKernel.MaxRows) and writes the logits of the next token (vocab f32, may be NULL). */
 L0B_API l0b_status l0b_model_prefill(l0b_model* model, const int32_t* ids, int32_t count, float* logits);
 /* LlmModel.Decode(tokenId): one token at Position; writes its logits (may be NULL). */
 L0B_API l0b_status l0b_model_decode(l0b_model* model, int32_t token, float* logits);

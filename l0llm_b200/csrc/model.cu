@@ -736,11 +736,13 @@ l0b_status step(l0b_model* m, int token, int position) {
     return s;
 }
 
-// LlmModel.IngestPrompt (L/LlmModel.cs:320-333): chunks of kMaxRows tokens; a 1-token chunk is a Step.
+// LlmModel.IngestPrompt (L/LlmModel.cs:320-333): chunks of kPrefillRows tokens (the reference chunks by
+// LlmGemvKernel.MaxRows; here a chunk is one tensor-core GEMM per projection, which reads each weight
+// once per chunk, so larger chunks stream the weights fewer times); a 1-token chunk is a Step.
 // `seq` selects the cache row (sequence) for a batched model; sequences other than 0 always take the
 // chunk path, whose head writes that sequence's greedy token and next position.
 l0b_status ingest_prompt(l0b_model* m, const int32_t* ids, int count, int seq = 0) {
-    const int chunk = kMaxRows < m->cap ? kMaxRows : m->cap;
+    const int chunk = kPrefillRows < m->cap ? kPrefillRows : m->cap;
     m->prefill_seq = seq;
     for (int start = 0; start < count; start += chunk) {
         const int n = count - start < chunk ? count - start : chunk;
@@ -1002,7 +1004,7 @@ L0B_API l0b_status l0b_model_create(l0b_device* dev, l0b_suite* suite, const l0b
     L0B_REQUIRE(m->batch_cap <= kMaxRows, L0B_ERR_OUT_OF_RANGE, "max_batch %d exceeds %d sequences", c.max_batch,
                 kMaxRows);
     m->seq_pos.assign(m->batch_cap, 0);
-    m->cap = kMaxRows;
+    m->cap = kPrefillRows;
     L0B_CHECK_CUDA(cudaSetDevice(dev->index));
 
     std::vector<float> table;

@@ -9,6 +9,8 @@
 namespace l0b {
 // LlmGemvKernel.MaxRows: rows per ExecuteRows call and per prefill chunk of the model.
 constexpr int kMaxRows = 64;
+// Tokens per prefill chunk of the model (activation rows it allocates).
+constexpr int kPrefillRows = 512;
 // 16-row tiles the suite's split-K GEMV scratch covers (N <= 65536 output rows).
 constexpr int kSuiteSplitTiles = 4096;
 }  // namespace l0b

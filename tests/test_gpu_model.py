@@ -89,12 +89,12 @@ def test_reduced_precision_matches_oracle(lz, orc, device, suite, name, precisio
     om.close()
 
 
-@pytest.mark.parametrize("length", [1, 2, 7, 8, 9, 16, 17, 35, 64, 65, 130])
+@pytest.mark.parametrize("length", [1, 2, 7, 8, 9, 16, 17, 35, 64, 65, 130, 513, 600])
 def test_prefill_matches_token_by_token(lz, device, suite, length):
     rng = np.random.default_rng(length)
     cfg = hf_tiny.TINY["llama3"]
     prompt = rng.integers(0, cfg["vocab"], length).astype(np.int32)
-    with make_model(lz, device, suite, "llama3", "float16", "f16") as model:
+    with make_model(lz, device, suite, "llama3", "float16", "f16", max_seq=max(256, length + 8)) as model:
         seq = None
         for i, tok in enumerate(prompt):
             seq = model.ComputeLogits(int(tok), i)
@@ -116,8 +116,8 @@ def test_prefill_tensor_core_gemm_matches_gemv(lz, device, suite, name, precisio
     into hi + lo 16-bit halves (int8: per-row scales, bytes converted to f16 in shared memory); the
     logits agree with the GEMV-only prefill up to f32 summation order."""
     rng = np.random.default_rng(7)
-    prompt = rng.integers(0, hf_tiny.TINY[name]["vocab"], 100).astype(np.int32)  # chunks of 64 and 36
-    with make_model(lz, device, suite, name, precision, kv) as model:
+    prompt = rng.integers(0, hf_tiny.TINY[name]["vocab"], 600).astype(np.int32)  # chunks of 512 and 88
+    with make_model(lz, device, suite, name, precision, kv, max_seq=640) as model:
         model.set_gemm_rows(0)
         want = model.Prefill(prompt)
         want_next = model.Decode(int(np.argmax(want)))
