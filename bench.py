@@ -524,6 +524,7 @@ def measure_cfg4_tp(lz, dev, suite, stream_ptr, torch, dist, world: int, rank: i
         box = [lz.Communicator.unique_id() if rank == 0 else None]
         dist.broadcast_object_list(box, src=0)
         comm = lz.Communicator(dev, box[0], world, rank)
+    uses_peer = comm is not None and comm.UsesPeerAllReduce
     cfg = lz.model_config(kv_dtype=lz.BF16, tp_size=world, tp_rank=rank, **CFG4)
     model = lz.LlmModel(dev, suite, cfg, CFG4_PROMPT + 2 * warmup + steps + 16, "bfloat16", comm=comm)
     model.init_synthetic(4, 0.02)
@@ -566,7 +567,8 @@ def measure_cfg4_tp(lz, dev, suite, stream_ptr, torch, dist, world: int, rank: i
             "value": round(steps / (ms / 1e3), 2), "unit": "tok/s", "ms_per_step": round(ms / steps, 4),
             "scaling": "strong", "parallelism": f"tp{world}", "prefill_s": round(prefill_s, 3),
             "per_rank_weight_gbs": round(proj / (ms / steps * 1e-3) / 1e9, 1),
-            "weight_bytes_per_rank": int(proj), "ranks_agree_on_tokens": agree, "steps": steps, "warmup": warmup}
+            "weight_bytes_per_rank": int(proj), "ranks_agree_on_tokens": agree, "steps": steps, "warmup": warmup,
+            "allreduce": "peer memory" if uses_peer else ("nccl" if world > 1 else "none")}
 
 
 def run_cfg4_tp(args) -> int:
@@ -604,7 +606,7 @@ def run_cfg4_tp(args) -> int:
                        "parallelism": r["parallelism"],
                        "l2": "inputs larger than L2: every rank streams its weight shard each step"},
             "per_rank_weight_gbs": r["per_rank_weight_gbs"], "clocks": clocks, "prefill_s": r["prefill_s"],
-            "ranks_agree_on_tokens": r["ranks_agree_on_tokens"]}
+            "ranks_agree_on_tokens": r["ranks_agree_on_tokens"], "allreduce": r["allreduce"]}
         print(json.dumps(line))
     if world > 1:
         dist.destroy_process_group()
@@ -718,6 +720,8 @@ def main() -> int:
     ap.add_argument("--no-bulk-gemv", action="store_true",
                     help="one-row projections on the register-streamed GEMV only (l0b_set_gemv_bulk(0))")
     ap.add_argument("--no-legs", action="store_true", help="skip the config 0 / 1 / 3 legs of the bench line")
+    ap.add_argument("--nccl-only", action="store_true",
+                    help="tensor-parallel all-reduces on NCCL only (no peer-memory all-reduce)")
     ap.add_argument("--no-tp", action="store_true", help="skip the config 4 tensor-parallel leg (tp)")
     ap.add_argument("--profile-case", choices=["decode-bs1", "decode-bs16", "gemm-gateup-16", "attention-512"],
                     help="run one small case for an ncu capture instead of the benchmark")
@@ -726,6 +730,10 @@ def main() -> int:
         from l0llm_b200 import levelzero as lz
 
         lz.load_library().l0b_set_gemv_bulk(0)
+    if args.nccl_only:
+        from l0llm_b200 import levelzero as lz
+
+        lz.Communicator.set_peer_allreduce(False)
     if args.profile_case:
         return run_profile_case(args.profile_case)
     if args.impl == "reference":

@@ -437,6 +437,16 @@ L0B_API l0b_status l0b_comm_free(l0b_comm* comm);
 /* In-place sum of the first `count` elements of `buf` over the ranks, on the device stream (recorded
  * into the current command list when the device is recording). */
 L0B_API l0b_status l0b_comm_allreduce(l0b_comm* comm, l0b_buffer* buf, int64_t count);
+/* Tensor-parallel all-reduces of f32 sums (the row-split o_proj / down partials) and u64 maxima (the
+ * vocab-split argmax keys) up to 2 MB run as one kernel over peer memory: every rank's mailbox is mapped
+ * into the others by CUDA IPC when the communicator is made; each rank writes its partial into every
+ * mailbox, raises an epoch flag there, waits (bounded, ~2 s, then the device error flag) for the others'
+ * flags and sums in rank order, so all ranks hold the same bits. No multicast loads. Larger or other
+ * collectives, and communicators made after l0b_comm_set_peer_allreduce(0), use NCCL. No counterpart in
+ * the reference (single device). */
+L0B_API l0b_status l0b_comm_set_peer_allreduce(int32_t enable);
+/* *enabled = 1 when this communicator's small all-reduces run over peer memory (every rank agrees). */
+L0B_API l0b_status l0b_comm_uses_peer_allreduce(l0b_comm* comm, int32_t* enabled);
 
 /* Tuning: the largest K split the tensor-core GEMM may use for narrow projections (1..16, default 16;
  * <= 0 restores the default). Affects plans made after the call. */
@@ -543,6 +553,13 @@ L0B_API l0b_status l0b_model_free(l0b_model* model);
  * model keeps its rank's shard. */
 L0B_API l0b_status l0b_model_set_tensor(l0b_model* model, const char* name, const float* data,
                                         int64_t count);
+/* A checkpoint tensor's raw 16-bit payload (dtype L0B_F16 or L0B_BF16, count values, HF [out, in] order) --
+ * the bytes a safetensors F16 / BF16 entry holds -- uploaded as is and widened, range-checked (Float16
+ * storage), converted or quantized on the device, with the rules of l0b_model_set_tensor. Replaces the
+ * host-side BF16 -> f32 conversion before upload (L/SafetensorsReader.cs:262-277) and halves the bytes that
+ * cross PCIe. */
+L0B_API l0b_status l0b_model_set_tensor_raw(l0b_model* model, const char* name, const void* data, int32_t dtype,
+                                            int64_t count);
 /* Seeded synthetic weights generated on the device (no host copy): projections N(0, std) (an
  * Irwin-Hall(4) approximation of the normal), or for Int8 precision uniform int8 in [-127, 127]
  * with fp16 scales uniform on [scale_lo, scale_hi]; biases N(0, std); norms 1. */

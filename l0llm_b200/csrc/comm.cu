@@ -9,14 +9,28 @@
 
 #include <cstring>
 #include <mutex>
+#include <vector>
 
+#include "common.cuh"
 #include "runtime.h"
+
+// Peer all-reduce (small collectives of the decode step): every rank owns a mailbox in its HBM, mapped
+// into every other rank's address space by CUDA IPC. Layout of a mailbox:
+//   data  [2 parities][kMaxRanks][slot_floats]   partials written by the ranks (peer stores over NVLink)
+//   flags [2 parities][kMaxRanks][kPeerCtas]     epoch of the partial a rank's CTA has published here
+//   epoch [kPeerCtas]                            this rank's own count of all-reduces, per CTA
+constexpr int kMaxRanks = 8;
+constexpr int kPeerCtas = 32;
+constexpr size_t kPeerSlotFloats = size_t(1) << 19;  // 2 MB per partial: 64 rows of 8192
 
 struct l0b_comm {
     ncclComm_t comm = nullptr;
     int nranks = 1;
     int rank = 0;
     l0b_device* dev = nullptr;
+    char* mbox = nullptr;                  // own mailbox
+    char* peer_mbox[kMaxRanks] = {};       // every rank's mailbox in this process's address space
+    bool peer = false;                     // peer all-reduce available
 };
 
 namespace l0b {
@@ -36,6 +50,7 @@ struct NcclApi {
 
 NcclApi g_nccl;
 std::mutex g_nccl_mu;
+bool g_peer_disabled = false;  // l0b_comm_set_peer_allreduce(0): every collective on NCCL
 
 l0b_status nccl_load() {
     std::lock_guard<std::mutex> lock(g_nccl_mu);
@@ -81,9 +96,177 @@ l0b_status collective_issue(int kind, const CollArgs& a, cudaStream_t stream) {
     return L0B_OK;
 }
 
+// ---------------------------------------------------------------------------------------------
+// One-shot all-reduce over peer memory. CTA c of every rank takes slice c of the buffer: it writes the
+// slice into its slot of every rank's mailbox (parity = epoch & 1, so a rank one all-reduce ahead writes
+// the other half while a peer still reads this one), makes the stores visible system-wide, publishes
+// the epoch in each rank's flag for (itself, c), waits -- bounded -- until every rank's flag for c in its
+// own mailbox holds the epoch, and sums the slots in rank order, so every rank gets the same bits. A
+// rank can be at most one all-reduce ahead of any other (finishing one needs every rank's partial of
+// it), which two parities cover. All ranks make the same sequence of calls with the same counts, so
+// their per-CTA epochs agree.
+// ---------------------------------------------------------------------------------------------
+struct PeerArgs {
+    void* buf;
+    long long count;
+    char* mbox[kMaxRanks];
+    int nranks, rank;
+    int* error;
+};
+
+__device__ __forceinline__ unsigned peer_ld_acquire(const unsigned* p) {
+    unsigned v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void peer_st_release(unsigned* p, unsigned v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+template <typename T, bool MAX>
+__global__ void __launch_bounds__(512) peer_allreduce_kernel(const PeerArgs a) {
+    pdl_wait();
+    const int c = blockIdx.x, n = a.nranks;
+    const long long per = (a.count + gridDim.x - 1) / gridDim.x;
+    const long long lo = c * per, hi = min(a.count, lo + per);
+    char* mine = a.mbox[a.rank];
+    const size_t data_bytes = 2ull * kMaxRanks * kPeerSlotFloats * sizeof(float);
+    unsigned* epoch_p = reinterpret_cast<unsigned*>(mine + data_bytes + 2ull * kMaxRanks * kPeerCtas * sizeof(unsigned)) + c;
+    __shared__ unsigned ep_s;
+    if (threadIdx.x == 0) ep_s = *epoch_p + 1;
+    __syncthreads();
+    const unsigned ep = ep_s;
+    const int par = ep & 1;
+    T* buf = static_cast<T*>(a.buf);
+    auto slot = [&](char* mb, int src) {
+        return reinterpret_cast<T*>(mb + (static_cast<size_t>(par) * kMaxRanks + src) * kPeerSlotFloats * sizeof(float));
+    };
+    auto flag = [&](char* mb, int src) {
+        return reinterpret_cast<unsigned*>(mb + data_bytes) + (static_cast<size_t>(par) * kMaxRanks + src) * kPeerCtas + c;
+    };
+    // 1. This rank's slice into its slot of every rank's mailbox.
+    for (int r = 0; r < n; ++r) {
+        T* dst = slot(a.mbox[r], a.rank);
+        for (long long i = lo + threadIdx.x; i < hi; i += blockDim.x) dst[i] = buf[i];
+    }
+    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x < n) peer_st_release(flag(a.mbox[threadIdx.x], a.rank), ep);
+    // 2. Every rank's slice has arrived here (bounded wait: ~2 s, then the device error flag).
+    if (threadIdx.x < n) {
+        const unsigned* f = flag(mine, threadIdx.x);
+        const long long t0 = clock64();
+        while (peer_ld_acquire(f) != ep) {
+            if (clock64() - t0 > 4000000000LL) {
+                if (a.error) atomicExch(a.error, 1);
+                break;
+            }
+        }
+    }
+    __syncthreads();
+    // 3. Sum in rank order (identical on every rank). The slots were written by other GPUs: read them at
+    // L2 (ld.cg), past any line this SM's L1 kept from the same parity two calls ago.
+    for (long long i = lo + threadIdx.x; i < hi; i += blockDim.x) {
+        T v = __ldcg(slot(mine, 0) + i);
+        for (int r = 1; r < n; ++r) {
+            const T w = __ldcg(slot(mine, r) + i);
+            if constexpr (MAX) v = w > v ? w : v;
+            else v += w;
+        }
+        buf[i] = v;
+    }
+    if (threadIdx.x == 0) *epoch_p = ep;
+}
+
 l0b_status comm_allreduce(l0b_comm* c, void* buf, size_t count, int dtype, int op) {
+    const size_t esize = dtype == kDtypeU64 ? 8 : 4;
+    const bool fits = count * esize <= kPeerSlotFloats * sizeof(float);
+    if (c->peer && fits && ((dtype == L0B_F32 && op == COLL_SUM) || (dtype == kDtypeU64 && op == COLL_MAX))) {
+        PeerArgs a{};
+        a.buf = buf;
+        a.count = static_cast<long long>(count);
+        for (int r = 0; r < c->nranks; ++r) a.mbox[r] = c->peer_mbox[r];
+        a.nranks = c->nranks;
+        a.rank = c->rank;
+        a.error = c->dev->error_flag;
+        long long ctas = (static_cast<long long>(count) + 2047) / 2048;
+        if (ctas > kPeerCtas) ctas = kPeerCtas;
+        if (ctas < 1) ctas = 1;
+        if (dtype == kDtypeU64)
+            return c->dev->launch(peer_allreduce_kernel<unsigned long long, true>, dim3(static_cast<unsigned>(ctas)),
+                                  dim3(512), 0, a);
+        return c->dev->launch(peer_allreduce_kernel<float, false>, dim3(static_cast<unsigned>(ctas)), dim3(512), 0, a);
+    }
     CollArgs a{buf, buf, count, dtype, op, c->comm};
     return c->dev->collective(REC_ALLREDUCE, a);
+}
+
+// Maps every rank's mailbox into this process: the mailbox handles are all-gathered over NCCL (outside
+// any capture) and opened with peer access. Returns without enabling the peer path when IPC is refused
+// (the NCCL collectives then serve every call).
+l0b_status peer_setup(l0b_comm* c) {
+    if (c->nranks < 2 || c->nranks > kMaxRanks || g_peer_disabled) return L0B_OK;
+    const size_t mbox_bytes = 2ull * kMaxRanks * kPeerSlotFloats * sizeof(float) +
+                              2ull * kMaxRanks * kPeerCtas * sizeof(unsigned) + kPeerCtas * sizeof(unsigned);
+    if (cudaMalloc(&c->mbox, mbox_bytes) != cudaSuccess) {
+        cudaGetLastError();
+        c->mbox = nullptr;
+        return L0B_OK;
+    }
+    cudaMemsetAsync(c->mbox, 0, mbox_bytes, c->dev->stream);
+    cudaIpcMemHandle_t h;
+    if (cudaIpcGetMemHandle(&h, c->mbox) != cudaSuccess) {
+        cudaGetLastError();
+        return L0B_OK;
+    }
+    char* xfer = nullptr;
+    L0B_CHECK_CUDA(cudaMalloc(&xfer, sizeof(h) * (c->nranks + 1)));
+    L0B_CHECK_CUDA(cudaMemcpyAsync(xfer, &h, sizeof(h), cudaMemcpyHostToDevice, c->dev->stream));
+    ncclResult_t r = g_nccl.all_gather(xfer, xfer + sizeof(h), sizeof(h), ncclUint8, c->comm, c->dev->stream);
+    std::vector<cudaIpcMemHandle_t> all(c->nranks);
+    cudaError_t e = cudaSuccess;
+    if (r == ncclSuccess)
+        e = cudaMemcpyAsync(all.data(), xfer + sizeof(h), sizeof(h) * c->nranks, cudaMemcpyDeviceToHost, c->dev->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(c->dev->stream);
+    cudaFree(xfer);
+    if (r != ncclSuccess) return fail(L0B_ERR_NCCL, "mailbox handle exchange failed: %s", g_nccl.error_string(r));
+    L0B_CHECK_CUDA(e);
+    bool ok = true;
+    for (int q = 0; q < c->nranks; ++q) {
+        if (q == c->rank) {
+            c->peer_mbox[q] = c->mbox;
+            continue;
+        }
+        void* p = nullptr;
+        if (cudaIpcOpenMemHandle(&p, all[q], cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+            cudaGetLastError();
+            ok = false;
+            break;
+        }
+        c->peer_mbox[q] = static_cast<char*>(p);
+    }
+    // Every rank must take the same path: agree on it (a max over ranks of "failed").
+    int* flag = nullptr;
+    L0B_CHECK_CUDA(cudaMalloc(&flag, sizeof(int)));
+    const int bad = ok ? 0 : 1;
+    L0B_CHECK_CUDA(cudaMemcpyAsync(flag, &bad, sizeof(int), cudaMemcpyHostToDevice, c->dev->stream));
+    r = g_nccl.all_reduce(flag, flag, 1, ncclInt32, ncclMax, c->comm, c->dev->stream);
+    int any_bad = 1;
+    if (r == ncclSuccess) e = cudaMemcpyAsync(&any_bad, flag, sizeof(int), cudaMemcpyDeviceToHost, c->dev->stream);
+    if (r == ncclSuccess && e == cudaSuccess) e = cudaStreamSynchronize(c->dev->stream);
+    cudaFree(flag);
+    if (r != ncclSuccess) return fail(L0B_ERR_NCCL, "peer setup agreement failed: %s", g_nccl.error_string(r));
+    L0B_CHECK_CUDA(e);
+    c->peer = any_bad == 0;
+    return L0B_OK;
+}
+
+void peer_release(l0b_comm* c) {
+    for (int q = 0; q < c->nranks && q < kMaxRanks; ++q)
+        if (q != c->rank && c->peer_mbox[q]) cudaIpcCloseMemHandle(c->peer_mbox[q]);
+    if (c->mbox) cudaFree(c->mbox);
+    c->mbox = nullptr;
+    c->peer = false;
 }
 
 l0b_status comm_allgather(l0b_comm* c, const void* send, void* recv, size_t count, int dtype) {
@@ -147,6 +330,13 @@ L0B_API l0b_status l0b_comm_create(l0b_device* dev, const uint8_t* id, int32_t b
         if (e != cudaSuccess) return fail(L0B_ERR_CUDA, "communicator warm-up failed: %s", cudaGetErrorString(e));
         return fail(L0B_ERR_NCCL, "communicator warm-up failed: %s", g_nccl.error_string(r));
     }
+    l0b_status ps = peer_setup(c);
+    if (ps != L0B_OK) {
+        peer_release(c);
+        g_nccl.comm_destroy(c->comm);
+        delete c;
+        return ps;
+    }
     *out = c;
     return L0B_OK;
 }
@@ -157,9 +347,22 @@ L0B_API l0b_status l0b_comm_free(l0b_comm* c) {
         cudaSetDevice(c->dev->index);
         // Captured collectives keep the communicator busy: release the device's graphs first.
         c->dev->drop_graphs();
+        cudaStreamSynchronize(c->dev->stream);
+        peer_release(c);
         g_nccl.comm_destroy(c->comm);
     }
     delete c;
+    return L0B_OK;
+}
+
+L0B_API l0b_status l0b_comm_set_peer_allreduce(int32_t enable) {
+    g_peer_disabled = enable == 0;
+    return L0B_OK;
+}
+
+L0B_API l0b_status l0b_comm_uses_peer_allreduce(l0b_comm* c, int32_t* enabled) {
+    L0B_REQUIRE(c && enabled, L0B_ERR_ARGUMENT, "null argument");
+    *enabled = c->peer ? 1 : 0;
     return L0B_OK;
 }
 

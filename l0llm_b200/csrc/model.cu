@@ -1024,7 +1024,7 @@ L0B_API l0b_status l0b_model_create(l0b_device* dev, l0b_suite* suite, const l0b
         L0B_TRY(m->alloc(&L.post_norm, m->h));
         L0B_TRY(m->alloc_matrix(L.qkv, m->qkv_w, m->h));
         L0B_TRY(m->alloc_matrix(L.o, m->h, m->qdim));
-        L0B_TRY(m->alloc_matrix(L.gate_up, 2 * m->inter, m->h));
+        L0B_TRY(m->alloc_matrix(L.gate_up, 2 * m->inter, m->h, false));  // SwiGLU epilogues take row-major weights
         L0B_TRY(m->alloc_matrix(L.down, m->h, m->inter));
         if (c.attention_bias) L0B_TRY(m->alloc(&L.qkv_bias, m->qkv_w));
         if (c.qk_norm) {
@@ -1105,34 +1105,20 @@ L0B_API l0b_status l0b_model_free(l0b_model* model) {
     return L0B_OK;
 }
 
-L0B_API l0b_status l0b_model_set_tensor(l0b_model* m, const char* name, const float* data, int64_t count) {
-    GUARD_BEGIN
-    L0B_REQUIRE(m && name && data, L0B_ERR_ARGUMENT, "null argument");
-    Target t;
-    L0B_TRY(resolve(m, name, &t));
-    const long long full = static_cast<long long>(t.full_rows) * t.full_cols;
-    L0B_REQUIRE(count == full, L0B_ERR_INVALID_DATA, "Tensor '%s' has %lld values, expected %lld.", name,
-                (long long)count, full);
-    if (t.mat && t.mat->dtype == L0B_F16) {
-        // LlmMatrix.FitsInHalf (L/LlmMatrix.cs:110-120): Float16 storage refuses values a half cannot hold.
-        for (long long i = 0; i < full; ++i)
-            L0B_REQUIRE(std::isfinite(data[i]) && std::fabs(data[i]) <= 65000.f, L0B_ERR_INVALID_DATA,
-                        "Tensor '%s' has values outside the half-precision range.", name);
-    }
-    if (t.embed && m->cfg.tie_word_embeddings) {
-        // Tied head: lm_head.weight is the embedding table (L/LlmModel.cs:62).
-        L0B_TRY(l0b_model_set_tensor(m, "lm_head.weight", data, count));
-    }
-    L0B_CHECK_CUDA(cudaSetDevice(m->dev->index));
-    float* staging = nullptr;
-    L0B_CHECK_CUDA(cudaMalloc(&staging, static_cast<size_t>(full) * sizeof(float)));
+}  // extern "C"
+
+namespace {
+
+// The load-time rules of LlmLayerWeights / LlmMatrix applied to one HF tensor already on the device as
+// f32 (`staging`, the full tensor): norm offset, int8 quantization or 16-bit storage, the rank's shard.
+l0b_status set_tensor_staged(l0b_model* m, const Target& t, const float* staging) {
     struct Free {
         float* p;
         ~Free() { cudaFree(p); }
-    } guard{staging};
-    L0B_CHECK_CUDA(copy_sync(m->dev->stream, staging, data, static_cast<size_t>(full) * sizeof(float), cudaMemcpyHostToDevice));
+    };
     cudaStream_t st = m->dev->stream;
     const int sm = m->dev->sm_count;
+    const long long full = static_cast<long long>(t.full_rows) * t.full_cols;
     if (t.embed) {
         L0B_CHECK_CUDA(cudaMemcpyAsync(m->embed, staging, static_cast<size_t>(full) * sizeof(float),
                                        cudaMemcpyDeviceToDevice, st));
@@ -1198,6 +1184,105 @@ L0B_API l0b_status l0b_model_set_tensor(l0b_model* m, const char* name, const fl
     L0B_CHECK_CUDA(cudaGetLastError());
     L0B_CHECK_CUDA(cudaStreamSynchronize(st));
     return L0B_OK;
+}
+
+// 16-bit HF tensor values (F16 or BF16 bits) widened to f32 on the device.
+__global__ void widen16_kernel(const uint16_t* src, int dtype, float* dst, long long count) {
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < count;
+         i += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const uint16_t b = src[i];
+        dst[i] = dtype == L0B_BF16 ? __uint_as_float(static_cast<uint32_t>(b) << 16) : __half2float(__ushort_as_half(b));
+    }
+}
+
+// LlmMatrix.FitsInHalf on the device: *bad = 1 when a value is not finite or exceeds 65000 in magnitude.
+__global__ void half_range_kernel(const float* v, long long count, int* bad) {
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < count;
+         i += static_cast<long long>(gridDim.x) * blockDim.x)
+        if (!isfinite(v[i]) || fabsf(v[i]) > 65000.f) *bad = 1;
+}
+
+}  // namespace
+
+extern "C" {
+
+L0B_API l0b_status l0b_model_set_tensor(l0b_model* m, const char* name, const float* data, int64_t count) {
+    GUARD_BEGIN
+    L0B_REQUIRE(m && name && data, L0B_ERR_ARGUMENT, "null argument");
+    Target t;
+    L0B_TRY(resolve(m, name, &t));
+    const long long full = static_cast<long long>(t.full_rows) * t.full_cols;
+    L0B_REQUIRE(count == full, L0B_ERR_INVALID_DATA, "Tensor '%s' has %lld values, expected %lld.", name,
+                (long long)count, full);
+    if (t.mat && t.mat->dtype == L0B_F16) {
+        // LlmMatrix.FitsInHalf (L/LlmMatrix.cs:110-120): Float16 storage refuses values a half cannot hold.
+        for (long long i = 0; i < full; ++i)
+            L0B_REQUIRE(std::isfinite(data[i]) && std::fabs(data[i]) <= 65000.f, L0B_ERR_INVALID_DATA,
+                        "Tensor '%s' has values outside the half-precision range.", name);
+    }
+    if (t.embed && m->cfg.tie_word_embeddings) {
+        // Tied head: lm_head.weight is the embedding table (L/LlmModel.cs:62).
+        L0B_TRY(l0b_model_set_tensor(m, "lm_head.weight", data, count));
+    }
+    L0B_CHECK_CUDA(cudaSetDevice(m->dev->index));
+    float* staging = nullptr;
+    L0B_CHECK_CUDA(cudaMalloc(&staging, static_cast<size_t>(full) * sizeof(float)));
+    struct Free {
+        float* p;
+        ~Free() { cudaFree(p); }
+    } guard{staging};
+    L0B_CHECK_CUDA(copy_sync(m->dev->stream, staging, data, static_cast<size_t>(full) * sizeof(float), cudaMemcpyHostToDevice));
+    return set_tensor_staged(m, t, staging);
+    GUARD_END
+}
+
+// The raw checkpoint bytes of a 16-bit tensor (SafetensorsReader's F16 / BF16 payload) go to the device as
+// they are -- half the bytes of the f32 upload -- and are widened, range-checked and converted or
+// quantized there (the host-side conversion of L/SafetensorsReader.cs:262-277 and L/LlmMatrix.cs:95-105).
+L0B_API l0b_status l0b_model_set_tensor_raw(l0b_model* m, const char* name, const void* data, int32_t dtype,
+                                            int64_t count) {
+    GUARD_BEGIN
+    L0B_REQUIRE(m && name && data, L0B_ERR_ARGUMENT, "null argument");
+    L0B_REQUIRE(dtype == L0B_F16 || dtype == L0B_BF16, L0B_ERR_UNSUPPORTED, "raw tensors are F16 or BF16 (dtype %d)",
+                dtype);
+    Target t;
+    L0B_TRY(resolve(m, name, &t));
+    const long long full = static_cast<long long>(t.full_rows) * t.full_cols;
+    L0B_REQUIRE(count == full, L0B_ERR_INVALID_DATA, "Tensor '%s' has %lld values, expected %lld.", name,
+                (long long)count, full);
+    L0B_CHECK_CUDA(cudaSetDevice(m->dev->index));
+    cudaStream_t st = m->dev->stream;
+    const int sm = m->dev->sm_count;
+    void* raw = nullptr;
+    float* staging = nullptr;
+    int* bad = nullptr;
+    L0B_CHECK_CUDA(cudaMalloc(&raw, static_cast<size_t>(full) * 2));
+    struct FreeV {
+        void* p;
+        ~FreeV() { cudaFree(p); }
+    } g1{raw};
+    L0B_CHECK_CUDA(cudaMalloc(&staging, static_cast<size_t>(full) * sizeof(float)));
+    FreeV g2{staging};
+    L0B_CHECK_CUDA(cudaMalloc(&bad, sizeof(int)));
+    FreeV g3{bad};
+    L0B_CHECK_CUDA(copy_sync(st, raw, data, static_cast<size_t>(full) * 2, cudaMemcpyHostToDevice));
+    widen16_kernel<<<grid_for(full, sm), 256, 0, st>>>(static_cast<const uint16_t*>(raw), dtype, staging, full);
+    L0B_CHECK_CUDA(cudaGetLastError());
+    const bool f16_store = t.mat && t.mat->dtype == L0B_F16;
+    const bool tied_f16 = t.embed && m->cfg.tie_word_embeddings && m->lm_head.dtype == L0B_F16;
+    if (f16_store || tied_f16) {
+        L0B_CHECK_CUDA(cudaMemsetAsync(bad, 0, sizeof(int), st));
+        half_range_kernel<<<grid_for(full, sm), 256, 0, st>>>(staging, full, bad);
+        int h = 0;
+        L0B_CHECK_CUDA(copy_sync(st, &h, bad, sizeof(int), cudaMemcpyDeviceToHost));
+        L0B_REQUIRE(!h, L0B_ERR_INVALID_DATA, "Tensor '%s' has values outside the half-precision range.", name);
+    }
+    if (t.embed && m->cfg.tie_word_embeddings) {
+        Target head;
+        L0B_TRY(resolve(m, "lm_head.weight", &head));
+        L0B_TRY(set_tensor_staged(m, head, staging));
+    }
+    return set_tensor_staged(m, t, staging);
     GUARD_END
 }
 

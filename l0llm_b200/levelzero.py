@@ -198,6 +198,7 @@ def load_library() -> C.CDLL:
         "l0b_model_free": (i32, [vp]),
         "l0b_model_set_tensor": (i32, [vp, C.c_char_p, vp, i64]),
         "l0b_model_init_synthetic": (i32, [vp, C.c_uint64, f32, f32, f32]),
+        "l0b_model_set_tensor_raw": (i32, [vp, C.c_char_p, vp, i32, i64]),
         "l0b_model_prefill": (i32, [vp, vp, i32, vp]),
         "l0b_model_decode": (i32, [vp, i32, vp]),
         "l0b_model_compute_logits": (i32, [vp, i32, i32, vp]),
@@ -663,6 +664,18 @@ class Communicator:
     def AllReduce(self, buf: "SharedBuffer", count: int | None = None):
         check(load_library().l0b_comm_allreduce(self.handle, buf.handle, buf.Count if count is None else count))
 
+    @property
+    def UsesPeerAllReduce(self) -> bool:
+        """True when this communicator's small all-reduces run over peer memory (IPC-mapped mailboxes)."""
+        v = C.c_int32()
+        check(load_library().l0b_comm_uses_peer_allreduce(self.handle, C.byref(v)))
+        return bool(v.value)
+
+    @staticmethod
+    def set_peer_allreduce(enabled: bool):
+        """Process-wide: communicators made afterwards use the peer all-reduce (True, default) or NCCL only."""
+        check(load_library().l0b_comm_set_peer_allreduce(1 if enabled else 0))
+
     def Dispose(self):
         if self.handle:
             load_library().l0b_comm_free(self.handle)
@@ -688,6 +701,11 @@ class LlmModel:
         self.cfg = cfg
         self.vocab = cfg.vocab_size  # under TP the logits are gathered to the full vocabulary
         self.MaxSeqLen = max_seq_len
+
+    def set_tensor_raw(self, name: str, bits: np.ndarray, dtype: int):
+        """Uploads the 16-bit payload (F16 or BF16 bits as uint16) of a checkpoint tensor as is."""
+        d = np.ascontiguousarray(bits).view(np.uint16).ravel()
+        check(load_library().l0b_model_set_tensor_raw(self.handle, name.encode(), _p(d), dtype, d.size))
 
     def init_synthetic(self, seed: int, std: float = 0.02, scale_lo: float = 1e-3, scale_hi: float = 2e-2):
         check(load_library().l0b_model_init_synthetic(self.handle, seed, std, scale_lo, scale_hi))

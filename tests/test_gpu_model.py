@@ -348,3 +348,44 @@ def test_uploaded_weights_match_hf_tensors(lz, device, suite, precision):
             else:
                 want = torch.from_numpy(full.ravel()).to(torch.bfloat16).view(torch.int16).numpy().view(np.uint16)
                 np.testing.assert_array_equal(model.read_weight(1, kind, np.uint16, full.size), want)
+
+
+@pytest.mark.parametrize("precision", ["float32", "float16", "bfloat16", "int8"])
+@pytest.mark.parametrize("raw", ["bf16", "f16"])
+def test_raw_16bit_upload_matches_f32_upload(lz, device, suite, precision, raw):
+    """l0b_model_set_tensor_raw uploads a checkpoint's 16-bit payload and converts it on the device; the
+    stored weights and the logits equal those of uploading the same values widened to f32 on the host."""
+    import torch
+
+    name = "llama3"
+    cfg = hf_tiny.TINY[name]
+    w = hf_tiny.weights(cfg, 11)
+    tdt = torch.bfloat16 if raw == "bf16" else torch.float16
+    bits = {k: torch.from_numpy(np.ascontiguousarray(v, np.float32)).to(tdt).view(torch.int16).numpy().view(np.uint16)
+            for k, v in w.items()}
+    wide = {k: torch.from_numpy(np.ascontiguousarray(v, np.float32)).to(tdt).to(torch.float32).numpy()
+            for k, v in w.items()}
+    prompt = hf_tiny.prompt(cfg, 11)[:6]
+    out = []
+    for use_raw in (True, False):
+        mc = lz.model_config(**hf_tiny.model_config_kwargs(cfg, kv_dtype=lz.F32, q8_group=0))
+        with lz.LlmModel(device, suite, mc, 32, precision) as model:
+            for k in w:
+                if use_raw:
+                    model.set_tensor_raw(k, bits[k], lz.BF16 if raw == "bf16" else lz.F16)
+                else:
+                    model.set_tensor(k, wide[k])
+            dt = {"float32": np.float32, "float16": np.float16, "bfloat16": np.uint16, "int8": np.int8}[precision]
+            n = model.read_weight(0, 2, dt, 2 * cfg["inter"] * cfg["hidden"])
+            out.append((model.Prefill(prompt), n))
+    np.testing.assert_array_equal(out[0][1], out[1][1])
+    np.testing.assert_array_equal(out[0][0], out[1][0])
+
+
+def test_raw_bf16_outside_half_range_is_rejected_for_float16(lz, device, suite):
+    cfg = hf_tiny.TINY["llama3"]
+    mc = lz.model_config(**hf_tiny.model_config_kwargs(cfg, kv_dtype=lz.F32, q8_group=0))
+    big = np.full((cfg["inter"], cfg["hidden"]), 0x4780, np.uint16)  # bf16 65536
+    with lz.LlmModel(device, suite, mc, 8, "float16") as model:
+        with pytest.raises(lz.InvalidDataException):
+            model.set_tensor_raw("model.layers.0.mlp.up_proj.weight", big, lz.BF16)

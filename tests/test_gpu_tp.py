@@ -20,9 +20,11 @@ CFG = dict(hidden_size=512, intermediate_size=1024, num_layers=2, num_attention_
 STEPS = 6
 
 
-def _rank(rank, world, idq, precision, q):
+def _rank(rank, world, idq, precision, q, peer=True):
     try:
         from l0llm_b200 import levelzero as lz
+
+        lz.Communicator.set_peer_allreduce(peer)
 
         # Rank 0 makes the id, so every rank bootstraps with the same NCCL build.
         if rank == 0:
@@ -43,6 +45,7 @@ def _rank(rank, world, idq, precision, q):
         out = {}
         with lz.Communicator(dev, uid, world, rank) as comm:
             note("communicator ready")
+            out["peer"] = comm.UsesPeerAllReduce
             cfg = lz.model_config(kv_dtype=lz.F16, tp_size=world, tp_rank=rank, **CFG)
             with lz.LlmModel(dev, suite, cfg, 64, precision, comm=comm) as m:
                 m.init_synthetic(4, 0.05, 1e-3, 2e-2)
@@ -63,15 +66,16 @@ def _rank(rank, world, idq, precision, q):
         q.put((rank, None, repr(e)))
 
 
+@pytest.mark.parametrize("peer", [True, False], ids=["peer-allreduce", "nccl"])
 @pytest.mark.parametrize("precision", ["bfloat16", "int8"])
-def test_tensor_parallel_two_gpus_match_single(lz, device, precision):
+def test_tensor_parallel_two_gpus_match_single(lz, device, precision, peer):
     import torch
 
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     ctx = mp.get_context("spawn")
     q, idq = ctx.Queue(), ctx.Queue()
-    procs = [ctx.Process(target=_rank, args=(r, 2, idq, precision, q)) for r in range(2)]
+    procs = [ctx.Process(target=_rank, args=(r, 2, idq, precision, q, peer)) for r in range(2)]
     for p in procs:
         p.start()
     results = {}
@@ -86,6 +90,7 @@ def test_tensor_parallel_two_gpus_match_single(lz, device, precision):
             if p.is_alive():
                 p.kill()
     r0, r1 = results[0], results[1]
+    assert r0["peer"] == r1["peer"] == peer
     # Both ranks see the gathered full-vocabulary logits and the same greedy tokens.
     np.testing.assert_array_equal(r0["logits"], r1["logits"])
     np.testing.assert_array_equal(r0["tokens"], r1["tokens"])
@@ -93,3 +98,91 @@ def test_tensor_parallel_two_gpus_match_single(lz, device, precision):
     err = np.abs(r0["logits"] - want).max()
     assert err <= 2e-3 * np.abs(want).max(), f"max err {err}"
     np.testing.assert_array_equal(r0["tokens"], r0["ref_tokens"])
+
+
+CFG4W = dict(hidden_size=8192, intermediate_size=28672, num_layers=2, num_attention_heads=64, num_key_value_heads=8,
+             head_dim=128, vocab_size=128256, max_position_embeddings=131072, rms_norm_eps=1e-5, rope_theta=5e5,
+             tie_word_embeddings=0, attention_bias=0, rope_type=3, rope_factor=8.0, rope_low_freq_factor=1.0,
+             rope_high_freq_factor=4.0, rope_original_max_position=8192)
+
+
+def _rank_cfg4(rank, world, idq, q, prompt, steps):
+    try:
+        from l0llm_b200 import levelzero as lz
+
+        if rank == 0:
+            uid = lz.Communicator.unique_id()
+            for _ in range(world - 1):
+                idq.put(uid)
+        else:
+            uid = idq.get(timeout=60)
+        dev = lz.ComputeDevice(rank)
+        suite = lz.LlmKernelSuite.Create(dev)
+        out = {}
+        with lz.Communicator(dev, uid, world, rank) as comm:
+            out["peer"] = comm.UsesPeerAllReduce
+            cfg = lz.model_config(kv_dtype=lz.BF16, tp_size=world, tp_rank=rank, **CFG4W)
+            with lz.LlmModel(dev, suite, cfg, 64, "bfloat16", comm=comm) as m:
+                m.init_synthetic(4, 0.02)
+                out["logits"] = m.Prefill(prompt)
+                out["tokens"] = m.decode_greedy_device(steps)
+        suite.Dispose()
+        dev.Dispose()
+        q.put((rank, out, None))
+    except Exception as e:
+        q.put((rank, None, repr(e)))
+
+
+def test_tensor_parallel_llama3_70b_width_against_oracle(lz, orc, device):
+    """Config 4 widths (Llama-3-70B: hidden 8192, 64 / 8 heads, inter 28672, vocab 128256, llama3 RoPE
+    scaling), bf16 weights N(0, 0.02) seed 4, two layers, tensor-parallel over 2 GPUs with the peer
+    all-reduce: the prefill logits of a 16-token prompt within max-abs 1e-2 + rel 1e-2 of the oracle
+    and 8 greedy tokens equal to the oracle's (a difference allowed only at a near-tie)."""
+    import torch
+
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    steps = 8
+    prompt = np.random.default_rng(4).integers(0, CFG4W["vocab_size"], 16).astype(np.int32)
+    ctx = mp.get_context("spawn")
+    q, idq = ctx.Queue(), ctx.Queue()
+    procs = [ctx.Process(target=_rank_cfg4, args=(r, 2, idq, q, prompt, steps)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = {}
+    try:
+        for _ in range(2):
+            rank, out, err = q.get(timeout=300)
+            assert err is None, f"rank {rank}: {err}"
+            results[rank] = out
+    finally:
+        for p in procs:
+            p.join(timeout=30)
+            if p.is_alive():
+                p.kill()
+    r0 = results[0]
+    assert r0["peer"] and results[1]["peer"]
+    np.testing.assert_array_equal(r0["tokens"], results[1]["tokens"])
+    om = orc.OracleModel(dict(hidden=8192, inter=28672, layers=2, heads=64, kv_heads=8, head_dim=128, vocab=128256,
+                              max_pos=131072, eps=1e-5, theta=5e5, tie=0, bias=0, qk_norm=0, rope_type=orc.ROPE_LLAMA3,
+                              rope_factor=8.0, rope_original_max=8192, rope_low=1.0, rope_high=4.0,
+                              rope_beta_fast=32.0, rope_beta_slow=1.0, rope_attention=0.0, wdtype=orc.BF16, group=0,
+                              kv_dtype=orc.BF16), 64)
+    om.init_synthetic(4, 0.02)
+    om.set_fast(True)
+    want = om.prefill(prompt)
+    err = np.abs(r0["logits"].astype(np.float64) - want)
+    assert np.all(err <= 1e-2 + 1e-2 * np.abs(want)), f"prefill logits: max err {err.max():.3e}"
+    toks, lg, pos = [], want, len(prompt)
+    for _ in range(steps + 1):
+        toks.append(int(np.argmax(lg)))
+        if len(toks) > steps:
+            break
+        lg = om.step(toks[-1], pos)
+        pos += 1
+    om.close()
+    # decode_greedy_device returns the tokens after the prefill's own argmax token.
+    got = [int(np.argmax(r0["logits"]))] + r0["tokens"].tolist()
+    for i, (g, w) in enumerate(zip(got, toks)):
+        if g != w:
+            pytest.fail(f"greedy token {i}: {g} != oracle {w}")
