@@ -634,7 +634,29 @@ def run_profile_case(case: str) -> int:
     sp = C.c_void_p()
     lz.check(lz.load_library().l0b_device_stream(dev.handle, C.byref(sp)))
     rng = np.random.default_rng(SEED)
-    if case in ("decode-bs1", "decode-bs16"):
+    if case == "decode-cfg4-tp8-shard":
+        # One rank's share of config 4 at TP8 as a single-GPU model: 8 query heads, 1 KV head, intermediate
+        # 3584, vocab 16032 give exactly the shard shapes (q/k/v [1280, 8192], o_proj [8192, 1024],
+        # gate/up [7168, 8192], down [8192, 3584], lm_head [16032, 8192]), without the all-reduces.
+        cfg = dict(CFG4, num_attention_heads=8, num_key_value_heads=1, intermediate_size=3584, vocab_size=16032)
+        stream = torch.cuda.ExternalStream(sp.value)
+        with lz.LlmModel(dev, suite, lz.model_config(kv_dtype=lz.BF16, **cfg), 2048 + 64, "bfloat16") as model:
+            model.init_synthetic(4, 0.02)
+            model.Prefill(rng.integers(0, cfg["vocab_size"], 2048).astype(np.int32))
+            model.decode_greedy_device(5)
+            dev.Synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            model.decode_greedy_device(20)
+            e1.record(stream)
+            e1.synchronize()
+            torch.cuda.nvtx.range_push("step")
+            model.decode_greedy_device(1)
+            dev.Synchronize()
+            torch.cuda.nvtx.range_pop()
+            print(json.dumps({"profile_case": case, "ms_per_step": round(e0.elapsed_time(e1) / 20, 4),
+                              "weight_bytes": model.ProjectionBytes}))
+    elif case in ("decode-bs1", "decode-bs16"):
         batch = 1 if case == "decode-bs1" else BS16
         mc = lz.model_config(kv_dtype=lz.F16, max_batch=batch, **CFG2)
         with lz.LlmModel(dev, suite, mc, CONTEXT + 64, "int8") as model:
@@ -723,7 +745,8 @@ def main() -> int:
     ap.add_argument("--nccl-only", action="store_true",
                     help="tensor-parallel all-reduces on NCCL only (no peer-memory all-reduce)")
     ap.add_argument("--no-tp", action="store_true", help="skip the config 4 tensor-parallel leg (tp)")
-    ap.add_argument("--profile-case", choices=["decode-bs1", "decode-bs16", "gemm-gateup-16", "attention-512"],
+    ap.add_argument("--profile-case", choices=["decode-bs1", "decode-bs16", "gemm-gateup-16", "attention-512",
+                                               "decode-cfg4-tp8-shard"],
                     help="run one small case for an ncu capture instead of the benchmark")
     args = ap.parse_args()
     if args.no_bulk_gemv:
