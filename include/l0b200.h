@@ -285,6 +285,11 @@ L0B_API l0b_status l0b_attention_decode_noalloc(void* stream, const float* q, co
  * probabilities, about fp32 accuracy) or on the scalar kernel (0). No counterpart in the reference. */
 L0B_API l0b_status l0b_set_attention_prefill_tensor_cores(int32_t enable);
 
+/* Tuning: decode attention clusters of up to 16 split CTAs (1, default, where the device can hold
+ * such non-portable clusters) or at most the portable 8 (0). More splits shorten each CTA's walk over
+ * the cache when a step has few (sequence, KV head) items. No counterpart in the reference. */
+L0B_API l0b_status l0b_set_attention_cluster16(int32_t enable);
+
 /* SigmoidGate.Execute(dev, x, gate, n) -- L/LlmDecoderLayer.cs:330,374. x *= sigmoid(gate). */
 L0B_API l0b_status l0b_sigmoid_gate_execute(l0b_suite* s, l0b_device* d, l0b_buffer* x, l0b_buffer* gate,
                                             int32_t n);
@@ -456,6 +461,10 @@ L0B_API l0b_status l0b_tc_set_max_splits(int32_t splits);
  * 512-k blocks of a tile for projections stored in the blocked layout (q/k/v, o_proj, down) -- or on the
  * register-streamed one (0). Affects launches made after the call. No counterpart in the reference. */
 L0B_API l0b_status l0b_set_gemv_bulk(int32_t enable);
+/* Tuning: largest K split (1, 2, 4 or 8; default 2) the register-streamed tensor-core GEMV takes only to
+ * fill SMs that its 16-row tiles would leave idle (fewer tiles than SMs, slices of at least 2048 k);
+ * 1 disables it. Affects launches made after the call. No counterpart in the reference. */
+L0B_API l0b_status l0b_set_gemv_fill_split(int32_t max_splits);
 /* Layout of the int8 weights of models created after the call: with blocking on (1, default), int8
  * projections with one scale per row, K % 512 == 0, N % 16 == 0 and fewer than 8 tiles of 16 rows per
  * SM (q/k/v, o_proj, down at Qwen2.5-7B widths) are stored as [N/16][K/512][16][512] bytes, so the k

@@ -28,6 +28,7 @@ namespace {
 constexpr int kT = 32;     // positions per tile
 constexpr int kMaxG = 8;   // query heads per CTA
 constexpr int kClusterThreads = 256;  // threads of the cluster decode kernel
+constexpr int kMaxClusterSplits = 16;  // CTAs per cluster of the cluster decode kernel (16 is non-portable)
 
 // Element d of a rotated head (HF rotate-half pairs) from the per-position cos/sin table.
 __device__ __forceinline__ float rope_elem(const float* head, int d, int rot, const float* cs, const float* sn) {
@@ -244,7 +245,7 @@ __global__ void __launch_bounds__(128) attn_kernel(const AttnParams p) {
 // ---------------------------------------------------------------------------------------------
 // Decode attention in thread-block clusters (no global partials, no counters).
 //
-// The S splits of one (query row, KV head group) form one cluster of (1, S, 1) CTAs, S <= 8. Each
+// The S splits of one (query row, KV head group) form one cluster of (1, S, 1) CTAs, S <= 16. Each
 // CTA walks its share of the positions -- chunk = max(p.chunk, 32 * ceil(seq / (32 S))) computed from
 // the live sequence length, so short contexts leave the tail CTAs idle instead of launching more --
 // with the next 32-position K/V tile loaded into registers while the current one is scored. Its
@@ -458,10 +459,10 @@ __global__ void __launch_bounds__(kClusterThreads) attn_cluster_kernel(const Att
     const int dper = HD / S;
     for (int o = tid; o < ng * dper; o += NT) {
         const int j = o / dper, d = split * dper + (o - (o / dper) * dper);
-        float mv[8], lv[8], av[8];
+        float mv[kMaxClusterSplits], lv[kMaxClusterSplits], av[kMaxClusterSplits];
         float mmax = kNegInf;
 #pragma unroll
-        for (int s = 0; s < 8; ++s) {
+        for (int s = 0; s < kMaxClusterSplits; ++s) {
             mv[s] = kNegInf, lv[s] = 0.f, av[s] = 0.f;
             if (s < nact) {
                 mv[s] = *peer(&m_s[j], s);
@@ -470,10 +471,10 @@ __global__ void __launch_bounds__(kClusterThreads) attn_cluster_kernel(const Att
             }
         }
 #pragma unroll
-        for (int s = 0; s < 8; ++s) mmax = fmaxf(mmax, mv[s]);
+        for (int s = 0; s < kMaxClusterSplits; ++s) mmax = fmaxf(mmax, mv[s]);
         float lsum = 0.f, y = 0.f;
 #pragma unroll
-        for (int s = 0; s < 8; ++s) {
+        for (int s = 0; s < kMaxClusterSplits; ++s) {
             if (s < nact) {
                 const float w = expf(mv[s] - mmax);
                 lsum = fmaf(w, lv[s], lsum);
@@ -511,6 +512,7 @@ l0b_status launch_attn(l0b_device* d, cudaStream_t stream, F kernel, dim3 grid, 
 // ---------------------------------------------------------------------------------------------
 constexpr int kPfBM = 64, kPfBN = 64;
 bool g_attn_prefill_mma = true;  // l0b_set_attention_prefill_tensor_cores
+bool g_attn_cluster16 = true;    // l0b_set_attention_cluster16
 
 __device__ __forceinline__ uint32_t pf_pack(float a, float b, bool bf) {
     if (bf) {
@@ -790,6 +792,42 @@ l0b_status attention_any(l0b_device* d, cudaStream_t stream, const AttnParams& p
     }
 }
 
+// Whether clusters of 16 CTAs (beyond the portable 8) of the cluster kernel can be resident: sets the
+// non-portable attribute on both instantiations and asks the occupancy calculator once per process.
+bool cluster16_ok() {
+    static std::once_flag once;
+    static bool ok = false;
+    std::call_once(once, [] {
+        const void* fns[2] = {reinterpret_cast<const void*>(attn_cluster_kernel<64>),
+                              reinterpret_cast<const void*>(attn_cluster_kernel<128>)};
+        bool all = true;
+        for (const void* f : fns) {
+            if (cudaFuncSetAttribute(f, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess) {
+                all = false;
+                break;
+            }
+            cudaLaunchConfig_t cfg = {};
+            cfg.gridDim = dim3(1, kMaxClusterSplits, 1);
+            cfg.blockDim = dim3(kClusterThreads);
+            cudaLaunchAttribute attr[1];
+            attr[0].id = cudaLaunchAttributeClusterDimension;
+            attr[0].val.clusterDim.x = 1;
+            attr[0].val.clusterDim.y = kMaxClusterSplits;
+            attr[0].val.clusterDim.z = 1;
+            cfg.attrs = attr;
+            cfg.numAttrs = 1;
+            int clusters = 0;
+            if (cudaOccupancyMaxActiveClusters(&clusters, f, &cfg) != cudaSuccess || clusters < 1) {
+                all = false;
+                break;
+            }
+        }
+        cudaGetLastError();
+        ok = all;
+    });
+    return ok;
+}
+
 template <typename F>
 l0b_status launch_attn_cluster(l0b_device* d, cudaStream_t stream, F kernel, dim3 grid, int S, const AttnParams& p) {
     if (d) return d->launch_cluster(kernel, grid, dim3(kClusterThreads), 0, S, p);
@@ -815,8 +853,8 @@ l0b_status launch_attn_cluster(l0b_device* d, cudaStream_t stream, F kernel, dim
 l0b_status attention_cluster_any(l0b_device* d, cudaStream_t stream, const AttnParams& p, int batch, int splits) {
     L0B_REQUIRE(p.nkv > 0 && p.nh % p.nkv == 0, L0B_ERR_ARGUMENT, "heads %d not a multiple of kv heads %d", p.nh,
                 p.nkv);
-    L0B_REQUIRE(splits == 1 || splits == 2 || splits == 4 || splits == 8, L0B_ERR_ARGUMENT,
-                "cluster splits %d (1, 2, 4 or 8)", splits);
+    L0B_REQUIRE(splits == 1 || splits == 2 || splits == 4 || splits == 8 || (splits == 16 && cluster16_ok()),
+                L0B_ERR_ARGUMENT, "cluster splits %d (1, 2, 4, 8, or 16 where the device runs such clusters)", splits);
     const int G = p.nh / p.nkv;
     const int gparts = (G + kMaxG - 1) / kMaxG;
     dim3 grid(p.nkv * gparts, splits, batch);
@@ -843,8 +881,8 @@ l0b_status attention_cluster_launch(l0b_device* d, const AttnParams& p, int batc
 
 int attention_cluster_splits(int max_seq, int work_items, int sm_count) {
     // Enough CTAs for about two per SM, and no split that the longest sequence cannot reach; at most
-    // the portable cluster size of 8.
-    int s = 8;
+    // 16 (the non-portable cluster size) where the device can hold such clusters, else the portable 8.
+    int s = g_attn_cluster16 && cluster16_ok() ? kMaxClusterSplits : 8;
     while (s > 1 && (static_cast<long long>(work_items) * s > 2LL * sm_count || 32LL * (s / 2) >= max_seq)) s >>= 1;
     return s;
 }
@@ -889,6 +927,11 @@ std::mutex g_noalloc_mutex;
 
 extern "C" L0B_API l0b_status l0b_set_attention_prefill_tensor_cores(int32_t enable) {
     l0b::g_attn_prefill_mma = enable != 0;
+    return L0B_OK;
+}
+
+extern "C" L0B_API l0b_status l0b_set_attention_cluster16(int32_t enable) {
+    l0b::g_attn_cluster16 = enable != 0;
     return L0B_OK;
 }
 

@@ -979,6 +979,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_mma_kernel(const GemvParams 
 
 bool g_gemv_mma = true;
 bool g_gemv_bulk = true;  // the bulk-copy one-row kernel where it applies (l0b_set_gemv_bulk)
+int g_gemv_fill_split = 2;  // largest split-K taken only to fill idle SMs (l0b_set_gemv_fill_split)
 
 template <typename F, typename... A>
 l0b_status launch_on(l0b_device* dev, cudaStream_t stream, F kernel, dim3 g, dim3 b, size_t smem, A... args) {
@@ -1465,15 +1466,28 @@ l0b_status launch_vec(l0b_device* dev, cudaStream_t stream, int sm_count, const 
 
 // Split count S (cluster size) for the tensor-core kernel: the smallest of 1, 2, 4, 8 whose K slice of
 // hi/lo activations fits the shared-memory budget (100 KB keeps two CTAs per SM); 0 = does not fit.
+// With sm_count > 0, S then doubles (up to g_gemv_fill_split) while the 16-row tiles alone would leave
+// SMs idle and each slice keeps at least 2048 k: a 1280-row projection over K = 8192 becomes 160 CTAs
+// of half rows instead of 80 CTAs of whole rows.
 template <typename WT>
-int mma_splits(const GemvParams& p, int rows) {
+int mma_splits(const GemvParams& p, int rows, int sm_count = 0) {
     const long long npieces = p.K / MmaPiece<WT>::kK;
-    for (int s = 1; s <= 8; s *= 2) {
-        const long long slice = (npieces + s - 1) / s * MmaPiece<WT>::kK;  // largest slice, in k
-        if (4ll * rows * slice <= 100 * 1024) return s;
+    int s = 0;
+    for (int c = 1; c <= 8 && !s; c *= 2) {
+        const long long slice = (npieces + c - 1) / c * MmaPiece<WT>::kK;  // largest slice, in k
+        if (4ll * rows * slice <= 100 * 1024) s = c;
     }
-    const long long slice8 = (npieces + 7) / 8 * MmaPiece<WT>::kK;
-    return 4ll * rows * slice8 <= 200 * 1024 ? 8 : 0;
+    if (!s) {
+        const long long slice8 = (npieces + 7) / 8 * MmaPiece<WT>::kK;
+        return 4ll * rows * slice8 <= 200 * 1024 ? 8 : 0;
+    }
+    if (sm_count > 0) {
+        const bool swiglu = p.epi == EPI_SWIGLU;
+        const long long ntiles = ((swiglu ? p.N / 2 : p.N) + (swiglu ? 7 : 15)) / (swiglu ? 8 : 16);
+        while (2 * s <= g_gemv_fill_split && ntiles * s < sm_count && npieces / (2 * s) * MmaPiece<WT>::kK >= 2048)
+            s *= 2;
+    }
+    return s;
 }
 
 template <typename WT, int NG>
@@ -1517,14 +1531,14 @@ l0b_status launch_mma(l0b_device* dev, cudaStream_t stream, int sm_count, const 
 // and up to 8 activation rows per pass, split over a cluster of up to 8 CTAs along K when the
 // activations of one CTA would not fit its shared memory. Returns the split count, 0 = does not apply.
 template <typename WT>
-int mma_applies(const GemvParams& p, int rows) {
+int mma_applies(const GemvParams& p, int rows, int sm_count = 0) {
     if constexpr (sizeof(WT) > 2) {
         return 0;
     } else {
         if (!(g_gemv_mma && p.K % MmaPiece<WT>::kK == 0 && reinterpret_cast<uintptr_t>(p.w) % 16 == 0 &&
               (sizeof(WT) != 1 || p.group >= p.K) && rows <= 8))
             return 0;
-        return mma_splits<WT>(p, rows);
+        return mma_splits<WT>(p, rows, sm_count);
     }
 }
 
@@ -1559,7 +1573,7 @@ l0b_status launch_typed(l0b_device* dev, cudaStream_t stream, int sm_count, Gemv
         if constexpr (sizeof(WT) <= 2) {
             GemvParams t8 = p;
             t8.M = mr;
-            splits = mma_applies<WT>(t8, mr);
+            splits = mma_applies<WT>(t8, mr, sm_count);
         }
         q.M = mr;
         q.x = static_cast<const char*>(p.x) + static_cast<size_t>(m0) * p.x_ld * dtype_size((l0b_dtype)p.x_dtype);
@@ -1675,6 +1689,7 @@ __global__ void __launch_bounds__(256) gemm_f32_kernel(int M, int N, int K, cons
 
 void gemv_set_tensor_cores(bool on) { g_gemv_mma = on; }
 void gemv_set_bulk(bool on) { g_gemv_bulk = on; }
+void gemv_set_fill_split(int s) { g_gemv_fill_split = s <= 1 ? 1 : (s >= 8 ? 8 : (s >= 4 ? 4 : 2)); }
 
 namespace {
 bool g_weight_blocking = true;  // l0b_set_weight_blocking

@@ -66,6 +66,7 @@ void gemv_set_tensor_cores(bool on);
 // Process-wide choice of the bulk-copy kernel for one activation row where it applies (default on);
 // launches already recorded keep their kernel.
 void gemv_set_bulk(bool on);
+void gemv_set_fill_split(int s);
 // Process-wide: models created afterwards store their int8 per-row-scaled projections with few row
 // tiles in the blocked layout (default on).
 bool weight_blocking();

@@ -65,6 +65,34 @@ def test_gemv_paths_store(lz, orc, device, suite, path, wkind, n, k, m):
     assert err <= tol * scale, f"{path}: max err {err} vs scale {scale}"
 
 
+@pytest.mark.parametrize("fill", [1, 2, 4, 8])
+@pytest.mark.parametrize("wkind", ["bf16", "i8c"])
+@pytest.mark.parametrize("n,k,m", [(1280, 8192, 1), (1280, 8192, 3), (200, 8192, 1), (1024, 4096, 2)])
+def test_gemv_fill_split(lz, orc, device, suite, fill, wkind, n, k, m):
+    """Projections with fewer 16-row tiles than SMs split K across a cluster only to fill idle SMs (the
+    q/k/v shard of an 8-way tensor-parallel 70B layer is 80 tiles over K = 8192): every split count
+    gives the oracle's result."""
+    lib = lz.load_library()
+    rng = np.random.default_rng(n + k + m + fill)
+    hf = ((rng.random((n, k)) * 2 - 1) * 0.05).astype(np.float32)
+    x = (rng.standard_normal((m, k)) * 2).astype(np.float32)
+    w_dev, w_orc, wdt, dt, scales, group = _weights(lz, orc, wkind, hf, k)
+    want = orc.gemv_out_in(x, w_orc, wdt, None if scales is None else scales.view(np.uint16), group)
+    lib.l0b_set_gemv_fill_split(fill)
+    try:
+        with lz.SharedBuffer.from_array(device, w_dev, dt) as W, lz.SharedBuffer.from_array(device, x) as xb, \
+                lz.SharedBuffer(device, lz.F32, m * n) as y:
+            sb = lz.SharedBuffer.from_array(device, scales) if scales is not None else None
+            suite.linear(device, m, n, k, xb, W, sb, group, None, y)
+            got = y.ToArray().reshape(m, n)
+            if sb is not None:
+                sb.Dispose()
+    finally:
+        lib.l0b_set_gemv_fill_split(2)
+    tol = 2e-4 if wkind == "bf16" else 2e-5
+    assert np.abs(got - want).max() <= tol * np.abs(want).max()
+
+
 @pytest.mark.parametrize("wkind", ["f16", "i8c"])
 @pytest.mark.parametrize("H,inter", [(896, 4864), (896, 100), (3584, 1000)])
 @pytest.mark.parametrize("m", [1, 3, 8, 16])

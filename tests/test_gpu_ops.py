@@ -319,10 +319,19 @@ def test_kv_cache_store_rounding(lz, orc, device, suite, dtype):
 ATTN_SHAPES = [(128, 28, 4), (64, 14, 2), (128, 64, 8), (128, 8, 1)]
 
 
+@pytest.fixture(params=[16, 8])
+def cluster_cap(request, lz):
+    """Largest decode-attention cluster: 16 split CTAs (non-portable clusters) or the portable 8."""
+    lib = lz.load_library()
+    lib.l0b_set_attention_cluster16(1 if request.param == 16 else 0)
+    yield request.param
+    lib.l0b_set_attention_cluster16(1)
+
+
 @pytest.mark.parametrize("hd,nh,nkv", ATTN_SHAPES)
 @pytest.mark.parametrize("seq", [1, 2, 31, 33, 64, 65, 513, 4096])
 @pytest.mark.parametrize("cache", ["f16", "f32"])
-def test_attention_decode(lz, orc, device, suite, hd, nh, nkv, seq, cache):
+def test_attention_decode(lz, orc, device, suite, cluster_cap, hd, nh, nkv, seq, cache):
     if cache == "f32" and seq > 600:
         pytest.skip("long sequences run with the f16 cache")
     rng = RNG(seq + hd + nh)
