@@ -525,6 +525,7 @@ def measure_cfg4_tp(lz, dev, suite, stream_ptr, torch, dist, world: int, rank: i
         dist.broadcast_object_list(box, src=0)
         comm = lz.Communicator(dev, box[0], world, rank)
     uses_peer = comm is not None and comm.UsesPeerAllReduce
+    fused = lz.Communicator.fused_allreduce()
     cfg = lz.model_config(kv_dtype=lz.BF16, tp_size=world, tp_rank=rank, **CFG4)
     model = lz.LlmModel(dev, suite, cfg, CFG4_PROMPT + 2 * warmup + steps + 16, "bfloat16", comm=comm)
     model.init_synthetic(4, 0.02)
@@ -560,7 +561,25 @@ def measure_cfg4_tp(lz, dev, suite, stream_ptr, torch, dist, world: int, rank: i
         agree = bool((same == ref).all())
     ms, prefill_s = float(t[0]), float(t[1])
     model.Dispose()
+    ar_us = None
     if comm is not None:
+        # The step's collective on its own: 2 x layers all-reduces of one hidden row per token, timed
+        # back to back with CUDA events on the model stream (max over ranks), for the all-reduce share.
+        n_ar = 2 * CFG4["num_layers"]
+        with lz.SharedBuffer(dev, lz.F32, CFG4["hidden_size"]) as hb:
+            for _ in range(20):
+                comm.AllReduce(hb)
+            barrier()
+            a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a0.record(stream)
+            for _ in range(n_ar):
+                comm.AllReduce(hb)
+            a1.record(stream)
+            a1.synchronize()
+            barrier()
+            ta = torch.tensor([a0.elapsed_time(a1) * 1e3 / n_ar], dtype=torch.float64, device="cuda")
+            dist.all_reduce(ta, op=dist.ReduceOp.MAX)
+            ar_us = float(ta[0])
         comm.Dispose()  # releases the device's captured graphs first
     return {"workload": f"config 4: Llama-3-70B-shape bf16 (80 layers, hidden 8192, 64/8 heads, inter 28672, vocab "
                         f"128256, llama3 RoPE), TP{world}, bs1, {CFG4_PROMPT}-token prompt",
@@ -568,7 +587,11 @@ def measure_cfg4_tp(lz, dev, suite, stream_ptr, torch, dist, world: int, rank: i
             "scaling": "strong", "parallelism": f"tp{world}", "prefill_s": round(prefill_s, 3),
             "per_rank_weight_gbs": round(proj / (ms / steps * 1e-3) / 1e9, 1),
             "weight_bytes_per_rank": int(proj), "ranks_agree_on_tokens": agree, "steps": steps, "warmup": warmup,
-            "allreduce": "peer memory" if uses_peer else ("nccl" if world > 1 else "none")}
+            "allreduce": ("peer memory, folded into the row-split GEMVs" if uses_peer and fused else "peer memory")
+            if uses_peer else ("nccl" if world > 1 else "none"),
+            "allreduce_us": None if ar_us is None else round(ar_us, 2),
+            "allreduce_share": None if ar_us is None else
+            round(2 * CFG4["num_layers"] * ar_us / (ms / steps * 1e3), 3)}
 
 
 def run_cfg4_tp(args) -> int:
@@ -606,7 +629,8 @@ def run_cfg4_tp(args) -> int:
                        "parallelism": r["parallelism"],
                        "l2": "inputs larger than L2: every rank streams its weight shard each step"},
             "per_rank_weight_gbs": r["per_rank_weight_gbs"], "clocks": clocks, "prefill_s": r["prefill_s"],
-            "ranks_agree_on_tokens": r["ranks_agree_on_tokens"], "allreduce": r["allreduce"]}
+            "ranks_agree_on_tokens": r["ranks_agree_on_tokens"], "allreduce": r["allreduce"],
+            "allreduce_us": r["allreduce_us"], "allreduce_share": r["allreduce_share"]}
         print(json.dumps(line))
     if world > 1:
         dist.destroy_process_group()
@@ -744,6 +768,8 @@ def main() -> int:
     ap.add_argument("--no-legs", action="store_true", help="skip the config 0 / 1 / 3 legs of the bench line")
     ap.add_argument("--nccl-only", action="store_true",
                     help="tensor-parallel all-reduces on NCCL only (no peer-memory all-reduce)")
+    ap.add_argument("--pair-allreduce", action="store_true",
+                    help="row-split GEMV + separate all-reduce kernel instead of the all-reduce folded into the GEMV")
     ap.add_argument("--no-tp", action="store_true", help="skip the config 4 tensor-parallel leg (tp)")
     ap.add_argument("--profile-case", choices=["decode-bs1", "decode-bs16", "gemm-gateup-16", "attention-512",
                                                "decode-cfg4-tp8-shard"],
@@ -757,6 +783,10 @@ def main() -> int:
         from l0llm_b200 import levelzero as lz
 
         lz.Communicator.set_peer_allreduce(False)
+    if args.pair_allreduce:
+        from l0llm_b200 import levelzero as lz
+
+        lz.Communicator.set_fused_allreduce(False)
     if args.profile_case:
         return run_profile_case(args.profile_case)
     if args.impl == "reference":

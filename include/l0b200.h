@@ -290,6 +290,12 @@ L0B_API l0b_status l0b_set_attention_prefill_tensor_cores(int32_t enable);
  * the cache when a step has few (sequence, KV head) items. No counterpart in the reference. */
 L0B_API l0b_status l0b_set_attention_cluster16(int32_t enable);
 
+/* Tuning: decode attention over f16 / bf16 caches (head dim 64 or 128) on the tensor cores (1, default:
+ * the query heads of a KV head as the rows of mma.sync tiles, hi + lo 16-bit queries and probabilities,
+ * about fp32 accuracy, the key and value of the new position as the cache stores them) or on the fp32
+ * FMA kernel (0). Affects launches recorded after the call. No counterpart in the reference. */
+L0B_API l0b_status l0b_set_attention_decode_tensor_cores(int32_t enable);
+
 /* SigmoidGate.Execute(dev, x, gate, n) -- L/LlmDecoderLayer.cs:330,374. x *= sigmoid(gate). */
 L0B_API l0b_status l0b_sigmoid_gate_execute(l0b_suite* s, l0b_device* d, l0b_buffer* x, l0b_buffer* gate,
                                             int32_t n);
@@ -452,6 +458,12 @@ L0B_API l0b_status l0b_comm_allreduce(l0b_comm* comm, l0b_buffer* buf, int64_t c
 L0B_API l0b_status l0b_comm_set_peer_allreduce(int32_t enable);
 /* *enabled = 1 when this communicator's small all-reduces run over peer memory (every rank agrees). */
 L0B_API l0b_status l0b_comm_uses_peer_allreduce(l0b_comm* comm, int32_t* enabled);
+/* With peer memory, a model's row-split decode projections (o_proj, down on the tensor-core GEMV) fold
+ * the all-reduce into the GEMV (1, default): each CTA sends its tiles' partial sums to every rank's
+ * mailbox, waits (bounded) for the same tiles from the other ranks and adds them to the residual stream
+ * in rank order -- the bits of the GEMV + all-reduce pair, one launch instead of two. 0: the pair.
+ * Process-wide; affects steps recorded after the call. No counterpart in the reference. */
+L0B_API l0b_status l0b_comm_set_fused_allreduce(int32_t enable);
 
 /* Tuning: the largest K split the tensor-core GEMM may use for narrow projections (1..16, default 16;
  * <= 0 restores the default). Affects plans made after the call. */

@@ -513,6 +513,7 @@ l0b_status launch_attn(l0b_device* d, cudaStream_t stream, F kernel, dim3 grid, 
 constexpr int kPfBM = 64, kPfBN = 64;
 bool g_attn_prefill_mma = true;  // l0b_set_attention_prefill_tensor_cores
 bool g_attn_cluster16 = true;    // l0b_set_attention_cluster16
+bool g_attn_decode_mma = true;   // l0b_set_attention_decode_tensor_cores
 
 __device__ __forceinline__ uint32_t pf_pack(float a, float b, bool bf) {
     if (bf) {
@@ -738,6 +739,362 @@ __global__ void __launch_bounds__(128) attn_prefill_mma_kernel(const AttnParams 
     }
 }
 
+// ---------------------------------------------------------------------------------------------
+// Decode attention on the tensor cores (mma.sync m16n8k16, fp32 accumulators), in thread-block
+// clusters like attn_cluster_kernel.
+//
+// CTA (KV head group of up to 16 query heads, split, sequence) walks its share of the positions in
+// 64-position tiles (K and V rows copied raw by cp.async into two swizzled stages). The query heads are
+// the MMA rows: warp w scores positions [16 w, 16 w + 16) of the tile for all of them (Q in hi + lo
+// 16-bit fragments, scaled by log2 e for exp2), keeps its own online softmax (running max, sum and
+// unnormalised output in registers) and adds P V with P split into hi + lo halves and V read by
+// ldmatrix.trans -- about fp32 accuracy from 16-bit operands, as in the prefill kernel. The new
+// position's key and value (RoPE applied, rounded to the cache type as the cache stores them) are
+// written into the tile by the CTA that owns the position. After the walk the four warps' states meet
+// in shared memory, then the cluster's splits meet through distributed shared memory as in the
+// FMA kernel (CTA r merges head dimensions [r HD / S, (r + 1) HD / S)).
+// ---------------------------------------------------------------------------------------------
+constexpr int kDmBN = 64;      // positions per tile
+constexpr int kDmHeads = 16;   // query heads per CTA (MMA rows)
+
+template <int HD>
+constexpr size_t decode_mma_smem() {
+    return 4ull * kDmBN * HD * 2;  // two stages of K and V tiles (16-bit)
+}
+
+template <int HD, bool BF>
+__global__ void __launch_bounds__(128) attn_decode_mma_kernel(const AttnParams p) {
+    namespace cg = cooperative_groups;
+    constexpr int NT = HD / 8;    // 8-column output tiles
+    constexpr int KS = HD / 16;   // 16-deep steps of Q K^T
+    constexpr int RB = HD * 2;    // bytes per tile row
+    constexpr int TILE = kDmBN * RB;
+    extern __shared__ __align__(128) unsigned char dm_smem[];
+    unsigned char* Ks = dm_smem;             // [2][kDmBN][HD] 16-bit, 16-byte chunks swizzled by row
+    unsigned char* Vs = dm_smem + 2 * TILE;  // [2][kDmBN][HD]
+    __shared__ __align__(16) float qn_s[kDmHeads][HD];   // rotated queries; after the walk, the CTA output
+    __shared__ float m_s[kDmHeads], l_s[kDmHeads];      // CTA state (log2 units) for the cluster merge
+    __shared__ float wm_s[4][kDmHeads], wl_s[4][kDmHeads];
+    __shared__ float cs_s[HD / 2], sn_s[HD / 2];
+    __shared__ __align__(16) uint16_t knew_s[HD], vnew_s[HD];
+
+    cg::cluster_group cluster = cg::this_cluster();
+    const int G = p.nh / p.nkv;
+    const int gparts = (G + kDmHeads - 1) / kDmHeads;
+    const int kvh = blockIdx.x / gparts, gp = blockIdx.x - (blockIdx.x / gparts) * gparts;
+    const int h0 = kvh * G + gp * kDmHeads;
+    const int ng = min(kDmHeads, G - gp * kDmHeads);
+    const int S = gridDim.y, split = blockIdx.y, b = blockIdx.z;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
+
+    pdl_wait();
+    const int qpos = p.positions ? p.positions[b] : p.pos_base + b * p.pos_step;
+    const int seq = qpos + 1;
+    int chunk = ((seq + S - 1) / S + kDmBN - 1) / kDmBN * kDmBN;
+    chunk = max(chunk, p.chunk);
+    const int nact = (seq + chunk - 1) / chunk;
+    const bool active = split < nact;
+    pdl_launch_dependents();
+    const int p_begin = split * chunk;
+    const int p_end = active ? min(seq, p_begin + chunk) : p_begin;
+    const bool owns_new = p.store_new && active && split == nact - 1;
+    const int ntiles = (p_end - p_begin + kDmBN - 1) / kDmBN;
+    const long long row_stride = static_cast<long long>(p.kv_dim) * 2;
+    const char* kbase = static_cast<const char*>(p.kc) + (b * p.cache_bstride + static_cast<long long>(kvh) * HD) * 2;
+    const char* vbase = static_cast<const char*>(p.vc) + (b * p.cache_bstride + static_cast<long long>(kvh) * HD) * 2;
+
+    // One K tile and V tile into stage st: 16-byte chunks, slots past the split zero-filled. The new
+    // position's row is left alone in tile 0 (patched from knew_s / vnew_s once they exist, before the
+    // first barrier that publishes the tile) and copied from them in later tiles.
+    const int qslot = owns_new ? qpos - p_begin : -1;  // the new position's slot in the CTA's range
+    auto load_tile = [&](int j, int st) {
+        for (int e = tid; e < kDmBN * (HD / 8); e += 128) {
+            const int r = e / (HD / 8), c = e - (e / (HD / 8)) * (HD / 8);
+            const int pos = p_begin + j * kDmBN + r;
+            const uint32_t off = static_cast<uint32_t>(r * RB + ((c ^ (r & 7)) * 16));
+            unsigned char* kd = Ks + st * TILE + off;
+            unsigned char* vd = Vs + st * TILE + off;
+            if (j * kDmBN + r == qslot) {
+                if (j > 0) {
+                    *reinterpret_cast<uint4*>(kd) = *reinterpret_cast<const uint4*>(knew_s + 8 * c);
+                    *reinterpret_cast<uint4*>(vd) = *reinterpret_cast<const uint4*>(vnew_s + 8 * c);
+                }
+            } else if (pos < p_end) {
+                const long long go = static_cast<long long>(pos) * row_stride + c * 16;
+                asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(static_cast<uint32_t>(
+                                 __cvta_generic_to_shared(kd))),
+                             "l"(kbase + go)
+                             : "memory");
+                asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(static_cast<uint32_t>(
+                                 __cvta_generic_to_shared(vd))),
+                             "l"(vbase + go)
+                             : "memory");
+            } else {
+                *reinterpret_cast<uint4*>(kd) = make_uint4(0, 0, 0, 0);
+                *reinterpret_cast<uint4*>(vd) = make_uint4(0, 0, 0, 0);
+            }
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+    if (ntiles > 0) load_tile(0, 0);  // in flight during the prologue
+
+    // Raw queries of the group (rows past ng zero), one 16-byte load each, all issued before any store.
+    const float* qb = p.q + b * p.q_bstride + static_cast<long long>(h0) * HD;
+    {
+        constexpr int PER = kDmHeads * HD / 4 / 128;  // float4s per thread
+        float4 v[PER];
+#pragma unroll
+        for (int i = 0; i < PER; ++i) {
+            const int idx = tid + i * 128, j = idx / (HD / 4);
+            v[i] = j < ng ? *reinterpret_cast<const float4*>(qb + 4 * idx) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int i = 0; i < PER; ++i) reinterpret_cast<float4*>(&qn_s[0][0])[tid + i * 128] = v[i];
+    }
+    if (p.rope) {
+        for (int i = tid; i < p.rot / 2; i += 128) {
+            const float ang = __fmul_rn(static_cast<float>(qpos), p.inv_freq[i]);
+            float sv, cv;
+            sincosf(ang, &sv, &cv);
+            cs_s[i] = __fmul_rn(cv, p.attn_scale);
+            sn_s[i] = __fmul_rn(sv, p.attn_scale);
+        }
+    }
+    __syncthreads();
+    // RoPE on the queries in place, one (d, d + rot / 2) pair per step.
+    if (p.rope) {
+        const int half = p.rot >> 1;
+        for (int idx = tid; idx < ng * half; idx += 128) {
+            const int j = idx / half, i = idx - (idx / half) * half;
+            const float x1 = qn_s[j][i], x2 = qn_s[j][i + half], c = cs_s[i], sn = sn_s[i];
+            qn_s[j][i] = __fsub_rn(__fmul_rn(x1, c), __fmul_rn(x2, sn));
+            qn_s[j][i + half] = __fadd_rn(__fmul_rn(x2, c), __fmul_rn(x1, sn));
+        }
+    }
+    // The new key (rotated) and value, rounded to the cache type; the group-0 CTA stores them, and the
+    // owner patches tile 0's slot when the new position lies in it.
+    if (owns_new) {
+        const float* kb = p.k_new + b * p.new_bstride + static_cast<long long>(kvh) * HD;
+        const float* vb = p.v_new + b * p.new_bstride + static_cast<long long>(kvh) * HD;
+        for (int d = tid; d < HD; d += 128) {
+            const float kv = p.rope ? rope_elem(kb, d, p.rot, cs_s, sn_s) : kb[d];
+            const float vv = vb[d];
+            uint16_t kbits, vbits;
+            if (BF) {
+                const __nv_bfloat16 kh = __float2bfloat16_rn(kv), vh = __float2bfloat16_rn(vv);
+                kbits = *reinterpret_cast<const uint16_t*>(&kh);
+                vbits = *reinterpret_cast<const uint16_t*>(&vh);
+            } else {
+                const __half kh = __float2half_rn(kv), vh = __float2half_rn(vv);
+                kbits = *reinterpret_cast<const uint16_t*>(&kh);
+                vbits = *reinterpret_cast<const uint16_t*>(&vh);
+            }
+            knew_s[d] = kbits;
+            vnew_s[d] = vbits;
+            if (gp == 0) {
+                const long long off = b * p.cache_bstride + static_cast<long long>(qpos) * p.kv_dim +
+                                      static_cast<long long>(kvh) * HD + d;
+                static_cast<uint16_t*>(p.kc)[off] = kbits;
+                static_cast<uint16_t*>(p.vc)[off] = vbits;
+            }
+        }
+        __syncthreads();
+        if (qslot < kDmBN) {
+            for (int c = tid; c < HD / 8; c += 128) {
+                const uint32_t off = static_cast<uint32_t>(qslot * RB + ((c ^ (qslot & 7)) * 16));
+                *reinterpret_cast<uint4*>(Ks + off) = *reinterpret_cast<const uint4*>(knew_s + 8 * c);
+                *reinterpret_cast<uint4*>(Vs + off) = *reinterpret_cast<const uint4*>(vnew_s + 8 * c);
+            }
+        }
+    }
+    __syncthreads();
+    const float qsc = p.scale * 1.4426950408889634f;
+    uint32_t qh[KS][4], ql[KS][4];
+#pragma unroll
+    for (int kk = 0; kk < KS; ++kk) {
+        const int c0 = 16 * kk + 2 * t, c1 = c0 + 8;
+        pf_split(qn_s[g][c0] * qsc, qn_s[g][c0 + 1] * qsc, BF, qh[kk][0], ql[kk][0]);
+        pf_split(qn_s[g + 8][c0] * qsc, qn_s[g + 8][c0 + 1] * qsc, BF, qh[kk][1], ql[kk][1]);
+        pf_split(qn_s[g][c1] * qsc, qn_s[g][c1 + 1] * qsc, BF, qh[kk][2], ql[kk][2]);
+        pf_split(qn_s[g + 8][c1] * qsc, qn_s[g + 8][c1 + 1] * qsc, BF, qh[kk][3], ql[kk][3]);
+    }
+    float o[NT][4];
+#pragma unroll
+    for (int n = 0; n < NT; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+    float ma = -INFINITY, mb = -INFINITY, la = 0.f, lb = 0.f;
+    for (int j = 0; j < ntiles; ++j) {
+        const int st = j & 1;
+        if (j + 1 < ntiles) {
+            load_tile(j + 1, st ^ 1);
+            asm volatile("cp.async.wait_group 1;" ::: "memory");
+        } else {
+            asm volatile("cp.async.wait_group 0;" ::: "memory");
+        }
+        __syncthreads();
+        const int w0 = p_begin + j * kDmBN + 16 * warp;  // this warp's first position (warp-uniform)
+        if (w0 < p_end) {
+            const unsigned char* kt = Ks + st * TILE;
+            const unsigned char* vt = Vs + st * TILE;
+            // S = Q K^T for the warp's 16 positions: two tiles of 8.
+            float sc[2][4];
+#pragma unroll
+            for (int nt = 0; nt < 2; ++nt) {
+                sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.f;
+                const int r = 16 * warp + nt * 8 + g;
+#pragma unroll
+                for (int kk = 0; kk < KS; ++kk) {
+                    const uint32_t b0 = *reinterpret_cast<const uint32_t*>(kt + r * RB + (((2 * kk) ^ (r & 7)) * 16) + 4 * t);
+                    const uint32_t b1 =
+                        *reinterpret_cast<const uint32_t*>(kt + r * RB + (((2 * kk + 1) ^ (r & 7)) * 16) + 4 * t);
+                    pf_mma(sc[nt], qh[kk][0], qh[kk][1], qh[kk][2], qh[kk][3], b0, b1, BF);
+                    pf_mma(sc[nt], ql[kk][0], ql[kk][1], ql[kk][2], ql[kk][3], b0, b1, BF);
+                }
+            }
+            // Positions past the split; online softmax over heads g (sc[.][0..1]) and g + 8 (sc[.][2..3]).
+            float ta = -INFINITY, tb = -INFINITY;
+#pragma unroll
+            for (int nt = 0; nt < 2; ++nt) {
+                const int s0 = w0 + nt * 8 + 2 * t;
+                if (s0 >= p_end) sc[nt][0] = sc[nt][2] = -INFINITY;
+                if (s0 + 1 >= p_end) sc[nt][1] = sc[nt][3] = -INFINITY;
+                ta = fmaxf(ta, fmaxf(sc[nt][0], sc[nt][1]));
+                tb = fmaxf(tb, fmaxf(sc[nt][2], sc[nt][3]));
+            }
+            ta = fmaxf(ta, __shfl_xor_sync(0xffffffffu, ta, 1));
+            ta = fmaxf(ta, __shfl_xor_sync(0xffffffffu, ta, 2));
+            tb = fmaxf(tb, __shfl_xor_sync(0xffffffffu, tb, 1));
+            tb = fmaxf(tb, __shfl_xor_sync(0xffffffffu, tb, 2));
+            const float na = fmaxf(ma, ta), nb = fmaxf(mb, tb);
+            const float aa = na == -INFINITY ? 1.f : exp2f(ma - na);
+            const float ab = nb == -INFINITY ? 1.f : exp2f(mb - nb);
+            ma = na;
+            mb = nb;
+            float sa = 0.f, sb = 0.f;
+#pragma unroll
+            for (int nt = 0; nt < 2; ++nt) {
+                sc[nt][0] = na == -INFINITY ? 0.f : exp2f(sc[nt][0] - na);
+                sc[nt][1] = na == -INFINITY ? 0.f : exp2f(sc[nt][1] - na);
+                sc[nt][2] = nb == -INFINITY ? 0.f : exp2f(sc[nt][2] - nb);
+                sc[nt][3] = nb == -INFINITY ? 0.f : exp2f(sc[nt][3] - nb);
+                sa += sc[nt][0] + sc[nt][1];
+                sb += sc[nt][2] + sc[nt][3];
+            }
+            la = la * aa + sa;
+            lb = lb * ab + sb;
+#pragma unroll
+            for (int n = 0; n < NT; ++n) {
+                o[n][0] *= aa;
+                o[n][1] *= aa;
+                o[n][2] *= ab;
+                o[n][3] *= ab;
+            }
+            // O += P V over the warp's 16 positions (one 16-deep step).
+            uint32_t ph[4], pl[4];
+            pf_split(sc[0][0], sc[0][1], BF, ph[0], pl[0]);
+            pf_split(sc[0][2], sc[0][3], BF, ph[1], pl[1]);
+            pf_split(sc[1][0], sc[1][1], BF, ph[2], pl[2]);
+            pf_split(sc[1][2], sc[1][3], BF, ph[3], pl[3]);
+#pragma unroll
+            for (int n = 0; n < NT; n += 2) {
+                const int r = 16 * warp + (lane & 7) + ((lane >> 3) & 1) * 8;
+                const int c = n + (lane >> 4);
+                const uint32_t addr = static_cast<uint32_t>(__cvta_generic_to_shared(vt + r * RB + ((c ^ (r & 7)) * 16)));
+                uint32_t v0, v1, v2, v3;
+                asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                             : "=r"(v0), "=r"(v1), "=r"(v2), "=r"(v3)
+                             : "r"(addr));
+                pf_mma(o[n], ph[0], ph[1], ph[2], ph[3], v0, v1, BF);
+                pf_mma(o[n], pl[0], pl[1], pl[2], pl[3], v0, v1, BF);
+                pf_mma(o[n + 1], ph[0], ph[1], ph[2], ph[3], v2, v3, BF);
+                pf_mma(o[n + 1], pl[0], pl[1], pl[2], pl[3], v2, v3, BF);
+            }
+        }
+        __syncthreads();  // stage st is refilled by the next iteration's prefetch
+    }
+    // The four warps' states meet in shared memory: (max, sum) per head, and each warp's output scaled by
+    // its weight 2^(m_w - M) into the free stage buffers (every copy has landed; the loop ended on a
+    // barrier), summed in warp order into qn_s, the CTA's unnormalised output.
+    la += __shfl_xor_sync(0xffffffffu, la, 1);
+    la += __shfl_xor_sync(0xffffffffu, la, 2);
+    lb += __shfl_xor_sync(0xffffffffu, lb, 1);
+    lb += __shfl_xor_sync(0xffffffffu, lb, 2);
+    if (t == 0) {
+        wm_s[warp][g] = ma;
+        wm_s[warp][g + 8] = mb;
+        wl_s[warp][g] = la;
+        wl_s[warp][g + 8] = lb;
+    }
+    __syncthreads();
+    {
+        float Ma = -INFINITY, Mb = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < 4; ++w) Ma = fmaxf(Ma, wm_s[w][g]), Mb = fmaxf(Mb, wm_s[w][g + 8]);
+        const float wa = ma == -INFINITY ? 0.f : exp2f(ma - Ma);
+        const float wb = mb == -INFINITY ? 0.f : exp2f(mb - Mb);
+        if (warp == 0 && t == 0) {
+            float La = 0.f, Lb = 0.f;
+#pragma unroll
+            for (int w = 0; w < 4; ++w) {
+                if (wm_s[w][g] != -INFINITY) La = fmaf(exp2f(wm_s[w][g] - Ma), wl_s[w][g], La);
+                if (wm_s[w][g + 8] != -INFINITY) Lb = fmaf(exp2f(wm_s[w][g + 8] - Mb), wl_s[w][g + 8], Lb);
+            }
+            m_s[g] = Ma;
+            m_s[g + 8] = Mb;
+            l_s[g] = La;
+            l_s[g + 8] = Lb;
+        }
+        float* wo = reinterpret_cast<float*>(dm_smem) + static_cast<size_t>(warp) * kDmHeads * HD;  // [16][HD]
+#pragma unroll
+        for (int n = 0; n < NT; ++n) {
+            const int c = n * 8 + 2 * t;
+            *reinterpret_cast<float2*>(wo + g * HD + c) = make_float2(wa * o[n][0], wa * o[n][1]);
+            *reinterpret_cast<float2*>(wo + (g + 8) * HD + c) = make_float2(wb * o[n][2], wb * o[n][3]);
+        }
+    }
+    __syncthreads();
+    {
+        const float4* w4 = reinterpret_cast<const float4*>(dm_smem);
+        constexpr int Q4 = kDmHeads * HD / 4;  // float4s per warp's output
+        for (int i = tid; i < Q4; i += 128) {
+            const float4 a0 = w4[i], a1 = w4[Q4 + i], a2 = w4[2 * Q4 + i], a3 = w4[3 * Q4 + i];
+            reinterpret_cast<float4*>(&qn_s[0][0])[i] = make_float4(((a0.x + a1.x) + a2.x) + a3.x, ((a0.y + a1.y) + a2.y) + a3.y,
+                                                                     ((a0.z + a1.z) + a2.z) + a3.z, ((a0.w + a1.w) + a2.w) + a3.w);
+        }
+    }
+    __syncthreads();
+    // Merge the cluster's splits: this CTA's slice of head dimensions from the nact active partials.
+    auto peer = [&](float* ptr, int s) { return S > 1 ? cluster.map_shared_rank(ptr, s) : ptr; };
+    if (S > 1) cluster.sync();
+    const int dper = HD / S;
+    for (int o2 = tid; o2 < ng * dper; o2 += 128) {
+        const int j = o2 / dper, d = split * dper + (o2 - (o2 / dper) * dper);
+        float mv[kMaxClusterSplits], lv[kMaxClusterSplits], av[kMaxClusterSplits];
+        float mmax = -INFINITY;
+#pragma unroll
+        for (int s2 = 0; s2 < kMaxClusterSplits; ++s2) {
+            mv[s2] = -INFINITY, lv[s2] = 0.f, av[s2] = 0.f;
+            if (s2 < nact) {
+                mv[s2] = *peer(&m_s[j], s2);
+                lv[s2] = *peer(&l_s[j], s2);
+                av[s2] = *peer(&qn_s[j][d], s2);
+            }
+        }
+#pragma unroll
+        for (int s2 = 0; s2 < kMaxClusterSplits; ++s2) mmax = fmaxf(mmax, mv[s2]);
+        float lsum = 0.f, y = 0.f;
+#pragma unroll
+        for (int s2 = 0; s2 < kMaxClusterSplits; ++s2) {
+            if (s2 < nact && mv[s2] != -INFINITY) {
+                const float w = exp2f(mv[s2] - mmax);
+                lsum = fmaf(w, lv[s2], lsum);
+                y = fmaf(w, av[s2], y);
+            }
+        }
+        p.out[b * p.out_bstride + static_cast<long long>(h0 + j) * HD + d] = y / lsum;
+    }
+    if (S > 1) cluster.sync();
+}
+
 template <int HD, bool BF>
 l0b_status launch_prefill_mma(l0b_device* d, cudaStream_t stream, const AttnParams& p, int rows) {
     constexpr size_t smem = 4ull * kPfBN * HD * 2;
@@ -850,11 +1207,67 @@ l0b_status launch_attn_cluster(l0b_device* d, cudaStream_t stream, F kernel, dim
     return L0B_OK;
 }
 
+// The tensor-core decode kernel: its shared-memory limit set per device, then launched in clusters of S.
+template <int HD, bool BF>
+l0b_status launch_decode_mma(l0b_device* d, cudaStream_t stream, const AttnParams& p, int batch, int S) {
+    constexpr size_t smem = decode_mma_smem<HD>();
+    auto kernel = attn_decode_mma_kernel<HD, BF>;
+    {
+        static bool configured[64] = {};
+        static std::mutex mu;
+        int dev = 0;
+        if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) dev = 0;
+        std::lock_guard<std::mutex> lock(mu);
+        if (!configured[dev]) {
+            cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+            if (e == cudaSuccess) e = cudaFuncSetAttribute(kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+            if (e != cudaSuccess) return fail(L0B_ERR_CUDA, "cudaFuncSetAttribute failed: %s", cudaGetErrorString(e));
+            configured[dev] = true;
+        }
+    }
+    const int gparts = (p.nh / p.nkv + kDmHeads - 1) / kDmHeads;
+    const dim3 grid(p.nkv * gparts, S, batch);
+    if (d) return d->launch_cluster(kernel, grid, dim3(128), smem, S, p);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(128);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    if (S > 1) {
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = 1;
+        attr[0].val.clusterDim.y = S;
+        attr[0].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+    }
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, p);
+    if (e != cudaSuccess) return fail(L0B_ERR_CUDA, "attention launch failed: %s", cudaGetErrorString(e));
+    add_launches(1);
+    return L0B_OK;
+}
+
+// Decode on the tensor-core kernel: f16 / bf16 caches, head dim 64 or 128, 16-byte aligned rows.
+bool decode_mma_applies(const AttnParams& p) {
+    if (!g_attn_decode_mma || (p.cache_dtype != L0B_F16 && p.cache_dtype != L0B_BF16)) return false;
+    if (p.hd != 64 && p.hd != 128) return false;
+    if ((p.kv_dim * 2) % 16 != 0 || (p.cache_bstride * 2) % 16 != 0) return false;
+    return (reinterpret_cast<uintptr_t>(p.kc) | reinterpret_cast<uintptr_t>(p.vc)) % 16 == 0;
+}
+
 l0b_status attention_cluster_any(l0b_device* d, cudaStream_t stream, const AttnParams& p, int batch, int splits) {
     L0B_REQUIRE(p.nkv > 0 && p.nh % p.nkv == 0, L0B_ERR_ARGUMENT, "heads %d not a multiple of kv heads %d", p.nh,
                 p.nkv);
     L0B_REQUIRE(splits == 1 || splits == 2 || splits == 4 || splits == 8 || (splits == 16 && cluster16_ok()),
                 L0B_ERR_ARGUMENT, "cluster splits %d (1, 2, 4, 8, or 16 where the device runs such clusters)", splits);
+    if (decode_mma_applies(p)) {
+        const bool bf = p.cache_dtype == L0B_BF16;
+        if (p.hd == 64) return bf ? launch_decode_mma<64, true>(d, stream, p, batch, splits)
+                                  : launch_decode_mma<64, false>(d, stream, p, batch, splits);
+        return bf ? launch_decode_mma<128, true>(d, stream, p, batch, splits)
+                  : launch_decode_mma<128, false>(d, stream, p, batch, splits);
+    }
     const int G = p.nh / p.nkv;
     const int gparts = (G + kMaxG - 1) / kMaxG;
     dim3 grid(p.nkv * gparts, splits, batch);
@@ -927,6 +1340,11 @@ std::mutex g_noalloc_mutex;
 
 extern "C" L0B_API l0b_status l0b_set_attention_prefill_tensor_cores(int32_t enable) {
     l0b::g_attn_prefill_mma = enable != 0;
+    return L0B_OK;
+}
+
+extern "C" L0B_API l0b_status l0b_set_attention_decode_tensor_cores(int32_t enable) {
+    l0b::g_attn_decode_mma = enable != 0;
     return L0B_OK;
 }
 

@@ -12,6 +12,7 @@
 #include <vector>
 
 #include "common.cuh"
+#include "gemv.cuh"
 #include "runtime.h"
 
 // Peer all-reduce (small collectives of the decode step): every rank owns a mailbox in its HBM, mapped
@@ -21,6 +22,7 @@
 //   epoch [kPeerCtas]                            this rank's own count of all-reduces, per CTA
 constexpr int kMaxRanks = 8;
 constexpr int kPeerCtas = 32;
+constexpr int kPeerChunkBytes = 8192;  // bytes per chunk; chunk j is always handled by CTA j % kPeerCtas
 constexpr size_t kPeerSlotFloats = size_t(1) << 19;  // 2 MB per partial: 64 rows of 8192
 
 struct l0b_comm {
@@ -31,6 +33,7 @@ struct l0b_comm {
     char* mbox = nullptr;                  // own mailbox
     char* peer_mbox[kMaxRanks] = {};       // every rank's mailbox in this process's address space
     bool peer = false;                     // peer all-reduce available
+    l0b::PeerSum* peer_sum = nullptr;      // device copy of the peer-sum mailboxes (GEMV all-reduce epilogue)
 };
 
 namespace l0b {
@@ -51,6 +54,7 @@ struct NcclApi {
 NcclApi g_nccl;
 std::mutex g_nccl_mu;
 bool g_peer_disabled = false;  // l0b_comm_set_peer_allreduce(0): every collective on NCCL
+bool g_peer_sum = true;        // l0b_comm_set_fused_allreduce: row-split GEMVs sum over peers in their epilogue
 
 l0b_status nccl_load() {
     std::lock_guard<std::mutex> lock(g_nccl_mu);
@@ -97,14 +101,17 @@ l0b_status collective_issue(int kind, const CollArgs& a, cudaStream_t stream) {
 }
 
 // ---------------------------------------------------------------------------------------------
-// One-shot all-reduce over peer memory. CTA c of every rank takes slice c of the buffer: it writes the
-// slice into its slot of every rank's mailbox (parity = epoch & 1, so a rank one all-reduce ahead writes
-// the other half while a peer still reads this one), makes the stores visible system-wide, publishes
-// the epoch in each rank's flag for (itself, c), waits -- bounded -- until every rank's flag for c in its
-// own mailbox holds the epoch, and sums the slots in rank order, so every rank gets the same bits. A
-// rank can be at most one all-reduce ahead of any other (finishing one needs every rank's partial of
-// it), which two parities cover. All ranks make the same sequence of calls with the same counts, so
-// their per-CTA epochs agree.
+// One-shot all-reduce over peer memory. The buffer is cut into chunks of kPeerChunkBytes and chunk j
+// always belongs to CTA j % kPeerCtas, whatever the count and type (the grid is min(kPeerCtas, chunks)
+// CTAs). CTA c of every rank writes its chunks into its slot of every rank's mailbox (parity = the CTA's
+// epoch & 1), makes the stores visible system-wide, publishes the epoch in each rank's flag for
+// (itself, c), waits -- bounded -- until every rank's flag for c in its own mailbox holds the epoch, and
+// sums the slots in rank order, so every rank gets the same bits. Every mailbox byte is only ever
+// handled by the same CTA index, whose epoch advances by one per call that reaches it: a rank can start
+// CTA c's next call only after finishing its current one, which needs every rank's partial of it, and a
+// peer publishes that only after its own previous call (stream order), so the two parities cover the
+// rank that is one call ahead. All ranks make the same sequence of calls with the same counts, so their
+// per-CTA epochs agree.
 // ---------------------------------------------------------------------------------------------
 struct PeerArgs {
     void* buf;
@@ -127,8 +134,8 @@ template <typename T, bool MAX>
 __global__ void __launch_bounds__(512) peer_allreduce_kernel(const PeerArgs a) {
     pdl_wait();
     const int c = blockIdx.x, n = a.nranks;
-    const long long per = (a.count + gridDim.x - 1) / gridDim.x;
-    const long long lo = c * per, hi = min(a.count, lo + per);
+    constexpr long long CH = kPeerChunkBytes / sizeof(T);        // elements per chunk
+    const long long stride = static_cast<long long>(gridDim.x) * CH;  // gridDim.x == kPeerCtas past 32 chunks
     char* mine = a.mbox[a.rank];
     const size_t data_bytes = 2ull * kMaxRanks * kPeerSlotFloats * sizeof(float);
     unsigned* epoch_p = reinterpret_cast<unsigned*>(mine + data_bytes + 2ull * kMaxRanks * kPeerCtas * sizeof(unsigned)) + c;
@@ -145,9 +152,12 @@ __global__ void __launch_bounds__(512) peer_allreduce_kernel(const PeerArgs a) {
         return reinterpret_cast<unsigned*>(mb + data_bytes) + (static_cast<size_t>(par) * kMaxRanks + src) * kPeerCtas + c;
     };
     // 1. This rank's slice into its slot of every rank's mailbox.
-    for (int r = 0; r < n; ++r) {
-        T* dst = slot(a.mbox[r], a.rank);
-        for (long long i = lo + threadIdx.x; i < hi; i += blockDim.x) dst[i] = buf[i];
+    for (long long lo = c * CH; lo < a.count; lo += stride) {
+        const long long hi = min(a.count, lo + CH);
+        for (int r = 0; r < n; ++r) {
+            T* dst = slot(a.mbox[r], a.rank);
+            for (long long i = lo + threadIdx.x; i < hi; i += blockDim.x) dst[i] = buf[i];
+        }
     }
     __threadfence_system();
     __syncthreads();
@@ -166,14 +176,17 @@ __global__ void __launch_bounds__(512) peer_allreduce_kernel(const PeerArgs a) {
     __syncthreads();
     // 3. Sum in rank order (identical on every rank). The slots were written by other GPUs: read them at
     // L2 (ld.cg), past any line this SM's L1 kept from the same parity two calls ago.
-    for (long long i = lo + threadIdx.x; i < hi; i += blockDim.x) {
-        T v = __ldcg(slot(mine, 0) + i);
-        for (int r = 1; r < n; ++r) {
-            const T w = __ldcg(slot(mine, r) + i);
-            if constexpr (MAX) v = w > v ? w : v;
-            else v += w;
+    for (long long lo = c * CH; lo < a.count; lo += stride) {
+        const long long hi = min(a.count, lo + CH);
+        for (long long i = lo + threadIdx.x; i < hi; i += blockDim.x) {
+            T v = __ldcg(slot(mine, 0) + i);
+            for (int r = 1; r < n; ++r) {
+                const T w = __ldcg(slot(mine, r) + i);
+                if constexpr (MAX) v = w > v ? w : v;
+                else v += w;
+            }
+            buf[i] = v;
         }
-        buf[i] = v;
     }
     if (threadIdx.x == 0) *epoch_p = ep;
 }
@@ -189,7 +202,8 @@ l0b_status comm_allreduce(l0b_comm* c, void* buf, size_t count, int dtype, int o
         a.nranks = c->nranks;
         a.rank = c->rank;
         a.error = c->dev->error_flag;
-        long long ctas = (static_cast<long long>(count) + 2047) / 2048;
+        const long long ch = kPeerChunkBytes / static_cast<long long>(esize);
+        long long ctas = (static_cast<long long>(count) + ch - 1) / ch;
         if (ctas > kPeerCtas) ctas = kPeerCtas;
         if (ctas < 1) ctas = 1;
         if (dtype == kDtypeU64)
@@ -206,8 +220,12 @@ l0b_status comm_allreduce(l0b_comm* c, void* buf, size_t count, int dtype, int o
 // (the NCCL collectives then serve every call).
 l0b_status peer_setup(l0b_comm* c) {
     if (c->nranks < 2 || c->nranks > kMaxRanks || g_peer_disabled) return L0B_OK;
-    const size_t mbox_bytes = 2ull * kMaxRanks * kPeerSlotFloats * sizeof(float) +
-                              2ull * kMaxRanks * kPeerCtas * sizeof(unsigned) + kPeerCtas * sizeof(unsigned);
+    static_assert(kMaxPeerRanks == kMaxRanks, "one rank limit for both mailboxes");
+    // One allocation: the all-reduce mailbox, then (from psum_off) the GEMV epilogue's peer-sum mailbox.
+    const size_t ar_bytes = 2ull * kMaxRanks * kPeerSlotFloats * sizeof(float) +
+                            2ull * kMaxRanks * kPeerCtas * sizeof(unsigned) + kPeerCtas * sizeof(unsigned);
+    const size_t psum_off = (ar_bytes + 255) & ~static_cast<size_t>(255);
+    const size_t mbox_bytes = psum_off + kPeerSumBytes;
     if (cudaMalloc(&c->mbox, mbox_bytes) != cudaSuccess) {
         cudaGetLastError();
         c->mbox = nullptr;
@@ -258,14 +276,28 @@ l0b_status peer_setup(l0b_comm* c) {
     if (r != ncclSuccess) return fail(L0B_ERR_NCCL, "peer setup agreement failed: %s", g_nccl.error_string(r));
     L0B_CHECK_CUDA(e);
     c->peer = any_bad == 0;
+    if (c->peer) {
+        PeerSum h{};
+        for (int q = 0; q < c->nranks; ++q) h.mbox[q] = c->peer_mbox[q] + psum_off;
+        h.nranks = c->nranks;
+        h.rank = c->rank;
+        h.error = c->dev->error_flag;
+        L0B_CHECK_CUDA(cudaMalloc(&c->peer_sum, sizeof(PeerSum)));
+        L0B_CHECK_CUDA(cudaMemcpyAsync(c->peer_sum, &h, sizeof(h), cudaMemcpyHostToDevice, c->dev->stream));
+        L0B_CHECK_CUDA(cudaStreamSynchronize(c->dev->stream));
+    }
     return L0B_OK;
 }
+
+const PeerSum* comm_peer_sum(const l0b_comm* c) { return c && c->peer && g_peer_sum ? c->peer_sum : nullptr; }
 
 void peer_release(l0b_comm* c) {
     for (int q = 0; q < c->nranks && q < kMaxRanks; ++q)
         if (q != c->rank && c->peer_mbox[q]) cudaIpcCloseMemHandle(c->peer_mbox[q]);
     if (c->mbox) cudaFree(c->mbox);
+    if (c->peer_sum) cudaFree(c->peer_sum);
     c->mbox = nullptr;
+    c->peer_sum = nullptr;
     c->peer = false;
 }
 
@@ -357,6 +389,11 @@ L0B_API l0b_status l0b_comm_free(l0b_comm* c) {
 
 L0B_API l0b_status l0b_comm_set_peer_allreduce(int32_t enable) {
     g_peer_disabled = enable == 0;
+    return L0B_OK;
+}
+
+L0B_API l0b_status l0b_comm_set_fused_allreduce(int32_t enable) {
+    g_peer_sum = enable != 0;
     return L0B_OK;
 }
 

@@ -535,6 +535,27 @@ __device__ __forceinline__ void split_hi_lo(const float (&v)[8], uint4& hi, uint
 }
 
 // Weight pieces: int8 = 64 k (16 bytes per lane, 4 MMAs), 16-bit = 32 k (16 bytes per lane, 2 MMAs).
+// Peer-sum mailbox addressing (layout in gemv.cuh) and the system-scope flag accesses.
+__device__ __forceinline__ float* peer_sum_slot(char* mb, int par, int src) {
+    return reinterpret_cast<float*>(mb) + (static_cast<long long>(par) * kMaxPeerRanks + src) * kPeerSumSlotFloats;
+}
+__device__ __forceinline__ unsigned* peer_sum_flag(char* mb, int par, int src, int cta) {
+    return reinterpret_cast<unsigned*>(mb + kPeerSumDataBytes) +
+           (static_cast<size_t>(par) * kMaxPeerRanks + src) * kPeerSumCtas + cta;
+}
+__device__ __forceinline__ unsigned* peer_sum_counter(char* mb, int i) {  // 0: epoch, 1: CTAs done
+    return reinterpret_cast<unsigned*>(mb + kPeerSumDataBytes + kPeerSumFlagBytes) + 32 * i;
+}
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
+    unsigned v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+constexpr long long kPeerSumWaitCycles = 4000000000LL;  // ~2 s at 1.9 GHz, then the error flag
+
 template <typename WT>
 struct MmaPiece {
     static constexpr int kK = sizeof(WT) == 1 ? 64 : 32;  // k per piece
@@ -681,6 +702,12 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_mma_kernel(const GemvParams 
 
     pdl_wait();
     pdl_launch_dependents();
+    // Peer-sum epilogue: this call's epoch (the previous call's last CTA advanced it before that kernel
+    // ended, and pdl_wait has waited for it) and mailbox parity.
+    const bool psum = p.epi == EPI_PEER_SUM;
+    const unsigned ep =
+        psum ? *reinterpret_cast<const volatile unsigned*>(peer_sum_counter(p.peer->mbox[p.peer->rank], 0)) + 1u : 0u;
+    const int par = static_cast<int>(ep & 1u);
 
     const bool xvec = p.x_dtype == L0B_F32 && (p.x_ld & 3) == 0 && (reinterpret_cast<uintptr_t>(p.x) & 15) == 0;
     const float* xf = static_cast<const float*>(p.x);
@@ -802,7 +829,18 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_mma_kernel(const GemvParams 
             const float y0 = y[ng].x, y1 = y[ng].y;
             const int m = 4 * ng + t;
             const bool live = m < M;
-            if (p.epi == EPI_ARGMAX) {
+            if (psum) {
+                // This rank's partial of rows (r0, r1) into its slot of every rank's mailbox.
+                if (live) {
+                    const PeerSum* ps = p.peer;
+                    const long long i0 = static_cast<long long>(m) * N + r0, i1 = static_cast<long long>(m) * N + r1;
+                    for (int d = 0; d < ps->nranks; ++d) {
+                        float* dst = peer_sum_slot(ps->mbox[d], par, ps->rank);
+                        if (v0) dst[i0] = y0;
+                        if (v1) dst[i1] = y1;
+                    }
+                }
+            } else if (p.epi == EPI_ARGMAX) {
                 unsigned long long key = 0;
                 if (live && v0) key = argmax_key(epilogue_store(p, r0, m, y0, false), r0 + p.argmax_base);
                 if (live && v1) key = max(key, argmax_key(epilogue_store(p, r1, m, y1, false), r1 + p.argmax_base));
@@ -974,6 +1012,51 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_mma_kernel(const GemvParams 
         cluster.sync();
         if (ks == 0 && my_tiles > 0 && warp == reducer(my_tiles - 1)) cluster_epilogue(my_tiles - 1);
         cluster.sync();
+    }
+    if (psum && ks == 0) {
+        // Every partial of this CTA's tiles is out: publish them, wait for the other ranks' partials of
+        // the same tiles (the same CTA index on every rank), then add the slots in rank order.
+        const PeerSum* ps = p.peer;
+        const int nr = ps->nranks, me = ps->rank;
+        char* mine = ps->mbox[me];
+        __threadfence_system();
+        __syncthreads();
+        if (threadIdx.x < nr) st_release_sys(peer_sum_flag(ps->mbox[threadIdx.x], par, me, blockIdx.x), ep);
+        if (threadIdx.x < nr) {
+            const unsigned* f = peer_sum_flag(mine, par, threadIdx.x, blockIdx.x);
+            const long long t0 = clock64();
+            while (ld_acquire_sys(f) != ep) {
+                if (clock64() - t0 > kPeerSumWaitCycles) {
+                    if (ps->error) atomicExch(ps->error, 1);
+                    break;
+                }
+            }
+        }
+        __syncthreads();
+        // Slots written by other GPUs: read at L2 (ld.cg), past any line L1 kept from two calls ago.
+        float* out = static_cast<float*>(p.seg[0].out);
+        const long long ld = p.seg[0].ld;
+        const int per = 16 * M;
+        for (int idx = threadIdx.x; idx < my_tiles * per; idx += kThreads) {
+            const int i = idx / per, rem = idx - (idx / per) * per, m = rem >> 4;
+            const int r = (blockIdx.x + i * gridDim.x) * 16 + (rem & 15);
+            if (r >= N) continue;
+            const long long si = static_cast<long long>(m) * N + r;
+            float v = out[m * ld + r];
+            for (int src = 0; src < nr; ++src) v += __ldcg(peer_sum_slot(mine, par, src) + si);
+            out[m * ld + r] = v;
+        }
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            // The last CTA of the call advances the epoch for the next one.
+            __threadfence();
+            unsigned* done = peer_sum_counter(mine, 1);
+            if (atomicAdd(done, 1u) == gridDim.x - 1) {
+                *done = 0u;
+                __threadfence();
+                *reinterpret_cast<volatile unsigned*>(peer_sum_counter(mine, 0)) = ep;
+            }
+        }
     }
 }
 
@@ -1504,7 +1587,8 @@ l0b_status launch_mma(l0b_device* dev, cudaStream_t stream, int sm_count, const 
     const bool swiglu = p.epi == EPI_SWIGLU;
     const int units = swiglu ? p.N / 2 : p.N;
     const int ntiles = (units + (swiglu ? 7 : 15)) / (swiglu ? 8 : 16);
-    const int cap = sm_count * resident_ctas(reinterpret_cast<const void*>(kernel), smem) / S;
+    int cap = sm_count * resident_ctas(reinterpret_cast<const void*>(kernel), smem) / S;
+    if (p.epi == EPI_PEER_SUM && cap > kPeerSumCtas) cap = kPeerSumCtas;  // one flag per CTA index
     const dim3 grid(ntiles < cap ? ntiles : (cap > 0 ? cap : 1), S);
     if (dev) return dev->launch_cluster(kernel, grid, dim3(kThreads), smem, S, p);
     cudaLaunchConfig_t cfg = {};
@@ -1549,8 +1633,15 @@ l0b_status launch_typed(l0b_device* dev, cudaStream_t stream, int sm_count, Gemv
     const bool vec_ok = (p.K % VEC == 0) && (reinterpret_cast<uintptr_t>(p.w) % 16 == 0) &&
                         (sizeof(WT) != 1 || (p.group % 16 == 0 && p.K % p.group == 0));
     const int M = p.M;
+    const bool psum = p.epi == EPI_PEER_SUM;
     if constexpr (sizeof(WT) == 1) {
-        if (bulk_applies(L0B_I8, p, sm_count)) return launch_bulk(dev, stream, sm_count, p);
+        if (!psum && bulk_applies(L0B_I8, p, sm_count)) return launch_bulk(dev, stream, sm_count, p);
+    }
+    if (psum) {
+        L0B_REQUIRE(p.peer && p.nseg == 1 && p.out_dtype == L0B_F32 && p.seg[0].out, L0B_ERR_ARGUMENT,
+                    "the peer-sum epilogue needs the communicator's mailboxes and one f32 output");
+        L0B_REQUIRE(static_cast<long long>(p.N) * (M < 8 ? M : 8) <= kPeerSumSlotFloats, L0B_ERR_OUT_OF_RANGE,
+                    "peer-sum partials of %d x %d floats exceed the mailbox slot", M < 8 ? M : 8, p.N);
     }
     L0B_REQUIRE(p.kb == 0 || p.kb == kWeightBlock, L0B_ERR_ARGUMENT, "blocked layout with %d k per block", p.kb);
     if (p.kb > 0) {
@@ -1591,6 +1682,7 @@ l0b_status launch_typed(l0b_device* dev, cudaStream_t stream, int sm_count, Gemv
                 continue;
             }
         }
+        L0B_REQUIRE(!psum, L0B_ERR_UNSUPPORTED, "the peer-sum epilogue runs on the tensor-core GEMV only");
         if (!vec_ok) {
             const long long outs = (p.epi == EPI_SWIGLU ? p.N / 2 : p.N) * static_cast<long long>(mr);
             const int grid = static_cast<int>((outs + kWarps - 1) / kWarps);
@@ -1686,6 +1778,19 @@ __global__ void __launch_bounds__(256) gemm_f32_kernel(int M, int N, int K, cons
 }
 
 }  // namespace
+
+bool gemv_peer_sum_applies(int w_dtype, const GemvParams& p) {
+    if (!p.peer || p.nseg != 1 || p.out_dtype != L0B_F32 || !p.seg[0].out || p.M < 1) return false;
+    if (static_cast<long long>(p.N) * (p.M < 8 ? p.M : 8) > kPeerSumSlotFloats) return false;
+    GemvParams t8 = p;
+    t8.M = p.M < 8 ? p.M : 8;
+    switch (w_dtype) {
+        case L0B_I8: return mma_applies<int8_t>(t8, t8.M) > 0;
+        case L0B_F16: return mma_applies<__half>(t8, t8.M) > 0;
+        case L0B_BF16: return mma_applies<__nv_bfloat16>(t8, t8.M) > 0;
+        default: return false;
+    }
+}
 
 void gemv_set_tensor_cores(bool on) { g_gemv_mma = on; }
 void gemv_set_bulk(bool on) { g_gemv_bulk = on; }

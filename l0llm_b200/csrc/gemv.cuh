@@ -10,7 +10,34 @@ enum GemvEpi : int {
     EPI_STORE = 0,   // out[m, n - seg_begin] = y (+ bias)
     EPI_ACCUM = 1,   // out[m, n] += y               (residual add, f32 out)
     EPI_SWIGLU = 2,  // W = [gate; up] stacked: out[m, i] = silu(y[i]) * y[i + N/2]
-    EPI_ARGMAX = 3   // store logits (optional) and fold argmax into a 64-bit key per row
+    EPI_ARGMAX = 3,  // store logits (optional) and fold argmax into a 64-bit key per row
+    EPI_PEER_SUM = 4  // out[m, n] += sum over the TP ranks, in rank order, of their y[m, n] (PeerSum below)
+};
+
+// All-reduce epilogue of a row-split projection under tensor parallelism (EPI_PEER_SUM, the tensor-core
+// GEMV only). Each rank owns a peer-sum mailbox in its HBM, mapped into every rank by CUDA IPC:
+//   data  [2 parities][kMaxPeerRanks][kPeerSumSlotFloats]  the ranks' partial outputs, [m][n]
+//   flags [2 parities][kMaxPeerRanks][kPeerSumCtas]        epoch a rank's CTA has published here
+// followed in the own mailbox by two counters: the epoch (fused calls completed) and the CTAs done in
+// the current call. All ranks launch the same grid, so CTA c handles the same tiles everywhere: it
+// stores its tiles' partials into its rank's slot of every mailbox, publishes the call's epoch in every
+// mailbox's flag for (rank, c), waits (bounded) for every rank's flag for c in its own mailbox and adds
+// the slots to `out` in rank order -- identical bits on every rank. The parity is the call's epoch & 1
+// (one epoch per call, for every CTA: the last CTA to finish advances it), so a rank one call ahead
+// writes the other half while a peer still reads this one; two calls ahead is impossible because
+// finishing a call needs every rank's flag of it, which each rank publishes only after its previous
+// call has completed (stream order).
+constexpr int kMaxPeerRanks = 8;
+constexpr int kPeerSumCtas = 1024;
+constexpr long long kPeerSumSlotFloats = 1LL << 17;  // 8 rows of 16384
+constexpr size_t kPeerSumDataBytes = 2ull * kMaxPeerRanks * kPeerSumSlotFloats * sizeof(float);
+constexpr size_t kPeerSumFlagBytes = 2ull * kMaxPeerRanks * kPeerSumCtas * sizeof(unsigned);
+constexpr size_t kPeerSumBytes = kPeerSumDataBytes + kPeerSumFlagBytes + 256;  // + epoch, done
+
+struct PeerSum {
+    char* mbox[kMaxPeerRanks];  // every rank's peer-sum mailbox in this process's address space
+    int nranks, rank;
+    int* error;  // device error flag, set when a wait gives up
 };
 
 struct GemvSeg {
@@ -54,6 +81,7 @@ struct GemvParams {
     int counter_count;
     int kb;      // > 0: int8 W in the blocked layout with this k per block (N % 16 == 0, K % kb == 0)
     int ugroup;  // bulk GEMV: k blocks per unit (set by the dispatcher)
+    const PeerSum* peer;  // EPI_PEER_SUM: the communicator's mailboxes (device memory)
 };
 
 // Launches y = x * W^T with the fused options in `p` (fills kt and the grid). `w_dtype` is
@@ -71,6 +99,13 @@ void gemv_set_fill_split(int s);
 // tiles in the blocked layout (default on).
 bool weight_blocking();
 void set_weight_blocking(bool on);
+
+// Whether gemv_nk_launch can run `p` (M rows) with the EPI_PEER_SUM epilogue: 16-bit or per-row int8
+// weights on the tensor-core GEMV, one f32 output segment, M x N within a mailbox slot.
+bool gemv_peer_sum_applies(int w_dtype, const GemvParams& p);
+// The communicator's peer-sum mailboxes (device memory), or null: no peer path, or fused all-reduces
+// switched off (l0b_comm_set_fused_allreduce).
+const PeerSum* comm_peer_sum(const l0b_comm* c);
 
 // Raw-stream variant (no device handle): immediate launch on `stream`.
 l0b_status gemv_nk_launch_stream(cudaStream_t stream, int sm_count, int w_dtype, GemvParams p);

@@ -421,10 +421,23 @@ l0b_status emit(l0b_model* m, int li, const char* stage, const float* dptr, long
     return L0B_OK;
 }
 
-// A row-split projection under TP, folded into the residual stream with one in-place all-reduce:
-// rank 0 accumulates its partial product into `hidden`, the other ranks store theirs there, so the
-// sum over ranks is hidden + sum of the partials on every rank (no separate add kernel).
+// A row-split projection under TP, folded into the residual stream. Where the tensor-core GEMV takes
+// it (decode rows) and the communicator has peer mailboxes, one kernel does both: each CTA sends its
+// tiles' partials to every rank and adds every rank's partials of the same tiles to `hidden` in rank
+// order. Otherwise one in-place all-reduce after the GEMV: rank 0 accumulates its partial into
+// `hidden`, the other ranks store theirs there, so the sum over ranks is hidden + the partials on every
+// rank. Both give ((hidden + p0) + p1) + ... in fp32, the same bits.
 l0b_status project_into_residual(l0b_model* m, const ModelMatrix& w, GemvParams p, int rows) {
+    if (const PeerSum* ps = comm_peer_sum(m->comm)) {
+        GemvParams q = p;
+        q.epi = EPI_PEER_SUM;
+        q.out_dtype = L0B_F32;
+        q.seg[0] = {m->hidden, nullptr, m->h, m->h};
+        q.peer = ps;
+        GemvParams t = q;
+        t.epi = EPI_ACCUM;  // the rows the tcgen05 GEMM would take stay on the GEMM + all-reduce path
+        if (!tc_takes(m, w, t) && gemv_peer_sum_applies(w.dtype, q)) return gemv_nk_launch(m->dev, w.dtype, q);
+    }
     p.epi = m->tp_rank == 0 ? EPI_ACCUM : EPI_STORE;
     p.out_dtype = L0B_F32;
     p.seg[0] = {m->hidden, nullptr, m->h, m->h};

@@ -177,6 +177,10 @@ def load_library() -> C.CDLL:
         "l0b_linear_tc_scaled": (i32, [vp, vp, i32, i32, i32, vp, vp, vp, i32, vp, f32, i32, vp, vp]),
         "l0b_tc_set_max_splits": (i32, [i32]),
         "l0b_set_gemv_bulk": (i32, [i32]),
+        "l0b_set_gemv_fill_split": (i32, [i32]),
+        "l0b_set_attention_cluster16": (i32, [i32]),
+        "l0b_set_attention_decode_tensor_cores": (i32, [i32]),
+        "l0b_comm_set_fused_allreduce": (i32, [i32]),
         "l0b_sample_execute": (i32, [vp, vp, vp, i32, vp, i32, f32, f32, i32, f32, C.c_double, vp]),
         "l0b_model_sample_logits": (i32, [vp, f32, f32, i32, f32, C.c_uint64, vp, i32, C.POINTER(i32)]),
         "l0b_model_decode_sample_device": (i32, [vp, i32, f32, f32, i32, f32, C.c_uint64, vp]),
@@ -675,6 +679,20 @@ class Communicator:
     def set_peer_allreduce(enabled: bool):
         """Process-wide: communicators made afterwards use the peer all-reduce (True, default) or NCCL only."""
         check(load_library().l0b_comm_set_peer_allreduce(1 if enabled else 0))
+
+    _fused = True
+
+    @staticmethod
+    def set_fused_allreduce(enabled: bool):
+        """Process-wide: steps recorded afterwards fold the row-split decode all-reduces into their GEMVs
+        (True, default, with peer memory) or run GEMV + all-reduce pairs."""
+        check(load_library().l0b_comm_set_fused_allreduce(1 if enabled else 0))
+        Communicator._fused = bool(enabled)
+
+    @staticmethod
+    def fused_allreduce() -> bool:
+        """The setting of set_fused_allreduce (as made through this module)."""
+        return Communicator._fused
 
     def Dispose(self):
         if self.handle:

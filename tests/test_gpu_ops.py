@@ -328,26 +328,43 @@ def cluster_cap(request, lz):
     lib.l0b_set_attention_cluster16(1)
 
 
+@pytest.fixture(params=["mma", "fma"])
+def decode_kernel(request, lz):
+    """Decode attention over 16-bit caches on the tensor cores (mma) or the fp32-FMA kernel."""
+    lib = lz.load_library()
+    lib.l0b_set_attention_decode_tensor_cores(1 if request.param == "mma" else 0)
+    yield request.param
+    lib.l0b_set_attention_decode_tensor_cores(1)
+
+
+def _bf16_bits(x):
+    import torch
+
+    return torch.from_numpy(np.ascontiguousarray(x)).to(torch.bfloat16).view(torch.int16).numpy().view(np.uint16)
+
+
 @pytest.mark.parametrize("hd,nh,nkv", ATTN_SHAPES)
 @pytest.mark.parametrize("seq", [1, 2, 31, 33, 64, 65, 513, 4096])
-@pytest.mark.parametrize("cache", ["f16", "f32"])
-def test_attention_decode(lz, orc, device, suite, cluster_cap, hd, nh, nkv, seq, cache):
-    if cache == "f32" and seq > 600:
-        pytest.skip("long sequences run with the f16 cache")
+@pytest.mark.parametrize("cache", ["f16", "bf16", "f32"])
+def test_attention_decode(lz, orc, device, suite, cluster_cap, decode_kernel, hd, nh, nkv, seq, cache):
+    if cache == "f32" and (seq > 600 or decode_kernel == "mma"):
+        pytest.skip("long sequences run with 16-bit caches; fp32 caches always take the FMA kernel")
     rng = RNG(seq + hd + nh)
     max_seq = max(seq, 64)
     kv_dim = nkv * hd
     kc = rng.standard_normal((max_seq, kv_dim)).astype(np.float32)
     vc = rng.standard_normal((max_seq, kv_dim)).astype(np.float32)
     q = rng.standard_normal(nh * hd).astype(np.float32)
-    code = lz.F16 if cache == "f16" else lz.F32
-    kstore = kc.astype(np.float16) if cache == "f16" else kc
-    vstore = vc.astype(np.float16) if cache == "f16" else vc
-    ocode = orc.F16 if cache == "f16" else orc.F32
-    kview = kstore.view(np.uint16) if cache == "f16" else kstore
-    vview = vstore.view(np.uint16) if cache == "f16" else vstore
+    if cache == "f16":
+        code, ocode = lz.F16, orc.F16
+        kview, vview = kc.astype(np.float16).view(np.uint16), vc.astype(np.float16).view(np.uint16)
+    elif cache == "bf16":
+        code, ocode = lz.BF16, orc.BF16
+        kview, vview = _bf16_bits(kc), _bf16_bits(vc)
+    else:
+        code, ocode, kview, vview = lz.F32, orc.F32, kc, vc
     want = orc.attention(q[None], kview, vview, ocode, hd, nh, nkv, seq - 1, 1)[0]
-    with buf(lz, device, q) as qb, buf(lz, device, kstore, code) as kb, buf(lz, device, vstore, code) as vb, \
+    with buf(lz, device, q) as qb, buf(lz, device, kview, code) as kb, buf(lz, device, vview, code) as vb, \
             lz.SharedBuffer(device, lz.F32, nh * hd) as ob:
         suite.Attention.Execute(device, qb, kb, vb, ob, hd, nh, nkv, seq, max_seq)
         close(ob.ToArray(), want, atol=1e-4, rtol=1e-3)

@@ -1,9 +1,10 @@
-"""Tensor parallelism over 2 GPUs (NCCL) against the same model on one GPU.
+"""Tensor parallelism over 2 GPUs against the same model on one GPU.
 
 Two ranks, one process each, build the model with tp_size = 2: q/k/v, gate/up and lm_head column-split,
 o_proj/down row-split with their partial sums all-reduced before the residual add, attention head-split,
-the vocab-sharded argmax keys max-reduced. Rank 0 compares the prefill logits and the device greedy
-tokens with a tp_size = 1 model of the same synthetic weights on its own GPU.
+the vocab-sharded argmax keys max-reduced. The all-reduces run folded into the row-split GEMVs (fused),
+as a separate kernel over peer memory, or on NCCL. Rank 0 compares the prefill logits and the device
+greedy tokens with a tp_size = 1 model of the same synthetic weights on its own GPU.
 """
 from __future__ import annotations
 
@@ -20,11 +21,11 @@ CFG = dict(hidden_size=512, intermediate_size=1024, num_layers=2, num_attention_
 STEPS = 6
 
 
-def _rank(rank, world, idq, precision, q, peer=True):
+def _rank(rank, world, idq, precision, q, mode="fused"):
     try:
         from l0llm_b200 import levelzero as lz
 
-        lz.Communicator.set_peer_allreduce(peer)
+        lz.Communicator.set_peer_allreduce(mode != "nccl")
 
         # Rank 0 makes the id, so every rank bootstraps with the same NCCL build.
         if rank == 0:
@@ -47,12 +48,18 @@ def _rank(rank, world, idq, precision, q, peer=True):
             note("communicator ready")
             out["peer"] = comm.UsesPeerAllReduce
             cfg = lz.model_config(kv_dtype=lz.F16, tp_size=world, tp_rank=rank, **CFG)
-            with lz.LlmModel(dev, suite, cfg, 64, precision, comm=comm) as m:
-                m.init_synthetic(4, 0.05, 1e-3, 2e-2)
-                out["logits"] = m.Prefill(prompt)
-                note("prefill done")
-                out["tokens"] = m.decode_greedy_device(STEPS)
-                note("decode done")
+            # "fused": the all-reduce inside the row-split GEMVs, then the same model with the separate
+            # GEMV + all-reduce pair, whose bits it must reproduce.
+            for key, fused in ([("", True), ("pair_", False)] if mode == "fused" else [("", False)]):
+                lz.Communicator.set_fused_allreduce(fused)
+                with lz.LlmModel(dev, suite, cfg, 64, precision, comm=comm) as m:
+                    m.init_synthetic(4, 0.05, 1e-3, 2e-2)
+                    out[key + "logits"] = m.Prefill(prompt)
+                    note("prefill done")
+                    out[key + "tokens"] = m.decode_greedy_device(STEPS)
+                    out[key + "decode_logits"] = m.Decode(int(out[key + "tokens"][-1]))
+                    note("decode done")
+            lz.Communicator.set_fused_allreduce(True)
         if rank == 0:
             cfg1 = lz.model_config(kv_dtype=lz.F16, **CFG)
             with lz.LlmModel(dev, suite, cfg1, 64, precision) as m1:
@@ -66,16 +73,16 @@ def _rank(rank, world, idq, precision, q, peer=True):
         q.put((rank, None, repr(e)))
 
 
-@pytest.mark.parametrize("peer", [True, False], ids=["peer-allreduce", "nccl"])
+@pytest.mark.parametrize("mode", ["fused", "peer-allreduce", "nccl"])
 @pytest.mark.parametrize("precision", ["bfloat16", "int8"])
-def test_tensor_parallel_two_gpus_match_single(lz, device, precision, peer):
+def test_tensor_parallel_two_gpus_match_single(lz, device, precision, mode):
     import torch
 
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     ctx = mp.get_context("spawn")
     q, idq = ctx.Queue(), ctx.Queue()
-    procs = [ctx.Process(target=_rank, args=(r, 2, idq, precision, q, peer)) for r in range(2)]
+    procs = [ctx.Process(target=_rank, args=(r, 2, idq, precision, q, mode)) for r in range(2)]
     for p in procs:
         p.start()
     results = {}
@@ -90,10 +97,15 @@ def test_tensor_parallel_two_gpus_match_single(lz, device, precision, peer):
             if p.is_alive():
                 p.kill()
     r0, r1 = results[0], results[1]
-    assert r0["peer"] == r1["peer"] == peer
+    assert r0["peer"] == r1["peer"] == (mode != "nccl")
     # Both ranks see the gathered full-vocabulary logits and the same greedy tokens.
     np.testing.assert_array_equal(r0["logits"], r1["logits"])
     np.testing.assert_array_equal(r0["tokens"], r1["tokens"])
+    np.testing.assert_array_equal(r0["decode_logits"], r1["decode_logits"])
+    if mode == "fused":
+        # The all-reduce folded into the GEMV gives the separate pair's bits.
+        np.testing.assert_array_equal(r0["tokens"], r0["pair_tokens"])
+        np.testing.assert_array_equal(r0["decode_logits"], r0["pair_decode_logits"])
     want = r0["ref_logits"]
     err = np.abs(r0["logits"] - want).max()
     assert err <= 2e-3 * np.abs(want).max(), f"max err {err}"
