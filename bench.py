@@ -565,12 +565,16 @@ def measure_cfg4_tp(lz, dev, suite, stream_ptr, torch, dist, world: int, rank: i
     if comm is not None:
         # The step's collective on its own: 2 x layers all-reduces of one hidden row per token, timed
         # back to back with CUDA events on the model stream (max over ranks), for the all-reduce share.
+        # They are queued behind a ~50 ms device sleep so the events time the GPU, not the host's
+        # per-call launch cost.
         n_ar = 2 * CFG4["num_layers"]
         with lz.SharedBuffer(dev, lz.F32, CFG4["hidden_size"]) as hb:
             for _ in range(20):
                 comm.AllReduce(hb)
             barrier()
             a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            with torch.cuda.stream(stream):
+                torch.cuda._sleep(100_000_000)
             a0.record(stream)
             for _ in range(n_ar):
                 comm.AllReduce(hb)
@@ -646,6 +650,12 @@ def run_profile_case(case: str) -> int:
     the tensor-core GEMM, 3 rotating weight copies (408 MB > L2), 6 warm-up launches then 30 timed.
     attention-512: Attention.Execute at the config-2 head shape (hd 128, 28 query / 4 KV heads, f32
     caches of 4096 rows, 512 live positions), 5 warm-up launches then 50 timed.
+    gemm-gateup-512: the gate/up projection of gemm-gateup-16 at 512 activation rows (a prefill chunk).
+    attention-tp8: decode attention at one config-4 TP8 rank's heads (8 query / 1 KV head, hd 128, bf16
+    caches, 2112 positions): the tensor-core kernel in 16-CTA clusters, 5 warm-up launches then 50 timed.
+    decode-bs1-1layer: config 2 cut to one layer, one decode step inside the NVTX range "step".
+    decode-cfg4-tp8-shard: one config-4 TP8 rank's shard shapes as a single-GPU model (no all-reduces),
+    20 timed device-resident greedy steps after a 2048-token prompt, then one step inside "step".
     """
     import ctypes as C
 
@@ -697,8 +707,9 @@ def run_profile_case(case: str) -> int:
             dev.Synchronize()
             torch.cuda.nvtx.range_pop()
         print(json.dumps({"profile_case": case, "ok": True}))
-    elif case == "gemm-gateup-16":
-        H, I, M, copies = CFG2["hidden_size"], CFG2["intermediate_size"], BS16, 3
+    elif case in ("gemm-gateup-16", "gemm-gateup-512"):
+        H, I, copies = CFG2["hidden_size"], CFG2["intermediate_size"], 3
+        M = BS16 if case == "gemm-gateup-16" else 512
         N = 2 * I
         qs = [lz.SharedBuffer.from_array(dev, rng.integers(-127, 128, (N, H), dtype=np.int8)) for _ in range(copies)]
         ss = [lz.SharedBuffer.from_array(dev, rng.uniform(1e-3, 2e-2, N).astype(np.float16)) for _ in range(copies)]
@@ -725,6 +736,44 @@ def run_profile_case(case: str) -> int:
                           "weight_gbs": round(N * H / us / 1e3, 1)}))
         for b in qs + ss + [x, out]:
             b.Dispose()
+    elif case == "attention-tp8":
+        # Decode attention at one config-4 TP8 rank's shape: 8 query heads on 1 KV head, bf16 caches,
+        # position 2111 (the 2048-token prompt plus decode steps), tensor-core kernel in 16-CTA clusters.
+        hd, nh, nkv, seq = 128, 8, 1, 2112
+        bits = lambda a: torch.from_numpy(a).to(torch.bfloat16).view(torch.int16).numpy().view(np.uint16)
+        q = lz.SharedBuffer.from_array(dev, rng.standard_normal(nh * hd).astype(np.float32))
+        kc = lz.SharedBuffer.from_array(dev, bits(rng.standard_normal(seq * nkv * hd).astype(np.float32)), lz.BF16)
+        vc = lz.SharedBuffer.from_array(dev, bits(rng.standard_normal(seq * nkv * hd).astype(np.float32)), lz.BF16)
+        out = lz.SharedBuffer(dev, lz.F32, nh * hd)
+        for _ in range(5):
+            suite.Attention.Execute(dev, q, kc, vc, out, hd, nh, nkv, seq, seq)
+        stream = torch.cuda.ExternalStream(sp.value)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        dev.Synchronize()
+        with torch.cuda.stream(stream):
+            torch.cuda._sleep(50_000_000)  # the launches queue behind it: the events time the GPU
+        e0.record(stream)
+        for _ in range(50):
+            suite.Attention.Execute(dev, q, kc, vc, out, hd, nh, nkv, seq, seq)
+        e1.record(stream)
+        e1.synchronize()
+        print(json.dumps({"profile_case": case, "us_per_call": round(e0.elapsed_time(e1) / 50 * 1e3, 2)}))
+        for b in (q, kc, vc, out):
+            b.Dispose()
+    elif case == "decode-bs1-1layer":
+        # Config 2 cut to one decoder layer (same shapes and int8 layout, ~3 GB on the device): a small
+        # case for full captures of the per-layer kernels; one step inside the NVTX range "step".
+        mc = lz.model_config(kv_dtype=lz.F16, **dict(CFG2, num_layers=1))
+        with lz.LlmModel(dev, suite, mc, CONTEXT + 64, "int8") as model:
+            model.init_synthetic(SEED, 0.02, 1e-3, 2e-2)
+            model.Prefill(rng.integers(0, CFG2["vocab_size"], CONTEXT).astype(np.int32))
+            model.decode_greedy_device(3)
+            dev.Synchronize()
+            torch.cuda.nvtx.range_push("step")
+            model.decode_greedy_device(1)
+            dev.Synchronize()
+            torch.cuda.nvtx.range_pop()
+        print(json.dumps({"profile_case": case, "ok": True}))
     elif case == "attention-512":
         hd, nh, nkv, seq, max_seq = 128, 28, 4, 512, 4096
         q = lz.SharedBuffer.from_array(dev, rng.standard_normal(nh * hd).astype(np.float32))
@@ -772,7 +821,8 @@ def main() -> int:
                     help="row-split GEMV + separate all-reduce kernel instead of the all-reduce folded into the GEMV")
     ap.add_argument("--no-tp", action="store_true", help="skip the config 4 tensor-parallel leg (tp)")
     ap.add_argument("--profile-case", choices=["decode-bs1", "decode-bs16", "gemm-gateup-16", "attention-512",
-                                               "decode-cfg4-tp8-shard"],
+                                               "decode-cfg4-tp8-shard", "gemm-gateup-512", "attention-tp8",
+                                               "decode-bs1-1layer"],
                     help="run one small case for an ncu capture instead of the benchmark")
     args = ap.parse_args()
     if args.no_bulk_gemv:

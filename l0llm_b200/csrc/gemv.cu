@@ -535,6 +535,15 @@ __device__ __forceinline__ void split_hi_lo(const float (&v)[8], uint4& hi, uint
 }
 
 // Weight pieces: int8 = 64 k (16 bytes per lane, 4 MMAs), 16-bit = 32 k (16 bytes per lane, 2 MMAs).
+// D += A B on the integer tensor cores: A 16 x 32 s8 (rows g, g + 8; k 4 t .. 4 t + 3 in a0 / a1 and
+// 16 + 4 t .. in a2 / a3), B 32 x 8 s8 (column g; k 4 t .. in b0, 16 + 4 t .. in b1), s32 accumulators.
+__device__ __forceinline__ void mma_s8_16832(int (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                             uint32_t b0, uint32_t b1) {
+    asm volatile("mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+                 : "+r"(c[0]), "+r"(c[1]), "+r"(c[2]), "+r"(c[3])
+                 : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
 // Peer-sum mailbox addressing (layout in gemv.cuh) and the system-scope flag accesses.
 __device__ __forceinline__ float* peer_sum_slot(char* mb, int par, int src) {
     return reinterpret_cast<float*>(mb) + (static_cast<long long>(par) * kMaxPeerRanks + src) * kPeerSumSlotFloats;
@@ -1082,19 +1091,20 @@ l0b_status launch_on(l0b_device* dev, cudaStream_t stream, F kernel, dim3 g, dim
 // mbarrier) of 16 K bytes (57 KB at K = 3584). Large contiguous copies are what the copy engine streams
 // fastest: a read-only probe of 8-64 KB copies measured 7.1-7.3 TB/s on B200, while copies of 512-byte
 // row segments (one per row) and 3-D tensor-map boxes of 128-byte lines were bound by the engine's cost
-// per operation and per line (0.5 and 2 TB/s). A producer warp keeps 2-3 tiles in flight per SM
-// (issued before the dependency wait: weights never depend on the previous kernel); eight consumer
-// warps stage the hi/lo activations once (as the register-streamed kernel) and split each tile's pieces
-// between them with the same k permutation, int8 conversion and mma.sync. The warps' partial sums meet
-// in double-buffered shared memory; a reducer warp rotating by tile runs the epilogue while the others
-// go on with the next tile. Each CTA (one per SM) takes a contiguous range of whole tiles, so the kernel
-// serves projections with many tiles per SM (gate/up, LM head); the others stay on the register GEMV.
+// per operation and per line (0.5 and 2 TB/s). A producer warp keeps 2-4 stages in flight per SM
+// (issued before the dependency wait: weights never depend on the previous kernel). The weights go to
+// the integer tensor cores as they are (mma.sync m16n8k32 s8, no conversion): the activation row enters
+// as four balanced base-128 int8 digits of x 2^e (|x 2^e| < 2^26, about 27 bits of the row's largest
+// value), four B columns of one MMA, so the s32 sums are exact (|sum| < 2^31 for K < 2^18) and the
+// digit columns join in int64 and f64 before one rounding. Sixteen consumer warps split each unit's
+// pieces; their partial sums meet (exact integers: any order gives the same bits) in double-buffered
+// shared memory, and a reducer warp rotating by tile runs the epilogue while the others go on.
 // ---------------------------------------------------------------------------------------------
 constexpr int kBulkCW = 16;                      // consumer warps
 constexpr int kBulkConsumers = kBulkCW * 32;
 constexpr int kBulkThreads = kBulkConsumers + 32;  // consumers + 1 producer warp
 constexpr int kBulkMaxStages = 8;
-constexpr int kBulkSmemBudget = 212 * 1024;  // dynamic; the static arrays take ~8 KB of the 227 KB
+constexpr int kBulkSmemBudget = 206 * 1024;  // dynamic; the static arrays take ~17 KB of the 227 KB
 constexpr long long kBulkWaitCycles = 4000000000LL;
 
 __device__ __forceinline__ uint32_t bulk_smem_u32(const void* p) {
@@ -1152,10 +1162,10 @@ inline int bulk_stages(int K, int UK) {
 template <bool BLK>
 __global__ void __launch_bounds__(kBulkThreads, 1) gemv_bulk_kernel(const GemvParams p, int stages, int* error) {
     extern __shared__ char bulk_smem[];
-    constexpr int PE = 64, KU = 2, C2 = 2;  // int8: 64 k per piece, two 32-k units; B columns hi, lo
-    __shared__ float2 red[2][kBulkCW][32];
+    constexpr int PE = 64;  // k per piece: lane t holds bytes [16 t, 16 t + 16) of rows g and g + 8
+    __shared__ int4 red[2][kBulkCW][32];
     __shared__ float ssq_s[kBulkCW], amax_s[kBulkCW];
-    __shared__ float oscale_s;
+    __shared__ double oscale_s;
     // After one timed-out wait the rest of the launch only drains: abort_s is set and units from
     // issued_s on (never copied, or stuck) are not waited for, so the kernel returns after one timeout.
     __shared__ int abort_s, issued_s;
@@ -1243,40 +1253,36 @@ __global__ void __launch_bounds__(kBulkThreads, 1) gemv_bulk_kernel(const GemvPa
     // Consumers.
     pdl_wait();
     pdl_launch_dependents();
-    // Stage x as hi / lo pairs in the piece order of the register-streamed kernel (32-k unit u, lane t).
+    // Stage x as int8 digits: item (piece pc, lane t) is x[64 pc + 16 t, + 16) -- the k of the 16 weight
+    // bytes lane t loads from each row -- and its slot (pc * 16 + t * 4 + dg) * 16 holds digit dg of those
+    // 16 values (byte i <-> k 64 pc + 16 t + i). Pass 1 keeps the raw values (times the RMS-norm weight)
+    // in the item's 64 bytes and forms the row's sum of squares and largest magnitude; pass 2 applies
+    // 1/RMS and 2^e (largest |x| 2^e just below 2^26) and writes the four balanced base-128 digits.
     {
-        const int items = npieces * KU * 4;
+        const int items = npieces * 4;
         const float* xf = static_cast<const float*>(p.x);
         const bool xvec = p.x_dtype == L0B_F32 && (reinterpret_cast<uintptr_t>(p.x) & 15) == 0;
-        auto item_slot = [&](int it, int& k) {
-            const int u = it >> 2, tt = it & 3;
-            k = (u >> 1) * 64 + 16 * tt + 8 * (u & 1);
-            return xs + static_cast<size_t>(u) * C2 * 64 + tt * 16;  // lo slot is +64
-        };
         float ss = 0.f, amax = 0.f;
         for (int it = threadIdx.x; it < items; it += kBulkConsumers) {
-            int k;
-            char* slot = item_slot(it, k);
-            float v[8];
-            if (xvec) {
-                const float4 a = *reinterpret_cast<const float4*>(xf + k);
-                const float4 c = *reinterpret_cast<const float4*>(xf + k + 4);
-                v[0] = a.x, v[1] = a.y, v[2] = a.z, v[3] = a.w, v[4] = c.x, v[5] = c.y, v[6] = c.z, v[7] = c.w;
-            } else {
+            const int k0 = it * 16;  // (pc, t) = (it / 4, it % 4): 64 pc + 16 t
+            float4* slot = reinterpret_cast<float4*>(xs + static_cast<size_t>(it) * 64);
 #pragma unroll
-                for (int e = 0; e < 8; ++e) v[e] = load_as_float(p.x, p.x_dtype, k + e);
-            }
-            if (p.norm_w) {
-#pragma unroll
-                for (int e = 0; e < 8; ++e) {
-                    ss = fmaf(v[e], v[e], ss);
-                    v[e] *= p.norm_w[k + e];
+            for (int q = 0; q < 4; ++q) {
+                float4 a;
+                if (xvec) {
+                    a = *reinterpret_cast<const float4*>(xf + k0 + 4 * q);
+                } else {
+                    a = make_float4(load_as_float(p.x, p.x_dtype, k0 + 4 * q), load_as_float(p.x, p.x_dtype, k0 + 4 * q + 1),
+                                    load_as_float(p.x, p.x_dtype, k0 + 4 * q + 2), load_as_float(p.x, p.x_dtype, k0 + 4 * q + 3));
                 }
+                if (p.norm_w) {
+                    ss = fmaf(a.x, a.x, fmaf(a.y, a.y, fmaf(a.z, a.z, fmaf(a.w, a.w, ss))));
+                    const float4 w = *reinterpret_cast<const float4*>(p.norm_w + k0 + 4 * q);
+                    a.x *= w.x, a.y *= w.y, a.z *= w.z, a.w *= w.w;
+                }
+                amax = fmaxf(amax, fmaxf(fmaxf(fabsf(a.x), fabsf(a.y)), fmaxf(fabsf(a.z), fabsf(a.w))));
+                slot[q] = a;
             }
-#pragma unroll
-            for (int e = 0; e < 8; ++e) amax = fmaxf(amax, fabsf(v[e]));
-            *reinterpret_cast<float4*>(slot) = make_float4(v[0], v[1], v[2], v[3]);
-            *reinterpret_cast<float4*>(slot + 64) = make_float4(v[4], v[5], v[6], v[7]);
         }
         ss = warp_sum(ss);
         amax = warp_max(amax);
@@ -1295,27 +1301,38 @@ __global__ void __launch_bounds__(kBulkThreads, 1) gemv_bulk_kernel(const GemvPa
         int e = 0;
         if (am * rs > 0.f && isfinite(am * rs)) {
             int ex;
-            frexpf(am * rs, &ex);
-            e = min(max(14 - ex, -100), 100);
+            frexpf(am * rs, &ex);  // am rs = f 2^ex, f in [0.5, 1): am rs 2^(26 - ex) < 2^26
+            e = min(max(26 - ex, -120), 120);
         }
-        const float in_scale = rs * ldexpf(1.0f, e);
-        if (threadIdx.x == 0) oscale_s = ldexpf(1.0f, -e);
+        const float sc = rs * ldexpf(1.0f, e);
+        if (threadIdx.x == 0) oscale_s = ldexp(1.0, -e);
         for (int it = threadIdx.x; it < items; it += kBulkConsumers) {
-            int k;
-            char* slot = item_slot(it, k);
-            const float4 a = *reinterpret_cast<const float4*>(slot);
-            const float4 c = *reinterpret_cast<const float4*>(slot + 64);
-            float v[8] = {a.x * in_scale, a.y * in_scale, a.z * in_scale, a.w * in_scale,
-                          c.x * in_scale, c.y * in_scale, c.z * in_scale, c.w * in_scale};
-            uint4 hi, lo;
-            split_hi_lo<false>(v, hi, lo);
-            *reinterpret_cast<uint4*>(slot) = hi;
-            *reinterpret_cast<uint4*>(slot + 64) = lo;
+            float4* slot = reinterpret_cast<float4*>(xs + static_cast<size_t>(it) * 64);
+            uint32_t dw[4][4] = {};
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const float4 a = slot[q];
+                const float v[4] = {a.x * sc, a.y * sc, a.z * sc, a.w * sc};
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    int X = __float2int_rn(v[i]);
+#pragma unroll
+                    for (int dg = 0; dg < 3; ++dg) {
+                        const int d = ((X + 64) & 127) - 64;
+                        dw[dg][q] |= (static_cast<uint32_t>(d) & 0xFFu) << (8 * i);
+                        X = (X - d) >> 7;
+                    }
+                    dw[3][q] |= (static_cast<uint32_t>(X) & 0xFFu) << (8 * i);
+                }
+            }
+            uint4* out = reinterpret_cast<uint4*>(slot);
+#pragma unroll
+            for (int dg = 0; dg < 4; ++dg) out[dg] = make_uint4(dw[dg][0], dw[dg][1], dw[dg][2], dw[dg][3]);
         }
         bulk_consumer_sync();
     }
 
-    // Epilogue of tile `tile` from the (row g, row g + 8) sums; the lanes with t == 0 hold the real ones.
+    // Epilogue of tile `tile` from the (row g, row g + 8) outputs; the lanes with t == 0 hold the real ones.
     // Rows (g, g + 8) of a tile and their scales; the reducer loads the scales when the tile starts so
     // the epilogue does not wait for them.
     auto tile_rows2 = [&](int tile, int& r0, int& r1, bool& v0, bool& v1) {
@@ -1346,12 +1363,14 @@ __global__ void __launch_bounds__(kBulkThreads, 1) gemv_bulk_kernel(const GemvPa
             }
         }
     };
-    // A tile two CTAs share: publish this CTA's part; the second to arrive adds the other's and finishes.
-    auto fixup = [&](int tile, int slot, float y0, float y1) {
-        float* mine = p.part + (static_cast<long long>(tile) * 2 + slot) * 16;
+    // A tile two CTAs share: publish this CTA's part (the exact x 2^e-scaled sums as doubles, 32 floats
+    // per part); the second to arrive adds the other's (exact: both are integers times the same 2^-e,
+    // below 2^53) and finishes.
+    auto fixup = [&](int tile, int slot, double d0, double d1, float s0, float s1) {
+        double* mine = reinterpret_cast<double*>(p.part) + (static_cast<long long>(tile) * 2 + slot) * 16;
         if (t == 0) {
-            mine[g] = y0;
-            mine[g + 8] = y1;
+            mine[g] = d0;
+            mine[g + 8] = d1;
         }
         __threadfence();
         __syncwarp();
@@ -1360,18 +1379,19 @@ __global__ void __launch_bounds__(kBulkThreads, 1) gemv_bulk_kernel(const GemvPa
         old = __shfl_sync(0xffffffffu, old, 0);
         if (old == 0) return;
         __threadfence();
-        const float* other = p.part + (static_cast<long long>(tile) * 2 + (slot ^ 1)) * 16;
+        const double* other = reinterpret_cast<const double*>(p.part) + (static_cast<long long>(tile) * 2 + (slot ^ 1)) * 16;
         if (t == 0) {
-            y0 += __ldcg(other + g);
-            y1 += __ldcg(other + g + 8);
+            d0 += __ldcg(other + g);
+            d1 += __ldcg(other + g + 8);
         }
         if (lane == 0) p.counters[tile] = 0u;
-        epilogue(tile, y0, y1);
+        epilogue(tile, static_cast<float>(d0 * s0), static_cast<float>(d1 * s1));
     };
 
-    const int col_off = g * 64 + t * 16;
+    // Digit dg of x for this lane's 16 k of a piece: columns g < 4 of the B fragment, zero above.
+    const char* xcol = g < 4 ? xs + t * 64 + g * 16 : nullptr;
     float sc0 = 0.f, sc1 = 0.f;  // the row scales of the tile this warp reduces next
-    float acc[4] = {0.f, 0.f, 0.f, 0.f}, acc2[4] = {0.f, 0.f, 0.f, 0.f};
+    int acc[4] = {0, 0, 0, 0}, acc2[4] = {0, 0, 0, 0};
     int seg_first = 0;  // first unit of the current tile in this CTA's range
     int j = 0;          // tiles finished by this CTA (reducer rotation, red[] buffer parity)
     for (int u = u_begin, i = 0; u < u_end; ++u, ++i) {
@@ -1386,7 +1406,7 @@ __global__ void __launch_bounds__(kBulkThreads, 1) gemv_bulk_kernel(const GemvPa
         if (first) {
             seg_first = uj;
 #pragma unroll
-            for (int e = 0; e < 4; ++e) acc[e] = acc2[e] = 0.f;
+            for (int e = 0; e < 4; ++e) acc[e] = acc2[e] = 0;
             if (reducer) {
                 int r0, r1;
                 bool v0, v1;
@@ -1414,42 +1434,36 @@ __global__ void __launch_bounds__(kBulkThreads, 1) gemv_bulk_kernel(const GemvPa
                                        : static_cast<size_t>(piece) * PE;
             const uint4 w0 = *reinterpret_cast<const uint4*>(wg0 + off);
             const uint4 w1 = *reinterpret_cast<const uint4*>(wg1 + off);
-            const char* ub = xs + static_cast<size_t>((xpiece0 + piece) * KU) * C2 * 64 + col_off;
-            uint32_t b[8];
-#pragma unroll
-            for (int jj = 0; jj < KU; ++jj) {
-                uint4 q = make_uint4(0, 0, 0, 0);
-                if (g < C2) q = *reinterpret_cast<const uint4*>(ub + static_cast<size_t>(jj) * C2 * 64);
-                b[4 * jj] = q.x, b[4 * jj + 1] = q.y, b[4 * jj + 2] = q.z, b[4 * jj + 3] = q.w;
-            }
-#pragma unroll
-            for (int jj = 0; jj < 4; ++jj) {
-                uint32_t a0, a1, a2, a3;
-                i8x4_to_h2x2(u4_get(w0, jj), a0, a2);
-                i8x4_to_h2x2(u4_get(w1, jj), a1, a3);
-                // Two accumulators: independent MMA chains.
-                mma_16816((jj & 1) ? acc2 : acc, a0, a1, a2, a3, b[2 * jj], b[2 * jj + 1], false);
-            }
+            const uint4 b = xcol ? *reinterpret_cast<const uint4*>(xcol + static_cast<size_t>(xpiece0 + piece) * 256)
+                                 : make_uint4(0, 0, 0, 0);
+            // k [16 t, 16 t + 8) and [16 t + 8, 16 t + 16) of the piece; two accumulators: independent chains.
+            mma_s8_16832(acc, w0.x, w1.x, w0.y, w1.y, b.x, b.y);
+            mma_s8_16832(acc2, w0.z, w1.z, w0.w, w1.w, b.z, b.w);
         }
         __syncwarp();
         if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bulk_smem_u32(&empty[s])) : "memory");
         if (!last) continue;
-        red[j & 1][warp][lane] = make_float2(acc[0] + acc[1] + acc2[0] + acc2[1], acc[2] + acc[3] + acc2[2] + acc2[3]);
+        red[j & 1][warp][lane] = make_int4(acc[0] + acc2[0], acc[1] + acc2[1], acc[2] + acc2[2], acc[3] + acc2[3]);
         bulk_consumer_sync();
-        // Tile j's partials are complete; its reducer sums them while the other warps go on (the next
-        // write to red[j & 1] comes after the next barrier, which the reducer reaches only when done).
+        // Tile j's partials are complete; its reducer sums them (exactly, in int32) while the other warps go
+        // on (the next write to red[j & 1] comes after the next barrier, which the reducer reaches only
+        // when done), then joins the four digit columns: lane t holds columns 2t, 2t + 1 of rows g, g + 8.
         if (reducer) {
-            float y0 = 0.f, y1 = 0.f;
+            int c[4] = {0, 0, 0, 0};
 #pragma unroll
             for (int w = 0; w < kBulkCW; ++w) {
-                y0 += red[j & 1][w][lane].x;
-                y1 += red[j & 1][w][lane].y;
+                const int4 q = red[j & 1][w][lane];
+                c[0] += q.x, c[1] += q.y, c[2] += q.z, c[3] += q.w;
             }
-            y0 *= oscale_s * sc0;
-            y1 *= oscale_s * sc1;
-            if constexpr (!blocked) epilogue(tile, y0, y1);
-            else if (seg_first == 0 && uj == ug - 1) epilogue(tile, y0, y1);
-            else fixup(tile, seg_first == 0 ? 0 : 1, y0, y1);
+            const long long lo0 = c[0] + 128LL * c[1], lo1 = c[2] + 128LL * c[3];  // t = 0: digits 0, 1; t = 1: 2, 3
+            const long long hi0 = __shfl_down_sync(0xffffffffu, lo0, 1);
+            const long long hi1 = __shfl_down_sync(0xffffffffu, lo1, 1);
+            const double d0 = static_cast<double>(lo0 + 16384LL * hi0) * oscale_s;
+            const double d1 = static_cast<double>(lo1 + 16384LL * hi1) * oscale_s;
+            if constexpr (!blocked) epilogue(tile, static_cast<float>(d0 * sc0), static_cast<float>(d1 * sc1));
+            else if (seg_first == 0 && uj == ug - 1)
+                epilogue(tile, static_cast<float>(d0 * sc0), static_cast<float>(d1 * sc1));
+            else fixup(tile, seg_first == 0 ? 0 : 1, d0, d1, sc0, sc1);
         }
         ++j;
     }

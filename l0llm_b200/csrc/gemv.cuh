@@ -74,8 +74,9 @@ struct GemvParams {
     int argmax_base;             // index of W's row 0 in the argmax (vocab shard offset under TP)
     int kt;                      // K elements per shared-memory tile (a multiple of 512)
     int prefetch;                // prefetch the first row block of weights into L2 before pdl_wait
-    // Split-K scratch of the one-row bulk GEMV over blocked weights (null: no split): part >= 32 floats
-    // per 16-row tile, counters >= one per tile, zero at rest (every launch leaves them zero).
+    // Split-K scratch of the one-row bulk GEMV over blocked weights (null: no split): part >= 64 floats
+    // (two parts of 16 doubles) per 16-row tile, counters >= one per tile, zero at rest (every launch
+    // leaves them zero).
     float* part;
     unsigned* counters;
     int counter_count;

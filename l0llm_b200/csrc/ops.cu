@@ -96,7 +96,7 @@ L0B_API l0b_status l0b_suite_create(l0b_device* dev, l0b_suite** out) {
     L0B_CHECK_CUDA(cudaSetDevice(dev->index));
     L0B_CHECK_CUDA(cudaMalloc(&s->error_flag, sizeof(int)));
     L0B_CHECK_CUDA(cudaMemsetAsync(s->error_flag, 0, sizeof(int), dev->stream));
-    L0B_CHECK_CUDA(cudaMalloc(&s->split_part, sizeof(float) * 32 * kSuiteSplitTiles));
+    L0B_CHECK_CUDA(cudaMalloc(&s->split_part, sizeof(float) * 64 * kSuiteSplitTiles));
     L0B_CHECK_CUDA(cudaMalloc(&s->split_counters, sizeof(unsigned) * kSuiteSplitTiles));
     L0B_CHECK_CUDA(cudaMemsetAsync(s->split_counters, 0, sizeof(unsigned) * kSuiteSplitTiles, dev->stream));
     L0B_CHECK_CUDA(cudaStreamSynchronize(dev->stream));
