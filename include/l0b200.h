@@ -477,6 +477,10 @@ L0B_API l0b_status l0b_set_gemv_bulk(int32_t enable);
  * fill SMs that its 16-row tiles would leave idle (fewer tiles than SMs, slices of at least 2048 k);
  * 1 disables it. Affects launches made after the call. No counterpart in the reference. */
 L0B_API l0b_status l0b_set_gemv_fill_split(int32_t max_splits);
+/* Tuning: blocked int8 projections with short rows (fewer than 16 blocks of 512 k: q/k/v and o_proj of
+ * a 3584-wide model) on the bulk-copy GEMV as well (1) or on the register-streamed one (0, default).
+ * Affects launches made after the call. No counterpart in the reference. */
+L0B_API l0b_status l0b_set_gemv_bulk_short_rows(int32_t enable);
 /* Layout of the int8 weights of models created after the call: with blocking on (1, default), int8
  * projections with one scale per row, K % 512 == 0, N % 16 == 0 and fewer than 8 tiles of 16 rows per
  * SM (q/k/v, o_proj, down at Qwen2.5-7B widths) are stored as [N/16][K/512][16][512] bytes, so the k

@@ -1072,6 +1072,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_mma_kernel(const GemvParams 
 bool g_gemv_mma = true;
 bool g_gemv_bulk = true;  // the bulk-copy one-row kernel where it applies (l0b_set_gemv_bulk)
 int g_gemv_fill_split = 2;  // largest split-K taken only to fill idle SMs (l0b_set_gemv_fill_split)
+bool g_gemv_bulk_short = false;  // blocked projections with short rows on the bulk GEMV too
 
 template <typename F, typename... A>
 l0b_status launch_on(l0b_device* dev, cudaStream_t stream, F kernel, dim3 g, dim3 b, size_t smem, A... args) {
@@ -1480,9 +1481,9 @@ int bulk_group(const GemvParams& p, int sm_count) {
     if (p.epi == EPI_SWIGLU || p.N % 16 != 0 || p.K % p.kb != 0 || p.kb != kWeightBlock) return 0;
     if (!p.part || !p.counters || p.counter_count < ntiles) return 0;
     const int nb = p.K / p.kb;
-    // Short rows (q/k/v and o_proj at K = 3584: 7 blocks) stream faster on the register GEMV, whose
-    // consumers need no stage round trip; long ones (down at K = 18944: 37 blocks) on the bulk GEMV.
-    if (nb < 16) return 0;
+    // Short rows (q/k/v and o_proj at K = 3584: 7 blocks) stay on the register GEMV unless
+    // l0b_set_gemv_bulk_short_rows(1); long ones (down at K = 18944: 37 blocks) take the bulk GEMV.
+    if (nb < 16 && !g_gemv_bulk_short) return 0;
     for (int G = 4; G >= 1; --G) {
         const int ug = (nb + G - 1) / G;
         const long long units = static_cast<long long>(ntiles) * ug;
@@ -1808,6 +1809,7 @@ bool gemv_peer_sum_applies(int w_dtype, const GemvParams& p) {
 
 void gemv_set_tensor_cores(bool on) { g_gemv_mma = on; }
 void gemv_set_bulk(bool on) { g_gemv_bulk = on; }
+void gemv_set_bulk_short_rows(bool on) { g_gemv_bulk_short = on; }
 void gemv_set_fill_split(int s) { g_gemv_fill_split = s <= 1 ? 1 : (s >= 8 ? 8 : (s >= 4 ? 4 : 2)); }
 
 namespace {

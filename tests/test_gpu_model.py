@@ -261,9 +261,19 @@ def test_config1_qwen05b_fp16_greedy_64_steps(lz, orc, device, suite):
             break
 
 
-def test_config2_qwen7b_int8_shape_two_layers(lz, orc, device, suite):
+@pytest.mark.parametrize("short_rows", ["register", "bulk"])
+def test_config2_qwen7b_int8_shape_two_layers(lz, orc, device, suite, short_rows):
     """Config 2 widths (hidden 3584, 28/4 heads, inter 18944, vocab 152064), int8 per-channel weights with
-    fp16 scales U[1e-3, 2e-2], fp16 KV; two layers so the oracle finishes in seconds."""
+    fp16 scales U[1e-3, 2e-2], fp16 KV; two layers so the oracle finishes in seconds. The decode steps run
+    q/k/v and o_proj (blocked, 7 blocks per row) on the register GEMV or on the bulk GEMV."""
+    lz.load_library().l0b_set_gemv_bulk_short_rows(1 if short_rows == "bulk" else 0)
+    try:
+        _config2_two_layers(lz, orc, device, suite)
+    finally:
+        lz.load_library().l0b_set_gemv_bulk_short_rows(0)
+
+
+def _config2_two_layers(lz, orc, device, suite):
     cfgd = dict(hidden_size=3584, intermediate_size=18944, num_layers=2, num_attention_heads=28,
                 num_key_value_heads=4, head_dim=128, vocab_size=152064, max_position_embeddings=32768,
                 rms_norm_eps=1e-6, rope_theta=1e6, attention_bias=1, q8_group=0)
