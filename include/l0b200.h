@@ -481,6 +481,11 @@ L0B_API l0b_status l0b_set_gemv_fill_split(int32_t max_splits);
  * a 3584-wide model) on the bulk-copy GEMV as well (1) or on the register-streamed one (0, default).
  * Affects launches made after the call. No counterpart in the reference. */
 L0B_API l0b_status l0b_set_gemv_bulk_short_rows(int32_t enable);
+/* Tuning: one-row blocked int8 projections of a model (q/k/v, o_proj, down) on the k-split GEMV (1,
+ * default: each CTA multiplies one 512-k block of a group of row tiles on the integer tensor cores and
+ * adds exact int64 row sums; the last CTA of a group runs the epilogue) or on the bulk / register GEMVs
+ * (0). Affects launches made after the call. No counterpart in the reference. */
+L0B_API l0b_status l0b_set_gemv_ksplit(int32_t enable);
 /* Layout of the int8 weights of models created after the call: with blocking on (1, default), int8
  * projections with one scale per row, K % 512 == 0, N % 16 == 0 and fewer than 8 tiles of 16 rows per
  * SM (q/k/v, o_proj, down at Qwen2.5-7B widths) are stored as [N/16][K/512][16][512] bytes, so the k

@@ -1073,6 +1073,7 @@ bool g_gemv_mma = true;
 bool g_gemv_bulk = true;  // the bulk-copy one-row kernel where it applies (l0b_set_gemv_bulk)
 int g_gemv_fill_split = 2;  // largest split-K taken only to fill idle SMs (l0b_set_gemv_fill_split)
 bool g_gemv_bulk_short = false;  // blocked projections with short rows on the bulk GEMV too
+bool g_gemv_ksplit = true;  // blocked one-row int8 projections on the k-split GEMV (l0b_set_gemv_ksplit)
 
 template <typename F, typename... A>
 l0b_status launch_on(l0b_device* dev, cudaStream_t stream, F kernel, dim3 g, dim3 b, size_t smem, A... args) {
@@ -1470,6 +1471,209 @@ __global__ void __launch_bounds__(kBulkThreads, 1) gemv_bulk_kernel(const GemvPa
     }
 }
 
+// ---------------------------------------------------------------------------------------------
+// K-split one-row GEMV over blocked int8 weights (q/k/v, o_proj, down at batch 1).
+//
+// CTA (k block kb, tile group tg) multiplies the 512 k of block kb of every 16-row tile of its group:
+// the (tile, kb) blocks are 8 KB contiguous each in the blocked layout, four per stage by bulk copy.
+// The activation row is read once for the RMS norm and its largest value (every CTA forms the same
+// e), but only the CTA's own 512 values become int8 digits, so no CTA stages the whole row. The weights
+// feed mma.sync m16n8k32 s8 as loaded (as in gemv_bulk_kernel); warp w takes pieces 2 (w % 4), +1 of
+// block w / 4 of each stage, joins its digit columns to one exact int64 per row and adds it to the
+// row's int64 sum with one atomic: integer addition is exact, so the result does not depend on the
+// order the CTAs arrive in. The last CTA of a group to finish (a counter per group) turns the group's
+// sums into outputs -- times 2^-e and the row scale in f64, one rounding -- runs the store / bias /
+// residual epilogue, and leaves the sums and the counter zero for the next launch.
+// ---------------------------------------------------------------------------------------------
+constexpr int kKsCW = 16;
+constexpr int kKsThreads = kKsCW * 32 + 32;  // consumers + 1 producer warp
+constexpr int kKsMaxStages = 6;
+constexpr int kKsBlockBytes = 16 * kWeightBlock;  // one (tile, k block) block
+constexpr int kKsStageBytes = 4 * kKsBlockBytes;
+
+__global__ void __launch_bounds__(kKsThreads, 1) gemv_ksplit_kernel(const GemvParams p, int stages, int groups,
+                                                                  int* error) {
+    extern __shared__ char ks_smem[];
+    constexpr int PE = 64;
+    __shared__ float ssq_s[kKsCW], amax_s[kKsCW];
+    __shared__ double oscale_s;
+    // After a timed-out wait the rest of the launch only drains: units from issued_s on were never
+    // copied and are not waited for; earlier ones still are (their copies land in this CTA's memory).
+    __shared__ int abort_s, issued_s, last_s;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+    const int N = p.N, K = p.K, nb = K / kWeightBlock;
+    const int ntiles = N >> 4;
+    const int kbi = blockIdx.x % nb, tg = blockIdx.x / nb;
+    const int t_begin = static_cast<int>(static_cast<long long>(ntiles) * tg / groups);
+    const int t_end = static_cast<int>(static_cast<long long>(ntiles) * (tg + 1) / groups);
+    const int nunits = (t_end - t_begin + 3) / 4;  // stages of up to four tiles
+    char* const base = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(ks_smem) + 1023) & ~uintptr_t(1023));
+    char* xs = base;            // 512 k as digits: item (piece, t) at (piece * 4 + t) * 64, digit dg at + dg * 16
+    char* ring = base + 2048;
+    uint64_t* full = reinterpret_cast<uint64_t*>(ring + static_cast<size_t>(stages) * kKsStageBytes);
+    uint64_t* empty = full + kKsMaxStages;
+    const char* W = static_cast<const char*>(p.w);
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < stages; ++s) {
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(bulk_smem_u32(&full[s])) : "memory");
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bulk_smem_u32(&empty[s])), "r"(kKsCW)
+                         : "memory");
+        }
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        abort_s = 0;
+        issued_s = INT_MAX;
+    }
+    __syncthreads();
+
+    if (warp == kKsCW) {
+        // Producer: the blocks of four tiles per stage (weights never depend on the previous kernel).
+        if (lane == 0) {
+            for (int u = 0; u < nunits; ++u) {
+                const int s = u % stages;
+                if (u >= stages && !bulk_wait(&empty[s], ((u / stages) & 1) ^ 1)) {
+                    if (error) atomicExch(error, 1);
+                    atomicMin(&issued_s, u);
+                    __threadfence_block();
+                    atomicExch(&abort_s, 1);
+                    break;
+                }
+                const int t0 = t_begin + 4 * u, nblk = min(4, t_end - t0);
+                asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bulk_smem_u32(&full[s])),
+                             "r"(nblk * kKsBlockBytes)
+                             : "memory");
+                for (int b = 0; b < nblk; ++b)
+                    bulk_copy(ring + static_cast<size_t>(s) * kKsStageBytes + b * kKsBlockBytes,
+                              W + (static_cast<long long>(t0 + b) * nb + kbi) * kKsBlockBytes, kKsBlockBytes, &full[s]);
+            }
+        }
+        return;
+    }
+
+    pdl_wait();
+    pdl_launch_dependents();
+    // The row's sum of squares and largest magnitude (after the RMS-norm weight), over all of K.
+    {
+        const float* xf = static_cast<const float*>(p.x);
+        float ss = 0.f, am = 0.f;
+        for (int k = 4 * threadIdx.x; k < K; k += 4 * kKsCW * 32) {
+            float4 a = *reinterpret_cast<const float4*>(xf + k);
+            if (p.norm_w) {
+                ss = fmaf(a.x, a.x, fmaf(a.y, a.y, fmaf(a.z, a.z, fmaf(a.w, a.w, ss))));
+                const float4 w = *reinterpret_cast<const float4*>(p.norm_w + k);
+                a.x *= w.x, a.y *= w.y, a.z *= w.z, a.w *= w.w;
+            }
+            am = fmaxf(am, fmaxf(fmaxf(fabsf(a.x), fabsf(a.y)), fmaxf(fabsf(a.z), fabsf(a.w))));
+        }
+        ss = warp_sum(ss);
+        am = warp_max(am);
+        if (lane == 0) {
+            ssq_s[warp] = ss;
+            amax_s[warp] = am;
+        }
+        bulk_consumer_sync();
+        float sst = 0.f, amt = 0.f;
+#pragma unroll
+        for (int w = 0; w < kKsCW; ++w) {
+            sst += ssq_s[w];
+            amt = fmaxf(amt, amax_s[w]);
+        }
+        const float rs = p.norm_w ? 1.0f / sqrtf(sst / static_cast<float>(K) + p.eps) : 1.0f;
+        int e = 0;
+        if (amt * rs > 0.f && isfinite(amt * rs)) {
+            int ex;
+            frexpf(amt * rs, &ex);
+            e = min(max(26 - ex, -120), 120);
+        }
+        const float sc = rs * ldexpf(1.0f, e);
+        if (threadIdx.x == 0) oscale_s = ldexp(1.0, -e);
+        // Digits of this CTA's 512 k: item i = (piece i / 4, lane i % 4) holds x[kb 512 + 16 i, + 16).
+        if (threadIdx.x < 32) {
+            const int k0 = kbi * kWeightBlock + 16 * threadIdx.x;
+            uint32_t dw[4][4] = {};
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                float4 a = *reinterpret_cast<const float4*>(xf + k0 + 4 * q);
+                if (p.norm_w) {
+                    const float4 w = *reinterpret_cast<const float4*>(p.norm_w + k0 + 4 * q);
+                    a.x *= w.x, a.y *= w.y, a.z *= w.z, a.w *= w.w;
+                }
+                const float v[4] = {a.x * sc, a.y * sc, a.z * sc, a.w * sc};
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    int X = __float2int_rn(v[i]);
+#pragma unroll
+                    for (int dg = 0; dg < 3; ++dg) {
+                        const int d = ((X + 64) & 127) - 64;
+                        dw[dg][q] |= (static_cast<uint32_t>(d) & 0xFFu) << (8 * i);
+                        X = (X - d) >> 7;
+                    }
+                    dw[3][q] |= (static_cast<uint32_t>(X) & 0xFFu) << (8 * i);
+                }
+            }
+            uint4* out = reinterpret_cast<uint4*>(xs + threadIdx.x * 64);
+#pragma unroll
+            for (int dg = 0; dg < 4; ++dg) out[dg] = make_uint4(dw[dg][0], dw[dg][1], dw[dg][2], dw[dg][3]);
+        }
+        bulk_consumer_sync();
+    }
+    // This warp's block of each stage and its two pieces; their B fragments serve every tile.
+    const int blk = warp >> 2, pc0 = (warp & 3) * 2;
+    uint4 bx0 = make_uint4(0, 0, 0, 0), bx1 = make_uint4(0, 0, 0, 0);
+    if (g < 4) {
+        bx0 = *reinterpret_cast<const uint4*>(xs + (pc0 * 4 + t) * 64 + g * 16);
+        bx1 = *reinterpret_cast<const uint4*>(xs + ((pc0 + 1) * 4 + t) * 64 + g * 16);
+    }
+    unsigned long long* acc = reinterpret_cast<unsigned long long*>(p.acc);
+    for (int u = 0; u < nunits; ++u) {
+        const int s = u % stages;
+        const bool skip = *reinterpret_cast<volatile int*>(&abort_s) && u >= *reinterpret_cast<volatile int*>(&issued_s);
+        if (!skip && !bulk_wait(&full[s], (u / stages) & 1) && lane == 0) {
+            if (error) atomicExch(error, 1);
+            atomicMin(&issued_s, u);
+            __threadfence_block();
+            atomicExch(&abort_s, 1);
+        }
+        const int tile = t_begin + 4 * u + blk;
+        if (tile < t_end) {
+            const char* blkp = ring + static_cast<size_t>(s) * kKsStageBytes + blk * kKsBlockBytes + t * 16;
+            const uint4 a0 = *reinterpret_cast<const uint4*>(blkp + g * kWeightBlock + pc0 * PE);
+            const uint4 a1 = *reinterpret_cast<const uint4*>(blkp + (g + 8) * kWeightBlock + pc0 * PE);
+            const uint4 c0 = *reinterpret_cast<const uint4*>(blkp + g * kWeightBlock + (pc0 + 1) * PE);
+            const uint4 c1 = *reinterpret_cast<const uint4*>(blkp + (g + 8) * kWeightBlock + (pc0 + 1) * PE);
+            int accA[4] = {0, 0, 0, 0}, accB[4] = {0, 0, 0, 0};
+            mma_s8_16832(accA, a0.x, a1.x, a0.y, a1.y, bx0.x, bx0.y);
+            mma_s8_16832(accB, a0.z, a1.z, a0.w, a1.w, bx0.z, bx0.w);
+            mma_s8_16832(accA, c0.x, c1.x, c0.y, c1.y, bx1.x, bx1.y);
+            mma_s8_16832(accB, c0.z, c1.z, c0.w, c1.w, bx1.z, bx1.w);
+            const long long lo0 = (accA[0] + accB[0]) + 128LL * (accA[1] + accB[1]);
+            const long long lo1 = (accA[2] + accB[2]) + 128LL * (accA[3] + accB[3]);
+            const long long hi0 = __shfl_down_sync(0xffffffffu, lo0, 1);
+            const long long hi1 = __shfl_down_sync(0xffffffffu, lo1, 1);
+            if (t == 0) {
+                atomicAdd(acc + tile * 16 + g, static_cast<unsigned long long>(lo0 + 16384LL * hi0));
+                atomicAdd(acc + tile * 16 + g + 8, static_cast<unsigned long long>(lo1 + 16384LL * hi1));
+            }
+        }
+        __syncwarp();
+        if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bulk_smem_u32(&empty[s])) : "memory");
+    }
+    // The last CTA of the group to get here finishes the group's rows.
+    __threadfence();
+    bulk_consumer_sync();
+    if (threadIdx.x == 0) last_s = atomicAdd(p.counters + tg, 1u) == static_cast<unsigned>(nb - 1);
+    bulk_consumer_sync();
+    if (!last_s) return;
+    __threadfence();
+    const __half* sc = static_cast<const __half*>(p.scales);
+    for (int r = t_begin * 16 + threadIdx.x; r < t_end * 16; r += kKsCW * 32) {
+        const long long D = static_cast<long long>(atomicExch(acc + r, 0ull));
+        const float y = static_cast<float>(static_cast<double>(D) * oscale_s * static_cast<double>(__half2float(sc[r])));
+        epilogue_store(p, r, 0, y);
+    }
+    if (threadIdx.x == 0) p.counters[tg] = 0u;
+}
+
 // Unit size of the one-row bulk GEMV, in k blocks (0 = the kernel does not apply): row-major weights
 // take whole 16-row tiles when there are at least 8 tiles per SM (returns 1); blocked weights take the
 // largest group of G <= 4 blocks that still gives every SM >= 6 units (smaller units balance the SMs,
@@ -1521,6 +1725,42 @@ l0b_status launch_bulk(l0b_device* dev, cudaStream_t stream, int sm_count, GemvP
     if (p.kb > 0)
         return launch_on(dev, stream, gemv_bulk_kernel<true>, dim3(sm_count), dim3(kBulkThreads), smem, p, stages, err);
     return launch_on(dev, stream, gemv_bulk_kernel<false>, dim3(sm_count), dim3(kBulkThreads), smem, p, stages, err);
+}
+
+// Tile groups of the k-split GEMV (0 = it does not apply): blocked int8 with one scale per row, one
+// activation row, a store / residual epilogue, f32 x and norm weight 16-byte aligned, at most one CTA per
+// SM: groups = SMs / k blocks (every CTA one k block of one group).
+int ksplit_groups(const GemvParams& p, int sm_count) {
+    if (!g_gemv_ksplit || !g_gemv_mma || p.kb != kWeightBlock || p.M != 1 || !p.acc || p.acc_count < p.N) return 0;
+    if (p.epi != EPI_STORE && p.epi != EPI_ACCUM) return 0;
+    if (p.group < p.K || p.N % 16 != 0 || p.K % kWeightBlock != 0 || p.x_dtype != L0B_F32) return 0;
+    if ((reinterpret_cast<uintptr_t>(p.x) | reinterpret_cast<uintptr_t>(p.w)) & 15) return 0;
+    if (p.norm_w && (reinterpret_cast<uintptr_t>(p.norm_w) & 15)) return 0;
+    const int nb = p.K / kWeightBlock;
+    if (nb > sm_count) return 0;
+    int groups = sm_count / nb;
+    if (groups > p.N / 16) groups = p.N / 16;
+    if (!p.counters || groups > p.counter_count) return 0;
+    return groups;
+}
+
+l0b_status launch_ksplit(l0b_device* dev, cudaStream_t stream, int sm_count, const GemvParams& p, int groups) {
+    (void)sm_count;
+    static bool configured = false;
+    if (!configured) {
+        cudaError_t e = cudaFuncSetAttribute(gemv_ksplit_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             kBulkSmemBudget);
+        if (e != cudaSuccess) return fail(L0B_ERR_CUDA, "cudaFuncSetAttribute failed: %s", cudaGetErrorString(e));
+        configured = true;
+    }
+    const int nb = p.K / kWeightBlock;
+    int stages = kKsMaxStages;
+    while (stages > 2 && 1024 + 2048 + static_cast<size_t>(stages) * kKsStageBytes + 2 * kKsMaxStages * 8 >
+                             static_cast<size_t>(kBulkSmemBudget))
+        --stages;
+    const size_t smem = 1024 + 2048 + static_cast<size_t>(stages) * kKsStageBytes + 2 * kKsMaxStages * 8;
+    int* err = dev ? dev->error_flag : nullptr;
+    return launch_on(dev, stream, gemv_ksplit_kernel, dim3(nb * groups), dim3(kKsThreads), smem, p, stages, groups, err);
 }
 
 // Resident CTAs per SM for (kernel, dynamic smem), cached: the persistent grid is SMs x this.
@@ -1650,6 +1890,7 @@ l0b_status launch_typed(l0b_device* dev, cudaStream_t stream, int sm_count, Gemv
     const int M = p.M;
     const bool psum = p.epi == EPI_PEER_SUM;
     if constexpr (sizeof(WT) == 1) {
+        if (const int groups = ksplit_groups(p, sm_count)) return launch_ksplit(dev, stream, sm_count, p, groups);
         if (!psum && bulk_applies(L0B_I8, p, sm_count)) return launch_bulk(dev, stream, sm_count, p);
     }
     if (psum) {
@@ -1810,6 +2051,7 @@ bool gemv_peer_sum_applies(int w_dtype, const GemvParams& p) {
 void gemv_set_tensor_cores(bool on) { g_gemv_mma = on; }
 void gemv_set_bulk(bool on) { g_gemv_bulk = on; }
 void gemv_set_bulk_short_rows(bool on) { g_gemv_bulk_short = on; }
+void gemv_set_ksplit(bool on) { g_gemv_ksplit = on; }
 void gemv_set_fill_split(int s) { g_gemv_fill_split = s <= 1 ? 1 : (s >= 8 ? 8 : (s >= 4 ? 4 : 2)); }
 
 namespace {

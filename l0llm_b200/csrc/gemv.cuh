@@ -83,6 +83,10 @@ struct GemvParams {
     int kb;      // > 0: int8 W in the blocked layout with this k per block (N % 16 == 0, K % kb == 0)
     int ugroup;  // bulk GEMV: k blocks per unit (set by the dispatcher)
     const PeerSum* peer;  // EPI_PEER_SUM: the communicator's mailboxes (device memory)
+    // K-split one-row GEMV over blocked int8 weights: int64 sums per output row, zero at rest (every
+    // launch leaves them zero), acc_count >= N; the tile-group counters are `counters`.
+    long long* acc;
+    int acc_count;
 };
 
 // Launches y = x * W^T with the fused options in `p` (fills kt and the grid). `w_dtype` is
@@ -97,6 +101,7 @@ void gemv_set_tensor_cores(bool on);
 void gemv_set_bulk(bool on);
 void gemv_set_fill_split(int s);
 void gemv_set_bulk_short_rows(bool on);
+void gemv_set_ksplit(bool on);
 // Process-wide: models created afterwards store their int8 per-row-scaled projections with few row
 // tiles in the blocked layout (default on).
 bool weight_blocking();

@@ -61,6 +61,8 @@ struct l0b_model {
     float* rscale = nullptr;  // [cap]
     float* tc_part = nullptr; // split-K partial tiles (tc_gemm_part_floats)
     unsigned* tc_counters = nullptr;  // [kTcCounters], zero at rest
+    long long* ks_acc = nullptr;      // k-split GEMV row sums [ks_acc_count], zero at rest
+    int ks_acc_count = 0;
     // Device-side step state: io = [tok(batch_cap) | pos(batch_cap)] written in one copy.
     int* io = nullptr;
     int* tok = nullptr;
@@ -364,6 +366,8 @@ GemvParams model_linear_params(const l0b_model* m, const ModelMatrix& w, int m_r
     p.part = m->tc_part;
     p.counters = m->tc_counters;
     p.counter_count = m->tc_counters ? kTcCounters : 0;
+    p.acc = m->ks_acc;
+    p.acc_count = m->ks_acc_count;
     return p;
 }
 
@@ -1089,6 +1093,8 @@ L0B_API l0b_status l0b_model_create(l0b_device* dev, l0b_suite* suite, const l0b
         L0B_TRY(m->alloc(&m->rscale, cap));
         L0B_TRY(m->alloc(&m->tc_part, tc_gemm_part_floats(m->dev->sm_count)));
         L0B_TRY(m->alloc(&m->tc_counters, kTcCounters));
+        m->ks_acc_count = m->qkv_w > m->h ? m->qkv_w : m->h;
+        L0B_TRY(m->alloc(&m->ks_acc, static_cast<size_t>(m->ks_acc_count)));
         m->tc_rows = 8;
     }
     L0B_TRY(m->alloc(&m->logits, static_cast<size_t>(m->batch_cap) * m->vocab));

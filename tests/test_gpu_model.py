@@ -261,16 +261,20 @@ def test_config1_qwen05b_fp16_greedy_64_steps(lz, orc, device, suite):
             break
 
 
-@pytest.mark.parametrize("short_rows", ["register", "bulk"])
-def test_config2_qwen7b_int8_shape_two_layers(lz, orc, device, suite, short_rows):
+@pytest.mark.parametrize("blocked_path", ["ksplit", "register", "bulk"])
+def test_config2_qwen7b_int8_shape_two_layers(lz, orc, device, suite, blocked_path):
     """Config 2 widths (hidden 3584, 28/4 heads, inter 18944, vocab 152064), int8 per-channel weights with
     fp16 scales U[1e-3, 2e-2], fp16 KV; two layers so the oracle finishes in seconds. The decode steps run
-    q/k/v and o_proj (blocked, 7 blocks per row) on the register GEMV or on the bulk GEMV."""
-    lz.load_library().l0b_set_gemv_bulk_short_rows(1 if short_rows == "bulk" else 0)
+    the blocked projections (q/k/v, o_proj: 7 blocks per row; down: 37) on the k-split GEMV, or with it
+    off on the register GEMV (short rows) and the bulk GEMV (down), or on the bulk GEMV for all three."""
+    lib = lz.load_library()
+    lib.l0b_set_gemv_ksplit(1 if blocked_path == "ksplit" else 0)
+    lib.l0b_set_gemv_bulk_short_rows(1 if blocked_path == "bulk" else 0)
     try:
         _config2_two_layers(lz, orc, device, suite)
     finally:
-        lz.load_library().l0b_set_gemv_bulk_short_rows(0)
+        lib.l0b_set_gemv_ksplit(1)
+        lib.l0b_set_gemv_bulk_short_rows(0)
 
 
 def _config2_two_layers(lz, orc, device, suite):
