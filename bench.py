@@ -11,12 +11,23 @@ fp16 KV cache. Weights are 7.07 GB per step, far larger than the 126 MB L2, so n
           position go host->device and the full vocab logits come back device->host, argmax on the host.
   roofline  the dominant kernel (the fused RMSNorm + gate/up int8 GEMV + SwiGLU of one layer, 2/3 of
           the weight bytes), launched on its own over 4 rotating weight copies and timed with events.
-  cpu_baseline  the CPU oracle port (C, OpenMP) of the same decoder and weights on the host cores.
+  cpu_baseline  the CPU oracle port (C, fp32 AVX2 FMA, OpenMP) of the same decoder and weights on the
+          host cores at the same 512-token context (all threads, plus a single-thread figure).
+  step_roofline  all bytes of a step (weights + KV) over the step time.
+  prefill_s  a warm prefill of the 512-token prompt (one 512-row tcgen05 GEMM per projection).
+  bs16    16 sequences decoded together (device-resident batched greedy, tcgen05 integer GEMM).
+  cfg0 / cfg1 / cfg3  the other BASELINE configurations on this GPU (N = 1 only): the config-0 GEMV
+          and GEMM, Qwen2.5-0.5B fp16 decode, and the Gated DeltaNet layer (decode bs1 / bs8, 4096-token
+          prefill).
+  tp      config 4 (Llama-3-70B shape, bf16) decoded tensor-parallel over all N ranks of the job (N = 1:
+          the whole model on one GPU), with the all-reduce path and its measured per-call time.
 
 --impl reference runs the reference's CPU path (the oracle port; the reference's own C# + Level Zero
 code cannot run here) on all host threads and prints the same metric.
-Multi-GPU (torchrun): config 2 runs on one GPU, so N ranks run N independent replicas (weak scaling);
-the timed region is bracketed by barriers and the max time over ranks is reported.
+Multi-GPU (torchrun): config 2 fits one GPU, so N ranks run N independent replicas (weak scaling; no
+collective on its data path); the timed region is bracketed by barriers and the max time over ranks is
+reported. The `tp` leg is the tensor-parallel measurement at every N. --workload cfg4 runs that leg alone
+(cfg3 the DeltaNet layer alone); --profile-case runs small cases for ncu captures.
 """
 from __future__ import annotations
 

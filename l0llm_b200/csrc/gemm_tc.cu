@@ -821,8 +821,10 @@ l0b_status tc_gemm_launch(l0b_device* d, const TcGemmArgs& a) {
     const bool q8 = a.wdtype == L0B_I8;
     L0B_REQUIRE(!q8 || a.wscale, L0B_ERR_ARGUMENT, "int8 weights need their row scales");
     if (q8 && a.kb > 0) {
-        L0B_REQUIRE(!swiglu, L0B_ERR_UNSUPPORTED, "the SwiGLU epilogue takes row-major weights");
-        L0B_TRY(make_map_blocked(&p.wmap, a.w, a.N, a.K, a.kb, kBM));
+        // SwiGLU loads 64 gate and 64 up rows per tile (four 16-row tiles of the blocked layout each).
+        L0B_REQUIRE(!swiglu || (a.N / 2) % 64 == 0, L0B_ERR_UNSUPPORTED,
+                    "blocked [gate; up] needs half the rows (%d) to be a multiple of 64", a.N / 2);
+        L0B_TRY(make_map_blocked(&p.wmap, a.w, a.N, a.K, a.kb, swiglu ? 64 : kBM));
         p.wkb = a.kb;
     } else {
         L0B_TRY(make_map(&p.wmap, a.w, a.wdtype, a.N, a.K, swiglu ? 64 : kBM));

@@ -1481,9 +1481,10 @@ __global__ void __launch_bounds__(kBulkThreads, 1) gemv_bulk_kernel(const GemvPa
 // feed mma.sync m16n8k32 s8 as loaded (as in gemv_bulk_kernel); warp w takes pieces 2 (w % 4), +1 of
 // block w / 4 of each stage, joins its digit columns to one exact int64 per row and adds it to the
 // row's int64 sum with one atomic: integer addition is exact, so the result does not depend on the
-// order the CTAs arrive in. The last CTA of a group to finish (a counter per group) turns the group's
+// order the CTAs arrive in. (Adding a block's four warps in shared memory first, one atomic per row,
+// measured slower: the atomics are not what bounds the kernel.) The last CTA of a group to finish (a counter per group) turns the group's
 // sums into outputs -- times 2^-e and the row scale in f64, one rounding -- runs the store / bias /
-// residual epilogue, and leaves the sums and the counter zero for the next launch.
+// residual / SwiGLU epilogue, and leaves the sums and the counter zero for the next launch.
 // ---------------------------------------------------------------------------------------------
 constexpr int kKsCW = 16;
 constexpr int kKsThreads = kKsCW * 32 + 32;  // consumers + 1 producer warp
@@ -1502,11 +1503,18 @@ __global__ void __launch_bounds__(kKsThreads, 1) gemv_ksplit_kernel(const GemvPa
     __shared__ int abort_s, issued_s, last_s;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
     const int N = p.N, K = p.K, nb = K / kWeightBlock;
-    const int ntiles = N >> 4;
+    // SwiGLU: the groups split the gate tiles, and a group's list is its gate tiles then the matching up
+    // tiles (N / 2 rows further), so its last CTA holds both sums of every output.
+    const bool swiglu = p.epi == EPI_SWIGLU;
+    const int half_tiles = (N >> 1) >> 4;
+    const int ntiles = swiglu ? half_tiles : N >> 4;
     const int kbi = blockIdx.x % nb, tg = blockIdx.x / nb;
     const int t_begin = static_cast<int>(static_cast<long long>(ntiles) * tg / groups);
     const int t_end = static_cast<int>(static_cast<long long>(ntiles) * (tg + 1) / groups);
-    const int nunits = (t_end - t_begin + 3) / 4;  // stages of up to four tiles
+    const int nt = t_end - t_begin;
+    const int nlist = swiglu ? 2 * nt : nt;
+    auto tile_of = [&](int j) { return swiglu && j >= nt ? half_tiles + t_begin + (j - nt) : t_begin + j; };
+    const int nunits = (nlist + 3) / 4;  // stages of up to four tiles
     char* const base = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(ks_smem) + 1023) & ~uintptr_t(1023));
     char* xs = base;            // 512 k as digits: item (piece, t) at (piece * 4 + t) * 64, digit dg at + dg * 16
     char* ring = base + 2048;
@@ -1538,13 +1546,14 @@ __global__ void __launch_bounds__(kKsThreads, 1) gemv_ksplit_kernel(const GemvPa
                     atomicExch(&abort_s, 1);
                     break;
                 }
-                const int t0 = t_begin + 4 * u, nblk = min(4, t_end - t0);
+                const int nblk = min(4, nlist - 4 * u);
                 asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bulk_smem_u32(&full[s])),
                              "r"(nblk * kKsBlockBytes)
                              : "memory");
                 for (int b = 0; b < nblk; ++b)
                     bulk_copy(ring + static_cast<size_t>(s) * kKsStageBytes + b * kKsBlockBytes,
-                              W + (static_cast<long long>(t0 + b) * nb + kbi) * kKsBlockBytes, kKsBlockBytes, &full[s]);
+                              W + (static_cast<long long>(tile_of(4 * u + b)) * nb + kbi) * kKsBlockBytes, kKsBlockBytes,
+                              &full[s]);
             }
         }
         return;
@@ -1634,8 +1643,8 @@ __global__ void __launch_bounds__(kKsThreads, 1) gemv_ksplit_kernel(const GemvPa
             __threadfence_block();
             atomicExch(&abort_s, 1);
         }
-        const int tile = t_begin + 4 * u + blk;
-        if (tile < t_end) {
+        if (4 * u + blk < nlist) {
+            const int tile = tile_of(4 * u + blk);
             const char* blkp = ring + static_cast<size_t>(s) * kKsStageBytes + blk * kKsBlockBytes + t * 16;
             const uint4 a0 = *reinterpret_cast<const uint4*>(blkp + g * kWeightBlock + pc0 * PE);
             const uint4 a1 = *reinterpret_cast<const uint4*>(blkp + (g + 8) * kWeightBlock + pc0 * PE);
@@ -1666,10 +1675,17 @@ __global__ void __launch_bounds__(kKsThreads, 1) gemv_ksplit_kernel(const GemvPa
     if (!last_s) return;
     __threadfence();
     const __half* sc = static_cast<const __half*>(p.scales);
-    for (int r = t_begin * 16 + threadIdx.x; r < t_end * 16; r += kKsCW * 32) {
+    auto row_out = [&](int r) {
         const long long D = static_cast<long long>(atomicExch(acc + r, 0ull));
-        const float y = static_cast<float>(static_cast<double>(D) * oscale_s * static_cast<double>(__half2float(sc[r])));
-        epilogue_store(p, r, 0, y);
+        return static_cast<float>(static_cast<double>(D) * oscale_s * static_cast<double>(__half2float(sc[r])));
+    };
+    for (int r = t_begin * 16 + threadIdx.x; r < t_end * 16; r += kKsCW * 32) {
+        if (swiglu) {
+            const float yg = row_out(r), yu = row_out((N >> 1) + r);
+            epilogue_store(p, r, 0, silu(yg) * yu);
+        } else {
+            epilogue_store(p, r, 0, row_out(r));
+        }
     }
     if (threadIdx.x == 0) p.counters[tg] = 0u;
 }
@@ -1732,14 +1748,16 @@ l0b_status launch_bulk(l0b_device* dev, cudaStream_t stream, int sm_count, GemvP
 // SM: groups = SMs / k blocks (every CTA one k block of one group).
 int ksplit_groups(const GemvParams& p, int sm_count) {
     if (!g_gemv_ksplit || !g_gemv_mma || p.kb != kWeightBlock || p.M != 1 || !p.acc || p.acc_count < p.N) return 0;
-    if (p.epi != EPI_STORE && p.epi != EPI_ACCUM) return 0;
+    if (p.epi != EPI_STORE && p.epi != EPI_ACCUM && p.epi != EPI_SWIGLU) return 0;
     if (p.group < p.K || p.N % 16 != 0 || p.K % kWeightBlock != 0 || p.x_dtype != L0B_F32) return 0;
+    if (p.epi == EPI_SWIGLU && (p.N / 2) % 16 != 0) return 0;
     if ((reinterpret_cast<uintptr_t>(p.x) | reinterpret_cast<uintptr_t>(p.w)) & 15) return 0;
     if (p.norm_w && (reinterpret_cast<uintptr_t>(p.norm_w) & 15)) return 0;
     const int nb = p.K / kWeightBlock;
     if (nb > sm_count) return 0;
+    const int ntiles = p.epi == EPI_SWIGLU ? p.N / 32 : p.N / 16;  // SwiGLU: gate tiles
     int groups = sm_count / nb;
-    if (groups > p.N / 16) groups = p.N / 16;
+    if (groups > ntiles) groups = ntiles;
     if (!p.counters || groups > p.counter_count) return 0;
     return groups;
 }

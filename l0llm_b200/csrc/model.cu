@@ -124,13 +124,17 @@ struct l0b_model {
     }
     // Int8 per-row-scaled projections with few 16-row tiles (under 8 per SM: q/k/v, o_proj, down) go in
     // the blocked layout, whose units of contiguous k blocks the one-row bulk GEMV streams as whole copies.
-    l0b_status alloc_matrix(ModelMatrix& m, int n, int k, bool may_block = true) {
+    // any_size: block whatever the tile count. Large matrices (gate/up of a whole model, the LM head) are
+    // otherwise row-major for the whole-tile bulk GEMV; blocked [gate; up] (TP shards) takes the k-split
+    // GEMV at batch 1, which pairs each gate tile with its up tile, and the tcgen05 GEMM above it. (A
+    // blocked config-2 gate/up on the k-split GEMV measured the same step time as the bulk GEMV.)
+    l0b_status alloc_matrix(ModelMatrix& m, int n, int k, bool may_block = true, bool any_size = false) {
         m.n = n;
         m.k = k;
         m.dtype = wdtype;
         m.group = wdtype == L0B_I8 ? (group > 0 ? group : k) : 0;
         m.kb = (may_block && weight_blocking() && wdtype == L0B_I8 && m.group >= k && k % kWeightBlock == 0 &&
-                n % 16 == 0 && n / 16 < 8 * dev->sm_count)
+                n % 16 == 0 && (any_size || n / 16 < 8 * dev->sm_count))
                    ? kWeightBlock
                    : 0;
         if (wdtype == L0B_I8) {
@@ -1041,7 +1045,7 @@ L0B_API l0b_status l0b_model_create(l0b_device* dev, l0b_suite* suite, const l0b
         L0B_TRY(m->alloc(&L.post_norm, m->h));
         L0B_TRY(m->alloc_matrix(L.qkv, m->qkv_w, m->h));
         L0B_TRY(m->alloc_matrix(L.o, m->h, m->qdim));
-        L0B_TRY(m->alloc_matrix(L.gate_up, 2 * m->inter, m->h, false));  // SwiGLU epilogues take row-major weights
+        L0B_TRY(m->alloc_matrix(L.gate_up, 2 * m->inter, m->h, (m->inter % 64) == 0));
         L0B_TRY(m->alloc_matrix(L.down, m->h, m->inter));
         if (c.attention_bias) L0B_TRY(m->alloc(&L.qkv_bias, m->qkv_w));
         if (c.qk_norm) {
@@ -1093,7 +1097,7 @@ L0B_API l0b_status l0b_model_create(l0b_device* dev, l0b_suite* suite, const l0b
         L0B_TRY(m->alloc(&m->rscale, cap));
         L0B_TRY(m->alloc(&m->tc_part, tc_gemm_part_floats(m->dev->sm_count)));
         L0B_TRY(m->alloc(&m->tc_counters, kTcCounters));
-        m->ks_acc_count = m->qkv_w > m->h ? m->qkv_w : m->h;
+        m->ks_acc_count = std::max(std::max(m->qkv_w, m->h), 2 * m->inter);
         L0B_TRY(m->alloc(&m->ks_acc, static_cast<size_t>(m->ks_acc_count)));
         m->tc_rows = 8;
     }

@@ -241,6 +241,46 @@ def _greedy_oracle(om, prompt, steps):
     return out, margins
 
 
+@pytest.mark.parametrize("ksplit", [1, 0])
+def test_int8_blocked_gate_up_prefill_and_decode_against_oracle(lz, orc, device, suite, ksplit):
+    """Int8 per-row weights at hidden 1024 / inter 2048: every projection, [gate; up] included, is stored in
+    the blocked layout (few row tiles), so the prompt runs the tcgen05 GEMM's SwiGLU epilogue over blocked
+    weights and the decode steps the k-split GEMV with gate / up tiles paired (ksplit 1) or the
+    register-streamed GEMV (ksplit 0). Logits of the prompt and of each decode step against the oracle."""
+    cfgd = dict(hidden_size=1024, intermediate_size=2048, num_layers=2, num_attention_heads=8, num_key_value_heads=2,
+                head_dim=128, vocab_size=4096, max_position_embeddings=4096, rms_norm_eps=1e-6, rope_theta=1e6,
+                attention_bias=1, q8_group=0)
+    orcd = dict(hidden=1024, inter=2048, layers=2, heads=8, kv_heads=2, head_dim=128, vocab=4096, max_pos=4096,
+                eps=1e-6, theta=1e6, tie=0, bias=1, qk_norm=0, rope_type=0, rope_factor=1.0, rope_original_max=0,
+                rope_low=1.0, rope_high=4.0, rope_beta_fast=32.0, rope_beta_slow=1.0, rope_attention=0.0,
+                wdtype=orc.I8, group=0, kv_dtype=orc.F16)
+    prompt = np.random.default_rng(7).integers(0, 4096, 40).astype(np.int32)
+    lib = lz.load_library()
+    lib.l0b_set_gemv_ksplit(ksplit)
+    try:
+        with lz.LlmModel(device, suite, lz.model_config(kv_dtype=lz.F16, **cfgd), 64, "int8") as model:
+            model.init_synthetic(3, 0.02, 2e-4, 1e-3)  # int8 weights of std ~0.04: a well-conditioned decoder
+            got = [model.Prefill(prompt)]
+            toks = [int(np.argmax(got[0]))]
+            for _ in range(4):
+                got.append(model.Decode(toks[-1]))
+                toks.append(int(np.argmax(got[-1])))
+    finally:
+        lib.l0b_set_gemv_ksplit(1)
+    om = orc.OracleModel(orcd, 64)
+    om.init_synthetic(3, 0.02, 2e-4, 1e-3)
+    want = None
+    for t, tok in enumerate(prompt):
+        want = om.step(int(tok), t, want_logits=(t == len(prompt) - 1))
+    wants = [want]
+    for i, tok in enumerate(toks[:-1]):
+        wants.append(om.step(tok, len(prompt) + i))
+    om.close()
+    for i, (g, w) in enumerate(zip(got, wants)):
+        err = np.abs(g.astype(np.float64) - w)
+        assert np.all(err <= 1e-2 + 1e-2 * np.abs(w)), f"step {i}: max err {err.max():.3e}"
+
+
 def test_config1_qwen05b_fp16_greedy_64_steps(lz, orc, device, suite):
     """Config 1: Qwen2.5-0.5B shape, fp16 weights N(0, 0.02) seed 1, 128-token prompt, greedy decode."""
     steps = 64
