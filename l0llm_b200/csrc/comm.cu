@@ -16,10 +16,13 @@
 #include "runtime.h"
 
 // Peer all-reduce (small collectives of the decode step): every rank owns a mailbox in its HBM, mapped
-// into every other rank's address space by CUDA IPC. Layout of a mailbox:
+// into every other rank's address space by CUDA IPC. A mailbox holds three regions:
+// 1. the u64 max all-reduce (the vocab-split argmax keys):
 //   data  [2 parities][kMaxRanks][slot_floats]   partials written by the ranks (peer stores over NVLink)
 //   flags [2 parities][kMaxRanks][kPeerCtas]     epoch of the partial a rank's CTA has published here
 //   epoch [kPeerCtas]                            this rank's own count of all-reduces, per CTA
+// 2. the peer-sum region of the row-split GEMV epilogue (layout in gemv.cuh);
+// 3. the tagged f32 sum all-reduce (kLLBytes, below).
 constexpr int kMaxRanks = 8;
 constexpr int kPeerCtas = 32;
 constexpr int kPeerChunkBytes = 8192;  // bytes per chunk; chunk j is always handled by CTA j % kPeerCtas
@@ -34,6 +37,7 @@ struct l0b_comm {
     char* peer_mbox[kMaxRanks] = {};       // every rank's mailbox in this process's address space
     bool peer = false;                     // peer all-reduce available
     l0b::PeerSum* peer_sum = nullptr;      // device copy of the peer-sum mailboxes (GEMV all-reduce epilogue)
+    size_t ll_off = 0;                     // tagged f32 all-reduce region in every mailbox
 };
 
 namespace l0b {
@@ -119,7 +123,15 @@ struct PeerArgs {
     char* mbox[kMaxRanks];
     int nranks, rank;
     int* error;
+    size_t ll_off;  // offset of the tagged f32 region in every mailbox
 };
+
+// Tagged f32 region (the f32 sums): data [2 parities][kMaxRanks][kLLSlotElems] 64-bit words (epoch << 32 |
+// f32 bits), then one epoch per CTA index. A value and its tag travel in one 64-bit store, so a reader
+// that sees the call's tag has the value: no fence, no separate flag.
+constexpr long long kLLSlotElems = 1LL << 17;
+constexpr int kLLChunk = 1024;  // elements per chunk; chunk j always belongs to CTA j % kPeerCtas
+constexpr size_t kLLBytes = 2ull * kMaxRanks * kLLSlotElems * 8 + kPeerCtas * sizeof(unsigned);
 
 __device__ __forceinline__ unsigned peer_ld_acquire(const unsigned* p) {
     unsigned v;
@@ -191,7 +203,74 @@ __global__ void __launch_bounds__(512) peer_allreduce_kernel(const PeerArgs a) {
     if (threadIdx.x == 0) *epoch_p = ep;
 }
 
+// f32 sum over peer memory with tagged values: CTA c owns chunks c, c + grid, ... of kLLChunk elements;
+// each thread sends its elements to every rank tagged with the CTA's epoch, then reads every rank's
+// copy of them from its own mailbox as they arrive (bounded wait, then the error flag) and sums them in
+// rank order -- the same bits on every rank. Parities and per-CTA epochs as in peer_allreduce_kernel.
+__global__ void __launch_bounds__(512) peer_allreduce_ll_kernel(const PeerArgs a) {
+    pdl_wait();
+    const int c = blockIdx.x, n = a.nranks;
+    const long long stride = static_cast<long long>(gridDim.x) * kLLChunk;
+    char* mine = a.mbox[a.rank] + a.ll_off;
+    unsigned* epoch_p = reinterpret_cast<unsigned*>(mine + 2ull * kMaxRanks * kLLSlotElems * 8) + c;
+    const unsigned ep = *reinterpret_cast<volatile unsigned*>(epoch_p) + 1;
+    const int par = ep & 1;
+    float* buf = static_cast<float*>(a.buf);
+    auto slot = [&](char* region, int src) {
+        return reinterpret_cast<unsigned long long*>(region) + (static_cast<long long>(par) * kMaxRanks + src) * kLLSlotElems;
+    };
+    for (long long lo = c * static_cast<long long>(kLLChunk); lo < a.count; lo += stride) {
+        const long long hi = min(a.count, lo + kLLChunk);
+        for (long long i = lo + threadIdx.x; i < hi; i += blockDim.x) {
+            const unsigned long long w = (static_cast<unsigned long long>(ep) << 32) | __float_as_uint(buf[i]);
+            for (int r = 0; r < n; ++r) {
+                unsigned long long* dst = slot(a.mbox[r] + a.ll_off, a.rank) + i;
+                asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(dst), "l"(w) : "memory");
+            }
+        }
+    }
+    const long long t0 = clock64();
+    bool late = false;
+    for (long long lo = c * static_cast<long long>(kLLChunk); lo < a.count; lo += stride) {
+        const long long hi = min(a.count, lo + kLLChunk);
+        for (long long i = lo + threadIdx.x; i < hi; i += blockDim.x) {
+            float v = 0.f;
+            for (int r = 0; r < n; ++r) {
+                const unsigned long long* q = slot(mine, r) + i;
+                unsigned long long w;
+                asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(w) : "l"(q) : "memory");
+                while (static_cast<unsigned>(w >> 32) != ep && !late) {
+                    if (clock64() - t0 > 4000000000LL) {
+                        late = true;
+                        if (a.error) atomicExch(a.error, 1);
+                    }
+                    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(w) : "l"(q) : "memory");
+                }
+                const float x = __uint_as_float(static_cast<unsigned>(w));
+                v = r == 0 ? x : v + x;
+            }
+            buf[i] = v;
+        }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) *epoch_p = ep;
+}
+
 l0b_status comm_allreduce(l0b_comm* c, void* buf, size_t count, int dtype, int op) {
+    if (c->peer && dtype == L0B_F32 && op == COLL_SUM && static_cast<long long>(count) <= kLLSlotElems) {
+        PeerArgs a{};
+        a.buf = buf;
+        a.count = static_cast<long long>(count);
+        for (int r = 0; r < c->nranks; ++r) a.mbox[r] = c->peer_mbox[r];
+        a.nranks = c->nranks;
+        a.rank = c->rank;
+        a.error = c->dev->error_flag;
+        a.ll_off = c->ll_off;
+        long long ctas = (static_cast<long long>(count) + kLLChunk - 1) / kLLChunk;
+        if (ctas > kPeerCtas) ctas = kPeerCtas;
+        if (ctas < 1) ctas = 1;
+        return c->dev->launch(peer_allreduce_ll_kernel, dim3(static_cast<unsigned>(ctas)), dim3(512), 0, a);
+    }
     const size_t esize = dtype == kDtypeU64 ? 8 : 4;
     const bool fits = count * esize <= kPeerSlotFloats * sizeof(float);
     if (c->peer && fits && ((dtype == L0B_F32 && op == COLL_SUM) || (dtype == kDtypeU64 && op == COLL_MAX))) {
@@ -221,11 +300,14 @@ l0b_status comm_allreduce(l0b_comm* c, void* buf, size_t count, int dtype, int o
 l0b_status peer_setup(l0b_comm* c) {
     if (c->nranks < 2 || c->nranks > kMaxRanks || g_peer_disabled) return L0B_OK;
     static_assert(kMaxPeerRanks == kMaxRanks, "one rank limit for both mailboxes");
-    // One allocation: the all-reduce mailbox, then (from psum_off) the GEMV epilogue's peer-sum mailbox.
+    // One allocation: the u64 all-reduce region, the GEMV epilogue's peer-sum region (from psum_off) and the
+    // tagged f32 all-reduce region (from ll_off).
     const size_t ar_bytes = 2ull * kMaxRanks * kPeerSlotFloats * sizeof(float) +
                             2ull * kMaxRanks * kPeerCtas * sizeof(unsigned) + kPeerCtas * sizeof(unsigned);
     const size_t psum_off = (ar_bytes + 255) & ~static_cast<size_t>(255);
-    const size_t mbox_bytes = psum_off + kPeerSumBytes;
+    const size_t ll_off = (psum_off + kPeerSumBytes + 255) & ~static_cast<size_t>(255);
+    const size_t mbox_bytes = ll_off + kLLBytes;
+    c->ll_off = ll_off;
     if (cudaMalloc(&c->mbox, mbox_bytes) != cudaSuccess) {
         cudaGetLastError();
         c->mbox = nullptr;

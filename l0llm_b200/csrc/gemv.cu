@@ -545,15 +545,21 @@ __device__ __forceinline__ void mma_s8_16832(int (&c)[4], uint32_t a0, uint32_t 
 }
 
 // Peer-sum mailbox addressing (layout in gemv.cuh) and the system-scope flag accesses.
-__device__ __forceinline__ float* peer_sum_slot(char* mb, int par, int src) {
-    return reinterpret_cast<float*>(mb) + (static_cast<long long>(par) * kMaxPeerRanks + src) * kPeerSumSlotFloats;
-}
-__device__ __forceinline__ unsigned* peer_sum_flag(char* mb, int par, int src, int cta) {
-    return reinterpret_cast<unsigned*>(mb + kPeerSumDataBytes) +
-           (static_cast<size_t>(par) * kMaxPeerRanks + src) * kPeerSumCtas + cta;
+__device__ __forceinline__ unsigned long long* peer_sum_slot(char* mb, int par, int src) {
+    return reinterpret_cast<unsigned long long*>(mb) + (static_cast<long long>(par) * kMaxPeerRanks + src) * kPeerSumSlotElems;
 }
 __device__ __forceinline__ unsigned* peer_sum_counter(char* mb, int i) {  // 0: epoch, 1: CTAs done
-    return reinterpret_cast<unsigned*>(mb + kPeerSumDataBytes + kPeerSumFlagBytes) + 32 * i;
+    return reinterpret_cast<unsigned*>(mb + kPeerSumDataBytes) + 32 * i;
+}
+// One tagged value: a single 64-bit store / load, so the tag and the value are seen together.
+__device__ __forceinline__ void st_tagged_sys(unsigned long long* p, unsigned tag, float v) {
+    const unsigned long long w = (static_cast<unsigned long long>(tag) << 32) | __float_as_uint(v);
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_tagged_sys(const unsigned long long* p) {
+    unsigned long long w;
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+    return w;
 }
 __device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
     unsigned v;
@@ -844,9 +850,9 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_mma_kernel(const GemvParams 
                     const PeerSum* ps = p.peer;
                     const long long i0 = static_cast<long long>(m) * N + r0, i1 = static_cast<long long>(m) * N + r1;
                     for (int d = 0; d < ps->nranks; ++d) {
-                        float* dst = peer_sum_slot(ps->mbox[d], par, ps->rank);
-                        if (v0) dst[i0] = y0;
-                        if (v1) dst[i1] = y1;
+                        unsigned long long* dst = peer_sum_slot(ps->mbox[d], par, ps->rank);
+                        if (v0) st_tagged_sys(dst + i0, ep, y0);
+                        if (v1) st_tagged_sys(dst + i1, ep, y1);
                     }
                 }
             } else if (p.epi == EPI_ARGMAX) {
@@ -1023,36 +1029,35 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_mma_kernel(const GemvParams 
         cluster.sync();
     }
     if (psum && ks == 0) {
-        // Every partial of this CTA's tiles is out: publish them, wait for the other ranks' partials of
-        // the same tiles (the same CTA index on every rank), then add the slots in rank order.
+        // Every partial of this CTA's tiles is on its way: read every rank's values of the same tiles (the
+        // same CTA index on every rank) as they arrive, and add them in rank order.
         const PeerSum* ps = p.peer;
         const int nr = ps->nranks, me = ps->rank;
         char* mine = ps->mbox[me];
-        __threadfence_system();
         __syncthreads();
-        if (threadIdx.x < nr) st_release_sys(peer_sum_flag(ps->mbox[threadIdx.x], par, me, blockIdx.x), ep);
-        if (threadIdx.x < nr) {
-            const unsigned* f = peer_sum_flag(mine, par, threadIdx.x, blockIdx.x);
-            const long long t0 = clock64();
-            while (ld_acquire_sys(f) != ep) {
-                if (clock64() - t0 > kPeerSumWaitCycles) {
-                    if (ps->error) atomicExch(ps->error, 1);
-                    break;
-                }
-            }
-        }
-        __syncthreads();
-        // Slots written by other GPUs: read at L2 (ld.cg), past any line L1 kept from two calls ago.
         float* out = static_cast<float*>(p.seg[0].out);
         const long long ld = p.seg[0].ld;
         const int per = 16 * M;
+        const long long t0 = clock64();
+        bool late = false;
         for (int idx = threadIdx.x; idx < my_tiles * per; idx += kThreads) {
             const int i = idx / per, rem = idx - (idx / per) * per, m = rem >> 4;
             const int r = (blockIdx.x + i * gridDim.x) * 16 + (rem & 15);
             if (r >= N) continue;
             const long long si = static_cast<long long>(m) * N + r;
             float v = out[m * ld + r];
-            for (int src = 0; src < nr; ++src) v += __ldcg(peer_sum_slot(mine, par, src) + si);
+            for (int src = 0; src < nr; ++src) {
+                const unsigned long long* q = peer_sum_slot(mine, par, src) + si;
+                unsigned long long w = ld_tagged_sys(q);
+                while (static_cast<unsigned>(w >> 32) != ep && !late) {
+                    if (clock64() - t0 > kPeerSumWaitCycles) {
+                        late = true;
+                        if (ps->error) atomicExch(ps->error, 1);
+                    }
+                    w = ld_tagged_sys(q);
+                }
+                v += __uint_as_float(static_cast<unsigned>(w));
+            }
             out[m * ld + r] = v;
         }
         __syncthreads();
@@ -1861,7 +1866,7 @@ l0b_status launch_mma(l0b_device* dev, cudaStream_t stream, int sm_count, const 
     const int units = swiglu ? p.N / 2 : p.N;
     const int ntiles = (units + (swiglu ? 7 : 15)) / (swiglu ? 8 : 16);
     int cap = sm_count * resident_ctas(reinterpret_cast<const void*>(kernel), smem) / S;
-    if (p.epi == EPI_PEER_SUM && cap > kPeerSumCtas) cap = kPeerSumCtas;  // one flag per CTA index
+    if (p.epi == EPI_PEER_SUM && cap > kPeerSumCtas) cap = kPeerSumCtas;
     const dim3 grid(ntiles < cap ? ntiles : (cap > 0 ? cap : 1), S);
     if (dev) return dev->launch_cluster(kernel, grid, dim3(kThreads), smem, S, p);
     cudaLaunchConfig_t cfg = {};
@@ -1914,7 +1919,7 @@ l0b_status launch_typed(l0b_device* dev, cudaStream_t stream, int sm_count, Gemv
     if (psum) {
         L0B_REQUIRE(p.peer && p.nseg == 1 && p.out_dtype == L0B_F32 && p.seg[0].out, L0B_ERR_ARGUMENT,
                     "the peer-sum epilogue needs the communicator's mailboxes and one f32 output");
-        L0B_REQUIRE(static_cast<long long>(p.N) * (M < 8 ? M : 8) <= kPeerSumSlotFloats, L0B_ERR_OUT_OF_RANGE,
+        L0B_REQUIRE(static_cast<long long>(p.N) * (M < 8 ? M : 8) <= kPeerSumSlotElems, L0B_ERR_OUT_OF_RANGE,
                     "peer-sum partials of %d x %d floats exceed the mailbox slot", M < 8 ? M : 8, p.N);
     }
     L0B_REQUIRE(p.kb == 0 || p.kb == kWeightBlock, L0B_ERR_ARGUMENT, "blocked layout with %d k per block", p.kb);
@@ -2053,9 +2058,13 @@ __global__ void __launch_bounds__(256) gemm_f32_kernel(int M, int N, int K, cons
 
 }  // namespace
 
+bool gemv_takes_ksplit(int w_dtype, const GemvParams& p, int sm_count) {
+    return w_dtype == L0B_I8 && ksplit_groups(p, sm_count) > 0;
+}
+
 bool gemv_peer_sum_applies(int w_dtype, const GemvParams& p) {
     if (!p.peer || p.nseg != 1 || p.out_dtype != L0B_F32 || !p.seg[0].out || p.M < 1) return false;
-    if (static_cast<long long>(p.N) * (p.M < 8 ? p.M : 8) > kPeerSumSlotFloats) return false;
+    if (static_cast<long long>(p.N) * (p.M < 8 ? p.M : 8) > kPeerSumSlotElems) return false;
     GemvParams t8 = p;
     t8.M = p.M < 8 ? p.M : 8;
     switch (w_dtype) {

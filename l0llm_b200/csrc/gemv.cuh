@@ -16,23 +16,23 @@ enum GemvEpi : int {
 
 // All-reduce epilogue of a row-split projection under tensor parallelism (EPI_PEER_SUM, the tensor-core
 // GEMV only). Each rank owns a peer-sum mailbox in its HBM, mapped into every rank by CUDA IPC:
-//   data  [2 parities][kMaxPeerRanks][kPeerSumSlotFloats]  the ranks' partial outputs, [m][n]
-//   flags [2 parities][kMaxPeerRanks][kPeerSumCtas]        epoch a rank's CTA has published here
+//   data [2 parities][kMaxPeerRanks][kPeerSumSlotElems]  the ranks' partial outputs, [m][n], each one
+//                                                        64-bit word (epoch << 32 | f32 bits)
 // followed in the own mailbox by two counters: the epoch (fused calls completed) and the CTAs done in
 // the current call. All ranks launch the same grid, so CTA c handles the same tiles everywhere: it
-// stores its tiles' partials into its rank's slot of every mailbox, publishes the call's epoch in every
-// mailbox's flag for (rank, c), waits (bounded) for every rank's flag for c in its own mailbox and adds
-// the slots to `out` in rank order -- identical bits on every rank. The parity is the call's epoch & 1
-// (one epoch per call, for every CTA: the last CTA to finish advances it), so a rank one call ahead
-// writes the other half while a peer still reads this one; two calls ahead is impossible because
-// finishing a call needs every rank's flag of it, which each rank publishes only after its previous
-// call has completed (stream order).
+// stores its tiles' partials, tagged with the call's epoch, into its rank's slot of every mailbox (one
+// 64-bit store per value: value and tag arrive together, so no fence and no separate flag), then reads
+// the same elements of every rank's slot in its own mailbox -- waiting (bounded) until each carries
+// the epoch -- and adds them to `out` in rank order: identical bits on every rank. The parity is the
+// call's epoch & 1 (one epoch per call for every CTA: the last CTA to finish advances it), so a rank
+// one call ahead writes the other half while a peer still reads this one; two calls ahead is
+// impossible because finishing a call needs every rank's values of it, which each rank writes only
+// after its previous call has completed (stream order).
 constexpr int kMaxPeerRanks = 8;
-constexpr int kPeerSumCtas = 1024;
-constexpr long long kPeerSumSlotFloats = 1LL << 17;  // 8 rows of 16384
-constexpr size_t kPeerSumDataBytes = 2ull * kMaxPeerRanks * kPeerSumSlotFloats * sizeof(float);
-constexpr size_t kPeerSumFlagBytes = 2ull * kMaxPeerRanks * kPeerSumCtas * sizeof(unsigned);
-constexpr size_t kPeerSumBytes = kPeerSumDataBytes + kPeerSumFlagBytes + 256;  // + epoch, done
+constexpr int kPeerSumCtas = 1024;                   // CTAs of one fused launch at most
+constexpr long long kPeerSumSlotElems = 1LL << 17;  // 8 rows of 16384
+constexpr size_t kPeerSumDataBytes = 2ull * kMaxPeerRanks * kPeerSumSlotElems * sizeof(unsigned long long);
+constexpr size_t kPeerSumBytes = kPeerSumDataBytes + 256;  // + epoch, done
 
 struct PeerSum {
     char* mbox[kMaxPeerRanks];  // every rank's peer-sum mailbox in this process's address space
@@ -110,6 +110,8 @@ void set_weight_blocking(bool on);
 // Whether gemv_nk_launch can run `p` (M rows) with the EPI_PEER_SUM epilogue: 16-bit or per-row int8
 // weights on the tensor-core GEMV, one f32 output segment, M x N within a mailbox slot.
 bool gemv_peer_sum_applies(int w_dtype, const GemvParams& p);
+// Whether gemv_nk_launch runs `p` on the k-split GEMV (blocked int8, one row).
+bool gemv_takes_ksplit(int w_dtype, const GemvParams& p, int sm_count);
 // The communicator's peer-sum mailboxes (device memory), or null: no peer path, or fused all-reduces
 // switched off (l0b_comm_set_fused_allreduce).
 const PeerSum* comm_peer_sum(const l0b_comm* c);

@@ -429,12 +429,13 @@ l0b_status emit(l0b_model* m, int li, const char* stage, const float* dptr, long
     return L0B_OK;
 }
 
-// A row-split projection under TP, folded into the residual stream. Where the tensor-core GEMV takes
-// it (decode rows) and the communicator has peer mailboxes, one kernel does both: each CTA sends its
-// tiles' partials to every rank and adds every rank's partials of the same tiles to `hidden` in rank
-// order. Otherwise one in-place all-reduce after the GEMV: rank 0 accumulates its partial into
-// `hidden`, the other ranks store theirs there, so the sum over ranks is hidden + the partials on every
-// rank. Both give ((hidden + p0) + p1) + ... in fp32, the same bits.
+// A row-split projection under TP, folded into the residual stream. Where the register-streamed
+// tensor-core GEMV takes it (decode rows of 16-bit or row-major int8 weights) and the communicator has
+// peer mailboxes, one kernel does both: each CTA sends its tiles' partials to every rank and adds every
+// rank's partials of the same tiles to `hidden` in rank order. Otherwise (the tcgen05 GEMM's rows, the
+// k-split GEMV's blocked int8) one in-place all-reduce after the GEMV: rank 0 accumulates its partial
+// into `hidden`, the other ranks store theirs there, so the sum over ranks is hidden + the partials on
+// every rank. Both give ((hidden + p0) + p1) + ... in fp32 over the same partials, the same bits.
 l0b_status project_into_residual(l0b_model* m, const ModelMatrix& w, GemvParams p, int rows) {
     if (const PeerSum* ps = comm_peer_sum(m->comm)) {
         GemvParams q = p;
@@ -443,8 +444,10 @@ l0b_status project_into_residual(l0b_model* m, const ModelMatrix& w, GemvParams 
         q.seg[0] = {m->hidden, nullptr, m->h, m->h};
         q.peer = ps;
         GemvParams t = q;
-        t.epi = EPI_ACCUM;  // the rows the tcgen05 GEMM would take stay on the GEMM + all-reduce path
-        if (!tc_takes(m, w, t) && gemv_peer_sum_applies(w.dtype, q)) return gemv_nk_launch(m->dev, w.dtype, q);
+        t.epi = EPI_ACCUM;  // what the pair would run: the tcgen05 GEMM or the k-split GEMV stay in the pair
+        if (!tc_takes(m, w, t) && !gemv_takes_ksplit(w.dtype, t, m->dev->sm_count) &&
+            gemv_peer_sum_applies(w.dtype, q))
+            return gemv_nk_launch(m->dev, w.dtype, q);
     }
     p.epi = m->tp_rank == 0 ? EPI_ACCUM : EPI_STORE;
     p.out_dtype = L0B_F32;
