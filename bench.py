@@ -305,7 +305,7 @@ def dominant_kernel_roofline(lz, dev, suite, stream_ptr, torch, peak: float, pea
     for b in qs + ss + [x, nw, out]:
         b.Dispose()
     name = ("gemv_bulk_kernel (int8 [gate;up] 37888x3584: whole 16-row tiles by bulk copy, RMSNorm prologue, "
-            "mma.sync, SwiGLU epilogue)" if bulk else
+            "integer mma.sync m16n8k32 on int8 digits, SwiGLU epilogue)" if bulk else
             "gemv_mma_kernel<int8> (register-streamed; RMSNorm prologue + [gate;up] 37888x3584 mma.sync + SwiGLU)")
     return {"kernel": name,
             "bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",

@@ -448,21 +448,24 @@ L0B_API l0b_status l0b_comm_free(l0b_comm* comm);
 /* In-place sum of the first `count` elements of `buf` over the ranks, on the device stream (recorded
  * into the current command list when the device is recording). */
 L0B_API l0b_status l0b_comm_allreduce(l0b_comm* comm, l0b_buffer* buf, int64_t count);
-/* Tensor-parallel all-reduces of f32 sums (the row-split o_proj / down partials) and u64 maxima (the
- * vocab-split argmax keys) up to 2 MB run as one kernel over peer memory: every rank's mailbox is mapped
- * into the others by CUDA IPC when the communicator is made; each rank writes its partial into every
- * mailbox, raises an epoch flag there, waits (bounded, ~2 s, then the device error flag) for the others'
- * flags and sums in rank order, so all ranks hold the same bits. No multicast loads. Larger or other
+/* Tensor-parallel all-reduces of f32 sums (the row-split o_proj / down partials, up to 131072 values)
+ * and u64 maxima (the vocab-split argmax keys, up to 2 MB) run as one kernel over peer memory: every
+ * rank's mailbox is mapped into the others by CUDA IPC when the communicator is made. f32 sums: each rank
+ * writes every value into every mailbox as one 64-bit word that also carries the call's epoch, and reads
+ * the others' words from its own mailbox as they arrive (bounded wait, ~2 s, then the device error
+ * flag), summing in rank order, so all ranks hold the same bits; no fence and no separate flag. u64
+ * maxima: partials, a system-scope fence and an epoch flag per rank. No multicast loads. Larger or other
  * collectives, and communicators made after l0b_comm_set_peer_allreduce(0), use NCCL. No counterpart in
  * the reference (single device). */
 L0B_API l0b_status l0b_comm_set_peer_allreduce(int32_t enable);
 /* *enabled = 1 when this communicator's small all-reduces run over peer memory (every rank agrees). */
 L0B_API l0b_status l0b_comm_uses_peer_allreduce(l0b_comm* comm, int32_t* enabled);
-/* With peer memory, a model's row-split decode projections (o_proj, down on the tensor-core GEMV) fold
- * the all-reduce into the GEMV (1, default): each CTA sends its tiles' partial sums to every rank's
- * mailbox, waits (bounded) for the same tiles from the other ranks and adds them to the residual stream
- * in rank order -- the bits of the GEMV + all-reduce pair, one launch instead of two. 0: the pair.
- * Process-wide; affects steps recorded after the call. No counterpart in the reference. */
+/* With peer memory, a model's row-split decode projections (o_proj, down on the register-streamed
+ * tensor-core GEMV: 16-bit or row-major int8 weights) fold the all-reduce into the GEMV (1, default):
+ * each CTA sends its tiles' partial sums, tagged with the call's epoch, to every rank's mailbox, reads
+ * (bounded wait) the same tiles from the other ranks and adds them to the residual stream in rank order
+ * -- the bits of the GEMV + all-reduce pair, one launch instead of two. 0: the pair. Process-wide;
+ * affects steps recorded after the call. No counterpart in the reference. */
 L0B_API l0b_status l0b_comm_set_fused_allreduce(int32_t enable);
 
 /* Tuning: the largest K split the tensor-core GEMM may use for narrow projections (1..16, default 16;

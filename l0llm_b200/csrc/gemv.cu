@@ -1570,14 +1570,22 @@ __global__ void __launch_bounds__(kKsThreads, 1) gemv_ksplit_kernel(const GemvPa
     {
         const float* xf = static_cast<const float*>(p.x);
         float ss = 0.f, am = 0.f;
-        for (int k = 4 * threadIdx.x; k < K; k += 4 * kKsCW * 32) {
-            float4 a = *reinterpret_cast<const float4*>(xf + k);
-            if (p.norm_w) {
-                ss = fmaf(a.x, a.x, fmaf(a.y, a.y, fmaf(a.z, a.z, fmaf(a.w, a.w, ss))));
-                const float4 w = *reinterpret_cast<const float4*>(p.norm_w + k);
-                a.x *= w.x, a.y *= w.y, a.z *= w.z, a.w *= w.w;
+        // Eight 16-byte loads in flight per thread (one L2 round trip per eight, not per load).
+        constexpr int kStep = 4 * kKsCW * 32;
+        for (int k0 = 4 * threadIdx.x; k0 < K; k0 += 8 * kStep) {
+            float4 a[8], w[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const int k = k0 + j * kStep;
+                a[j] = k < K ? *reinterpret_cast<const float4*>(xf + k) : make_float4(0.f, 0.f, 0.f, 0.f);
+                w[j] = (p.norm_w && k < K) ? *reinterpret_cast<const float4*>(p.norm_w + k) : make_float4(1.f, 1.f, 1.f, 1.f);
             }
-            am = fmaxf(am, fmaxf(fmaxf(fabsf(a.x), fabsf(a.y)), fmaxf(fabsf(a.z), fabsf(a.w))));
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                ss = fmaf(a[j].x, a[j].x, fmaf(a[j].y, a[j].y, fmaf(a[j].z, a[j].z, fmaf(a[j].w, a[j].w, ss))));
+                const float4 b = make_float4(a[j].x * w[j].x, a[j].y * w[j].y, a[j].z * w[j].z, a[j].w * w[j].w);
+                am = fmaxf(am, fmaxf(fmaxf(fabsf(b.x), fabsf(b.y)), fmaxf(fabsf(b.z), fabsf(b.w))));
+            }
         }
         ss = warp_sum(ss);
         am = warp_max(am);
