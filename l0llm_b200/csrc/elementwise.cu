@@ -27,6 +27,24 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(float* x, const float* res
     for (int i = threadIdx.x; i < width; i += blockDim.x) out[base + i] = (x[base + i] * rstd) * w[i];
 }
 
+// QK-norm of the fused layer (LlmDecoderLayer, L/LlmDecoderLayer.cs:308-313): RMSNorm of every query and
+// key head of the stacked q|k|v rows in place, CTA (row, head) -- the arithmetic of rmsnorm_kernel at 32
+// threads (the same sums in the same order: head dims below 256, where that kernel runs 32 threads).
+__global__ void __launch_bounds__(32) head_norm_kernel(float* qkv, long long ld, int nq, int hd, const float* wq,
+                                                       const float* wk, float eps) {
+    __shared__ float red[32];
+    pdl_wait();
+    const int h = blockIdx.y;
+    const bool is_q = h < nq;
+    float* x = qkv + static_cast<long long>(blockIdx.x) * ld + static_cast<long long>(h) * hd;
+    const float* w = is_q ? wq : wk;
+    float ss = 0.f;
+    for (int i = threadIdx.x; i < hd; i += blockDim.x) ss += x[i] * x[i];
+    ss = block_sum(ss, red);
+    const float rstd = 1.0f / sqrtf(ss / static_cast<float>(hd) + eps);
+    for (int i = threadIdx.x; i < hd; i += blockDim.x) x[i] = (x[i] * rstd) * w[i];
+}
+
 __global__ void bias_add_kernel(float* x, const float* b, int width, long long total) {
     pdl_wait();
     for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
@@ -221,6 +239,11 @@ l0b_status k_rmsnorm(l0b_device* d, float* x, const float* res, const float* w, 
                      int rows, int add_res) {
     const int threads = width >= 1024 ? 256 : (width >= 256 ? 128 : 32);
     return d->launch(rmsnorm_kernel, dim3(rows), dim3(threads), 0, x, res, w, out, eps, width, add_res);
+}
+
+l0b_status k_head_norm(l0b_device* d, float* qkv, long long ld, int nq, int nk, int hd, const float* wq,
+                       const float* wk, float eps, int rows) {
+    return d->launch(head_norm_kernel, dim3(rows, nq + nk), dim3(32), 0, qkv, ld, nq, hd, wq, wk, eps);
 }
 
 l0b_status k_bias_add(l0b_device* d, float* x, const float* b, int width, int rows) {

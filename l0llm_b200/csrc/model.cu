@@ -467,6 +467,9 @@ l0b_status record_layer_fused(l0b_model* m, int li, int rows, bool decode, int p
     p.eps = c.rms_norm_eps;
     p.seg[0] = {m->qkv, L.qkv_bias, m->qkv_w, m->qkv_w};
     L0B_TRY(gemv(m, L.qkv, p));
+    // QK-norm (Qwen3): each query and key head RMS-normalised in place before RoPE.
+    if (c.qk_norm)
+        L0B_TRY(k_head_norm(m->dev, m->qkv, m->qkv_w, m->nh, m->nkv, m->hd, L.q_norm, L.k_norm, c.rms_norm_eps, rows));
     // 2. Attention.
     AttnParams a = {};
     a.q = m->qkv;
@@ -1020,7 +1023,7 @@ L0B_API l0b_status l0b_model_create(l0b_device* dev, l0b_suite* suite, const l0b
     m->vocab_full = c.vocab_size;
     m->cache_dtype = c.kv_dtype;
     m->softmax_scale = static_cast<float>(1.0 / std::sqrt(static_cast<double>(c.head_dim)));
-    m->fused = !c.qk_norm;
+    m->fused = true;
     m->tp = tp;
     m->tp_rank = tp > 1 ? c.tp_rank : 0;
     m->comm = tp > 1 ? comm : nullptr;
@@ -1661,7 +1664,6 @@ L0B_API l0b_status l0b_model_set_recording(l0b_model* m, int32_t enabled) {
 
 L0B_API l0b_status l0b_model_set_fused(l0b_model* m, int32_t enabled) {
     L0B_REQUIRE(m, L0B_ERR_ARGUMENT, "model is null");
-    L0B_REQUIRE(!enabled || !m->cfg.qk_norm, L0B_ERR_UNSUPPORTED, "the fused layer has no QK-norm");
     m->fused = enabled != 0;
     return L0B_OK;
 }

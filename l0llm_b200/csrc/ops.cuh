@@ -11,6 +11,10 @@ l0b_status k_rmsnorm(l0b_device* d, float* x, const float* res, const float* w, 
                      int rows, int add_res);
 l0b_status k_bias_add(l0b_device* d, float* x, const float* b, int width, int rows);
 // q_stride / k_stride / in_stride: elements between tokens (<= 0: packed rows).
+// RMSNorm of every head of the nq query and nk key heads of `rows` stacked q|k|v rows (row stride ld), in
+// place, with the query / key norm weights.
+l0b_status k_head_norm(l0b_device* d, float* qkv, long long ld, int nq, int nk, int hd, const float* wq,
+                       const float* wk, float eps, int rows);
 l0b_status k_rope(l0b_device* d, float* q, float* k, const int* positions, const float* inv_freq, int hd, int nh,
                   int nkv, float attn_scale, int rot, int tokens, long long q_stride = 0, long long k_stride = 0);
 l0b_status k_kv_store(l0b_device* d, const float* k, const float* v, void* kc, void* vc, int cache_dtype, int pos0,

@@ -53,8 +53,6 @@ def max_diff(a, b):
 @pytest.mark.parametrize("fused", [True, False])
 @pytest.mark.parametrize("name", sorted(hf_tiny.TINY))
 def test_logits_and_greedy_match_transformers(lz, device, suite, name, fused):
-    if fused and hf_tiny.TINY[name]["qk_norm"]:
-        pytest.skip("QK-norm layers run the reference op sequence")
     seed, prompt, logits_hf, greedy_hf = hf_golden(name)
     with make_model(lz, device, suite, name) as model:
         model.set_fused(fused)
@@ -170,11 +168,13 @@ def test_device_greedy_matches_host_greedy_and_reuses_one_graph(lz, device, suit
         assert model.Position == len(prompt) + 23
 
 
-def test_fused_and_reference_sequence_agree(lz, device, suite):
-    _, prompt, _, _ = hf_golden("qwen2")
+@pytest.mark.parametrize("name", ["qwen2", "qwen3"])
+def test_fused_and_reference_sequence_agree(lz, device, suite, name):
+    """The fused decoder layer against the one-op-per-reference-call sequence (qwen3: with QK-norm)."""
+    _, prompt, _, _ = hf_golden(name)
     outs = []
     for fused in (True, False):
-        with make_model(lz, device, suite, "qwen2", "int8", "f16") as model:
+        with make_model(lz, device, suite, name, "int8", "f16") as model:
             model.set_fused(fused)
             outs.append((model.Prefill(prompt), model.Decode(7), model.GenerateGreedy(prompt, 10)))
     assert max_diff(outs[0][0], outs[1][0]) < 1e-3
