@@ -489,6 +489,10 @@ L0B_API l0b_status l0b_set_gemv_bulk_short_rows(int32_t enable);
  * adds exact int64 row sums; the last CTA of a group runs the epilogue) or on the bulk / register GEMVs
  * (0). Affects launches made after the call. No counterpart in the reference. */
 L0B_API l0b_status l0b_set_gemv_ksplit(int32_t enable);
+/* Tuning: stages (32 KB each, 2..6, default 4) of the k-split GEMV's bulk-copy ring. Fewer stages leave
+ * room on an SM for the next kernel's CTAs to start early (config 2 bs1: 6 stages 448, 4 stages 453, 2
+ * stages 446 tok/s). Affects launches made after the call. No counterpart in the reference. */
+L0B_API l0b_status l0b_set_gemv_ksplit_stages(int32_t stages);
 /* Layout of the int8 weights of models created after the call: with blocking on (1, default), int8
  * projections with one scale per row, K % 512 == 0, N % 16 == 0 and fewer than 8 tiles of 16 rows per
  * SM (q/k/v, o_proj, down at Qwen2.5-7B widths) are stored as [N/16][K/512][16][512] bytes, so the k

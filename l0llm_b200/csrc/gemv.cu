@@ -1079,6 +1079,7 @@ bool g_gemv_bulk = true;  // the bulk-copy one-row kernel where it applies (l0b_
 int g_gemv_fill_split = 2;  // largest split-K taken only to fill idle SMs (l0b_set_gemv_fill_split)
 bool g_gemv_bulk_short = false;  // blocked projections with short rows on the bulk GEMV too
 bool g_gemv_ksplit = true;  // blocked one-row int8 projections on the k-split GEMV (l0b_set_gemv_ksplit)
+int g_ksplit_stages = 4;     // stages of the k-split GEMV's ring (l0b_set_gemv_ksplit_stages)
 
 template <typename F, typename... A>
 l0b_status launch_on(l0b_device* dev, cudaStream_t stream, F kernel, dim3 g, dim3 b, size_t smem, A... args) {
@@ -1785,7 +1786,7 @@ l0b_status launch_ksplit(l0b_device* dev, cudaStream_t stream, int sm_count, con
         configured = true;
     }
     const int nb = p.K / kWeightBlock;
-    int stages = kKsMaxStages;
+    int stages = g_ksplit_stages;
     while (stages > 2 && 1024 + 2048 + static_cast<size_t>(stages) * kKsStageBytes + 2 * kKsMaxStages * 8 >
                              static_cast<size_t>(kBulkSmemBudget))
         --stages;
@@ -2087,6 +2088,7 @@ void gemv_set_tensor_cores(bool on) { g_gemv_mma = on; }
 void gemv_set_bulk(bool on) { g_gemv_bulk = on; }
 void gemv_set_bulk_short_rows(bool on) { g_gemv_bulk_short = on; }
 void gemv_set_ksplit(bool on) { g_gemv_ksplit = on; }
+void gemv_set_ksplit_stages(int s) { g_ksplit_stages = s < 2 ? 2 : (s > kKsMaxStages ? kKsMaxStages : s); }
 void gemv_set_fill_split(int s) { g_gemv_fill_split = s <= 1 ? 1 : (s >= 8 ? 8 : (s >= 4 ? 4 : 2)); }
 
 namespace {

@@ -102,6 +102,7 @@ void gemv_set_bulk(bool on);
 void gemv_set_fill_split(int s);
 void gemv_set_bulk_short_rows(bool on);
 void gemv_set_ksplit(bool on);
+void gemv_set_ksplit_stages(int s);
 // Process-wide: models created afterwards store their int8 per-row-scaled projections with few row
 // tiles in the blocked layout (default on).
 bool weight_blocking();

@@ -676,6 +676,11 @@ L0B_API l0b_status l0b_set_gemv_ksplit(int32_t enable) {
     return L0B_OK;
 }
 
+L0B_API l0b_status l0b_set_gemv_ksplit_stages(int32_t stages) {
+    gemv_set_ksplit_stages(stages);
+    return L0B_OK;
+}
+
 L0B_API l0b_status l0b_set_gemv_bulk_short_rows(int32_t enable) {
     gemv_set_bulk_short_rows(enable != 0);
     return L0B_OK;
