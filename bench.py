@@ -9,8 +9,9 @@ fp16 KV cache. Weights are 7.07 GB per step, far larger than the 126 MB L2, so n
           K steps replay one cached CUDA graph; timed with CUDA events on the model's stream.
   e2e     the same decode through the public C-ABI call (LlmModel.Decode): per step the token id and
           position go host->device and the full vocab logits come back device->host, argmax on the host.
-  roofline  the dominant kernel (the fused RMSNorm + gate/up int8 GEMV + SwiGLU of one layer, 2/3 of
-          the weight bytes), launched on its own over 4 rotating weight copies and timed with events.
+  roofline  the dominant kernel by device time (the k-split int8 GEMV of q/k/v, o_proj and down), each
+          projection launched on its own over rotating weight copies (more than L2) and timed with events;
+          by_launch adds each projection and the bulk GEMV's gate/up (with ncu DRAM traffic).
   cpu_baseline  the CPU oracle port (C, fp32 AVX2 FMA, OpenMP) of the same decoder and weights on the
           host cores at the same 512-token context (all threads, plus a single-thread figure).
   step_roofline  all bytes of a step (weights + KV) over the step time.
@@ -270,47 +271,93 @@ def run_reference(args) -> int:
 # GPU
 # ------------------------------------------------------------------------------------------------
 
-def dominant_kernel_roofline(lz, dev, suite, stream_ptr, torch, peak: float, peak_kind: str, bulk: bool = True) -> dict:
-    """The fused RMSNorm + [gate; up] int8 GEMV + SwiGLU of config 2 (gemv_bulk_kernel), over 4 rotating
-    weight copies."""
-    H, I = 3584, 18944
-    N = 2 * I
-    copies = 4
-    rng = np.random.default_rng(5)
-    qs, ss = [], []
-    for _ in range(copies):
-        qs.append(lz.SharedBuffer.from_array(dev, rng.integers(-127, 128, (N, H), dtype=np.int8)))
-        ss.append(lz.SharedBuffer.from_array(dev, rng.uniform(1e-3, 2e-2, N).astype(np.float16)))
-    x = lz.SharedBuffer.from_array(dev, rng.standard_normal(H).astype(np.float32))
-    nw = lz.SharedBuffer.from_array(dev, np.ones(H, np.float32))
-    out = lz.SharedBuffer(dev, lz.F32, I)
+def _time_projection(lz, dev, suite, stream_ptr, torch, n: int, k: int, epi: int, norm: bool, bias: bool,
+                     blocked: bool, copies: int, reps: int = 25) -> tuple[float, int]:
+    """One config-2 decode projection (int8, one f16 scale per row, one activation row) launched on its
+    own through l0b_linear_fused, cycling over `copies` weight copies (more than L2 holds) so every launch
+    streams its weights from HBM; CUDA events on the library's stream. Returns (average ms per launch,
+    algorithmic bytes per launch: weights + scales + x (+ norm weight, bias) + output (read and written
+    for the residual add))."""
+    rng = np.random.default_rng(5 + n + k)
+    q = rng.integers(-127, 128, (n, k), dtype=np.int8)
+    if blocked:
+        q = lz.block_int8(q)
+    s = rng.uniform(1e-3, 2e-2, n).astype(np.float16)
+    ws = [lz.SharedBuffer.from_array(dev, q) for _ in range(copies)]
+    sb = lz.SharedBuffer.from_array(dev, s)
+    x = lz.SharedBuffer.from_array(dev, rng.standard_normal(k).astype(np.float32))
+    nw = lz.SharedBuffer.from_array(dev, np.ones(k, np.float32)) if norm else None
+    bb = lz.SharedBuffer.from_array(dev, np.zeros(n, np.float32)) if bias else None
+    out_cols = n // 2 if epi == suite.EPI_SWIGLU else n
+    out = lz.SharedBuffer.from_array(dev, np.zeros(out_cols, np.float32))
+    flag = epi | (suite.EPI_BLOCKED_WEIGHTS if blocked else 0)
     stream = torch.cuda.ExternalStream(stream_ptr)
-    reps = 25
-    for i in range(8):
-        suite.linear_fused(dev, 1, N, H, x, qs[i % copies], ss[i % copies], H, nw, 1e-6, suite.EPI_SWIGLU, None, out)
+
+    def launch(i):
+        suite.linear_fused(dev, 1, n, k, x, ws[i % copies], sb, k, nw, 1e-6, flag, bb, out)
+
+    for i in range(2 * copies):
+        launch(i)
     dev.Synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     for i in range(reps * copies):
-        suite.linear_fused(dev, 1, N, H, x, qs[i % copies], ss[i % copies], H, nw, 1e-6, suite.EPI_SWIGLU, None, out)
+        launch(i)
     e1.record(stream)
     e1.synchronize()
     avg_ms = e0.elapsed_time(e1) / (reps * copies)
-    bytes_per_launch = N * H + N * 2 + H * 4 + H * 4 + I * 4
-    achieved = bytes_per_launch / (avg_ms * 1e-3) / 1e9
-    traffic = None
-    tf = ROOT / "profiles" / "gemv_i8_swiglu_cfg2.traffic.json"
-    if tf.exists() and bulk:
-        traffic = json.loads(tf.read_text()).get("dram_bytes_per_launch")
-    for b in qs + ss + [x, nw, out]:
-        b.Dispose()
-    name = ("gemv_bulk_kernel (int8 [gate;up] 37888x3584: whole 16-row tiles by bulk copy, RMSNorm prologue, "
-            "integer mma.sync m16n8k32 on int8 digits, SwiGLU epilogue)" if bulk else
-            "gemv_mma_kernel<int8> (register-streamed; RMSNorm prologue + [gate;up] 37888x3584 mma.sync + SwiGLU)")
-    return {"kernel": name,
-            "bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
-            "frac": round(achieved / peak, 4), "traffic": traffic, "algorithmic_bytes": bytes_per_launch,
-            "avg_us": round(avg_ms * 1e3, 2)}
+    for b in ws + [sb, x, nw, bb, out]:
+        if b is not None:
+            b.Dispose()
+    nbytes = n * k + 2 * n + 4 * k + (4 * k if norm else 0) + (4 * n if bias else 0) + \
+        4 * out_cols * (2 if epi == suite.EPI_ACCUM else 1)
+    return avg_ms, nbytes
+
+
+def _traffic(name: str):
+    tf = ROOT / "profiles" / name
+    if tf.exists():
+        return json.loads(tf.read_text()).get("dram_bytes_per_launch")
+    return None
+
+
+def dominant_kernel_roofline(lz, dev, suite, stream_ptr, torch, peak: float, peak_kind: str, bulk: bool = True) -> dict:
+    """The step's dominant kernel by device time (profiles/decode_step_cfg2_launches.md: gemv_ksplit_kernel,
+    50% of the bs1 step -- q/k/v, o_proj and down of every layer -- ahead of gemv_bulk_kernel, 39%: gate/up
+    and the LM head). Each config-2 projection runs on its own over rotating weight copies (more than L2);
+    `achieved` is the k-split kernel's average launch over one layer's mix (one q/k/v, one o_proj, one
+    down): their algorithmic bytes over their summed durations. `by_launch` gives each projection, and the
+    bulk kernel's gate/up, on its own with the DRAM traffic of its ncu capture where one exists."""
+    H, I, QKV = 3584, 18944, 4608
+    cases = {
+        # name: (n, k, epilogue, norm, bias, blocked, copies)
+        "qkv": (QKV, H, suite.EPI_STORE, True, True, True, 12),
+        "o_proj": (H, H, suite.EPI_ACCUM, False, False, True, 16),
+        "down": (H, I, suite.EPI_ACCUM, False, False, True, 4),
+        "gate_up": (2 * I, H, suite.EPI_SWIGLU, True, False, False, 4),
+    }
+    by = {}
+    for name, (n, k, epi, norm, bias, blocked, copies) in cases.items():
+        ms, nbytes = _time_projection(lz, dev, suite, stream_ptr, torch, n, k, epi, norm, bias, blocked, copies)
+        gbs = nbytes / (ms * 1e-3) / 1e9
+        by[name] = {"kernel": ("gemv_bulk_kernel" if bulk else "gemv_mma_kernel<int8>") if name == "gate_up" else
+                    "gemv_ksplit_kernel",
+                    "shape": f"int8 [{n}, {k}]" + (" blocked" if blocked else " row-major"),
+                    "avg_us": round(ms * 1e3, 2), "algorithmic_bytes": nbytes, "achieved": round(gbs, 1),
+                    "frac": round(gbs / peak, 4)}
+    by["down"]["traffic"] = _traffic("gemv_ksplit_i8_down_cfg2.traffic.json")
+    by["gate_up"]["traffic"] = _traffic("gemv_i8_swiglu_cfg2.traffic.json") if bulk else None
+    mix = ("qkv", "o_proj", "down")
+    nbytes = sum(by[c]["algorithmic_bytes"] for c in mix)
+    us = sum(by[c]["avg_us"] for c in mix)
+    achieved = nbytes / (us * 1e-6) / 1e9
+    name = ("gemv_ksplit_kernel (int8 blocked [N/16][K/512][16][512]; one 512-k block of a group of row tiles per "
+            "CTA, bulk copies, integer mma.sync m16n8k32 on int8 digits, exact int64 row sums): q/k/v + o_proj + "
+            "down of one layer")
+    return {"kernel": name, "bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "peak_kind": peak_kind,
+            "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": None,
+            "traffic_note": "measured per launch for the down projection only (by_launch.down.traffic)",
+            "algorithmic_bytes": nbytes // 3, "avg_us": round(us / 3, 2), "by_launch": by}
 
 
 def measure_cfg0(lz, dev, suite, stream_ptr, torch, peak: float, peak_kind: str, tflops_peak: float) -> dict:

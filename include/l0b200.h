@@ -406,7 +406,14 @@ typedef enum l0b_epilogue {
     /* l0b_linear_tc only, OR'ed into the epilogue: the x rows enter as hi + lo 16-bit halves (each row
      * scaled by a power of two for f16's range) so the products keep about f32 activation precision,
      * at twice the tensor-core work; the mode the model's prefill uses. */
-    L0B_EPI_F32_ACTIVATIONS = 0x100
+    L0B_EPI_F32_ACTIVATIONS = 0x100,
+    /* l0b_linear_fused only, OR'ed into the epilogue: W is int8 with one f16 scale per row (group = K)
+     * stored in the blocked layout [N/16][K/512][16][512] bytes (N % 16 == 0, K % 512 == 0) -- the
+     * 16 rows x 512 k of one (row tile, k block) are one contiguous 8 KB block, the layout a model keeps
+     * its q/k/v, o_proj and down projections in. One activation row runs on the k-split GEMV (each CTA
+     * one k block of a group of row tiles, exact integer row sums in the suite's scratch); more rows on
+     * the tensor-core GEMV with blocked addressing. N <= 65536. */
+    L0B_EPI_BLOCKED_WEIGHTS = 0x200
 } l0b_epilogue;
 
 /* Fused linear layer of the decode path: optional RMSNorm of each x row with norm_w (eps) as the

@@ -43,6 +43,7 @@ l0b_suite::~l0b_suite() {
     if (split_part) cudaFree(split_part);
     if (gdn_rec) cudaFree(gdn_rec);
     if (split_counters) cudaFree(split_counters);
+    if (ks_acc) cudaFree(ks_acc);
 }
 
 namespace {
@@ -99,6 +100,8 @@ L0B_API l0b_status l0b_suite_create(l0b_device* dev, l0b_suite** out) {
     L0B_CHECK_CUDA(cudaMalloc(&s->split_part, sizeof(float) * 64 * kSuiteSplitTiles));
     L0B_CHECK_CUDA(cudaMalloc(&s->split_counters, sizeof(unsigned) * kSuiteSplitTiles));
     L0B_CHECK_CUDA(cudaMemsetAsync(s->split_counters, 0, sizeof(unsigned) * kSuiteSplitTiles, dev->stream));
+    L0B_CHECK_CUDA(cudaMalloc(&s->ks_acc, sizeof(long long) * kSuiteKsRows));
+    L0B_CHECK_CUDA(cudaMemsetAsync(s->ks_acc, 0, sizeof(long long) * kSuiteKsRows, dev->stream));
     L0B_CHECK_CUDA(cudaStreamSynchronize(dev->stream));
     *out = s.release();
     return L0B_OK;
@@ -536,6 +539,8 @@ L0B_API l0b_status l0b_linear_fused(l0b_suite* s, l0b_device* d, int32_t m, int3
                                     int32_t epilogue, l0b_buffer* bias, l0b_buffer* out) {
     L0B_TRY(check_suite(s, d));
     L0B_REQUIRE(m > 0 && n > 0 && k > 0, L0B_ERR_OUT_OF_RANGE, "shape M=%d N=%d K=%d", m, n, k);
+    const bool blocked = (epilogue & L0B_EPI_BLOCKED_WEIGHTS) != 0;
+    epilogue &= ~L0B_EPI_BLOCKED_WEIGHTS;
     L0B_REQUIRE(epilogue >= L0B_EPI_STORE && epilogue <= L0B_EPI_SWIGLU, L0B_ERR_ARGUMENT, "epilogue %d", epilogue);
     L0B_REQUIRE(epilogue != L0B_EPI_SWIGLU || n % 2 == 0, L0B_ERR_ARGUMENT, "SwiGLU needs an even N");
     L0B_REQUIRE(epilogue != L0B_EPI_SWIGLU || !bias, L0B_ERR_ARGUMENT, "the SwiGLU epilogue takes no bias");
@@ -551,6 +556,15 @@ L0B_API l0b_status l0b_linear_fused(l0b_suite* s, l0b_device* d, int32_t m, int3
         if (group <= 0) group = k;
         L0B_REQUIRE(k % group == 0, L0B_ERR_ARGUMENT, "group %d does not divide K %d", group, k);
         L0B_TRY(need(scales, "scales", L0B_F16, nk / group));
+    }
+    if (blocked) {
+        L0B_REQUIRE(wdt == L0B_I8 && group >= k, L0B_ERR_ARGUMENT,
+                    "blocked weights must be int8 with one scale per row");
+        L0B_REQUIRE(n % 16 == 0 && k % kWeightBlock == 0, L0B_ERR_ARGUMENT,
+                    "blocked weights need N %% 16 == 0 and K %% %d == 0 (N=%d K=%d)", kWeightBlock, n, k);
+        L0B_REQUIRE(n <= kSuiteKsRows, L0B_ERR_OUT_OF_RANGE, "blocked weights with N=%d > %d rows", n, kSuiteKsRows);
+        L0B_REQUIRE(epilogue != L0B_EPI_SWIGLU || (n / 2) % 16 == 0, L0B_ERR_ARGUMENT,
+                    "blocked [gate; up] needs N/2 %% 16 == 0");
     }
     if (norm_w) L0B_TRY(need(norm_w, "norm_w", L0B_F32, k));
     if (bias) L0B_TRY(need(bias, "bias", L0B_F32, out_cols));
@@ -577,6 +591,11 @@ L0B_API l0b_status l0b_linear_fused(l0b_suite* s, l0b_device* d, int32_t m, int3
     p.part = s->split_part;
     p.counters = s->split_counters;
     p.counter_count = kSuiteSplitTiles;
+    if (blocked) {
+        p.kb = kWeightBlock;
+        p.acc = s->ks_acc;
+        p.acc_count = kSuiteKsRows;
+    }
     return gemv_nk_launch(d, wdt, p);
 }
 

@@ -13,6 +13,8 @@ constexpr int kMaxRows = 64;
 constexpr int kPrefillRows = 512;
 // 16-row tiles the suite's split-K GEMV scratch covers (N <= 65536 output rows).
 constexpr int kSuiteSplitTiles = 4096;
+// Output rows the suite's k-split GEMV row sums cover (l0b_linear_fused over blocked int8 weights).
+constexpr int kSuiteKsRows = 16 * kSuiteSplitTiles;
 }  // namespace l0b
 
 struct l0b_suite {
@@ -28,6 +30,9 @@ struct l0b_suite {
     long long gdn_floats = 0;
     float* split_part = nullptr;
     unsigned* split_counters = nullptr;
+    // Exact int64 row sums of the k-split GEMV [kSuiteKsRows], zero at rest (every launch leaves them
+    // zero); its tile-group counters are split_counters.
+    long long* ks_acc = nullptr;
     std::map<std::pair<int, double>, float*> rope_tables;
     ~l0b_suite();
 };

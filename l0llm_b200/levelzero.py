@@ -593,6 +593,7 @@ class LlmKernelSuite:
 
     EPI_STORE, EPI_ACCUM, EPI_SWIGLU = 0, 1, 2
     EPI_F32_ACTIVATIONS = 0x100  # linear_tc only: x enters as hi + lo 16-bit halves
+    EPI_BLOCKED_WEIGHTS = 0x200  # linear_fused only: int8 W (one scale per row) in the blocked layout
 
     def linear_fused(self, dev, M, N, K, x, W, scales, group, norm_w, eps, epilogue, bias, out):
         """RMSNorm prologue (norm_w) + projection + store / residual-add / SwiGLU epilogue, one kernel."""
@@ -609,6 +610,20 @@ class LlmKernelSuite:
 
     def __exit__(self, *exc):
         self.Dispose()
+
+
+WEIGHT_BLOCK = 512  # k per block of the blocked int8 layout
+
+
+def block_int8(q: np.ndarray) -> np.ndarray:
+    """Row-major int8 [N, K] -> the blocked layout [N/16][K/512][16][512] that models keep their q/k/v,
+    o_proj and down projections in (the bytes of one 16-row x 512-k block are contiguous). N % 16 == 0 and
+    K % 512 == 0. For LlmKernelSuite.linear_fused with EPI_BLOCKED_WEIGHTS."""
+    n, k = q.shape
+    if n % 16 or k % WEIGHT_BLOCK:
+        raise ValueError(f"blocked layout needs N % 16 == 0 and K % {WEIGHT_BLOCK} == 0, got {n} x {k}")
+    b = q.reshape(n // 16, 16, k // WEIGHT_BLOCK, WEIGHT_BLOCK).transpose(0, 2, 1, 3)
+    return np.ascontiguousarray(b).reshape(n, k)
 
 
 def q8_quantize_out_in(hf: np.ndarray, group: int = 32) -> tuple[np.ndarray, np.ndarray]:

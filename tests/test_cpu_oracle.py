@@ -413,3 +413,20 @@ def test_config2_weights_amplify_rounding(orc):
     err = np.abs(fast.astype(np.float64) - exact)
     assert (err > 1e-2 + 1e-2 * np.abs(exact)).sum() > 0
     assert err.max() <= 1e-2 * np.abs(exact).max()
+
+
+def test_block_int8_matches_blocked_index():
+    """levelzero.block_int8 puts element (r, c) of a row-major int8 [N, K] matrix at byte
+    ((r / 16) * (K / 512) + c / 512) * 16 * 512 + (r % 16) * 512 + c % 512: the blocked layout the
+    library's GEMVs and GEMM address (blocked_index in csrc/gemv.cuh)."""
+    from l0llm_b200 import levelzero as lz
+
+    rng = np.random.default_rng(0)
+    n, k = 48, 1536
+    q = rng.integers(-127, 128, (n, k)).astype(np.int8)
+    b = lz.block_int8(q).reshape(-1)
+    r, c = np.meshgrid(np.arange(n), np.arange(k), indexing="ij")
+    idx = ((r // 16) * (k // 512) + c // 512) * 16 * 512 + (r % 16) * 512 + c % 512
+    assert np.array_equal(b[idx], q)
+    with pytest.raises(ValueError):
+        lz.block_int8(q[:40])

@@ -284,3 +284,56 @@ def test_blocked_layout_set_tensor_round_trip(lz, device, suite):
                                       want["self_attn.o_proj"][0])
         np.testing.assert_array_equal(model.read_weight(0, 3, np.int8, 3584 * 18944).reshape(3584, 18944),
                                       want["mlp.down_proj"][0])
+
+
+@pytest.mark.parametrize("m", [1, 3])
+@pytest.mark.parametrize("case", ["down", "qkv", "gate_up"])
+def test_linear_fused_blocked_weights(lz, orc, device, suite, case, m):
+    """l0b_linear_fused with L0B_EPI_BLOCKED_WEIGHTS: int8 weights handed over in the blocked layout
+    [N/16][K/512][16][512] give the oracle's result for the row-major bytes. One row runs the k-split GEMV
+    (down: 37 k blocks x 4 tile groups, residual add; q/k/v: 7 x 21, RMSNorm prologue + bias; [gate; up]
+    with SwiGLU); three rows the register-streamed GEMV with blocked addressing. Two calls in a row check
+    that the k-split scratch (row sums, group counters) is left at zero."""
+    rng = np.random.default_rng({"down": 11, "qkv": 12, "gate_up": 13}[case] + m)
+    if case == "down":
+        n, k, epi, norm, bias = 3584, 18944, suite.EPI_ACCUM, False, False
+    elif case == "qkv":
+        n, k, epi, norm, bias = 4608, 3584, suite.EPI_STORE, True, True
+    else:
+        n, k, epi, norm, bias = 2 * 1024, 4096, suite.EPI_SWIGLU, True, False
+    q = rng.integers(-127, 128, (n, k)).astype(np.int8)
+    s = rng.uniform(1e-3, 2e-2, n).astype(np.float16)
+    x = rng.standard_normal((m, k)).astype(np.float32)
+    nw = (1 + 0.1 * rng.standard_normal(k)).astype(np.float32)
+    bv = (rng.standard_normal(n) * 0.1).astype(np.float32)
+    xin = orc.rmsnorm(x, nw, 1e-6)[1] if norm else x
+    y = orc.gemv_out_in(xin, q, orc.I8, s.view(np.uint16), k)
+    out_cols = n // 2 if epi == suite.EPI_SWIGLU else n
+    base = rng.standard_normal((m, out_cols)).astype(np.float32)
+    if epi == suite.EPI_ACCUM:
+        want = base + y
+    elif epi == suite.EPI_SWIGLU:
+        g, u = y[:, :n // 2], y[:, n // 2:]
+        want = g / (1 + np.exp(-g.astype(np.float64))) * u
+    else:
+        want = y + (bv if bias else 0)
+    with lz.SharedBuffer.from_array(device, lz.block_int8(q)) as W, lz.SharedBuffer.from_array(device, s) as S, \
+            lz.SharedBuffer.from_array(device, x) as xb, lz.SharedBuffer.from_array(device, nw) as nb, \
+            lz.SharedBuffer.from_array(device, bv) as bb, lz.SharedBuffer(device, lz.F32, m * out_cols) as ob:
+        for _ in range(2):
+            ob.Write(base.reshape(-1))
+            suite.linear_fused(device, m, n, k, xb, W, S, k, nb if norm else None, 1e-6,
+                               epi | suite.EPI_BLOCKED_WEIGHTS, bb if bias else None, ob)
+            got = ob.ToArray().reshape(m, out_cols)
+            err = np.abs(got - want)
+            scale = np.abs(want).max()
+            assert np.all(err <= 2e-5 * scale + 1e-5 * np.abs(want)), f"{case} m={m}: max err {err.max()} ({scale})"
+
+
+def test_linear_fused_blocked_weights_rejects_bad_shapes(lz, device, suite):
+    """The blocked flag needs int8 with one scale per row, N % 16 == 0 and K % 512 == 0."""
+    with lz.SharedBuffer(device, lz.I8, 40 * 512) as W, lz.SharedBuffer(device, lz.F16, 40) as S, \
+            lz.SharedBuffer(device, lz.F32, 512) as xb, lz.SharedBuffer(device, lz.F32, 40) as ob:
+        with pytest.raises(lz.ArgumentException):
+            suite.linear_fused(device, 1, 40, 512, xb, W, S, 512, None, 0.0,
+                               suite.EPI_STORE | suite.EPI_BLOCKED_WEIGHTS, None, ob)
