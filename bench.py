@@ -445,8 +445,9 @@ def measure_cfg3(lz, dev, suite, stream_ptr, torch, warmup: int) -> dict:
     """Config 3: one Gated DeltaNet layer (Qwen3.5 shape, bf16 projections) driven through the library's
     ops as LlmDecoderLayer.MixLinear calls them: in_proj (q, k, v | z) and (b | a) projections, causal
     conv + SiLU, the gated delta recurrence with its gated RMSNorm, out_proj. Decode: one token per
-    step for bs sequences (projections, conv and recurrence each one launch over all rows), one recorded
-    command list per step. Prefill: 4096 tokens, projections on the tcgen05 GEMM, the recurrence chunked."""
+    step for bs sequences (the four in-projections one shared launch, conv and recurrence each one launch
+    over all rows), one recorded command list per step. Prefill: 4096 tokens, projections on the tcgen05
+    GEMM, the recurrence chunked."""
     H, HK, HV, DK, DV, KC, T = 2048, 16, 32, 128, 128, 4, 4096
     CONV = 2 * HK * DK + HV * DV
     ZD = HV * DV
@@ -468,8 +469,14 @@ def measure_cfg3(lz, dev, suite, stream_ptr, torch, warmup: int) -> dict:
         owned.append(lz.SharedBuffer(dev, lz.F32, n))
         return owned[-1]
 
-    w_qkv, w_z, w_b, w_a, w_o = bf16((CONV, H), 0.02), bf16((ZD, H), 0.02), bf16((HV, H), 0.02), \
-        bf16((HV, H), 0.02), bf16((H, ZD), 0.02)
+    # The in-projections [qkv; z; b; a] stacked in one matrix (ProjectShared: one launch streams it once);
+    # views of it serve the per-projection prefill GEMMs.
+    IN_ROWS = [CONV, ZD, HV, HV]
+    w_in = bf16((sum(IN_ROWS), H), 0.02)
+    offs = np.cumsum([0] + IN_ROWS) * H
+    w_qkv, w_z, w_b, w_a = (w_in.View(int(offs[i]), IN_ROWS[i] * H) for i in range(4))
+    owned.extend([w_qkv, w_z, w_b, w_a])
+    w_o = bf16((H, ZD), 0.02)
     conv_w = f32(rng.standard_normal((CONV, KC)) * 0.3)
     a_log = f32(np.log(rng.uniform(1, 16, HV)))
     dt_bias = f32(rng.standard_normal(HV) * 0.1)
@@ -500,10 +507,8 @@ def measure_cfg3(lz, dev, suite, stream_ptr, torch, warmup: int) -> dict:
 
         def step():
             dev.BeginRecording()
-            suite.linear(dev, bs, CONV, H, buf["x"], w_qkv, None, 0, None, buf["qkv"])
-            suite.linear(dev, bs, ZD, H, buf["x"], w_z, None, 0, None, buf["z"])
-            suite.linear(dev, bs, HV, H, buf["x"], w_b, None, 0, None, buf["b"])
-            suite.linear(dev, bs, HV, H, buf["x"], w_a, None, 0, None, buf["a"])
+            suite.linear_shared(dev, bs, H, buf["x"], w_in, None, 0, IN_ROWS,
+                                [buf["qkv"], buf["z"], buf["b"], buf["a"]])
             suite.CausalConv.ExecuteBatch(dev, buf["qkv"], conv_states, conv_w, buf["conv"], CONV, KC, bs)
             suite.GatedDelta.ExecuteBatch(dev, buf["conv"], buf["z"], buf["b"], buf["a"], a_log, dt_bias, norm_w,
                                           states, buf["o"], HK, HV, DK, DV, bs, 1e-6)
@@ -536,7 +541,7 @@ def measure_cfg3(lz, dev, suite, stream_ptr, torch, warmup: int) -> dict:
         1e-6), 3)
     phases["out_proj"] = timed(lambda: tc(T, H, ZD, pre["o"], w_o, pre["y"]), 3)
     total = sum(phases.values())
-    for bb in owned:
+    for bb in reversed(owned):  # views before the buffer they view
         bb.Dispose()
     return {"decode": results, "prefill_4096_ms": {k: round(v, 3) for k, v in phases.items()} | {"total": round(total, 3)},
             "config": "config 3: Gated DeltaNet layer alone, hidden 2048, 16 key / 32 value heads of 128, conv 4, "

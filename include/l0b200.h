@@ -399,6 +399,16 @@ L0B_API l0b_status l0b_linear(l0b_suite* s, l0b_device* d, int32_t m, int32_t n,
                               l0b_buffer* w, l0b_buffer* scales, int32_t group, l0b_buffer* bias,
                               l0b_buffer* y);
 
+/* LlmMatrix.ProjectShared(dev, suite, rows, x, W1, y1, ..., W4, y4) -- L/LlmMatrix.cs:177-218 -- for up
+ * to four projections of the same x whose weights are stored stacked in one matrix W = [W1; W2; ...]
+ * ([out, in] order, sum(seg_rows) rows; int8 with scales stacked the same way): one launch streams W
+ * once and writes Y_i [m, seg_rows[i]] (+ biases[i] f32 when biases and biases[i] are non-null). The
+ * outputs share one dtype (f32/f16/bf16). Gated DeltaNet's in-projections (qkv, z, b, a) and the
+ * attention's q/k/v are the reference's uses. */
+L0B_API l0b_status l0b_linear_shared(l0b_suite* s, l0b_device* d, int32_t m, int32_t k, l0b_buffer* x,
+                                     l0b_buffer* w, l0b_buffer* scales, int32_t group, int32_t nseg,
+                                     const int32_t* seg_rows, l0b_buffer* const* biases, l0b_buffer* const* outs);
+
 typedef enum l0b_epilogue {
     L0B_EPI_STORE = 0,  /* out[m, n] = y[m, n] (+ bias) */
     L0B_EPI_ACCUM = 1,  /* out[m, n] += y[m, n] (+ bias): the residual add of o_proj / down_proj */
@@ -500,6 +510,13 @@ L0B_API l0b_status l0b_set_gemv_ksplit(int32_t enable);
  * room on an SM for the next kernel's CTAs to start early (config 2 bs1: 6 stages 448, 4 stages 453, 2
  * stages 446 tok/s). Affects launches made after the call. No counterpart in the reference. */
 L0B_API l0b_status l0b_set_gemv_ksplit_stages(int32_t stages);
+/* Tuning: L2 prefetch in the one-row decode step of a single-GPU model (0 = off). With gate_up_mb > 0
+ * the k-split GEMVs, whose latency-bound launches leave HBM mostly idle, prefetch constant weights of the
+ * projections that follow into L2 (cp.async.bulk.prefetch.L2): q/k/v prefetches o_proj's weights, o_proj
+ * the first gate_up_mb MB of the [gate; up] weights (half from each), down the next layer's q/k/v.
+ * Results are unchanged (a prefetch only moves data into the cache). Affects steps recorded after the
+ * call. No counterpart in the reference. */
+L0B_API l0b_status l0b_set_l2_prefetch(int32_t gate_up_mb);
 /* Layout of the int8 weights of models created after the call: with blocking on (1, default), int8
  * projections with one scale per row, K % 512 == 0, N % 16 == 0 and fewer than 8 tiles of 16 rows per
  * SM (q/k/v, o_proj, down at Qwen2.5-7B widths) are stored as [N/16][K/512][16][512] bytes, so the k
@@ -597,6 +614,38 @@ L0B_API l0b_status l0b_model_free(l0b_model* model);
  * model keeps its rank's shard. */
 L0B_API l0b_status l0b_model_set_tensor(l0b_model* model, const char* name, const float* data,
                                         int64_t count);
+
+/* Where l0b_model_set_tensor puts checkpoint tensor `name` for rank cfg->tp_rank of cfg->tp_size: the
+ * model's tensor-parallel split as plain host arithmetic (no device, no model), the plan set_tensor
+ * itself follows. Column-split projections (q/k/v by whole heads, gate/up, lm_head) keep output rows
+ * [row0, row0 + rows) of the [full_rows, full_cols] tensor and place them at row dst_row of the rank's
+ * stacked matrix ([q; k; v] or [gate; up]); row-split projections (o_proj, down) keep input columns
+ * [col0, col0 + cols) of every row; a vector keeps elements [col0, col0 + cols) at element dst_row of its
+ * destination (the q/k/v biases follow their projection's rows); norms and the embedding are whole on every
+ * rank. The layout is this backend's; the reference runs one device (L/LlmLayerWeights.cs:110-212 loads the
+ * same names unsplit). Unknown or unused names fail with L0B_ERR_INVALID_DATA, as l0b_model_set_tensor. */
+typedef enum l0b_shard_kind {
+    L0B_SHARD_MATRIX = 0,
+    L0B_SHARD_VECTOR = 1,
+    L0B_SHARD_EMBEDDING = 2
+} l0b_shard_kind;
+typedef enum l0b_shard_slot {
+    /* matrices */
+    L0B_SLOT_QKV = 0, L0B_SLOT_O = 1, L0B_SLOT_GATE_UP = 2, L0B_SLOT_DOWN = 3, L0B_SLOT_LM_HEAD = 4,
+    /* vectors */
+    L0B_SLOT_IN_NORM = 0, L0B_SLOT_POST_NORM = 1, L0B_SLOT_QKV_BIAS = 2, L0B_SLOT_Q_NORM = 3,
+    L0B_SLOT_K_NORM = 4, L0B_SLOT_FINAL_NORM = 5
+} l0b_shard_slot;
+typedef struct l0b_shard_plan {
+    int32_t kind;                 /* l0b_shard_kind */
+    int32_t layer;                /* decoder layer, -1 for model-level tensors */
+    int32_t slot;                 /* l0b_shard_slot of the destination */
+    int32_t full_rows, full_cols; /* the checkpoint tensor ([1, n] for a vector) */
+    int32_t row0, rows;           /* rows kept */
+    int32_t col0, cols;           /* columns (vector: elements) kept */
+    int32_t dst_row;              /* first destination row (vector: element) */
+} l0b_shard_plan;
+L0B_API l0b_status l0b_model_shard_plan(const l0b_model_config* cfg, const char* name, l0b_shard_plan* out);
 /* A checkpoint tensor's raw 16-bit payload (dtype L0B_F16 or L0B_BF16, count values, HF [out, in] order) --
  * the bytes a safetensors F16 / BF16 entry holds -- uploaded as is and widened, range-checked (Float16
  * storage), converted or quantized on the device, with the rules of l0b_model_set_tensor. Replaces the

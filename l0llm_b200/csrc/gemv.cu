@@ -1080,6 +1080,7 @@ int g_gemv_fill_split = 2;  // largest split-K taken only to fill idle SMs (l0b_
 bool g_gemv_bulk_short = false;  // blocked projections with short rows on the bulk GEMV too
 bool g_gemv_ksplit = true;  // blocked one-row int8 projections on the k-split GEMV (l0b_set_gemv_ksplit)
 int g_ksplit_stages = 4;     // stages of the k-split GEMV's ring (l0b_set_gemv_ksplit_stages)
+int g_l2_prefetch_mb = 0;    // gate/up megabytes prefetched into L2 by the decode step (l0b_set_l2_prefetch)
 
 template <typename F, typename... A>
 l0b_status launch_on(l0b_device* dev, cudaStream_t stream, F kernel, dim3 g, dim3 b, size_t smem, A... args) {
@@ -1498,6 +1499,19 @@ constexpr int kKsMaxStages = 6;
 constexpr int kKsBlockBytes = 16 * kWeightBlock;  // one (tile, k block) block
 constexpr int kKsStageBytes = 4 * kKsBlockBytes;
 
+// This CTA's slice of [base, base + bytes) as L2 prefetches of at most 32 KB (16-byte multiples).
+__device__ __forceinline__ void l2_prefetch_slice(const void* base, long long bytes) {
+    if (!base || bytes < 16 || (reinterpret_cast<uintptr_t>(base) & 15)) return;
+    const long long G = gridDim.x, c = blockIdx.x;
+    const long long b0 = (bytes * c / G) & ~15LL;
+    const long long b1 = c + 1 == G ? (bytes & ~15LL) : ((bytes * (c + 1) / G) & ~15LL);
+    for (long long o = b0; o < b1; o += 32768) {
+        const uint32_t n = static_cast<uint32_t>(b1 - o < 32768 ? b1 - o : 32768);
+        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(static_cast<const char*>(base) + o), "r"(n)
+                     : "memory");
+    }
+}
+
 __global__ void __launch_bounds__(kKsThreads, 1) gemv_ksplit_kernel(const GemvParams p, int stages, int groups,
                                                                   int* error) {
     extern __shared__ char ks_smem[];
@@ -1560,6 +1574,11 @@ __global__ void __launch_bounds__(kKsThreads, 1) gemv_ksplit_kernel(const GemvPa
                     bulk_copy(ring + static_cast<size_t>(s) * kKsStageBytes + b * kKsBlockBytes,
                               W + (static_cast<long long>(tile_of(4 * u + b)) * nb + kbi) * kKsBlockBytes, kKsBlockBytes,
                               &full[s]);
+                // Once the first stages are on their way, the later projection's weights go to L2.
+                if (u + 1 == min(stages, nunits)) {
+                    l2_prefetch_slice(p.l2pf[0], p.l2pf_bytes[0]);
+                    l2_prefetch_slice(p.l2pf[1], p.l2pf_bytes[1]);
+                }
             }
         }
         return;
@@ -2088,6 +2107,8 @@ void gemv_set_tensor_cores(bool on) { g_gemv_mma = on; }
 void gemv_set_bulk(bool on) { g_gemv_bulk = on; }
 void gemv_set_bulk_short_rows(bool on) { g_gemv_bulk_short = on; }
 void gemv_set_ksplit(bool on) { g_gemv_ksplit = on; }
+int gemv_l2_prefetch_mb() { return g_l2_prefetch_mb; }
+void gemv_set_l2_prefetch_mb(int mb) { g_l2_prefetch_mb = mb < 0 ? 0 : mb; }
 void gemv_set_ksplit_stages(int s) { g_ksplit_stages = s < 2 ? 2 : (s > kKsMaxStages ? kKsMaxStages : s); }
 void gemv_set_fill_split(int s) { g_gemv_fill_split = s <= 1 ? 1 : (s >= 8 ? 8 : (s >= 4 ? 4 : 2)); }
 

@@ -87,6 +87,12 @@ struct GemvParams {
     // launch leaves them zero), acc_count >= N; the tile-group counters are `counters`.
     long long* acc;
     int acc_count;
+    // L2 prefetch of up to two read-only regions (the weights of a later projection of the step): the
+    // k-split GEMV's producer warps issue cp.async.bulk.prefetch.L2 over them, an even slice per CTA,
+    // after their first stages. Only that kernel issues them; null or 0 bytes = none. The regions must
+    // lie inside allocations and start 16-byte aligned.
+    const void* l2pf[2];
+    long long l2pf_bytes[2];
 };
 
 // Launches y = x * W^T with the fused options in `p` (fills kt and the grid). `w_dtype` is
@@ -103,6 +109,11 @@ void gemv_set_fill_split(int s);
 void gemv_set_bulk_short_rows(bool on);
 void gemv_set_ksplit(bool on);
 void gemv_set_ksplit_stages(int s);
+// Megabytes of the gate/up weights the one-row decode step prefetches into L2 ahead of their projection
+// (the o_proj GEMV issues them; q/k/v also prefetches o_proj's weights and down the next layer's q/k/v);
+// 0 = no prefetch. Process-wide; affects steps recorded afterwards.
+int gemv_l2_prefetch_mb();
+void gemv_set_l2_prefetch_mb(int mb);
 // Process-wide: models created afterwards store their int8 per-row-scaled projections with few row
 // tiles in the blocked layout (default on).
 bool weight_blocking();

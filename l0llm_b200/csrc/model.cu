@@ -461,11 +461,22 @@ l0b_status project_into_residual(l0b_model* m, const ModelMatrix& w, GemvParams 
 l0b_status record_layer_fused(l0b_model* m, int li, int rows, bool decode, int pos0) {
     ModelLayer& L = m->layers[li];
     const l0b_model_config& c = m->cfg;
+    // L2 prefetch plan of the one-row decode step (l0b_set_l2_prefetch): the latency-bound k-split GEMVs
+    // pull the weights of the projections after them into L2 (weights only: a row-major int8 matrix's
+    // bytes, without its scales).
+    const long long pf_gate_up = decode && rows == 1 && !m->comm ? 1048576LL * gemv_l2_prefetch_mb() : 0;
+    auto w_bytes = [](const ModelMatrix& w) {
+        return static_cast<long long>(w.n) * w.k * dtype_size(static_cast<l0b_dtype>(w.dtype));
+    };
     // 1. QKV projection with the input RMSNorm prologue and the bias epilogue.
     GemvParams p = model_linear_params(m, L.qkv, rows, m->hidden, m->h);
     p.norm_w = L.in_norm;
     p.eps = c.rms_norm_eps;
     p.seg[0] = {m->qkv, L.qkv_bias, m->qkv_w, m->qkv_w};
+    if (pf_gate_up > 0) {
+        p.l2pf[0] = L.o.w;
+        p.l2pf_bytes[0] = w_bytes(L.o);
+    }
     L0B_TRY(gemv(m, L.qkv, p));
     // QK-norm (Qwen3): each query and key head RMS-normalised in place before RoPE.
     if (c.qk_norm)
@@ -520,6 +531,15 @@ l0b_status record_layer_fused(l0b_model* m, int li, int rows, bool decode, int p
     if (m->comm) {
         L0B_TRY(project_into_residual(m, L.o, p, rows));
     } else {
+        if (pf_gate_up > 0) {
+            // The first rows of the gate half and of the up half ([gate; up] is stacked row-major).
+            const long long half = w_bytes(L.gate_up) / 2;
+            const long long each = std::min(pf_gate_up / 2, half);
+            p.l2pf[0] = L.gate_up.w;
+            p.l2pf_bytes[0] = each;
+            p.l2pf[1] = static_cast<const char*>(L.gate_up.w) + half;
+            p.l2pf_bytes[1] = each;
+        }
         p.epi = EPI_ACCUM;
         p.seg[0] = {m->hidden, nullptr, m->h, m->h};
         L0B_TRY(gemv(m, L.o, p));
@@ -534,6 +554,10 @@ l0b_status record_layer_fused(l0b_model* m, int li, int rows, bool decode, int p
     // 5. down, added into the residual stream.
     p = model_linear_params(m, L.down, rows, m->act, m->inter);
     if (m->comm) return project_into_residual(m, L.down, p, rows);
+    if (pf_gate_up > 0 && li + 1 < c.num_layers) {
+        p.l2pf[0] = m->layers[li + 1].qkv.w;
+        p.l2pf_bytes[0] = w_bytes(m->layers[li + 1].qkv);
+    }
     p.epi = EPI_ACCUM;
     p.seg[0] = {m->hidden, nullptr, m->h, m->h};
     return gemv(m, L.down, p);
@@ -840,89 +864,137 @@ bool parse_layer(const std::string& name, const std::string& prefix, int* layer,
     return true;
 }
 
-l0b_status resolve(l0b_model* m, const std::string& name, Target* t) {
-    const l0b_model_config& c = m->cfg;
+// Where checkpoint tensor `name` goes for rank c.tp_rank of c.tp_size: pure arithmetic on the config
+// (l0b_model_shard_plan exports it). Column-split projections (q/k/v, gate/up, lm_head) keep whole output
+// rows [row0, row0 + rows) -- q/k/v whole heads, so each rank's query heads keep their KV head -- placed
+// at dst_row of the stacked local matrix; row-split ones (o_proj, down) keep input columns
+// [col0, col0 + cols) of every row; the q/k/v biases follow their projection's rows; norms and the
+// embedding table are replicated. *tkind: the TensorKind of a layer tensor (ids of the synthetic
+// generator), -1 otherwise.
+l0b_status shard_plan(const l0b_model_config& c, const std::string& name, l0b_shard_plan* sp, int* tkind) {
     const int tp = c.tp_size > 1 ? c.tp_size : 1, rank = c.tp_size > 1 ? c.tp_rank : 0;
     const int H = c.hidden_size, I = c.intermediate_size;
     const int QD = c.num_attention_heads * c.head_dim, KD = c.num_key_value_heads * c.head_dim;
+    const int qd = QD / tp, kd = KD / tp, inter = I / tp, vocab = c.vocab_size / tp;
+    *sp = l0b_shard_plan{};
+    *tkind = -1;
+    sp->layer = -1;
+    auto matrix = [&](int slot, int full_rows, int full_cols) {
+        sp->kind = L0B_SHARD_MATRIX;
+        sp->slot = slot;
+        sp->full_rows = full_rows;
+        sp->full_cols = full_cols;
+        sp->rows = full_rows;
+        sp->cols = full_cols;
+    };
+    auto col_split = [&](int slot, int dst_row, int full_rows, int kind) {
+        matrix(slot, full_rows, H);
+        sp->rows = full_rows / tp;
+        sp->row0 = rank * sp->rows;
+        sp->dst_row = dst_row;
+        *tkind = kind;
+    };
+    auto row_split = [&](int slot, int full_cols, int kind) {
+        matrix(slot, H, full_cols);
+        sp->cols = full_cols / tp;
+        sp->col0 = rank * sp->cols;
+        *tkind = kind;
+    };
+    auto vec = [&](int slot, int full, int local, int src_off, int dst_off, int kind) {
+        sp->kind = L0B_SHARD_VECTOR;
+        sp->slot = slot;
+        sp->full_rows = 1;
+        sp->full_cols = full;
+        sp->rows = 1;
+        sp->cols = local;
+        sp->col0 = src_off;
+        sp->dst_row = dst_off;
+        *tkind = kind;
+    };
     if (name == "model.embed_tokens.weight") {
-        t->embed = true;
-        t->full_rows = c.vocab_size;
-        t->full_cols = H;
-        t->id = kIdEmbed;
+        matrix(0, c.vocab_size, H);
+        sp->kind = L0B_SHARD_EMBEDDING;
         return L0B_OK;
     }
     if (name == "model.norm.weight") {
-        t->vec = m->final_norm;
-        t->length = H;
-        t->full_rows = 1;
-        t->full_cols = H;
-        t->id = kIdFinalNorm;
+        vec(L0B_SLOT_FINAL_NORM, H, H, 0, 0, -1);
         return L0B_OK;
     }
     if (name == "lm_head.weight") {
-        t->mat = &m->lm_head;
-        t->full_rows = c.vocab_size;
-        t->full_cols = H;
-        t->row0 = rank * m->vocab;
-        t->rows = m->vocab;
-        t->cols = H;
-        t->id = kIdLmHead;
-        t->scale_id = kIdLmHeadScale;
+        matrix(L0B_SLOT_LM_HEAD, c.vocab_size, H);
+        sp->rows = vocab;
+        sp->row0 = rank * vocab;
         return L0B_OK;
     }
     int li;
     std::string rest;
     if (!parse_layer(name, "model.layers.", &li, &rest) || li < 0 || li >= c.num_layers)
         return fail(L0B_ERR_INVALID_DATA, "unknown tensor '%s'", name.c_str());
-    ModelLayer& L = m->layers[li];
-    auto col_split = [&](ModelMatrix* mat, int dst_row, int full_rows, int kind) {
-        const int local = full_rows / tp;
-        t->mat = mat;
-        t->dst_row = dst_row;
-        t->full_rows = full_rows;
-        t->full_cols = H;
-        t->row0 = rank * local;
-        t->rows = local;
-        t->cols = H;
-        t->id = layer_tensor_id(li, kind);
-        t->scale_id = layer_tensor_id(li, T_SCALE + kind);
-    };
-    auto row_split = [&](ModelMatrix* mat, int full_cols, int kind) {
-        const int local = full_cols / tp;
-        t->mat = mat;
-        t->full_rows = H;
-        t->full_cols = full_cols;
-        t->rows = H;
-        t->col0 = rank * local;
-        t->cols = local;
-        t->id = layer_tensor_id(li, kind);
-        t->scale_id = layer_tensor_id(li, T_SCALE + kind);
-    };
-    auto vec = [&](float* dst, int full, int local, int off, int kind) {
-        t->vec = dst;
-        t->length = local;
-        t->full_rows = 1;
-        t->full_cols = full;
-        t->col0 = off;
-        t->id = layer_tensor_id(li, kind);
-    };
-    if (rest == "input_layernorm.weight") vec(L.in_norm, H, H, 0, T_IN_NORM);
-    else if (rest == "post_attention_layernorm.weight") vec(L.post_norm, H, H, 0, T_POST_NORM);
-    else if (rest == "self_attn.q_proj.weight") col_split(&L.qkv, 0, QD, T_Q);
-    else if (rest == "self_attn.k_proj.weight") col_split(&L.qkv, m->qdim, KD, T_K);
-    else if (rest == "self_attn.v_proj.weight") col_split(&L.qkv, m->qdim + m->kvdim, KD, T_V);
-    else if (rest == "self_attn.o_proj.weight") row_split(&L.o, QD, T_O);
-    else if (rest == "mlp.gate_proj.weight") col_split(&L.gate_up, 0, I, T_GATE);
-    else if (rest == "mlp.up_proj.weight") col_split(&L.gate_up, m->inter, I, T_UP);
-    else if (rest == "mlp.down_proj.weight") row_split(&L.down, I, T_DOWN);
-    else if (rest == "self_attn.q_proj.bias" && L.qkv_bias) vec(L.qkv_bias, QD, m->qdim, rank * m->qdim, T_QB);
-    else if (rest == "self_attn.k_proj.bias" && L.qkv_bias) vec(L.qkv_bias + m->qdim, KD, m->kvdim, rank * m->kvdim, T_KB);
-    else if (rest == "self_attn.v_proj.bias" && L.qkv_bias)
-        vec(L.qkv_bias + m->qdim + m->kvdim, KD, m->kvdim, rank * m->kvdim, T_VB);
-    else if (rest == "self_attn.q_norm.weight" && L.q_norm) vec(L.q_norm, c.head_dim, c.head_dim, 0, T_QN);
-    else if (rest == "self_attn.k_norm.weight" && L.k_norm) vec(L.k_norm, c.head_dim, c.head_dim, 0, T_KN);
+    sp->layer = li;
+    if (rest == "input_layernorm.weight") vec(L0B_SLOT_IN_NORM, H, H, 0, 0, T_IN_NORM);
+    else if (rest == "post_attention_layernorm.weight") vec(L0B_SLOT_POST_NORM, H, H, 0, 0, T_POST_NORM);
+    else if (rest == "self_attn.q_proj.weight") col_split(L0B_SLOT_QKV, 0, QD, T_Q);
+    else if (rest == "self_attn.k_proj.weight") col_split(L0B_SLOT_QKV, qd, KD, T_K);
+    else if (rest == "self_attn.v_proj.weight") col_split(L0B_SLOT_QKV, qd + kd, KD, T_V);
+    else if (rest == "self_attn.o_proj.weight") row_split(L0B_SLOT_O, QD, T_O);
+    else if (rest == "mlp.gate_proj.weight") col_split(L0B_SLOT_GATE_UP, 0, I, T_GATE);
+    else if (rest == "mlp.up_proj.weight") col_split(L0B_SLOT_GATE_UP, inter, I, T_UP);
+    else if (rest == "mlp.down_proj.weight") row_split(L0B_SLOT_DOWN, I, T_DOWN);
+    else if (rest == "self_attn.q_proj.bias" && c.attention_bias) vec(L0B_SLOT_QKV_BIAS, QD, qd, rank * qd, 0, T_QB);
+    else if (rest == "self_attn.k_proj.bias" && c.attention_bias) vec(L0B_SLOT_QKV_BIAS, KD, kd, rank * kd, qd, T_KB);
+    else if (rest == "self_attn.v_proj.bias" && c.attention_bias)
+        vec(L0B_SLOT_QKV_BIAS, KD, kd, rank * kd, qd + kd, T_VB);
+    else if (rest == "self_attn.q_norm.weight" && c.qk_norm) vec(L0B_SLOT_Q_NORM, c.head_dim, c.head_dim, 0, 0, T_QN);
+    else if (rest == "self_attn.k_norm.weight" && c.qk_norm) vec(L0B_SLOT_K_NORM, c.head_dim, c.head_dim, 0, 0, T_KN);
     else return fail(L0B_ERR_INVALID_DATA, "unknown or unused tensor '%s'", name.c_str());
+    return L0B_OK;
+}
+
+// The plan of `name` bound to this model's buffers.
+l0b_status resolve(l0b_model* m, const std::string& name, Target* t) {
+    l0b_shard_plan sp;
+    int kind;
+    L0B_TRY(shard_plan(m->cfg, name, &sp, &kind));
+    t->full_rows = sp.full_rows;
+    t->full_cols = sp.full_cols;
+    if (sp.kind == L0B_SHARD_EMBEDDING) {
+        t->embed = true;
+        t->id = kIdEmbed;
+        return L0B_OK;
+    }
+    if (sp.kind == L0B_SHARD_VECTOR) {
+        float* dst = nullptr;
+        if (sp.slot == L0B_SLOT_FINAL_NORM) {
+            dst = m->final_norm;
+            t->id = kIdFinalNorm;
+        } else {
+            ModelLayer& L = m->layers[sp.layer];
+            dst = sp.slot == L0B_SLOT_IN_NORM ? L.in_norm : sp.slot == L0B_SLOT_POST_NORM ? L.post_norm
+                : sp.slot == L0B_SLOT_QKV_BIAS ? L.qkv_bias : sp.slot == L0B_SLOT_Q_NORM ? L.q_norm : L.k_norm;
+            t->id = layer_tensor_id(sp.layer, kind);
+        }
+        L0B_REQUIRE(dst, L0B_ERR_INVALID_DATA, "unknown or unused tensor '%s'", name.c_str());
+        t->vec = dst + sp.dst_row;
+        t->length = sp.cols;
+        t->col0 = sp.col0;
+        return L0B_OK;
+    }
+    if (sp.slot == L0B_SLOT_LM_HEAD) {
+        t->mat = &m->lm_head;
+        t->id = kIdLmHead;
+        t->scale_id = kIdLmHeadScale;
+    } else {
+        ModelLayer& L = m->layers[sp.layer];
+        t->mat = sp.slot == L0B_SLOT_QKV ? &L.qkv : sp.slot == L0B_SLOT_O ? &L.o
+               : sp.slot == L0B_SLOT_GATE_UP ? &L.gate_up : &L.down;
+        t->id = layer_tensor_id(sp.layer, kind);
+        t->scale_id = layer_tensor_id(sp.layer, T_SCALE + kind);
+    }
+    t->dst_row = sp.dst_row;
+    t->row0 = sp.row0;
+    t->rows = sp.rows;
+    t->col0 = sp.col0;
+    t->cols = sp.cols;
     return L0B_OK;
 }
 
@@ -943,6 +1015,22 @@ l0b_status resolve(l0b_model* m, const std::string& name, Target* t) {
     }
 
 extern "C" {
+
+L0B_API l0b_status l0b_model_shard_plan(const l0b_model_config* cfg, const char* name, l0b_shard_plan* out) {
+    GUARD_BEGIN
+    L0B_REQUIRE(cfg && name && out, L0B_ERR_ARGUMENT, "null argument");
+    const int tp = cfg->tp_size > 1 ? cfg->tp_size : 1;
+    L0B_REQUIRE(tp == 1 || (cfg->tp_rank >= 0 && cfg->tp_rank < tp), L0B_ERR_ARGUMENT, "tp_rank %d of %d",
+                cfg->tp_rank, tp);
+    L0B_REQUIRE(cfg->num_attention_heads > 0 && cfg->num_key_value_heads > 0 && cfg->head_dim > 0 &&
+                    cfg->num_layers > 0 && cfg->hidden_size > 0,
+                L0B_ERR_INVALID_DATA, "head counts, head_dim, layers and hidden size must be positive");
+    L0B_REQUIRE(cfg->num_key_value_heads % tp == 0 && cfg->intermediate_size % tp == 0 && cfg->vocab_size % tp == 0,
+                L0B_ERR_UNSUPPORTED, "kv heads, intermediate size and vocab must divide by tp_size %d", tp);
+    int kind;
+    return shard_plan(*cfg, name, out, &kind);
+    GUARD_END
+}
 
 L0B_API l0b_status l0b_model_config_init(l0b_model_config* c) {
     L0B_REQUIRE(c, L0B_ERR_ARGUMENT, "config is null");

@@ -534,6 +534,58 @@ L0B_API l0b_status l0b_linear(l0b_suite* s, l0b_device* d, int32_t m, int32_t n,
     return gemv_nk_launch(d, wdt, p);
 }
 
+L0B_API l0b_status l0b_linear_shared(l0b_suite* s, l0b_device* d, int32_t m, int32_t k, l0b_buffer* x, l0b_buffer* w,
+                                     l0b_buffer* scales, int32_t group, int32_t nseg, const int32_t* seg_rows,
+                                     l0b_buffer* const* biases, l0b_buffer* const* outs) {
+    L0B_TRY(check_suite(s, d));
+    L0B_REQUIRE(nseg >= 1 && nseg <= 4, L0B_ERR_ARGUMENT, "1..4 projections share x, got %d", nseg);
+    L0B_REQUIRE(seg_rows && outs, L0B_ERR_ARGUMENT, "seg_rows and outs are required");
+    L0B_REQUIRE(m > 0 && k > 0, L0B_ERR_OUT_OF_RANGE, "shape M=%d K=%d", m, k);
+    L0B_TRY(need_float(x, "x", static_cast<long long>(m) * k));
+    L0B_REQUIRE(w, L0B_ERR_ARGUMENT, "W is null");
+    GemvParams p = {};
+    long long n = 0;
+    for (int i = 0; i < nseg; ++i) {
+        L0B_REQUIRE(seg_rows[i] > 0, L0B_ERR_OUT_OF_RANGE, "projection %d has %d rows", i, seg_rows[i]);
+        L0B_TRY(need_float(outs[i], "output", static_cast<long long>(m) * seg_rows[i]));
+        L0B_REQUIRE(outs[i]->dtype == outs[0]->dtype, L0B_ERR_ARGUMENT, "the outputs must share one dtype");
+        l0b_buffer* b = biases ? biases[i] : nullptr;
+        if (b) L0B_TRY(need(b, "bias", L0B_F32, seg_rows[i]));
+        n += seg_rows[i];
+        L0B_REQUIRE(n <= INT32_MAX, L0B_ERR_OUT_OF_RANGE, "stacked rows exceed int32");
+        p.seg[i].out = outs[i]->ptr;
+        p.seg[i].bias = b ? F(b) : nullptr;
+        p.seg[i].row_end = static_cast<int>(n);
+        p.seg[i].ld = seg_rows[i];
+    }
+    const long long nk = n * k;
+    int wdt = w->dtype == L0B_I32 ? L0B_I8 : w->dtype;
+    L0B_REQUIRE(static_cast<long long>(w->bytes()) >= nk * static_cast<long long>(dtype_size((l0b_dtype)wdt)),
+                L0B_ERR_ARGUMENT, "W is smaller than (sum of rows) * K");
+    if (wdt == L0B_I8) {
+        if (group <= 0) group = k;
+        L0B_REQUIRE(k % group == 0, L0B_ERR_ARGUMENT, "group %d does not divide K %d", group, k);
+        L0B_TRY(need(scales, "scales", L0B_F16, nk / group));
+    }
+    p.w = w->ptr;
+    p.scales = scales ? scales->ptr : nullptr;
+    p.group = group;
+    p.N = static_cast<int>(n);
+    p.K = k;
+    p.M = m;
+    p.x = x->ptr;
+    p.x_dtype = x->dtype;
+    p.x_ld = k;
+    p.epi = EPI_STORE;
+    p.out_dtype = outs[0]->dtype;
+    p.nseg = nseg;
+    p.prefetch = 1;
+    p.part = s->split_part;
+    p.counters = s->split_counters;
+    p.counter_count = kSuiteSplitTiles;
+    return gemv_nk_launch(d, wdt, p);
+}
+
 L0B_API l0b_status l0b_linear_fused(l0b_suite* s, l0b_device* d, int32_t m, int32_t n, int32_t k, l0b_buffer* x,
                                     l0b_buffer* w, l0b_buffer* scales, int32_t group, l0b_buffer* norm_w, float eps,
                                     int32_t epilogue, l0b_buffer* bias, l0b_buffer* out) {
@@ -692,6 +744,11 @@ L0B_API l0b_status l0b_set_gemv_bulk(int32_t enable) {
 
 L0B_API l0b_status l0b_set_gemv_ksplit(int32_t enable) {
     gemv_set_ksplit(enable != 0);
+    return L0B_OK;
+}
+
+L0B_API l0b_status l0b_set_l2_prefetch(int32_t gate_up_mb) {
+    gemv_set_l2_prefetch_mb(gate_up_mb);
     return L0B_OK;
 }
 

@@ -181,6 +181,7 @@ def load_library() -> C.CDLL:
         "l0b_set_gemv_bulk_short_rows": (i32, [i32]),
         "l0b_set_gemv_ksplit": (i32, [i32]),
         "l0b_set_gemv_ksplit_stages": (i32, [i32]),
+        "l0b_set_l2_prefetch": (i32, [i32]),
         "l0b_set_attention_cluster16": (i32, [i32]),
         "l0b_set_attention_decode_tensor_cores": (i32, [i32]),
         "l0b_comm_set_fused_allreduce": (i32, [i32]),
@@ -200,6 +201,8 @@ def load_library() -> C.CDLL:
         "l0b_model_sequence_position": (i32, [vp, i32, C.POINTER(i32)]),
         "l0b_attention_decode_noalloc": (i32, [vp, vp, vp, vp, i32, vp, i32, i32, i32, i32, i32]),
         "l0b_model_config_init": (i32, [C.POINTER(ModelConfig)]),
+        "l0b_linear_shared": (i32, [vp, vp, i32, i32, vp, vp, vp, i32, i32, vp, vp, vp]),
+        "l0b_model_shard_plan": (i32, [C.POINTER(ModelConfig), C.c_char_p, vp]),
         "l0b_rope_frequencies": (i32, [C.POINTER(ModelConfig), vp, i32, C.POINTER(i32), C.POINTER(f32)]),
         "l0b_model_create": (i32, [vp, vp, C.POINTER(ModelConfig), i32, i32, vp, pp]),
         "l0b_model_free": (i32, [vp]),
@@ -595,6 +598,15 @@ class LlmKernelSuite:
     EPI_F32_ACTIVATIONS = 0x100  # linear_tc only: x enters as hi + lo 16-bit halves
     EPI_BLOCKED_WEIGHTS = 0x200  # linear_fused only: int8 W (one scale per row) in the blocked layout
 
+    def linear_shared(self, dev, M, K, x, W, scales, group, seg_rows, outs, biases=None):
+        """ProjectShared over stacked weights W = [W1; W2; ...]: one launch, Y_i = X W_i^T (+ b_i)."""
+        n = len(seg_rows)
+        rows = (C.c_int32 * n)(*seg_rows)
+        ob = (C.c_void_p * n)(*[o.handle for o in outs])
+        bb = (C.c_void_p * n)(*[_h(b) for b in biases]) if biases is not None else None
+        check(load_library().l0b_linear_shared(self.handle, dev.handle, M, K, x.handle, W.handle, _h(scales), group,
+                                               n, rows, bb, ob))
+
     def linear_fused(self, dev, M, N, K, x, W, scales, group, norm_w, eps, epilogue, bias, out):
         """RMSNorm prologue (norm_w) + projection + store / residual-add / SwiGLU epilogue, one kernel."""
         check(load_library().l0b_linear_fused(self.handle, dev.handle, M, N, K, x.handle, W.handle, _h(scales),
@@ -662,6 +674,28 @@ def model_config(**kw) -> ModelConfig:
             v = ROPE_TYPES[v]
         setattr(cfg, k, v)
     return cfg
+
+
+class ShardPlan(C.Structure):
+    """l0b_shard_plan: where l0b_model_set_tensor puts one checkpoint tensor on one tensor-parallel rank."""
+    _fields_ = [(n, C.c_int32) for n in ("kind", "layer", "slot", "full_rows", "full_cols", "row0", "rows", "col0",
+                                         "cols", "dst_row")]
+    MATRIX, VECTOR, EMBEDDING = 0, 1, 2
+    QKV, O, GATE_UP, DOWN, LM_HEAD = 0, 1, 2, 3, 4
+    IN_NORM, POST_NORM, QKV_BIAS, Q_NORM, K_NORM, FINAL_NORM = 0, 1, 2, 3, 4, 5
+
+    def take(self, full: np.ndarray) -> np.ndarray:
+        """This rank's part of the full checkpoint tensor (rows x cols of it)."""
+        full = np.asarray(full).reshape(self.full_rows, self.full_cols)
+        return full[self.row0:self.row0 + self.rows, self.col0:self.col0 + self.cols]
+
+
+def shard_plan(cfg: ModelConfig, name: str) -> ShardPlan:
+    """The model's tensor-parallel placement of checkpoint tensor `name` for rank cfg.tp_rank of
+    cfg.tp_size (host arithmetic; no device needed)."""
+    out = ShardPlan()
+    check(load_library().l0b_model_shard_plan(C.byref(cfg), name.encode(), C.byref(out)))
+    return out
 
 
 class Communicator:

@@ -337,3 +337,47 @@ def test_linear_fused_blocked_weights_rejects_bad_shapes(lz, device, suite):
         with pytest.raises(lz.ArgumentException):
             suite.linear_fused(device, 1, 40, 512, xb, W, S, 512, None, 0.0,
                                suite.EPI_STORE | suite.EPI_BLOCKED_WEIGHTS, None, ob)
+
+
+@pytest.mark.parametrize("wkind", ["bf16", "i8c"])
+@pytest.mark.parametrize("m", [1, 8])
+def test_linear_shared_equals_separate_projections(lz, orc, device, suite, wkind, m):
+    """ProjectShared over stacked weights (l0b_linear_shared): the Gated DeltaNet in-projections of
+    config 3 (qkv 8192, z 4096, b 32, a 32 rows over K = 2048) as one launch give the oracle's result for
+    each projection, with a bias on one of them, and the same values as four separate l0b_linear calls."""
+    rng = np.random.default_rng(31 + m)
+    K, rows = 2048, [8192, 4096, 32, 32]
+    hf = ((rng.random((sum(rows), K)) * 2 - 1) * 0.05).astype(np.float32)
+    x = rng.standard_normal((m, K)).astype(np.float32)
+    bias = (rng.standard_normal(rows[1]) * 0.1).astype(np.float32)
+    w_dev, w_orc, wdt, dt, scales, group = _weights(lz, orc, wkind, hf, K)
+    want = orc.gemv_out_in(x, w_orc, wdt, None if scales is None else scales.view(np.uint16), group)
+    edges = np.cumsum([0] + rows)
+    with lz.SharedBuffer.from_array(device, w_dev, dt) as W, lz.SharedBuffer.from_array(device, x) as xb, \
+            lz.SharedBuffer.from_array(device, bias) as bb:
+        sb = lz.SharedBuffer.from_array(device, scales) if scales is not None else None
+        outs = [lz.SharedBuffer(device, lz.F32, m * r) for r in rows]
+        suite.linear_shared(device, m, K, xb, W, sb, group, rows, outs, [None, bb, None, None])
+        got = [o.ToArray().reshape(m, r) for o, r in zip(outs, rows)]
+        tol = 2e-4 if wkind == "bf16" else 2e-5
+        for i, r in enumerate(rows):
+            w_i = want[:, edges[i]:edges[i + 1]] + (bias if i == 1 else 0)
+            err = np.abs(got[i] - w_i).max()
+            assert err <= tol * max(np.abs(w_i).max(), 1e-3), f"projection {i}: max err {err}"
+        # Separate calls over the same rows (views of W) give the same values.
+        wv = w_dev.reshape(sum(rows), K)
+        for i, r in enumerate(rows):
+            with lz.SharedBuffer.from_array(device, np.ascontiguousarray(wv[edges[i]:edges[i + 1]]), dt) as Wi, \
+                    lz.SharedBuffer(device, lz.F32, m * r) as yi:
+                si = lz.SharedBuffer.from_array(device, np.ascontiguousarray(scales[edges[i]:edges[i + 1]])) \
+                    if scales is not None else None
+                suite.linear(device, m, r, K, xb, Wi, si, group, bb if i == 1 else None, yi)
+                sep = yi.ToArray().reshape(m, r)
+                if si is not None:
+                    si.Dispose()
+            err = np.abs(sep - got[i]).max()
+            assert err <= tol * max(np.abs(sep).max(), 1e-3), f"projection {i}: shared vs separate {err}"
+        for o in outs:
+            o.Dispose()
+        if sb is not None:
+            sb.Dispose()
