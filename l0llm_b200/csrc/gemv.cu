@@ -1149,8 +1149,16 @@ __host__ __device__ inline size_t bulk_xs_bytes(int K) { return (static_cast<siz
 inline size_t bulk_smem_bytes(int K, int stages, int UK) {
     return 1024 + bulk_xs_bytes(K) + static_cast<size_t>(stages) * 16 * UK + 2 * kBulkMaxStages * 8;
 }
-inline int bulk_stages(int K, int UK) {
-    for (int s = kBulkMaxStages; s >= 2; --s)
+// Stage cap of the bulk GEMV's ring (l0b_set_gemv_bulk_stages; 0 = as many as fit). Two stages of whole
+// 57 KB tiles (gate/up, LM head at K = 3584) leave an SM room for the next k-split GEMV's CTAs, which then
+// start their weight copies while this kernel drains: config 2 bs1 2.192 ms per step against 2.231 with
+// three stages.
+// The cap applies to whole tiles (row-major weights); units of blocked k blocks keep every stage that fits.
+int g_bulk_max_stages = 2;
+inline int bulk_stages(int K, int UK, bool whole_tiles) {
+    const int top = whole_tiles && g_bulk_max_stages >= 2 && g_bulk_max_stages < kBulkMaxStages ? g_bulk_max_stages
+                                                                                                  : kBulkMaxStages;
+    for (int s = top; s >= 2; --s)
         if (bulk_smem_bytes(K, s, UK) <= static_cast<size_t>(kBulkSmemBudget)) return s;
     return 0;
 }
@@ -1730,7 +1738,7 @@ __global__ void __launch_bounds__(kKsThreads, 1) gemv_ksplit_kernel(const GemvPa
 // units-per-tile - 1 long (a tile then spans at most two CTAs).
 int bulk_group(const GemvParams& p, int sm_count) {
     const int ntiles = p.epi == EPI_SWIGLU ? (p.N / 2 + 7) / 8 : (p.N + 15) / 16;
-    if (p.kb <= 0) return ntiles >= 8 * sm_count && bulk_stages(p.K, p.K) >= 2 ? 1 : 0;
+    if (p.kb <= 0) return ntiles >= 8 * sm_count && bulk_stages(p.K, p.K, true) >= 2 ? 1 : 0;
     if (p.epi == EPI_SWIGLU || p.N % 16 != 0 || p.K % p.kb != 0 || p.kb != kWeightBlock) return 0;
     if (!p.part || !p.counters || p.counter_count < ntiles) return 0;
     const int nb = p.K / p.kb;
@@ -1740,7 +1748,7 @@ int bulk_group(const GemvParams& p, int sm_count) {
     for (int G = 4; G >= 1; --G) {
         const int ug = (nb + G - 1) / G;
         const long long units = static_cast<long long>(ntiles) * ug;
-        if (bulk_stages(p.K, G * p.kb) < 3 || units / sm_count < ug - 1) continue;
+        if (bulk_stages(p.K, G * p.kb, false) < 3 || units / sm_count < ug - 1) continue;
         if (units >= 6LL * sm_count || G == 1) return G;
     }
     return 0;
@@ -1768,7 +1776,7 @@ l0b_status launch_bulk(l0b_device* dev, cudaStream_t stream, int sm_count, GemvP
     }
     p.ugroup = bulk_group(p, sm_count);
     const int UK = p.kb > 0 ? p.ugroup * p.kb : p.K;  // k per stage
-    const int stages = bulk_stages(p.K, UK);
+    const int stages = bulk_stages(p.K, UK, p.kb <= 0);
     const size_t smem = bulk_smem_bytes(p.K, stages, UK);
     int* err = dev ? dev->error_flag : nullptr;
     if (p.kb > 0)
@@ -2107,6 +2115,7 @@ void gemv_set_tensor_cores(bool on) { g_gemv_mma = on; }
 void gemv_set_bulk(bool on) { g_gemv_bulk = on; }
 void gemv_set_bulk_short_rows(bool on) { g_gemv_bulk_short = on; }
 void gemv_set_ksplit(bool on) { g_gemv_ksplit = on; }
+void gemv_set_bulk_stages(int s) { g_bulk_max_stages = s < 2 ? 0 : s; }
 int gemv_l2_prefetch_mb() { return g_l2_prefetch_mb; }
 void gemv_set_l2_prefetch_mb(int mb) { g_l2_prefetch_mb = mb < 0 ? 0 : mb; }
 void gemv_set_ksplit_stages(int s) { g_ksplit_stages = s < 2 ? 2 : (s > kKsMaxStages ? kKsMaxStages : s); }

@@ -747,6 +747,11 @@ L0B_API l0b_status l0b_set_gemv_ksplit(int32_t enable) {
     return L0B_OK;
 }
 
+L0B_API l0b_status l0b_set_gemv_bulk_stages(int32_t stages) {
+    gemv_set_bulk_stages(stages);
+    return L0B_OK;
+}
+
 L0B_API l0b_status l0b_set_l2_prefetch(int32_t gate_up_mb) {
     gemv_set_l2_prefetch_mb(gate_up_mb);
     return L0B_OK;

@@ -182,6 +182,7 @@ def load_library() -> C.CDLL:
         "l0b_set_gemv_ksplit": (i32, [i32]),
         "l0b_set_gemv_ksplit_stages": (i32, [i32]),
         "l0b_set_l2_prefetch": (i32, [i32]),
+        "l0b_set_gemv_bulk_stages": (i32, [i32]),
         "l0b_set_attention_cluster16": (i32, [i32]),
         "l0b_set_attention_decode_tensor_cores": (i32, [i32]),
         "l0b_comm_set_fused_allreduce": (i32, [i32]),
