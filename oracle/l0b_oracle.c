@@ -728,6 +728,13 @@ typedef struct {
     float *in_norm, *post_norm, *qb, *kb, *vb, *qn, *kn;
     orc_mat q, k, v, o, gate, up, down;
     void *kc, *vc;
+    /* Qwen3.5: attention output gate rows (split from q_proj), and a Gated DeltaNet layer's weights
+     * (L/LlmLinearAttention.cs:7-40) and per-sequence state (conv window, recurrent state; :42-90). */
+    orc_mat qg;
+    int linear;
+    orc_mat in_qkv, in_z, in_b, in_a, out;
+    float *conv_w, *a_log, *dt_bias, *lin_norm;
+    float *conv_state, *rec_state;
 } orc_layer;
 
 struct orc_model {
@@ -744,6 +751,10 @@ struct orc_model {
     /* row scratch, [rows_cap, width] */
     int rows_cap;
     float *hidden, *normed, *q, *k, *v, *attn, *proj, *gate, *up, *down;
+    /* Qwen3.5 row scratch: the attention gate [rows, qd]; linear layers' projections and outputs */
+    int lin_cap;
+    float *ag, *lq, *lz, *lb, *la, *lc, *lo;
+    int conv_dim, lin_vd;
     orc_probe_fn probe;
     void* probe_user;
 };
@@ -795,6 +806,38 @@ static void free_rows(orc_model* m) {
     free(m->down);
     m->hidden = m->normed = m->q = m->k = m->v = m->attn = m->proj = m->gate = m->up = m->down = NULL;
     m->rows_cap = 0;
+    free(m->ag);
+    free(m->lq);
+    free(m->lz);
+    free(m->lb);
+    free(m->la);
+    free(m->lc);
+    free(m->lo);
+    m->ag = m->lq = m->lz = m->lb = m->la = m->lc = m->lo = NULL;
+    m->lin_cap = 0;
+}
+
+/* Row scratch of the Qwen3.5 layers (attention gate, Gated DeltaNet projections), grown with rows. */
+static int ensure_hybrid_rows(orc_model* m, int rows) {
+    if (rows <= m->lin_cap) return 0;
+    const size_t r = (size_t)rows, hv = (size_t)(m->c.lin_v_heads > 0 ? m->c.lin_v_heads : 1);
+    free(m->ag);
+    free(m->lq);
+    free(m->lz);
+    free(m->lb);
+    free(m->la);
+    free(m->lc);
+    free(m->lo);
+    m->ag = (float*)calloc(r * (size_t)m->qd, sizeof(float));
+    m->lq = (float*)calloc(r * (size_t)(m->conv_dim + 1), sizeof(float));
+    m->lc = (float*)calloc(r * (size_t)(m->conv_dim + 1), sizeof(float));
+    m->lz = (float*)calloc(r * (size_t)(m->lin_vd + 1), sizeof(float));
+    m->lo = (float*)calloc(r * (size_t)(m->lin_vd + 1), sizeof(float));
+    m->lb = (float*)calloc(r * hv, sizeof(float));
+    m->la = (float*)calloc(r * hv, sizeof(float));
+    if (!m->ag || !m->lq || !m->lc || !m->lz || !m->lo || !m->lb || !m->la) return -1;
+    m->lin_cap = rows;
+    return 0;
 }
 
 static int ensure_rows(orc_model* m, int rows) {
@@ -836,7 +879,12 @@ orc_model* orc_model_create_batch(const orc_config* cfg, int max_seq, int batch)
     m->qd = cfg->heads * cfg->head_dim;
     m->kvd = cfg->kv_heads * cfg->head_dim;
     m->inv_freq = (float*)calloc((size_t)cfg->head_dim, sizeof(float));
-    m->rot = 2 * orc_rope_frequencies(cfg->head_dim, cfg->theta, cfg->max_pos, cfg->rope_type, cfg->rope_factor,
+    const int rope_dim = cfg->partial_rotary > 0.0 && cfg->partial_rotary < 1.0
+                             ? (int)(cfg->head_dim * cfg->partial_rotary)
+                             : cfg->head_dim;
+    m->conv_dim = 2 * cfg->lin_k_heads * cfg->lin_k_dim + cfg->lin_v_heads * cfg->lin_v_dim;
+    m->lin_vd = cfg->lin_v_heads * cfg->lin_v_dim;
+    m->rot = 2 * orc_rope_frequencies(rope_dim, cfg->theta, cfg->max_pos, cfg->rope_type, cfg->rope_factor,
                                       cfg->rope_original_max, cfg->rope_low, cfg->rope_high, cfg->rope_beta_fast,
                                       cfg->rope_beta_slow, cfg->rope_attention, 0, 0, 1, m->inv_freq, &m->attn_scale);
     const int H = cfg->hidden, I = cfg->inter;
@@ -867,6 +915,28 @@ orc_model* orc_model_create_batch(const orc_config* cfg, int max_seq, int batch)
             L->qn = (float*)malloc(sizeof(float) * (size_t)cfg->head_dim);
             L->kn = (float*)malloc(sizeof(float) * (size_t)cfg->head_dim);
             for (int i = 0; i < cfg->head_dim; ++i) L->qn[i] = L->kn[i] = 1.f;
+        }
+        if (cfg->attn_gate) mat_alloc(&L->qg, m->qd, H, cfg->wdtype, cfg->group);
+        L->linear = l < 64 && ((cfg->linear_mask >> l) & 1ULL);
+        if (L->linear) {
+            const int hv = cfg->lin_v_heads, cd = m->conv_dim, vd = m->lin_vd, km1 = cfg->lin_conv - 1;
+            if (hv < 1 || cfg->lin_k_heads < 1 || hv % cfg->lin_k_heads || cfg->lin_conv < 2) {
+                m->c.layers = l + 1;
+                orc_model_free(m);
+                return NULL;
+            }
+            mat_alloc(&L->in_qkv, cd, H, cfg->wdtype, cfg->group);
+            mat_alloc(&L->in_z, vd, H, cfg->wdtype, cfg->group);
+            mat_alloc(&L->in_b, hv, H, cfg->wdtype, cfg->group);
+            mat_alloc(&L->in_a, hv, H, cfg->wdtype, cfg->group);
+            mat_alloc(&L->out, H, vd, cfg->wdtype, cfg->group);
+            L->conv_w = (float*)calloc((size_t)cd * cfg->lin_conv, sizeof(float));
+            L->a_log = (float*)calloc((size_t)hv, sizeof(float));
+            L->dt_bias = (float*)calloc((size_t)hv, sizeof(float));
+            L->lin_norm = (float*)malloc(sizeof(float) * (size_t)cfg->lin_v_dim);
+            for (int i = 0; i < cfg->lin_v_dim; ++i) L->lin_norm[i] = 1.f;
+            L->conv_state = (float*)calloc((size_t)batch * cd * km1, sizeof(float));
+            L->rec_state = (float*)calloc((size_t)batch * hv * cfg->lin_k_dim * cfg->lin_v_dim, sizeof(float));
         }
         L->kc = calloc((size_t)batch * max_seq * m->kvd, kvb);
         L->vc = calloc((size_t)batch * max_seq * m->kvd, kvb);
@@ -906,6 +976,18 @@ void orc_model_free(orc_model* m) {
         mat_free(&L->down);
         free(L->kc);
         free(L->vc);
+        mat_free(&L->qg);
+        mat_free(&L->in_qkv);
+        mat_free(&L->in_z);
+        mat_free(&L->in_b);
+        mat_free(&L->in_a);
+        mat_free(&L->out);
+        free(L->conv_w);
+        free(L->a_log);
+        free(L->dt_bias);
+        free(L->lin_norm);
+        free(L->conv_state);
+        free(L->rec_state);
     }
     free(m->L);
     mat_free(&m->lm_head);
@@ -970,7 +1052,7 @@ int orc_model_set_tensor(orc_model* m, const char* name, const float* data, int6
         return 0;
     }
     if (!strcmp(name, "model.norm.weight")) {
-        memcpy(m->final_norm, data, sizeof(float) * (size_t)H);
+        for (int i = 0; i < H; ++i) m->final_norm[i] = data[i] + c->norm_offset;
         return 0;
     }
     if (!strcmp(name, "lm_head.weight")) {
@@ -981,9 +1063,52 @@ int orc_model_set_tensor(orc_model* m, const char* name, const float* data, int6
     char rest[128];
     if (sscanf(name, "model.layers.%d.%127s", &l, rest) != 2 || l < 0 || l >= c->layers) return -1;
     orc_layer* L = &m->L[l];
-    if (!strcmp(rest, "input_layernorm.weight")) memcpy(L->in_norm, data, sizeof(float) * (size_t)H);
-    else if (!strcmp(rest, "post_attention_layernorm.weight")) memcpy(L->post_norm, data, sizeof(float) * (size_t)H);
-    else if (!strcmp(rest, "self_attn.q_proj.weight")) mat_set_f32(&L->q, data);
+    const float off = c->norm_offset;
+    if (L->linear) {
+        /* LlmLayerWeights.Load, linear branch (L/LlmLayerWeights.cs:146-163): the gated norm weight is
+         * loaded as is (no offset); conv1d.weight [conv_dim, 1, k] is [conv_dim, k]. */
+        const int hv = c->lin_v_heads;
+        if (!strcmp(rest, "linear_attn.in_proj_qkv.weight")) mat_set_f32(&L->in_qkv, data);
+        else if (!strcmp(rest, "linear_attn.in_proj_z.weight")) mat_set_f32(&L->in_z, data);
+        else if (!strcmp(rest, "linear_attn.in_proj_b.weight")) mat_set_f32(&L->in_b, data);
+        else if (!strcmp(rest, "linear_attn.in_proj_a.weight")) mat_set_f32(&L->in_a, data);
+        else if (!strcmp(rest, "linear_attn.out_proj.weight")) mat_set_f32(&L->out, data);
+        else if (!strcmp(rest, "linear_attn.conv1d.weight"))
+            memcpy(L->conv_w, data, sizeof(float) * (size_t)m->conv_dim * c->lin_conv);
+        else if (!strcmp(rest, "linear_attn.A_log")) memcpy(L->a_log, data, sizeof(float) * (size_t)hv);
+        else if (!strcmp(rest, "linear_attn.dt_bias")) memcpy(L->dt_bias, data, sizeof(float) * (size_t)hv);
+        else if (!strcmp(rest, "linear_attn.norm.weight")) memcpy(L->lin_norm, data, sizeof(float) * (size_t)c->lin_v_dim);
+        else goto common;
+        return 0;
+    }
+    if (c->attn_gate && !strcmp(rest, "self_attn.q_proj.weight")) {
+        /* SplitQueryAndGate (L/LlmLayerWeights.cs:282-297): per head, hd query rows then hd gate rows. */
+        const size_t blk = (size_t)c->head_dim * H;
+        float* qr = (float*)malloc(sizeof(float) * blk * (size_t)c->heads);
+        float* gr = (float*)malloc(sizeof(float) * blk * (size_t)c->heads);
+        if (!qr || !gr) {
+            free(qr);
+            free(gr);
+            return -2;
+        }
+        for (int h = 0; h < c->heads; ++h) {
+            memcpy(qr + h * blk, data + (2 * (size_t)h) * blk, sizeof(float) * blk);
+            memcpy(gr + h * blk, data + (2 * (size_t)h + 1) * blk, sizeof(float) * blk);
+        }
+        mat_set_f32(&L->q, qr);
+        mat_set_f32(&L->qg, gr);
+        free(qr);
+        free(gr);
+        return 0;
+    }
+common:
+    if (!strcmp(rest, "input_layernorm.weight")) {
+        for (int i = 0; i < H; ++i) L->in_norm[i] = data[i] + off;
+    } else if (!strcmp(rest, "post_attention_layernorm.weight")) {
+        for (int i = 0; i < H; ++i) L->post_norm[i] = data[i] + off;
+    } else if (L->linear && strncmp(rest, "mlp.", 4) != 0) {
+        return -1;
+    } else if (!strcmp(rest, "self_attn.q_proj.weight")) mat_set_f32(&L->q, data);
     else if (!strcmp(rest, "self_attn.k_proj.weight")) mat_set_f32(&L->k, data);
     else if (!strcmp(rest, "self_attn.v_proj.weight")) mat_set_f32(&L->v, data);
     else if (!strcmp(rest, "self_attn.o_proj.weight")) mat_set_f32(&L->o, data);
@@ -993,10 +1118,40 @@ int orc_model_set_tensor(orc_model* m, const char* name, const float* data, int6
     else if (!strcmp(rest, "self_attn.q_proj.bias") && L->qb) memcpy(L->qb, data, sizeof(float) * (size_t)m->qd);
     else if (!strcmp(rest, "self_attn.k_proj.bias") && L->kb) memcpy(L->kb, data, sizeof(float) * (size_t)m->kvd);
     else if (!strcmp(rest, "self_attn.v_proj.bias") && L->vb) memcpy(L->vb, data, sizeof(float) * (size_t)m->kvd);
-    else if (!strcmp(rest, "self_attn.q_norm.weight") && L->qn) memcpy(L->qn, data, sizeof(float) * (size_t)c->head_dim);
-    else if (!strcmp(rest, "self_attn.k_norm.weight") && L->kn) memcpy(L->kn, data, sizeof(float) * (size_t)c->head_dim);
-    else return -1;
+    else if (!strcmp(rest, "self_attn.q_norm.weight") && L->qn) {
+        for (int i = 0; i < c->head_dim; ++i) L->qn[i] = data[i] + off;
+    } else if (!strcmp(rest, "self_attn.k_norm.weight") && L->kn) {
+        for (int i = 0; i < c->head_dim; ++i) L->kn[i] = data[i] + off;
+    } else return -1;
     return 0;
+}
+
+/* LlmDecoderLayer.MixLinear (L/LlmDecoderLayer.cs:381-397) for `rows` tokens: the four in-projections of the
+ * normed rows, then row by row in order the causal conv and the gated delta step on the row's sequence
+ * state (reset when the row is at position 0, as MixLinear resets at a chunk starting at 0), then
+ * out_proj into m->proj. */
+static void mix_linear(orc_model* m, orc_layer* L, int rows, const int* positions, const int* seqs) {
+    const orc_config* c = &m->c;
+    const int cd = m->conv_dim, vd = m->lin_vd, hv = c->lin_v_heads, km1 = c->lin_conv - 1;
+    const size_t st = (size_t)hv * c->lin_k_dim * c->lin_v_dim;
+    mat_apply_rows(m, &L->in_qkv, rows, m->normed, m->lq);
+    mat_apply_rows(m, &L->in_z, rows, m->normed, m->lz);
+    mat_apply_rows(m, &L->in_b, rows, m->normed, m->lb);
+    mat_apply_rows(m, &L->in_a, rows, m->normed, m->la);
+    for (int r = 0; r < rows; ++r) {
+        const int sq = seqs ? seqs[r] : 0;
+        float* cs = L->conv_state + (size_t)sq * cd * km1;
+        float* rs = L->rec_state + (size_t)sq * st;
+        if (positions[r] == 0) {
+            memset(cs, 0, sizeof(float) * (size_t)cd * km1);
+            memset(rs, 0, sizeof(float) * st);
+        }
+        orc_causal_conv(m->lq + (int64_t)r * cd, cs, L->conv_w, m->lc + (int64_t)r * cd, cd, c->lin_conv, 1);
+        orc_gated_delta(m->lc + (int64_t)r * cd, m->lz + (int64_t)r * vd, m->lb + (int64_t)r * hv,
+                        m->la + (int64_t)r * hv, L->a_log, L->dt_bias, L->lin_norm, rs, m->lo + (int64_t)r * vd,
+                        c->lin_k_heads, hv, c->lin_k_dim, c->lin_v_dim, 1, c->eps);
+    }
+    mat_apply_rows(m, &L->out, rows, m->lo, m->proj);
 }
 
 /* LlmModel.Step / StepBatch / IngestPrompt + LlmDecoderLayer.Forward / ForwardBatch (L/LlmModel.cs:156-251,
@@ -1019,11 +1174,17 @@ int orc_model_forward(orc_model* m, int rows, const int* tokens, const int* posi
     for (int r = 0; r < rows; ++r)
         memcpy(m->hidden + (int64_t)r * H, m->embed + (int64_t)tokens[r] * H, sizeof(float) * (size_t)H);
     const int nl = m->layer_limit > 0 && m->layer_limit < c->layers ? m->layer_limit : c->layers;
+    if ((c->linear_mask || c->attn_gate) && ensure_hybrid_rows(m, rows) != 0) return -2;
     for (int l = 0; l < nl; ++l) {
         orc_layer* L = &m->L[l];
         orc_rmsnorm(m->hidden, NULL, L->in_norm, m->normed, c->eps, H, rows, 0);
         emit(m, l, "input_norm", m->normed, H);
+        if (L->linear) {
+            mix_linear(m, L, rows, positions, seqs);
+            goto mlp;
+        }
         mat_apply_rows(m, &L->q, rows, m->normed, m->q);
+        if (c->attn_gate) mat_apply_rows(m, &L->qg, rows, m->normed, m->ag);
         mat_apply_rows(m, &L->k, rows, m->normed, m->k);
         mat_apply_rows(m, &L->v, rows, m->normed, m->v);
         if (c->bias) {
@@ -1049,7 +1210,10 @@ int orc_model_forward(orc_model* m, int rows, const int* tokens, const int* posi
             orc_attention(m->q + (int64_t)r * m->qd, seq_cache(m, L->kc, sq), seq_cache(m, L->vc, sq), c->kv_dtype,
                           m->attn + (int64_t)r * m->qd, hd, c->heads, c->kv_heads, positions[r], 1);
         }
+        /* MixFull (L/LlmDecoderLayer.cs:328-331): the optional sigmoid output gate before o_proj. */
+        if (c->attn_gate) orc_sigmoid_gate(m->attn, m->ag, (int64_t)rows * m->qd);
         mat_apply_rows(m, &L->o, rows, m->attn, m->proj);
+    mlp:
         emit(m, l, "attn_out", m->proj, H);
         orc_rmsnorm(m->hidden, m->proj, L->post_norm, m->normed, c->eps, H, rows, 1);
         emit(m, l, "post_norm", m->normed, H);

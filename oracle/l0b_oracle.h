@@ -113,6 +113,15 @@ typedef struct orc_config {
     int rope_original_max;
     double rope_low, rope_high, rope_beta_fast, rope_beta_slow, rope_attention;
     int wdtype, group, kv_dtype;
+    /* Qwen3.5 hybrid (all zero: a standard decoder). Layer l is a Gated DeltaNet layer when bit l of
+     * linear_mask is set (HfModelConfig.IsLinearLayer); attn_gate: q_proj carries a sigmoid output gate
+     * per head (AttentionOutputGate); norm_offset is added to the input / post-attention / final / q / k
+     * norm weights at load (RmsNormOffset); partial_rotary: fraction of head_dim rotated (0 = all). */
+    uint64_t linear_mask;
+    int lin_k_heads, lin_v_heads, lin_k_dim, lin_v_dim, lin_conv;
+    int attn_gate;
+    float norm_offset;
+    double partial_rotary;
 } orc_config;
 
 typedef struct orc_model orc_model;

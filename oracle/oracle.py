@@ -39,6 +39,9 @@ class OrcConfig(C.Structure):
         ("rope_low", C.c_double), ("rope_high", C.c_double), ("rope_beta_fast", C.c_double),
         ("rope_beta_slow", C.c_double), ("rope_attention", C.c_double),
         ("wdtype", C.c_int), ("group", C.c_int), ("kv_dtype", C.c_int),
+        ("linear_mask", C.c_uint64), ("lin_k_heads", C.c_int), ("lin_v_heads", C.c_int), ("lin_k_dim", C.c_int),
+        ("lin_v_dim", C.c_int), ("lin_conv", C.c_int), ("attn_gate", C.c_int), ("norm_offset", C.c_float),
+        ("partial_rotary", C.c_double),
     ]
 
 

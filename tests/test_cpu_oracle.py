@@ -219,6 +219,45 @@ def test_oracle_model_matches_transformers(orc, name):
     m.close()
 
 
+def test_oracle_hybrid_model_matches_transformers(orc):
+    """A Qwen3.5-style hybrid decoder (hf_tiny.HYBRID: Gated DeltaNet layers between full-attention
+    layers with the sigmoid output gate in q_proj, QK-norm, partial rotary, (1 + w) norms) in the oracle
+    against transformers' Qwen3_5ForCausalLM in fp32 (tests/golden/hf_tiny_hybrid.json): every prompt
+    position's logits token by token, the 16 greedy tokens after it, and the prompt as one prefill chunk
+    (the linear layers walk the chunk's rows in order from a reset state)."""
+    cfg = hf_tiny.HYBRID["qwen3_5"]
+    doc = json.loads((GOLDEN / "hf_tiny_hybrid.json").read_text())
+    g = doc["models"]["qwen3_5"]
+    logits_hf = np.frombuffer(base64.b64decode(g["logits"]), "<f4").reshape(g["shape"])
+    prompt = np.array(g["prompt"], np.int32)
+    assert np.array_equal(prompt, hf_tiny.prompt(cfg, doc["seed"]))
+    w = hf_tiny.hybrid_weights(cfg, doc["seed"])
+    m = orc.OracleModel(hf_tiny.hybrid_oracle_config(cfg), 64, batch=2)
+    for k, v in w.items():
+        m.set_tensor(k, v)
+    for t, tok in enumerate(prompt):
+        lg = m.step(int(tok), t)
+        np.testing.assert_allclose(lg, logits_hf[t], atol=2e-4, rtol=1e-3)
+    toks, pos, nxt = [], len(prompt), int(np.argmax(lg))
+    for _ in range(len(g["greedy"])):
+        toks.append(nxt)
+        nxt = int(np.argmax(m.step(nxt, pos)))
+        pos += 1
+    assert toks == g["greedy"]
+    # The whole prompt as one chunk of sequence 1 (state reset at position 0, rows in order).
+    chunk = m.forward(prompt, np.arange(prompt.size), np.ones(prompt.size, np.int32))
+    np.testing.assert_allclose(chunk, logits_hf, atol=2e-4, rtol=1e-3)
+    m.close()
+
+
+def test_oracle_hybrid_rejects_attention_names_on_linear_layers(orc):
+    cfg = hf_tiny.HYBRID["qwen3_5"]
+    m = orc.OracleModel(hf_tiny.hybrid_oracle_config(cfg), 8)
+    with pytest.raises(Exception):
+        m.set_tensor("model.layers.0.self_attn.k_proj.weight", np.zeros((64, 128), np.float32))
+    m.close()
+
+
 # --------------------------------------------------------------------------------------------
 # Gated DeltaNet: the oracle against transformers' torch reference functions (Qwen3.5)
 # --------------------------------------------------------------------------------------------
