@@ -593,6 +593,18 @@ typedef struct l0b_model_config {
     int32_t tp_size;             /* tensor-parallel ranks (1 = none) */
     int32_t tp_rank;
     int32_t max_batch;           /* sequences decoded together (KV cache rows); default 1, at most 64 */
+    /* Qwen3.5 hybrid decoders (L/HfModelConfig.cs:186-205, 340-370); all zero for the other families.
+     * Layer l is a Gated DeltaNet (linear attention) layer when bit l of linear_layer_mask is set
+     * (IsLinearLayer); such a model runs on one GPU, one sequence, on the reference op sequence. */
+    uint64_t linear_layer_mask;
+    int32_t linear_num_key_heads;
+    int32_t linear_num_value_heads;
+    int32_t linear_key_head_dim;   /* 64 or 128 */
+    int32_t linear_value_head_dim; /* <= 256 */
+    int32_t linear_conv_kernel;    /* 2..8 */
+    int32_t attention_output_gate; /* q_proj holds [query | gate] rows per head (AttentionOutputGate) */
+    float rms_norm_offset;         /* added to the input / post-attention / final / q / k norm weights at
+                                      load (RmsNormOffset: 1 for Qwen3.5) */
 } l0b_model_config;
 
 /* Fills a config with the defaults HfModelConfig.Parse applies. */
@@ -633,14 +645,21 @@ L0B_API l0b_status l0b_model_set_tensor(l0b_model* model, const char* name, cons
 typedef enum l0b_shard_kind {
     L0B_SHARD_MATRIX = 0,
     L0B_SHARD_VECTOR = 1,
-    L0B_SHARD_EMBEDDING = 2
+    L0B_SHARD_EMBEDDING = 2,
+    /* a Qwen3.5 q_proj with its output gate: per head, head_dim query rows then head_dim gate rows
+     * (SplitQueryAndGate, L/LlmLayerWeights.cs:282-297). The `rows` query rows land at dst_row of the
+     * stacked [q; k; v; gate] matrix, the gate rows after v. */
+    L0B_SHARD_QUERY_GATE = 3
 } l0b_shard_kind;
 typedef enum l0b_shard_slot {
     /* matrices */
     L0B_SLOT_QKV = 0, L0B_SLOT_O = 1, L0B_SLOT_GATE_UP = 2, L0B_SLOT_DOWN = 3, L0B_SLOT_LM_HEAD = 4,
+    L0B_SLOT_LIN_IN = 5,  /* Gated DeltaNet in-projections stacked [qkv; z; b; a] */
+    L0B_SLOT_LIN_OUT = 6, /* Gated DeltaNet out_proj */
     /* vectors */
     L0B_SLOT_IN_NORM = 0, L0B_SLOT_POST_NORM = 1, L0B_SLOT_QKV_BIAS = 2, L0B_SLOT_Q_NORM = 3,
-    L0B_SLOT_K_NORM = 4, L0B_SLOT_FINAL_NORM = 5
+    L0B_SLOT_K_NORM = 4, L0B_SLOT_FINAL_NORM = 5, L0B_SLOT_LIN_CONV = 6, L0B_SLOT_LIN_A_LOG = 7,
+    L0B_SLOT_LIN_DT_BIAS = 8, L0B_SLOT_LIN_NORM = 9
 } l0b_shard_slot;
 typedef struct l0b_shard_plan {
     int32_t kind;                 /* l0b_shard_kind */

@@ -96,6 +96,11 @@ struct l0b_model {
     float* host_logits = nullptr; // pinned [batch_cap * vocab]
     bool fused = true;
     bool recording = true;
+    // Qwen3.5 hybrid (Gated DeltaNet layers, gated attention): one GPU, one sequence, reference op sequence.
+    bool hybrid = false;
+    int lin_hk = 0, lin_hv = 0, lin_dk = 0, lin_dv = 0, lin_kconv = 0, lin_cd = 0, lin_vd = 0;
+    float *lq = nullptr, *lz = nullptr, *lb = nullptr, *la = nullptr, *lc = nullptr, *lo = nullptr;
+    float* gb = nullptr;  // attention output gate rows [cap, qdim]
     int position = 0;
     l0b_probe_fn probe = nullptr;
     void* probe_user = nullptr;
@@ -563,6 +568,35 @@ l0b_status record_layer_fused(l0b_model* m, int li, int rows, bool decode, int p
     return gemv(m, L.down, p);
 }
 
+l0b_status record_layer_tail(l0b_model* m, int li, int rows);
+
+// LlmDecoderLayer.MixLinear (L/LlmDecoderLayer.cs:381-397) for `rows` consecutive tokens of the sequence at
+// pos0, pos0 + 1, ...: the four in-projections in one launch ([qkv; z; b; a] stacked, ProjectShared), the
+// causal conv + SiLU over the conv window, the gated delta rule over the recurrent state (both reset when
+// the rows start at position 0), out_proj into attn_proj.
+l0b_status record_mix_linear(l0b_model* m, ModelLayer& L, int rows, int pos0) {
+    const l0b_model_config& c = m->cfg;
+    l0b_device* d = m->dev;
+    const int cd = m->lin_cd, vd = m->lin_vd, hv = m->lin_hv;
+    GemvParams p = model_linear_params(m, L.lin_in, rows, m->normed, m->h);
+    p.nseg = 4;
+    p.seg[0] = {m->lq, nullptr, cd, cd};
+    p.seg[1] = {m->lz, nullptr, cd + vd, vd};
+    p.seg[2] = {m->lb, nullptr, cd + vd + hv, hv};
+    p.seg[3] = {m->la, nullptr, cd + vd + 2 * hv, hv};
+    L0B_TRY(gemv(m, L.lin_in, p));
+    if (pos0 == 0) {  // LlmLinearState.Reset at position 0
+        L0B_TRY(k_fill_u32(d, reinterpret_cast<uint32_t*>(L.conv_state), 0u, cd * (m->lin_kconv - 1)));
+        L0B_TRY(k_fill_u32(d, reinterpret_cast<uint32_t*>(L.rec_state), 0u, hv * m->lin_dk * m->lin_dv));
+    }
+    L0B_TRY(k_causal_conv(d, m->lq, L.conv_state, L.conv_w, m->lc, cd, m->lin_kconv, rows));
+    L0B_TRY(k_gated_delta(m->suite, d, m->lc, m->lz, m->lb, m->la, L.a_log, L.dt_bias, L.lin_norm, L.rec_state, m->lo,
+                          m->lin_hk, hv, m->lin_dk, m->lin_dv, rows, c.rms_norm_eps));
+    p = model_linear_params(m, L.lin_out, rows, m->lo, vd);
+    p.seg[0] = {m->attn_proj, nullptr, m->h, m->h};
+    return gemv(m, L.lin_out, p);
+}
+
 // The reference op sequence of LlmDecoderLayer.Forward / ForwardBatch (L/LlmDecoderLayer.cs:129-378).
 l0b_status record_layer_reference(l0b_model* m, int li, int rows, bool decode, int pos0) {
     ModelLayer& L = m->layers[li];
@@ -570,11 +604,19 @@ l0b_status record_layer_reference(l0b_model* m, int li, int rows, bool decode, i
     l0b_device* d = m->dev;
     L0B_TRY(k_rmsnorm(d, m->hidden, nullptr, L.in_norm, m->normed, c.rms_norm_eps, m->h, rows, 0));
     L0B_TRY(emit(m, li, "input_norm", m->normed, m->h));
+    if (L.linear) {
+        L0B_TRY(record_mix_linear(m, L, rows, pos0));
+        return record_layer_tail(m, li, rows);
+    }
     GemvParams p = model_linear_params(m, L.qkv, rows, m->normed, m->h);
     p.nseg = 3;
     p.seg[0] = {m->qb, nullptr, m->qdim, m->qdim};
     p.seg[1] = {m->kb, nullptr, m->qdim + m->kvdim, m->kvdim};
     p.seg[2] = {m->vb, nullptr, m->qkv_w, m->kvdim};
+    if (c.attention_output_gate) {  // Qwen3.5: the gate rows stacked after v
+        p.nseg = 4;
+        p.seg[3] = {m->gb, nullptr, m->qkv_w + m->qdim, m->qdim};
+    }
     L0B_TRY(gemv(m, L.qkv, p));
     if (L.qkv_bias) {
         L0B_TRY(k_bias_add(d, m->qb, L.qkv_bias, m->qdim, rows));
@@ -617,10 +659,22 @@ l0b_status record_layer_reference(l0b_model* m, int li, int rows, bool decode, i
         a.max_splits = 1;
         L0B_TRY(attention_launch(d, a, rows));
     }
+    // MixFull's optional sigmoid output gate before o_proj (L/LlmDecoderLayer.cs:328-331,372-375).
+    if (c.attention_output_gate) L0B_TRY(k_sigmoid_gate(d, m->attn, m->gb, static_cast<long long>(rows) * m->qdim));
     p = model_linear_params(m, L.o, rows, m->attn, m->qdim);
     p.seg[0] = {m->attn_proj, nullptr, m->h, m->h};
     L0B_TRY(gemv(m, L.o, p));
     if (m->comm) L0B_TRY(comm_allreduce(m->comm, m->attn_proj, static_cast<size_t>(rows) * m->h, L0B_F32, COLL_SUM));
+    return record_layer_tail(m, li, rows);
+}
+
+// Forward steps 3-5 after the token mixer's output is in attn_proj: residual + post-attention RMSNorm,
+// gate/up + SwiGLU, down, residual add (L/LlmDecoderLayer.cs:178-195).
+l0b_status record_layer_tail(l0b_model* m, int li, int rows) {
+    ModelLayer& L = m->layers[li];
+    const l0b_model_config& c = m->cfg;
+    l0b_device* d = m->dev;
+    GemvParams p;
     L0B_TRY(emit(m, li, "attn_out", m->attn_proj, m->h));
     L0B_TRY(k_rmsnorm(d, m->hidden, m->attn_proj, L.post_norm, m->normed, c.rms_norm_eps, m->h, rows, 1));
     L0B_TRY(emit(m, li, "post_norm", m->normed, m->h));
@@ -852,6 +906,7 @@ struct Target {
     float offset = 0.f;
     uint64_t id = 0, scale_id = 0;
     bool embed = false;
+    bool query_gate = false;  // Qwen3.5 q_proj: split into query rows and gate rows on load
 };
 
 bool parse_layer(const std::string& name, const std::string& prefix, int* layer, std::string* rest) {
@@ -931,6 +986,39 @@ l0b_status shard_plan(const l0b_model_config& c, const std::string& name, l0b_sh
     if (!parse_layer(name, "model.layers.", &li, &rest) || li < 0 || li >= c.num_layers)
         return fail(L0B_ERR_INVALID_DATA, "unknown tensor '%s'", name.c_str());
     sp->layer = li;
+    const bool linear = li < 64 && ((c.linear_layer_mask >> li) & 1ULL);
+    if (linear) {
+        // A Gated DeltaNet layer (LlmLayerWeights.Load, L/LlmLayerWeights.cs:146-163): its in-projections
+        // stacked [qkv; z; b; a] in one matrix, out_proj, conv taps [conv_dim, k], A_log, dt_bias, norm.
+        const int hv = c.linear_num_value_heads, dv = c.linear_value_head_dim;
+        const int cd = 2 * c.linear_num_key_heads * c.linear_key_head_dim + hv * dv, vd = hv * dv;
+        if (rest == "input_layernorm.weight") vec(L0B_SLOT_IN_NORM, H, H, 0, 0, T_IN_NORM);
+        else if (rest == "post_attention_layernorm.weight") vec(L0B_SLOT_POST_NORM, H, H, 0, 0, T_POST_NORM);
+        else if (rest == "mlp.gate_proj.weight") col_split(L0B_SLOT_GATE_UP, 0, I, T_GATE);
+        else if (rest == "mlp.up_proj.weight") col_split(L0B_SLOT_GATE_UP, inter, I, T_UP);
+        else if (rest == "mlp.down_proj.weight") row_split(L0B_SLOT_DOWN, I, T_DOWN);
+        else if (rest == "linear_attn.in_proj_qkv.weight") col_split(L0B_SLOT_LIN_IN, 0, cd, -1);
+        else if (rest == "linear_attn.in_proj_z.weight") col_split(L0B_SLOT_LIN_IN, cd, vd, -1);
+        else if (rest == "linear_attn.in_proj_b.weight") col_split(L0B_SLOT_LIN_IN, cd + vd, hv, -1);
+        else if (rest == "linear_attn.in_proj_a.weight") col_split(L0B_SLOT_LIN_IN, cd + vd + hv, hv, -1);
+        else if (rest == "linear_attn.out_proj.weight") row_split(L0B_SLOT_LIN_OUT, vd, -1);
+        else if (rest == "linear_attn.conv1d.weight") {
+            const int n = cd * c.linear_conv_kernel;
+            vec(L0B_SLOT_LIN_CONV, n, n, 0, 0, -1);
+        } else if (rest == "linear_attn.A_log") vec(L0B_SLOT_LIN_A_LOG, hv, hv, 0, 0, -1);
+        else if (rest == "linear_attn.dt_bias") vec(L0B_SLOT_LIN_DT_BIAS, hv, hv, 0, 0, -1);
+        else if (rest == "linear_attn.norm.weight") vec(L0B_SLOT_LIN_NORM, dv, dv, 0, 0, -1);
+        else return fail(L0B_ERR_INVALID_DATA, "unknown or unused tensor '%s'", name.c_str());
+        return L0B_OK;
+    }
+    if (rest == "self_attn.q_proj.weight" && c.attention_output_gate) {
+        // [query | gate] rows per head (SplitQueryAndGate): the query rows go to the top of [q; k; v; gate].
+        matrix(L0B_SLOT_QKV, 2 * QD, H);
+        sp->kind = L0B_SHARD_QUERY_GATE;
+        sp->rows = QD;
+        *tkind = T_Q;
+        return L0B_OK;
+    }
     if (rest == "input_layernorm.weight") vec(L0B_SLOT_IN_NORM, H, H, 0, 0, T_IN_NORM);
     else if (rest == "post_attention_layernorm.weight") vec(L0B_SLOT_POST_NORM, H, H, 0, 0, T_POST_NORM);
     else if (rest == "self_attn.q_proj.weight") col_split(L0B_SLOT_QKV, 0, QD, T_Q);
@@ -969,10 +1057,25 @@ l0b_status resolve(l0b_model* m, const std::string& name, Target* t) {
             t->id = kIdFinalNorm;
         } else {
             ModelLayer& L = m->layers[sp.layer];
-            dst = sp.slot == L0B_SLOT_IN_NORM ? L.in_norm : sp.slot == L0B_SLOT_POST_NORM ? L.post_norm
-                : sp.slot == L0B_SLOT_QKV_BIAS ? L.qkv_bias : sp.slot == L0B_SLOT_Q_NORM ? L.q_norm : L.k_norm;
-            t->id = layer_tensor_id(sp.layer, kind);
+            switch (sp.slot) {
+                case L0B_SLOT_IN_NORM: dst = L.in_norm; break;
+                case L0B_SLOT_POST_NORM: dst = L.post_norm; break;
+                case L0B_SLOT_QKV_BIAS: dst = L.qkv_bias; break;
+                case L0B_SLOT_Q_NORM: dst = L.q_norm; break;
+                case L0B_SLOT_K_NORM: dst = L.k_norm; break;
+                case L0B_SLOT_LIN_CONV: dst = L.conv_w; break;
+                case L0B_SLOT_LIN_A_LOG: dst = L.a_log; break;
+                case L0B_SLOT_LIN_DT_BIAS: dst = L.dt_bias; break;
+                case L0B_SLOT_LIN_NORM: dst = L.lin_norm; break;
+                default: dst = nullptr;
+            }
+            if (kind >= 0) t->id = layer_tensor_id(sp.layer, kind);
         }
+        // RmsNormOffset (Qwen3.5: 1) on the input, post-attention, final and q / k norms, not on the gated
+        // norm of a linear layer (L/LlmLayerWeights.cs:127-129,162; L/LlmModel.cs:59).
+        if (sp.slot == L0B_SLOT_IN_NORM || sp.slot == L0B_SLOT_POST_NORM || sp.slot == L0B_SLOT_FINAL_NORM ||
+            sp.slot == L0B_SLOT_Q_NORM || sp.slot == L0B_SLOT_K_NORM)
+            t->offset = m->cfg.rms_norm_offset;
         L0B_REQUIRE(dst, L0B_ERR_INVALID_DATA, "unknown or unused tensor '%s'", name.c_str());
         t->vec = dst + sp.dst_row;
         t->length = sp.cols;
@@ -986,9 +1089,14 @@ l0b_status resolve(l0b_model* m, const std::string& name, Target* t) {
     } else {
         ModelLayer& L = m->layers[sp.layer];
         t->mat = sp.slot == L0B_SLOT_QKV ? &L.qkv : sp.slot == L0B_SLOT_O ? &L.o
-               : sp.slot == L0B_SLOT_GATE_UP ? &L.gate_up : &L.down;
-        t->id = layer_tensor_id(sp.layer, kind);
-        t->scale_id = layer_tensor_id(sp.layer, T_SCALE + kind);
+               : sp.slot == L0B_SLOT_GATE_UP ? &L.gate_up : sp.slot == L0B_SLOT_DOWN ? &L.down
+               : sp.slot == L0B_SLOT_LIN_IN ? &L.lin_in : &L.lin_out;
+        L0B_REQUIRE(t->mat->w, L0B_ERR_INVALID_DATA, "unknown or unused tensor '%s'", name.c_str());
+        if (kind >= 0) {
+            t->id = layer_tensor_id(sp.layer, kind);
+            t->scale_id = layer_tensor_id(sp.layer, T_SCALE + kind);
+        }
+        t->query_gate = sp.kind == L0B_SHARD_QUERY_GATE;
     }
     t->dst_row = sp.dst_row;
     t->row0 = sp.row0;
@@ -1027,6 +1135,8 @@ L0B_API l0b_status l0b_model_shard_plan(const l0b_model_config* cfg, const char*
                 L0B_ERR_INVALID_DATA, "head counts, head_dim, layers and hidden size must be positive");
     L0B_REQUIRE(cfg->num_key_value_heads % tp == 0 && cfg->intermediate_size % tp == 0 && cfg->vocab_size % tp == 0,
                 L0B_ERR_UNSUPPORTED, "kv heads, intermediate size and vocab must divide by tp_size %d", tp);
+    L0B_REQUIRE(tp == 1 || (cfg->linear_layer_mask == 0 && cfg->attention_output_gate == 0), L0B_ERR_UNSUPPORTED,
+                "Qwen3.5 hybrid models run on one GPU");
     int kind;
     return shard_plan(*cfg, name, out, &kind);
     GUARD_END
@@ -1083,6 +1193,24 @@ L0B_API l0b_status l0b_model_create(l0b_device* dev, l0b_suite* suite, const l0b
     L0B_REQUIRE(c.head_dim == 64 || c.head_dim == 128, L0B_ERR_UNSUPPORTED, "head_dim %d (64 or 128 are supported)",
                 c.head_dim);
     L0B_REQUIRE((c.num_attention_heads / c.num_key_value_heads) <= 64, L0B_ERR_UNSUPPORTED, "GQA group too large");
+    const bool hybrid = c.linear_layer_mask != 0 || c.attention_output_gate != 0;
+    if (hybrid) {
+        L0B_REQUIRE(tp == 1 && c.max_batch <= 1, L0B_ERR_UNSUPPORTED,
+                    "Qwen3.5 hybrid models run on one GPU and one sequence");
+        L0B_REQUIRE(c.num_layers <= 64, L0B_ERR_UNSUPPORTED, "linear_layer_mask covers 64 layers");
+    }
+    if (c.linear_layer_mask) {
+        L0B_REQUIRE(c.linear_num_key_heads > 0 && c.linear_num_value_heads > 0 &&
+                        c.linear_num_value_heads % c.linear_num_key_heads == 0,
+                    L0B_ERR_INVALID_DATA, "linear value heads (%d) must be a multiple of key heads (%d)",
+                    c.linear_num_value_heads, c.linear_num_key_heads);
+        L0B_REQUIRE(c.linear_key_head_dim == 64 || c.linear_key_head_dim == 128, L0B_ERR_UNSUPPORTED,
+                    "linear key head dim %d (64 or 128 are supported)", c.linear_key_head_dim);
+        L0B_REQUIRE(c.linear_value_head_dim > 0 && c.linear_value_head_dim <= 256, L0B_ERR_UNSUPPORTED,
+                    "linear value head dim %d (1..256)", c.linear_value_head_dim);
+        L0B_REQUIRE(c.linear_conv_kernel >= 2 && c.linear_conv_kernel <= 8, L0B_ERR_UNSUPPORTED,
+                    "linear conv kernel %d (2..8)", c.linear_conv_kernel);
+    }
 
     std::unique_ptr<l0b_model> m(new l0b_model());
     m->dev = dev;
@@ -1111,7 +1239,15 @@ L0B_API l0b_status l0b_model_create(l0b_device* dev, l0b_suite* suite, const l0b
     m->vocab_full = c.vocab_size;
     m->cache_dtype = c.kv_dtype;
     m->softmax_scale = static_cast<float>(1.0 / std::sqrt(static_cast<double>(c.head_dim)));
-    m->fused = true;
+    m->fused = !hybrid;
+    m->hybrid = hybrid;
+    m->lin_hk = c.linear_num_key_heads;
+    m->lin_hv = c.linear_num_value_heads;
+    m->lin_dk = c.linear_key_head_dim;
+    m->lin_dv = c.linear_value_head_dim;
+    m->lin_kconv = c.linear_conv_kernel;
+    m->lin_cd = 2 * m->lin_hk * m->lin_dk + m->lin_hv * m->lin_dv;
+    m->lin_vd = m->lin_hv * m->lin_dv;
     m->tp = tp;
     m->tp_rank = tp > 1 ? c.tp_rank : 0;
     m->comm = tp > 1 ? comm : nullptr;
@@ -1134,10 +1270,27 @@ L0B_API l0b_status l0b_model_create(l0b_device* dev, l0b_suite* suite, const l0b
     L0B_TRY(m->alloc_matrix(m->lm_head, m->vocab, m->h, false));
     m->layers.resize(c.num_layers);
     const size_t cache_elems = static_cast<size_t>(m->batch_cap) * max_seq_len * m->kvdim;
-    for (auto& L : m->layers) {
+    for (int li = 0; li < c.num_layers; ++li) {
+        ModelLayer& L = m->layers[li];
+        L.linear = li < 64 && ((c.linear_layer_mask >> li) & 1ULL);
         L0B_TRY(m->alloc(&L.in_norm, m->h));
         L0B_TRY(m->alloc(&L.post_norm, m->h));
-        L0B_TRY(m->alloc_matrix(L.qkv, m->qkv_w, m->h));
+        if (L.linear) {
+            // Gated DeltaNet layer: no attention projections and no KV cache.
+            L0B_TRY(m->alloc_matrix(L.lin_in, m->lin_cd + m->lin_vd + 2 * m->lin_hv, m->h));
+            L0B_TRY(m->alloc_matrix(L.lin_out, m->h, m->lin_vd));
+            L0B_TRY(m->alloc_matrix(L.gate_up, 2 * m->inter, m->h, (m->inter % 64) == 0));
+            L0B_TRY(m->alloc_matrix(L.down, m->h, m->inter));
+            L0B_TRY(m->alloc(&L.conv_w, static_cast<size_t>(m->lin_cd) * m->lin_kconv));
+            L0B_TRY(m->alloc(&L.a_log, m->lin_hv));
+            L0B_TRY(m->alloc(&L.dt_bias, m->lin_hv));
+            L0B_TRY(m->alloc(&L.lin_norm, m->lin_dv));
+            L0B_TRY(m->alloc(&L.conv_state, static_cast<size_t>(m->lin_cd) * (m->lin_kconv - 1)));
+            L0B_TRY(m->alloc(&L.rec_state, static_cast<size_t>(m->lin_hv) * m->lin_dk * m->lin_dv));
+            continue;
+        }
+        // [q; k; v] (+ the output gate rows of a Qwen3.5 full-attention layer).
+        L0B_TRY(m->alloc_matrix(L.qkv, m->qkv_w + (c.attention_output_gate ? m->qdim : 0), m->h));
         L0B_TRY(m->alloc_matrix(L.o, m->h, m->qdim));
         L0B_TRY(m->alloc_matrix(L.gate_up, 2 * m->inter, m->h, (m->inter % 64) == 0));
         L0B_TRY(m->alloc_matrix(L.down, m->h, m->inter));
@@ -1165,6 +1318,11 @@ L0B_API l0b_status l0b_model_create(l0b_device* dev, l0b_suite* suite, const l0b
                 L0B_CHECK_CUDA(copy_sync(m->dev->stream, L.q_norm, ones.data(), m->hd * sizeof(float), cudaMemcpyHostToDevice));
                 L0B_CHECK_CUDA(copy_sync(m->dev->stream, L.k_norm, ones.data(), m->hd * sizeof(float), cudaMemcpyHostToDevice));
             }
+            if (L.lin_norm) {
+                std::vector<float> ones_v(m->lin_dv, one);
+                L0B_CHECK_CUDA(copy_sync(m->dev->stream, L.lin_norm, ones_v.data(), m->lin_dv * sizeof(float),
+                                         cudaMemcpyHostToDevice));
+            }
         }
     }
     // Activations.
@@ -1177,6 +1335,17 @@ L0B_API l0b_status l0b_model_create(l0b_device* dev, l0b_suite* suite, const l0b
     L0B_TRY(m->alloc(&m->vb, cap * m->kvdim));
     L0B_TRY(m->alloc(&m->attn, cap * m->qdim));
     L0B_TRY(m->alloc(&m->attn_proj, cap * m->h));
+    if (hybrid) {
+        L0B_TRY(m->alloc(&m->gb, cap * m->qdim));
+        if (c.linear_layer_mask) {
+            L0B_TRY(m->alloc(&m->lq, cap * m->lin_cd));
+            L0B_TRY(m->alloc(&m->lc, cap * m->lin_cd));
+            L0B_TRY(m->alloc(&m->lz, cap * m->lin_vd));
+            L0B_TRY(m->alloc(&m->lo, cap * m->lin_vd));
+            L0B_TRY(m->alloc(&m->lb, cap * m->lin_hv));
+            L0B_TRY(m->alloc(&m->la, cap * m->lin_hv));
+        }
+    }
     L0B_TRY(m->alloc(&m->gate, cap * m->inter));
     L0B_TRY(m->alloc(&m->up, cap * m->inter));
     L0B_TRY(m->alloc(&m->act, cap * m->inter));
@@ -1185,6 +1354,7 @@ L0B_API l0b_status l0b_model_create(l0b_device* dev, l0b_suite* suite, const l0b
     if (m->wdtype == L0B_F16 || m->wdtype == L0B_BF16 || m->wdtype == L0B_I8) {
         int kmax = m->h > m->inter ? m->h : m->inter;
         if (m->qdim > kmax) kmax = m->qdim;
+        if (m->lin_vd > kmax) kmax = m->lin_vd;  // Gated DeltaNet out_proj reads value-dim rows
         uint16_t* x16 = nullptr;
         L0B_TRY(m->alloc(&x16, (2 * cap + 256) * static_cast<size_t>(kmax)));
         m->x16 = x16;
@@ -1323,6 +1493,42 @@ __global__ void half_range_kernel(const float* v, long long count, int* bad) {
 
 extern "C" {
 
+}  // extern "C"
+
+namespace {
+
+// SplitQueryAndGate (L/LlmLayerWeights.cs:282-297) on the host: [heads][2][hd][hidden] rows of a Qwen3.5
+// q_proj become [query rows (heads * hd); gate rows (heads * hd)], elements of `elem` bytes.
+std::vector<char> split_query_gate(const void* src, size_t elem, int heads, int hd, int hidden) {
+    const size_t blk = static_cast<size_t>(hd) * hidden * elem;
+    std::vector<char> out(2 * blk * heads);
+    const char* s = static_cast<const char*>(src);
+    for (int h = 0; h < heads; ++h) {
+        std::memcpy(out.data() + h * blk, s + (2 * static_cast<size_t>(h)) * blk, blk);
+        std::memcpy(out.data() + (heads + h) * blk, s + (2 * static_cast<size_t>(h) + 1) * blk, blk);
+    }
+    return out;
+}
+
+// A split q_proj in staging ([query; gate] rows): the query rows to the top of [q; k; v; gate], the gate rows
+// after v.
+l0b_status set_query_gate_staged(l0b_model* m, const Target& t, const float* staging) {
+    Target q = t;
+    q.row0 = 0;
+    q.rows = m->qdim;
+    q.dst_row = 0;
+    L0B_TRY(set_tensor_staged(m, q, staging));
+    Target g = t;
+    g.row0 = m->qdim;
+    g.rows = m->qdim;
+    g.dst_row = m->qkv_w;
+    return set_tensor_staged(m, g, staging);
+}
+
+}  // namespace
+
+extern "C" {
+
 L0B_API l0b_status l0b_model_set_tensor(l0b_model* m, const char* name, const float* data, int64_t count) {
     GUARD_BEGIN
     L0B_REQUIRE(m && name && data, L0B_ERR_ARGUMENT, "null argument");
@@ -1348,6 +1554,12 @@ L0B_API l0b_status l0b_model_set_tensor(l0b_model* m, const char* name, const fl
         float* p;
         ~Free() { cudaFree(p); }
     } guard{staging};
+    if (t.query_gate) {
+        const std::vector<char> split = split_query_gate(data, sizeof(float), m->nh, m->hd, m->h);
+        L0B_CHECK_CUDA(copy_sync(m->dev->stream, staging, split.data(), static_cast<size_t>(full) * sizeof(float),
+                                 cudaMemcpyHostToDevice));
+        return set_query_gate_staged(m, t, staging);
+    }
     L0B_CHECK_CUDA(copy_sync(m->dev->stream, staging, data, static_cast<size_t>(full) * sizeof(float), cudaMemcpyHostToDevice));
     return set_tensor_staged(m, t, staging);
     GUARD_END
@@ -1382,6 +1594,11 @@ L0B_API l0b_status l0b_model_set_tensor_raw(l0b_model* m, const char* name, cons
     FreeV g2{staging};
     L0B_CHECK_CUDA(cudaMalloc(&bad, sizeof(int)));
     FreeV g3{bad};
+    std::vector<char> split;
+    if (t.query_gate) {
+        split = split_query_gate(data, 2, m->nh, m->hd, m->h);
+        data = split.data();
+    }
     L0B_CHECK_CUDA(copy_sync(st, raw, data, static_cast<size_t>(full) * 2, cudaMemcpyHostToDevice));
     widen16_kernel<<<grid_for(full, sm), 256, 0, st>>>(static_cast<const uint16_t*>(raw), dtype, staging, full);
     L0B_CHECK_CUDA(cudaGetLastError());
@@ -1399,6 +1616,7 @@ L0B_API l0b_status l0b_model_set_tensor_raw(l0b_model* m, const char* name, cons
         L0B_TRY(resolve(m, "lm_head.weight", &head));
         L0B_TRY(set_tensor_staged(m, head, staging));
     }
+    if (t.query_gate) return set_query_gate_staged(m, t, staging);
     return set_tensor_staged(m, t, staging);
     GUARD_END
 }
@@ -1406,6 +1624,7 @@ L0B_API l0b_status l0b_model_set_tensor_raw(l0b_model* m, const char* name, cons
 L0B_API l0b_status l0b_model_init_synthetic(l0b_model* m, uint64_t seed, float std, float scale_lo, float scale_hi) {
     GUARD_BEGIN
     L0B_REQUIRE(m, L0B_ERR_ARGUMENT, "model is null");
+    L0B_REQUIRE(!m->hybrid, L0B_ERR_UNSUPPORTED, "synthetic weights cover the standard decoders, not Qwen3.5 hybrids");
     L0B_CHECK_CUDA(cudaSetDevice(m->dev->index));
     Synth s{m, seed, std, scale_lo, scale_hi};
     const l0b_model_config& c = m->cfg;
@@ -1739,7 +1958,8 @@ L0B_API l0b_status l0b_model_reset_sequence(l0b_model* m) {
 L0B_API l0b_status l0b_model_projection_bytes(l0b_model* m, int64_t* bytes) {
     L0B_REQUIRE(m && bytes, L0B_ERR_ARGUMENT, "null argument");
     int64_t b = static_cast<int64_t>(m->lm_head.bytes());
-    for (auto& L : m->layers) b += L.qkv.bytes() + L.o.bytes() + L.gate_up.bytes() + L.down.bytes();
+    for (auto& L : m->layers)
+        b += L.qkv.bytes() + L.o.bytes() + L.gate_up.bytes() + L.down.bytes() + L.lin_in.bytes() + L.lin_out.bytes();
     *bytes = b;
     return L0B_OK;
 }
@@ -1752,6 +1972,7 @@ L0B_API l0b_status l0b_model_set_recording(l0b_model* m, int32_t enabled) {
 
 L0B_API l0b_status l0b_model_set_fused(l0b_model* m, int32_t enabled) {
     L0B_REQUIRE(m, L0B_ERR_ARGUMENT, "model is null");
+    L0B_REQUIRE(!(enabled && m->hybrid), L0B_ERR_UNSUPPORTED, "Qwen3.5 hybrid models run the reference op sequence");
     m->fused = enabled != 0;
     return L0B_OK;
 }
@@ -1820,6 +2041,8 @@ L0B_API l0b_status l0b_model_read_kv(l0b_model* m, int32_t layer, int32_t row0, 
     L0B_REQUIRE(m && keys && values, L0B_ERR_ARGUMENT, "null argument");
     L0B_REQUIRE(layer >= 0 && layer < static_cast<int>(m->layers.size()), L0B_ERR_OUT_OF_RANGE, "layer %d", layer);
     L0B_REQUIRE(row0 >= 0 && rows >= 0 && row0 + rows <= m->max_seq, L0B_ERR_OUT_OF_RANGE, "rows outside the cache");
+    L0B_REQUIRE(!m->layers[layer].linear, L0B_ERR_INVALID_OPERATION, "layer %d is a linear-attention layer (no KV cache)",
+                layer);
     if (rows == 0) return L0B_OK;
     const size_t n = static_cast<size_t>(rows) * m->kvdim;
     const size_t es = dtype_size(static_cast<l0b_dtype>(m->cache_dtype));

@@ -35,6 +35,13 @@ struct ModelLayer {
     float* k_norm = nullptr;
     void* kc = nullptr;  // [batch_cap, max_seq, kv_dim] (cache dtype)
     void* vc = nullptr;
+    // Qwen3.5 Gated DeltaNet layer (LlmLinearAttentionWeights / LlmLinearState, L/LlmLinearAttention.cs):
+    // in-projections stacked [qkv; z; b; a], out_proj, conv taps [conv_dim, k], A_log, dt_bias, the gated
+    // norm weight, and the sequence's conv window [conv_dim, k - 1] and recurrent state [hv, dk, dv].
+    bool linear = false;
+    ModelMatrix lin_in, lin_out;
+    float *conv_w = nullptr, *a_log = nullptr, *dt_bias = nullptr, *lin_norm = nullptr;
+    float *conv_state = nullptr, *rec_state = nullptr;
 };
 
 // Rotary table per L/RopeFrequencies.cs:67-183 (default, linear, yarn, llama3).

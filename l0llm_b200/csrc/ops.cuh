@@ -86,6 +86,12 @@ void attention_pick_split(int max_seq, int work_items, int sm_count, int* chunk,
 l0b_status sample_check(float temperature, float top_p, int top_k, float penalty, int vocab);
 // p[0..n) = v.
 l0b_status k_fill_u32(l0b_device* d, uint32_t* p, uint32_t v, int n);
+// CausalConv / GatedDelta over raw device pointers (the checked entry points wrap these; deltanet.cu).
+l0b_status k_causal_conv(l0b_device* d, const float* x, float* state, const float* w, float* out, int conv_dim,
+                         int kernel, int tokens);
+l0b_status k_gated_delta(l0b_suite* s, l0b_device* d, const float* conv, const float* z, const float* b, const float* a,
+                         const float* a_log, const float* dt_bias, const float* norm_w, float* state, float* out, int hk,
+                         int hv, int dk, int dv, int tokens, float eps);
 // 32-bit words of a context bitmap over `vocab` tokens.
 size_t sample_seen_words(int vocab);
 // 32-bit words of the key scratch sample_step takes for `vocab` tokens (keys, the max word, which must

@@ -85,6 +85,10 @@ class ModelConfig(C.Structure):
         ("rope_attention_factor", C.c_double), ("rope_mscale", C.c_double), ("rope_mscale_all_dim", C.c_double),
         ("rope_truncate", C.c_int32), ("partial_rotary_factor", C.c_double), ("kv_dtype", C.c_int32),
         ("q8_group", C.c_int32), ("tp_size", C.c_int32), ("tp_rank", C.c_int32), ("max_batch", C.c_int32),
+        ("linear_layer_mask", C.c_uint64), ("linear_num_key_heads", C.c_int32),
+        ("linear_num_value_heads", C.c_int32), ("linear_key_head_dim", C.c_int32),
+        ("linear_value_head_dim", C.c_int32), ("linear_conv_kernel", C.c_int32),
+        ("attention_output_gate", C.c_int32), ("rms_norm_offset", C.c_float),
     ]
 
 
@@ -681,9 +685,10 @@ class ShardPlan(C.Structure):
     """l0b_shard_plan: where l0b_model_set_tensor puts one checkpoint tensor on one tensor-parallel rank."""
     _fields_ = [(n, C.c_int32) for n in ("kind", "layer", "slot", "full_rows", "full_cols", "row0", "rows", "col0",
                                          "cols", "dst_row")]
-    MATRIX, VECTOR, EMBEDDING = 0, 1, 2
-    QKV, O, GATE_UP, DOWN, LM_HEAD = 0, 1, 2, 3, 4
+    MATRIX, VECTOR, EMBEDDING, QUERY_GATE = 0, 1, 2, 3
+    QKV, O, GATE_UP, DOWN, LM_HEAD, LIN_IN, LIN_OUT = 0, 1, 2, 3, 4, 5, 6
     IN_NORM, POST_NORM, QKV_BIAS, Q_NORM, K_NORM, FINAL_NORM = 0, 1, 2, 3, 4, 5
+    LIN_CONV, LIN_A_LOG, LIN_DT_BIAS, LIN_NORM = 6, 7, 8, 9
 
     def take(self, full: np.ndarray) -> np.ndarray:
         """This rank's part of the full checkpoint tensor (rows x cols of it)."""

@@ -151,3 +151,17 @@ def hybrid_oracle_config(cfg: dict, wdtype: int = 0, group: int = 0, kv_dtype: i
                 kv_dtype=kv_dtype, linear_mask=mask, lin_k_heads=cfg["lin_k_heads"], lin_v_heads=cfg["lin_v_heads"],
                 lin_k_dim=cfg["lin_k_dim"], lin_v_dim=cfg["lin_v_dim"], lin_conv=cfg["lin_conv"], attn_gate=1,
                 norm_offset=1.0, partial_rotary=cfg["partial_rotary"])
+
+
+def hybrid_model_config_kwargs(cfg: dict, kv_dtype: int = 0, q8_group: int = 0) -> dict:
+    """Keyword arguments of levelzero.model_config for a HYBRID config."""
+    mask = sum(1 << i for i, k in enumerate(cfg["layer_types"]) if k == "linear_attention")
+    return dict(hidden_size=cfg["hidden"], intermediate_size=cfg["inter"], num_layers=cfg["layers"],
+                num_attention_heads=cfg["heads"], num_key_value_heads=cfg["kv_heads"], head_dim=cfg["head_dim"],
+                vocab_size=cfg["vocab"], max_position_embeddings=cfg["max_pos"], rms_norm_eps=cfg["eps"],
+                rope_theta=cfg["theta"], tie_word_embeddings=0, attention_bias=0, qk_norm=1,
+                partial_rotary_factor=cfg["partial_rotary"], kv_dtype=kv_dtype, q8_group=q8_group,
+                linear_layer_mask=mask, linear_num_key_heads=cfg["lin_k_heads"],
+                linear_num_value_heads=cfg["lin_v_heads"], linear_key_head_dim=cfg["lin_k_dim"],
+                linear_value_head_dim=cfg["lin_v_dim"], linear_conv_kernel=cfg["lin_conv"], attention_output_gate=1,
+                rms_norm_offset=1.0)
