@@ -47,3 +47,18 @@ def test_hybrid_plan_refusals(lz):
     # Hybrid models run on one GPU.
     with pytest.raises(lz.NotSupportedException):
         lz.shard_plan(_cfg(lz, tp_size=2, tp_rank=0), "model.layers.0.mlp.up_proj.weight")
+
+
+def test_model_config_mirror_matches_the_c_struct(lz):
+    """levelzero.ModelConfig mirrors l0b_model_config field for field: l0b_model_config_init writes
+    exactly sizeof(ModelConfig) bytes (a canary right after it survives) and its defaults land on the
+    fields that carry them."""
+    import ctypes as C
+
+    n = C.sizeof(lz.ModelConfig)
+    buf = (C.c_uint8 * (n + 64))(*([0xA5] * (n + 64)))
+    cfg = lz.ModelConfig.from_buffer(buf)
+    lz.check(lz.load_library().l0b_model_config_init(C.byref(cfg)))
+    assert bytes(buf[n:]) == b"\xa5" * 64
+    assert cfg.max_position_embeddings == 2048 and cfg.rope_truncate == 1 and cfg.partial_rotary_factor == 1.0
+    assert cfg.linear_layer_mask == 0 and cfg.attention_output_gate == 0 and cfg.rms_norm_offset == 0.0
