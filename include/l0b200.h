@@ -517,11 +517,11 @@ L0B_API l0b_status l0b_set_gemv_ksplit_stages(int32_t stages);
  * Results are unchanged (a prefetch only moves data into the cache). Affects steps recorded after the
  * call. No counterpart in the reference. */
 L0B_API l0b_status l0b_set_l2_prefetch(int32_t gate_up_mb);
-/* Tuning: stage cap (2..8, default 2) of the bulk-copy GEMV's ring of whole 16-row tiles (row-major int8:
- * gate/up, LM head; units of blocked k blocks are not capped); below 2 takes as many
- * stages as its shared-memory budget holds (3 at K = 3584). Two stages leave room on an SM for the next
- * k-split GEMV's CTAs (config 2 bs1: 2.192 ms per step, 2.231 with three). Affects launches made after the
- * call. No counterpart in the reference. */
+/* Tuning: the bulk-copy GEMV's ring of whole 16-row tiles (row-major int8: gate/up, LM head; units of
+ * blocked k blocks are not affected). 0 (default): at most 120 KB of tiles, at least two -- two at K = 3584,
+ * which leaves room on an SM for the next k-split GEMV's CTAs (config 2 bs1: 2.192 ms per step, 2.231 with
+ * three), eight at K = 896; 2..8: at most that many tiles; 1: as many as its shared-memory budget holds.
+ * Affects launches made after the call. No counterpart in the reference. */
 L0B_API l0b_status l0b_set_gemv_bulk_stages(int32_t stages);
 /* Layout of the int8 weights of models created after the call: with blocking on (1, default), int8
  * projections with one scale per row, K % 512 == 0, N % 16 == 0 and fewer than 8 tiles of 16 rows per

@@ -1149,15 +1149,22 @@ __host__ __device__ inline size_t bulk_xs_bytes(int K) { return (static_cast<siz
 inline size_t bulk_smem_bytes(int K, int stages, int UK) {
     return 1024 + bulk_xs_bytes(K) + static_cast<size_t>(stages) * 16 * UK + 2 * kBulkMaxStages * 8;
 }
-// Stage cap of the bulk GEMV's ring (l0b_set_gemv_bulk_stages; 0 = as many as fit). Two stages of whole
-// 57 KB tiles (gate/up, LM head at K = 3584) leave an SM room for the next k-split GEMV's CTAs, which then
-// start their weight copies while this kernel drains: config 2 bs1 2.192 ms per step against 2.231 with
-// three stages.
-// The cap applies to whole tiles (row-major weights); units of blocked k blocks keep every stage that fits.
-int g_bulk_max_stages = 2;
+// Ring of whole tiles (row-major weights; units of blocked k blocks keep every stage that fits). By default
+// it holds at most kBulkRingBytes of tiles (at least two): two 57 KB tiles at K = 3584 (gate/up, LM head)
+// leave an SM room for the next k-split GEMV's CTAs, which then start their weight copies while this
+// kernel drains (config 2 bs1: 2.192 ms per step against 2.231 with three stages), and short rows keep a
+// deep ring (eight 14 KB tiles at K = 896). l0b_set_gemv_bulk_stages: n >= 2 caps the ring at n tiles, 1
+// takes as many as the shared-memory budget holds, 0 restores the default.
+constexpr int kBulkRingBytes = 120 * 1024;
+int g_bulk_max_stages = 0;
 inline int bulk_stages(int K, int UK, bool whole_tiles) {
-    const int top = whole_tiles && g_bulk_max_stages >= 2 && g_bulk_max_stages < kBulkMaxStages ? g_bulk_max_stages
-                                                                                                  : kBulkMaxStages;
+    int top = kBulkMaxStages;
+    if (whole_tiles && g_bulk_max_stages >= 2) {
+        top = g_bulk_max_stages < kBulkMaxStages ? g_bulk_max_stages : kBulkMaxStages;
+    } else if (whole_tiles && g_bulk_max_stages == 0) {
+        const int by_bytes = kBulkRingBytes / (16 * UK);
+        top = by_bytes < 2 ? 2 : (by_bytes < kBulkMaxStages ? by_bytes : kBulkMaxStages);
+    }
     for (int s = top; s >= 2; --s)
         if (bulk_smem_bytes(K, s, UK) <= static_cast<size_t>(kBulkSmemBudget)) return s;
     return 0;
@@ -2115,7 +2122,7 @@ void gemv_set_tensor_cores(bool on) { g_gemv_mma = on; }
 void gemv_set_bulk(bool on) { g_gemv_bulk = on; }
 void gemv_set_bulk_short_rows(bool on) { g_gemv_bulk_short = on; }
 void gemv_set_ksplit(bool on) { g_gemv_ksplit = on; }
-void gemv_set_bulk_stages(int s) { g_bulk_max_stages = s < 2 ? 0 : s; }
+void gemv_set_bulk_stages(int s) { g_bulk_max_stages = s < 0 ? 0 : s; }
 int gemv_l2_prefetch_mb() { return g_l2_prefetch_mb; }
 void gemv_set_l2_prefetch_mb(int mb) { g_l2_prefetch_mb = mb < 0 ? 0 : mb; }
 void gemv_set_ksplit_stages(int s) { g_ksplit_stages = s < 2 ? 2 : (s > kKsMaxStages ? kKsMaxStages : s); }

@@ -109,7 +109,8 @@ void gemv_set_fill_split(int s);
 void gemv_set_bulk_short_rows(bool on);
 void gemv_set_ksplit(bool on);
 void gemv_set_ksplit_stages(int s);
-// Stage cap of the bulk GEMV's ring (2..8, default 2; below 2 = as many as fit its shared-memory budget).
+// The bulk GEMV's ring of whole tiles: 0 = at most 120 KB of tiles (default), 2..8 = at most that many,
+// 1 = as many as its shared-memory budget holds.
 void gemv_set_bulk_stages(int s);
 // Megabytes of the gate/up weights the one-row decode step prefetches into L2 ahead of their projection
 // (the o_proj GEMV issues them; q/k/v also prefetches o_proj's weights and down the next layer's q/k/v);
