@@ -2008,6 +2008,7 @@ L0B_API l0b_status l0b_model_read_weight(l0b_model* m, int32_t layer, int32_t ki
         mats[3] = &L.down;
     }
     const ModelMatrix& mat = *mats[kind % 4];
+    L0B_REQUIRE(mat.w, L0B_ERR_INVALID_OPERATION, "layer %d has no such matrix (a linear-attention layer)", layer);
     const void* src;
     size_t size;
     if (kind < 4) {
