@@ -575,12 +575,14 @@ def run_cfg3_deltanet(args) -> int:
 
 
 def measure_cfg4_tp(lz, dev, suite, stream_ptr, torch, dist, world: int, rank: int, local: int, steps: int,
-                    warmup: int) -> dict:
+                    warmup: int, batch: int = 1) -> dict:
     """Config 4 (Llama-3-70B shape, bf16, llama3 RoPE) decoded tensor-parallel over the `world` ranks of the
     job (world = 1: the whole 139 GB model on one GPU, the scaling anchor): q/k/v, gate/up and lm_head
     column-split, o_proj/down row-split with an all-reduce after each, KV heads split. A 2048-token prompt,
     then `warmup` + `steps` device-resident greedy steps at bs1; CUDA events on the model stream, max
-    over ranks. Every rank takes the same collective steps; returns the result on every rank."""
+    over ranks. Every rank takes the same collective steps; returns the result on every rank. batch > 1
+    (BASELINE config 4's batch 32): the prompt is prefilled once and forked on the device into `batch`
+    sequences, which then decode together (one graph per step)."""
     stream = torch.cuda.ExternalStream(stream_ptr)
     comm = None
     if world > 1:
@@ -589,7 +591,7 @@ def measure_cfg4_tp(lz, dev, suite, stream_ptr, torch, dist, world: int, rank: i
         comm = lz.Communicator(dev, box[0], world, rank)
     uses_peer = comm is not None and comm.UsesPeerAllReduce
     fused = lz.Communicator.fused_allreduce()
-    cfg = lz.model_config(kv_dtype=lz.BF16, tp_size=world, tp_rank=rank, **CFG4)
+    cfg = lz.model_config(kv_dtype=lz.BF16, tp_size=world, tp_rank=rank, max_batch=batch, **CFG4)
     model = lz.LlmModel(dev, suite, cfg, CFG4_PROMPT + 2 * warmup + steps + 16, "bfloat16", comm=comm)
     model.init_synthetic(4, 0.02)
     prompt = np.random.default_rng(4).integers(0, CFG4["vocab_size"], CFG4_PROMPT).astype(np.int32)
@@ -604,11 +606,17 @@ def measure_cfg4_tp(lz, dev, suite, stream_ptr, torch, dist, world: int, rank: i
     model.Prefill(prompt)
     barrier()
     prefill_s = time.perf_counter() - t0
-    model.decode_greedy_device(warmup)
+    for sq in range(1, batch):
+        model.ForkSequence(0, sq, 0)
+
+    def decode(n):
+        return model.decode_greedy_device(n) if batch == 1 else model.decode_greedy_device_batch(n, batch)
+
+    decode(warmup)
     barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
-    toks = model.decode_greedy_device(steps)
+    toks = decode(steps)
     e1.record(stream)
     e1.synchronize()
     barrier()
@@ -649,8 +657,8 @@ def measure_cfg4_tp(lz, dev, suite, stream_ptr, torch, dist, world: int, rank: i
             ar_us = float(ta[0])
         comm.Dispose()  # releases the device's captured graphs first
     return {"workload": f"config 4: Llama-3-70B-shape bf16 (80 layers, hidden 8192, 64/8 heads, inter 28672, vocab "
-                        f"128256, llama3 RoPE), TP{world}, bs1, {CFG4_PROMPT}-token prompt",
-            "value": round(steps / (ms / 1e3), 2), "unit": "tok/s", "ms_per_step": round(ms / steps, 4),
+                        f"128256, llama3 RoPE), TP{world}, bs{batch}, {CFG4_PROMPT}-token prompt",
+            "value": round(batch * steps / (ms / 1e3), 2), "unit": "tok/s", "ms_per_step": round(ms / steps, 4),
             "scaling": "strong", "parallelism": f"tp{world}", "prefill_s": round(prefill_s, 3),
             "per_rank_weight_gbs": round(proj / (ms / steps * 1e-3) / 1e9, 1),
             "weight_bytes_per_rank": int(proj), "ranks_agree_on_tokens": agree, "steps": steps, "warmup": warmup,
@@ -682,17 +690,18 @@ def run_cfg4_tp(args) -> int:
     sampler = ClockSampler(local)
     sampler.start()
     t_begin = time.monotonic()
-    r = measure_cfg4_tp(lz, dev, suite, sp.value, torch, dist, world, rank, local, args.steps, args.warmup)
+    r = measure_cfg4_tp(lz, dev, suite, sp.value, torch, dist, world, rank, local, args.steps, args.warmup,
+                        batch=args.tp_batch)
     sampler.mark(t_begin, time.monotonic())
     clocks = sampler.stop()
     suite.Dispose()
     dev.Dispose()
     if rank == 0:
         line = {
-            "metric": "decode tok/s (Llama-3-70B bf16, TP, bs1)", "value": r["value"], "unit": "tok/s",
+            "metric": f"decode tok/s (Llama-3-70B bf16, TP, bs{args.tp_batch})", "value": r["value"], "unit": "tok/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": r["ms_per_step"],
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": r["workload"], "global_batch": 1, "seq_len": CFG4_PROMPT,
+            "config": {"workload": r["workload"], "global_batch": args.tp_batch, "seq_len": CFG4_PROMPT,
                        "parallelism": r["parallelism"],
                        "l2": "inputs larger than L2: every rank streams its weight shard each step"},
             "per_rank_weight_gbs": r["per_rank_weight_gbs"], "clocks": clocks, "prefill_s": r["prefill_s"],
@@ -883,6 +892,9 @@ def main() -> int:
     ap.add_argument("--pair-allreduce", action="store_true",
                     help="row-split GEMV + separate all-reduce kernel instead of the all-reduce folded into the GEMV")
     ap.add_argument("--no-tp", action="store_true", help="skip the config 4 tensor-parallel leg (tp)")
+    ap.add_argument("--tp-batch", type=int, default=1,
+                    help="--workload cfg4 only: sequences decoded together (BASELINE config 4 also runs 32), one "
+                         "prompt prefilled and forked on the device")
     ap.add_argument("--profile-case", choices=["decode-bs1", "decode-bs16", "gemm-gateup-16", "attention-512",
                                                "decode-cfg4-tp8-shard", "gemm-gateup-512", "attention-tp8",
                                                "decode-bs1-1layer"],
