@@ -13,7 +13,8 @@ fp16 KV cache. Weights are 7.07 GB per step, far larger than the 126 MB L2, so n
           projection launched on its own over rotating weight copies (more than L2) and timed with events;
           by_launch adds each projection and the bulk GEMV's gate/up (with ncu DRAM traffic).
   cpu_baseline  the CPU oracle port (C, fp32 AVX2 FMA, OpenMP) of the same decoder and weights on the
-          host cores at the same 512-token context (all threads, plus a single-thread figure).
+          host cores at the same 512-token context (all threads, plus a single-thread figure); the legs
+          below carry the same port on their own configuration (config 4: one layer, extrapolated).
   step_roofline  all bytes of a step (weights + KV) over the step time.
   prefill_s  a warm prefill of the 512-token prompt (one 512-row tcgen05 GEMM per projection).
   bs16    16 sequences decoded together (device-resident batched greedy, tcgen05 integer GEMM).
@@ -240,6 +241,119 @@ def cpu_baseline(budget_s: float) -> dict:
     dec.close()
     allc["single_thread"] = {"value": one["value"], "unit": "tok/s", "cores": 1, "sample": one["sample"]}
     return allc
+
+
+def _timed_steps(fn, budget_s: float, max_reps: int) -> tuple[int, float]:
+    """One untimed call sizes the sample; then as many calls as fit the budget (at least one)."""
+    t0 = time.perf_counter()
+    fn()
+    first = time.perf_counter() - t0
+    reps = max(1, min(max_reps, int(budget_s / max(first, 1e-4))))
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        fn()
+    return reps, time.perf_counter() - t0
+
+
+def cpu_legs(budget_s: float) -> dict:
+    """The oracle port on the host cores (all threads, fp32-accumulate timing build) for the other BASELINE
+    configurations, each a bounded sample: config 0 (the int8 GEMV and its M = 128 GEMM), config 1 (decode
+    of the fp16 Qwen2.5-0.5B shape at a 128-token context), config 3 (one Gated DeltaNet layer's decode
+    step: projections, conv, recurrence, gated norm, out_proj; bf16 weights) and config 4 (one bf16 decoder
+    layer of the Llama-3-70B shape at a 2048-token context, extrapolated to 80 layers plus the LM head by
+    bytes)."""
+    from oracle import oracle as orc
+
+    threads = os.cpu_count() or 1
+    orc.set_num_threads(threads)
+    each = budget_s / 4
+    out = {}
+    rng = np.random.default_rng(0)
+    # Config 0.
+    n, k = 4864, 896
+    q = rng.integers(-127, 128, (n, k)).astype(np.int8)
+    sc = orc.f16_bits(rng.uniform(1e-3, 2e-2, n).astype(np.float32))
+    x1 = rng.standard_normal((1, k)).astype(np.float32)
+    x128 = rng.standard_normal((128, k)).astype(np.float32)
+    r1, t1 = _timed_steps(lambda: orc.gemm_fast(x1, q, orc.I8, sc, k), each / 2, 20000)
+    r2, t2 = _timed_steps(lambda: orc.gemm_fast(x128, q, orc.I8, sc, k), each / 2, 2000)
+    b1, b128 = n * k + 2 * n + 2 * k + 2 * n, n * k + 2 * n + 128 * (2 * k + 2 * n)
+    out["cfg0"] = {"gemv_us": round(t1 / r1 * 1e6, 2), "gemv_gbs": round(b1 * r1 / t1 / 1e9, 2),
+                   "gemm_m128_us": round(t2 / r2 * 1e6, 2), "gemm_m128_tflops": round(2 * 128 * n * k * r2 / t2 / 1e12, 4),
+                   "cores": threads, "kind": "port",
+                   "sample": f"{r1} GEMVs and {r2} M = 128 GEMMs of the int8 [4864, 896] weights (per-channel scales)"}
+    # Config 1.
+    c1 = dict(hidden=896, inter=4864, layers=24, heads=14, kv_heads=2, head_dim=64, vocab=151936, max_pos=32768,
+              eps=1e-6, theta=1e6, tie=1, bias=1, qk_norm=0, rope_type=0, rope_factor=1.0, rope_original_max=0,
+              rope_low=1.0, rope_high=4.0, rope_beta_fast=32.0, rope_beta_slow=1.0, rope_attention=0.0,
+              wdtype=orc.F16, group=0, kv_dtype=orc.F16)
+    om = orc.OracleModel(c1, 160)
+    om.init_synthetic(1, 0.02)
+    om.set_fast(True)
+    for layer in range(24):
+        om.write_kv(layer, 0, rng.standard_normal((128, 128)).astype(np.float32),
+                    rng.standard_normal((128, 128)).astype(np.float32))
+    st = {"pos": 128, "tok": 1}
+
+    def step1():
+        lg = om.step(st["tok"], st["pos"])
+        st["tok"], st["pos"] = int(np.argmax(lg)), min(st["pos"] + 1, 150)
+
+    r, t = _timed_steps(step1, each, 20)
+    om.close()
+    out["cfg1"] = {"value": round(r / t, 2), "unit": "tok/s", "cores": threads, "kind": "port",
+                   "sample": f"{r} greedy decode steps of the 24-layer fp16 decoder at a 128-token context"}
+    # Config 3: a one-layer hybrid oracle whose only layer is the Gated DeltaNet layer (tiny MLP, vocab and
+    # embedding so that the layer dominates).
+    H, HK, HV, DK, DV = 2048, 16, 32, 128, 128
+    c3 = dict(hidden=H, inter=16, layers=1, heads=16, kv_heads=16, head_dim=128, vocab=16, max_pos=4096, eps=1e-6,
+              theta=1e6, tie=0, bias=0, qk_norm=0, rope_type=0, rope_factor=1.0, rope_low=1.0, rope_high=4.0,
+              rope_beta_fast=32.0, rope_beta_slow=1.0, wdtype=orc.BF16, group=0, kv_dtype=orc.F32, linear_mask=1,
+              lin_k_heads=HK, lin_v_heads=HV, lin_k_dim=DK, lin_v_dim=DV, lin_conv=4, attn_gate=0, norm_offset=0.0)
+    om = orc.OracleModel(c3, 4096)
+    cd, vd = 2 * HK * DK + HV * DV, HV * DV
+    for name, shape in (("in_proj_qkv.weight", (cd, H)), ("in_proj_z.weight", (vd, H)), ("in_proj_b.weight", (HV, H)),
+                        ("in_proj_a.weight", (HV, H)), ("out_proj.weight", (H, vd)), ("conv1d.weight", (cd, 4)),
+                        ("A_log", (HV,)), ("dt_bias", (HV,))):
+        om.set_tensor("model.layers.0.linear_attn." + name, (rng.standard_normal(shape) * 0.02).astype(np.float32))
+    om.set_fast(True)
+    st = {"pos": 0}
+
+    def step3():
+        om.step(1, st["pos"])
+        st["pos"] += 1
+
+    r, t = _timed_steps(step3, each, 256)
+    om.close()
+    out["cfg3"] = {"us_per_step": round(t / r * 1e6, 1), "cores": threads, "kind": "port",
+                   "sample": f"{r} decode steps of one Gated DeltaNet layer (16 / 32 heads of 128, bf16 projections, "
+                             f"fp32 state), bs1"}
+    # Config 4: one bf16 layer at the Llama-3-70B width, extrapolated.
+    c4 = dict(hidden=8192, inter=28672, layers=1, heads=64, kv_heads=8, head_dim=128, vocab=16, max_pos=131072,
+              eps=1e-5, theta=5e5, tie=0, bias=0, qk_norm=0, rope_type=3, rope_factor=8.0, rope_original_max=8192,
+              rope_low=1.0, rope_high=4.0, rope_beta_fast=32.0, rope_beta_slow=1.0, rope_attention=0.0,
+              wdtype=orc.BF16, group=0, kv_dtype=orc.BF16)
+    om = orc.OracleModel(c4, 2100)
+    om.init_synthetic(4, 0.02)
+    om.set_fast(True)
+    om.write_kv(0, 0, rng.standard_normal((2048, 1024)).astype(np.float32),
+                rng.standard_normal((2048, 1024)).astype(np.float32))
+    st = {"pos": 2048}
+
+    def step4():
+        om.step(1, st["pos"])
+        st["pos"] = min(st["pos"] + 1, 2090)
+
+    r, t = _timed_steps(step4, each, 20)
+    om.close()
+    layer_bytes = 2 * (8192 * (8192 + 2 * 1024) + 8192 * 8192 + 3 * 8192 * 28672)
+    head_bytes = 2 * 128256 * 8192
+    step_s = t / r * (80 + head_bytes / layer_bytes)
+    out["cfg4"] = {"value": round(1.0 / step_s, 4), "unit": "tok/s", "cores": threads, "kind": "port",
+                   "extrapolated": True, "layer_ms": round(t / r * 1e3, 2),
+                   "sample": f"{r} decode steps of one bf16 Llama-3-70B-width layer at a 2048-token context, scaled "
+                             f"to 80 layers plus the LM head by their weight bytes"}
+    return out
 
 
 def run_reference(args) -> int:
@@ -1063,6 +1177,16 @@ def main() -> int:
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline(budget_s=25.0)
+        # The same CPU port beside each of the other configurations' GPU legs (bounded samples).
+        try:
+            cl = cpu_legs(budget_s=20.0)
+        except Exception as e:  # a baseline that failed is reported, not fatal to the GPU line
+            cl = {k: {"error": f"{type(e).__name__}: {e}"} for k in ("cfg0", "cfg1", "cfg3", "cfg4")}
+        for key in ("cfg0", "cfg1", "cfg3"):
+            if key in legs:
+                legs[key]["cpu_baseline"] = cl[key]
+        if tp is not None:
+            tp["cpu_baseline"] = cl["cfg4"]
     suite.Dispose()
     dev.Dispose()
     if rank == 0:
